@@ -1,0 +1,163 @@
+#!/usr/bin/env python3
+"""Generate the golden vectors that pin the oracle (and the CUDA path) to the
+reference implementation of the Naylis MoM hot path.
+
+Run HERE, where the reference checkout is importable:
+
+    python tests/golden/make_golden.py --reference <path-to-reference-checkout>
+
+It imports the reference's own ``model.MoMLayer`` and ``mom_kernels.reference``
+(no code is copied) and runs them on seeded inputs. Inputs are NOT stored:
+``golden_inputs.py`` regenerates them bit-identically from torch's CPU RNG, and
+their SHA-256 digests are stored so a drift in the generator is detected.
+Outputs are stored in full where small, and as SHA-256 + a seeded subsample
+where large (config 1).
+
+Cases:
+  cfg1_fwd        BASELINE config 1: fp32 layer forward, B=1 S=256 d=1024,
+                  16x64 heads, bank 8x128, rank 32, top-2, mom_scale=1, eval.
+  small_f32       layer forward+backward, fp32, the reference test-suite
+                  geometry (tests/test_parity.py:74-77), upstream grad N(0,1).
+  small_bf16      layer forward+backward under CPU bf16 autocast.
+  read_f32/bf16   read only (build_gate_bias + mom_attention_reference), with
+                  gradients w.r.t. q, k, v and the gates.
+  scan            prefix mean h at (2, 1024, 64), fp32 and bf16 input: SHA-256.
+"""
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+import golden_inputs as gi  # noqa: E402
+
+
+def sha(t) -> str:
+    import torch
+    a = t.detach().contiguous()
+    if a.dtype == torch.bfloat16:
+        a = a.float()
+    return hashlib.sha256(a.cpu().numpy().tobytes()).hexdigest()
+
+
+def to_np(t):
+    import torch
+    t = t.detach()
+    if t.dtype == torch.bfloat16:
+        t = t.float()
+    return t.cpu().numpy()
+
+
+def build_layer(model_mod, geo):
+    return model_mod.MoMLayer(
+        d_model=geo["d"], n_heads=geo["H"], mem_size=geo["nb"] * geo["bs"],
+        block_size=geo["bs"], top_blocks=geo["top"], router_rank=geo["r"])
+
+
+def run_cfg1(model_mod, reference):
+    import torch
+    geo = gi.CFG1
+    layer = build_layer(model_mod, geo)
+    inp = gi.layer_inputs(geo, layer)
+    layer.eval()
+    with torch.no_grad():
+        out, probs, top_idx, gates = reference.mom_full_reference(inp["x"], layer, inp["M"])
+        out_layer = layer(inp["x"], inp["M"])
+        logits = layer._router_logits(inp["x"])
+        h = reference.prefix_mean_reference(inp["x"])
+    assert torch.equal(out, out_layer)
+    rng = np.random.default_rng(1234)
+    sub = rng.choice(out.numel(), size=4096, replace=False)
+    return dict(
+        input_sha=np.array(gi.input_digest(inp)),
+        out_sha=np.array(sha(out)), h_sha=np.array(sha(h)),
+        out_sub_idx=sub.astype(np.int64), out_sub=to_np(out).reshape(-1)[sub],
+        h_sub=to_np(h).reshape(-1)[sub],
+        probs=to_np(probs).reshape(geo["B"], geo["S"], -1),
+        top_idx=to_np(top_idx).astype(np.int64),
+        gates=to_np(gates), logits=to_np(logits),
+    )
+
+
+def run_layer_small(model_mod, autocast: bool):
+    import torch
+    geo = gi.SMALL_BF16 if autocast else gi.SMALL_F32
+    layer = build_layer(model_mod, geo)
+    inp = gi.layer_inputs(geo, layer)
+    layer.train()
+    layer.noise_scale = 0.0          # deterministic routing, no Gumbel draw
+    x = inp["x"].clone().requires_grad_(True)
+    M = inp["M"].clone().requires_grad_(True)
+    dout = gi.upstream_grad(geo)
+    with torch.autocast("cpu", dtype=torch.bfloat16, enabled=autocast):
+        out = layer(x, M)
+    out.backward(dout)
+    res = dict(input_sha=np.array(gi.input_digest(inp)), out=to_np(out),
+               probs=to_np(layer.last_router_probs).reshape(geo["B"], geo["S"], -1),
+               top_idx=to_np(layer.last_top_idx).reshape(geo["B"], geo["S"], -1).astype(np.int64),
+               dx=to_np(x.grad), dM_blocks=to_np(M.grad))
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16, enabled=autocast):
+        res["logits"] = to_np(layer._router_logits(inp["x"]))
+    for name, p in layer.named_parameters():
+        res["d_" + name.replace(".weight", "")] = to_np(p.grad)
+    return res
+
+
+def run_read(reference, dtype_name: str):
+    import torch
+    geo = gi.READ
+    q, k, v, top, g, dout = gi.read_inputs(geo, dtype_name)
+    for t in (q, k, v, g):
+        t.requires_grad_(True)
+    bias = reference.build_gate_bias(top, g, geo["nb"], geo["bs"], q.dtype)
+    out = reference.mom_attention_reference(q, k, v, bias)
+    out.backward(dout)
+    return dict(out=to_np(out), dq=to_np(q.grad), dk=to_np(k.grad), dv=to_np(v.grad),
+                dgates=to_np(g.grad), top_idx=to_np(top).astype(np.int64))
+
+
+def run_scan(reference):
+    import torch
+    res = {}
+    for name in ("f32", "bf16"):
+        x = gi.scan_input(name)
+        h = reference.prefix_mean_reference(x)
+        res[f"h_sha_{name}"] = np.array(sha(h))
+        res[f"x_sha_{name}"] = np.array(sha(x))
+        res[f"h_first_row_{name}"] = to_np(h[:, :4])
+        assert h.dtype == torch.float32
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--out", default=HERE)
+    args = ap.parse_args()
+    sys.path.insert(0, os.path.abspath(args.reference))
+    import torch
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    import model as model_mod
+    from mom_kernels import reference
+
+    cases = {
+        "cfg1_fwd": lambda: run_cfg1(model_mod, reference),
+        "small_f32": lambda: run_layer_small(model_mod, autocast=False),
+        "small_bf16": lambda: run_layer_small(model_mod, autocast=True),
+        "read_f32": lambda: run_read(reference, "f32"),
+        "read_bf16": lambda: run_read(reference, "bf16"),
+        "scan": lambda: run_scan(reference),
+    }
+    for name, fn in cases.items():
+        res = fn()
+        path = os.path.join(args.out, f"{name}.npz")
+        np.savez_compressed(path, **res)
+        print(f"wrote {path} ({os.path.getsize(path) / 1024:.1f} KiB)")
+
+
+if __name__ == "__main__":
+    main()
