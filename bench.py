@@ -1,0 +1,449 @@
+#!/usr/bin/env python3
+"""Benchmark of the sm100 MoM hot path (one JSON line on rank 0).
+
+Workload: one MoM layer forward+backward — fused router,
+q/k/v/o projections, the bucketed memory read — on B=8 x S=2048 tokens per
+GPU, d=1024, 16x64 heads, bank 8x128 slots, router rank 32, top-2, bf16
+autocast with fp32 master weights, Gumbel exploration on (training mode).
+At N>1 every rank runs its own 8x2048 shard (weak scaling) and the gradients
+are averaged with the bucketed NCCL all-reduce of naylis_b200.data_parallel.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sm100|reference]
+
+``--impl reference`` times the CPU restatement of the reference's eager path
+(oracle/mom_oracle.py: layer_step_fp32) on this host's cores, same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CFG = dict(B=8, S=2048, d=1024, H=16, nb=8, bs=128, top=2, r=32)
+METRIC = "MoM layer fwd+bwd tokens/s (router + read + projections), BASELINE config 2"
+WORKLOAD = ("cfg2: one MoM layer fwd+bwd per GPU, B=8 S=2048 d=1024, 16x64 heads, "
+            "bank 8x128 slots, router rank 32, top-2, bf16 autocast, fp32 master weights")
+
+
+def read_flops(N, d, top, bs):
+    """Algorithmic read FLOPs, active slots only: fwd 4*N*d*La, bwd 8*N*d*La."""
+    La = top * bs
+    return 4 * N * d * La, 8 * N * d * La
+
+
+def router_bytes(N, d, nb, top, r, x_bytes=2):
+    """Algorithmic router-forward HBM bytes: read x once, write probs, idx
+    (int64), gates and the saved activations."""
+    return N * d * x_bytes + N * nb * 4 + N * top * 8 + N * top * 4 + N * r * 2
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm=p["hbm_gbs"], bf16=p["bf16_tflops"], bf16_sust=p["bf16_tflops_sustained"],
+                    src="measured")
+    return dict(hbm=6650.0, bf16=1590.0, bf16_sust=1400.0, src="fallback")
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) taken while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.window = (0.0, 0.0)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append((time.time(), [c.strip() for c in line.split(",")]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        t0, t1 = self.window
+        rows = [r for t, r in self.rows if t0 <= t <= t1] or [r for _, r in self.rows]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ------------------------------------------------------------------ GPU arm
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    from naylis_b200 import _lib
+    from naylis_b200 import mom_kernels as mk
+    from naylis_b200.data_parallel import GradAllReduce
+    from naylis_b200.model import MoMLayer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    c = CFG
+    N = c["B"] * c["S"]
+    torch.manual_seed(1234 + rank)
+    layer = MoMLayer(c["d"], c["H"], c["nb"] * c["bs"], c["bs"], c["top"], c["r"], use_kernel=True)
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02)
+        layer.mom_scale.fill_(1.0)
+    layer = layer.to(dev).train()
+    layer.noise_scale = 1.0
+    M = torch.nn.Parameter(torch.randn(c["nb"], c["bs"] * c["d"], device=dev) * 0.02)
+    x = torch.randn(c["B"], c["S"], c["d"], device=dev).to(torch.bfloat16).requires_grad_(True)
+    dout = torch.randn(c["B"], c["S"], c["d"], device=dev).to(torch.bfloat16)
+
+    holder = torch.nn.Module()
+    holder.layer = layer
+    holder.M = M
+    dp = GradAllReduce(holder) if world > 1 else None
+    mk.resolve_mode(dev, torch.bfloat16, head_dim=c["d"] // c["H"])
+
+    def step(xin, gin):
+        if dp is not None:
+            dp.zero_grad()
+        else:
+            for p in holder.parameters():
+                p.grad = None
+        xin.grad = None
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            out = layer(xin, M)
+        out.backward(gin)
+        if dp is not None:
+            dp.finish()
+
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 256 MiB > L2
+    for _ in range(args.warmup):
+        step(x, dout)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.5)
+    lib = _lib.load()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = lib.mom_kernel_launches()
+    t_wall0 = time.time()
+    for i in range(args.steps):
+        flush.fill_(float(i))                       # evict L2 between timed steps (untimed)
+        starts[i].record()
+        step(x, dout)
+        ends[i].record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_wall1 = time.time()
+    launches = lib.mom_kernel_launches() - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if clocks:
+        clocks.window = (t_wall0, t_wall1)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    tokens_per_s = world * N * args.steps / (total_ms / 1e3)
+
+    # ---- dominant kernels: the read (fwd + bwd) and the router, on this rank's data
+    extra = {}
+    if rank == 0:
+        extra = measure_kernels(layer, x, M, dout, dev, args)
+    # ---- end to end through the public API with host buffers
+    e2e = measure_e2e(step, x, dout, dev, args, world, N)
+    if clocks:
+        clocks.stop()
+    if rank == 0:
+        pk = peaks()
+        roof = extra["read"]
+        line = {
+            "metric": METRIC,
+            "value": round(tokens_per_s, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights and bank)",
+            "config": {"workload": WORKLOAD, "global_batch": c["B"] * world, "seq_len": c["S"],
+                       "parallelism": f"dp{world}", "l2": "flushed between timed steps (256 MiB write, untimed)"},
+            "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
+                         "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
+                         "traffic": None, "kernel": "MoM read fwd+bwd (bucket + fwd + dq + dkdv)",
+                         "flops_per_launch": roof["flops"], "ms_per_launch": roof["ms"],
+                         "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
+            "router": extra["router"],
+            "read": roof,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "gpu_launches_per_step": round(launches / args.steps, 2),
+            "clocks": clocks.summary() if clocks else None,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(samples=args.cpu_samples)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def measure_kernels(layer, x, M, dout, dev, args):
+    """CUDA-event timing of the read and the router through the C ABI, on the
+    launching (current) stream, L2 flushed between iterations."""
+    import torch
+    from naylis_b200 import _lib
+    from naylis_b200 import mom_kernels as mk
+    c = CFG
+    B, S, d, H, nb, bs, top, r = (c[k] for k in ("B", "S", "d", "H", "nb", "bs", "top", "r"))
+    hd = d // H
+    N = B * S
+    lib = _lib.load()
+    st = torch.cuda.current_stream(dev).cuda_stream
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        probs, idx, gates = mk.mom_route(x, layer.router_down.weight, layer.router_up.weight, top)
+        q = layer.q_proj(x).view(B, S, H, hd).contiguous()
+        slots = M.view(nb * bs, d)
+        k = layer.k_proj(slots).contiguous()
+        v = layer.v_proj(slots).contiguous()
+    lg = gates.clamp_min(1e-9).log().float().contiguous()
+    plan = torch.empty(lib.mom_plan_size(N, nb, top), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(q)
+    lse = torch.empty(N, H, dtype=torch.float32, device=dev)
+    dq = torch.empty_like(q)
+    dk = torch.empty(nb * bs, d, dtype=torch.float32, device=dev)
+    dv = torch.empty_like(dk)
+    dlg = torch.empty(N, top, dtype=torch.float32, device=dev)
+    ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=dev)
+    do4 = dout.view(B, S, H, hd)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    def read_once():
+        _lib.call("mom_bucket", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
+                  plan.numel(), st)
+        _lib.call("mom_read_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd, nb,
+                  bs, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(), st)
+        _lib.call("mom_read_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                  do4.data_ptr(), lse.data_ptr(), _lib.BF16, B, S, H, hd, nb, bs, top, plan.data_ptr(),
+                  dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(), ws.data_ptr(),
+                  ws.numel(), st)
+
+    xb = x.detach().contiguous()
+    wd = layer.router_down.weight.detach().to(torch.bfloat16).contiguous()
+    wu = layer.router_up.weight.detach().to(torch.bfloat16).contiguous()
+    probs_o = torch.empty(N, nb, dtype=torch.float32, device=dev)
+    idx_o = torch.empty(N, top, dtype=torch.int64, device=dev)
+    gates_o = torch.empty(N, top, dtype=torch.float32, device=dev)
+    act_o = torch.empty(N, r, dtype=torch.bfloat16, device=dev)
+    rws = torch.empty(lib.mom_route_workspace_size(B, S, d, r, nb, _lib.BF16), dtype=torch.uint8, device=dev)
+
+    def route_once():
+        _lib.call("mom_route_fwd", xb.data_ptr(), _lib.BF16, B, S, d, wd.data_ptr(), wu.data_ptr(),
+                  _lib.BF16, r, nb, top, None, 0, probs_o.data_ptr(), idx_o.data_ptr(), _lib.I64,
+                  gates_o.data_ptr(), None, act_o.data_ptr(), rws.data_ptr(), rws.numel(), st)
+
+    def timed(fn, iters):
+        for _ in range(3):
+            fn()
+        times = []
+        for i in range(iters):
+            flush.fill_(float(i))
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            times.append((a, b))
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in times) / iters
+
+    iters = max(10, min(100, args.steps))
+    t_read = timed(read_once, iters)
+    t_route = timed(route_once, iters)
+    fwd_f, bwd_f = read_flops(N, d, top, bs)
+    rb = router_bytes(N, d, nb, top, r)
+    pk = peaks()
+    return {
+        "read": {"ms": round(t_read, 4), "flops": fwd_f + bwd_f,
+                 "tflops": round((fwd_f + bwd_f) / (t_read / 1e3) / 1e12, 2),
+                 "tokens_per_s": round(N / (t_read / 1e3), 1)},
+        "router": {"ms": round(t_route, 4), "bytes": rb,
+                   "gbs": round(rb / (t_route / 1e3) / 1e9, 1),
+                   "frac_of_hbm": round(rb / (t_route / 1e3) / 1e9 / pk["hbm"], 4),
+                   "hbm_peak_gbs": pk["hbm"]},
+    }
+
+
+def measure_e2e(step, x, dout, dev, args, world, N):
+    """The same step through the public API with host buffers: per step, the
+    inputs (x, upstream grad) come from pinned host memory and dx goes back."""
+    import torch
+    import torch.distributed as dist
+    xh = x.detach().cpu().pin_memory()
+    gh = dout.cpu().pin_memory()
+    dxh = torch.empty_like(xh).pin_memory()
+    xd = torch.empty_like(x.detach()).requires_grad_(True)
+    gd = torch.empty_like(dout)
+    iters = max(5, min(50, args.steps))
+
+    def one():
+        with torch.no_grad():
+            xd.copy_(xh, non_blocking=True)
+            gd.copy_(gh, non_blocking=True)
+        step(xd, gd)
+        dxh.copy_(xd.grad, non_blocking=True)
+
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    nbytes = xh.numel() * xh.element_size()
+    return {"value": round(world * N * iters / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": 2 * nbytes, "d2h_bytes_per_step": nbytes}
+
+
+# ------------------------------------------------------------------ CPU arms
+def _cpu_step_inputs(S_sample):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    import golden_inputs as gi
+    import mom_oracle as O
+    c = CFG
+    geo = dict(B=1, S=S_sample, d=c["d"], H=c["H"], nb=c["nb"], bs=c["bs"], top=c["top"], r=c["r"],
+               seed=0, x_std=1.0, m_std=0.02, w_std=0.02, mom_scale=1.0)
+    inp = gi.layer_inputs(geo)
+    return O, inp["x"].numpy(), gi.oracle_params(inp, geo), gi.upstream_grad(geo).numpy()
+
+
+def cpu_baseline(samples=3, S_sample=2048):
+    """The oracle port of the reference's eager layer step (fp32, dense over
+    all L slots) on this host's cores, a bounded sample of the workload."""
+    O, x, P, g = _cpu_step_inputs(S_sample)
+    c = CFG
+    O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])   # warm-up
+    t = time.perf_counter()
+    for _ in range(samples):
+        O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])
+    dt = (time.perf_counter() - t) / samples
+    return {"value": round(S_sample / dt, 1), "unit": "tokens/s", "cores": os.cpu_count(),
+            "kind": "port",
+            "sample": f"{samples} x one 1x{S_sample}-token sequence of the cfg2 layer, fwd+bwd, fp32 numpy "
+                      f"(oracle/mom_oracle.py layer_step_fp32; BLAS threads = all cores)"}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    S_sample = 2048
+    O, x, P, g = _cpu_step_inputs(S_sample)
+    c = CFG
+    for _ in range(min(args.warmup, 1)):
+        O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])
+    steps = args.steps if args.steps <= 5 else 5
+    t = time.perf_counter()
+    for _ in range(steps):
+        O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])
+    dt = (time.perf_counter() - t) / steps
+    val = round(S_sample / dt, 1)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
+        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": round(dt * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": S_sample,
+                                        "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"one 1x{S_sample}-token sequence per step (the reference's eager "
+                                   f"layer math restated in fp32 numpy, oracle/mom_oracle.py)"},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="sm100", choices=["sm100", "reference"])
+    ap.add_argument("--cpu-samples", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,153 @@
+/*
+ * naylis_mom.h — C ABI of the B200 (sm_100a) Mixture-of-Memory hot path.
+ *
+ * Every entry point takes plain device pointers, int64 sizes, dtype enums and
+ * a CUDA stream passed as `void *` (a cudaStream_t; NULL = legacy default
+ * stream). No call allocates device memory, synchronises the host or throws:
+ * the caller owns every buffer (workspace sizes are queried first) and each
+ * call returns an `int` status (mom_status). The library holds no device
+ * memory across calls.
+ *
+ * The entry points replace the reference's Python-level hot path; each
+ * declaration names the reference interface it stands in for.
+ */
+#ifndef NAYLIS_MOM_H
+#define NAYLIS_MOM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOM_API __attribute__((visibility("default")))
+#else
+#define MOM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    MOM_OK = 0,
+    MOM_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad size, inconsistent geometry   */
+    MOM_ERR_UNSUPPORTED = 2,      /* valid request outside what the kernels implement */
+    MOM_ERR_ARCH = 3,             /* current device is not sm_100                     */
+    MOM_ERR_WORKSPACE = 4,        /* workspace / plan buffer smaller than required    */
+    MOM_ERR_LAUNCH = 5,           /* a kernel launch failed (message has the CUDA error) */
+    MOM_ERR_DEVICE_TIMEOUT = 6,   /* a bounded device-side wait gave up               */
+    MOM_ERR_DEVICE_INDEX = 7      /* a kernel saw a routing index outside [0, nb)     */
+} mom_status;
+
+typedef enum { MOM_F32 = 0, MOM_BF16 = 1, MOM_I32 = 2, MOM_I64 = 3 } mom_dtype;
+
+typedef enum {
+    MOM_SCAN_FP64 = 0, /* sequential fp64 accumulation per column (torch CPU cumsum)          */
+    MOM_SCAN_FP32 = 1  /* sequential fp32 accumulation per column (torch CUDA outer-dim scan) */
+} mom_scan_mode;
+
+/* Library version (major*10000 + minor*100 + patch). */
+MOM_API int mom_version(void);
+
+/* Number of kernels this library has launched since it was loaded (telemetry). */
+MOM_API uint64_t mom_kernel_launches(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+MOM_API const char *mom_last_error_string(void);
+
+/* MOM_OK when `device` is an sm_100 GPU this build has code for.
+ * Stands in for mom_kernels/__init__.py:37-53 (preflight) on the native side. */
+MOM_API int mom_device_check(int device);
+
+/* ------------------------------------------------------------------ prefix mean
+ * h[b,t,:] = cumsum_{i<=t} x[b,i,:] / (t+1), rounded to out_dtype (F32|BF16).
+ * Replaces mom_kernels/reference.py:32-36 (prefix_mean_reference) and
+ * model.py:169-176 (MoMLayer._prefix_mean); bit-exact to torch.cumsum of the
+ * chosen backend (scan_mode) followed by the fp32 division. */
+MOM_API int mom_prefix_mean(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, void *out,
+                    int out_dtype, int scan_mode, void *stream);
+
+/* ------------------------------------------------------------------ router
+ * Fused causal router forward. Replaces model.py:178-220
+ * (MoMLayer._prefix_mean, _router_logits and the softmax / topk / gate block
+ * of MoMLayer.forward); the reference keeps it inline, outside the
+ * mom_kernels door.
+ *
+ *   h      = cumsum_t(x) / (t+1)      (exact: scan_mode picks the backend semantics)
+ *   z      = round_cd(round_cd(h) . w_down^T)         w_down (r, d)
+ *   act    = round_cd(tanh(z))                        saved for the backward
+ *   logits = float(round_cd(act . w_up^T))            w_up (nb, r)
+ *   probs  = softmax(logits)
+ *   top_idx, top_vals = topk(logits + noise, top)     value desc, ties -> lower index
+ *   gates  = softmax(top_vals);  log_gates = log(max(gates, 1e-9))
+ *
+ * x: (B,S,d) of x_dtype (F32|BF16); w_down/w_up/act of compute_dtype (F32|BF16),
+ * the dtype the router linears run in (BF16 under autocast). noise: (B,S,nb)
+ * fp32 or NULL. top_idx of idx_dtype (I32|I64). log_gates and act may be NULL.
+ */
+MOM_API size_t mom_route_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb,
+                                int compute_dtype);
+MOM_API int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d,
+                  const void *w_down, const void *w_up, int compute_dtype,
+                  int64_t r, int64_t nb, int64_t top, const float *noise, int scan_mode,
+                  float *probs, void *top_idx, int idx_dtype, float *gates,
+                  float *log_gates, void *act, void *workspace, size_t workspace_bytes,
+                  void *stream);
+
+/* Router backward: autograd of the block above (model.py:186-220).
+ * dlog_gates (B,S,top): gradient w.r.t. log_gates, or NULL; dgates: w.r.t. gates,
+ * or NULL; dprobs (B,S,nb): w.r.t. probs (the aux load-balance loss), or NULL.
+ * Outputs: dx (B,S,d) of dx_dtype (F32|BF16; accumulated into when
+ * accumulate_dx != 0), dw_down (r,d) fp32, dw_up (nb,r) fp32.
+ * The reverse scan runs in rank-r space: dx_t = w_down^T sum_{s>=t} dz_s/(s+1). */
+MOM_API size_t mom_route_bwd_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb);
+MOM_API int mom_route_bwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d,
+                  const void *w_down, const void *w_up, int compute_dtype, int64_t r,
+                  int64_t nb, int64_t top, const float *probs, const void *top_idx,
+                  int idx_dtype, const float *gates, const void *act,
+                  const float *dlog_gates, const float *dgates, const float *dprobs,
+                  void *dx, int dx_dtype, int accumulate_dx, float *dw_down, float *dw_up,
+                  void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------ bucketing
+ * Routing permutation: groups the N = B*S tokens by the SET of blocks they
+ * selected, into tiles of at most tile_m tokens that all read the same blocks.
+ * The reference has no counterpart (its kernels read all L slots for every
+ * token, mom_kernels/triton_gpu.py:98-133); it turns the per-token hard mask
+ * into block skipping. The plan is an opaque device buffer of
+ * mom_plan_size() bytes, consumed by mom_read_fwd / mom_read_bwd.
+ * top_idx (N, top) of idx_dtype, log_gates (N, top) fp32. */
+MOM_API size_t mom_plan_size(int64_t N, int64_t nb, int64_t top);
+MOM_API int mom_bucket(const void *top_idx, int idx_dtype, const float *log_gates, int64_t N,
+               int64_t nb, int64_t top, void *plan, size_t plan_bytes, void *stream);
+
+/* ------------------------------------------------------------------ memory read
+ * Gated memory read forward. Replaces mom_kernels/__init__.py:87-102
+ * (mom_read) -> mom_kernels/triton_gpu.py:323-356 (_MomReadFunction.forward).
+ * q (B,S,H,hd) and out of dtype (BF16); k, v: the shared bank projections
+ * (L, H*hd), L = nb*bs; lse (B*S, H) fp32 saved for the backward.
+ * `plan` comes from mom_bucket on the same routing. */
+MOM_API int mom_read_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B,
+                 int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top,
+                 const void *plan, void *out, float *lse, void *stream);
+
+/* Gated memory read backward. Replaces mom_kernels/triton_gpu.py:358-409
+ * (_MomReadFunction.backward). Produces dq (B,S,H,hd) of dtype, dk_acc and
+ * dv_acc (L, H*hd) fp32 (overwritten), dlog_gates (B*S, top) fp32 in the
+ * caller's top order (gradient w.r.t. log(max(gate, 1e-9))). */
+MOM_API size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H);
+MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void *out,
+                 const void *dout, const float *lse, int dtype, int64_t B, int64_t S,
+                 int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top,
+                 const void *plan, void *dq, float *dk_acc, float *dv_acc,
+                 float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Reads (and clears) the device error word of a plan: MOM_OK, or
+ * MOM_ERR_DEVICE_INDEX when mom_bucket saw an index outside [0, nb).
+ * Synchronises `stream`. */
+MOM_API int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NAYLIS_MOM_H */

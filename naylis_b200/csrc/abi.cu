@@ -1,0 +1,316 @@
+// extern "C" entry points of libnaylis_mom.so (declared in include/naylis_mom.h).
+//
+// This layer validates every argument, turns CUDA errors into status codes
+// with a thread-local message, and forwards to the launchers. It allocates
+// nothing and never synchronises the host, except mom_plan_check, whose job
+// is to read the plan's device error word.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace mom {
+static std::atomic<uint64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(static_cast<uint64_t>(n), std::memory_order_relaxed); }
+uint64_t launches() { return g_launches.load(std::memory_order_relaxed); }
+}  // namespace mom
+
+namespace {
+
+thread_local char g_err[512] = {0};
+
+int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *where) {
+    return fail(MOM_ERR_LAUNCH, "%s: %s (%s)", where, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool is_float_dtype(int dt) { return dt == MOM_F32 || dt == MOM_BF16; }
+bool is_idx_dtype(int dt) { return dt == MOM_I32 || dt == MOM_I64; }
+size_t dt_size(int dt) { return (dt == MOM_BF16) ? 2 : (dt == MOM_I64 ? 8 : 4); }
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// sm_100 check of the current device, cached per device.
+int check_current_device() {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    static std::mutex mu;
+    static int cache[64];
+    static bool init = false;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!init) {
+        for (int &c : cache) c = -1;
+        init = true;
+    }
+    if (dev >= 0 && dev < 64 && cache[dev] >= 0)
+        return cache[dev] ? MOM_OK : fail(MOM_ERR_ARCH, "device %d is not sm_100", dev);
+    int major = 0, minor = 0;
+    if ((e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute");
+    if ((e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess)
+        return cuda_fail(e, "cudaDeviceGetAttribute");
+    const bool ok = major == 10 && minor == 0;
+    if (dev >= 0 && dev < 64) cache[dev] = ok ? 1 : 0;
+    return ok ? MOM_OK
+              : fail(MOM_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a only",
+                     dev, major, minor);
+}
+
+#define MOM_REQUIRE(cond, ...)                                  \
+    do {                                                        \
+        if (!(cond)) return fail(MOM_ERR_INVALID_ARGUMENT, __VA_ARGS__); \
+    } while (0)
+
+int check_router_geometry(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb, int64_t top) {
+    MOM_REQUIRE(B >= 0 && S >= 0, "B and S must be >= 0 (got %lld, %lld)", (long long)B, (long long)S);
+    MOM_REQUIRE(d > 0 && d % 8 == 0, "d_model must be a positive multiple of 8 (got %lld)", (long long)d);
+    MOM_REQUIRE(r > 0 && r <= 128, "router_rank must be in [1, 128] (got %lld)", (long long)r);
+    MOM_REQUIRE(nb > 0 && nb <= 64, "num_blocks must be in [1, 64] (got %lld)", (long long)nb);
+    MOM_REQUIRE(top > 0 && top <= 8 && top <= nb, "top_blocks must be in [1, min(8, num_blocks)] (got %lld)",
+                (long long)top);
+    MOM_REQUIRE(B * S < (int64_t(1) << 31), "B*S too large");
+    MOM_REQUIRE(S < (int64_t(1) << 24), "sequence length too large for the fp32 divisor");
+    return MOM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mom_version(void) { return 100; }
+
+uint64_t mom_kernel_launches(void) { return mom::launches(); }
+
+const char *mom_last_error_string(void) { return g_err; }
+
+int mom_device_check(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(MOM_ERR_INVALID_ARGUMENT, "no CUDA device %d", device);
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device);
+    if (major != 10 || minor != 0)
+        return fail(MOM_ERR_ARCH, "device %d is sm_%d%d; this library is built for sm_100a only",
+                    device, major, minor);
+    return MOM_OK;
+}
+
+// ------------------------------------------------------------------ prefix mean
+int mom_prefix_mean(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, void *out,
+                    int out_dtype, int scan_mode, void *stream) {
+    MOM_REQUIRE(B >= 0 && S >= 0 && S < (int64_t(1) << 24), "bad B, S");
+    MOM_REQUIRE(d > 0 && d % 8 == 0, "d must be a positive multiple of 8 (got %lld)", (long long)d);
+    MOM_REQUIRE(is_float_dtype(x_dtype) && is_float_dtype(out_dtype), "dtypes must be F32 or BF16");
+    MOM_REQUIRE(scan_mode == MOM_SCAN_FP64 || scan_mode == MOM_SCAN_FP32, "unknown scan mode %d", scan_mode);
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(x && out, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_route_scan(x, x_dtype, out, out_dtype, (int)B, (int)S, (int)d, scan_mode,
+                                           static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "prefix_mean");
+}
+
+// ------------------------------------------------------------------ router
+size_t mom_route_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb,
+                                int compute_dtype) {
+    (void)r;
+    (void)nb;
+    if (B < 0 || S < 0 || d < 0 || !is_float_dtype(compute_dtype)) return 0;
+    return align256(static_cast<size_t>(B) * S * d * dt_size(compute_dtype));
+}
+
+int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
+                  const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
+                  const float *noise, int scan_mode, float *probs, void *top_idx, int idx_dtype,
+                  float *gates, float *log_gates, void *act, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+    int rc = check_router_geometry(B, S, d, r, nb, top);
+    if (rc) return rc;
+    MOM_REQUIRE(is_float_dtype(x_dtype), "x dtype must be F32 or BF16");
+    MOM_REQUIRE(is_float_dtype(compute_dtype), "compute dtype must be F32 or BF16");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(scan_mode == MOM_SCAN_FP64 || scan_mode == MOM_SCAN_FP32, "unknown scan mode %d", scan_mode);
+    const int64_t N = B * S;
+    if (N == 0) return MOM_OK;
+    MOM_REQUIRE(x && w_down && w_up && probs && top_idx && gates, "null pointer argument");
+    const size_t need = mom_route_workspace_size(B, S, d, r, nb, compute_dtype);
+    if (workspace_bytes < need || (need && !workspace))
+        return fail(MOM_ERR_WORKSPACE, "route workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = mom::launch_route_scan(x, x_dtype, workspace, compute_dtype, (int)B, (int)S, (int)d,
+                                           scan_mode, st);
+    if (e != cudaSuccess) return cuda_fail(e, "route_scan");
+    e = mom::launch_route_head(workspace, w_down, w_up, compute_dtype, N, (int)d, (int)r, (int)nb,
+                               (int)top, noise, probs, top_idx, idx_dtype == MOM_I64, gates,
+                               log_gates, act, st);
+    if (e != cudaSuccess) return cuda_fail(e, "route_head");
+    return MOM_OK;
+}
+
+size_t mom_route_bwd_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb) {
+    (void)d;
+    if (B < 0 || S < 0 || r < 0 || nb < 0) return 0;
+    const size_t N = static_cast<size_t>(B) * S;
+    return align256(N * nb * 4) + 2 * align256(N * r * 4);
+}
+
+int mom_route_bwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
+                  const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
+                  const float *probs, const void *top_idx, int idx_dtype, const float *gates,
+                  const void *act, const float *dlog_gates, const float *dgates,
+                  const float *dprobs, void *dx, int dx_dtype, int accumulate_dx, float *dw_down,
+                  float *dw_up, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_router_geometry(B, S, d, r, nb, top);
+    if (rc) return rc;
+    MOM_REQUIRE(is_float_dtype(x_dtype) && is_float_dtype(compute_dtype) && is_float_dtype(dx_dtype),
+                "x / compute / dx dtypes must be F32 or BF16");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(x && w_down && w_up && probs && top_idx && gates && act && dx && dw_down && dw_up,
+                "null pointer argument");
+    const size_t need = mom_route_bwd_workspace_size(B, S, d, r, nb);
+    if (workspace_bytes < need || !workspace)
+        return fail(MOM_ERR_WORKSPACE, "route bwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    const size_t N = static_cast<size_t>(B) * S;
+    char *ws = static_cast<char *>(workspace);
+    float *dlogits = reinterpret_cast<float *>(ws);
+    float *dz = reinterpret_cast<float *>(ws + align256(N * nb * 4));
+    float *u = reinterpret_cast<float *>(ws + align256(N * nb * 4) + align256(N * r * 4));
+    cudaError_t e = mom::launch_route_bwd(
+        x, x_dtype, (int)B, (int)S, (int)d, w_down, w_up, compute_dtype, (int)r, (int)nb, (int)top,
+        probs, top_idx, idx_dtype == MOM_I64, gates, act, dlog_gates, dgates, dprobs, dx, dx_dtype,
+        accumulate_dx, dw_down, dw_up, dlogits, dz, u, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "route_bwd");
+    return MOM_OK;
+}
+
+// ------------------------------------------------------------------ bucketing
+size_t mom_plan_size(int64_t N, int64_t nb, int64_t top) {
+    if (N < 0 || nb <= 0 || nb > 64 || top <= 0 || top > 8 || top > nb) return 0;
+    if (mom::num_route_keys(nb, top) > mom::kMaxKeys) return 0;
+    return mom::plan_layout(N, nb, top).total;
+}
+
+int mom_bucket(const void *top_idx, int idx_dtype, const float *log_gates, int64_t N, int64_t nb,
+               int64_t top, void *plan, size_t plan_bytes, void *stream) {
+    MOM_REQUIRE(N >= 0 && N < (int64_t(1) << 31), "token count out of range");
+    MOM_REQUIRE(nb > 0 && nb <= 64 && top > 0 && top <= 8 && top <= nb, "bad (num_blocks, top)");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    const int64_t keys = mom::num_route_keys(nb, top);
+    if (keys > mom::kMaxKeys)
+        return fail(MOM_ERR_UNSUPPORTED,
+                    "%lld routing sets for top-%lld of %lld blocks exceed the %d the set bucketing supports",
+                    (long long)keys, (long long)top, (long long)nb, mom::kMaxKeys);
+    const mom::PlanLayout L = mom::plan_layout(N, nb, top);
+    MOM_REQUIRE(plan, "null plan");
+    if (plan_bytes < L.total) return fail(MOM_ERR_WORKSPACE, "plan %zu < %zu bytes", plan_bytes, L.total);
+    MOM_REQUIRE(N == 0 || (top_idx && log_gates), "null routing tensors");
+    int rc = check_current_device();
+    if (rc) return rc;
+    const mom::PlanView P = mom::plan_view(plan, L);
+    cudaError_t e = mom::launch_bucket(top_idx, idx_dtype == MOM_I64, log_gates, L, P,
+                                       static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "bucket");
+    return MOM_OK;
+}
+
+int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *stream) {
+    MOM_REQUIRE(plan, "null plan");
+    const mom::PlanLayout L = mom::plan_layout(N, nb, top);
+    const mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    int err = 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&err, P.err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "plan_check");
+    if (err) {
+        cudaMemsetAsync(P.err, 0, sizeof(int), st);
+        return fail(MOM_ERR_DEVICE_INDEX, "top_idx holds a block index outside [0, %lld)", (long long)nb);
+    }
+    return MOM_OK;
+}
+
+// ------------------------------------------------------------------ read
+static int check_read_geometry(int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb,
+                               int64_t bs, int64_t top) {
+    MOM_REQUIRE(dtype == MOM_BF16, "the read kernels take bf16 activations (got dtype %d)", dtype);
+    MOM_REQUIRE(B >= 0 && S >= 0 && B * S < (int64_t(1) << 31), "bad B, S");
+    MOM_REQUIRE(H > 0 && H <= 1024, "bad n_heads %lld", (long long)H);
+    if (hd != 64 && hd != 128)
+        return fail(MOM_ERR_UNSUPPORTED, "head_dim %lld: the sm_100a read kernels take 64 or 128",
+                    (long long)hd);
+    MOM_REQUIRE(nb > 0 && nb <= 64 && top > 0 && top <= 8 && top <= nb, "bad (num_blocks, top)");
+    MOM_REQUIRE(bs > 0 && nb * bs < (int64_t(1) << 24), "bad block_size %lld", (long long)bs);
+    if (mom::num_route_keys(nb, top) > mom::kMaxKeys)
+        return fail(MOM_ERR_UNSUPPORTED, "top-%lld of %lld blocks: too many routing sets", (long long)top,
+                    (long long)nb);
+    return MOM_OK;
+}
+
+int mom_read_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B, int64_t S,
+                 int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top, const void *plan,
+                 void *out, float *lse, void *stream) {
+    int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(q && k && v && plan && out && lse, "null pointer argument");
+    if ((rc = check_current_device())) return rc;
+    const mom::PlanLayout L = mom::plan_layout(B * S, nb, top);
+    const mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    cudaError_t e = mom::launch_read_fwd(q, k, v, (int)B, (int)S, (int)H, (int)hd, (int)nb, (int)bs,
+                                         (int)top, L, P, out, lse, static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "read_fwd");
+    return MOM_OK;
+}
+
+size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H) {
+    if (B < 0 || S < 0 || H < 0) return 0;
+    return align256(static_cast<size_t>(B) * S * H * 4);
+}
+
+int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, const void *dout,
+                 const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd,
+                 int64_t nb, int64_t bs, int64_t top, const void *plan, void *dq, float *dk_acc,
+                 float *dv_acc, float *dlog_gates, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+    int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    MOM_REQUIRE(k && v && dk_acc && dv_acc, "null pointer argument");
+    MOM_REQUIRE(B * S == 0 || (q && out && dout && lse && plan && dq && dlog_gates), "null pointer argument");
+    const size_t need = mom_read_bwd_workspace_size(B, S, H);
+    if (workspace_bytes < need || (need && !workspace))
+        return fail(MOM_ERR_WORKSPACE, "read bwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    if (B * S == 0) {
+        const size_t kv = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        cudaError_t e = cudaMemsetAsync(dk_acc, 0, kv, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(dv_acc, 0, kv, st);
+        return e == cudaSuccess ? MOM_OK : cuda_fail(e, "read_bwd");
+    }
+    const mom::PlanLayout L = mom::plan_layout(B * S, nb, top);
+    const mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    cudaError_t e = mom::launch_read_bwd(q, k, v, out, dout, lse, (int)B, (int)S, (int)H, (int)hd,
+                                         (int)nb, (int)bs, (int)top, L, P, dq, dk_acc, dv_acc,
+                                         dlog_gates, static_cast<float *>(workspace),
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "read_bwd");
+    return MOM_OK;
+}
+
+}  // extern "C"

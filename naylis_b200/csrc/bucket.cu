@@ -1,0 +1,310 @@
+// Routing permutation: a stable counting sort of the tokens by the set of
+// memory blocks they selected, cut into tiles of at most kTileM tokens that
+// all read the same blocks. This is what lets the read touch only the
+// selected slots (top*bs per token) instead of all L slots with a mask, as
+// the reference kernels do (mom_kernels/triton_gpu.py:98-133).
+//
+// Three launches, no host synchronisation:
+//   bucket_keys    per token: validated, sorted set -> key; per-chunk histogram
+//   bucket_scan    one CTA: key totals, offsets, tiles, per-block tile lists
+//   bucket_scatter per token: stable rank inside its chunk -> permuted row,
+//                  with the row's per-block biases and the caller-order map.
+#include "common.cuh"
+#include "launch.h"
+
+namespace mom {
+
+__host__ __device__ inline uint64_t binom(int n, int k) {
+    if (k < 0 || k > n) return 0;
+    if (k > n - k) k = n - k;
+    uint64_t r = 1;
+    for (int i = 1; i <= k; ++i) r = r * static_cast<uint64_t>(n - k + i) / static_cast<uint64_t>(i);
+    return r;
+}
+
+int64_t num_route_keys(int64_t nb, int64_t top) {
+    uint64_t n = 0;
+    for (int s = 0; s <= top; ++s) n += binom(static_cast<int>(nb), s);
+    return static_cast<int64_t>(n);
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+PlanLayout plan_layout(int64_t N, int64_t nb, int64_t top) {
+    PlanLayout L;
+    L.N = N;
+    L.nb = nb;
+    L.top = top;
+    L.num_keys = num_route_keys(nb, top);
+    L.chunks = (N + kBucketChunk - 1) / kBucketChunk;
+    L.max_tiles = (N + kTileM - 1) / kTileM + std::min<int64_t>(N, L.num_keys);
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t at = o; o = align256(o + bytes); return at; };
+    L.off_err = take(sizeof(int));
+    L.off_ntiles = take(sizeof(int));
+    L.off_key = take(sizeof(int) * N);
+    L.off_hist = take(sizeof(int) * L.chunks * L.num_keys);
+    L.off_keytot = take(sizeof(int) * L.num_keys);
+    L.off_keybase = take(sizeof(int) * L.num_keys);
+    L.off_keytb = take(sizeof(int) * L.num_keys);
+    L.off_keyset = take(sizeof(int) * L.num_keys * top);
+    L.off_perm = take(sizeof(int) * N);
+    L.off_rowbias = take(sizeof(float) * N * top);
+    L.off_rowkmap = take(sizeof(uint32_t) * N);
+    L.off_tiles = take(sizeof(int4) * L.max_tiles);
+    L.off_blkcount = take(sizeof(int) * nb);
+    L.off_blktiles = take(sizeof(int) * nb * L.max_tiles);
+    L.total = o;
+    return L;
+}
+
+PlanView plan_view(void *plan, const PlanLayout &L) {
+    char *p = static_cast<char *>(plan);
+    PlanView v;
+    v.err = reinterpret_cast<int *>(p + L.off_err);
+    v.ntiles = reinterpret_cast<int *>(p + L.off_ntiles);
+    v.key = reinterpret_cast<int *>(p + L.off_key);
+    v.hist = reinterpret_cast<int *>(p + L.off_hist);
+    v.keytot = reinterpret_cast<int *>(p + L.off_keytot);
+    v.keybase = reinterpret_cast<int *>(p + L.off_keybase);
+    v.keytb = reinterpret_cast<int *>(p + L.off_keytb);
+    v.keyset = reinterpret_cast<int *>(p + L.off_keyset);
+    v.perm = reinterpret_cast<int *>(p + L.off_perm);
+    v.rowbias = reinterpret_cast<float *>(p + L.off_rowbias);
+    v.rowkmap = reinterpret_cast<uint32_t *>(p + L.off_rowkmap);
+    v.tiles = reinterpret_cast<int4 *>(p + L.off_tiles);
+    v.blkcount = reinterpret_cast<int *>(p + L.off_blkcount);
+    v.blktiles = reinterpret_cast<int *>(p + L.off_blktiles);
+    return v;
+}
+
+// The distinct, ascending set of blocks of one token (invalid entries dropped).
+struct TokenSet {
+    int blk[8];
+    int n;
+    bool bad;
+};
+
+__device__ __forceinline__ int load_idx(const void *top_idx, int idx64, int64_t i) {
+    if (idx64) {
+        const int64_t v = reinterpret_cast<const int64_t *>(top_idx)[i];
+        return (v < INT32_MIN || v > INT32_MAX) ? -1 : static_cast<int>(v);
+    }
+    return reinterpret_cast<const int32_t *>(top_idx)[i];
+}
+
+__device__ TokenSet token_set(const void *top_idx, int idx64, int64_t t, int nb, int top) {
+    TokenSet s;
+    s.n = 0;
+    s.bad = false;
+    for (int k = 0; k < top; ++k) {
+        const int b = load_idx(top_idx, idx64, t * top + k);
+        if (b < 0 || b >= nb) { s.bad = true; continue; }
+        int pos = 0;
+        bool dup = false;
+        while (pos < s.n && s.blk[pos] <= b) { dup |= s.blk[pos] == b; ++pos; }
+        if (dup) continue;
+        for (int q = s.n; q > pos; --q) s.blk[q] = s.blk[q - 1];
+        s.blk[pos] = b;
+        ++s.n;
+    }
+    return s;
+}
+
+__device__ int set_key(const TokenSet &s, int nb) {
+    uint64_t off = 0;
+    for (int q = 0; q < s.n; ++q) off += binom(nb, q);
+    uint64_t rank = 0;
+    for (int q = 0; q < s.n; ++q) rank += binom(s.blk[q], q + 1);
+    return static_cast<int>(off + rank);
+}
+
+__global__ void __launch_bounds__(kBucketChunk)
+bucket_keys_kernel(const void *__restrict__ top_idx, int idx64, int64_t N, int nb, int top,
+                   int num_keys, PlanView P) {
+    extern __shared__ int s_hist[];
+    for (int i = threadIdx.x; i < num_keys; i += blockDim.x) s_hist[i] = 0;
+    __syncthreads();
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kBucketChunk + threadIdx.x;
+    if (t < N) {
+        const TokenSet s = token_set(top_idx, idx64, t, nb, top);
+        if (s.bad) atomicOr(P.err, 1);
+        const int key = set_key(s, nb);
+        P.key[t] = key;
+        atomicAdd(&s_hist[key], 1);
+    }
+    __syncthreads();
+    int *h = P.hist + static_cast<int64_t>(blockIdx.x) * num_keys;
+    for (int i = threadIdx.x; i < num_keys; i += blockDim.x) h[i] = s_hist[i];
+}
+
+// Exclusive block-wide scan of one value per thread (blockDim.x == 1024).
+__device__ int block_exclusive_scan(int v, int *s_tmp, int &total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) s_tmp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < (blockDim.x >> 5) ? s_tmp[lane] : 0;
+        int wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += n;
+        }
+        s_tmp[32 + lane] = wi - w;
+        if (lane == 31) s_tmp[64] = wi;
+    }
+    __syncthreads();
+    const int res = s_tmp[32 + warp] + incl - v;
+    total = s_tmp[64];
+    __syncthreads();
+    return res;
+}
+
+__global__ void __launch_bounds__(1024)
+bucket_scan_kernel(int64_t N, int nb, int top, int num_keys, int chunks, int max_tiles, PlanView P) {
+    __shared__ int s_tmp[96];
+    const int tid = threadIdx.x;
+    const int per = (num_keys + 1023) / 1024;
+    const int k0 = min(num_keys, tid * per), k1 = min(num_keys, k0 + per);
+    // key totals and per-chunk offsets (relative to the key's base for now)
+    int rows = 0, tiles = 0;
+    for (int k = k0; k < k1; ++k) {
+        int run = 0;
+        for (int c = 0; c < chunks; ++c) {
+            int *h = P.hist + static_cast<int64_t>(c) * num_keys + k;
+            const int n = *h;
+            *h = run;
+            run += n;
+        }
+        P.keytot[k] = run;
+        rows += run;
+        tiles += (run + kTileM - 1) / kTileM;
+    }
+    int total_rows, total_tiles;
+    int row_base = block_exclusive_scan(rows, s_tmp, total_rows);
+    int tile_base = block_exclusive_scan(tiles, s_tmp, total_tiles);
+    for (int k = k0; k < k1; ++k) {
+        const int n = P.keytot[k];
+        P.keybase[k] = row_base;
+        P.keytb[k] = tile_base;
+        for (int c = 0; c < chunks; ++c) P.hist[static_cast<int64_t>(c) * num_keys + k] += row_base;
+        const int nt = (n + kTileM - 1) / kTileM;
+        for (int j = 0; j < nt; ++j)
+            P.tiles[tile_base + j] = make_int4(row_base + j * kTileM, min(kTileM, n - j * kTileM), k, 0);
+        row_base += n;
+        tile_base += nt;
+        // decode the key into its block set
+        int s = 0;
+        uint64_t off = 0;
+        while (s < top && off + binom(nb, s) <= static_cast<uint64_t>(k)) { off += binom(nb, s); ++s; }
+        uint64_t rank = static_cast<uint64_t>(k) - off;
+        int *set = P.keyset + static_cast<int64_t>(k) * top;
+        for (int q = top - 1; q >= 0; --q) set[q] = -1;
+        for (int q = s - 1; q >= 0; --q) {
+            int b = q;
+            while (b + 1 < nb && binom(b + 1, q + 1) <= rank) ++b;
+            set[q] = b;
+            rank -= binom(b, q + 1);
+        }
+    }
+    if (tid == 0) *P.ntiles = total_tiles;
+    __syncthreads();
+    // per-block tile lists, in key order (warp per block)
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int b = warp; b < nb; b += 32) {
+        int count = 0;
+        for (int kb = 0; kb < num_keys; kb += 32) {
+            const int k = kb + lane;
+            int nt = 0;
+            if (k < num_keys) {
+                const int *set = P.keyset + static_cast<int64_t>(k) * top;
+                bool member = false;
+                for (int q = 0; q < top; ++q) member |= set[q] == b;
+                if (member) nt = (P.keytot[k] + kTileM - 1) / kTileM;
+            }
+            int incl = nt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += n;
+            }
+            const int base = count + incl - nt;
+            for (int j = 0; j < nt; ++j)
+                P.blktiles[static_cast<int64_t>(b) * max_tiles + base + j] = P.keytb[k] + j;
+            count += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) P.blkcount[b] = count;
+    }
+}
+
+__global__ void __launch_bounds__(kBucketChunk)
+bucket_scatter_kernel(const void *__restrict__ top_idx, int idx64, const float *__restrict__ log_gates,
+                      int64_t N, int nb, int top, int num_keys, PlanView P) {
+    extern __shared__ int s_run[];
+    for (int i = threadIdx.x; i < num_keys; i += blockDim.x) s_run[i] = 0;
+    __syncthreads();
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kBucketChunk + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int key = t < N ? P.key[t] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    int pos = -1;
+    for (int w = 0; w < (kBucketChunk >> 5); ++w) {
+        if (warp == w && key >= 0) {
+            pos = s_run[key] + rank;
+            __syncwarp(peers);
+            if (lane == leader) s_run[key] += __popc(peers);
+        }
+        __syncthreads();
+    }
+    if (t >= N) return;
+    pos += P.hist[static_cast<int64_t>(blockIdx.x) * num_keys + key];
+    P.perm[pos] = static_cast<int>(t);
+    const int *set = P.keyset + static_cast<int64_t>(key) * top;
+    uint32_t kmap = 0xFFFFFFFFu;
+    for (int j = 0; j < top; ++j) P.rowbias[static_cast<int64_t>(pos) * top + j] = 0.0f;
+    for (int k = 0; k < top; ++k) {
+        const int b = load_idx(top_idx, idx64, t * top + k);
+        for (int j = 0; j < top; ++j) {
+            if (set[j] >= 0 && set[j] == b) {
+                P.rowbias[static_cast<int64_t>(pos) * top + j] += log_gates[t * top + k];
+                kmap = (kmap & ~(0xFu << (4 * k))) | (static_cast<uint32_t>(j) << (4 * k));
+            }
+        }
+    }
+    P.rowkmap[pos] = kmap;
+}
+
+cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
+                          const PlanLayout &L, const PlanView &P, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(P.err, 0, sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    if (L.N == 0) return cudaMemsetAsync(P.ntiles, 0, sizeof(int), st);
+    const int nk = static_cast<int>(L.num_keys);
+    const size_t smem = sizeof(int) * nk;
+    if (smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(bucket_keys_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(bucket_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    bucket_keys_kernel<<<static_cast<unsigned>(L.chunks), kBucketChunk, smem, st>>>(
+        top_idx, idx64, L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk, P); count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    bucket_scan_kernel<<<1, 1024, 0, st>>>(L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk,
+                                           static_cast<int>(L.chunks), static_cast<int>(L.max_tiles), P); count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    bucket_scatter_kernel<<<static_cast<unsigned>(L.chunks), kBucketChunk, smem, st>>>(
+        top_idx, idx64, log_gates, L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk, P); count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mom

@@ -1,0 +1,72 @@
+// Host-side launchers shared between the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace mom {
+
+// Kernels launched by this library since it was loaded (all devices/threads).
+void count_launch(int n = 1);
+uint64_t launches();
+
+constexpr int kTileM = 64;        // tokens per read tile (one routing set per tile)
+constexpr int kMaxKeys = 8192;    // routing sets the bucketing supports
+constexpr int kBucketChunk = 1024;
+
+// Routing sets of size s <= top over nb blocks, ranked by the combinatorial
+// number system; key = (number of sets of smaller size) + rank.
+int64_t num_route_keys(int64_t nb, int64_t top);
+
+struct PlanLayout {
+    int64_t N = 0, nb = 0, top = 0, num_keys = 0, chunks = 0, max_tiles = 0;
+    size_t off_err = 0, off_ntiles = 0, off_key = 0, off_hist = 0, off_keytot = 0,
+           off_keybase = 0, off_keytb = 0, off_keyset = 0, off_perm = 0, off_rowbias = 0,
+           off_rowkmap = 0, off_tiles = 0, off_blkcount = 0, off_blktiles = 0, total = 0;
+};
+PlanLayout plan_layout(int64_t N, int64_t nb, int64_t top);
+
+// Device view of a plan (pointers into the caller's buffer).
+struct PlanView {
+    int *err;            // [1]     error word (bit 0: index out of range)
+    int *ntiles;         // [1]     number of tiles
+    int *key;            // [N]     routing-set key of each token
+    int *hist;           // [chunks][num_keys] per-chunk counts -> offsets
+    int *keytot;         // [num_keys]
+    int *keybase;        // [num_keys] first permuted row of each key
+    int *keytb;          // [num_keys] first tile of each key
+    int *keyset;         // [num_keys][top] blocks of each set, ascending, -1 padded
+    int *perm;           // [N]     token of each permuted row
+    float *rowbias;      // [N][top] bias of the j-th block of the row's set
+    uint32_t *rowkmap;   // [N]     4 bits per caller slot k: set position j (0xF = none)
+    int4 *tiles;         // [max_tiles] {first row, rows, key, 0}
+    int *blkcount;       // [nb]
+    int *blktiles;       // [nb][max_tiles] tiles whose set contains block b
+};
+PlanView plan_view(void *plan, const PlanLayout &L);
+
+cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, int S, int d,
+                              int mode, cudaStream_t st);
+cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_up, int cdt,
+                              int64_t ntok, int d, int r, int nb, int top, const float *noise,
+                              float *probs, void *top_idx, int idx64, float *gates,
+                              float *log_gates, void *act, cudaStream_t st);
+cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const void *w_down,
+                             const void *w_up, int cdt, int r, int nb, int top, const float *probs,
+                             const void *top_idx, int idx64, const float *gates, const void *act,
+                             const float *dlog_gates, const float *dgates, const float *dprobs,
+                             void *dx, int dxdt, int accumulate, float *dw_down, float *dw_up,
+                             float *ws_dlogits, float *ws_dz, float *ws_u, cudaStream_t st);
+cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
+                          const PlanLayout &L, const PlanView &P, cudaStream_t st);
+cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
+                            int hd, int nb, int bs, int top, const PlanLayout &L,
+                            const PlanView &P, void *out, float *lse, cudaStream_t st);
+cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const void *out,
+                            const void *dout, const float *lse, int B, int S, int H, int hd,
+                            int nb, int bs, int top, const PlanLayout &L, const PlanView &P,
+                            void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
+                            float *ws_delta, cudaStream_t st);
+
+}  // namespace mom

@@ -1,0 +1,627 @@
+// Causal router of the MoM layer: exact prefix mean, rank-r tanh bottleneck,
+// softmax / top-k / gate softmax, and the backward in rank-r space.
+//
+// Reference semantics: model.py:169-220 (MoMLayer._prefix_mean,
+// _router_logits, forward's softmax/topk/gates block).
+#include "common.cuh"
+#include "launch.h"
+
+namespace mom {
+
+// ============================================================ prefix scan
+// One thread per column of one batch row walks t in order with the carry in a
+// register: the only association that reproduces torch.cumsum bit-for-bit
+// (sequential fp64 on CPU, sequential fp32 on CUDA). Rows are streamed through
+// a ring of shared-memory stages filled by cp.async so that each SM keeps tens
+// of KB of x in flight while the carry chain runs.
+constexpr int kScanCols = 64;    // columns per CTA (one thread each)
+constexpr int kScanRows = 32;    // rows per stage
+constexpr int kScanStages = 8;   // ring depth
+
+template <int XDT, int CDT, int MODE>
+__global__ void __launch_bounds__(kScanCols)
+route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
+                  typename Elem<CDT>::T *__restrict__ hq, int S, int d) {
+    using XT = typename Elem<XDT>::T;
+    constexpr int kRowBytes = kScanCols * sizeof(XT);
+    constexpr int kChunksPerRow = kRowBytes / 16;
+    constexpr int kStageBytes = kScanRows * kRowBytes;
+    extern __shared__ __align__(128) unsigned char smem[];
+
+    const int tid = threadIdx.x;
+    const int c0 = blockIdx.x * kScanCols;
+    const int b = blockIdx.y;
+    const int col = c0 + tid;
+    const XT *xb = x + static_cast<int64_t>(b) * S * d;
+    const int nstage = (S + kScanRows - 1) / kScanRows;
+    const int valid_cols = min(kScanCols, d - c0);
+    const int valid_bytes = valid_cols * static_cast<int>(sizeof(XT));
+
+    auto issue = [&](int s) {
+        if (s < nstage) {
+            const uint32_t base = smem_u32(smem + (s % kScanStages) * kStageBytes);
+            for (int i = tid; i < kScanRows * kChunksPerRow; i += kScanCols) {
+                const int r = i / kChunksPerRow, ch = i % kChunksPerRow;
+                const int t = s * kScanRows + r;
+                int nbytes = 0;
+                const XT *src = xb;
+                if (t < S) {
+                    nbytes = min(16, max(0, valid_bytes - ch * 16));
+                    src = xb + static_cast<int64_t>(t) * d + c0 + ch * (16 / sizeof(XT));
+                    if (nbytes == 0) src = xb;
+                }
+                cp_async16(base + r * kRowBytes + ch * 16, src, nbytes);
+            }
+        }
+        cp_async_commit();
+    };
+
+#pragma unroll 1
+    for (int s = 0; s < kScanStages - 1; ++s) issue(s);
+
+    double acc64 = 0.0;
+    float acc32 = 0.0f;
+    typename Elem<CDT>::T *out = hq + static_cast<int64_t>(b) * S * d + col;
+#pragma unroll 1
+    for (int s = 0; s < nstage; ++s) {
+        cp_async_wait<kScanStages - 2>();
+        __syncthreads();
+        issue(s + kScanStages - 1);
+        const XT *stage = reinterpret_cast<const XT *>(smem + (s % kScanStages) * kStageBytes);
+        const int t0 = s * kScanRows;
+        const int rows = min(kScanRows, S - t0);
+        if (col < d) {
+#pragma unroll 8
+            for (int r = 0; r < rows; ++r) {
+                const float v = Elem<XDT>::load(stage, r * kScanCols + tid);
+                float cs;
+                if (MODE == MOM_SCAN_FP64) {
+                    acc64 = __dadd_rn(acc64, static_cast<double>(v));
+                    cs = __double2float_rn(acc64);
+                } else {
+                    acc32 = __fadd_rn(acc32, v);
+                    cs = acc32;
+                }
+                const float h = __fdiv_rn(cs, static_cast<float>(t0 + r + 1));
+                Elem<CDT>::store(out, static_cast<int64_t>(t0 + r) * d, h);
+            }
+        }
+    }
+    cp_async_wait<0>();
+}
+
+// ============================================================ router head
+// Per token: z = round(hq . Wd^T), act = round(tanh z), logits = round(act . Wu^T),
+// then softmax, top-k (value desc, lower index on ties) and the gate softmax.
+constexpr int kHeadTokens = 64;   // tokens per CTA
+constexpr int kHeadThreads = 128; // 4 warps x 16 tokens (mma path)
+constexpr int kHeadKC = 64;       // d-columns per pipeline step
+constexpr int kMaxNb = 64;
+constexpr int kMaxTop = 8;
+constexpr int kMaxRank = 128;
+
+// Epilogue shared by both head variants: sA holds act (fp32 values already
+// rounded to the compute dtype) for kHeadTokens tokens x r.
+template <int CDT>
+__device__ void head_epilogue(const float *sA, float *sLogit, const typename Elem<CDT>::T *w_up,
+                              int r, int nb, int top, int64_t tok0, int64_t ntok,
+                              const float *__restrict__ noise, float *__restrict__ probs,
+                              void *__restrict__ top_idx, int idx64, float *__restrict__ gates,
+                              float *__restrict__ log_gates) {
+    const int tid = threadIdx.x;
+    for (int i = tid; i < kHeadTokens * nb; i += blockDim.x) {
+        const int tl = i / nb, e = i % nb;
+        float acc = 0.0f;
+        for (int j = 0; j < r; ++j)
+            acc = __fmaf_rn(sA[tl * r + j], Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), acc);
+        sLogit[tl * nb + e] = Elem<CDT>::round(acc);
+    }
+    __syncthreads();
+    if (tid < kHeadTokens && tok0 + tid < ntok) {
+        const int64_t t = tok0 + tid;
+        const float *lg = sLogit + tid * nb;
+        float m = -INFINITY;
+        for (int e = 0; e < nb; ++e) m = fmaxf(m, lg[e]);
+        float ssum = 0.0f;
+        for (int e = 0; e < nb; ++e) ssum += expf(lg[e] - m);
+        for (int e = 0; e < nb; ++e) probs[t * nb + e] = expf(lg[e] - m) / ssum;
+        // top-k by repeated selection: strictly greater wins, so among equal
+        // values the lower block index is taken first.
+        float vals[kMaxTop];
+        int idxs[kMaxTop];
+        uint64_t taken = 0;
+        for (int k = 0; k < top; ++k) {
+            float best = -INFINITY;
+            int bi = -1;
+            for (int e = 0; e < nb; ++e) {
+                if ((taken >> e) & 1ull) continue;
+                const float v = noise ? lg[e] + noise[t * nb + e] : lg[e];
+                if (bi < 0 || v > best) { best = v; bi = e; }
+            }
+            taken |= 1ull << bi;
+            vals[k] = best;
+            idxs[k] = bi;
+        }
+        float gm = vals[0];
+        for (int k = 1; k < top; ++k) gm = fmaxf(gm, vals[k]);
+        float gs = 0.0f;
+        for (int k = 0; k < top; ++k) gs += expf(vals[k] - gm);
+        for (int k = 0; k < top; ++k) {
+            const float g = expf(vals[k] - gm) / gs;
+            gates[t * top + k] = g;
+            if (log_gates) log_gates[t * top + k] = logf(fmaxf(g, 1e-9f));
+            if (idx64) reinterpret_cast<int64_t *>(top_idx)[t * top + k] = idxs[k];
+            else reinterpret_cast<int32_t *>(top_idx)[t * top + k] = idxs[k];
+        }
+    }
+}
+
+// bf16 compute dtype: z on the tensor cores (bf16 x bf16 products are exact in
+// fp32; fp32 accumulation), r must be 32 or 64 here.
+template <int RANK>
+__global__ void __launch_bounds__(kHeadThreads)
+route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restrict__ w_down,
+                       const uint16_t *__restrict__ w_up, int64_t ntok, int d, int nb, int top,
+                       const float *__restrict__ noise, float *__restrict__ probs,
+                       void *__restrict__ top_idx, int idx64, float *__restrict__ gates,
+                       float *__restrict__ log_gates, uint16_t *__restrict__ act) {
+    constexpr int kRowB = kHeadKC * 2;                   // 128 B per smem row
+    constexpr int kHqBytes = kHeadTokens * kRowB;        // 8 KB
+    constexpr int kWBytes = RANK * kRowB;                // 4/8 KB
+    constexpr int kStage = kHqBytes + kWBytes;
+    constexpr int NT = RANK / 8;                          // n-tiles of 8
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *sA = reinterpret_cast<float *>(smem + 2 * kStage);
+    float *sLogit = sA + kHeadTokens * RANK;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kHeadTokens;
+    const int nchunk = d / kHeadKC;
+
+    auto issue = [&](int c) {
+        if (c < nchunk) {
+            const uint32_t base = smem_u32(smem + (c & 1) * kStage);
+            for (int i = tid; i < kHeadTokens * 8; i += kHeadThreads) {
+                const int row = i >> 3, ch = i & 7;
+                const int64_t t = tok0 + row;
+                const bool ok = t < ntok;
+                const uint16_t *src = ok ? hq + t * d + c * kHeadKC + ch * 8 : hq;
+                cp_async16(base + swz(row, ch, kRowB), src, ok ? 16 : 0);
+            }
+            for (int i = tid; i < RANK * 8; i += kHeadThreads) {
+                const int row = i >> 3, ch = i & 7;
+                cp_async16(base + kHqBytes + swz(row, ch, kRowB),
+                           w_down + static_cast<int64_t>(row) * d + c * kHeadKC + ch * 8, 16);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+
+    issue(0);
+#pragma unroll 1
+    for (int c = 0; c < nchunk; ++c) {
+        issue(c + 1);
+        cp_async_wait<1>();
+        __syncthreads();
+        const uint32_t sq = smem_u32(smem + (c & 1) * kStage);
+        const uint32_t sw = sq + kHqBytes;
+#pragma unroll
+        for (int ks = 0; ks < kHeadKC / 16; ++ks) {
+            uint32_t a[4];
+            const int arow = warp * 16 + (lane & 15);
+            ldmatrix_x4(a, sq + swz(arow, ks * 2 + (lane >> 4), kRowB));
+#pragma unroll
+            for (int j = 0; j < NT; j += 2) {
+                uint32_t bfr[4];
+                const int brow = j * 8 + (lane & 7) + ((lane >> 4) << 3);
+                ldmatrix_x4(bfr, sw + swz(brow, ks * 2 + ((lane >> 3) & 1), kRowB));
+                mma_bf16_16816(acc[j], a, bfr[0], bfr[1]);
+                mma_bf16_16816(acc[j + 1], a, bfr[2], bfr[3]);
+            }
+        }
+        __syncthreads();
+    }
+
+    // z -> act, kept as fp32 values rounded to bf16
+    const int g = lane >> 2, q2 = (lane & 3) * 2;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int row = warp * 16 + g + h * 8;
+            const int col = j * 8 + q2;
+            const float a0 = round_bf16(tanhf(round_bf16(acc[j][2 * h])));
+            const float a1 = round_bf16(tanhf(round_bf16(acc[j][2 * h + 1])));
+            sA[row * RANK + col] = a0;
+            sA[row * RANK + col + 1] = a1;
+            const int64_t t = tok0 + row;
+            if (act && t < ntok) {
+                *reinterpret_cast<uint32_t *>(act + t * RANK + col) = pack_bf16x2(a0, a1);
+            }
+        }
+    }
+    __syncthreads();
+    head_epilogue<MOM_BF16>(sA, sLogit, w_up, RANK, nb, top, tok0, ntok, noise, probs, top_idx,
+                            idx64, gates, log_gates);
+}
+
+// Generic SIMT head (fp32 compute dtype, or any rank): fp32 FMA accumulation.
+template <int CDT>
+__global__ void __launch_bounds__(kHeadThreads)
+route_head_simt_kernel(const typename Elem<CDT>::T *__restrict__ hq,
+                       const typename Elem<CDT>::T *__restrict__ w_down,
+                       const typename Elem<CDT>::T *__restrict__ w_up, int64_t ntok, int d, int r,
+                       int nb, int top, const float *__restrict__ noise, float *__restrict__ probs,
+                       void *__restrict__ top_idx, int idx64, float *__restrict__ gates,
+                       float *__restrict__ log_gates, typename Elem<CDT>::T *__restrict__ act) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    float *sA = reinterpret_cast<float *>(smem);
+    float *sLogit = sA + kHeadTokens * r;
+    float *sH = sLogit + kHeadTokens * kMaxNb;         // kHeadTokens x kHeadKC
+    float *sW = sH + kHeadTokens * kHeadKC;             // r x kHeadKC
+    const int tid = threadIdx.x;
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kHeadTokens;
+    // thread -> (token tl, ranks j = jr, jr + 2, ...)
+    const int tl = tid >> 1, jr = tid & 1;
+    float acc[kMaxRank / 2];
+    for (int j = 0; j < kMaxRank / 2; ++j) acc[j] = 0.0f;
+    for (int c0 = 0; c0 < d; c0 += kHeadKC) {
+        const int kc = min(kHeadKC, d - c0);
+        __syncthreads();
+        for (int i = tid; i < kHeadTokens * kHeadKC; i += blockDim.x) {
+            const int row = i / kHeadKC, cc = i % kHeadKC;
+            const int64_t t = tok0 + row;
+            sH[i] = (t < ntok && cc < kc) ? Elem<CDT>::load(hq, t * d + c0 + cc) : 0.0f;
+        }
+        for (int i = tid; i < r * kHeadKC; i += blockDim.x) {
+            const int row = i / kHeadKC, cc = i % kHeadKC;
+            sW[i] = cc < kc ? Elem<CDT>::load(w_down, static_cast<int64_t>(row) * d + c0 + cc) : 0.0f;
+        }
+        __syncthreads();
+        for (int jj = 0, j = jr; j < r; j += 2, ++jj) {
+            float a = acc[jj];
+            for (int cc = 0; cc < kc; ++cc) a = __fmaf_rn(sH[tl * kHeadKC + cc], sW[j * kHeadKC + cc], a);
+            acc[jj] = a;
+        }
+    }
+    for (int jj = 0, j = jr; j < r; j += 2, ++jj) {
+        const float a = Elem<CDT>::round(tanhf(Elem<CDT>::round(acc[jj])));
+        sA[tl * r + j] = a;
+        const int64_t t = tok0 + tl;
+        if (act && t < ntok) Elem<CDT>::store(act, t * r + j, a);
+    }
+    __syncthreads();
+    head_epilogue<CDT>(sA, sLogit, w_up, r, nb, top, tok0, ntok, noise, probs, top_idx, idx64,
+                       gates, log_gates);
+}
+
+// ============================================================ router backward
+// Per token (one warp): gate-softmax and probs-softmax adjoints -> dlogits,
+// then da = dlogits . Wu and dz = da * (1 - act^2).
+template <int CDT>
+__global__ void route_bwd_token_kernel(int64_t ntok, int r, int nb, int top,
+                                       const float *__restrict__ probs, const void *__restrict__ top_idx,
+                                       int idx64, const float *__restrict__ gates,
+                                       const typename Elem<CDT>::T *__restrict__ act,
+                                       const typename Elem<CDT>::T *__restrict__ w_up,
+                                       const float *__restrict__ dlog_gates,
+                                       const float *__restrict__ dgates,
+                                       const float *__restrict__ dprobs, float *__restrict__ dlogits,
+                                       float *__restrict__ dz) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= ntok) return;
+    // gate softmax backward (lanes < top)
+    float g = 0.0f, dg = 0.0f;
+    int idx = -1;
+    if (lane < top) {
+        g = gates[t * top + lane];
+        if (dlog_gates) dg += (g >= 1e-9f) ? dlog_gates[t * top + lane] / fmaxf(g, 1e-9f) : 0.0f;
+        if (dgates) dg += dgates[t * top + lane];
+        idx = idx64 ? static_cast<int>(reinterpret_cast<const int64_t *>(top_idx)[t * top + lane])
+                    : reinterpret_cast<const int32_t *>(top_idx)[t * top + lane];
+    }
+    const float sgdg = warp_sum(g * dg);
+    const float dtv = g * (dg - sgdg);
+    // probs softmax backward
+    float sp = 0.0f;
+    if (dprobs) {
+        float part = 0.0f;
+        for (int e = lane; e < nb; e += 32) part += probs[t * nb + e] * dprobs[t * nb + e];
+        sp = warp_sum(part);
+    }
+    // Every shuffle below runs on all 32 lanes: the loops have warp-uniform
+    // trip counts and only the loads/stores are predicated.
+    float dl0 = 0.0f, dl1 = 0.0f;   // dlogits for e = lane and e = lane + 32
+#pragma unroll
+    for (int half = 0; half < kMaxNb / 32; ++half) {
+        const int e = half * 32 + lane;
+        float v = 0.0f;
+        for (int k = 0; k < top; ++k) {
+            const int ik = __shfl_sync(0xffffffffu, idx, k);
+            const float dk = __shfl_sync(0xffffffffu, dtv, k);
+            if (ik == e) v += dk;
+        }
+        if (e < nb) {
+            if (dprobs) {
+                const float p = probs[t * nb + e];
+                v += p * (dprobs[t * nb + e] - sp);
+            }
+            dlogits[t * nb + e] = v;
+        } else {
+            v = 0.0f;
+        }
+        if (half == 0) dl0 = v; else dl1 = v;
+    }
+    // da_j = sum_e dlogits_e * Wu[e, j]
+    for (int j0 = 0; j0 < r; j0 += 32) {
+        const int j = j0 + lane;
+        float da = 0.0f;
+        for (int e = 0; e < nb; ++e) {
+            const float dle = __shfl_sync(0xffffffffu, e < 32 ? dl0 : dl1, e & 31);
+            if (j < r) da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
+        }
+        if (j < r) {
+            const float a = Elem<CDT>::load(act, t * r + j);
+            dz[t * r + j] = da * (1.0f - a * a);
+        }
+    }
+}
+
+// u[b, t, j] = sum_{s >= t} dz[b, s, j] / (s + 1), one thread per (b, j).
+__global__ void route_bwd_revscan_kernel(const float *__restrict__ dz, float *__restrict__ u, int B,
+                                         int S, int r) {
+    const int col = blockIdx.x * blockDim.x + threadIdx.x;
+    if (col >= B * r) return;
+    const int b = col / r, j = col % r;
+    const float *src = dz + static_cast<int64_t>(b) * S * r + j;
+    float *dst = u + static_cast<int64_t>(b) * S * r + j;
+    float acc = 0.0f;
+    int t = S - 1;
+    for (; t >= 7; t -= 8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = src[static_cast<int64_t>(t - i) * r] / static_cast<float>(t - i + 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            acc += v[i];
+            dst[static_cast<int64_t>(t - i) * r] = acc;
+        }
+    }
+    for (; t >= 0; --t) {
+        acc += src[static_cast<int64_t>(t) * r] / static_cast<float>(t + 1);
+        dst[static_cast<int64_t>(t) * r] = acc;
+    }
+}
+
+// dx[t, c] (+)= sum_j u[t, j] * Wd[j, c]
+constexpr int kDxTokens = 16;
+template <int CDT, int DXDT>
+__global__ void __launch_bounds__(256)
+route_bwd_dx_kernel(const float *__restrict__ u, const typename Elem<CDT>::T *__restrict__ w_down,
+                    int64_t ntok, int d, int r, typename Elem<DXDT>::T *__restrict__ dx, int accumulate) {
+    __shared__ float sU[kDxTokens * kMaxRank];
+    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kDxTokens;
+    for (int i = threadIdx.x; i < kDxTokens * r; i += blockDim.x) {
+        const int64_t t = tok0 + i / r;
+        sU[i] = t < ntok ? u[t * r + (i % r)] : 0.0f;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        float w[kMaxRank];
+        for (int j = 0; j < r; ++j) w[j] = Elem<CDT>::load(w_down, static_cast<int64_t>(j) * d + c);
+        for (int tl = 0; tl < kDxTokens; ++tl) {
+            const int64_t t = tok0 + tl;
+            if (t >= ntok) break;
+            float acc = 0.0f;
+            for (int j = 0; j < r; ++j) acc = fmaf(sU[tl * r + j], w[j], acc);
+            if (accumulate) acc += Elem<DXDT>::load(dx, t * d + c);
+            Elem<DXDT>::store(dx, t * d + c, acc);
+        }
+    }
+}
+
+// dWd[j, c] += sum_{t in chunk} u[t, j] * x[t, c]; fp32 atomics across chunks.
+constexpr int kDwTok = 256;
+constexpr int kDwCols = 64;
+template <int XDT>
+__global__ void __launch_bounds__(256)
+route_bwd_dwdown_kernel(const float *__restrict__ u, const typename Elem<XDT>::T *__restrict__ x,
+                        int64_t ntok, int d, int r, float *__restrict__ dw_down) {
+    __shared__ float sU[32 * kMaxRank];
+    __shared__ float sX[32 * kDwCols];
+    const int c0 = blockIdx.x * kDwCols;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kDwTok;
+    const int tid = threadIdx.x;
+    const int cl = tid % kDwCols;     // column within the slab
+    const int jg = tid / kDwCols;     // rank group: j = jg, jg+4, ...
+    float acc[kMaxRank / 4];
+    for (int i = 0; i < kMaxRank / 4; ++i) acc[i] = 0.0f;
+    for (int tb = 0; tb < kDwTok; tb += 32) {
+        __syncthreads();
+        for (int i = tid; i < 32 * r; i += 256) {
+            const int64_t t = t0 + tb + i / r;
+            sU[i] = t < ntok ? u[t * r + i % r] : 0.0f;
+        }
+        for (int i = tid; i < 32 * kDwCols; i += 256) {
+            const int64_t t = t0 + tb + i / kDwCols;
+            const int c = c0 + i % kDwCols;
+            sX[i] = (t < ntok && c < d) ? Elem<XDT>::load(x, t * d + c) : 0.0f;
+        }
+        __syncthreads();
+        for (int tt = 0; tt < 32; ++tt) {
+            const float xv = sX[tt * kDwCols + cl];
+            for (int j = jg, i = 0; j < r; j += 4, ++i) acc[i] = fmaf(sU[tt * r + j], xv, acc[i]);
+        }
+    }
+    const int c = c0 + cl;
+    if (c < d)
+        for (int j = jg, i = 0; j < r; j += 4, ++i) atomicAdd(dw_down + static_cast<int64_t>(j) * d + c, acc[i]);
+}
+
+// dWu[e, j] += sum_t dlogits[t, e] * act[t, j]
+template <int CDT>
+__global__ void __launch_bounds__(256)
+route_bwd_dwup_kernel(const float *__restrict__ dlogits, const typename Elem<CDT>::T *__restrict__ act,
+                      int64_t ntok, int r, int nb, float *__restrict__ dw_up) {
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 1024;
+    for (int o = threadIdx.x; o < nb * r; o += blockDim.x) {
+        const int e = o / r, j = o % r;
+        float acc = 0.0f;
+        const int64_t tend = min(ntok, t0 + 1024);
+        for (int64_t t = t0; t < tend; ++t) acc = fmaf(dlogits[t * nb + e], Elem<CDT>::load(act, t * r + j), acc);
+        atomicAdd(dw_up + o, acc);
+    }
+}
+
+// ============================================================ host launchers
+template <int XDT, int CDT, int MODE>
+static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
+    using XT = typename Elem<XDT>::T;
+    const size_t smem = kScanStages * kScanRows * kScanCols * sizeof(XT);
+    auto k = route_scan_kernel<XDT, CDT, MODE>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((d + kScanCols - 1) / kScanCols, B);
+    k<<<grid, kScanCols, smem, st>>>(static_cast<const XT *>(x),
+                                     static_cast<typename Elem<CDT>::T *>(hq), S, d); count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, int S, int d,
+                              int mode, cudaStream_t st) {
+#define MOM_SCAN_CASE(X, C, M)                                                       \
+    if (xdt == X && cdt == C && mode == M) return launch_scan_t<X, C, M>(x, hq, B, S, d, st);
+    MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP64)
+    MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP32)
+    MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP64)
+    MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP32)
+    MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP64)
+    MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP32)
+    MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP64)
+    MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP32)
+#undef MOM_SCAN_CASE
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_up, int cdt,
+                              int64_t ntok, int d, int r, int nb, int top, const float *noise,
+                              float *probs, void *top_idx, int idx64, float *gates,
+                              float *log_gates, void *act, cudaStream_t st) {
+    const int grid = static_cast<int>((ntok + kHeadTokens - 1) / kHeadTokens);
+    if (cdt == MOM_BF16 && (r == 32 || r == 64) && d % kHeadKC == 0) {
+        const size_t smem = 2 * (kHeadTokens + r) * kHeadKC * 2 +
+                            (kHeadTokens * r + kHeadTokens * kMaxNb) * sizeof(float);
+        if (r == 32) {
+            auto k = route_head_bf16_kernel<32>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, kHeadThreads, smem, st>>>(
+                static_cast<const uint16_t *>(hq), static_cast<const uint16_t *>(w_down),
+                static_cast<const uint16_t *>(w_up), ntok, d, nb, top, noise, probs, top_idx, idx64,
+                gates, log_gates, static_cast<uint16_t *>(act)); count_launch();
+        } else {
+            auto k = route_head_bf16_kernel<64>;
+            cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            k<<<grid, kHeadThreads, smem, st>>>(
+                static_cast<const uint16_t *>(hq), static_cast<const uint16_t *>(w_down),
+                static_cast<const uint16_t *>(w_up), ntok, d, nb, top, noise, probs, top_idx, idx64,
+                gates, log_gates, static_cast<uint16_t *>(act)); count_launch();
+        }
+        return cudaGetLastError();
+    }
+    const size_t smem = (kHeadTokens * r + kHeadTokens * kMaxNb + kHeadTokens * kHeadKC + r * kHeadKC) * sizeof(float);
+    if (cdt == MOM_BF16) {
+        auto k = route_head_simt_kernel<MOM_BF16>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<grid, kHeadThreads, smem, st>>>(
+            static_cast<const uint16_t *>(hq), static_cast<const uint16_t *>(w_down),
+            static_cast<const uint16_t *>(w_up), ntok, d, r, nb, top, noise, probs, top_idx, idx64,
+            gates, log_gates, static_cast<uint16_t *>(act)); count_launch();
+    } else {
+        auto k = route_head_simt_kernel<MOM_F32>;
+        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        k<<<grid, kHeadThreads, smem, st>>>(
+            static_cast<const float *>(hq), static_cast<const float *>(w_down),
+            static_cast<const float *>(w_up), ntok, d, r, nb, top, noise, probs, top_idx, idx64,
+            gates, log_gates, static_cast<float *>(act)); count_launch();
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const void *w_down,
+                             const void *w_up, int cdt, int r, int nb, int top, const float *probs,
+                             const void *top_idx, int idx64, const float *gates, const void *act,
+                             const float *dlog_gates, const float *dgates, const float *dprobs,
+                             void *dx, int dxdt, int accumulate, float *dw_down, float *dw_up,
+                             float *ws_dlogits, float *ws_dz, float *ws_u, cudaStream_t st) {
+    const int64_t ntok = static_cast<int64_t>(B) * S;
+    cudaError_t e;
+    e = cudaMemsetAsync(dw_down, 0, sizeof(float) * r * d, st);
+    if (e != cudaSuccess) return e;
+    e = cudaMemsetAsync(dw_up, 0, sizeof(float) * nb * r, st);
+    if (e != cudaSuccess) return e;
+    {
+        const int warps = 8;
+        const int grid = static_cast<int>((ntok + warps - 1) / warps);
+        if (cdt == MOM_BF16)
+            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, 0, st>>>(
+                ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const uint16_t *>(act),
+                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
+        else
+            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, 0, st>>>(
+                ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const float *>(act),
+                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
+        count_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    route_bwd_revscan_kernel<<<(B * r + 127) / 128, 128, 0, st>>>(ws_dz, ws_u, B, S, r); count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    {
+        const int grid = static_cast<int>((ntok + kDxTokens - 1) / kDxTokens);
+#define MOM_DX_CASE(C, X)                                                                         \
+    if (cdt == C && dxdt == X)                                                                    \
+        route_bwd_dx_kernel<C, X><<<grid, 256, 0, st>>>(                                           \
+            ws_u, static_cast<const typename Elem<C>::T *>(w_down), ntok, d, r,                  \
+            static_cast<typename Elem<X>::T *>(dx), accumulate);
+        MOM_DX_CASE(MOM_BF16, MOM_BF16)
+        MOM_DX_CASE(MOM_BF16, MOM_F32)
+        MOM_DX_CASE(MOM_F32, MOM_BF16)
+        MOM_DX_CASE(MOM_F32, MOM_F32)
+#undef MOM_DX_CASE
+        count_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    {
+        dim3 grid((d + kDwCols - 1) / kDwCols, static_cast<unsigned>((ntok + kDwTok - 1) / kDwTok));
+        if (xdt == MOM_BF16)
+            route_bwd_dwdown_kernel<MOM_BF16><<<grid, 256, 0, st>>>(
+                ws_u, static_cast<const uint16_t *>(x), ntok, d, r, dw_down);
+        else
+            route_bwd_dwdown_kernel<MOM_F32><<<grid, 256, 0, st>>>(
+                ws_u, static_cast<const float *>(x), ntok, d, r, dw_down);
+        count_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    {
+        const int grid = static_cast<int>((ntok + 1023) / 1024);
+        if (cdt == MOM_BF16)
+            route_bwd_dwup_kernel<MOM_BF16><<<grid, 256, 0, st>>>(
+                ws_dlogits, static_cast<const uint16_t *>(act), ntok, r, nb, dw_up);
+        else
+            route_bwd_dwup_kernel<MOM_F32><<<grid, 256, 0, st>>>(
+                ws_dlogits, static_cast<const float *>(act), ntok, r, nb, dw_up);
+        count_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace mom

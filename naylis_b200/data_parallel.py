@@ -1,0 +1,104 @@
+"""Explicit data-parallel gradient exchange for MoM training over NCCL.
+
+Replaces the reference's implicit DDP (HF Trainer under torchrun,
+pretrain.py:792-817 with ddp_find_unused_parameters=False,
+run_biggpu.sh:16-42): one process per GPU, the batch sharded by sequence
+(every sequence whole on one rank, so the causal router needs no exchange),
+and every gradient — the shared bank ``M_blocks`` (summed over all layers
+first), the router and the q/k/v/o projections — averaged across ranks.
+
+Design: each parameter's ``.grad`` is a view into a flat fp32 bucket, so
+autograd accumulates straight into the communication buffer (no copy). A
+post-accumulate hook marks the parameter ready; buckets are launched as
+asynchronous all-reduces strictly in bucket order (identical on every rank,
+as NCCL requires) as soon as all their parameters are ready, so the exchange
+overlaps the rest of the backward. ``finish()`` launches whatever is left,
+waits, and scales by 1/world.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+class GradAllReduce:
+    def __init__(self, module: torch.nn.Module, process_group=None, bucket_mb: float = 32.0,
+                 average: bool = True):
+        self.group = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.average = average
+        params = [p for p in module.parameters() if p.requires_grad]
+        # gradients arrive roughly in reverse registration order
+        params = list(reversed(params))
+        cap = int(bucket_mb * (1 << 20) // 4)
+        self.buckets = []
+        cur = []
+        size = 0
+        for p in params:
+            if p.dtype != torch.float32:
+                raise RuntimeError("GradAllReduce keeps fp32 master gradients; got "
+                                   f"a {p.dtype} parameter")
+            if cur and size + p.numel() > cap:
+                self.buckets.append(cur)
+                cur, size = [], 0
+            cur.append(p)
+            size += p.numel()
+        if cur:
+            self.buckets.append(cur)
+        self.flat = []
+        self._bucket_of = {}
+        for i, ps in enumerate(self.buckets):
+            n = sum(p.numel() for p in ps)
+            buf = torch.zeros(n, dtype=torch.float32, device=ps[0].device)
+            off = 0
+            for p in ps:
+                p.grad = buf[off:off + p.numel()].view_as(p)
+                off += p.numel()
+                self._bucket_of[p] = i
+            self.flat.append(buf)
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_ready) for p in params]
+        self._reset_state()
+
+    def _reset_state(self):
+        self._pending = [len(ps) for ps in self.buckets]
+        self._next = 0
+        self._works = []
+
+    def zero_grad(self):
+        for buf in self.flat:
+            buf.zero_()
+        for i, ps in enumerate(self.buckets):
+            # an optimizer may have replaced .grad; re-attach the views
+            off = 0
+            for p in ps:
+                if p.grad is None or p.grad.data_ptr() != self.flat[i].data_ptr() + off * 4:
+                    p.grad = self.flat[i][off:off + p.numel()].view_as(p)
+                off += p.numel()
+        self._reset_state()
+
+    def _launch_ready(self, force: bool = False):
+        while self._next < len(self.buckets) and (force or self._pending[self._next] == 0):
+            buf = self.flat[self._next]
+            if self.world > 1:
+                self._works.append(dist.all_reduce(buf, group=self.group, async_op=True))
+            self._next += 1
+
+    def _on_ready(self, p):
+        i = self._bucket_of[p]
+        self._pending[i] -= 1
+        self._launch_ready()
+
+    def finish(self):
+        """Launch the remaining buckets, wait for all, average."""
+        self._launch_ready(force=True)
+        for w in self._works:
+            w.wait()
+        if self.average and self.world > 1:
+            for buf in self.flat:
+                buf.div_(self.world)
+        self._works = []
+
+    def remove(self):
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []

@@ -1,0 +1,280 @@
+"""The ``mom_kernels`` door of the sm_100a backend.
+
+Mirrors the reference's dispatch door (mom_kernels/__init__.py:37-117: same
+function names, arguments and fail-loud behaviour) for one new mode,
+``"sm100"``: the gated memory read and the fused causal router run as
+hand-written CUDA kernels for B200 through ``libnaylis_mom.so``. There is no
+fallback inside this mode — a missing library, a non-sm_100 device or an
+unsupported shape raises.
+
+Added entry, not in the reference door: ``mom_route`` (the reference's router
+is inline in model.py:178-220; the fused router kernel replaces it).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+MODE = "sm100"
+_ANNOUNCED = {"backend": None}
+
+
+def _device_type(device) -> str:
+    if isinstance(device, torch.device):
+        return device.type
+    return str(device).split(":")[0].lower()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _device_ok(device) -> None:
+    idx = device.index if isinstance(device, torch.device) and device.index is not None \
+        else torch.cuda.current_device()
+    _lib.call("mom_device_check", idx)
+
+
+def preflight(device_type: str) -> None:
+    """Fail fast at startup if ``device_type`` cannot run the sm100 backend
+    (reference: mom_kernels/__init__.py:37-53)."""
+    if device_type != "cuda":
+        raise RuntimeError(
+            f"use_kernel=true with the sm100 backend requires a CUDA B200 (sm_100) device; "
+            f"this process resolved to {device_type!r}. Set use_kernel=false (eager SDPA, "
+            f"the parity reference) or run on the accelerator.")
+    if not torch.cuda.is_available():
+        raise RuntimeError("use_kernel=true (sm100): CUDA is not available in this process.")
+    _lib.load()
+    _device_ok(torch.device("cuda", torch.cuda.current_device()))
+
+
+def resolve_mode(device, dtype, *, head_dim=None) -> str:
+    """Pick the kernel backend and check its contract (reference:
+    mom_kernels/__init__.py:56-84). Only ``"sm100"`` is served here: bf16
+    activations and head_dim 64 or 128 on an sm_100 device; anything else
+    raises instead of falling back."""
+    device_type = _device_type(device)
+    if device_type != "cuda":
+        raise RuntimeError(
+            f"use_kernel=true: no sm100 kernel backend for device {device_type!r} "
+            f"(the sm100 backend runs on CUDA B200 only).")
+    if dtype != torch.bfloat16:
+        raise RuntimeError(
+            f"use_kernel=true (sm100) requires bf16 activations (the repo AMP dtype; "
+            f"fp16 is unsupported); got {dtype}.")
+    if head_dim is not None:
+        if head_dim > 128 or head_dim & (head_dim - 1) != 0:
+            raise RuntimeError(
+                f"use_kernel=true (sm100): head_dim {head_dim} must be a power of two <= 128.")
+        if head_dim not in (64, 128):
+            raise RuntimeError(
+                f"use_kernel=true (sm100): the read kernels implement head_dim 64 and 128; "
+                f"got {head_dim}.")
+    _lib.load()
+    dev = torch.device(device) if not isinstance(device, torch.device) else device
+    if torch.cuda.is_available():
+        _device_ok(dev)
+    else:
+        raise RuntimeError("use_kernel=true (sm100): CUDA is not available in this process.")
+    return MODE
+
+
+def announce(backend: str) -> None:
+    """Print the backend banner once per process (reference: :105-117)."""
+    if _ANNOUNCED["backend"] != backend:
+        _ANNOUNCED["backend"] = backend
+        if backend == MODE:
+            print("[MoM] use_kernel=true -> backend 'sm100': routing-set bucketing, "
+                  "read over the selected blocks only (hand-written sm_100a kernels), "
+                  "fused exact-prefix-scan router.")
+
+
+# ====================================================================== read
+class _MomReadFunction(torch.autograd.Function):
+    """Autograd of the sm100 read: saves q, k, v, out, the fp32 log-sum-exp
+    and the routing plan (reference: mom_kernels/triton_gpu.py:323-409)."""
+
+    @staticmethod
+    def forward(ctx, q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
+        B, S, H, hd = q_sh.shape
+        L = k.shape[0]
+        N, top = B * S, top_idx.shape[-1]
+        dev = q_sh.device
+        st = _stream(dev)
+        idx = top_idx.reshape(N, top)
+        if idx.dtype not in (torch.int64, torch.int32):
+            idx = idx.to(torch.int64)
+        idx = idx.contiguous()
+        lg = log_gates.reshape(N, top).to(torch.float32).contiguous()
+        plan = torch.empty(_lib.load().mom_plan_size(N, num_blocks, top), dtype=torch.uint8, device=dev)
+        _lib.call("mom_bucket", idx.data_ptr(), _lib.I64 if idx.dtype == torch.int64 else _lib.I32,
+                  lg.data_ptr(), N, num_blocks, top, plan.data_ptr(), plan.numel(), st)
+        out = torch.empty_like(q_sh)
+        lse = torch.empty((N, H), dtype=torch.float32, device=dev)
+        _lib.call("mom_read_fwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd,
+                  num_blocks, block_size, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(), st)
+        ctx.save_for_backward(q_sh, k, v, out, lse, plan)
+        ctx.meta = (num_blocks, block_size, top, L)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q_sh, k, v, out, lse, plan = ctx.saved_tensors
+        num_blocks, block_size, top, L = ctx.meta
+        B, S, H, hd = q_sh.shape
+        N = B * S
+        dev = q_sh.device
+        st = _stream(dev)
+        dout = dout.to(torch.bfloat16).contiguous()
+        dq = torch.empty_like(q_sh)
+        dk = torch.empty((L, H * hd), dtype=torch.float32, device=dev)
+        dv = torch.empty_like(dk)
+        dlg = torch.empty((B, S, top), dtype=torch.float32, device=dev)
+        ws = torch.empty(_lib.load().mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=dev)
+        _lib.call("mom_read_bwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                  dout.data_ptr(), lse.data_ptr(), _lib.BF16, B, S, H, hd, num_blocks, block_size,
+                  top, plan.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(),
+                  ws.data_ptr(), ws.numel(), st)
+        return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
+
+
+def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: str = MODE):
+    """MoM memory read with the per-token gate bias (reference door:
+    mom_kernels/__init__.py:87-102; contract of mom_kernels/triton_gpu.py:412-439).
+
+    q_sh (B, S, H, hd) bf16; shared k, v (L, H*hd) bf16 with L = num_blocks *
+    block_size; top_idx (B, S, top) block ids; top_gates (B, S, top) fp32
+    softmax gates. Returns (B, S, H, hd). Gradients reach q, k, v and the
+    gates (through log(clamp_min(g, 1e-9)), as the reference bias does).
+    """
+    if mode != MODE:
+        raise RuntimeError(f"unknown kernel mode {mode!r} (this door serves {MODE!r})")
+    if k.dim() != 2 or v.dim() != 2:
+        raise RuntimeError("sm100 mom_read: shared K/V (L, D) only, got batched inputs")
+    if q_sh.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError(f"sm100 mom_read requires bf16 activations, got q {q_sh.dtype}, "
+                           f"k {k.dtype}, v {v.dtype}")
+    if not q_sh.is_cuda:
+        raise RuntimeError("sm100 mom_read: tensors must be on a CUDA device")
+    if k.shape[0] != num_blocks * block_size:
+        raise RuntimeError(
+            f"sm100 mom_read: bank is {k.shape[0]} slots but num_blocks ({num_blocks}) x "
+            f"block_size ({block_size}) disagrees")
+    B, S, H, hd = q_sh.shape
+    if k.shape[1] != H * hd or v.shape != k.shape:
+        raise RuntimeError(f"sm100 mom_read: k/v must be (L, {H * hd}), got {tuple(k.shape)}, {tuple(v.shape)}")
+    if top_idx.shape != top_gates.shape or top_idx.shape[:2] != (B, S):
+        raise RuntimeError("sm100 mom_read: top_idx / top_gates must be (B, S, top)")
+    log_gates = top_gates.clamp_min(1e-9).log().float()
+    return _MomReadFunction.apply(q_sh.contiguous(), k.contiguous(), v.contiguous(), top_idx,
+                                  log_gates, int(num_blocks), int(block_size))
+
+
+# ====================================================================== router
+def _compute_dtype(w: torch.Tensor) -> torch.dtype:
+    """The dtype the router linears run in: autocast's dtype when enabled."""
+    if torch.is_autocast_enabled("cuda"):
+        return torch.get_autocast_dtype("cuda")
+    return w.dtype
+
+
+def _dt_code(dtype) -> int:
+    if dtype == torch.float32:
+        return _lib.F32
+    if dtype == torch.bfloat16:
+        return _lib.BF16
+    raise RuntimeError(f"sm100 router: unsupported dtype {dtype} (fp32 or bf16)")
+
+
+class _MomRouteFunction(torch.autograd.Function):
+    """Fused causal router (reference: model.py:178-220). Outputs router_probs,
+    top_idx (no gradient) and top_gates; the backward returns dx, dW_down and
+    dW_up (the reverse prefix scan runs in rank-r space)."""
+
+    @staticmethod
+    def forward(ctx, x, w_down, w_up, noise, top, compute_dtype, scan_mode):
+        B, S, d = x.shape
+        r, nb = w_down.shape[0], w_up.shape[0]
+        dev = x.device
+        st = _stream(dev)
+        x_c = x.contiguous()
+        wd = w_down.detach().to(compute_dtype).contiguous()
+        wu = w_up.detach().to(compute_dtype).contiguous()
+        probs = torch.empty((B, S, nb), dtype=torch.float32, device=dev)
+        top_idx = torch.empty((B, S, top), dtype=torch.int64, device=dev)
+        gates = torch.empty((B, S, top), dtype=torch.float32, device=dev)
+        act = torch.empty((B, S, r), dtype=compute_dtype, device=dev)
+        cd = _dt_code(compute_dtype)
+        ws = torch.empty(_lib.load().mom_route_workspace_size(B, S, d, r, nb, cd), dtype=torch.uint8, device=dev)
+        nz = None
+        if noise is not None:
+            nz = noise.to(torch.float32).contiguous()
+        _lib.call("mom_route_fwd", x_c.data_ptr(), _dt_code(x.dtype), B, S, d, wd.data_ptr(),
+                  wu.data_ptr(), cd, r, nb, top, _ptr(nz), _lib.SCAN_MODES[scan_mode],
+                  probs.data_ptr(), top_idx.data_ptr(), _lib.I64, gates.data_ptr(), None,
+                  act.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        ctx.save_for_backward(x_c, wd, wu, probs, top_idx, gates, act)
+        ctx.meta = (top, cd, w_down.dtype, w_up.dtype)
+        ctx.mark_non_differentiable(top_idx)
+        return probs, top_idx, gates
+
+    @staticmethod
+    def backward(ctx, dprobs, _didx, dgates):
+        x, wd, wu, probs, top_idx, gates, act = ctx.saved_tensors
+        top, cd, wd_dtype, wu_dtype = ctx.meta
+        B, S, d = x.shape
+        r, nb = wd.shape[0], wu.shape[0]
+        dev = x.device
+        st = _stream(dev)
+        dp = None if dprobs is None else dprobs.to(torch.float32).contiguous()
+        dg = None if dgates is None else dgates.to(torch.float32).contiguous()
+        dx = torch.empty_like(x)
+        dw_down = torch.empty((r, d), dtype=torch.float32, device=dev)
+        dw_up = torch.empty((nb, r), dtype=torch.float32, device=dev)
+        ws = torch.empty(_lib.load().mom_route_bwd_workspace_size(B, S, d, r, nb), dtype=torch.uint8, device=dev)
+        _lib.call("mom_route_bwd", x.data_ptr(), _dt_code(x.dtype), B, S, d, wd.data_ptr(),
+                  wu.data_ptr(), cd, r, nb, top, probs.data_ptr(), top_idx.data_ptr(), _lib.I64,
+                  gates.data_ptr(), act.data_ptr(), None, _ptr(dg), _ptr(dp), dx.data_ptr(),
+                  _dt_code(x.dtype), 0, dw_down.data_ptr(), dw_up.data_ptr(), ws.data_ptr(),
+                  ws.numel(), st)
+        return dx, dw_down.to(wd_dtype), dw_up.to(wu_dtype), None, None, None, None
+
+
+def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
+              scan_mode: str = "fp64"):
+    """Fused causal router: returns (router_probs, top_idx, top_gates).
+
+    x (B, S, d) fp32/bf16 on CUDA; w_down (r, d) and w_up (nb, r) are the
+    router_down / router_up weights (any float dtype; they are cast to the
+    compute dtype — autocast's when enabled, as nn.Linear would be). noise
+    (B, S, nb): the already-scaled Gumbel noise added before top-k, or None.
+    scan_mode "fp64" reproduces torch's CPU cumsum bit-for-bit, "fp32" its
+    CUDA cumsum.
+    """
+    if not x.is_cuda:
+        raise RuntimeError("sm100 mom_route: x must be on a CUDA device")
+    if x.dim() != 3 or w_down.dim() != 2 or w_up.dim() != 2 or w_down.shape[1] != x.shape[2] \
+            or w_up.shape[1] != w_down.shape[0]:
+        raise RuntimeError(
+            f"sm100 mom_route: shapes x {tuple(x.shape)}, w_down {tuple(w_down.shape)}, "
+            f"w_up {tuple(w_up.shape)} disagree")
+    if scan_mode not in _lib.SCAN_MODES:
+        raise RuntimeError(f"sm100 mom_route: scan_mode must be one of {sorted(_lib.SCAN_MODES)}")
+    cd = compute_dtype or _compute_dtype(w_down)
+    return _MomRouteFunction.apply(x, w_down, w_up, noise, int(top_blocks), cd, scan_mode)
+
+
+def gumbel_noise(shape, device, noise_scale: float):
+    """Scaled Gumbel noise drawn exactly as the reference draws it
+    (model.py:209-213: torch.rand_like on the fp32 logits)."""
+    u = torch.rand(shape, device=device, dtype=torch.float32)
+    return noise_scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
+
+
+__all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "gumbel_noise"]

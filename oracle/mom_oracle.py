@@ -252,28 +252,28 @@ def read_forward(q, k, v, top_idx, log_gates, num_blocks: int, block_size: int,
 
 
 def read_backward(q, k, v, top_idx, log_gates, dout, num_blocks: int,
-                  block_size: int) -> dict:
+                  block_size: int, dtype=f64) -> dict:
     """fp64 gradients of ``read_forward`` with respect to q, k, v, log_gates.
 
     Same decomposition as mom_kernels/triton_gpu.py:143-320: P rebuilt from
     the scores, dS = P * (dP - delta), dq = dS k * scale, dk = dS^T q * scale,
     dv = P^T do, and dlog_gates[b,s,t] = sum_h sum_{j in block top[b,s,t]} dS.
     """
-    q = np.asarray(q, f64)
+    q = np.asarray(q, dtype)
     B, S, H, hd = q.shape
     L = k.shape[0]
-    scale = 1.0 / math.sqrt(hd)
-    kh = np.asarray(k, f64).reshape(L, H, hd).transpose(1, 0, 2)
-    vh = np.asarray(v, f64).reshape(L, H, hd).transpose(1, 0, 2)
-    bias = np.repeat(block_bias(top_idx, log_gates, num_blocks), block_size, axis=-1)
+    scale = dtype(1.0 / math.sqrt(hd))
+    kh = np.asarray(k, dtype).reshape(L, H, hd).transpose(1, 0, 2)
+    vh = np.asarray(v, dtype).reshape(L, H, hd).transpose(1, 0, 2)
+    bias = np.repeat(block_bias(top_idx, log_gates, num_blocks), block_size, axis=-1).astype(dtype)
     idx = np.asarray(top_idx)
-    dq = np.empty((B, S, H, hd), f64)
-    dk = np.zeros((H, L, hd), f64)
-    dv = np.zeros((H, L, hd), f64)
-    dlg = np.zeros(idx.shape, f64)
+    dq = np.empty((B, S, H, hd), dtype)
+    dk = np.zeros((H, L, hd), dtype)
+    dv = np.zeros((H, L, hd), dtype)
+    dlg = np.zeros(idx.shape, dtype)
     for b in range(B):
         qb = q[b].transpose(1, 0, 2)
-        dob = np.asarray(dout[b], f64).transpose(1, 0, 2)
+        dob = np.asarray(dout[b], dtype).transpose(1, 0, 2)
         sc = np.matmul(qb, kh.transpose(0, 2, 1)) * scale + bias[b][None]
         p = np.exp(sc - sc.max(-1, keepdims=True))
         p /= p.sum(-1, keepdims=True)
@@ -293,7 +293,7 @@ def read_backward(q, k, v, top_idx, log_gates, dout, num_blocks: int,
 # ------------------------------------------------------------------ MoM layer
 def layer_forward(x, params: dict, n_heads: int, num_blocks: int, block_size: int,
                   top_k: int, compute: str = "f32", noise=None,
-                  scan_mode: str = "fp64") -> dict:
+                  scan_mode: str = "fp64", read_dtype=f64) -> dict:
     """MoMLayer.forward (model.py:189-276) as autocast runs it in ``compute``.
 
     params: w_down (r,d), w_up (nb,r), wq/wk/wv/wo (d,d), mom_scale (scalar),
@@ -308,7 +308,7 @@ def layer_forward(x, params: dict, n_heads: int, num_blocks: int, block_size: in
     slots = np.asarray(params["M_blocks"], f32).reshape(L, d)
     k = linear(slots, params["wk"], compute)
     v = linear(slots, params["wv"], compute)
-    rd = read_forward(q, k, v, rt["top_idx"], rt["log_gates"], num_blocks, block_size)
+    rd = read_forward(q, k, v, rt["top_idx"], rt["log_gates"], num_blocks, block_size, read_dtype)
     r = round_to(rd["out"], compute).reshape(B, S, d)
     o = linear(r, params["wo"], compute)
     out = (f32(params["mom_scale"]) * o).astype(f32)
@@ -316,7 +316,7 @@ def layer_forward(x, params: dict, n_heads: int, num_blocks: int, block_size: in
 
 
 def layer_backward(fwd: dict, x, params: dict, dout, n_heads: int, num_blocks: int,
-                   block_size: int, dprobs=None) -> dict:
+                   block_size: int, dprobs=None, read_dtype=f64) -> dict:
     """fp64 adjoint of ``layer_forward`` (gradients of every parameter and x)."""
     x = np.asarray(x, f64)
     B, S, d = x.shape
@@ -331,7 +331,7 @@ def layer_backward(fwd: dict, x, params: dict, dout, n_heads: int, num_blocks: i
     dr = do_ @ np.asarray(params["wo"], f64)
     rb = read_backward(fwd["q"], fwd["k"], fwd["v"], fwd["router"]["top_idx"],
                        fwd["router"]["log_gates"], dr.reshape(B, S, n_heads, hd),
-                       num_blocks, block_size)
+                       num_blocks, block_size, read_dtype)
     dq = rb["dq"].reshape(B, S, d)
     dwq = np.einsum("bsi,bsj->ij", dq, x)
     dx = dq @ np.asarray(params["wq"], f64)
@@ -353,3 +353,41 @@ def scaled_err(a, b) -> float:
     a = np.asarray(a, f64)
     b = np.asarray(b, f64)
     return float(np.abs(a - b).max()) / max(float(np.abs(b).max()), 1e-6)
+
+
+# ------------------------------------------------------- timed CPU baseline
+def layer_step_fp32(x, params: dict, dout, n_heads: int, num_blocks: int, block_size: int,
+                    top_k: int) -> dict:
+    """One MoM layer forward + backward in plain fp32 numpy, dense over all L
+    slots as the reference's eager path computes it (model.py:189-276 with
+    mom_kernels/reference.py:14-61, autograd in fp32). This is the port timed
+    as the CPU baseline; the fp64 functions above are the checker."""
+    x = np.asarray(x, f32)
+    B, S, d = x.shape
+    hd = d // n_heads
+    L = num_blocks * block_size
+    wq, wk, wv, wo = (np.asarray(params[k], f32) for k in ("wq", "wk", "wv", "wo"))
+    rt = router_forward(x, params["w_down"], params["w_up"], top_k, "f32")
+    q = (x @ wq.T).reshape(B, S, n_heads, hd)
+    slots = np.asarray(params["M_blocks"], f32).reshape(L, d)
+    k = slots @ wk.T
+    v = slots @ wv.T
+    rd = read_forward(q, k, v, rt["top_idx"], rt["log_gates"], num_blocks, block_size, f32)
+    r = rd["out"].reshape(B, S, d).astype(f32)
+    o = r @ wo.T
+    s = f32(params["mom_scale"])
+    out = s * o
+    do_ = np.asarray(dout, f32) * s
+    dwo = do_.reshape(-1, d).T @ r.reshape(-1, d)
+    dr = do_ @ wo
+    rb = read_backward(q, k, v, rt["top_idx"], rt["log_gates"], dr.reshape(B, S, n_heads, hd),
+                       num_blocks, block_size, f32)
+    dq = rb["dq"].reshape(B, S, d)
+    dwq = dq.reshape(-1, d).T @ x.reshape(-1, d)
+    dx = dq @ wq
+    dwk = rb["dk"].T @ slots
+    dwv = rb["dv"].T @ slots
+    dslots = rb["dk"] @ wk + rb["dv"] @ wv
+    rtb = router_backward(rt, x, params["w_down"], params["w_up"], rb["dlog_gates"])
+    dx = dx + rtb["dx"].astype(f32)
+    return dict(out=out, dx=dx, dwq=dwq, dwk=dwk, dwv=dwv, dwo=dwo, dM=dslots)

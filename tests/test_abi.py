@@ -1,0 +1,128 @@
+"""CPU tests of the C ABI boundary and the Python door (no GPU needed):
+the library loads, exports every function include/naylis_mom.h declares, and
+rejects bad arguments with the documented status codes before any device work.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "naylis_mom.h")
+
+
+def _declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:MOM_API\s+)?(?:const\s+)?\w+\s*\*?\s*(mom_\w+)\s*\(", src, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from naylis_b200 import _lib, build
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_the_survey_minimum():
+    names = _declared_functions()
+    for required in ("mom_route_fwd", "mom_route_bwd", "mom_bucket", "mom_read_fwd", "mom_read_bwd",
+                     "mom_last_error_string", "mom_plan_size", "mom_route_workspace_size",
+                     "mom_read_bwd_workspace_size", "mom_prefix_mean"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from naylis_b200 import _lib
+    names = _declared_functions()
+    assert names
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in naylis_mom.h but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+
+
+def test_only_declared_symbols_are_exported(lib):
+    import subprocess
+    from naylis_b200 import _lib
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("nm unavailable")
+    exported = {ln.split()[-1] for ln in out.stdout.splitlines() if " T " in ln}
+    ours = {s for s in exported if s.startswith("mom_")}
+    assert ours == set(_declared_functions())
+
+
+def test_version_and_error_string(lib):
+    assert lib.mom_version() >= 100
+    assert isinstance(lib.mom_last_error_string(), bytes)
+
+
+def test_invalid_arguments_fail_before_device_work(lib):
+    from naylis_b200 import _lib
+    # router: d not a multiple of 8
+    rc = lib.mom_route_fwd(None, _lib.BF16, 1, 4, 12, None, None, _lib.BF16, 32, 8, 2, None, 0,
+                           None, None, _lib.I64, None, None, None, None, 0, None)
+    assert rc == 1 and b"multiple of 8" in lib.mom_last_error_string()
+    # router: top > nb
+    rc = lib.mom_route_fwd(None, _lib.BF16, 1, 4, 64, None, None, _lib.BF16, 32, 2, 3, None, 0,
+                           None, None, _lib.I64, None, None, None, None, 0, None)
+    assert rc == 1
+    # read: head_dim 96 is unsupported (status 2), fp32 is invalid (status 1)
+    rc = lib.mom_read_fwd(None, None, None, _lib.BF16, 1, 1, 2, 96, 4, 64, 2, None, None, None, None)
+    assert rc == 2
+    rc = lib.mom_read_fwd(None, None, None, _lib.F32, 1, 1, 2, 64, 4, 64, 2, None, None, None, None)
+    assert rc == 1
+    # bucketing: too many routing sets (top-4 of 32 blocks) is reported as unsupported
+    rc = lib.mom_bucket(None, _lib.I64, None, 16, 32, 4, None, 0, None)
+    assert rc == 2
+    assert lib.mom_plan_size(16, 32, 4) == 0
+    # plan too small
+    rc = lib.mom_bucket(None, _lib.I64, None, 1024, 8, 2, ctypes.c_void_p(16), 8, None)
+    assert rc == 4
+
+
+def test_plan_size_grows_with_tokens(lib):
+    a, b = lib.mom_plan_size(1024, 8, 2), lib.mom_plan_size(16384, 8, 2)
+    assert 0 < a < b
+    assert lib.mom_read_bwd_workspace_size(8, 2048, 16) >= 8 * 2048 * 16 * 4
+    assert lib.mom_route_workspace_size(8, 2048, 1024, 32, 8, 1) >= 8 * 2048 * 1024 * 2
+
+
+def test_door_fails_loud_off_gpu():
+    from naylis_b200 import mom_kernels as mk
+    with pytest.raises(RuntimeError):
+        mk.preflight("cpu")
+    with pytest.raises(RuntimeError):
+        mk.resolve_mode(torch.device("cpu"), torch.bfloat16, head_dim=64)
+    with pytest.raises(RuntimeError):
+        mk.resolve_mode("cuda", torch.float32, head_dim=64)
+    with pytest.raises(RuntimeError):
+        mk.resolve_mode("cuda", torch.bfloat16, head_dim=96)
+    q = torch.zeros(1, 4, 2, 64, dtype=torch.bfloat16)
+    k = torch.zeros(256, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):
+        mk.mom_read(q, k, k, torch.zeros(1, 4, 2, dtype=torch.int64), torch.ones(1, 4, 2),
+                    num_blocks=4, block_size=64)
+    with pytest.raises(RuntimeError):
+        mk.mom_route(torch.zeros(1, 4, 64), torch.zeros(8, 64), torch.zeros(4, 8), 2)
+
+
+def test_layer_eager_path_matches_reference_semantics():
+    """use_kernel=False is the reference's eager path: it must equal the oracle
+    on the reference test-suite geometry (fp32)."""
+    import numpy as np
+    import golden_inputs as gi
+    import mom_oracle as O
+    from naylis_b200.model import MoMLayer
+    geo = gi.SMALL_F32
+    layer = MoMLayer(geo["d"], geo["H"], geo["nb"] * geo["bs"], geo["bs"], geo["top"], geo["r"])
+    inp = gi.layer_inputs(geo, layer)
+    layer.eval()
+    with torch.no_grad():
+        out = layer(inp["x"], inp["M"])
+    g = np.load(os.path.join(ROOT, "tests", "golden", "small_f32.npz"))
+    assert O.scaled_err(out.numpy(), g["out"]) < 1e-6

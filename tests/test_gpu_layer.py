@@ -1,0 +1,105 @@
+"""GPU parity of the whole MoM layer (router + projections + read, forward and
+backward) with ``use_kernel=True`` (mode "sm100"), under bf16 autocast as the
+reference trains, against the reference's golden vectors and the oracle.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import mom_oracle as O
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _layer(geo, use_kernel=True):
+    from naylis_b200.model import MoMLayer
+    layer = MoMLayer(d_model=geo["d"], n_heads=geo["H"], mem_size=geo["nb"] * geo["bs"],
+                     block_size=geo["bs"], top_blocks=geo["top"], router_rank=geo["r"],
+                     use_kernel=use_kernel)
+    inp = gi.layer_inputs(geo, layer)
+    return layer, inp
+
+
+def _run(layer, inp, dout, train=True):
+    dev = torch.device("cuda")
+    layer = layer.to(dev)
+    layer.train(train)
+    layer.noise_scale = 0.0
+    x = inp["x"].to(dev).requires_grad_(True)
+    M = inp["M"].to(dev).requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = layer(x, M)
+    out.backward(dout.to(dev))
+    torch.cuda.synchronize()
+    res = {"out": out.detach().float().cpu().numpy(), "dx": x.grad.float().cpu().numpy(),
+           "dM_blocks": M.grad.float().cpu().numpy(),
+           "top_idx": layer.last_top_idx.cpu().numpy()}
+    for name, p in layer.named_parameters():
+        res["d_" + name.replace(".weight", "")] = p.grad.float().cpu().numpy()
+    return res
+
+
+def test_layer_matches_reference_golden_bf16():
+    geo = gi.SMALL_BF16
+    g = np.load(os.path.join(GOLDEN, "small_bf16.npz"))
+    layer, inp = _layer(geo)
+    assert gi.input_digest(inp) == str(g["input_sha"])
+    got = _run(layer, inp, gi.upstream_grad(geo))
+    assert np.array_equal(got["top_idx"].reshape(g["top_idx"].shape), g["top_idx"])
+    keys = ["out", "dx", "dM_blocks", "d_router_down", "d_router_up", "d_q_proj", "d_k_proj",
+            "d_v_proj", "d_o_proj"]
+    errs = {k: O.scaled_err(got[k], g[k]) for k in keys}
+    assert all(e < TOL for e in errs.values()), errs
+    assert abs(got["d_mom_scale"][0] - g["d_mom_scale"][0]) <= TOL * abs(g["d_mom_scale"][0])
+
+
+def test_layer_config2_geometry_matches_oracle():
+    # config-2 geometry (d=1024, 16x64 heads, bank 8x128, rank 32, top-2) on
+    # one 2048-token sequence, so that the fp64 oracle stays within seconds
+    geo = dict(B=1, S=2048, d=1024, H=16, nb=8, bs=128, top=2, r=32, seed=0, x_std=1.0,
+               m_std=0.02, w_std=0.02, mom_scale=1.0)
+    layer, inp = _layer(geo)
+    dout = gi.upstream_grad(geo)
+    got = _run(layer, inp, dout)
+    P = gi.oracle_params(inp, geo)
+    f = O.layer_forward(inp["x"].numpy(), P, geo["H"], geo["nb"], geo["bs"], geo["top"], "bf16")
+    mism = np.any(got["top_idx"].reshape(f["router"]["top_idx"].shape) != f["router"]["top_idx"], -1)
+    assert not mism.any(), f"{int(mism.sum())} routing mismatches"
+    b = O.layer_backward(f, inp["x"].numpy(), P, dout.numpy(), geo["H"], geo["nb"], geo["bs"])
+    pairs = [("out", f["out"]), ("dx", b["dx"]), ("dM_blocks", b["dM_blocks"]),
+             ("d_router_down", b["dw_down"]), ("d_router_up", b["dw_up"]), ("d_q_proj", b["dwq"]),
+             ("d_k_proj", b["dwk"]), ("d_v_proj", b["dwv"]), ("d_o_proj", b["dwo"])]
+    errs = {k: O.scaled_err(got[k], ref) for k, ref in pairs}
+    assert all(e < TOL for e in errs.values()), errs
+
+
+def test_layer_kernel_path_is_causal():
+    geo = dict(B=2, S=512, d=256, H=4, nb=8, bs=64, top=2, r=32, seed=3, x_std=1.0,
+               m_std=1.0, w_std=0.06, mom_scale=1.0)
+    layer, inp = _layer(geo)
+    dev = torch.device("cuda")
+    layer = layer.to(dev).eval()
+    x = inp["x"].to(dev)
+    M = inp["M"].to(dev)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        a = layer(x, M)
+        x2 = x.clone()
+        x2[:, 301:] += 1.0
+        b = layer(x2, M)
+    assert torch.equal(a[:, :301], b[:, :301])
+
+
+def test_resolve_mode_contract_on_gpu():
+    from naylis_b200 import mom_kernels as mk
+    assert mk.resolve_mode("cuda", torch.bfloat16, head_dim=64) == "sm100"
+    assert mk.resolve_mode(torch.device("cuda", 0), torch.bfloat16, head_dim=128) == "sm100"
+    with pytest.raises(RuntimeError):
+        mk.resolve_mode("cuda", torch.float32, head_dim=64)
+    with pytest.raises(RuntimeError):
+        mk.resolve_mode("cuda", torch.bfloat16, head_dim=96)
+    assert mk.preflight("cuda") is None

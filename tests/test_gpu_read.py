@@ -1,0 +1,148 @@
+"""GPU parity of the sm100 gated memory read (forward and backward) through
+the C ABI, against the oracle and the reference's golden vectors.
+
+Tolerance: scaled max error (max|a-b| / max|b|) < 2e-2 in bf16, the
+reference's own bar (tests/test_parity.py:477-490).
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import mom_oracle as O
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+def _mk(B, S, H, hd, nb, bs, top, seed, routing="random", dup=False):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(B, S, H, hd, generator=g) * 0.7)
+    k = torch.randn(nb * bs, H * hd, generator=g) * 0.4
+    v = torch.randn(nb * bs, H * hd, generator=g) * 0.4
+    gates = torch.softmax(torch.randn(B, S, top, generator=g), -1)
+    if routing == "random":
+        idx = torch.argsort(torch.rand(B, S, nb, generator=g), -1)[..., :top]
+    elif routing == "skewed":
+        idx = torch.arange(top).expand(B, S, top).clone()
+        idx[:, ::7] = torch.argsort(torch.rand(B, S, nb, generator=g), -1)[:, ::7, :top]
+    else:
+        raise ValueError(routing)
+    if dup:
+        idx[:, ::3, -1] = idx[:, ::3, 0]
+    dout = torch.randn(B, S, H, hd, generator=g)
+    bf = lambda t: t.to(torch.bfloat16)
+    return bf(q), bf(k), bf(v), idx, gates, bf(dout)
+
+
+def _run_gpu(q, k, v, idx, gates, dout, nb, bs):
+    from naylis_b200 import mom_kernels as mk
+    dev = torch.device("cuda")
+    qd, kd, vd = (t.to(dev).requires_grad_(True) for t in (q, k, v))
+    gd = gates.to(dev).requires_grad_(True)
+    out = mk.mom_read(qd, kd, vd, idx.to(dev), gd, num_blocks=nb, block_size=bs, mode="sm100")
+    out.backward(dout.to(dev))
+    torch.cuda.synchronize()
+    return {"out": out.detach().float().cpu().numpy(), "dq": qd.grad.float().cpu().numpy(),
+            "dk": kd.grad.float().cpu().numpy(), "dv": vd.grad.float().cpu().numpy(),
+            "dgates": gd.grad.float().cpu().numpy()}
+
+
+def _oracle(q, k, v, idx, gates, dout, nb, bs):
+    lg = np.log(np.maximum(gates.numpy().astype(np.float64), 1e-9)).astype(np.float32)
+    args = (q.float().numpy(), k.float().numpy(), v.float().numpy(), idx.numpy(), lg)
+    f = O.read_forward(*args, nb, bs)
+    b = O.read_backward(*args, dout.float().numpy(), nb, bs)
+    return {"out": f["out"], "dq": b["dq"], "dk": b["dk"], "dv": b["dv"],
+            "dgates": b["dlog_gates"] / np.maximum(gates.numpy(), 1e-9)}
+
+
+def _compare(got, ref, tol=TOL):
+    errs = {k: O.scaled_err(got[k], ref[k]) for k in ref}
+    bad = {k: e for k, e in errs.items() if not e < tol}
+    assert not bad, f"scaled errors over {tol}: {bad} (all: {errs})"
+    return errs
+
+
+def test_read_matches_reference_golden():
+    geo = gi.READ
+    g = np.load(os.path.join(GOLDEN, "read_bf16.npz"))
+    q, k, v, top, gates, dout = gi.read_inputs(geo, "bf16")
+    got = _run_gpu(q, k, v, top, gates, dout, geo["nb"], geo["bs"])
+    _compare(got, {k_: g[k_] for k_ in ("out", "dq", "dk", "dv", "dgates")})
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=2, S=512, H=4, hd=64, nb=8, bs=128, top=2, seed=1),            # config-2 geometry, fewer tokens
+    dict(B=1, S=300, H=2, hd=128, nb=8, bs=128, top=2, seed=2),           # head_dim 128, ragged S
+    dict(B=2, S=129, H=2, hd=64, nb=4, bs=64, top=1, seed=3),             # top-1
+    dict(B=2, S=200, H=3, hd=64, nb=4, bs=64, top=3, seed=4),             # top-3, odd head count
+    dict(B=1, S=257, H=2, hd=64, nb=6, bs=48, top=2, seed=5),             # block not a multiple of 64
+    dict(B=2, S=333, H=2, hd=64, nb=8, bs=128, top=2, seed=6, routing="skewed"),  # one dominant set
+    dict(B=2, S=150, H=2, hd=64, nb=4, bs=64, top=2, seed=7, dup=True),   # repeated block ids
+])
+def test_read_matches_oracle(case):
+    case = dict(case)
+    routing = case.pop("routing", "random")
+    dup = case.pop("dup", False)
+    seed = case.pop("seed")
+    q, k, v, idx, gates, dout = _mk(**case, seed=seed, routing=routing, dup=dup)
+    got = _run_gpu(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    ref = _oracle(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    _compare(got, ref)
+
+
+def test_read_is_deterministic_forward_and_dq():
+    q, k, v, idx, gates, dout = _mk(2, 256, 2, 64, 8, 128, 2, seed=11)
+    a = _run_gpu(q, k, v, idx, gates, dout, 8, 128)
+    b = _run_gpu(q, k, v, idx, gates, dout, 8, 128)
+    for key in ("out", "dq", "dgates"):
+        assert np.array_equal(a[key], b[key]), key
+
+
+def test_read_empty_batch():
+    from naylis_b200 import mom_kernels as mk
+    dev = torch.device("cuda")
+    q = torch.zeros(0, 16, 2, 64, dtype=torch.bfloat16, device=dev, requires_grad=True)
+    k = torch.randn(256, 128, dtype=torch.bfloat16, device=dev, requires_grad=True)
+    v = torch.randn(256, 128, dtype=torch.bfloat16, device=dev, requires_grad=True)
+    idx = torch.zeros(0, 16, 2, dtype=torch.int64, device=dev)
+    g = torch.full((0, 16, 2), 0.5, device=dev, requires_grad=True)
+    out = mk.mom_read(q, k, v, idx, g, num_blocks=4, block_size=64)
+    assert out.shape == q.shape
+    out.sum().backward()
+    assert float(k.grad.abs().sum()) == 0.0
+
+
+def test_bucket_flags_out_of_range_index():
+    from naylis_b200 import _lib
+    dev = torch.device("cuda")
+    N, nb, top = 100, 4, 2
+    idx = torch.randint(0, nb, (N, top), dtype=torch.int64, device=dev)
+    idx[17, 1] = nb + 3   # out of range: must be reported, never read
+    lg = torch.zeros(N, top, device=dev)
+    plan = torch.empty(_lib.load().mom_plan_size(N, nb, top), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("mom_bucket", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
+              plan.numel(), st)
+    with pytest.raises(_lib.MomError) as ei:
+        _lib.call("mom_plan_check", plan.data_ptr(), N, nb, top, st)
+    assert ei.value.status == 7
+
+
+def test_read_rejects_contract_violations():
+    from naylis_b200 import mom_kernels as mk
+    dev = torch.device("cuda")
+    q = torch.randn(1, 8, 2, 64, device=dev)                     # fp32: rejected
+    k = torch.randn(256, 128, device=dev, dtype=torch.bfloat16)
+    idx = torch.zeros(1, 8, 2, dtype=torch.int64, device=dev)
+    g = torch.full((1, 8, 2), 0.5, device=dev)
+    with pytest.raises(RuntimeError):
+        mk.mom_read(q, k, k, idx, g, num_blocks=4, block_size=64)
+    with pytest.raises(RuntimeError):
+        mk.mom_read(q.bfloat16(), k, k, idx, g, num_blocks=3, block_size=64)   # L mismatch
+    with pytest.raises(RuntimeError):
+        mk.mom_read(q.bfloat16(), k.unsqueeze(0), k.unsqueeze(0), idx, g, num_blocks=4, block_size=64)

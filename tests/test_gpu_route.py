@@ -1,0 +1,160 @@
+"""GPU parity of the fused causal router through the C ABI.
+
+* prefix mean: bitwise against the reference's golden digests (fp64 mode,
+  torch CPU cumsum semantics) and against torch.cumsum on CUDA (fp32 mode);
+* top-k indices: bitwise against the oracle and the reference golden vectors
+  (a token may differ only where the oracle's k-th / (k+1)-th logit gap is
+  within a rounding of zero — reported, and required to be absent here);
+* probabilities and gates: scaled error < 1e-5 (fp32) / 2e-2 (bf16);
+* backward: dx, dW_down, dW_up against the oracle's fp64 adjoint.
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import golden_inputs as gi
+import mom_oracle as O
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefix_mean_gpu(x, mode, out_dtype=torch.float32):
+    from naylis_b200 import _lib
+    xd = x.cuda().contiguous()
+    B, S, d = xd.shape
+    out = torch.empty(B, S, d, dtype=out_dtype, device="cuda")
+    code = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+    _lib.call("mom_prefix_mean", xd.data_ptr(), code[xd.dtype], B, S, d, out.data_ptr(),
+              code[out_dtype], _lib.SCAN_MODES[mode], torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return out.cpu()
+
+
+@pytest.mark.parametrize("name", ["f32", "bf16"])
+def test_prefix_mean_fp64_mode_bitwise_vs_reference(name):
+    g = np.load(os.path.join(GOLDEN, "scan.npz"))
+    x = gi.scan_input(name)
+    h = _prefix_mean_gpu(x, "fp64")
+    assert hashlib.sha256(h.numpy().tobytes()).hexdigest() == str(g[f"h_sha_{name}"])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_prefix_mean_fp32_mode_bitwise_vs_torch_cuda(dtype):
+    torch.manual_seed(0)
+    x = torch.randn(2, 2048, 1024).to(dtype)
+    h = _prefix_mean_gpu(x, "fp32")
+    xc = x.cuda()
+    ref = torch.cumsum(xc.float(), dim=1) / torch.arange(1, 2049, device="cuda",
+                                                          dtype=torch.float32).view(1, -1, 1)
+    assert torch.equal(h, ref.cpu())
+
+
+def test_prefix_mean_causality_and_bf16_output():
+    torch.manual_seed(1)
+    x = torch.randn(3, 700, 64)
+    h = _prefix_mean_gpu(x, "fp64")
+    x2 = x.clone()
+    x2[:, 400:] += 3.0
+    h2 = _prefix_mean_gpu(x2, "fp64")
+    assert torch.equal(h[:, :400], h2[:, :400])
+    hb = _prefix_mean_gpu(x, "fp64", torch.bfloat16)
+    assert torch.equal(hb, h.to(torch.bfloat16))
+
+
+def _route_gpu(x, w_down, w_up, top, compute_dtype, noise=None, scan_mode="fp64", grad=None):
+    from naylis_b200 import mom_kernels as mk
+    xd = x.cuda().requires_grad_(grad is not None)
+    wd = w_down.cuda().requires_grad_(grad is not None)
+    wu = w_up.cuda().requires_grad_(grad is not None)
+    nz = None if noise is None else noise.cuda()
+    probs, idx, gates = mk.mom_route(xd, wd, wu, top, nz, compute_dtype=compute_dtype,
+                                     scan_mode=scan_mode)
+    res = {"probs": probs.detach().cpu().numpy(), "top_idx": idx.cpu().numpy(),
+           "gates": gates.detach().cpu().numpy()}
+    if grad is not None:
+        dgates, dprobs = (t.cuda() for t in grad)
+        torch.autograd.backward([gates, probs], [dgates, dprobs])
+        res.update(dx=xd.grad.float().cpu().numpy(), dw_down=wd.grad.cpu().numpy(),
+                   dw_up=wu.grad.cpu().numpy())
+    return res
+
+
+def _assert_indices(got_idx, rt, top, tag):
+    mism = np.any(got_idx != rt["top_idx"], axis=-1)
+    if mism.any():
+        margin = O.topk_margin(rt["noisy"], top)[mism]
+        raise AssertionError(f"{tag}: {int(mism.sum())} tokens differ; oracle top-k margins there: "
+                             f"{margin[:10]}")
+
+
+def test_router_cfg1_matches_reference_golden():
+    geo = gi.CFG1
+    g = np.load(os.path.join(GOLDEN, "cfg1_fwd.npz"))
+    inp = gi.layer_inputs(geo)
+    h = _prefix_mean_gpu(inp["x"], "fp64")
+    assert hashlib.sha256(h.numpy().tobytes()).hexdigest() == str(g["h_sha"])
+    got = _route_gpu(inp["x"], inp["w"]["router_down"], inp["w"]["router_up"], geo["top"],
+                     torch.float32)
+    assert np.array_equal(got["top_idx"], g["top_idx"])
+    assert O.scaled_err(got["probs"], g["probs"]) < 1e-5
+    assert O.scaled_err(got["gates"], g["gates"]) < 1e-5
+
+
+@pytest.mark.parametrize("compute,x_dtype,B,S,d,r,nb,top", [
+    ("bf16", torch.bfloat16, 2, 2048, 1024, 32, 8, 2),   # config-2 router geometry
+    ("bf16", torch.bfloat16, 1, 1000, 2048, 64, 32, 4),  # config-4 router geometry, ragged S
+    ("f32", torch.float32, 2, 300, 256, 16, 8, 2),       # SIMT head, odd rank
+    ("bf16", torch.float32, 1, 513, 512, 32, 8, 2),      # fp32 residual stream under autocast
+])
+def test_router_matches_oracle(compute, x_dtype, B, S, d, r, nb, top):
+    torch.manual_seed(B * 1000 + S)
+    x = torch.randn(B, S, d).to(x_dtype)
+    w_down = torch.randn(r, d) * 0.02
+    w_up = torch.randn(nb, r) * 0.02 * 8
+    cd = torch.bfloat16 if compute == "bf16" else torch.float32
+    got = _route_gpu(x, w_down, w_up, top, cd)
+    rt = O.router_forward(x.float().numpy(), w_down.numpy(), w_up.numpy(), top, compute)
+    _assert_indices(got["top_idx"], rt, top, "router")
+    tol = 1e-5 if compute == "f32" else 2e-2
+    assert O.scaled_err(got["probs"], rt["probs"]) < tol
+    assert O.scaled_err(got["gates"], rt["gates"]) < tol
+
+
+def test_router_noise_goes_into_topk_only():
+    torch.manual_seed(3)
+    x = torch.randn(2, 256, 512, dtype=torch.bfloat16)
+    w_down = torch.randn(32, 512) * 0.02
+    w_up = torch.randn(8, 32) * 0.2
+    noise = torch.randn(2, 256, 8) * 2.0
+    got = _route_gpu(x, w_down, w_up, 2, torch.bfloat16, noise=noise)
+    rt = O.router_forward(x.float().numpy(), w_down.numpy(), w_up.numpy(), 2, "bf16",
+                          noise=noise.numpy())
+    _assert_indices(got["top_idx"], rt, 2, "noisy router")
+    assert O.scaled_err(got["probs"], rt["probs"]) < 2e-2   # probs from the clean logits
+    assert O.scaled_err(got["gates"], rt["gates"]) < 2e-2   # gates from the noisy top values
+
+
+@pytest.mark.parametrize("compute,tol", [("f32", 1e-5), ("bf16", 2e-2)])
+def test_router_backward_matches_oracle(compute, tol):
+    torch.manual_seed(7)
+    B, S, d, r, nb, top = 2, 384, 256, 32, 8, 2
+    cd = torch.bfloat16 if compute == "bf16" else torch.float32
+    x = torch.randn(B, S, d).to(cd)
+    w_down = torch.randn(r, d) * 0.05
+    w_up = torch.randn(nb, r) * 0.3
+    dgates = torch.randn(B, S, top)
+    dprobs = torch.randn(B, S, nb)
+    got = _route_gpu(x, w_down, w_up, top, cd, grad=(dgates, dprobs))
+    rt = O.router_forward(x.float().numpy(), w_down.numpy(), w_up.numpy(), top, compute)
+    _assert_indices(got["top_idx"], rt, top, "router")
+    g = rt["gates"].astype(np.float64)
+    dlg = dgates.numpy().astype(np.float64) * np.maximum(g, 1e-9)   # d/dlog_gates
+    ref = O.router_backward(rt, x.float().numpy(), w_down.numpy(), w_up.numpy(), dlg,
+                            dprobs.numpy())
+    for key in ("dx", "dw_down", "dw_up"):
+        err = O.scaled_err(got[key], ref[key])
+        assert err < tol, f"{key}: {err:.3e}"
