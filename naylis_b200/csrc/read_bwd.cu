@@ -8,7 +8,9 @@
 //   read_bwd_dq_kernel    one CTA per token tile, all heads in turn:
 //                         delta = rowsum(O*dO), dQ = dS K * scale, and the gate
 //                         gradient dlog_gates = sum over heads and the block's
-//                         slots of dS, reduced in registers (no atomics).
+//                         slots of dS, reduced in registers (no atomics) from
+//                         per-block fp32 sums of P*dP and P, so that it does not
+//                         inherit the rounding of the bf16 output used for delta.
 //   read_bwd_dkdv_kernel  one CTA per (block, 64-slot chunk, head, split): walks
 //                         the tiles whose set contains the block, accumulates
 //                         dK = dS^T Q * scale and dV = P^T dO in registers and
@@ -138,9 +140,12 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
         float dqa[NTO][4];
 #pragma unroll
         for (int j = 0; j < NTO; ++j) dqa[j][0] = dqa[j][1] = dqa[j][2] = dqa[j][3] = 0.0f;
-        float db[2][kMaxTopBwd];
+        // per block j: A_j = sum P*dP and B_j = sum P over the block's slots
+        // (fp32); the gate gradient is A_j - delta * B_j with delta = sum_j A_j,
+        // which cancels exactly when a row reads a single block.
+        float dba[2][kMaxTopBwd], dbb[2][kMaxTopBwd];
 #pragma unroll
-        for (int jj = 0; jj < kMaxTopBwd; ++jj) db[0][jj] = db[1][jj] = 0.0f;
+        for (int jj = 0; jj < kMaxTopBwd; ++jj) dba[0][jj] = dba[1][jj] = dbb[0][jj] = dbb[1][jj] = 0.0f;
 
 #pragma unroll 1
         for (int c = 0; c < nchunk; ++c) {
@@ -172,7 +177,7 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
                 }
             }
             const float bias0 = sBias[r0 * top + j], bias1 = sBias[(r0 + 8) * top + j];
-            float rs0 = 0.0f, rs1 = 0.0f;
+            float pa0 = 0.0f, pa1 = 0.0f, pb0 = 0.0f, pb1 = 0.0f;
             uint32_t dsf[NTS / 2][4];
 #pragma unroll
             for (int n = 0; n < NTS; ++n) {
@@ -185,15 +190,15 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
                         ? exp2f(fmaf(s[n][e], scale_log2, hi ? bias1 : bias0) - (hi ? lse1 : lse0))
                         : 0.0f;
                     ds[e] = p * (dp[n][e] - (hi ? dl1 : dl0));
+                    if (hi) { pa1 = fmaf(p, dp[n][e], pa1); pb1 += p; }
+                    else    { pa0 = fmaf(p, dp[n][e], pa0); pb0 += p; }
                 }
-                rs0 += ds[0] + ds[1];
-                rs1 += ds[2] + ds[3];
                 dsf[n >> 1][(n & 1) * 2 + 0] = pack_bf16x2(ds[0], ds[1]);
                 dsf[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
             }
 #pragma unroll
             for (int jj = 0; jj < kMaxTopBwd; ++jj)
-                if (jj == j) { db[0][jj] += rs0; db[1][jj] += rs1; }
+                if (jj == j) { dba[0][jj] += pa0; dba[1][jj] += pa1; dbb[0][jj] += pb0; dbb[1][jj] += pb1; }
             // dQ += dS K
 #pragma unroll
             for (int kk = 0; kk < NTS / 2; ++kk) {
@@ -211,14 +216,20 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
         }
         cp_async_wait<0>();
 #pragma unroll
-        for (int jj = 0; jj < kMaxTopBwd; ++jj) {
+        for (int r = 0; r < 2; ++r) {
+            float sa = 0.0f, sb = 0.0f;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                float vsum = db[r][jj];
-                vsum += __shfl_xor_sync(0xffffffffu, vsum, 1);
-                vsum += __shfl_xor_sync(0xffffffffu, vsum, 2);
-                dbacc[r][jj] += vsum;
+            for (int jj = 0; jj < kMaxTopBwd; ++jj) {
+                dba[r][jj] += __shfl_xor_sync(0xffffffffu, dba[r][jj], 1);
+                dba[r][jj] += __shfl_xor_sync(0xffffffffu, dba[r][jj], 2);
+                dbb[r][jj] += __shfl_xor_sync(0xffffffffu, dbb[r][jj], 1);
+                dbb[r][jj] += __shfl_xor_sync(0xffffffffu, dbb[r][jj], 2);
+                sa += dba[r][jj];
+                sb += dbb[r][jj];
             }
+            const float delta_row = sb > 0.0f ? sa / sb : 0.0f;
+#pragma unroll
+            for (int jj = 0; jj < kMaxTopBwd; ++jj) dbacc[r][jj] += fmaf(-delta_row, dbb[r][jj], dba[r][jj]);
         }
         // dQ * scale -> stage in sQ (no longer read) -> 16-B stores
         __syncthreads();

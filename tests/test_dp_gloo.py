@@ -1,0 +1,157 @@
+"""Data-parallel gradient exchange (naylis_b200.data_parallel.GradAllReduce)
+on world_size-2 gloo process groups on CPU.
+
+* the bucketed, hook-driven all-reduce of a MoM layer + shared bank, each rank
+  on its own shard of the batch, equals the single-process full-batch
+  gradient (mean loss, so the average over ranks is exact up to rounding);
+* parameters that get no gradient in a step do not stall the exchange;
+* failure detection on the host: a rank that dies before the collective makes
+  the survivor's next exchange fail within the process-group timeout.
+"""
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _build(seed=0):
+    from naylis_b200.model import MoMLayer
+    torch.manual_seed(seed)
+    layer = MoMLayer(d_model=32, n_heads=2, mem_size=64, block_size=16, top_blocks=2, router_rank=8)
+    with torch.no_grad():
+        layer.mom_scale.fill_(0.5)
+    holder = torch.nn.Module()
+    holder.layer = layer
+    holder.M = torch.nn.Parameter(torch.randn(4, 16 * 32))
+    holder.unused = torch.nn.Parameter(torch.zeros(3))   # never receives a gradient
+    holder.train()
+    layer.noise_scale = 0.0
+    return holder
+
+
+def _data():
+    g = torch.Generator().manual_seed(123)
+    return torch.randn(4, 24, 32, generator=g)
+
+
+def _loss(holder, x):
+    out = holder.layer(x, holder.M)
+    return (out.float() ** 2).mean()
+
+
+def _worker(rank, world, port, q, mode):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        import sys
+        sys.path.insert(0, ROOT)
+        timeout = datetime.timedelta(seconds=10 if mode == "fault" else 60)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
+        from naylis_b200.data_parallel import GradAllReduce
+        holder = _build()
+        dp = GradAllReduce(holder, bucket_mb=0.004)      # tiny buckets: several in flight
+        x = _data()
+        shard = x.chunk(world, dim=0)[rank]
+        if mode == "fault":
+            # step 1 completes on both ranks; rank 1 then dies before step 2
+            dp.zero_grad()
+            _loss(holder, shard).backward()
+            dp.finish()
+            if rank == 1:
+                os._exit(3)
+            dp.zero_grad()
+            try:
+                _loss(holder, shard).backward()   # bucket all-reduces start in the hooks
+                dp.finish()
+                q.put((rank, "no error"))
+            except Exception as e:  # the survivor must see the failure, not hang
+                q.put((rank, f"error: {type(e).__name__}"))
+            q.close()
+            q.join_thread()       # flush the queue before the hard exit
+            os._exit(0)
+        for _ in range(2):   # two steps: zero_grad re-arms the hooks and views
+            dp.zero_grad()
+            _loss(holder, shard).backward()
+            dp.finish()
+        grads = {n: p.grad.clone() for n, p in holder.named_parameters()}
+        q.put((rank, {"grads": grads, "nbuckets": len(dp.buckets)}))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def _spawn(world, mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, mode)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    expected = world if mode != "fault" else 1
+    for _ in range(expected):
+        rank, res = q.get(timeout=120)
+        results[rank] = res
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+def test_grad_allreduce_equals_full_batch_gradient():
+    world = 2
+    res = _spawn(world, "ok")
+    for r in range(world):
+        assert isinstance(res[r], dict), res[r]
+    assert res[0]["nbuckets"] > 2
+    holder = _build()
+    for p in holder.parameters():
+        p.grad = None
+    _loss(holder, _data()).backward()
+    for n, p in holder.named_parameters():
+        ref = p.grad if p.grad is not None else torch.zeros_like(p)
+        for r in range(world):
+            got = res[r]["grads"][n]
+            assert torch.allclose(got, ref, rtol=1e-4, atol=1e-6), (n, (got - ref).abs().max())
+    # the shared bank gets its gradient once, summed over all uses, then averaged
+    assert float(res[0]["grads"]["M"].abs().sum()) > 0
+    assert torch.equal(res[0]["grads"]["unused"], torch.zeros(3))
+
+
+def test_rank_failure_is_detected_on_the_host():
+    res = _spawn(2, "fault")
+    assert 0 in res
+    assert str(res[0]).startswith("error"), res[0]
+
+
+@pytest.mark.parametrize("bucket_mb", [0.001, 64.0])
+def test_single_process_is_a_plain_backward(bucket_mb):
+    from naylis_b200.data_parallel import GradAllReduce
+    holder = _build()
+    dp = GradAllReduce(holder, bucket_mb=bucket_mb)
+    dp.zero_grad()
+    _loss(holder, _data()).backward()
+    dp.finish()
+    got = {n: p.grad.clone() for n, p in holder.named_parameters()}
+    ref_h = _build()
+    _loss(ref_h, _data()).backward()
+    for n, p in ref_h.named_parameters():
+        ref = p.grad if p.grad is not None else torch.zeros_like(p)
+        assert torch.allclose(got[n], ref, rtol=1e-6, atol=1e-7), n

@@ -61,7 +61,16 @@ def _oracle(q, k, v, idx, gates, dout, nb, bs):
 
 
 def _compare(got, ref, tol=TOL):
-    errs = {k: O.scaled_err(got[k], ref[k]) for k in ref}
+    """Scaled error per output. A reference that is identically zero in exact
+    arithmetic (the gate gradient of a token that reads a single block: top-1,
+    or the same block twice, since its softmax weights sum to one) has no
+    scale; there the kernel's value must be below an absolute 1e-4."""
+    errs = {}
+    for k in ref:
+        if float(np.abs(ref[k]).max()) < 1e-9:
+            errs[k] = float(np.abs(got[k]).max()) / 1e-4 * tol
+        else:
+            errs[k] = O.scaled_err(got[k], ref[k])
     bad = {k: e for k, e in errs.items() if not e < tol}
     assert not bad, f"scaled errors over {tol}: {bad} (all: {errs})"
     return errs
