@@ -240,6 +240,8 @@ int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *s
     if (e != cudaSuccess) return cuda_fail(e, "plan_check");
     if (err) {
         cudaMemsetAsync(P.err, 0, sizeof(int), st);
+        if (err & 2)
+            return fail(MOM_ERR_DEVICE_TIMEOUT, "a bounded device-side wait of a read kernel gave up");
         return fail(MOM_ERR_DEVICE_INDEX, "top_idx holds a block index outside [0, %lld)", (long long)nb);
     }
     return MOM_OK;

@@ -1,0 +1,362 @@
+// Gated memory read, forward, on the 5th-generation tensor cores (tcgen05).
+//
+// Same math as read_fwd.cu (reference: mom_kernels/reference.py:39-61 with the
+// bias of :14-29, triton_gpu.py:64-141), specialised for the shapes of the
+// Naylis configurations: head_dim 64, 128-slot blocks, at most two blocks per
+// routing set (top-2). A work item is (tile of <= 128 tokens sharing one block
+// set, head); CTAs are persistent over items.
+//
+// Warp roles (192 threads):
+//   warp 0     loader: K, V blocks by TMA (SWIZZLE_128B boxes of 128 slots x 64),
+//              the tile's Q rows by cp.async (gathered through the permutation)
+//   warp 1     TMEM owner and MMA issuer (one elected lane):
+//              S[128 x 256] = Q K^T into TMEM, then O[128 x 64] = P V
+//   warps 2-5  softmax (one TMEM lane = one token row per thread): row max,
+//              exp2, row sum, P as bf16 into shared memory; then the epilogue
+//              O / l -> global, log-sum-exp -> global
+// Q/K/V stages are double-buffered, O is double-buffered in TMEM, so the
+// epilogue of item i-1 and the loads of item i+1 overlap the softmax of item i.
+// All waits are bounded (tc::mbar_wait); a timeout sets bit 1 of the plan's
+// error word and every role unwinds.
+#include <cudaTypedefs.h>
+
+#include "launch.h"
+#include "tc_common.cuh"
+
+namespace mom {
+
+namespace {
+constexpr int kHD = 64;
+constexpr int kBS = 128;
+constexpr int kTM = 128;                       // token rows per tile (TMEM lanes)
+constexpr int kThreads = 192;
+constexpr uint32_t kQBytes = kTM * kHD * 2;    // 16 KiB
+constexpr uint32_t kBlkBytes = kBS * kHD * 2;  // 16 KiB per 128-slot block of K or V
+constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) + V(2 blocks)
+constexpr uint32_t kPBytes = kTM * 2 * kBS * 2;             // 64 KiB: P[128 x 256] bf16
+constexpr uint32_t kSmemBytes = 2 * kStageBytes + kPBytes + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;                // O buffers at columns 256 and 320
+
+struct Bars {
+    uint64_t full[2], empty[2], s_full, p_full, o_full[2], o_free[2], drain;
+    uint32_t tmem_base;
+    int abort;
+};
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                   const uint16_t *__restrict__ q, int H, int top, float scale_log2, PlanView P,
+                   uint16_t *__restrict__ out, float *__restrict__ lse) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char *sbase = smem_raw + (base - raw);
+    const uint32_t sP = base + 2 * kStageBytes;
+    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kPBytes);
+    volatile int *abort_flag = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = *P.ntiles;
+    const int nitems = ntiles * H;
+    const int64_t ld = static_cast<int64_t>(H) * kHD;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&bars->full[s], 33);
+            tc::mbar_init(&bars->empty[s], 1);
+            tc::mbar_init(&bars->o_full[s], 1);
+            tc::mbar_init(&bars->o_free[s], 128);
+        }
+        tc::mbar_init(&bars->s_full, 1);
+        tc::mbar_init(&bars->p_full, 128);
+        tc::mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&bars->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        tc::prefetch_tensormap(&tmap_k);
+        tc::prefetch_tensormap(&tmap_v);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ loader
+        int issued = 0;
+        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
+            const int s = i & 1, j = i >> 1;
+            if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+            const int tile = item / H, h = item % H;
+            const int4 td = P.tiles[tile];
+            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
+            int nblk = 0;
+            while (nblk < top && set[nblk] >= 0) ++nblk;
+            const int nload = nblk > 0 ? nblk : 1;
+            const uint32_t sQ = base + s * kStageBytes;
+            const uint32_t sK = sQ + kQBytes;
+            const uint32_t sV = sK + 2 * kBlkBytes;
+            if (lane == 0) {
+                tc::mbar_arrive_expect_tx(&bars->full[s], 2 * nload * kBlkBytes);
+                for (int jb = 0; jb < nload; ++jb) {
+                    const int blk = nblk > 0 ? set[jb] : 0;
+                    tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
+                    tc::tma_load_2d(sV + jb * kBlkBytes, &tmap_v, h * kHD, blk * kBS, &bars->full[s]);
+                }
+            }
+            for (int rr = 0; rr < kTM / 32; ++rr) {
+                const int r = rr * 32 + lane;
+                const int tok = r < td.y ? P.perm[td.x + r] : -1;
+                const uint16_t *src = tok >= 0 ? q + tok * ld + h * kHD : q;
+#pragma unroll
+                for (int c = 0; c < 8; ++c)
+                    cp_async16(sQ + r * 128 + ((c ^ (r & 7)) << 4), src + (tok >= 0 ? c * 8 : 0),
+                               tok >= 0 ? 16 : 0);
+            }
+            tc::cp_async_wait_all();
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive(&bars->full[s]);
+            issued = i + 1;
+        }
+        // make sure no TMA write is still in flight when the CTA retires
+        if (issued > 0) {
+            const int i = issued - 1;
+            tc::mbar_wait(&bars->full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
+        int prev_nblk = 1, prev_s = 0, count = 0;
+        bool ok = true;
+        auto issue_o = [&](int i) {   // O(i) = P V, stage of item i, buffer i & 1
+            const int b = i & 1;
+            if (!tc::mbar_wait(&bars->p_full, i & 1, P.err, 2, abort_flag)) return false;
+            if (!tc::mbar_wait(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) return false;
+            tc::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t sV = base + prev_s * kStageBytes + kQBytes + 2 * kBlkBytes;
+                const int ksteps = prev_nblk * (kBS / 16);
+                for (int kk = 0; kk < ksteps; ++kk) {
+                    const uint64_t ad = tc::smem_desc_sw128(sP + (kk >> 2) * (kTM * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(sV + kk * 2048, kBlkBytes * 2, 1024);
+                    tc::mma_bf16_ss(tmem + kOCol + b * kHD, ad, bd, idesc_o, kk > 0);
+                }
+                tc::mma_commit(&bars->o_full[b]);
+                tc::mma_commit(&bars->empty[prev_s]);
+            }
+            __syncwarp();
+            return true;
+        };
+        for (int item = blockIdx.x, i = 0; item < nitems && ok; item += gridDim.x, ++i) {
+            const int s = i & 1, j = i >> 1;
+            if (i > 0 && !issue_o(i - 1)) break;
+            if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            const int tile = item / H;
+            const int4 td = P.tiles[tile];
+            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
+            int nblk = 0;
+            while (nblk < top && set[nblk] >= 0) ++nblk;
+            const int nload = nblk > 0 ? nblk : 1;
+            tc::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
+                const uint32_t sQ = base + s * kStageBytes;
+                const uint32_t sK = sQ + kQBytes;
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk) {
+                    const uint64_t ad = tc::smem_desc_sw128(sQ + kk * 32, 16, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(sK + kk * 32, 16, 1024);
+                    tc::mma_bf16_ss(tmem, ad, bd, idesc_s, kk > 0);
+                }
+                tc::mma_commit(&bars->s_full);
+            }
+            __syncwarp();
+            prev_nblk = nload;
+            prev_s = s;
+            count = i + 1;
+        }
+        if (count > 0 && !*abort_flag) issue_o(count - 1);
+        // drain: every MMA this thread issued has completed before TMEM is freed
+        if (lane == 0) tc::mma_commit(&bars->drain);
+        __syncwarp();
+        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+    } else {
+        // ------------------------------------------------------------ softmax + epilogue
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        int prev_tok = -1, prev_h = 0;
+        float prev_inv = 0.0f, prev_lse = -INFINITY;
+        auto epilogue = [&](int i) {
+            const int b = i & 1;
+            tc::tc_fence_after();
+            uint32_t o0[32], o1[32];
+            tc::tmem_ld32(trow + kOCol + b * kHD, o0);
+            tc::tmem_ld32(trow + kOCol + b * kHD + 32, o1);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->o_free[b]);
+            if (prev_tok >= 0) {
+                uint4 *dst = reinterpret_cast<uint4 *>(out + prev_tok * ld + prev_h * kHD);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint4 v0, v1;
+                    v0.x = pack_bf16x2(__uint_as_float(o0[8 * c + 0]) * prev_inv, __uint_as_float(o0[8 * c + 1]) * prev_inv);
+                    v0.y = pack_bf16x2(__uint_as_float(o0[8 * c + 2]) * prev_inv, __uint_as_float(o0[8 * c + 3]) * prev_inv);
+                    v0.z = pack_bf16x2(__uint_as_float(o0[8 * c + 4]) * prev_inv, __uint_as_float(o0[8 * c + 5]) * prev_inv);
+                    v0.w = pack_bf16x2(__uint_as_float(o0[8 * c + 6]) * prev_inv, __uint_as_float(o0[8 * c + 7]) * prev_inv);
+                    v1.x = pack_bf16x2(__uint_as_float(o1[8 * c + 0]) * prev_inv, __uint_as_float(o1[8 * c + 1]) * prev_inv);
+                    v1.y = pack_bf16x2(__uint_as_float(o1[8 * c + 2]) * prev_inv, __uint_as_float(o1[8 * c + 3]) * prev_inv);
+                    v1.z = pack_bf16x2(__uint_as_float(o1[8 * c + 4]) * prev_inv, __uint_as_float(o1[8 * c + 5]) * prev_inv);
+                    v1.w = pack_bf16x2(__uint_as_float(o1[8 * c + 6]) * prev_inv, __uint_as_float(o1[8 * c + 7]) * prev_inv);
+                    dst[c] = v0;
+                    dst[4 + c] = v1;
+                }
+                lse[static_cast<int64_t>(prev_tok) * H + prev_h] = prev_lse;
+            }
+        };
+        int count = 0;
+        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
+            const int tile = item / H, h = item % H;
+            const int4 td = P.tiles[tile];
+            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
+            int nblk = 0;
+            while (nblk < top && set[nblk] >= 0) ++nblk;
+            const int nload = nblk > 0 ? nblk : 1;
+            const int tok = r < td.y ? P.perm[td.x + r] : -1;
+            float bias[2] = {0.0f, 0.0f};
+            if (tok >= 0)
+                for (int jb = 0; jb < nblk; ++jb) bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+            if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            // pass 1: raw row maximum of each block
+            float mx[2] = {-INFINITY, -INFINITY};
+            for (int c = 0; c < nload * 4; ++c) {
+                uint32_t v[32];
+                tc::tmem_ld32(trow + c * 32, v);
+                tc::tmem_ld_wait();
+                float m = __uint_as_float(v[0]);
+#pragma unroll
+                for (int e = 1; e < 32; ++e) m = fmaxf(m, __uint_as_float(v[e]));
+                mx[c >> 2] = fmaxf(mx[c >> 2], m);
+            }
+            float m2 = -INFINITY;
+            for (int jb = 0; jb < nblk; ++jb) m2 = fmaxf(m2, fmaf(mx[jb], scale_log2, bias[jb]));
+            const float mref = (m2 == -INFINITY) ? 0.0f : m2;
+            // P is free once O(i-1) has consumed it
+            if (i > 0 && !tc::mbar_wait(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag)) break;
+            // pass 2: p = exp2(s*scale + bias - m) -> bf16 P, row sum
+            float l = 0.0f;
+            for (int c = 0; c < nload * 4; ++c) {
+                uint32_t v[32];
+                tc::tmem_ld32(trow + c * 32, v);
+                tc::tmem_ld_wait();
+                const int jb = c >> 2;
+                const float bj = bias[jb];
+                const bool live = jb < nblk;
+                uint32_t pk[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = live ? exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj) - mref) : 0.0f;
+                    const float p1 = live ? exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj) - mref) : 0.0f;
+                    l += p0 + p1;
+                    pk[e] = pack_bf16x2(p0, p1);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int cg = c * 4 + u;            // 16-B chunk index along the row
+                    const uint32_t dst = sP + (cg >> 3) * (kTM * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(pk[4 * u]),
+                                 "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
+                                 : "memory");
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->p_full);
+            if (i > 0) epilogue(i - 1);
+            prev_tok = tok;
+            prev_h = h;
+            prev_inv = l > 0.0f ? 1.0f / l : 0.0f;
+            prev_lse = l > 0.0f ? (m2 + log2f(l)) * kLn2 : -INFINITY;
+            count = i + 1;
+        }
+        if (count > 0 && !*abort_flag) {
+            const int i = count - 1;
+            if (tc::mbar_wait(&bars->o_full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag)) epilogue(i);
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+// 2-D bf16 map over a row-major [rows, cols] matrix, box = 64 columns x box_rows, 128-B swizzle.
+static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {64, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+bool read_fwd_tc_supported(int hd, int bs, int top, const void *k, const void *v, int H) {
+    return hd == kHD && bs == kBS && top >= 1 && top <= 2 && (reinterpret_cast<uintptr_t>(k) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(v) % 16) == 0 && (H * kHD * 2) % 16 == 0 && encode_fn() != nullptr;
+}
+
+static int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
+                               const PlanLayout &L, const PlanView &P, void *out, float *lse,
+                               cudaStream_t st) {
+    CUtensorMap mk, mv;
+    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
+    if (!make_map(&mk, k, rows, cols, kBS) || !make_map(&mv, v, rows, cols, kBS)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    const int64_t items = L.max_tiles * H;
+    const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));
+    const float scale_log2 = kLog2e / sqrtf(static_cast<float>(kHD));
+    read_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(mk, mv, static_cast<const uint16_t *>(q), H, top,
+                                                          scale_log2, P, static_cast<uint16_t *>(out), lse);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mom

@@ -90,6 +90,92 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
     cp_async_wait<0>();
 }
 
+// ------------------------------------------------------------ parallel exact fp64 scan
+// Sequential fp64 accumulation (the CPU cumsum) is re-association-proof when
+// no partial sum rounds. Every element is an integer multiple of its ulp, so
+// with e_min the smallest ulp exponent of a column's non-zero elements, every
+// partial sum of any subset of them is a multiple of 2^e_min bounded by
+// A = sum |x|; if A < 2^(52 + e_min) all of them are exactly representable in
+// fp64 and ANY summation order returns the exact prefix sums — the values the
+// sequential loop produces. The kernel checks that certificate per column and
+// walks the column sequentially when it fails (tiny or huge dynamic range).
+//
+// CTA = 32 columns x 32 chunks of the sequence (1024 threads):
+//   phase 1  chunk sums, sums of |x| and min ulp exponent
+//   phase 2  per column: exclusive scan of the chunk sums, certificate
+//   phase 3  each chunk re-walks its rows from its carry and writes h.
+template <int XDT>
+__device__ __forceinline__ int ulp_exponent(float v) {
+    const uint32_t bits = __float_as_uint(v);
+    const int e = static_cast<int>((bits >> 23) & 0xFF);
+    return (e == 0 ? 1 : e) - 127 - (XDT == MOM_BF16 ? 7 : 23);
+}
+
+template <int XDT, int CDT>
+__global__ void __launch_bounds__(1024)
+route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem<CDT>::T *__restrict__ hq,
+                      int S, int d) {
+    __shared__ double s_sum[32][33];
+    __shared__ double s_abs[32][33];
+    __shared__ int s_emin[32][33];
+    __shared__ int s_cert[32];
+    const int c = threadIdx.x & 31, k = threadIdx.x >> 5;
+    const int b = blockIdx.y;
+    const int col = blockIdx.x * 32 + c;
+    const int len = (S + 31) / 32;
+    const int t0 = k * len, t1 = min(S, t0 + len);
+    const typename Elem<XDT>::T *xc = x + static_cast<int64_t>(b) * S * d + col;
+    typename Elem<CDT>::T *hc = hq + static_cast<int64_t>(b) * S * d + col;
+    const bool live = col < d;
+    double sum = 0.0, asum = 0.0;
+    int emin = 1 << 20;
+    if (live) {
+#pragma unroll 4
+        for (int t = t0; t < t1; ++t) {
+            const float v = Elem<XDT>::load(xc, static_cast<int64_t>(t) * d);
+            sum = __dadd_rn(sum, static_cast<double>(v));
+            asum = __dadd_rn(asum, static_cast<double>(fabsf(v)));
+            if (v != 0.0f) emin = min(emin, ulp_exponent<XDT>(v));
+        }
+    }
+    s_sum[c][k] = sum;
+    s_abs[c][k] = asum;
+    s_emin[c][k] = emin;
+    __syncthreads();
+    if (k == 0) {
+        double run = 0.0, at = 0.0;
+        int em = 1 << 20;
+        for (int kk = 0; kk < 32; ++kk) {
+            const double v = s_sum[c][kk];
+            s_sum[c][kk] = run;
+            run = __dadd_rn(run, v);
+            at = __dadd_rn(at, s_abs[c][kk]);
+            em = min(em, s_emin[c][kk]);
+        }
+        // all zero -> trivially exact; else A < 2^(52 + e_min)
+        s_cert[c] = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
+    }
+    __syncthreads();
+    if (!live) return;
+    if (s_cert[c]) {
+        double run = s_sum[c][k];
+#pragma unroll 4
+        for (int t = t0; t < t1; ++t) {
+            const float v = Elem<XDT>::load(xc, static_cast<int64_t>(t) * d);
+            run = __dadd_rn(run, static_cast<double>(v));
+            const float h = __fdiv_rn(__double2float_rn(run), static_cast<float>(t + 1));
+            Elem<CDT>::store(hc, static_cast<int64_t>(t) * d, h);
+        }
+    } else if (k == 0) {
+        double acc = 0.0;
+        for (int t = 0; t < S; ++t) {
+            acc = __dadd_rn(acc, static_cast<double>(Elem<XDT>::load(xc, static_cast<int64_t>(t) * d)));
+            const float h = __fdiv_rn(__double2float_rn(acc), static_cast<float>(t + 1));
+            Elem<CDT>::store(hc, static_cast<int64_t>(t) * d, h);
+        }
+    }
+}
+
 // ============================================================ router head
 // Per token: z = round(hq . Wd^T), act = round(tanh z), logits = round(act . Wu^T),
 // then softmax, top-k (value desc, lower index on ties) and the gate softmax.
@@ -299,185 +385,6 @@ route_head_simt_kernel(const typename Elem<CDT>::T *__restrict__ hq,
                        gates, log_gates);
 }
 
-// ============================================================ router backward
-// Per token (one warp): gate-softmax and probs-softmax adjoints -> dlogits,
-// then da = dlogits . Wu and dz = da * (1 - act^2).
-template <int CDT>
-__global__ void route_bwd_token_kernel(int64_t ntok, int r, int nb, int top,
-                                       const float *__restrict__ probs, const void *__restrict__ top_idx,
-                                       int idx64, const float *__restrict__ gates,
-                                       const typename Elem<CDT>::T *__restrict__ act,
-                                       const typename Elem<CDT>::T *__restrict__ w_up,
-                                       const float *__restrict__ dlog_gates,
-                                       const float *__restrict__ dgates,
-                                       const float *__restrict__ dprobs, float *__restrict__ dlogits,
-                                       float *__restrict__ dz) {
-    const int lane = threadIdx.x & 31;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= ntok) return;
-    // gate softmax backward (lanes < top)
-    float g = 0.0f, dg = 0.0f;
-    int idx = -1;
-    if (lane < top) {
-        g = gates[t * top + lane];
-        if (dlog_gates) dg += (g >= 1e-9f) ? dlog_gates[t * top + lane] / fmaxf(g, 1e-9f) : 0.0f;
-        if (dgates) dg += dgates[t * top + lane];
-        idx = idx64 ? static_cast<int>(reinterpret_cast<const int64_t *>(top_idx)[t * top + lane])
-                    : reinterpret_cast<const int32_t *>(top_idx)[t * top + lane];
-    }
-    const float sgdg = warp_sum(g * dg);
-    const float dtv = g * (dg - sgdg);
-    // probs softmax backward
-    float sp = 0.0f;
-    if (dprobs) {
-        float part = 0.0f;
-        for (int e = lane; e < nb; e += 32) part += probs[t * nb + e] * dprobs[t * nb + e];
-        sp = warp_sum(part);
-    }
-    // Every shuffle below runs on all 32 lanes: the loops have warp-uniform
-    // trip counts and only the loads/stores are predicated.
-    float dl0 = 0.0f, dl1 = 0.0f;   // dlogits for e = lane and e = lane + 32
-#pragma unroll
-    for (int half = 0; half < kMaxNb / 32; ++half) {
-        const int e = half * 32 + lane;
-        float v = 0.0f;
-        for (int k = 0; k < top; ++k) {
-            const int ik = __shfl_sync(0xffffffffu, idx, k);
-            const float dk = __shfl_sync(0xffffffffu, dtv, k);
-            if (ik == e) v += dk;
-        }
-        if (e < nb) {
-            if (dprobs) {
-                const float p = probs[t * nb + e];
-                v += p * (dprobs[t * nb + e] - sp);
-            }
-            dlogits[t * nb + e] = v;
-        } else {
-            v = 0.0f;
-        }
-        if (half == 0) dl0 = v; else dl1 = v;
-    }
-    // da_j = sum_e dlogits_e * Wu[e, j]
-    for (int j0 = 0; j0 < r; j0 += 32) {
-        const int j = j0 + lane;
-        float da = 0.0f;
-        for (int e = 0; e < nb; ++e) {
-            const float dle = __shfl_sync(0xffffffffu, e < 32 ? dl0 : dl1, e & 31);
-            if (j < r) da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
-        }
-        if (j < r) {
-            const float a = Elem<CDT>::load(act, t * r + j);
-            dz[t * r + j] = da * (1.0f - a * a);
-        }
-    }
-}
-
-// u[b, t, j] = sum_{s >= t} dz[b, s, j] / (s + 1), one thread per (b, j).
-__global__ void route_bwd_revscan_kernel(const float *__restrict__ dz, float *__restrict__ u, int B,
-                                         int S, int r) {
-    const int col = blockIdx.x * blockDim.x + threadIdx.x;
-    if (col >= B * r) return;
-    const int b = col / r, j = col % r;
-    const float *src = dz + static_cast<int64_t>(b) * S * r + j;
-    float *dst = u + static_cast<int64_t>(b) * S * r + j;
-    float acc = 0.0f;
-    int t = S - 1;
-    for (; t >= 7; t -= 8) {
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = src[static_cast<int64_t>(t - i) * r] / static_cast<float>(t - i + 1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            acc += v[i];
-            dst[static_cast<int64_t>(t - i) * r] = acc;
-        }
-    }
-    for (; t >= 0; --t) {
-        acc += src[static_cast<int64_t>(t) * r] / static_cast<float>(t + 1);
-        dst[static_cast<int64_t>(t) * r] = acc;
-    }
-}
-
-// dx[t, c] (+)= sum_j u[t, j] * Wd[j, c]
-constexpr int kDxTokens = 16;
-template <int CDT, int DXDT>
-__global__ void __launch_bounds__(256)
-route_bwd_dx_kernel(const float *__restrict__ u, const typename Elem<CDT>::T *__restrict__ w_down,
-                    int64_t ntok, int d, int r, typename Elem<DXDT>::T *__restrict__ dx, int accumulate) {
-    __shared__ float sU[kDxTokens * kMaxRank];
-    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kDxTokens;
-    for (int i = threadIdx.x; i < kDxTokens * r; i += blockDim.x) {
-        const int64_t t = tok0 + i / r;
-        sU[i] = t < ntok ? u[t * r + (i % r)] : 0.0f;
-    }
-    __syncthreads();
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        float w[kMaxRank];
-        for (int j = 0; j < r; ++j) w[j] = Elem<CDT>::load(w_down, static_cast<int64_t>(j) * d + c);
-        for (int tl = 0; tl < kDxTokens; ++tl) {
-            const int64_t t = tok0 + tl;
-            if (t >= ntok) break;
-            float acc = 0.0f;
-            for (int j = 0; j < r; ++j) acc = fmaf(sU[tl * r + j], w[j], acc);
-            if (accumulate) acc += Elem<DXDT>::load(dx, t * d + c);
-            Elem<DXDT>::store(dx, t * d + c, acc);
-        }
-    }
-}
-
-// dWd[j, c] += sum_{t in chunk} u[t, j] * x[t, c]; fp32 atomics across chunks.
-constexpr int kDwTok = 256;
-constexpr int kDwCols = 64;
-template <int XDT>
-__global__ void __launch_bounds__(256)
-route_bwd_dwdown_kernel(const float *__restrict__ u, const typename Elem<XDT>::T *__restrict__ x,
-                        int64_t ntok, int d, int r, float *__restrict__ dw_down) {
-    __shared__ float sU[32 * kMaxRank];
-    __shared__ float sX[32 * kDwCols];
-    const int c0 = blockIdx.x * kDwCols;
-    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kDwTok;
-    const int tid = threadIdx.x;
-    const int cl = tid % kDwCols;     // column within the slab
-    const int jg = tid / kDwCols;     // rank group: j = jg, jg+4, ...
-    float acc[kMaxRank / 4];
-    for (int i = 0; i < kMaxRank / 4; ++i) acc[i] = 0.0f;
-    for (int tb = 0; tb < kDwTok; tb += 32) {
-        __syncthreads();
-        for (int i = tid; i < 32 * r; i += 256) {
-            const int64_t t = t0 + tb + i / r;
-            sU[i] = t < ntok ? u[t * r + i % r] : 0.0f;
-        }
-        for (int i = tid; i < 32 * kDwCols; i += 256) {
-            const int64_t t = t0 + tb + i / kDwCols;
-            const int c = c0 + i % kDwCols;
-            sX[i] = (t < ntok && c < d) ? Elem<XDT>::load(x, t * d + c) : 0.0f;
-        }
-        __syncthreads();
-        for (int tt = 0; tt < 32; ++tt) {
-            const float xv = sX[tt * kDwCols + cl];
-            for (int j = jg, i = 0; j < r; j += 4, ++i) acc[i] = fmaf(sU[tt * r + j], xv, acc[i]);
-        }
-    }
-    const int c = c0 + cl;
-    if (c < d)
-        for (int j = jg, i = 0; j < r; j += 4, ++i) atomicAdd(dw_down + static_cast<int64_t>(j) * d + c, acc[i]);
-}
-
-// dWu[e, j] += sum_t dlogits[t, e] * act[t, j]
-template <int CDT>
-__global__ void __launch_bounds__(256)
-route_bwd_dwup_kernel(const float *__restrict__ dlogits, const typename Elem<CDT>::T *__restrict__ act,
-                      int64_t ntok, int r, int nb, float *__restrict__ dw_up) {
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 1024;
-    for (int o = threadIdx.x; o < nb * r; o += blockDim.x) {
-        const int e = o / r, j = o % r;
-        float acc = 0.0f;
-        const int64_t tend = min(ntok, t0 + 1024);
-        for (int64_t t = t0; t < tend; ++t) acc = fmaf(dlogits[t * nb + e], Elem<CDT>::load(act, t * r + j), acc);
-        atomicAdd(dw_up + o, acc);
-    }
-}
-
 // ============================================================ host launchers
 template <int XDT, int CDT, int MODE>
 static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
@@ -492,17 +399,29 @@ static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, c
     return cudaGetLastError();
 }
 
+template <int XDT, int CDT>
+static cudaError_t launch_scan_par_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
+    dim3 grid((d + 31) / 32, B);
+    route_scan_par_kernel<XDT, CDT><<<grid, 1024, 0, st>>>(static_cast<const typename Elem<XDT>::T *>(x),
+                                                          static_cast<typename Elem<CDT>::T *>(hq), S, d);
+    count_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, int S, int d,
                               int mode, cudaStream_t st) {
+    if (mode == MOM_SCAN_FP64) {
+        if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_par_t<MOM_BF16, MOM_BF16>(x, hq, B, S, d, st);
+        if (xdt == MOM_BF16 && cdt == MOM_F32) return launch_scan_par_t<MOM_BF16, MOM_F32>(x, hq, B, S, d, st);
+        if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_par_t<MOM_F32, MOM_BF16>(x, hq, B, S, d, st);
+        if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_par_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st);
+        return cudaErrorInvalidValue;
+    }
 #define MOM_SCAN_CASE(X, C, M)                                                       \
     if (xdt == X && cdt == C && mode == M) return launch_scan_t<X, C, M>(x, hq, B, S, d, st);
-    MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP64)
     MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP64)
     MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP64)
     MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP64)
     MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP32)
 #undef MOM_SCAN_CASE
     return cudaErrorInvalidValue;
@@ -554,74 +473,6 @@ cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_
             gates, log_gates, static_cast<float *>(act)); count_launch();
     }
     return cudaGetLastError();
-}
-
-cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const void *w_down,
-                             const void *w_up, int cdt, int r, int nb, int top, const float *probs,
-                             const void *top_idx, int idx64, const float *gates, const void *act,
-                             const float *dlog_gates, const float *dgates, const float *dprobs,
-                             void *dx, int dxdt, int accumulate, float *dw_down, float *dw_up,
-                             float *ws_dlogits, float *ws_dz, float *ws_u, cudaStream_t st) {
-    const int64_t ntok = static_cast<int64_t>(B) * S;
-    cudaError_t e;
-    e = cudaMemsetAsync(dw_down, 0, sizeof(float) * r * d, st);
-    if (e != cudaSuccess) return e;
-    e = cudaMemsetAsync(dw_up, 0, sizeof(float) * nb * r, st);
-    if (e != cudaSuccess) return e;
-    {
-        const int warps = 8;
-        const int grid = static_cast<int>((ntok + warps - 1) / warps);
-        if (cdt == MOM_BF16)
-            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, 0, st>>>(
-                ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const uint16_t *>(act),
-                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
-        else
-            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, 0, st>>>(
-                ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const float *>(act),
-                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    route_bwd_revscan_kernel<<<(B * r + 127) / 128, 128, 0, st>>>(ws_dz, ws_u, B, S, r); count_launch();
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    {
-        const int grid = static_cast<int>((ntok + kDxTokens - 1) / kDxTokens);
-#define MOM_DX_CASE(C, X)                                                                         \
-    if (cdt == C && dxdt == X)                                                                    \
-        route_bwd_dx_kernel<C, X><<<grid, 256, 0, st>>>(                                           \
-            ws_u, static_cast<const typename Elem<C>::T *>(w_down), ntok, d, r,                  \
-            static_cast<typename Elem<X>::T *>(dx), accumulate);
-        MOM_DX_CASE(MOM_BF16, MOM_BF16)
-        MOM_DX_CASE(MOM_BF16, MOM_F32)
-        MOM_DX_CASE(MOM_F32, MOM_BF16)
-        MOM_DX_CASE(MOM_F32, MOM_F32)
-#undef MOM_DX_CASE
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    {
-        dim3 grid((d + kDwCols - 1) / kDwCols, static_cast<unsigned>((ntok + kDwTok - 1) / kDwTok));
-        if (xdt == MOM_BF16)
-            route_bwd_dwdown_kernel<MOM_BF16><<<grid, 256, 0, st>>>(
-                ws_u, static_cast<const uint16_t *>(x), ntok, d, r, dw_down);
-        else
-            route_bwd_dwdown_kernel<MOM_F32><<<grid, 256, 0, st>>>(
-                ws_u, static_cast<const float *>(x), ntok, d, r, dw_down);
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    {
-        const int grid = static_cast<int>((ntok + 1023) / 1024);
-        if (cdt == MOM_BF16)
-            route_bwd_dwup_kernel<MOM_BF16><<<grid, 256, 0, st>>>(
-                ws_dlogits, static_cast<const uint16_t *>(act), ntok, r, nb, dw_up);
-        else
-            route_bwd_dwup_kernel<MOM_F32><<<grid, 256, 0, st>>>(
-                ws_dlogits, static_cast<const float *>(act), ntok, r, nb, dw_up);
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    return cudaSuccess;
 }
 
 }  // namespace mom

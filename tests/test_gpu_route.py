@@ -53,6 +53,22 @@ def test_prefix_mean_fp32_mode_bitwise_vs_torch_cuda(dtype):
     assert torch.equal(h, ref.cpu())
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_prefix_mean_fp64_mode_dynamic_range_fallback(dtype):
+    """Columns whose dynamic range defeats the exactness certificate of the
+    parallel scan (a 1e-30 next to O(1) values, or 1e30 values) must still be
+    bit-identical to the sequential fp64 cumsum (they take the sequential walk)."""
+    torch.manual_seed(2)
+    x = torch.randn(2, 3000, 96)
+    x[0, 17, 5] = 1e-30
+    x[1, 2999, 40] = -3e-38
+    x[1, :, 77] *= 1e30
+    x = x.to(dtype)
+    h = _prefix_mean_gpu(x, "fp64")
+    ref = O.prefix_mean(x.float().numpy(), "fp64")
+    assert np.array_equal(h.numpy(), ref)
+
+
 def test_prefix_mean_causality_and_bf16_output():
     torch.manual_seed(1)
     x = torch.randn(3, 700, 64)
