@@ -11,7 +11,7 @@ namespace mom {
 void count_launch(int n = 1);
 uint64_t launches();
 
-constexpr int kTileM = 64;        // tokens per read tile (one routing set per tile)
+constexpr int kTileM = 128;       // tokens per read tile (one routing set per tile)
 constexpr int kMaxKeys = 8192;    // routing sets the bucketing supports
 constexpr int kBucketChunk = 1024;
 

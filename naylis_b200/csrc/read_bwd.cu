@@ -270,7 +270,7 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kReadThreads)
+__global__ void __launch_bounds__(kDkvThreads)
 read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
                      const uint16_t *__restrict__ v, const uint16_t *__restrict__ dout,
                      const float *__restrict__ lse, const float *__restrict__ ws_delta, int H, int bs,
@@ -279,7 +279,7 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
     constexpr int kRowB = HD * 2;
     constexpr int kChunks = HD / 8;
     constexpr int kTileBytes = kTileM * kRowB;
-    constexpr int NTT = kTileM / 8;        // token n-tiles
+    constexpr int NTT = kDkvSub / 8;       // token n-tiles per compute sub-tile
     constexpr int NTO = HD / 8;
     extern __shared__ __align__(128) unsigned char smem[];
     unsigned char *sK = smem;
@@ -302,7 +302,7 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
     const int ntile = count > split ? (count - split + nsplit - 1) / nsplit : 0;
     if (ntile == 0) return;
 
-    for (int i = tid; i < kSlotChunk * kChunks; i += kReadThreads) {
+    for (int i = tid; i < kSlotChunk * kChunks; i += kDkvThreads) {
         const int r = i / kChunks, ch = i % kChunks;
         const bool ok = r < valid;
         const int64_t off = ok ? (slot0 + r) * ld + h * HD + ch * 8 : 0;
@@ -320,7 +320,7 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
             const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
             int jb = 0;
             while (jb < top - 1 && set[jb] != blk) ++jb;   // the list only holds tiles whose set has blk
-            for (int r = tid; r < kTileM; r += kReadThreads) {
+            for (int r = tid; r < kTileM; r += kDkvThreads) {
                 const int tok = r < td.y ? P.perm[td.x + r] : -1;
                 sTok[buf * kTileM + r] = tok;
                 sBias[buf * kTileM + r] = tok >= 0 ? P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e : 0.0f;
@@ -330,7 +330,7 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
             __syncthreads();
             const uint32_t sq = smem_u32(sT + buf * 2 * kTileBytes);
             const uint32_t sd = sq + kTileBytes;
-            for (int e = tid; e < kTileM * kChunks; e += kReadThreads) {
+            for (int e = tid; e < kTileM * kChunks; e += kDkvThreads) {
                 const int r = e / kChunks, ch = e % kChunks;
                 const int tok = sTok[buf * kTileM + r];
                 const int64_t off = tok >= 0 ? tok * ld + h * HD + ch * 8 : 0;
@@ -359,60 +359,62 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
         const float *bias = sBias + buf * kTileM;
         const float *lsev = sLse + buf * kTileM;
         const float *delt = sDelta + buf * kTileM;
-        float s[NTT][4], dp[NTT][4];
-#pragma unroll
-        for (int n = 0; n < NTT; ++n)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < HD / 16; ++ks) {
-            uint32_t kf[4], vf[4];
-            const uint32_t aoff = swz(warp * 16 + (lane & 15), ks * 2 + (lane >> 4), kRowB);
-            ldmatrix_x4(kf, smem_u32(sK) + aoff);
-            ldmatrix_x4(vf, smem_u32(sV) + aoff);
-#pragma unroll
-            for (int n = 0; n < NTT; n += 2) {
-                const uint32_t off = swz(n * 8 + (lane & 7) + ((lane >> 4) << 3),
-                                         ks * 2 + ((lane >> 3) & 1), kRowB);
-                uint32_t b[4];
-                ldmatrix_x4(b, sq + off);
-                mma_bf16_16816(s[n], kf, b[0], b[1]);
-                mma_bf16_16816(s[n + 1], kf, b[2], b[3]);
-                ldmatrix_x4(b, sd + off);
-                mma_bf16_16816(dp[n], vf, b[0], b[1]);
-                mma_bf16_16816(dp[n + 1], vf, b[2], b[3]);
+        for (int r0 = 0; r0 < kTileM; r0 += kDkvSub) {
+            float s[NTT][4], dp[NTT][4];
+    #pragma unroll
+            for (int n = 0; n < NTT; ++n)
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) s[n][e] = dp[n][e] = 0.0f;
+    #pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                uint32_t kf[4], vf[4];
+                const uint32_t aoff = swz(warp * 16 + (lane & 15), ks * 2 + (lane >> 4), kRowB);
+                ldmatrix_x4(kf, smem_u32(sK) + aoff);
+                ldmatrix_x4(vf, smem_u32(sV) + aoff);
+    #pragma unroll
+                for (int n = 0; n < NTT; n += 2) {
+                    const uint32_t off = swz(r0 + n * 8 + (lane & 7) + ((lane >> 4) << 3),
+                                             ks * 2 + ((lane >> 3) & 1), kRowB);
+                    uint32_t b[4];
+                    ldmatrix_x4(b, sq + off);
+                    mma_bf16_16816(s[n], kf, b[0], b[1]);
+                    mma_bf16_16816(s[n + 1], kf, b[2], b[3]);
+                    ldmatrix_x4(b, sd + off);
+                    mma_bf16_16816(dp[n], vf, b[0], b[1]);
+                    mma_bf16_16816(dp[n + 1], vf, b[2], b[3]);
+                }
             }
-        }
-        uint32_t pf[NTT / 2][4], dsf[NTT / 2][4];
-#pragma unroll
-        for (int n = 0; n < NTT; ++n) {
-            float p[4], ds[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int col = n * 8 + q2 + (e & 1);
-                p[e] = exp2f(fmaf(s[n][e], scale_log2, bias[col]) - lsev[col]);
-                ds[e] = p[e] * (dp[n][e] - delt[col]);
+            uint32_t pf[NTT / 2][4], dsf[NTT / 2][4];
+    #pragma unroll
+            for (int n = 0; n < NTT; ++n) {
+                float p[4], ds[4];
+    #pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int col = r0 + n * 8 + q2 + (e & 1);
+                    p[e] = exp2f(fmaf(s[n][e], scale_log2, bias[col]) - lsev[col]);
+                    ds[e] = p[e] * (dp[n][e] - delt[col]);
+                }
+                pf[n >> 1][(n & 1) * 2 + 0] = pack_bf16x2(p[0], p[1]);
+                pf[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(p[2], p[3]);
+                dsf[n >> 1][(n & 1) * 2 + 0] = pack_bf16x2(ds[0], ds[1]);
+                dsf[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
             }
-            pf[n >> 1][(n & 1) * 2 + 0] = pack_bf16x2(p[0], p[1]);
-            pf[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(p[2], p[3]);
-            dsf[n >> 1][(n & 1) * 2 + 0] = pack_bf16x2(ds[0], ds[1]);
-            dsf[n >> 1][(n & 1) * 2 + 1] = pack_bf16x2(ds[2], ds[3]);
-        }
-#pragma unroll
-        for (int kk = 0; kk < NTT / 2; ++kk) {
-            const uint32_t ap[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
-            const uint32_t as[4] = {dsf[kk][0], dsf[kk][1], dsf[kk][2], dsf[kk][3]};
-#pragma unroll
-            for (int jn = 0; jn < NTO; jn += 2) {
-                const uint32_t off = swz(kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8,
-                                         jn + (lane >> 4), kRowB);
-                uint32_t b[4];
-                ldmatrix_x4_trans(b, sd + off);
-                mma_bf16_16816(dva[jn], ap, b[0], b[1]);
-                mma_bf16_16816(dva[jn + 1], ap, b[2], b[3]);
-                ldmatrix_x4_trans(b, sq + off);
-                mma_bf16_16816(dka[jn], as, b[0], b[1]);
-                mma_bf16_16816(dka[jn + 1], as, b[2], b[3]);
+    #pragma unroll
+            for (int kk = 0; kk < NTT / 2; ++kk) {
+                const uint32_t ap[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+                const uint32_t as[4] = {dsf[kk][0], dsf[kk][1], dsf[kk][2], dsf[kk][3]};
+    #pragma unroll
+                for (int jn = 0; jn < NTO; jn += 2) {
+                    const uint32_t off = swz(r0 + kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8,
+                                             jn + (lane >> 4), kRowB);
+                    uint32_t b[4];
+                    ldmatrix_x4_trans(b, sd + off);
+                    mma_bf16_16816(dva[jn], ap, b[0], b[1]);
+                    mma_bf16_16816(dva[jn + 1], ap, b[2], b[3]);
+                    ldmatrix_x4_trans(b, sq + off);
+                    mma_bf16_16816(dka[jn], as, b[0], b[1]);
+                    mma_bf16_16816(dka[jn + 1], as, b[2], b[3]);
+                }
             }
         }
         __syncthreads();
@@ -463,7 +465,7 @@ static cudaError_t launch_bwd_t(const void *q, const void *k, const void *v, con
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         dim3 grid(nb * cpb, H, nsplit);
-        kern<<<grid, kReadThreads, smem, st>>>(
+        kern<<<grid, kDkvThreads, smem, st>>>(
             static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
             static_cast<const uint16_t *>(v), static_cast<const uint16_t *>(dout), lse, ws_delta, H,
             bs, top, cpb, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2, P, dk_acc, dv_acc); count_launch();

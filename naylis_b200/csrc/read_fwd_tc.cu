@@ -235,16 +235,25 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 for (int jb = 0; jb < nblk; ++jb) bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
             if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
-            // pass 1: raw row maximum of each block
+            // pass 1: raw row maximum of each block (four 32-column loads in flight)
             float mx[2] = {-INFINITY, -INFINITY};
-            for (int c = 0; c < nload * 4; ++c) {
-                uint32_t v[32];
-                tc::tmem_ld32(trow + c * 32, v);
+            for (int jb = 0; jb < nload; ++jb) {
+                uint32_t v0[32], v1[32], v2[32], v3[32];
+                tc::tmem_ld32(trow + jb * 128, v0);
+                tc::tmem_ld32(trow + jb * 128 + 32, v1);
+                tc::tmem_ld32(trow + jb * 128 + 64, v2);
+                tc::tmem_ld32(trow + jb * 128 + 96, v3);
                 tc::tmem_ld_wait();
-                float m = __uint_as_float(v[0]);
+                float m0 = __uint_as_float(v0[0]), m1 = __uint_as_float(v1[0]);
+                float m2_ = __uint_as_float(v2[0]), m3 = __uint_as_float(v3[0]);
 #pragma unroll
-                for (int e = 1; e < 32; ++e) m = fmaxf(m, __uint_as_float(v[e]));
-                mx[c >> 2] = fmaxf(mx[c >> 2], m);
+                for (int e = 1; e < 32; ++e) {
+                    m0 = fmaxf(m0, __uint_as_float(v0[e]));
+                    m1 = fmaxf(m1, __uint_as_float(v1[e]));
+                    m2_ = fmaxf(m2_, __uint_as_float(v2[e]));
+                    m3 = fmaxf(m3, __uint_as_float(v3[e]));
+                }
+                mx[jb] = fmaxf(fmaxf(m0, m1), fmaxf(m2_, m3));
             }
             float m2 = -INFINITY;
             for (int jb = 0; jb < nblk; ++jb) m2 = fmaxf(m2, fmaf(mx[jb], scale_log2, bias[jb]));
@@ -253,28 +262,34 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (i > 0 && !tc::mbar_wait(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag)) break;
             // pass 2: p = exp2(s*scale + bias - m) -> bf16 P, row sum
             float l = 0.0f;
-            for (int c = 0; c < nload * 4; ++c) {
-                uint32_t v[32];
-                tc::tmem_ld32(trow + c * 32, v);
+            for (int c2 = 0; c2 < nload * 2; ++c2) {      // 64 columns per step, two loads in flight
+                uint32_t va[32], vb[32];
+                tc::tmem_ld32(trow + c2 * 64, va);
+                tc::tmem_ld32(trow + c2 * 64 + 32, vb);
                 tc::tmem_ld_wait();
-                const int jb = c >> 2;
-                const float bj = bias[jb];
+                const int jb = c2 >> 1;
+                const float bj = bias[jb] - mref;
                 const bool live = jb < nblk;
-                uint32_t pk[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float p0 = live ? exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj) - mref) : 0.0f;
-                    const float p1 = live ? exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj) - mref) : 0.0f;
-                    l += p0 + p1;
-                    pk[e] = pack_bf16x2(p0, p1);
-                }
+                for (int half = 0; half < 2; ++half) {
+                    const uint32_t *v = half ? vb : va;
+                    uint32_t pk[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int cg = c * 4 + u;            // 16-B chunk index along the row
-                    const uint32_t dst = sP + (cg >> 3) * (kTM * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(pk[4 * u]),
-                                 "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
-                                 : "memory");
+                    for (int e = 0; e < 16; ++e) {
+                        const float p0 = live ? exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj)) : 0.0f;
+                        const float p1 = live ? exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj)) : 0.0f;
+                        l += p0 + p1;
+                        pk[e] = pack_bf16x2(p0, p1);
+                    }
+                    const int c = c2 * 2 + half;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int cg = c * 4 + u;            // 16-B chunk index along the row
+                        const uint32_t dst = sP + (cg >> 3) * (kTM * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(pk[4 * u]),
+                                     "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
+                                     : "memory");
+                    }
                 }
             }
             tc::fence_proxy_async_smem();
