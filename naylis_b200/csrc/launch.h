@@ -63,7 +63,7 @@ cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
                             int hd, int nb, int bs, int top, const PlanLayout &L,
                             const PlanView &P, void *out, float *lse, cudaStream_t st);
-bool read_fwd_tc_supported(int hd, int bs, int top, const void *k, const void *v, int H);
+bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H);
 cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st);

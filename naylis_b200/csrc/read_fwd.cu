@@ -237,7 +237,7 @@ cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, 
     if (L.max_tiles == 0) return cudaSuccess;
     // the tensor-core kernel covers head_dim 64, 128-slot blocks, top <= 2;
     // other geometries take the warp-level mma kernel below
-    if (read_fwd_tc_supported(hd, bs, top, k, v, H))
+    if (read_fwd_tc_supported(hd, bs, top, q, k, v, H))
         return launch_read_fwd_tc(q, k, v, H, nb, top, L, P, out, lse, st);
     if (hd == 64) return launch_fwd_t<64>(q, k, v, H, bs, top, L, P, out, lse, st);
     if (hd == 128) return launch_fwd_t<128>(q, k, v, H, bs, top, L, P, out, lse, st);

@@ -47,7 +47,7 @@ struct Bars {
 
 __global__ void __launch_bounds__(kThreads, 1)
 read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                   const uint16_t *__restrict__ q, int H, int top, float scale_log2, PlanView P,
+                   const __grid_constant__ CUtensorMap tmap_q, int H, int top, float scale_log2, PlanView P,
                    uint16_t *__restrict__ out, float *__restrict__ lse) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -64,7 +64,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(&bars->full[s], 33);
+            tc::mbar_init(&bars->full[s], 1);
             tc::mbar_init(&bars->empty[s], 1);
             tc::mbar_init(&bars->o_full[s], 1);
             tc::mbar_init(&bars->o_free[s], 128);
@@ -81,6 +81,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     if (warp == 0 && lane == 0) {
         tc::prefetch_tensormap(&tmap_k);
         tc::prefetch_tensormap(&tmap_v);
+        tc::prefetch_tensormap(&tmap_q);
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -102,26 +103,24 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const uint32_t sQ = base + s * kStageBytes;
             const uint32_t sK = sQ + kQBytes;
             const uint32_t sV = sK + 2 * kBlkBytes;
+            // each lane gathers 4 Q rows (tokens of rows 4*lane .. 4*lane+3); padding
+            // rows read token 0 and are never stored
+            int rows[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int rr = lane * 4 + u;
+                rows[u] = rr < td.y ? P.perm[td.x + rr] : 0;
+            }
             if (lane == 0) {
-                tc::mbar_arrive_expect_tx(&bars->full[s], 2 * nload * kBlkBytes);
+                tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + 2 * nload * kBlkBytes);
                 for (int jb = 0; jb < nload; ++jb) {
                     const int blk = nblk > 0 ? set[jb] : 0;
                     tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
                     tc::tma_load_2d(sV + jb * kBlkBytes, &tmap_v, h * kHD, blk * kBS, &bars->full[s]);
                 }
             }
-            for (int rr = 0; rr < kTM / 32; ++rr) {
-                const int r = rr * 32 + lane;
-                const int tok = r < td.y ? P.perm[td.x + r] : -1;
-                const uint16_t *src = tok >= 0 ? q + tok * ld + h * kHD : q;
-#pragma unroll
-                for (int c = 0; c < 8; ++c)
-                    cp_async16(sQ + r * 128 + ((c ^ (r & 7)) << 4), src + (tok >= 0 ? c * 8 : 0),
-                               tok >= 0 ? 16 : 0);
-            }
-            tc::cp_async_wait_all();
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive(&bars->full[s]);
+            __syncwarp();
+            tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             issued = i + 1;
         }
         // make sure no TMA write is still in flight when the CTA retires
@@ -221,18 +220,29 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 lse[static_cast<int64_t>(prev_tok) * H + prev_h] = prev_lse;
             }
         };
-        int count = 0;
-        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
-            const int tile = item / H, h = item % H;
+        // per-item row metadata, fetched one item ahead so that its global-load
+        // latency hides behind the current item's softmax
+        struct Meta { int h, nblk, tok; float bias[2]; };
+        auto fetch = [&](int item, Meta &m) {
+            const int tile = item / H;
+            m.h = item % H;
             const int4 td = P.tiles[tile];
             const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
-            int nblk = 0;
-            while (nblk < top && set[nblk] >= 0) ++nblk;
+            m.nblk = 0;
+            while (m.nblk < top && set[m.nblk] >= 0) ++m.nblk;
+            m.tok = r < td.y ? P.perm[td.x + r] : -1;
+            m.bias[0] = m.bias[1] = 0.0f;
+            if (m.tok >= 0)
+                for (int jb = 0; jb < m.nblk; ++jb) m.bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+        };
+        Meta cur, nxt;
+        if (static_cast<int>(blockIdx.x) < nitems) fetch(blockIdx.x, cur);
+        int count = 0;
+        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
+            const int h = cur.h, nblk = cur.nblk, tok = cur.tok;
             const int nload = nblk > 0 ? nblk : 1;
-            const int tok = r < td.y ? P.perm[td.x + r] : -1;
-            float bias[2] = {0.0f, 0.0f};
-            if (tok >= 0)
-                for (int jb = 0; jb < nblk; ++jb) bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+            const float bias[2] = {cur.bias[0], cur.bias[1]};
+            if (item + static_cast<int>(gridDim.x) < nitems) fetch(item + gridDim.x, nxt);
             if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             // pass 1: raw row maximum of each block (four 32-column loads in flight)
@@ -298,6 +308,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (i > 0) epilogue(i - 1);
             prev_tok = tok;
             prev_h = h;
+            cur = nxt;
             prev_inv = l > 0.0f ? 1.0f / l : 0.0f;
             prev_lse = l > 0.0f ? (m2 + log2f(l)) * kLn2 : -INFINITY;
             count = i + 1;
@@ -340,9 +351,10 @@ static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t 
     return r == CUDA_SUCCESS;
 }
 
-bool read_fwd_tc_supported(int hd, int bs, int top, const void *k, const void *v, int H) {
+bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H) {
     return hd == kHD && bs == kBS && top >= 1 && top <= 2 && (reinterpret_cast<uintptr_t>(k) % 16) == 0 &&
-           (reinterpret_cast<uintptr_t>(v) % 16) == 0 && (H * kHD * 2) % 16 == 0 && encode_fn() != nullptr;
+           (reinterpret_cast<uintptr_t>(v) % 16) == 0 && (reinterpret_cast<uintptr_t>(q) % 16) == 0 &&
+           (H * kHD * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
 static int sm_count() {
@@ -359,16 +371,18 @@ static int sm_count() {
 cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st) {
-    CUtensorMap mk, mv;
+    CUtensorMap mk, mv, mq;
     const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
-    if (!make_map(&mk, k, rows, cols, kBS) || !make_map(&mv, v, rows, cols, kBS)) return cudaErrorInvalidValue;
+    if (!make_map(&mk, k, rows, cols, kBS) || !make_map(&mv, v, rows, cols, kBS) ||
+        !make_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1))
+        return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
     const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));
     const float scale_log2 = kLog2e / sqrtf(static_cast<float>(kHD));
-    read_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(mk, mv, static_cast<const uint16_t *>(q), H, top,
+    read_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(mk, mv, mq, H, top,
                                                           scale_log2, P, static_cast<uint16_t *>(out), lse);
     count_launch();
     return cudaGetLastError();
