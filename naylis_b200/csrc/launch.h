@@ -67,6 +67,12 @@ bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k
 cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st);
+bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,
+                           const void *dout, int H);
+cudaError_t launch_read_bwd_tc(const void *q, const void *k, const void *v, const void *dout, const float *lse,
+                               int H, int nb, int top, const PlanLayout &L, const PlanView &P, void *dq,
+                               float *dk_acc, float *dv_acc, float *dlog_gates, float *ws_delta,
+                               cudaStream_t st);
 cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const void *out,
                             const void *dout, const float *lse, int B, int S, int H, int hd,
                             int nb, int bs, int top, const PlanLayout &L, const PlanView &P,

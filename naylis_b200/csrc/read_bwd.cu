@@ -486,6 +486,11 @@ cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const v
     const int64_t N = static_cast<int64_t>(B) * S;
     if ((e = cudaMemsetAsync(dlog_gates, 0, sizeof(float) * N * top, st)) != cudaSuccess) return e;
     if (L.max_tiles == 0) return cudaSuccess;
+    // tensor-core kernels for head_dim 64, 128-slot blocks, top <= 2; other
+    // geometries take the warp-level mma kernels below
+    if (read_bwd_tc_supported(hd, bs, top, q, k, v, dout, H))
+        return launch_read_bwd_tc(q, k, v, dout, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
+                                  ws_delta, st);
     if (hd == 64)
         return launch_bwd_t<64>(q, k, v, out, dout, lse, H, nb, bs, top, L, P, dq, dk_acc, dv_acc,
                                 dlog_gates, ws_delta, st);

@@ -1,0 +1,622 @@
+// Gated memory read, backward, on the tensor cores (tcgen05 + TMA + TMEM).
+//
+// Reference semantics: mom_kernels/triton_gpu.py:143-409 (P rebuilt from the
+// saved log-sum-exp, dS = P (dP - delta), dq = dS k * scale, dk = dS^T q *
+// scale, dv = P^T do, dlog_gates = per-block sums of dS over slots and heads).
+// Specialised like read_fwd_tc.cu: head_dim 64, 128-slot blocks, top <= 2.
+//
+// read_bwd_dq_tc_kernel — item = (128-token tile, head), persistent CTAs over
+// contiguous runs of items ordered head-major, so consecutive items usually
+// share their block set and head and reuse the K/V tiles in shared memory.
+//   warp 0     loader: Q, dO rows by TMA gather4; K, V blocks by TMA (on change)
+//   warp 1     MMA: S = Q K^T (TMEM cols 0-255), dP = dO V^T (cols 256-511),
+//              then dQ = dS K (cols 0-63, after the softmax warps drained S)
+//   warps 2-5  pass 1: P = exp2(S*scale + bias - lse) -> bf16 P in smem,
+//              delta = sum P dP (exact, fp32: no read of O), per-block sums of
+//              P dP and P for the gate gradient; pass 2: dS = P (dP - delta)
+//              over P in place; then dQ -> global, delta -> workspace,
+//              gate gradient -> global (fp32 atomics over heads)
+// read_bwd_dkdv_tc_kernel — item = (block, head, split of the block's tiles)
+//   warp 0     loader: K_b, V_b once per item; per tile Q, dO rows (gather4)
+//              and the tile's per-token lse, delta, bias into shared memory
+//   warp 1     MMA: S^T = K_b Q^T (cols 0-127), dP^T = V_b dO^T (cols 128-255),
+//              then dK += dS^T Q (cols 256-319), dV += P^T dO (cols 320-383)
+//   warps 2-5  P^T, dS^T (one slot row per thread) -> bf16 in smem; at the end
+//              of the item dK * scale, dV -> fp32 reductions into global.
+// Every wait is bounded; a timeout sets bit 1 of the plan's error word.
+#include <cudaTypedefs.h>
+
+#include "launch.h"
+#include "tc_common.cuh"
+
+namespace mom {
+
+namespace {
+constexpr int kHD = 64;
+constexpr int kBS = 128;
+constexpr int kTM = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t kRowTile = kTM * kHD * 2;     // 16 KiB: 128 rows x 64 bf16
+constexpr uint32_t kTmemCols = 512;
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+// byte address of 16-B chunk `cg` of row r in a [128 rows x (8 * nchunk) bf16] K-major
+// operand stored as consecutive [128 x 64] SWIZZLE_128B tiles
+__device__ __forceinline__ uint32_t kmaj_addr(uint32_t base, int r, int cg) {
+    return base + (cg >> 3) * kRowTile + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+}
+
+// set of a tile, number of live blocks
+__device__ __forceinline__ int tile_nblk(const PlanView &P, int key, int top, const int **set_out) {
+    const int *set = P.keyset + static_cast<int64_t>(key) * top;
+    int n = 0;
+    while (n < top && set[n] >= 0) ++n;
+    *set_out = set;
+    return n;
+}
+
+struct DqBars {
+    uint64_t full[2], empty[2], kv_full, kv_empty, s_full, ds_full, dq_full, dq_free, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
+constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
+constexpr uint32_t kDqP = 4 * kRowTile;                          // P / dS [128 x 256] bf16
+constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqP + 1024 + 1024;
+}  // namespace
+
+// ============================================================================ dQ
+__global__ void __launch_bounds__(kThreads, 1)
+read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                      const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                      const float *__restrict__ lse, int H, int top, float scale, float scale_log2, PlanView P,
+                      uint16_t *__restrict__ dq, float *__restrict__ dlog_gates, float *__restrict__ ws_delta) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char *sbase = smem_raw + (base - raw);
+    const uint32_t sKV = base + 2 * kDqStage;
+    const uint32_t sK = sKV, sV = sKV + 2 * kRowTile;
+    const uint32_t sP = sKV + kDqKV;
+    DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqP);
+    volatile int *abort_flag = &bars->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = *P.ntiles;
+    const int nitems = ntiles * H;
+    const int per = (nitems + gridDim.x - 1) / gridDim.x;
+    const int it0 = blockIdx.x * per, it1 = min(nitems, it0 + per);
+    const int64_t ld = static_cast<int64_t>(H) * kHD;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&bars->full[s], 1);
+            tc::mbar_init(&bars->empty[s], 1);
+        }
+        tc::mbar_init(&bars->kv_full, 1);
+        tc::mbar_init(&bars->kv_empty, 1);
+        tc::mbar_init(&bars->s_full, 1);
+        tc::mbar_init(&bars->ds_full, 128);
+        tc::mbar_init(&bars->dq_full, 1);
+        tc::mbar_init(&bars->dq_free, 128);
+        tc::mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&bars->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    // item -> (tile, head); items are head-major so runs of one CTA share (set, head)
+    auto item_tile = [&](int item) { return item % ntiles; };
+    auto item_head = [&](int item) { return item / ntiles; };
+    auto item_key = [&](int item) { return P.tiles[item_tile(item)].z; };
+    auto kv_change = [&](int item) {   // this item needs a K/V (re)load
+        return item == it0 || item_key(item) != item_key(item - 1) || item_head(item) != item_head(item - 1);
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ loader
+        int nreload = 0, last_full = -1;
+        for (int item = it0, i = 0; item < it1; ++item, ++i) {
+            const int s = i & 1, j = i >> 1;
+            if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+            const int tile = item_tile(item), h = item_head(item);
+            const int4 td = P.tiles[tile];
+            const int *set;
+            const int nblk = tile_nblk(P, td.z, top, &set);
+            const int nload = nblk > 0 ? nblk : 1;
+            if (kv_change(item)) {
+                if (nreload > 0 && !tc::mbar_wait(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
+                if (lane == 0) {
+                    tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kRowTile);
+                    for (int jb = 0; jb < nload; ++jb) {
+                        const int blk = nblk > 0 ? set[jb] : 0;
+                        tc::tma_load_2d(sK + jb * kRowTile, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
+                        tc::tma_load_2d(sV + jb * kRowTile, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
+                    }
+                }
+                ++nreload;
+            }
+            int rows[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int rr = lane * 4 + u;
+                rows[u] = rr < td.y ? P.perm[td.x + rr] : 0;
+            }
+            const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
+            __syncwarp();
+            tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
+            tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
+            last_full = i;
+        }
+        if (last_full >= 0) tc::mbar_wait(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
+        if (nreload > 0) tc::mbar_wait(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
+        int nreload = 0, issued = 0;
+        for (int item = it0, i = 0; item < it1; ++item, ++i) {
+            const int s = i & 1, j = i >> 1;
+            const int4 td = P.tiles[item_tile(item)];
+            const int *set;
+            const int nblk = tile_nblk(P, td.z, top, &set);
+            const int nload = nblk > 0 ? nblk : 1;
+            const bool reload = kv_change(item);
+            if (reload) {
+                if (!tc::mbar_wait(&bars->kv_full, nreload & 1, P.err, 2, abort_flag)) break;
+                ++nreload;
+            }
+            if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            // S and dP overwrite TMEM columns that dQ(i-1) used: wait for its epilogue
+            if (i > 0 && !tc::mbar_wait(&bars->dq_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
+                const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk) {
+                    tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sQ + kk * 32, 16, 1024),
+                                    tc::smem_desc_sw128(sK + kk * 32, 16, 1024), idesc_s, kk > 0);
+                    tc::mma_bf16_ss(tmem + 256, tc::smem_desc_sw128(sD + kk * 32, 16, 1024),
+                                    tc::smem_desc_sw128(sV + kk * 32, 16, 1024), idesc_s, kk > 0);
+                }
+                tc::mma_commit(&bars->s_full);
+                tc::mma_commit(&bars->empty[s]);
+            }
+            __syncwarp();
+            if (!tc::mbar_wait(&bars->ds_full, i & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            if (lane == 0) {
+                const int ksteps = nload * (kBS / 16);
+                for (int kk = 0; kk < ksteps; ++kk)
+                    tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sP + (kk >> 2) * kRowTile + (kk & 3) * 32, 16, 1024),
+                                    tc::smem_desc_sw128(sK + kk * 2048, 4 * kRowTile, 1024), idesc_dq, kk > 0);
+                tc::mma_commit(&bars->dq_full);
+                // K/V of this run are no longer needed once dQ is done
+                if (item + 1 >= it1 || kv_change(item + 1)) tc::mma_commit(&bars->kv_empty);
+            }
+            __syncwarp();
+            issued = i + 1;
+        }
+        (void)issued;
+        if (lane == 0) tc::mma_commit(&bars->drain);
+        __syncwarp();
+        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+    } else {
+        // ------------------------------------------------------------ softmax-backward
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        for (int item = it0, i = 0; item < it1; ++item, ++i) {
+            const int tile = item_tile(item), h = item_head(item);
+            const int4 td = P.tiles[tile];
+            const int *set;
+            const int nblk = tile_nblk(P, td.z, top, &set);
+            const int nload = nblk > 0 ? nblk : 1;
+            const int tok = r < td.y ? P.perm[td.x + r] : -1;
+            float bias[2] = {0.0f, 0.0f};
+            float lse2 = INFINITY;
+            if (tok >= 0) {
+                for (int jb = 0; jb < nblk; ++jb) bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+                lse2 = lse[static_cast<int64_t>(tok) * H + h] * kLog2e;
+            }
+            if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            // pass 1: P, delta, per-block sums; P -> smem (bf16)
+            float pa[2] = {0.0f, 0.0f}, pb[2] = {0.0f, 0.0f};
+            for (int c = 0; c < nload * 4; ++c) {
+                uint32_t sv[32], dv[32];
+                tc::tmem_ld32(trow + c * 32, sv);
+                tc::tmem_ld32(trow + 256 + c * 32, dv);
+                tc::tmem_ld_wait();
+                const int jb = c >> 2;
+                const bool live = jb < nblk && tok >= 0;
+                const float bj = bias[jb] - lse2;
+                uint32_t pk[16];
+                float sa = 0.0f, sb = 0.0f;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float p0 = live ? exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj)) : 0.0f;
+                    const float p1 = live ? exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj)) : 0.0f;
+                    sa = fmaf(p0, __uint_as_float(dv[2 * e]), sa);
+                    sa = fmaf(p1, __uint_as_float(dv[2 * e + 1]), sa);
+                    sb += p0 + p1;
+                    pk[e] = pack_bf16x2(p0, p1);
+                }
+                pa[jb] += sa;
+                pb[jb] += sb;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    st_shared_v4(kmaj_addr(sP, r, c * 4 + u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+            }
+            const float delta = pa[0] + pa[1];
+            // pass 2: dS = P (dP - delta), in place over P
+            for (int c = 0; c < nload * 4; ++c) {
+                uint32_t dv[32];
+                tc::tmem_ld32(trow + 256 + c * 32, dv);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t addr = kmaj_addr(sP, r, c * 4 + u);
+                    const uint4 pv = ld_shared_v4(addr);
+                    const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+                    uint32_t ow[4];
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) {
+                        const float p0 = __uint_as_float(pw[w] << 16), p1 = __uint_as_float(pw[w] & 0xFFFF0000u);
+                        const int e = u * 8 + w * 2;
+                        ow[w] = pack_bf16x2(p0 * (__uint_as_float(dv[e]) - delta),
+                                            p1 * (__uint_as_float(dv[e + 1]) - delta));
+                    }
+                    st_shared_v4(addr, ow[0], ow[1], ow[2], ow[3]);
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->ds_full);
+            // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
+            if (tok >= 0) {
+                ws_delta[static_cast<int64_t>(tok) * H + h] = delta;
+                const uint32_t kmap = P.rowkmap[td.x + r];
+                for (int kk = 0; kk < top; ++kk) {
+                    const int jsel = (kmap >> (4 * kk)) & 0xF;
+                    if (jsel < nblk) atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk,
+                                               fmaf(-delta, pb[jsel], pa[jsel]));
+                }
+            }
+            // epilogue: dQ * scale -> global
+            if (!tc::mbar_wait(&bars->dq_full, i & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            uint32_t o0[32], o1[32];
+            tc::tmem_ld32(trow, o0);
+            tc::tmem_ld32(trow + 32, o1);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->dq_free);
+            if (tok >= 0) {
+                uint4 *dst = reinterpret_cast<uint4 *>(dq + tok * ld + h * kHD);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint4 v0, v1;
+                    v0.x = pack_bf16x2(__uint_as_float(o0[8 * c + 0]) * scale, __uint_as_float(o0[8 * c + 1]) * scale);
+                    v0.y = pack_bf16x2(__uint_as_float(o0[8 * c + 2]) * scale, __uint_as_float(o0[8 * c + 3]) * scale);
+                    v0.z = pack_bf16x2(__uint_as_float(o0[8 * c + 4]) * scale, __uint_as_float(o0[8 * c + 5]) * scale);
+                    v0.w = pack_bf16x2(__uint_as_float(o0[8 * c + 6]) * scale, __uint_as_float(o0[8 * c + 7]) * scale);
+                    v1.x = pack_bf16x2(__uint_as_float(o1[8 * c + 0]) * scale, __uint_as_float(o1[8 * c + 1]) * scale);
+                    v1.y = pack_bf16x2(__uint_as_float(o1[8 * c + 2]) * scale, __uint_as_float(o1[8 * c + 3]) * scale);
+                    v1.z = pack_bf16x2(__uint_as_float(o1[8 * c + 4]) * scale, __uint_as_float(o1[8 * c + 5]) * scale);
+                    v1.w = pack_bf16x2(__uint_as_float(o1[8 * c + 6]) * scale, __uint_as_float(o1[8 * c + 7]) * scale);
+                    dst[c] = v0;
+                    dst[4 + c] = v1;
+                }
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ============================================================================ dK / dV
+namespace {
+struct DkvBars {
+    uint64_t full[2], empty[2], kv_full, s_full, pds_full, pds_free, acc_full, acc_free, drain;
+    uint32_t tmem_base;
+    int abort;
+};
+constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
+constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
+constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
+constexpr uint32_t kDkvSmem = 2 * kKvTile + 2 * kDkvStage + 2 * (kBS * kTM * 2) + 2 * kMetaBytes + 1024 + 1024;
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads, 1)
+read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                        const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                        const float *__restrict__ lse, const float *__restrict__ ws_delta, int H, int nb, int top,
+                        int nsplit, int max_tiles, float scale, float scale_log2, PlanView P,
+                        float *__restrict__ dk_acc, float *__restrict__ dv_acc) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char *sbase = smem_raw + (base - raw);
+    const uint32_t sK = base, sV = base + kKvTile;
+    const uint32_t sStage = base + 2 * kKvTile;                  // [2][Q | dO]
+    const uint32_t sPT = sStage + 2 * kDkvStage;                 // P^T  [128 slots x 128 tokens]
+    const uint32_t sDS = sPT + kBS * kTM * 2;                    // dS^T
+    float *meta = reinterpret_cast<float *>(sbase + (sDS + kBS * kTM * 2 - base));   // [2][3][128]
+    DkvBars *bars = reinterpret_cast<DkvBars *>(reinterpret_cast<unsigned char *>(meta) + 2 * kMetaBytes);
+    volatile int *abort_flag = &bars->abort;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t ld = static_cast<int64_t>(H) * kHD;
+    const int nitems = nb * H * nsplit;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&bars->full[s], 33);
+            tc::mbar_init(&bars->empty[s], 1);
+        }
+        tc::mbar_init(&bars->kv_full, 1);
+        tc::mbar_init(&bars->s_full, 1);
+        tc::mbar_init(&bars->pds_full, 128);
+        tc::mbar_init(&bars->pds_free, 1);
+        tc::mbar_init(&bars->acc_full, 1);
+        tc::mbar_init(&bars->acc_free, 128);
+        tc::mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&bars->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    // item -> (block, head, split); number of tiles of the item
+    auto item_ntile = [&](int item) {
+        const int blk = item / (H * nsplit), split = item % nsplit;
+        const int count = P.blkcount[blk];
+        return count > split ? (count - split + nsplit - 1) / nsplit : 0;
+    };
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ loader
+        int g = 0, nkv = 0, last = -1;         // g: global tile-step counter of this CTA
+        for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
+            const int blk = item / (H * nsplit), h = (item / nsplit) % H, split = item % nsplit;
+            const int nt = item_ntile(item);
+            if (nt == 0) continue;
+            // K_b, V_b: the previous item's MMAs have all completed once its
+            // accumulators were handed to the epilogue (acc_full), which the
+            // epilogue acknowledges before the loader may overwrite them
+            if (nkv > 0 && !tc::mbar_wait(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            if (lane == 0) {
+                tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
+                tc::tma_load_2d(sK, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
+                tc::tma_load_2d(sV, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
+            }
+            ++nkv;
+            const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
+            for (int t = 0; t < nt; ++t, ++g) {
+                const int s = g & 1, j = g >> 1;
+                if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+                const int tile = list[split + t * nsplit];
+                const int4 td = P.tiles[tile];
+                const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
+                int jb = 0;
+                while (jb < top - 1 && set[jb] != blk) ++jb;
+                float *mb = meta + s * 3 * kTM;
+                int rows[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int rr = lane * 4 + u;
+                    const int tok = rr < td.y ? P.perm[td.x + rr] : -1;
+                    rows[u] = tok >= 0 ? tok : 0;
+                    mb[rr] = tok >= 0 ? P.rowbias[static_cast<int64_t>(td.x + rr) * top + jb] * kLog2e : 0.0f;
+                    mb[kTM + rr] = tok >= 0 ? lse[static_cast<int64_t>(tok) * H + h] * kLog2e : INFINITY;
+                    mb[2 * kTM + rr] = tok >= 0 ? ws_delta[static_cast<int64_t>(tok) * H + h] : 0.0f;
+                }
+                const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
+                if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
+                __syncwarp();
+                tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
+                tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
+                tc::mbar_arrive(&bars->full[s]);
+                last = g;
+            }
+            if (*abort_flag) break;
+        }
+        if (last >= 0) tc::mbar_wait(&bars->full[last & 1], (last >> 1) & 1, P.err, 2, abort_flag);
+        if (nkv > 0) tc::mbar_wait(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kTM, false, false);
+        const uint32_t idesc_acc = tc::idesc_bf16_f32(kBS, kHD, false, true);
+        int g = 0, nkv = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+            const int nt = item_ntile(item);
+            if (nt == 0) continue;
+            if (!tc::mbar_wait(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
+            // the accumulators are reset by the first MMA of the item; the
+            // epilogue of the previous item must have read them
+            if (nkv > 0 && !tc::mbar_wait(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            ++nkv;
+            for (int t = 0; t < nt; ++t, ++g) {
+                const int s = g & 1, j = g >> 1;
+                if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                tc::tc_fence_after();
+                const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < kHD / 16; ++kk) {
+                        tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sK + kk * 32, 16, 1024),
+                                        tc::smem_desc_sw128(sQ + kk * 32, 16, 1024), idesc_s, kk > 0);
+                        tc::mma_bf16_ss(tmem + 128, tc::smem_desc_sw128(sV + kk * 32, 16, 1024),
+                                        tc::smem_desc_sw128(sD + kk * 32, 16, 1024), idesc_s, kk > 0);
+                    }
+                    tc::mma_commit(&bars->s_full);
+                }
+                __syncwarp();
+                if (!tc::mbar_wait(&bars->pds_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                tc::tc_fence_after();
+                if (lane == 0) {
+#pragma unroll
+                    for (int kk = 0; kk < kTM / 16; ++kk) {
+                        const uint32_t aoff = (kk >> 2) * (kBS * 128) + (kk & 3) * 32;
+                        const uint32_t boff = kk * 2048;
+                        const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+                        tc::mma_bf16_ss(tmem + 256, tc::smem_desc_sw128(sDS + aoff, 16, 1024),
+                                        tc::smem_desc_sw128(sQ + boff, 2 * kRowTile, 1024), idesc_acc, acc);
+                        tc::mma_bf16_ss(tmem + 320, tc::smem_desc_sw128(sPT + aoff, 16, 1024),
+                                        tc::smem_desc_sw128(sD + boff, 2 * kRowTile, 1024), idesc_acc, acc);
+                    }
+                    tc::mma_commit(&bars->pds_free);
+                    tc::mma_commit(&bars->empty[s]);
+                    if (t + 1 == nt) tc::mma_commit(&bars->acc_full);
+                }
+                __syncwarp();
+            }
+        }
+        if (lane == 0) tc::mma_commit(&bars->drain);
+        __syncwarp();
+        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+    } else {
+        // ------------------------------------------------------------ P^T, dS^T, epilogue
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;                       // slot row within the block
+        const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        int g = 0, nkv = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+            const int blk = item / (H * nsplit), h = (item / nsplit) % H;
+            const int nt = item_ntile(item);
+            if (nt == 0) continue;
+            for (int t = 0; t < nt; ++t, ++g) {
+                const int s = g & 1;
+                if (!tc::mbar_wait(&bars->s_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                // the smem P^T / dS^T of the previous tile must have been consumed
+                if (g > 0 && !tc::mbar_wait(&bars->pds_free, (g - 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                // the loader's per-token metadata of this stage (acquire it directly)
+                if (!tc::mbar_wait(&bars->full[s], (g >> 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                tc::tc_fence_after();
+                const float *mb = meta + s * 3 * kTM;
+                for (int c = 0; c < kTM / 32; ++c) {
+                    uint32_t sv[32], dv[32];
+                    tc::tmem_ld32(trow + c * 32, sv);
+                    tc::tmem_ld32(trow + 128 + c * 32, dv);
+                    tc::tmem_ld_wait();
+                    uint32_t pk[16], dk[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int col = c * 32 + 2 * e;
+                        const float p0 = exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, mb[col]) - mb[kTM + col]);
+                        const float p1 = exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) - mb[kTM + col + 1]);
+                        pk[e] = pack_bf16x2(p0, p1);
+                        dk[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - mb[2 * kTM + col]),
+                                            p1 * (__uint_as_float(dv[2 * e + 1]) - mb[2 * kTM + col + 1]));
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int cg = c * 4 + u;
+                        const uint32_t off = (cg >> 3) * (kBS * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+                        st_shared_v4(sPT + off, pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+                        st_shared_v4(sDS + off, dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
+                    }
+                }
+                tc::fence_proxy_async_smem();
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bars->pds_full);
+            }
+            if (stop) break;
+            // epilogue of the item: dK * scale, dV -> fp32 reductions
+            if (!tc::mbar_wait(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
+            tc::tc_fence_after();
+            uint32_t k0[32], k1[32], v0[32], v1[32];
+            tc::tmem_ld32(trow + 256, k0);
+            tc::tmem_ld32(trow + 288, k1);
+            tc::tmem_ld32(trow + 320, v0);
+            tc::tmem_ld32(trow + 352, v1);
+            tc::tmem_ld_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->acc_free);
+            ++nkv;
+            float *dkr = dk_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD;
+            float *dvr = dv_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD;
+#pragma unroll
+            for (int c = 0; c < 32; c += 2) {
+                red_add_v2(dkr + c, __uint_as_float(k0[c]) * scale, __uint_as_float(k0[c + 1]) * scale);
+                red_add_v2(dkr + 32 + c, __uint_as_float(k1[c]) * scale, __uint_as_float(k1[c + 1]) * scale);
+                red_add_v2(dvr + c, __uint_as_float(v0[c]), __uint_as_float(v0[c + 1]));
+                red_add_v2(dvr + 32 + c, __uint_as_float(v1[c]), __uint_as_float(v1[c + 1]));
+            }
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (warp == 1) tc::tmem_dealloc(tmem, kTmemCols);
+}
+
+// ------------------------------------------------------------------ host side
+bool make_bf16_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows);
+int device_sm_count();
+
+bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,
+                           const void *dout, int H) {
+    return read_fwd_tc_supported(hd, bs, top, q, k, v, H) && (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
+}
+
+cudaError_t launch_read_bwd_tc(const void *q, const void *k, const void *v, const void *dout, const float *lse,
+                               int H, int nb, int top, const PlanLayout &L, const PlanView &P, void *dq,
+                               float *dk_acc, float *dv_acc, float *dlog_gates, float *ws_delta,
+                               cudaStream_t st) {
+    CUtensorMap mk, mv, mq, md;
+    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
+    if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
+        !make_bf16_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1) ||
+        !make_bf16_map(&md, dout, static_cast<uint64_t>(L.N), cols, 1))
+        return cudaErrorInvalidValue;
+    const float scale = 1.0f / sqrtf(static_cast<float>(kHD));
+    const float scale_log2 = scale * kLog2e;
+    const int sms = device_sm_count();
+    cudaError_t e = cudaFuncSetAttribute(read_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kDqSmem);
+    if (e != cudaSuccess) return e;
+    const int64_t items = L.max_tiles * H;
+    const int grid = static_cast<int>(std::min<int64_t>(items, sms));
+    read_bwd_dq_tc_kernel<<<grid, kThreads, kDqSmem, st>>>(mk, mv, mq, md, lse, H, top, scale, scale_log2, P,
+                                                           static_cast<uint16_t *>(dq), dlog_gates, ws_delta);
+    count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDkvSmem);
+    if (e != cudaSuccess) return e;
+    const int nsplit = std::max(1, std::min(16, (4 * sms + nb * H - 1) / (nb * H)));
+    const int items2 = nb * H * nsplit;
+    read_bwd_dkdv_tc_kernel<<<std::min(items2, sms), kThreads, kDkvSmem, st>>>(
+        mk, mv, mq, md, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2, P,
+        dk_acc, dv_acc);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mom

@@ -338,7 +338,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 map over a row-major [rows, cols] matrix, box = 64 columns x box_rows, 128-B swizzle.
-static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+bool make_bf16_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t cols, uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
@@ -357,7 +357,7 @@ bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k
            (H * kHD * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
-static int sm_count() {
+int device_sm_count() {
     static int n = 0;
     if (!n) {
         int dev = 0;
@@ -373,14 +373,14 @@ cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int 
                                cudaStream_t st) {
     CUtensorMap mk, mv, mq;
     const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
-    if (!make_map(&mk, k, rows, cols, kBS) || !make_map(&mv, v, rows, cols, kBS) ||
-        !make_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1))
+    if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
+        !make_bf16_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
-    const int grid = static_cast<int>(std::min<int64_t>(items, sm_count()));
+    const int grid = static_cast<int>(std::min<int64_t>(items, device_sm_count()));
     const float scale_log2 = kLog2e / sqrtf(static_cast<float>(kHD));
     read_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(mk, mv, mq, H, top,
                                                           scale_log2, P, static_cast<uint16_t *>(out), lse);
