@@ -35,7 +35,9 @@ namespace {
 constexpr int kHD = 64;
 constexpr int kBS = 128;
 constexpr int kTM = 128;
-constexpr int kThreads = 192;
+constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
+constexpr int kSoftThreads = kSoftWarps * 32;
+constexpr int kThreads = 64 + kSoftThreads;
 constexpr uint32_t kRowTile = kTM * kHD * 2;     // 16 KiB: 128 rows x 64 bf16
 constexpr uint32_t kTmemCols = 512;
 
@@ -74,7 +76,8 @@ struct DqBars {
 constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
 constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
 constexpr uint32_t kDqP = 4 * kRowTile;                          // P / dS [128 x 256] bf16
-constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqP + 1024 + 1024;
+constexpr uint32_t kDqScratch = 2 * 2 * 4 * kTM * 4;                // [2 items][P.dP | P][4 groups][128] fp32
+constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqP + kDqScratch + 1024 + 1024;
 }  // namespace
 
 // ============================================================================ dQ
@@ -90,7 +93,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
     const uint32_t sKV = base + 2 * kDqStage;
     const uint32_t sK = sKV, sV = sKV + 2 * kRowTile;
     const uint32_t sP = sKV + kDqKV;
-    DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqP);
+    float *sPart = reinterpret_cast<float *>(sbase + 2 * kDqStage + kDqKV + kDqP);
+    DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqP + kDqScratch);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = *P.ntiles;
@@ -107,9 +111,9 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         tc::mbar_init(&bars->kv_full, 1);
         tc::mbar_init(&bars->kv_empty, 1);
         tc::mbar_init(&bars->s_full, 1);
-        tc::mbar_init(&bars->ds_full, 128);
+        tc::mbar_init(&bars->ds_full, kSoftThreads);
         tc::mbar_init(&bars->dq_full, 1);
-        tc::mbar_init(&bars->dq_free, 128);
+        tc::mbar_init(&bars->dq_free, kSoftThreads);
         tc::mbar_init(&bars->drain, 1);
         bars->abort = 0;
     }
@@ -221,111 +225,129 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax-backward
+        // 16 warps: warp & 3 = TMEM lane quarter (token rows), grp = (warp-2) >> 2 the
+        // 64-column group of the 256 S / dP columns (block grp >> 1). Partial sums of
+        // P*dP and P per group meet in shared memory under named barrier 1 + quarter,
+        // which is also where the four warps of a quarter agree to stop on a timeout.
         const int quarter = warp & 3;
+        const int grp = (warp - 2) >> 2;
+        const int jb = grp >> 1;
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int bar_id = 1 + quarter;
+        bool dead = false;
         for (int item = it0, i = 0; item < it1; ++item, ++i) {
             const int tile = item_tile(item), h = item_head(item);
             const int4 td = P.tiles[tile];
             const int *set;
             const int nblk = tile_nblk(P, td.z, top, &set);
-            const int nload = nblk > 0 ? nblk : 1;
             const int tok = r < td.y ? P.perm[td.x + r] : -1;
-            float bias[2] = {0.0f, 0.0f};
-            float lse2 = INFINITY;
+            float bias = 0.0f, lse2 = INFINITY;
             if (tok >= 0) {
-                for (int jb = 0; jb < nblk; ++jb) bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+                if (jb < nblk) bias = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
                 lse2 = lse[static_cast<int64_t>(tok) * H + h] * kLog2e;
             }
-            if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
+            if (!dead && !tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             tc::tc_fence_after();
-            // pass 1: P, delta, per-block sums; P -> smem (bf16)
-            float pa[2] = {0.0f, 0.0f}, pb[2] = {0.0f, 0.0f};
-            for (int c = 0; c < nload * 4; ++c) {
-                uint32_t sv[32], dv[32];
-                tc::tmem_ld32(trow + c * 32, sv);
-                tc::tmem_ld32(trow + 256 + c * 32, dv);
-                tc::tmem_ld_wait();
-                const int jb = c >> 2;
-                const bool live = jb < nblk && tok >= 0;
-                const float bj = bias[jb] - lse2;
-                uint32_t pk[16];
-                float sa = 0.0f, sb = 0.0f;
+            const bool live = jb < nblk && tok >= 0 && !dead;
+            // pass 1: P over this thread's 64 columns -> smem (bf16), partial sums
+            float pa = 0.0f, pb = 0.0f;
+            if (live) {
+                const float bj = bias - lse2;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float p0 = live ? exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj)) : 0.0f;
-                    const float p1 = live ? exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj)) : 0.0f;
-                    sa = fmaf(p0, __uint_as_float(dv[2 * e]), sa);
-                    sa = fmaf(p1, __uint_as_float(dv[2 * e + 1]), sa);
-                    sb += p0 + p1;
-                    pk[e] = pack_bf16x2(p0, p1);
-                }
-                pa[jb] += sa;
-                pb[jb] += sb;
+                for (int c = 0; c < 2; ++c) {
+                    const int col0 = grp * 64 + c * 32;
+                    uint32_t sv[32], dv[32];
+                    tc::tmem_ld32(trow + col0, sv);
+                    tc::tmem_ld32(trow + 256 + col0, dv);
+                    tc::tmem_ld_wait();
+                    uint32_t pk[16];
 #pragma unroll
-                for (int u = 0; u < 4; ++u)
-                    st_shared_v4(kmaj_addr(sP, r, c * 4 + u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-            }
-            const float delta = pa[0] + pa[1];
-            // pass 2: dS = P (dP - delta), in place over P
-            for (int c = 0; c < nload * 4; ++c) {
-                uint32_t dv[32];
-                tc::tmem_ld32(trow + 256 + c * 32, dv);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const uint32_t addr = kmaj_addr(sP, r, c * 4 + u);
-                    const uint4 pv = ld_shared_v4(addr);
-                    const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
-                    uint32_t ow[4];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        const float p0 = __uint_as_float(pw[w] << 16), p1 = __uint_as_float(pw[w] & 0xFFFF0000u);
-                        const int e = u * 8 + w * 2;
-                        ow[w] = pack_bf16x2(p0 * (__uint_as_float(dv[e]) - delta),
-                                            p1 * (__uint_as_float(dv[e + 1]) - delta));
+                    for (int e = 0; e < 16; ++e) {
+                        const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj));
+                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj));
+                        pa = fmaf(p0, __uint_as_float(dv[2 * e]), pa);
+                        pa = fmaf(p1, __uint_as_float(dv[2 * e + 1]), pa);
+                        pb += p0 + p1;
+                        pk[e] = pack_bf16x2(p0, p1);
                     }
-                    st_shared_v4(addr, ow[0], ow[1], ow[2], ow[3]);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        st_shared_v4(kmaj_addr(sP, r, col0 / 8 + u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2],
+                                     pk[4 * u + 3]);
+                }
+            } else if (!dead && jb < (nblk > 0 ? nblk : 1)) {
+                // padding row or empty set: P = 0, so dS = 0 and dQ = 0 for the row
+#pragma unroll
+                for (int u = 0; u < 8; ++u) st_shared_v4(kmaj_addr(sP, r, grp * 8 + u), 0u, 0u, 0u, 0u);
+            }
+            float *part = sPart + (i & 1) * (2 * 4 * kTM);
+            part[grp * kTM + r] = pa;
+            part[(4 + grp) * kTM + r] = pb;
+            dead = tc::named_bar_or(bar_id, 128, dead);
+            if (dead) break;
+            const float delta = part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
+            // pass 2: dS = P (dP - delta), in place over P
+            if (live) {
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    const int col0 = grp * 64 + c * 32;
+                    uint32_t dv[32];
+                    tc::tmem_ld32(trow + 256 + col0, dv);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const uint32_t addr = kmaj_addr(sP, r, col0 / 8 + u);
+                        const uint4 pv = ld_shared_v4(addr);
+                        const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+                        uint32_t ow[4];
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) {
+                            const float p0 = __uint_as_float(pw[w] << 16), p1 = __uint_as_float(pw[w] & 0xFFFF0000u);
+                            const int e = u * 8 + w * 2;
+                            ow[w] = pack_bf16x2(p0 * (__uint_as_float(dv[e]) - delta),
+                                                p1 * (__uint_as_float(dv[e + 1]) - delta));
+                        }
+                        st_shared_v4(addr, ow[0], ow[1], ow[2], ow[3]);
+                    }
                 }
             }
             tc::fence_proxy_async_smem();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->ds_full);
             // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
-            if (tok >= 0) {
+            if (grp == 0 && tok >= 0) {
                 ws_delta[static_cast<int64_t>(tok) * H + h] = delta;
+                const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
+                const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
                 const uint32_t kmap = P.rowkmap[td.x + r];
                 for (int kk = 0; kk < top; ++kk) {
                     const int jsel = (kmap >> (4 * kk)) & 0xF;
-                    if (jsel < nblk) atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk,
-                                               fmaf(-delta, pb[jsel], pa[jsel]));
+                    if (jsel < nblk && jsel < 2)
+                        atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk, fmaf(-delta, Bv[jsel], A[jsel]));
                 }
             }
-            // epilogue: dQ * scale -> global
-            if (!tc::mbar_wait(&bars->dq_full, i & 1, P.err, 2, abort_flag)) break;
+            // epilogue: 16 of the 64 dQ columns * scale -> global
+            if (!tc::mbar_wait(&bars->dq_full, i & 1, P.err, 2, abort_flag)) { dead = true; continue; }
             tc::tc_fence_after();
-            uint32_t o0[32], o1[32];
-            tc::tmem_ld32(trow, o0);
-            tc::tmem_ld32(trow + 32, o1);
+            uint32_t o[16];
+            tc::tmem_ld16(trow + grp * 16, o);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->dq_free);
             if (tok >= 0) {
-                uint4 *dst = reinterpret_cast<uint4 *>(dq + tok * ld + h * kHD);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint4 v0, v1;
-                    v0.x = pack_bf16x2(__uint_as_float(o0[8 * c + 0]) * scale, __uint_as_float(o0[8 * c + 1]) * scale);
-                    v0.y = pack_bf16x2(__uint_as_float(o0[8 * c + 2]) * scale, __uint_as_float(o0[8 * c + 3]) * scale);
-                    v0.z = pack_bf16x2(__uint_as_float(o0[8 * c + 4]) * scale, __uint_as_float(o0[8 * c + 5]) * scale);
-                    v0.w = pack_bf16x2(__uint_as_float(o0[8 * c + 6]) * scale, __uint_as_float(o0[8 * c + 7]) * scale);
-                    v1.x = pack_bf16x2(__uint_as_float(o1[8 * c + 0]) * scale, __uint_as_float(o1[8 * c + 1]) * scale);
-                    v1.y = pack_bf16x2(__uint_as_float(o1[8 * c + 2]) * scale, __uint_as_float(o1[8 * c + 3]) * scale);
-                    v1.z = pack_bf16x2(__uint_as_float(o1[8 * c + 4]) * scale, __uint_as_float(o1[8 * c + 5]) * scale);
-                    v1.w = pack_bf16x2(__uint_as_float(o1[8 * c + 6]) * scale, __uint_as_float(o1[8 * c + 7]) * scale);
-                    dst[c] = v0;
-                    dst[4 + c] = v1;
-                }
+                uint4 v0, v1;
+                v0.x = pack_bf16x2(__uint_as_float(o[0]) * scale, __uint_as_float(o[1]) * scale);
+                v0.y = pack_bf16x2(__uint_as_float(o[2]) * scale, __uint_as_float(o[3]) * scale);
+                v0.z = pack_bf16x2(__uint_as_float(o[4]) * scale, __uint_as_float(o[5]) * scale);
+                v0.w = pack_bf16x2(__uint_as_float(o[6]) * scale, __uint_as_float(o[7]) * scale);
+                v1.x = pack_bf16x2(__uint_as_float(o[8]) * scale, __uint_as_float(o[9]) * scale);
+                v1.y = pack_bf16x2(__uint_as_float(o[10]) * scale, __uint_as_float(o[11]) * scale);
+                v1.z = pack_bf16x2(__uint_as_float(o[12]) * scale, __uint_as_float(o[13]) * scale);
+                v1.w = pack_bf16x2(__uint_as_float(o[14]) * scale, __uint_as_float(o[15]) * scale);
+                uint4 *dst = reinterpret_cast<uint4 *>(dq + tok * ld + h * kHD + grp * 16);
+                dst[0] = v0;
+                dst[1] = v1;
             }
         }
     }
@@ -376,10 +398,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         }
         tc::mbar_init(&bars->kv_full, 1);
         tc::mbar_init(&bars->s_full, 1);
-        tc::mbar_init(&bars->pds_full, 128);
+        tc::mbar_init(&bars->pds_full, kSoftThreads);
         tc::mbar_init(&bars->pds_free, 1);
         tc::mbar_init(&bars->acc_full, 1);
-        tc::mbar_init(&bars->acc_free, 128);
+        tc::mbar_init(&bars->acc_free, kSoftThreads);
         tc::mbar_init(&bars->drain, 1);
         bars->abort = 0;
     }
@@ -502,7 +524,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ P^T, dS^T, epilogue
+        // 16 warps: warp & 3 = TMEM lane quarter (slot rows), (warp-2) >> 2 = the
+        // 32-token column group this thread handles; no cross-thread reduction.
         const int quarter = warp & 3;
+        const int grp = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;                       // slot row within the block
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         int g = 0, nkv = 0;
@@ -520,24 +545,26 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 if (!tc::mbar_wait(&bars->full[s], (g >> 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 const float *mb = meta + s * 3 * kTM;
-                for (int c = 0; c < kTM / 32; ++c) {
-                    uint32_t sv[32], dv[32];
-                    tc::tmem_ld32(trow + c * 32, sv);
-                    tc::tmem_ld32(trow + 128 + c * 32, dv);
-                    tc::tmem_ld_wait();
-                    uint32_t pk[16], dk[16];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int col = c * 32 + 2 * e;
-                        const float p0 = exp2f(fmaf(__uint_as_float(sv[2 * e]), scale_log2, mb[col]) - mb[kTM + col]);
-                        const float p1 = exp2f(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) - mb[kTM + col + 1]);
+                for (int c = 0; c < 2; ++c) {                    // 16 token columns per step
+                    const int col0 = grp * 32 + c * 16;
+                    uint32_t sv[16], dv[16];
+                    tc::tmem_ld16(trow + col0, sv);
+                    tc::tmem_ld16(trow + 128 + col0, dv);
+                    tc::tmem_ld_wait();
+                    uint32_t pk[8], dk[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const int col = col0 + 2 * e;
+                        const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, mb[col]) - mb[kTM + col]);
+                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) - mb[kTM + col + 1]);
                         pk[e] = pack_bf16x2(p0, p1);
                         dk[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - mb[2 * kTM + col]),
                                             p1 * (__uint_as_float(dv[2 * e + 1]) - mb[2 * kTM + col + 1]));
                     }
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int cg = c * 4 + u;
+                    for (int u = 0; u < 2; ++u) {
+                        const int cg = (col0 >> 3) + u;          // 16-B chunk along the token axis
                         const uint32_t off = (cg >> 3) * (kBS * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
                         st_shared_v4(sPT + off, pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
                         st_shared_v4(sDS + off, dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
@@ -548,26 +575,23 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 tc::mbar_arrive(&bars->pds_full);
             }
             if (stop) break;
-            // epilogue of the item: dK * scale, dV -> fp32 reductions
+            // epilogue of the item: 16 of the 64 dK columns and 16 of the 64 dV
+            // columns per thread -> fp32 reductions
             if (!tc::mbar_wait(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
-            uint32_t k0[32], k1[32], v0[32], v1[32];
-            tc::tmem_ld32(trow + 256, k0);
-            tc::tmem_ld32(trow + 288, k1);
-            tc::tmem_ld32(trow + 320, v0);
-            tc::tmem_ld32(trow + 352, v1);
+            uint32_t kr[16], vr[16];
+            tc::tmem_ld16(trow + 256 + grp * 16, kr);
+            tc::tmem_ld16(trow + 320 + grp * 16, vr);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->acc_free);
             ++nkv;
-            float *dkr = dk_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD;
-            float *dvr = dv_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD;
+            float *dkr = dk_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + grp * 16;
+            float *dvr = dv_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + grp * 16;
 #pragma unroll
-            for (int c = 0; c < 32; c += 2) {
-                red_add_v2(dkr + c, __uint_as_float(k0[c]) * scale, __uint_as_float(k0[c + 1]) * scale);
-                red_add_v2(dkr + 32 + c, __uint_as_float(k1[c]) * scale, __uint_as_float(k1[c + 1]) * scale);
-                red_add_v2(dvr + c, __uint_as_float(v0[c]), __uint_as_float(v0[c + 1]));
-                red_add_v2(dvr + 32 + c, __uint_as_float(v1[c]), __uint_as_float(v1[c + 1]));
+            for (int c = 0; c < 16; c += 2) {
+                red_add_v2(dkr + c, __uint_as_float(kr[c]) * scale, __uint_as_float(kr[c + 1]) * scale);
+                red_add_v2(dvr + c, __uint_as_float(vr[c]), __uint_as_float(vr[c + 1]));
             }
         }
     }

@@ -29,12 +29,18 @@ namespace {
 constexpr int kHD = 64;
 constexpr int kBS = 128;
 constexpr int kTM = 128;                       // token rows per tile (TMEM lanes)
-constexpr int kThreads = 192;
+constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
+constexpr int kSoftThreads = kSoftWarps * 32;
+constexpr int kThreads = 64 + kSoftThreads;     // loader + MMA + softmax
 constexpr uint32_t kQBytes = kTM * kHD * 2;    // 16 KiB
 constexpr uint32_t kBlkBytes = kBS * kHD * 2;  // 16 KiB per 128-slot block of K or V
 constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) + V(2 blocks)
-constexpr uint32_t kPBytes = kTM * 2 * kBS * 2;             // 64 KiB: P[128 x 256] bf16
-constexpr uint32_t kSmemBytes = 2 * kStageBytes + kPBytes + 1024 /*barriers*/ + 1024 /*align*/;
+// P[128 x 256] bf16 = four 16 KiB K-chunks: chunks 0-2 overlay the item's own Q, K0, K1
+// (dead once S is computed; the stage is refilled only after O(i) completed), chunk 3
+// has its own buffer.
+constexpr uint32_t kPXBytes = kTM * 64 * 2;
+constexpr uint32_t kScratchBytes = 8 * kTM * 4;   // partial row max [4][128], row sums [4][128]
+constexpr uint32_t kSmemBytes = 2 * kStageBytes + kPXBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;                // O buffers at columns 256 and 320
 
@@ -53,8 +59,12 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
-    const uint32_t sP = base + 2 * kStageBytes;
-    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kPBytes);
+    const uint32_t sPX = base + 2 * kStageBytes;
+    float *sMax = reinterpret_cast<float *>(sbase + 2 * kStageBytes + kPXBytes);  // [4][128]
+    float *sSum = sMax + 4 * kTM;                                                   // [4][128]
+    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kPXBytes + kScratchBytes);
+    // K-chunk c of P for an item in stage s
+    auto p_chunk = [&](int s, int c) -> uint32_t { return c < 3 ? base + s * kStageBytes + c * (kTM * 128) : sPX; };
     volatile int *abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -67,10 +77,10 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             tc::mbar_init(&bars->full[s], 1);
             tc::mbar_init(&bars->empty[s], 1);
             tc::mbar_init(&bars->o_full[s], 1);
-            tc::mbar_init(&bars->o_free[s], 128);
+            tc::mbar_init(&bars->o_free[s], kSoftThreads);
         }
         tc::mbar_init(&bars->s_full, 1);
-        tc::mbar_init(&bars->p_full, 128);
+        tc::mbar_init(&bars->p_full, kSoftThreads);
         tc::mbar_init(&bars->drain, 1);
         bars->abort = 0;
     }
@@ -142,7 +152,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 const uint32_t sV = base + prev_s * kStageBytes + kQBytes + 2 * kBlkBytes;
                 const int ksteps = prev_nblk * (kBS / 16);
                 for (int kk = 0; kk < ksteps; ++kk) {
-                    const uint64_t ad = tc::smem_desc_sw128(sP + (kk >> 2) * (kTM * 128) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t ad = tc::smem_desc_sw128(p_chunk(prev_s, kk >> 2) + (kk & 3) * 32, 16, 1024);
                     const uint64_t bd = tc::smem_desc_sw128(sV + kk * 2048, kBlkBytes * 2, 1024);
                     tc::mma_bf16_ss(tmem + kOCol + b * kHD, ad, bd, idesc_o, kk > 0);
                 }
@@ -187,42 +197,49 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax + epilogue
+        // 16 warps: warp & 3 is the TMEM lane quarter (hardware rule), (warp-2) >> 2
+        // the 64-column group of the 256 score columns (block = group >> 1). The
+        // four warps of one lane quarter exchange partial row max / sum through
+        // shared memory under named barrier 1 + quarter.
         const int quarter = warp & 3;
+        const int grp = (warp - 2) >> 2;
+        const int jb = grp >> 1;
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        const int bar_id = 1 + quarter;
         int prev_tok = -1, prev_h = 0;
-        float prev_inv = 0.0f, prev_lse = -INFINITY;
+        float prev_m = 0.0f;
+        float prev_l = 0.0f;
         auto epilogue = [&](int i) {
             const int b = i & 1;
+            const float l = prev_l;
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             tc::tc_fence_after();
-            uint32_t o0[32], o1[32];
-            tc::tmem_ld32(trow + kOCol + b * kHD, o0);
-            tc::tmem_ld32(trow + kOCol + b * kHD + 32, o1);
+            uint32_t o[16];
+            tc::tmem_ld16(trow + kOCol + b * kHD + grp * 16, o);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->o_free[b]);
             if (prev_tok >= 0) {
-                uint4 *dst = reinterpret_cast<uint4 *>(out + prev_tok * ld + prev_h * kHD);
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint4 v0, v1;
-                    v0.x = pack_bf16x2(__uint_as_float(o0[8 * c + 0]) * prev_inv, __uint_as_float(o0[8 * c + 1]) * prev_inv);
-                    v0.y = pack_bf16x2(__uint_as_float(o0[8 * c + 2]) * prev_inv, __uint_as_float(o0[8 * c + 3]) * prev_inv);
-                    v0.z = pack_bf16x2(__uint_as_float(o0[8 * c + 4]) * prev_inv, __uint_as_float(o0[8 * c + 5]) * prev_inv);
-                    v0.w = pack_bf16x2(__uint_as_float(o0[8 * c + 6]) * prev_inv, __uint_as_float(o0[8 * c + 7]) * prev_inv);
-                    v1.x = pack_bf16x2(__uint_as_float(o1[8 * c + 0]) * prev_inv, __uint_as_float(o1[8 * c + 1]) * prev_inv);
-                    v1.y = pack_bf16x2(__uint_as_float(o1[8 * c + 2]) * prev_inv, __uint_as_float(o1[8 * c + 3]) * prev_inv);
-                    v1.z = pack_bf16x2(__uint_as_float(o1[8 * c + 4]) * prev_inv, __uint_as_float(o1[8 * c + 5]) * prev_inv);
-                    v1.w = pack_bf16x2(__uint_as_float(o1[8 * c + 6]) * prev_inv, __uint_as_float(o1[8 * c + 7]) * prev_inv);
-                    dst[c] = v0;
-                    dst[4 + c] = v1;
-                }
-                lse[static_cast<int64_t>(prev_tok) * H + prev_h] = prev_lse;
+                uint4 v0, v1;
+                v0.x = pack_bf16x2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
+                v0.y = pack_bf16x2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
+                v0.z = pack_bf16x2(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
+                v0.w = pack_bf16x2(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
+                v1.x = pack_bf16x2(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
+                v1.y = pack_bf16x2(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
+                v1.z = pack_bf16x2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
+                v1.w = pack_bf16x2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
+                uint4 *dst = reinterpret_cast<uint4 *>(out + prev_tok * ld + prev_h * kHD + grp * 16);
+                dst[0] = v0;
+                dst[1] = v1;
+                if (grp == 0)
+                    lse[static_cast<int64_t>(prev_tok) * H + prev_h] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
             }
         };
         // per-item row metadata, fetched one item ahead so that its global-load
         // latency hides behind the current item's softmax
-        struct Meta { int h, nblk, tok; float bias[2]; };
+        struct Meta { int h, nblk, tok; float bias; };
         auto fetch = [&](int item, Meta &m) {
             const int tile = item / H;
             m.h = item % H;
@@ -231,90 +248,90 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             m.nblk = 0;
             while (m.nblk < top && set[m.nblk] >= 0) ++m.nblk;
             m.tok = r < td.y ? P.perm[td.x + r] : -1;
-            m.bias[0] = m.bias[1] = 0.0f;
-            if (m.tok >= 0)
-                for (int jb = 0; jb < m.nblk; ++jb) m.bias[jb] = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
+            m.bias = (m.tok >= 0 && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e : 0.0f;
         };
         Meta cur, nxt;
         if (static_cast<int>(blockIdx.x) < nitems) fetch(blockIdx.x, cur);
         int count = 0;
+        bool dead = false;   // a bounded wait gave up: skip work, keep the barrier structure
         for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
             const int h = cur.h, nblk = cur.nblk, tok = cur.tok;
-            const int nload = nblk > 0 ? nblk : 1;
-            const float bias[2] = {cur.bias[0], cur.bias[1]};
+            const float bias = cur.bias;
             if (item + static_cast<int>(gridDim.x) < nitems) fetch(item + gridDim.x, nxt);
-            if (!tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) break;
+            // the row sum of item i-1 (complete since the second barrier of i-1), read
+            // before this item's first barrier lets anyone overwrite it
+            if (i > 0) prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
+            if (!dead && !tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
+            const bool live = jb < nblk && !dead;
             tc::tc_fence_after();
-            // pass 1: raw row maximum of each block (four 32-column loads in flight)
-            float mx[2] = {-INFINITY, -INFINITY};
-            for (int jb = 0; jb < nload; ++jb) {
-                uint32_t v0[32], v1[32], v2[32], v3[32];
-                tc::tmem_ld32(trow + jb * 128, v0);
-                tc::tmem_ld32(trow + jb * 128 + 32, v1);
-                tc::tmem_ld32(trow + jb * 128 + 64, v2);
-                tc::tmem_ld32(trow + jb * 128 + 96, v3);
-                tc::tmem_ld_wait();
-                float m0 = __uint_as_float(v0[0]), m1 = __uint_as_float(v1[0]);
-                float m2_ = __uint_as_float(v2[0]), m3 = __uint_as_float(v3[0]);
+            // pass 1: partial row maximum over this thread's 64 columns
+            float mpart = -INFINITY;
+            if (live) {
+                float mx = -INFINITY;
 #pragma unroll
-                for (int e = 1; e < 32; ++e) {
-                    m0 = fmaxf(m0, __uint_as_float(v0[e]));
-                    m1 = fmaxf(m1, __uint_as_float(v1[e]));
-                    m2_ = fmaxf(m2_, __uint_as_float(v2[e]));
-                    m3 = fmaxf(m3, __uint_as_float(v3[e]));
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t v[32];
+                    tc::tmem_ld32(trow + grp * 64 + c * 32, v);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
                 }
-                mx[jb] = fmaxf(fmaxf(m0, m1), fmaxf(m2_, m3));
+                mpart = fmaf(mx, scale_log2, bias);
             }
-            float m2 = -INFINITY;
-            for (int jb = 0; jb < nblk; ++jb) m2 = fmaxf(m2, fmaf(mx[jb], scale_log2, bias[jb]));
-            const float mref = (m2 == -INFINITY) ? 0.0f : m2;
-            // P is free once O(i-1) has consumed it
-            if (i > 0 && !tc::mbar_wait(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag)) break;
-            // pass 2: p = exp2(s*scale + bias - m) -> bf16 P, row sum
-            float l = 0.0f;
-            for (int c2 = 0; c2 < nload * 2; ++c2) {      // 64 columns per step, two loads in flight
-                uint32_t va[32], vb[32];
-                tc::tmem_ld32(trow + c2 * 64, va);
-                tc::tmem_ld32(trow + c2 * 64 + 32, vb);
-                tc::tmem_ld_wait();
-                const int jb = c2 >> 1;
-                const float bj = bias[jb] - mref;
-                const bool live = jb < nblk;
+            sMax[grp * kTM + r] = mpart;
+            tc::named_bar(bar_id, 128);
+            float m = sMax[r];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    const uint32_t *v = half ? vb : va;
+            for (int g = 1; g < 4; ++g) m = fmaxf(m, sMax[g * kTM + r]);
+            const float mref = (m == -INFINITY) ? 0.0f : m;
+            // P is free once O(i-1) has consumed it
+            if (!dead && i > 0 && !tc::mbar_wait(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag))
+                dead = true;
+            // pass 2: p = 2^(s*scale + bias - m) -> bf16 P (K-chunk grp), partial row sum
+            float lpart = 0.0f;
+            if (live && !dead) {
+                const float bj = bias - mref;
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t v[32];
+                    tc::tmem_ld32(trow + grp * 64 + c * 32, v);
+                    tc::tmem_ld_wait();
                     uint32_t pk[16];
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
-                        const float p0 = live ? exp2f(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj)) : 0.0f;
-                        const float p1 = live ? exp2f(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj)) : 0.0f;
-                        l += p0 + p1;
+                        const float p0 = tc::ex2(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj));
+                        const float p1 = tc::ex2(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj));
+                        lpart += p0 + p1;
                         pk[e] = pack_bf16x2(p0, p1);
                     }
-                    const int c = c2 * 2 + half;
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int cg = c * 4 + u;            // 16-B chunk index along the row
-                        const uint32_t dst = sP + (cg >> 3) * (kTM * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
+                        const int cw = c * 4 + u;                 // 16-B chunk within the K-chunk
+                        const uint32_t dst = p_chunk(i & 1, grp) + r * 128 + ((cw ^ (r & 7)) << 4);
                         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(pk[4 * u]),
                                      "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
                                      : "memory");
                     }
                 }
             }
+            sSum[grp * kTM + r] = lpart;
             tc::fence_proxy_async_smem();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->p_full);
+            // row sums of item i complete; the four warps of this lane quarter agree
+            // on stopping together
+            dead = tc::named_bar_or(bar_id, 128, dead);
+            if (dead) break;
             if (i > 0) epilogue(i - 1);
             prev_tok = tok;
             prev_h = h;
+            prev_m = m;
             cur = nxt;
-            prev_inv = l > 0.0f ? 1.0f / l : 0.0f;
-            prev_lse = l > 0.0f ? (m2 + log2f(l)) * kLn2 : -INFINITY;
             count = i + 1;
         }
-        if (count > 0 && !*abort_flag) {
+        if (count > 0 && !dead && !*abort_flag) {
             const int i = count - 1;
+            prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
             if (tc::mbar_wait(&bars->o_full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag)) epilogue(i);
         }
     }
