@@ -139,14 +139,14 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         int nreload = 0, last_full = -1;
         for (int item = it0, i = 0; item < it1; ++item, ++i) {
             const int s = i & 1, j = i >> 1;
-            if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
             const int tile = item_tile(item), h = item_head(item);
             const int4 td = P.tiles[tile];
             const int *set;
             const int nblk = tile_nblk(P, td.z, top, &set);
             const int nload = nblk > 0 ? nblk : 1;
             if (kv_change(item)) {
-                if (nreload > 0 && !tc::mbar_wait(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
+                if (nreload > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
                 if (lane == 0) {
                     tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kRowTile);
                     for (int jb = 0; jb < nload; ++jb) {
@@ -170,8 +170,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             last_full = i;
         }
-        if (last_full >= 0) tc::mbar_wait(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
-        if (nreload > 0) tc::mbar_wait(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
+        if (last_full >= 0) tc::mbar_wait_warp(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
+        if (nreload > 0) tc::mbar_wait_warp(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
@@ -184,12 +184,12 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             const int nload = nblk > 0 ? nblk : 1;
             const bool reload = kv_change(item);
             if (reload) {
-                if (!tc::mbar_wait(&bars->kv_full, nreload & 1, P.err, 2, abort_flag)) break;
+                if (!tc::mbar_wait_warp(&bars->kv_full, nreload & 1, P.err, 2, abort_flag)) break;
                 ++nreload;
             }
-            if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
             // S and dP overwrite TMEM columns that dQ(i-1) used: wait for its epilogue
-            if (i > 0 && !tc::mbar_wait(&bars->dq_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
+            if (i > 0 && !tc::mbar_wait_warp(&bars->dq_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
                 const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
@@ -205,7 +205,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 tc::mma_commit(&bars->empty[s]);
             }
             __syncwarp();
-            if (!tc::mbar_wait(&bars->ds_full, i & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->ds_full, i & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
                 const int ksteps = nload * (kBS / 16);
@@ -222,7 +222,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         (void)issued;
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
-        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+        tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax-backward
         // 16 warps: warp & 3 = TMEM lane quarter (token rows), grp = (warp-2) >> 2 the
@@ -247,9 +247,11 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 if (jb < nblk) bias = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
                 lse2 = lse[static_cast<int64_t>(tok) * H + h] * kLog2e;
             }
-            if (!dead && !tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
+            if (!dead && !tc::mbar_wait_warp(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             tc::tc_fence_after();
-            const bool live = jb < nblk && tok >= 0 && !dead;
+            // warp-uniform: the tcgen05.ld below are warp-collective. Padding rows
+            // (tok < 0) have lse2 = +inf and get P = 0 from the same code.
+            const bool live = jb < nblk && !dead;
             // pass 1: P over this thread's 64 columns -> smem (bf16), partial sums
             float pa = 0.0f, pb = 0.0f;
             if (live) {
@@ -276,8 +278,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                         st_shared_v4(kmaj_addr(sP, r, col0 / 8 + u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2],
                                      pk[4 * u + 3]);
                 }
-            } else if (!dead && jb < (nblk > 0 ? nblk : 1)) {
-                // padding row or empty set: P = 0, so dS = 0 and dQ = 0 for the row
+            } else if (!dead && nblk == 0 && jb == 0) {
+                // empty block set: P = 0, so dS = 0 and dQ = 0
 #pragma unroll
                 for (int u = 0; u < 8; ++u) st_shared_v4(kmaj_addr(sP, r, grp * 8 + u), 0u, 0u, 0u, 0u);
             }
@@ -328,7 +330,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 }
             }
             // epilogue: 16 of the 64 dQ columns * scale -> global
-            if (!tc::mbar_wait(&bars->dq_full, i & 1, P.err, 2, abort_flag)) { dead = true; continue; }
+            if (!tc::mbar_wait_warp(&bars->dq_full, i & 1, P.err, 2, abort_flag)) { dead = true; continue; }
             tc::tc_fence_after();
             uint32_t o[16];
             tc::tmem_ld16(trow + grp * 16, o);
@@ -430,7 +432,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             // K_b, V_b: the previous item's MMAs have all completed once its
             // accumulators were handed to the epilogue (acc_full), which the
             // epilogue acknowledges before the loader may overwrite them
-            if (nkv > 0 && !tc::mbar_wait(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             if (lane == 0) {
                 tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
                 tc::tma_load_2d(sK, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
@@ -440,7 +442,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
             for (int t = 0; t < nt; ++t, ++g) {
                 const int s = g & 1, j = g >> 1;
-                if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+                if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
                 const int tile = list[split + t * nsplit];
                 const int4 td = P.tiles[tile];
                 const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
@@ -467,8 +469,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             }
             if (*abort_flag) break;
         }
-        if (last >= 0) tc::mbar_wait(&bars->full[last & 1], (last >> 1) & 1, P.err, 2, abort_flag);
-        if (nkv > 0) tc::mbar_wait(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
+        if (last >= 0) tc::mbar_wait_warp(&bars->full[last & 1], (last >> 1) & 1, P.err, 2, abort_flag);
+        if (nkv > 0) tc::mbar_wait_warp(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kTM, false, false);
@@ -478,14 +480,14 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
             const int nt = item_ntile(item);
             if (nt == 0) continue;
-            if (!tc::mbar_wait(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
             // the accumulators are reset by the first MMA of the item; the
             // epilogue of the previous item must have read them
-            if (nkv > 0 && !tc::mbar_wait(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             ++nkv;
             for (int t = 0; t < nt; ++t, ++g) {
                 const int s = g & 1, j = g >> 1;
-                if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
                 if (lane == 0) {
@@ -499,7 +501,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     tc::mma_commit(&bars->s_full);
                 }
                 __syncwarp();
-                if (!tc::mbar_wait(&bars->pds_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (!tc::mbar_wait_warp(&bars->pds_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 if (lane == 0) {
 #pragma unroll
@@ -521,7 +523,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         }
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
-        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+        tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ P^T, dS^T, epilogue
         // 16 warps: warp & 3 = TMEM lane quarter (slot rows), (warp-2) >> 2 = the
@@ -538,11 +540,11 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             if (nt == 0) continue;
             for (int t = 0; t < nt; ++t, ++g) {
                 const int s = g & 1;
-                if (!tc::mbar_wait(&bars->s_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (!tc::mbar_wait_warp(&bars->s_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 // the smem P^T / dS^T of the previous tile must have been consumed
-                if (g > 0 && !tc::mbar_wait(&bars->pds_free, (g - 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (g > 0 && !tc::mbar_wait_warp(&bars->pds_free, (g - 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 // the loader's per-token metadata of this stage (acquire it directly)
-                if (!tc::mbar_wait(&bars->full[s], (g >> 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (!tc::mbar_wait_warp(&bars->full[s], (g >> 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 const float *mb = meta + s * 3 * kTM;
 #pragma unroll
@@ -577,7 +579,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             if (stop) break;
             // epilogue of the item: 16 of the 64 dK columns and 16 of the 64 dV
             // columns per thread -> fp32 reductions
-            if (!tc::mbar_wait(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             uint32_t kr[16], vr[16];
             tc::tmem_ld16(trow + 256 + grp * 16, kr);

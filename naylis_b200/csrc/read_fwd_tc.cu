@@ -103,7 +103,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         int issued = 0;
         for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
             const int s = i & 1, j = i >> 1;
-            if (!tc::mbar_wait(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
             const int tile = item / H, h = item % H;
             const int4 td = P.tiles[tile];
             const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
@@ -136,7 +136,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         // make sure no TMA write is still in flight when the CTA retires
         if (issued > 0) {
             const int i = issued - 1;
-            tc::mbar_wait(&bars->full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag);
+            tc::mbar_wait_warp(&bars->full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag);
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -145,8 +145,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         bool ok = true;
         auto issue_o = [&](int i) {   // O(i) = P V, stage of item i, buffer i & 1
             const int b = i & 1;
-            if (!tc::mbar_wait(&bars->p_full, i & 1, P.err, 2, abort_flag)) return false;
-            if (!tc::mbar_wait(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) return false;
+            if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) return false;
+            if (!tc::mbar_wait_warp(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) return false;
             tc::tc_fence_after();
             if (lane == 0) {
                 const uint32_t sV = base + prev_s * kStageBytes + kQBytes + 2 * kBlkBytes;
@@ -165,7 +165,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         for (int item = blockIdx.x, i = 0; item < nitems && ok; item += gridDim.x, ++i) {
             const int s = i & 1, j = i >> 1;
             if (i > 0 && !issue_o(i - 1)) break;
-            if (!tc::mbar_wait(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
             const int tile = item / H;
             const int4 td = P.tiles[tile];
             const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
@@ -194,7 +194,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         // drain: every MMA this thread issued has completed before TMEM is freed
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
-        tc::mbar_wait(&bars->drain, 0, P.err, 2, abort_flag);
+        tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax + epilogue
         // 16 warps: warp & 3 is the TMEM lane quarter (hardware rule), (warp-2) >> 2
@@ -261,7 +261,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             // the row sum of item i-1 (complete since the second barrier of i-1), read
             // before this item's first barrier lets anyone overwrite it
             if (i > 0) prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
-            if (!dead && !tc::mbar_wait(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
+            if (!dead && !tc::mbar_wait_warp(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             const bool live = jb < nblk && !dead;
             tc::tc_fence_after();
             // pass 1: partial row maximum over this thread's 64 columns
@@ -285,7 +285,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             for (int g = 1; g < 4; ++g) m = fmaxf(m, sMax[g * kTM + r]);
             const float mref = (m == -INFINITY) ? 0.0f : m;
             // P is free once O(i-1) has consumed it
-            if (!dead && i > 0 && !tc::mbar_wait(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag))
+            if (!dead && i > 0 && !tc::mbar_wait_warp(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag))
                 dead = true;
             // pass 2: p = 2^(s*scale + bias - m) -> bf16 P (K-chunk grp), partial row sum
             float lpart = 0.0f;
@@ -332,7 +332,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         if (count > 0 && !dead && !*abort_flag) {
             const int i = count - 1;
             prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
-            if (tc::mbar_wait(&bars->o_full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag)) epilogue(i);
+            if (tc::mbar_wait_warp(&bars->o_full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag)) epilogue(i);
         }
     }
     tc::tc_fence_before();

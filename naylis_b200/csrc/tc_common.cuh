@@ -67,6 +67,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
     }
 }
 
+// Warp-uniform form of mbar_wait: every lane waits, all lanes get the same
+// answer (the tcgen05.ld / named-barrier code after it must not diverge).
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int *err, int err_bit,
+                                               volatile int *abort) {
+    const bool ok = mbar_wait(bar, parity, err, err_bit, abort);
+    return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------ proxies
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
