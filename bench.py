@@ -139,7 +139,9 @@ def run_gpu(args):
     layer.noise_scale = 1.0
     M = torch.nn.Parameter(torch.randn(c["nb"], c["bs"] * c["d"], device=dev) * 0.02)
     x = torch.randn(c["B"], c["S"], c["d"], device=dev).to(torch.bfloat16).requires_grad_(True)
-    dout = torch.randn(c["B"], c["S"], c["d"], device=dev).to(torch.bfloat16)
+    # the layer's output is fp32 (bf16 o_proj output times the fp32 mom_scale,
+    # model.py:239), so the upstream gradient is fp32 too
+    dout = torch.randn(c["B"], c["S"], c["d"], device=dev)
 
     holder = torch.nn.Module()
     holder.layer = layer
@@ -270,7 +272,7 @@ def measure_kernels(layer, x, M, dout, dev, args):
     dv = torch.empty_like(dk)
     dlg = torch.empty(N, top, dtype=torch.float32, device=dev)
     ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=dev)
-    do4 = dout.view(B, S, H, hd)
+    do4 = dout.to(torch.bfloat16).view(B, S, H, hd)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def read_once():
@@ -365,9 +367,9 @@ def measure_e2e(step, x, dout, dev, args, world, N):
         t = torch.tensor([ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    nbytes = xh.numel() * xh.element_size()
     return {"value": round(world * N * iters / (ms / 1e3), 1), "unit": "tokens/s",
-            "h2d_bytes_per_step": 2 * nbytes, "d2h_bytes_per_step": nbytes}
+            "h2d_bytes_per_step": xh.numel() * xh.element_size() + gh.numel() * gh.element_size(),
+            "d2h_bytes_per_step": dxh.numel() * dxh.element_size()}
 
 
 # ------------------------------------------------------------------ CPU arms

@@ -141,6 +141,16 @@ MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void
                  const void *plan, void *dq, float *dk_acc, float *dv_acc,
                  float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------------------------ output scale
+ * ReZero output scale of the layer, fused: y = scale[0] * o with y in fp32
+ * (model.py:239, `self.mom_scale * out`: a (1,) fp32 parameter times the bf16
+ * o_proj output promotes to fp32). `scale` is a device pointer to one float. */
+MOM_API int mom_scale_fwd(const void *o, int o_dtype, int64_t n, const float *scale, float *y,
+                          void *stream);
+/* Its backward in one pass: d_o = scale[0] * g in o's dtype, d_scale[0] = sum(g * o). */
+MOM_API int mom_scale_bwd(const void *g, int g_dtype, const void *o, int o_dtype, int64_t n,
+                          const float *scale, void *d_o, float *d_scale, void *stream);
+
 /* Reads (and clears) the device error word of a plan: MOM_OK, or
  * MOM_ERR_DEVICE_INDEX when mom_bucket saw an index outside [0, nb).
  * Synchronises `stream`. */

@@ -229,6 +229,30 @@ int mom_bucket(const void *top_idx, int idx_dtype, const float *log_gates, int64
     return MOM_OK;
 }
 
+// ------------------------------------------------------------------ output scale
+int mom_scale_fwd(const void *o, int o_dtype, int64_t n, const float *scale, float *y, void *stream) {
+    MOM_REQUIRE(n >= 0, "n must be >= 0");
+    MOM_REQUIRE(is_float_dtype(o_dtype), "o dtype must be F32 or BF16");
+    if (n == 0) return MOM_OK;
+    MOM_REQUIRE(o && scale && y, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_scale_fwd(o, o_dtype, scale, n, y, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "scale_fwd");
+}
+
+int mom_scale_bwd(const void *g, int g_dtype, const void *o, int o_dtype, int64_t n, const float *scale,
+                  void *d_o, float *d_scale, void *stream) {
+    MOM_REQUIRE(n >= 0, "n must be >= 0");
+    MOM_REQUIRE(is_float_dtype(o_dtype) && is_float_dtype(g_dtype), "dtypes must be F32 or BF16");
+    MOM_REQUIRE(scale && d_scale && (n == 0 || (g && o && d_o)), "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_scale_bwd(g, g_dtype, o, o_dtype, scale, n, d_o, d_scale,
+                                          static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "scale_bwd");
+}
+
 int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *stream) {
     MOM_REQUIRE(plan, "null plan");
     const mom::PlanLayout L = mom::plan_layout(N, nb, top);

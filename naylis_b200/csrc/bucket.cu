@@ -61,6 +61,7 @@ PlanLayout plan_layout(int64_t N, int64_t nb, int64_t top) {
 PlanView plan_view(void *plan, const PlanLayout &L) {
     char *p = static_cast<char *>(plan);
     PlanView v;
+    v.n = L.N;
     v.err = reinterpret_cast<int *>(p + L.off_err);
     v.ntiles = reinterpret_cast<int *>(p + L.off_ntiles);
     v.key = reinterpret_cast<int *>(p + L.off_key);

@@ -29,6 +29,7 @@ PlanLayout plan_layout(int64_t N, int64_t nb, int64_t top);
 
 // Device view of a plan (pointers into the caller's buffer).
 struct PlanView {
+    int64_t n;           // tokens (rows of the plan)
     int *err;            // [1]     error word (bit 0: index out of range)
     int *ntiles;         // [1]     number of tiles
     int *key;            // [N]     routing-set key of each token
@@ -58,6 +59,9 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
                              const float *dlog_gates, const float *dgates, const float *dprobs,
                              void *dx, int dxdt, int accumulate, float *dw_down, float *dw_up,
                              float *ws_dlogits, float *ws_dz, float *ws_u, cudaStream_t st);
+cudaError_t launch_scale_fwd(const void *o, int odt, const float *scale, int64_t n, float *y, cudaStream_t st);
+cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, const float *scale, int64_t n,
+                             void *d_o, float *d_scale, cudaStream_t st);
 cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
                           const PlanLayout &L, const PlanView &P, cudaStream_t st);
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,

@@ -122,8 +122,8 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
             const int tok = sTok[r];
             if (half == 0) {
                 sDelta[r] = tok >= 0 ? acc : 0.0f;
-                sLse[r] = tok >= 0 ? lse[static_cast<int64_t>(tok) * H + h] * kLog2e : INFINITY;
-                if (tok >= 0) ws_delta[static_cast<int64_t>(tok) * H + h] = acc;
+                sLse[r] = tok >= 0 ? lse[static_cast<int64_t>(h) * P.n + row0 + r] * kLog2e : INFINITY;
+                if (tok >= 0) ws_delta[static_cast<int64_t>(h) * P.n + row0 + r] = acc;
             }
         }
         __syncthreads();
@@ -324,8 +324,8 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
                 const int tok = r < td.y ? P.perm[td.x + r] : -1;
                 sTok[buf * kTileM + r] = tok;
                 sBias[buf * kTileM + r] = tok >= 0 ? P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e : 0.0f;
-                sLse[buf * kTileM + r] = tok >= 0 ? lse[static_cast<int64_t>(tok) * H + h] * kLog2e : INFINITY;
-                sDelta[buf * kTileM + r] = tok >= 0 ? ws_delta[static_cast<int64_t>(tok) * H + h] : 0.0f;
+                sLse[buf * kTileM + r] = tok >= 0 ? lse[static_cast<int64_t>(h) * P.n + td.x + r] * kLog2e : INFINITY;
+                sDelta[buf * kTileM + r] = tok >= 0 ? ws_delta[static_cast<int64_t>(h) * P.n + td.x + r] : 0.0f;
             }
             __syncthreads();
             const uint32_t sq = smem_u32(sT + buf * 2 * kTileBytes);

@@ -245,7 +245,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             float bias = 0.0f, lse2 = INFINITY;
             if (tok >= 0) {
                 if (jb < nblk) bias = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
-                lse2 = lse[static_cast<int64_t>(tok) * H + h] * kLog2e;
+                lse2 = lse[static_cast<int64_t>(h) * P.n + td.x + r] * kLog2e;
             }
             if (!dead && !tc::mbar_wait_warp(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             tc::tc_fence_after();
@@ -319,7 +319,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             tc::mbar_arrive(&bars->ds_full);
             // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
             if (grp == 0 && tok >= 0) {
-                ws_delta[static_cast<int64_t>(tok) * H + h] = delta;
+                ws_delta[static_cast<int64_t>(h) * P.n + td.x + r] = delta;
                 const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
                 const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
                 const uint32_t kmap = P.rowkmap[td.x + r];
@@ -362,14 +362,15 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
 // ============================================================================ dK / dV
 namespace {
 struct DkvBars {
-    uint64_t full[2], empty[2], kv_full, s_full, pds_full, pds_free, acc_full, acc_free, drain;
+    uint64_t full[3], empty[3], kv_full, s_full, pds_full, pds_free, acc_full, acc_free, drain;
     uint32_t tmem_base;
     int abort;
 };
 constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
 constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
 constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
-constexpr uint32_t kDkvSmem = 2 * kKvTile + 2 * kDkvStage + 2 * (kBS * kTM * 2) + 2 * kMetaBytes + 1024 + 1024;
+constexpr int kDkvStages = 3;
+constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + 2 * (kBS * kTM * 2) + kDkvStages * kMetaBytes + 1024 + 1024;
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -383,18 +384,18 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
     const uint32_t sK = base, sV = base + kKvTile;
-    const uint32_t sStage = base + 2 * kKvTile;                  // [2][Q | dO]
-    const uint32_t sPT = sStage + 2 * kDkvStage;                 // P^T  [128 slots x 128 tokens]
+    const uint32_t sStage = base + 2 * kKvTile;                  // [3][Q | dO]
+    const uint32_t sPT = sStage + kDkvStages * kDkvStage;        // P^T  [128 slots x 128 tokens]
     const uint32_t sDS = sPT + kBS * kTM * 2;                    // dS^T
-    float *meta = reinterpret_cast<float *>(sbase + (sDS + kBS * kTM * 2 - base));   // [2][3][128]
-    DkvBars *bars = reinterpret_cast<DkvBars *>(reinterpret_cast<unsigned char *>(meta) + 2 * kMetaBytes);
+    float *meta = reinterpret_cast<float *>(sbase + (sDS + kBS * kTM * 2 - base));   // [3][3][128]
+    DkvBars *bars = reinterpret_cast<DkvBars *>(reinterpret_cast<unsigned char *>(meta) + kDkvStages * kMetaBytes);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t ld = static_cast<int64_t>(H) * kHD;
     const int nitems = nb * H * nsplit;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kDkvStages; ++s) {
             tc::mbar_init(&bars->full[s], 33);
             tc::mbar_init(&bars->empty[s], 1);
         }
@@ -441,7 +442,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             ++nkv;
             const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
             for (int t = 0; t < nt; ++t, ++g) {
-                const int s = g & 1, j = g >> 1;
+                const int s = g % kDkvStages, j = g / kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
                 const int tile = list[split + t * nsplit];
                 const int4 td = P.tiles[tile];
@@ -452,12 +453,14 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 int rows[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
+                    // lse and delta are stored in plan-row order: no dependence on perm
                     const int rr = lane * 4 + u;
-                    const int tok = rr < td.y ? P.perm[td.x + rr] : -1;
-                    rows[u] = tok >= 0 ? tok : 0;
-                    mb[rr] = tok >= 0 ? P.rowbias[static_cast<int64_t>(td.x + rr) * top + jb] * kLog2e : 0.0f;
-                    mb[kTM + rr] = tok >= 0 ? lse[static_cast<int64_t>(tok) * H + h] * kLog2e : INFINITY;
-                    mb[2 * kTM + rr] = tok >= 0 ? ws_delta[static_cast<int64_t>(tok) * H + h] : 0.0f;
+                    const bool ok = rr < td.y;
+                    const int64_t prow = static_cast<int64_t>(h) * P.n + td.x + rr;
+                    rows[u] = ok ? P.perm[td.x + rr] : 0;
+                    mb[rr] = ok ? P.rowbias[static_cast<int64_t>(td.x + rr) * top + jb] * kLog2e : 0.0f;
+                    mb[kTM + rr] = ok ? lse[prow] * kLog2e : INFINITY;
+                    mb[2 * kTM + rr] = ok ? ws_delta[prow] : 0.0f;
                 }
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
                 if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
@@ -469,7 +472,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             }
             if (*abort_flag) break;
         }
-        if (last >= 0) tc::mbar_wait_warp(&bars->full[last & 1], (last >> 1) & 1, P.err, 2, abort_flag);
+        if (last >= 0) tc::mbar_wait_warp(&bars->full[last % kDkvStages], (last / kDkvStages) & 1, P.err, 2, abort_flag);
         if (nkv > 0) tc::mbar_wait_warp(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -486,7 +489,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             ++nkv;
             for (int t = 0; t < nt; ++t, ++g) {
-                const int s = g & 1, j = g >> 1;
+                const int s = g % kDkvStages, j = g / kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
@@ -539,12 +542,12 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             const int nt = item_ntile(item);
             if (nt == 0) continue;
             for (int t = 0; t < nt; ++t, ++g) {
-                const int s = g & 1;
+                const int s = g % kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->s_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 // the smem P^T / dS^T of the previous tile must have been consumed
                 if (g > 0 && !tc::mbar_wait_warp(&bars->pds_free, (g - 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 // the loader's per-token metadata of this stage (acquire it directly)
-                if (!tc::mbar_wait_warp(&bars->full[s], (g >> 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                if (!tc::mbar_wait_warp(&bars->full[s], (g / kDkvStages) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 tc::tc_fence_after();
                 const float *mb = meta + s * 3 * kTM;
 #pragma unroll
@@ -636,7 +639,7 @@ cudaError_t launch_read_bwd_tc(const void *q, const void *k, const void *v, cons
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDkvSmem);
     if (e != cudaSuccess) return e;
-    const int nsplit = std::max(1, std::min(16, (4 * sms + nb * H - 1) / (nb * H)));
+    const int nsplit = std::max(1, std::min(16, (2 * sms + nb * H - 1) / (nb * H)));
     const int items2 = nb * H * nsplit;
     read_bwd_dkdv_tc_kernel<<<std::min(items2, sms), kThreads, kDkvSmem, st>>>(
         mk, mv, mq, md, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2, P,

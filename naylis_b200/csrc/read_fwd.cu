@@ -199,8 +199,8 @@ read_fwd_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
     if ((lane & 3) == 0) {
         const int r0 = warp * 16 + g;
         const int t0 = sTok[r0], t1 = sTok[r0 + 8];
-        if (t0 >= 0) lse[static_cast<int64_t>(t0) * H + h] = l_r[0] > 0.0f ? (m_r[0] + log2f(l_r[0])) * kLn2 : -INFINITY;
-        if (t1 >= 0) lse[static_cast<int64_t>(t1) * H + h] = l_r[1] > 0.0f ? (m_r[1] + log2f(l_r[1])) * kLn2 : -INFINITY;
+        if (t0 >= 0) lse[static_cast<int64_t>(h) * P.n + row0 + r0] = l_r[0] > 0.0f ? (m_r[0] + log2f(l_r[0])) * kLn2 : -INFINITY;
+        if (t1 >= 0) lse[static_cast<int64_t>(h) * P.n + row0 + r0 + 8] = l_r[1] > 0.0f ? (m_r[1] + log2f(l_r[1])) * kLn2 : -INFINITY;
     }
     __syncthreads();
     for (int i = tid; i < kTileM * kChunks; i += kReadThreads) {

@@ -207,7 +207,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const int bar_id = 1 + quarter;
-        int prev_tok = -1, prev_h = 0;
+        int prev_tok = -1, prev_h = 0, prev_row = 0;
         float prev_m = 0.0f;
         float prev_l = 0.0f;
         auto epilogue = [&](int i) {
@@ -234,12 +234,12 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 dst[0] = v0;
                 dst[1] = v1;
                 if (grp == 0)
-                    lse[static_cast<int64_t>(prev_tok) * H + prev_h] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
+                    lse[static_cast<int64_t>(prev_h) * P.n + prev_row] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
             }
         };
         // per-item row metadata, fetched one item ahead so that its global-load
         // latency hides behind the current item's softmax
-        struct Meta { int h, nblk, tok; float bias; };
+        struct Meta { int h, nblk, tok, row; float bias; };
         auto fetch = [&](int item, Meta &m) {
             const int tile = item / H;
             m.h = item % H;
@@ -248,6 +248,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             m.nblk = 0;
             while (m.nblk < top && set[m.nblk] >= 0) ++m.nblk;
             m.tok = r < td.y ? P.perm[td.x + r] : -1;
+            m.row = td.x + r;
             m.bias = (m.tok >= 0 && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e : 0.0f;
         };
         Meta cur, nxt;
@@ -325,6 +326,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (i > 0) epilogue(i - 1);
             prev_tok = tok;
             prev_h = h;
+            prev_row = cur.row;
             prev_m = m;
             cur = nxt;
             count = i + 1;

@@ -1,0 +1,111 @@
+// ReZero output scale of the MoM layer, fused: model.py:239 (`self.mom_scale * out`).
+//
+// Under autocast `out` (the o_proj result) is bf16 and mom_scale a (1,) fp32
+// parameter, so the product is fp32. Forward: y = s * o (one pass). Backward:
+// d_o = s * g rounded to o's dtype and d_s = sum(g * o), in one pass over g
+// and o instead of the mul / cast / mul / reduce kernels autograd would run.
+#include "common.cuh"
+#include "launch.h"
+
+namespace mom {
+
+template <int ODT>
+__global__ void __launch_bounds__(256)
+scale_fwd_kernel(const typename Elem<ODT>::T *__restrict__ o, const float *__restrict__ scale, int64_t n,
+                 float *__restrict__ y) {
+    const float s = *scale;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float4 v;
+        if (ODT == MOM_BF16) {
+            const uint2 raw = reinterpret_cast<const uint2 *>(o)[i];
+            v = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xFFFF0000u),
+                            __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xFFFF0000u));
+        } else {
+            v = reinterpret_cast<const float4 *>(o)[i];
+        }
+        reinterpret_cast<float4 *>(y)[i] = make_float4(s * v.x, s * v.y, s * v.z, s * v.w);
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = s * Elem<ODT>::load(o, i);
+}
+
+template <int ODT, int GDT>
+__global__ void __launch_bounds__(256)
+scale_bwd_kernel(const typename Elem<GDT>::T *__restrict__ g, const typename Elem<ODT>::T *__restrict__ o,
+                 const float *__restrict__ scale, int64_t n, typename Elem<ODT>::T *__restrict__ d_o,
+                 float *__restrict__ d_scale) {
+    const float s = *scale;
+    float acc = 0.0f;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float gv[4], ov[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            gv[k] = Elem<GDT>::load(g, 4 * i + k);
+            ov[k] = Elem<ODT>::load(o, 4 * i + k);
+            acc = fmaf(gv[k], ov[k], acc);
+        }
+        if (ODT == MOM_BF16) {
+            uint2 w;
+            w.x = pack_bf16x2(s * gv[0], s * gv[1]);
+            w.y = pack_bf16x2(s * gv[2], s * gv[3]);
+            reinterpret_cast<uint2 *>(d_o)[i] = w;
+        } else {
+            reinterpret_cast<float4 *>(d_o)[i] = make_float4(s * gv[0], s * gv[1], s * gv[2], s * gv[3]);
+        }
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float gv = Elem<GDT>::load(g, i), ov = Elem<ODT>::load(o, i);
+        acc = fmaf(gv, ov, acc);
+        Elem<ODT>::store(d_o, i, s * gv);
+    }
+    __shared__ float red[8];
+    acc = warp_sum(acc);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) atomicAdd(d_scale, v);
+    }
+}
+
+static int scale_grid(int64_t n) {
+    const int64_t want = (n / 4 + 255) / 256;
+    return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 148 * 8)));
+}
+
+cudaError_t launch_scale_fwd(const void *o, int odt, const float *scale, int64_t n, float *y, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    if (odt == MOM_BF16)
+        scale_fwd_kernel<MOM_BF16><<<scale_grid(n), 256, 0, st>>>(static_cast<const uint16_t *>(o), scale, n, y);
+    else
+        scale_fwd_kernel<MOM_F32><<<scale_grid(n), 256, 0, st>>>(static_cast<const float *>(o), scale, n, y);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, const float *scale, int64_t n,
+                             void *d_o, float *d_scale, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(d_scale, 0, sizeof(float), st);
+    if (e != cudaSuccess || n == 0) return e;
+#define MOM_SB(O, G)                                                                                   \
+    if (odt == O && gdt == G)                                                                          \
+        scale_bwd_kernel<O, G><<<scale_grid(n), 256, 0, st>>>(                                         \
+            static_cast<const typename Elem<G>::T *>(g), static_cast<const typename Elem<O>::T *>(o), scale, \
+            n, static_cast<typename Elem<O>::T *>(d_o), d_scale);
+    MOM_SB(MOM_BF16, MOM_F32)
+    MOM_SB(MOM_BF16, MOM_BF16)
+    MOM_SB(MOM_F32, MOM_F32)
+    MOM_SB(MOM_F32, MOM_BF16)
+#undef MOM_SB
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mom

@@ -121,6 +121,8 @@ class MoMLayer(nn.Module):
                 use_reentrant=False, preserve_rng_state=False)
         else:
             out = self._read(x, top_idx, top_gates, M_blocks, mode)
+        if mode is not None and torch.result_type(self.mom_scale, out) == torch.float32:
+            return mom_kernels.mom_scale(out, self.mom_scale)
         return self.mom_scale * out
 
     def _read(self, x, top_idx, top_gates, M_blocks, mode=None):

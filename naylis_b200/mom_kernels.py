@@ -270,6 +270,43 @@ def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=Non
     return _MomRouteFunction.apply(x, w_down, w_up, noise, int(top_blocks), cd, scan_mode)
 
 
+class _MomScaleFunction(torch.autograd.Function):
+    """y = mom_scale * o with the reference's dtype promotion (model.py:239):
+    fp32 result from a bf16 o; the backward is one fused pass."""
+
+    @staticmethod
+    def forward(ctx, o, scale):
+        oc = o.contiguous()
+        sc = scale.detach().to(torch.float32).contiguous()
+        y = torch.empty(oc.shape, dtype=torch.float32, device=oc.device)
+        _lib.call("mom_scale_fwd", oc.data_ptr(), _dt_code(oc.dtype), oc.numel(), sc.data_ptr(),
+                  y.data_ptr(), _stream(oc.device))
+        ctx.save_for_backward(oc, sc)
+        ctx.scale_dtype = scale.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        oc, sc = ctx.saved_tensors
+        if g.dtype not in (torch.float32, torch.bfloat16):
+            g = g.float()
+        g = g.contiguous()
+        d_o = torch.empty_like(oc)
+        d_s = torch.empty(1, dtype=torch.float32, device=oc.device)
+        _lib.call("mom_scale_bwd", g.data_ptr(), _dt_code(g.dtype), oc.data_ptr(), _dt_code(oc.dtype),
+                  oc.numel(), sc.data_ptr(), d_o.data_ptr(), d_s.data_ptr(), _stream(oc.device))
+        return d_o, d_s.to(ctx.scale_dtype)
+
+
+def mom_scale(o, scale):
+    """``scale * o`` for the layer output (scale: the (1,) mom_scale parameter)."""
+    if not o.is_cuda:
+        raise RuntimeError("sm100 mom_scale: o must be on a CUDA device")
+    if scale.numel() != 1:
+        raise RuntimeError("sm100 mom_scale: scale must hold one element")
+    return _MomScaleFunction.apply(o, scale)
+
+
 def gumbel_noise(shape, device, noise_scale: float):
     """Scaled Gumbel noise drawn exactly as the reference draws it
     (model.py:209-213: torch.rand_like on the fp32 logits)."""
@@ -277,4 +314,5 @@ def gumbel_noise(shape, device, noise_scale: float):
     return noise_scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
 
 
-__all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "gumbel_noise"]
+__all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "mom_scale",
+           "gumbel_noise"]

@@ -103,3 +103,24 @@ def test_resolve_mode_contract_on_gpu():
     with pytest.raises(RuntimeError):
         mk.resolve_mode("cuda", torch.bfloat16, head_dim=96)
     assert mk.preflight("cuda") is None
+
+
+@pytest.mark.parametrize("g_dtype", [torch.float32, torch.bfloat16])
+def test_fused_output_scale_matches_torch(g_dtype):
+    """mom_scale (model.py:239 fused): fp32 y = s * o from bf16 o; backward
+    d_o = s * g in bf16 and d_s = sum(g * o), against torch's own mul."""
+    from naylis_b200 import mom_kernels as mk
+    torch.manual_seed(0)
+    dev = torch.device("cuda")
+    o = torch.randn(3, 257, 64, device=dev).to(torch.bfloat16).requires_grad_(True)
+    s = torch.tensor([0.37], device=dev, requires_grad=True)
+    g = torch.randn(3, 257, 64, device=dev).to(g_dtype)
+    y = mk.mom_scale(o, s)
+    y.backward(g)
+    o2 = o.detach().clone().requires_grad_(True)
+    s2 = s.detach().clone().requires_grad_(True)
+    y2 = s2 * o2
+    y2.backward(g.float())
+    assert y.dtype == torch.float32 and torch.equal(y, y2)
+    assert torch.equal(o.grad, o2.grad)
+    assert abs(float(s.grad) - float(s2.grad)) <= 1e-5 * abs(float(s2.grad))
