@@ -100,7 +100,7 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
 // sequential loop produces. The kernel checks that certificate per column and
 // walks the column sequentially when it fails (tiny or huge dynamic range).
 //
-// CTA = 32 columns x 32 chunks of the sequence (1024 threads):
+// CTA = 64 columns (32 pairs) x 32 chunks of the sequence (1024 threads):
 //   phase 1  chunk sums, sums of |x| and min ulp exponent
 //   phase 2  per column: exclusive scan of the chunk sums, certificate
 //   phase 3  each chunk re-walks its rows from its carry and writes h.
@@ -111,67 +111,106 @@ __device__ __forceinline__ int ulp_exponent(float v) {
     return (e == 0 ? 1 : e) - 127 - (XDT == MOM_BF16 ? 7 : 23);
 }
 
+// Two adjacent columns per thread (one 4-byte bf16 pair or 8-byte fp32 pair per
+// row) and 16 rows in flight per thread: the certificate pass and the output
+// pass are each one streaming read of the CTA's 64 columns.
+template <int XDT> struct Pair;
+template <> struct Pair<MOM_BF16> {
+    static __device__ __forceinline__ float2 load(const uint16_t *p) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    }
+};
+template <> struct Pair<MOM_F32> {
+    static __device__ __forceinline__ float2 load(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+};
+template <int CDT> struct PairStore;
+template <> struct PairStore<MOM_BF16> {
+    static __device__ __forceinline__ void store(uint16_t *p, float a, float b) {
+        *reinterpret_cast<uint32_t *>(p) = pack_bf16x2(a, b);
+    }
+};
+template <> struct PairStore<MOM_F32> {
+    static __device__ __forceinline__ void store(float *p, float a, float b) {
+        *reinterpret_cast<float2 *>(p) = make_float2(a, b);
+    }
+};
+
 template <int XDT, int CDT>
 __global__ void __launch_bounds__(1024)
 route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem<CDT>::T *__restrict__ hq,
                       int S, int d) {
-    __shared__ double s_sum[32][33];
-    __shared__ double s_abs[32][33];
-    __shared__ int s_emin[32][33];
-    __shared__ int s_cert[32];
-    const int c = threadIdx.x & 31, k = threadIdx.x >> 5;
+    __shared__ double s_sum[64][33];
+    __shared__ double s_abs[64][33];
+    __shared__ int s_emin[64][33];
+    __shared__ int s_cert[64];
+    const int c2 = threadIdx.x & 31, k = threadIdx.x >> 5;    // column pair, chunk
     const int b = blockIdx.y;
-    const int col = blockIdx.x * 32 + c;
+    const int col = blockIdx.x * 64 + 2 * c2;
     const int len = (S + 31) / 32;
     const int t0 = k * len, t1 = min(S, t0 + len);
     const typename Elem<XDT>::T *xc = x + static_cast<int64_t>(b) * S * d + col;
     typename Elem<CDT>::T *hc = hq + static_cast<int64_t>(b) * S * d + col;
-    const bool live = col < d;
-    double sum = 0.0, asum = 0.0;
-    int emin = 1 << 20;
+    const bool live = col < d;                                   // d % 8 == 0: pairs are whole
+    double sum0 = 0.0, sum1 = 0.0, as0 = 0.0, as1 = 0.0;
+    int em0 = 1 << 20, em1 = 1 << 20;
     if (live) {
-#pragma unroll 4
+#pragma unroll 16
         for (int t = t0; t < t1; ++t) {
-            const float v = Elem<XDT>::load(xc, static_cast<int64_t>(t) * d);
-            sum = __dadd_rn(sum, static_cast<double>(v));
-            asum = __dadd_rn(asum, static_cast<double>(fabsf(v)));
-            if (v != 0.0f) emin = min(emin, ulp_exponent<XDT>(v));
+            const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
+            sum0 = __dadd_rn(sum0, static_cast<double>(v.x));
+            sum1 = __dadd_rn(sum1, static_cast<double>(v.y));
+            as0 = __dadd_rn(as0, static_cast<double>(fabsf(v.x)));
+            as1 = __dadd_rn(as1, static_cast<double>(fabsf(v.y)));
+            if (v.x != 0.0f) em0 = min(em0, ulp_exponent<XDT>(v.x));
+            if (v.y != 0.0f) em1 = min(em1, ulp_exponent<XDT>(v.y));
         }
     }
-    s_sum[c][k] = sum;
-    s_abs[c][k] = asum;
-    s_emin[c][k] = emin;
+    s_sum[2 * c2][k] = sum0;
+    s_sum[2 * c2 + 1][k] = sum1;
+    s_abs[2 * c2][k] = as0;
+    s_abs[2 * c2 + 1][k] = as1;
+    s_emin[2 * c2][k] = em0;
+    s_emin[2 * c2 + 1][k] = em1;
     __syncthreads();
-    if (k == 0) {
+    if (threadIdx.x < 64) {                                      // one thread per column
+        const int cc = threadIdx.x;
         double run = 0.0, at = 0.0;
         int em = 1 << 20;
         for (int kk = 0; kk < 32; ++kk) {
-            const double v = s_sum[c][kk];
-            s_sum[c][kk] = run;
+            const double v = s_sum[cc][kk];
+            s_sum[cc][kk] = run;
             run = __dadd_rn(run, v);
-            at = __dadd_rn(at, s_abs[c][kk]);
-            em = min(em, s_emin[c][kk]);
+            at = __dadd_rn(at, s_abs[cc][kk]);
+            em = min(em, s_emin[cc][kk]);
         }
         // all zero -> trivially exact; else A < 2^(52 + e_min)
-        s_cert[c] = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
+        s_cert[cc] = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
     }
     __syncthreads();
     if (!live) return;
-    if (s_cert[c]) {
-        double run = s_sum[c][k];
-#pragma unroll 4
+    const bool ok0 = s_cert[2 * c2], ok1 = s_cert[2 * c2 + 1];
+    if (ok0 && ok1) {
+        double r0 = s_sum[2 * c2][k], r1 = s_sum[2 * c2 + 1][k];
+#pragma unroll 16
         for (int t = t0; t < t1; ++t) {
-            const float v = Elem<XDT>::load(xc, static_cast<int64_t>(t) * d);
-            run = __dadd_rn(run, static_cast<double>(v));
-            const float h = __fdiv_rn(__double2float_rn(run), static_cast<float>(t + 1));
-            Elem<CDT>::store(hc, static_cast<int64_t>(t) * d, h);
+            const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
+            r0 = __dadd_rn(r0, static_cast<double>(v.x));
+            r1 = __dadd_rn(r1, static_cast<double>(v.y));
+            const float den = static_cast<float>(t + 1);
+            PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, __fdiv_rn(__double2float_rn(r0), den),
+                                  __fdiv_rn(__double2float_rn(r1), den));
         }
     } else if (k == 0) {
-        double acc = 0.0;
+        // a certificate failed: both columns of the pair walk sequentially
+        double a0 = 0.0, a1 = 0.0;
         for (int t = 0; t < S; ++t) {
-            acc = __dadd_rn(acc, static_cast<double>(Elem<XDT>::load(xc, static_cast<int64_t>(t) * d)));
-            const float h = __fdiv_rn(__double2float_rn(acc), static_cast<float>(t + 1));
-            Elem<CDT>::store(hc, static_cast<int64_t>(t) * d, h);
+            const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
+            a0 = __dadd_rn(a0, static_cast<double>(v.x));
+            a1 = __dadd_rn(a1, static_cast<double>(v.y));
+            const float den = static_cast<float>(t + 1);
+            PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, __fdiv_rn(__double2float_rn(a0), den),
+                                  __fdiv_rn(__double2float_rn(a1), den));
         }
     }
 }
@@ -401,7 +440,7 @@ static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, c
 
 template <int XDT, int CDT>
 static cudaError_t launch_scan_par_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
-    dim3 grid((d + 31) / 32, B);
+    dim3 grid((d + 63) / 64, B);
     route_scan_par_kernel<XDT, CDT><<<grid, 1024, 0, st>>>(static_cast<const typename Elem<XDT>::T *>(x),
                                                           static_cast<typename Elem<CDT>::T *>(hq), S, d);
     count_launch();

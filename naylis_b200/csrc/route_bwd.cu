@@ -92,27 +92,30 @@ __global__ void route_bwd_token_kernel(int64_t ntok, int r, int nb, int top,
 }
 
 // ---------------------------------------------------------------- reverse scan
-// CTA = 32 columns x 32 chunks of the sequence (1024 threads) of one batch row.
+// CTA = 8 columns x 128 chunks of the sequence (1024 threads) of one batch row.
 // Phase 1: chunk sums; phase 2: suffix scan of the chunk sums per column;
 // phase 3: each thread walks its chunk backwards from its carry.
+constexpr int kRsCols = 8, kRsChunks = 128;
 __global__ void __launch_bounds__(1024)
 route_bwd_revscan_kernel(const float *__restrict__ dz, float *__restrict__ u, int S, int r) {
-    __shared__ float s_tot[32][33];
-    const int c = threadIdx.x & 31, k = threadIdx.x >> 5;
+    __shared__ float s_tot[kRsCols][kRsChunks + 1];
+    const int c = threadIdx.x % kRsCols, k = threadIdx.x / kRsCols;
     const int b = blockIdx.y;
-    const int j = blockIdx.x * 32 + c;
-    const int len = (S + 31) / 32;
+    const int j = blockIdx.x * kRsCols + c;
+    const int len = (S + kRsChunks - 1) / kRsChunks;
     const int t0 = k * len, t1 = min(S, t0 + len);
     const float *src = dz + static_cast<int64_t>(b) * S * r + j;
     float *dst = u + static_cast<int64_t>(b) * S * r + j;
     float acc = 0.0f;
-    if (j < r)
+    if (j < r) {
+#pragma unroll 8
         for (int t = t0; t < t1; ++t) acc += src[static_cast<int64_t>(t) * r] / static_cast<float>(t + 1);
+    }
     s_tot[c][k] = acc;
     __syncthreads();
-    if (k == 0) {   // suffix scan over the 32 chunks of column c
+    if (k == 0) {   // suffix scan over the chunks of column c
         float run = 0.0f;
-        for (int kk = 31; kk >= 0; --kk) {
+        for (int kk = kRsChunks - 1; kk >= 0; --kk) {
             const float v = s_tot[c][kk];
             s_tot[c][kk] = run;   // exclusive: sum of the chunks after kk
             run += v;
@@ -121,6 +124,7 @@ route_bwd_revscan_kernel(const float *__restrict__ dz, float *__restrict__ u, in
     __syncthreads();
     if (j >= r) return;
     float run = s_tot[c][k];
+#pragma unroll 8
     for (int t = t1 - 1; t >= t0; --t) {
         run += src[static_cast<int64_t>(t) * r] / static_cast<float>(t + 1);
         dst[static_cast<int64_t>(t) * r] = run;
@@ -142,9 +146,11 @@ route_bwd_dx_mma_kernel(const float *__restrict__ u, const uint16_t *__restrict_
     constexpr int kTok = 64, kCols = 128;
     constexpr int kUStride = R * 2 + 16;        // bytes per token row (padded)
     constexpr int kWStride = kCols * 2 + 16;    // bytes per rank row (padded)
-    __shared__ __align__(16) unsigned char sUh[kTok * kUStride];
-    __shared__ __align__(16) unsigned char sUl[kTok * kUStride];
-    __shared__ __align__(16) unsigned char sW[R * kWStride];
+    // one buffer: [u hi | u lo | Wd] while computing, the fp32 output tile after
+    __shared__ __align__(16) unsigned char sBuf[2 * kTok * kUStride + R * kWStride];
+    unsigned char *sUh = sBuf;
+    unsigned char *sUl = sBuf + kTok * kUStride;
+    unsigned char *sW = sBuf + 2 * kTok * kUStride;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kTok;
     const int c0 = blockIdx.y * kCols;
@@ -186,24 +192,48 @@ route_bwd_dx_mma_kernel(const float *__restrict__ u, const uint16_t *__restrict_
             mma_bf16_16816(acc[2 * p + 1], al, bfr[2], bfr[3]);
         }
     }
+    // stage the fp32 tile in shared memory (reusing the operand buffers), 64
+    // columns at a time, then write whole 16-B vectors of dx
+    float *sOut = reinterpret_cast<float *>(sBuf);               // [kTok][kHalf + 4] fp32
+    constexpr int kHalf = kCols / 2, kOS = kHalf + 4;
+    static_assert(kTok * kOS * 4 <= 2 * kTok * kUStride + R * kWStride, "staging buffer");
     const int g = lane >> 2, q2 = (lane & 3) * 2;
 #pragma unroll
-    for (int n = 0; n < kCols / 8; ++n) {
-        const int c = c0 + n * 8 + q2;
-        if (c >= d) continue;
+    for (int half = 0; half < 2; ++half) {
+        __syncthreads();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int64_t t = tok0 + warp * 16 + g + h * 8;
-            if (t >= ntok) continue;
-            float v0 = acc[n][2 * h], v1 = acc[n][2 * h + 1];
-            if (accumulate) {
-                v0 += Elem<DXDT>::load(dx, t * d + c);
-                v1 += Elem<DXDT>::load(dx, t * d + c + 1);
+        for (int n = 0; n < kHalf / 8; ++n)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int row = warp * 16 + g + h * 8;
+                sOut[row * kOS + n * 8 + q2] = acc[half * (kHalf / 8) + n][2 * h];
+                sOut[row * kOS + n * 8 + q2 + 1] = acc[half * (kHalf / 8) + n][2 * h + 1];
             }
+        __syncthreads();
+        for (int i = threadIdx.x; i < kTok * (kHalf / 4); i += 128) {
+            const int row = i / (kHalf / 4), c4 = (i % (kHalf / 4)) * 4;
+            const int64_t t = tok0 + row;
+            const int c = c0 + half * kHalf + c4;
+            if (t >= ntok || c >= d) continue;
+            float v[4] = {sOut[row * kOS + c4], sOut[row * kOS + c4 + 1], sOut[row * kOS + c4 + 2],
+                          sOut[row * kOS + c4 + 3]};
             if (DXDT == MOM_BF16) {
-                *reinterpret_cast<uint32_t *>(reinterpret_cast<uint16_t *>(dx) + t * d + c) = pack_bf16x2(v0, v1);
+                uint2 *p = reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(dx) + t * d + c);
+                if (accumulate) {
+                    const uint2 o = *p;
+                    v[0] += __uint_as_float(o.x << 16);
+                    v[1] += __uint_as_float(o.x & 0xFFFF0000u);
+                    v[2] += __uint_as_float(o.y << 16);
+                    v[3] += __uint_as_float(o.y & 0xFFFF0000u);
+                }
+                *p = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
             } else {
-                *reinterpret_cast<float2 *>(reinterpret_cast<float *>(dx) + t * d + c) = make_float2(v0, v1);
+                float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(dx) + t * d + c);
+                if (accumulate) {
+                    const float4 o = *p;
+                    v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
+                }
+                *p = make_float4(v[0], v[1], v[2], v[3]);
             }
         }
     }
@@ -426,10 +456,12 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
         count_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
-    route_bwd_revscan_kernel<<<dim3((r + 31) / 32, B), 1024, 0, st>>>(ws_dz, ws_u, S, r);
+    route_bwd_revscan_kernel<<<dim3((r + kRsCols - 1) / kRsCols, B), 1024, 0, st>>>(ws_dz, ws_u, S, r);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const bool tc = cdt == MOM_BF16 && (r == 32 || r == 64) && d % 8 == 0;
+    // the tensor-core pair stores dx and reads x in 16-B vectors
+    const bool tc = cdt == MOM_BF16 && (r == 32 || r == 64) && d % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     if (tc) {
         dim3 grid(static_cast<unsigned>((ntok + 63) / 64), (d + 127) / 128);
 #define MOM_DX_TC(R, X)                                                                              \
