@@ -141,6 +141,22 @@ MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void
                  const void *plan, void *dq, float *dk_acc, float *dv_acc,
                  float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream);
 
+/* mom_read_bwd without a workspace argument: for callers that cannot allocate
+ * device memory (a plugin whose host framework's caching allocator owns the
+ * device, or an FFI caller with no device allocator). It has no counterpart
+ * in the reference. The delta scratch is a fixed 4 MiB device array
+ * inside the library (mom_read_bwd_noalloc_max_bytes()), so B*S*H may be at
+ * most 1,048,576; larger calls return MOM_ERR_WORKSPACE. It calls no
+ * cudaMalloc/cudaFree. Its first call on a device looks the array's address
+ * up (make that call before any stream capture). All calls share the array:
+ * calls that overlap on the GPU race. Arguments and results as mom_read_bwd. */
+MOM_API size_t mom_read_bwd_noalloc_max_bytes(void);
+MOM_API int mom_read_bwd_noalloc(const void *q, const void *k, const void *v, const void *out,
+                                 const void *dout, const float *lse, int dtype, int64_t B,
+                                 int64_t S, int64_t H, int64_t head_dim, int64_t num_blocks,
+                                 int64_t block_size, int64_t top, const void *plan, void *dq,
+                                 float *dk_acc, float *dv_acc, float *dlog_gates, void *stream);
+
 /* ------------------------------------------------------------------ output scale
  * ReZero output scale of the layer, fused: y = scale[0] * o with y in fp32
  * (model.py:239, `self.mom_scale * out`: a (1,) fp32 parameter times the bf16

@@ -49,6 +49,9 @@ SIGNATURES = {
     "mom_read_bwd_workspace_size": (_sz, [_i64, _i64, _i64]),
     "mom_read_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                             _i64, _i64, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
+    "mom_read_bwd_noalloc_max_bytes": (_sz, []),
+    "mom_read_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
+                                    _i64, _i64, _vp, _vp, _fp, _fp, _fp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -339,4 +339,67 @@ int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, c
     return MOM_OK;
 }
 
+// ------------------------------------------------- read backward, no allocation
+// mom_read_bwd_noalloc runs mom_read_bwd with its workspace (the per-row delta,
+// H x B*S fp32) in a fixed device array of this library instead of caller
+// memory. It is for callers that cannot allocate device memory: a plugin
+// handed its tensors by a framework whose caching allocator has reserved the
+// device (a cudaMalloc of its own would fail or sit outside that pool), or a C
+// caller over FFI with no device allocator at all.
+//
+// The array is kNoAllocScratchBytes (4 MiB) and lives in every device's copy
+// of this library's code, from when the CUDA runtime loads it on that device
+// until the process exits. In host code `g_read_bwd_scratch` only names the
+// symbol; its device address comes from cudaGetSymbolAddress, looked up once
+// per device with that device current, on the first call made on it (make
+// that first call before any stream capture). All calls share the one array
+// and it keeps the last call's contents; nothing in it has to start at zero
+// (the dQ pass writes every delta entry that the dK/dV pass reads), but calls
+// that overlap on the GPU (two streams, or two threads) race on it.
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
+constexpr int kNoAllocMaxDevices = 64;
+__device__ __align__(256) unsigned char g_read_bwd_scratch[kNoAllocScratchBytes];
+
+int noalloc_scratch(void **ptr) {
+    static std::mutex mu;
+    static void *addr[kNoAllocMaxDevices] = {};
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= kNoAllocMaxDevices)
+        return fail(MOM_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        if ((e = cudaGetSymbolAddress(&p, g_read_bwd_scratch)) != cudaSuccess)
+            return cuda_fail(e, "cudaGetSymbolAddress(read bwd scratch)");
+        addr[dev] = p;
+    }
+    *ptr = addr[dev];
+    return MOM_OK;
+}
+}  // namespace
+
+size_t mom_read_bwd_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
+
+int mom_read_bwd_noalloc(const void *q, const void *k, const void *v, const void *out, const void *dout,
+                         const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd,
+                         int64_t nb, int64_t bs, int64_t top, const void *plan, void *dq, float *dk_acc,
+                         float *dv_acc, float *dlog_gates, void *stream) {
+    int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    const size_t need = mom_read_bwd_workspace_size(B, S, H);
+    if (need > kNoAllocScratchBytes)
+        return fail(MOM_ERR_WORKSPACE,
+                    "mom_read_bwd_noalloc: B*S*H = %lld needs %zu bytes of scratch, over its fixed %zu "
+                    "(at most %zu tokens x heads); use mom_read_bwd with a caller workspace",
+                    (long long)(B * S * H), need, kNoAllocScratchBytes, kNoAllocScratchBytes / 4);
+    if ((rc = check_current_device())) return rc;
+    void *scratch = nullptr;
+    if ((rc = noalloc_scratch(&scratch))) return rc;
+    return mom_read_bwd(q, k, v, out, dout, lse, dtype, B, S, H, hd, nb, bs, top, plan, dq, dk_acc, dv_acc,
+                        dlog_gates, scratch, kNoAllocScratchBytes, stream);
+}
+
 }  // extern "C"
