@@ -146,10 +146,14 @@ def run_gpu(args):
     holder = torch.nn.Module()
     holder.layer = layer
     holder.M = M
-    dp = GradAllReduce(holder) if world > 1 else None
+    use_graph = not args.no_graph
+    # under a CUDA graph the bucket all-reduces run after each replay (no
+    # collective inside the captured backward)
+    dp = GradAllReduce(holder, overlap=not use_graph) if world > 1 else None
     mk.resolve_mode(dev, torch.bfloat16, head_dim=c["d"] // c["H"])
+    lib = _lib.load()
 
-    def step(xin, gin):
+    def body(xin, gin):
         if dp is not None:
             dp.zero_grad()
         else:
@@ -159,8 +163,35 @@ def run_gpu(args):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             out = layer(xin, M)
         out.backward(gin)
+
+    def step(xin, gin):
+        body(xin, gin)
         if dp is not None:
             dp.finish()
+
+    graph = None
+    launches_per_replay = None
+    if use_graph:
+        # the whole step (zero grads, forward, backward) as one CUDA graph over
+        # static x / dout; warm-up on a side stream first, as capture requires
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                body(x, dout)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        l0 = lib.mom_kernel_launches()
+        with torch.cuda.graph(graph):
+            body(x, dout)
+        launches_per_replay = lib.mom_kernel_launches() - l0
+
+        def step(xin, gin):
+            assert xin is x and gin is dout, "the graphed step reads the static x / dout"
+            graph.replay()
+            if dp is not None:
+                dp.finish()
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 256 MiB > L2
     for _ in range(args.warmup):
@@ -171,7 +202,6 @@ def run_gpu(args):
     if clocks:
         clocks.start()
         time.sleep(0.5)
-    lib = _lib.load()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     if world > 1:
@@ -189,6 +219,10 @@ def run_gpu(args):
         dist.barrier()
     t_wall1 = time.time()
     launches = lib.mom_kernel_launches() - launches0
+    if graph is not None:
+        # replays launch the captured kernels without passing through the
+        # host-side counter: count what one capture launched, per replay
+        launches = launches_per_replay * args.steps
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     if clocks:
@@ -224,7 +258,10 @@ def run_gpu(args):
             "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights and bank)",
             "config": {"workload": WORKLOAD, "global_batch": c["B"] * world, "seq_len": c["S"],
-                       "parallelism": f"dp{world}", "l2": "flushed between timed steps (256 MiB write, untimed)"},
+                       "parallelism": f"dp{world}", "l2": "flushed between timed steps (256 MiB write, untimed)",
+                       "cuda_graph": ("fwd+bwd captured once, replayed per step"
+                                      + ("; bucket all-reduce after replay" if world > 1 else ""))
+                       if graph is not None else "off (eager launches)"},
             "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
                          "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
                          "traffic": None, "kernel": "MoM read fwd+bwd (bucket + fwd + dq + dkdv)",
@@ -240,6 +277,8 @@ def run_gpu(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(samples=args.cpu_samples)
         print(json.dumps(line), flush=True)
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -339,8 +378,7 @@ def measure_e2e(step, x, dout, dev, args, world, N):
     xh = x.detach().cpu().pin_memory()
     gh = dout.cpu().pin_memory()
     dxh = torch.empty_like(xh).pin_memory()
-    xd = torch.empty_like(x.detach()).requires_grad_(True)
-    gd = torch.empty_like(dout)
+    xd, gd = x, dout          # the step's own device input buffers (static under a graph)
     iters = max(5, min(50, args.steps))
 
     def one():
@@ -438,6 +476,7 @@ def main():
     ap.add_argument("--impl", default="sm100", choices=["sm100", "reference"])
     ap.add_argument("--cpu-samples", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch the step eagerly, no CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

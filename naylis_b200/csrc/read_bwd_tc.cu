@@ -60,18 +60,11 @@ __device__ __forceinline__ uint32_t kmaj_addr(uint32_t base, int r, int cg) {
 }
 
 // set of a tile, number of live blocks
-__device__ __forceinline__ int tile_nblk(const PlanView &P, int key, int top, const int **set_out) {
-    const int *set = P.keyset + static_cast<int64_t>(key) * top;
-    int n = 0;
-    while (n < top && set[n] >= 0) ++n;
-    *set_out = set;
-    return n;
-}
-
 struct DqBars {
     uint64_t full[2], empty[2], kv_full, kv_empty, s_full, ds_full, dq_full, dq_free, drain;
     uint32_t tmem_base;
     int abort;
+    int meta[2];      // per stage: blocks loaded | (K/V reload << 8); written before the stage's barrier
 };
 constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
 constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
@@ -129,65 +122,88 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
     // item -> (tile, head); items are head-major so runs of one CTA share (set, head)
     auto item_tile = [&](int item) { return item % ntiles; };
     auto item_head = [&](int item) { return item / ntiles; };
-    auto item_key = [&](int item) { return P.tiles[item_tile(item)].z; };
-    auto kv_change = [&](int item) {   // this item needs a K/V (re)load
-        return item == it0 || item_key(item) != item_key(item - 1) || item_head(item) != item_head(item - 1);
-    };
+    const int nmine = max(0, it1 - it0);
 
     if (warp == 0) {
         // ------------------------------------------------------------ loader
+        // Tile metadata 32 items at a time (one per lane), the Q / dO rows of item
+        // i+1 read while item i waits for its stage. Per stage the loader posts the
+        // block count and whether K/V change (a new (set, head) run) in shared
+        // memory before the stage's barrier; Q / dO go first, then, on a change,
+        // K/V once the MMAs of the previous run are done with them (kv_empty,
+        // committed by the MMA warp when it meets the change).
+        tc::LaneTile lt;
+        int mh = 0, mreload = 0, prev_key = -1, prev_h = -1;
+        int rows[4], nrows[4];
         int nreload = 0, last_full = -1;
-        for (int item = it0, i = 0; item < it1; ++item, ++i) {
-            const int s = i & 1, j = i >> 1;
-            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-            const int tile = item_tile(item), h = item_head(item);
-            const int4 td = P.tiles[tile];
-            const int *set;
-            const int nblk = tile_nblk(P, td.z, top, &set);
-            const int nload = nblk > 0 ? nblk : 1;
-            if (kv_change(item)) {
-                if (nreload > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
-                if (lane == 0) {
-                    tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kRowTile);
-                    for (int jb = 0; jb < nload; ++jb) {
-                        const int blk = nblk > 0 ? set[jb] : 0;
-                        tc::tma_load_2d(sK + jb * kRowTile, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
-                        tc::tma_load_2d(sV + jb * kRowTile, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
-                    }
+        for (int i = 0; i < nmine; ++i) {
+            const int s = i & 1, j = i >> 1, src = i & 31;
+            if (src == 0) {
+                const int item = it0 + i + lane;
+                if (item < it1) {
+                    lt.fetch(P, item_tile(item), top);
+                    mh = item_head(item);
                 }
-                ++nreload;
+                int pk = __shfl_up_sync(0xffffffffu, lt.key, 1), ph = __shfl_up_sync(0xffffffffu, mh, 1);
+                if (lane == 0) {
+                    pk = prev_key;
+                    ph = prev_h;
+                }
+                mreload = (lt.key != pk || mh != ph) ? 1 : 0;
+                prev_key = tc::get(lt.key, 31);
+                prev_h = tc::get(mh, 31);
+                tc::gather_rows(P, tc::get(lt.x, 0), tc::get(lt.y, 0), lane, nrows);
             }
-            int rows[4];
+            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int rr = lane * 4 + u;
-                rows[u] = rr < td.y ? P.perm[td.x + rr] : 0;
-            }
+            for (int u = 0; u < 4; ++u) rows[u] = nrows[u];
+            if (src < 31 && i + 1 < nmine) tc::gather_rows(P, tc::get(lt.x, src + 1), tc::get(lt.y, src + 1), lane, nrows);
+            const int h = tc::get(mh, src), nblk = tc::get(lt.nblk, src);
+            const int b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
+            const int reload = tc::get(mreload, src);
+            const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
+            if (lane == 0) {
+                bars->meta[s] = nload | (reload << 8);   // released by the arrive below
+                tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
+            }
             __syncwarp();
             tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             last_full = i;
+            if (reload) {
+                if (nreload > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
+                if (lane == 0) {
+                    tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kRowTile);
+                    for (int jb = 0; jb < nload; ++jb) {
+                        const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
+                        tc::tma_load_2d(sK + jb * kRowTile, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
+                        tc::tma_load_2d(sV + jb * kRowTile, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
+                    }
+                }
+                __syncwarp();
+                ++nreload;
+            }
         }
         if (last_full >= 0) tc::mbar_wait_warp(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
         if (nreload > 0) tc::mbar_wait_warp(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
-        int nreload = 0, issued = 0;
-        for (int item = it0, i = 0; item < it1; ++item, ++i) {
+        int nreload = 0;
+        for (int i = 0; i < nmine; ++i) {
             const int s = i & 1, j = i >> 1;
-            const int4 td = P.tiles[item_tile(item)];
-            const int *set;
-            const int nblk = tile_nblk(P, td.z, top, &set);
-            const int nload = nblk > 0 ? nblk : 1;
-            const bool reload = kv_change(item);
-            if (reload) {
+            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            const int meta = tc::ld_shared_volatile(&bars->meta[s]);
+            const int nload = meta & 0xFF;
+            if ((meta >> 8) & 1) {
+                // a new (set, head) run: the previous run's K/V are free once every
+                // MMA issued so far has completed
+                if (i > 0 && lane == 0) tc::mma_commit(&bars->kv_empty);
+                __syncwarp();
                 if (!tc::mbar_wait_warp(&bars->kv_full, nreload & 1, P.err, 2, abort_flag)) break;
                 ++nreload;
             }
-            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
             // S and dP overwrite TMEM columns that dQ(i-1) used: wait for its epilogue
             if (i > 0 && !tc::mbar_wait_warp(&bars->dq_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
@@ -213,13 +229,9 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                     tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sP + (kk >> 2) * kRowTile + (kk & 3) * 32, 16, 1024),
                                     tc::smem_desc_sw128(sK + kk * 2048, 4 * kRowTile, 1024), idesc_dq, kk > 0);
                 tc::mma_commit(&bars->dq_full);
-                // K/V of this run are no longer needed once dQ is done
-                if (item + 1 >= it1 || kv_change(item + 1)) tc::mma_commit(&bars->kv_empty);
             }
             __syncwarp();
-            issued = i + 1;
         }
-        (void)issued;
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
         tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
@@ -236,17 +248,38 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const int bar_id = 1 + quarter;
         bool dead = false;
-        for (int item = it0, i = 0; item < it1; ++item, ++i) {
-            const int tile = item_tile(item), h = item_head(item);
-            const int4 td = P.tiles[tile];
-            const int *set;
-            const int nblk = tile_nblk(P, td.z, top, &set);
-            const int tok = r < td.y ? P.perm[td.x + r] : -1;
-            float bias = 0.0f, lse2 = INFINITY;
-            if (tok >= 0) {
-                if (jb < nblk) bias = P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e;
-                lse2 = lse[static_cast<int64_t>(h) * P.n + td.x + r] * kLog2e;
+        // per-item row metadata: tile fields 32 items at a time (one per lane),
+        // this thread's row (token, bias, lse, caller-slot map) one item ahead
+        struct Meta { int x, nblk, h, tok; float bias, lse2; uint32_t kmap; };
+        tc::LaneTile lt;
+        int mh = 0;
+        auto fetch = [&](int src, Meta &m) {
+            m.x = tc::get(lt.x, src);
+            const int y = tc::get(lt.y, src);
+            m.nblk = tc::get(lt.nblk, src);
+            m.h = tc::get(mh, src);
+            const bool in = r < y;
+            m.tok = in ? P.perm[m.x + r] : -1;
+            m.bias = (in && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(m.x + r) * top + jb] * kLog2e : 0.0f;
+            m.lse2 = in ? lse[static_cast<int64_t>(m.h) * P.n + m.x + r] * kLog2e : INFINITY;
+            m.kmap = (in && grp == 0) ? P.rowkmap[m.x + r] : 0u;
+        };
+        Meta cur, nxt;
+        for (int i = 0; i < nmine; ++i) {
+            const int src = i & 31;
+            if (src == 0) {
+                const int item = it0 + i + lane;
+                if (item < it1) {
+                    lt.fetch(P, item_tile(item), top);
+                    mh = item_head(item);
+                }
+                fetch(0, cur);
+            } else {
+                cur = nxt;   // prefetched during item i-1
             }
+            if (src < 31 && i + 1 < nmine) fetch(src + 1, nxt);
+            const int h = cur.h, nblk = cur.nblk, tok = cur.tok;
+            const float bias = cur.bias, lse2 = cur.lse2;
             if (!dead && !tc::mbar_wait_warp(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             tc::tc_fence_after();
             // warp-uniform: the tcgen05.ld below are warp-collective. Padding rows
@@ -319,10 +352,10 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             tc::mbar_arrive(&bars->ds_full);
             // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
             if (grp == 0 && tok >= 0) {
-                ws_delta[static_cast<int64_t>(h) * P.n + td.x + r] = delta;
+                ws_delta[static_cast<int64_t>(h) * P.n + cur.x + r] = delta;
                 const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
                 const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
-                const uint32_t kmap = P.rowkmap[td.x + r];
+                const uint32_t kmap = cur.kmap;
                 for (int kk = 0; kk < top; ++kk) {
                     const int jsel = (kmap >> (4 * kk)) & 0xF;
                     if (jsel < nblk && jsel < 2)
@@ -425,15 +458,33 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
 
     if (warp == 0) {
         // ------------------------------------------------------------ loader
+        // Per item: the tile list entry, tile descriptor and the block's position
+        // in the tile's set for 32 tiles at a time (one per lane); per tile the
+        // rows, gate bias, lse and delta (one round trip) one tile ahead.
         int g = 0, nkv = 0, last = -1;         // g: global tile-step counter of this CTA
+        int cx = 0, cy = 0, cjb = 0;           // this lane's tile of the current chunk
+        struct RowPre { int rows[4]; float bias[4], lse2[4], delta[4]; };
+        auto fetch_rows = [&](int src, int h, RowPre &m) {
+            const int x = tc::get(cx, src), y = tc::get(cy, src), jb = tc::get(cjb, src);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                // lse and delta are stored in plan-row order: no dependence on perm
+                const int rr = lane * 4 + u;
+                const bool ok = rr < y;
+                const int64_t prow = static_cast<int64_t>(h) * P.n + x + rr;
+                m.rows[u] = ok ? P.perm[x + rr] : 0;
+                m.bias[u] = ok ? P.rowbias[static_cast<int64_t>(x + rr) * top + jb] * kLog2e : 0.0f;
+                m.lse2[u] = ok ? lse[prow] * kLog2e : INFINITY;
+                m.delta[u] = ok ? ws_delta[prow] : 0.0f;
+            }
+        };
         for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
             const int blk = item / (H * nsplit), h = (item / nsplit) % H, split = item % nsplit;
             const int nt = item_ntile(item);
             if (nt == 0) continue;
-            // K_b, V_b: the previous item's MMAs have all completed once its
-            // accumulators were handed to the epilogue (acc_full), which the
-            // epilogue acknowledges before the loader may overwrite them
-            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            // K_b, V_b: every MMA of the previous item has completed once its
+            // accumulators were committed (acc_full)
+            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_full, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             if (lane == 0) {
                 tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
                 tc::tma_load_2d(sK, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
@@ -441,36 +492,42 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             }
             ++nkv;
             const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
+            RowPre cur, nxt;
+            bool stop = false;
             for (int t = 0; t < nt; ++t, ++g) {
+                const int src = t & 31;
+                if (src == 0) {
+                    if (t + lane < nt) {
+                        const int tile = list[split + (t + lane) * nsplit];
+                        const int4 td = P.tiles[tile];
+                        cx = td.x;
+                        cy = td.y;
+                        cjb = (top > 1 && P.keyset[static_cast<int64_t>(td.z) * top] != blk) ? 1 : 0;
+                    }
+                    fetch_rows(0, h, cur);
+                } else {
+                    cur = nxt;
+                }
+                if (src < 31 && t + 1 < nt) fetch_rows(src + 1, h, nxt);
                 const int s = g % kDkvStages, j = g / kDkvStages;
-                if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-                const int tile = list[split + t * nsplit];
-                const int4 td = P.tiles[tile];
-                const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
-                int jb = 0;
-                while (jb < top - 1 && set[jb] != blk) ++jb;
+                if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) { stop = true; break; }
                 float *mb = meta + s * 3 * kTM;
-                int rows[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    // lse and delta are stored in plan-row order: no dependence on perm
                     const int rr = lane * 4 + u;
-                    const bool ok = rr < td.y;
-                    const int64_t prow = static_cast<int64_t>(h) * P.n + td.x + rr;
-                    rows[u] = ok ? P.perm[td.x + rr] : 0;
-                    mb[rr] = ok ? P.rowbias[static_cast<int64_t>(td.x + rr) * top + jb] * kLog2e : 0.0f;
-                    mb[kTM + rr] = ok ? lse[prow] * kLog2e : INFINITY;
-                    mb[2 * kTM + rr] = ok ? ws_delta[prow] : 0.0f;
+                    mb[rr] = cur.bias[u];
+                    mb[kTM + rr] = cur.lse2[u];
+                    mb[2 * kTM + rr] = cur.delta[u];
                 }
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
                 if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
                 __syncwarp();
-                tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
-                tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
+                tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, cur.rows[0], cur.rows[1], cur.rows[2], cur.rows[3], &bars->full[s]);
+                tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, cur.rows[0], cur.rows[1], cur.rows[2], cur.rows[3], &bars->full[s]);
                 tc::mbar_arrive(&bars->full[s]);
                 last = g;
             }
-            if (*abort_flag) break;
+            if (stop || *abort_flag) break;
         }
         if (last >= 0) tc::mbar_wait_warp(&bars->full[last % kDkvStages], (last / kDkvStages) & 1, P.err, 2, abort_flag);
         if (nkv > 0) tc::mbar_wait_warp(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);

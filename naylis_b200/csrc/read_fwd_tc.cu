@@ -6,14 +6,17 @@
 // routing set (top-2). A work item is (tile of <= 128 tokens sharing one block
 // set, head); CTAs are persistent over items.
 //
-// Warp roles (192 threads):
+// Warp roles (576 threads):
 //   warp 0     loader: K, V blocks by TMA (SWIZZLE_128B boxes of 128 slots x 64),
-//              the tile's Q rows by cp.async (gathered through the permutation)
+//              the tile's Q rows by TMA tile::gather4 through the permutation;
+//              tile metadata is fetched 32 items at a time (one per lane) and
+//              the rows of item i+1 while item i waits for its stage
 //   warp 1     TMEM owner and MMA issuer (one elected lane):
 //              S[128 x 256] = Q K^T into TMEM, then O[128 x 64] = P V
-//   warps 2-5  softmax (one TMEM lane = one token row per thread): row max,
-//              exp2, row sum, P as bf16 into shared memory; then the epilogue
-//              O / l -> global, log-sum-exp -> global
+//   warps 2-17 softmax (one TMEM lane = one token row per thread; four warps per
+//              lane quarter, 64 score columns each): row max, exp2, row sum, P as
+//              bf16 into shared memory; then the epilogue O / l -> global,
+//              log-sum-exp -> global
 // Q/K/V stages are double-buffered, O is double-buffered in TMEM, so the
 // epilogue of item i-1 and the loads of item i+1 overlap the softmax of item i.
 // All waits are bounded (tc::mbar_wait); a timeout sets bit 1 of the plan's
@@ -48,6 +51,7 @@ struct Bars {
     uint64_t full[2], empty[2], s_full, p_full, o_full[2], o_free[2], drain;
     uint32_t tmem_base;
     int abort;
+    int nload[2];     // blocks loaded into each stage; written before the stage's barrier
 };
 }  // namespace
 
@@ -70,6 +74,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = *P.ntiles;
     const int nitems = ntiles * H;
+    // items of this CTA: blockIdx.x + i * gridDim.x, i < nmine
+    const int nmine = static_cast<int>(blockIdx.x) < nitems ? (nitems - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
     const int64_t ld = static_cast<int64_t>(H) * kHD;
 
     if (threadIdx.x == 0) {
@@ -100,31 +106,33 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 
     if (warp == 0) {
         // ------------------------------------------------------------ loader
+        tc::LaneTile lt;
+        int rows[4], nrows[4];
         int issued = 0;
-        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
-            const int s = i & 1, j = i >> 1;
+        for (int i = 0; i < nmine; ++i) {
+            const int item = blockIdx.x + i * gridDim.x;
+            const int s = i & 1, j = i >> 1, src = i & 31;
+            if (src == 0) {   // metadata of items i .. i+31, then the rows of item i
+                if (i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
+                tc::gather_rows(P, tc::get(lt.x, 0), tc::get(lt.y, 0), lane, nrows);
+            }
             if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-            const int tile = item / H, h = item % H;
-            const int4 td = P.tiles[tile];
-            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
-            int nblk = 0;
-            while (nblk < top && set[nblk] >= 0) ++nblk;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) rows[u] = nrows[u];
+            // each lane gathers 4 Q rows (tokens of rows 4*lane .. 4*lane+3); padding
+            // rows read token 0 and are never stored
+            if (src < 31 && i + 1 < nmine) tc::gather_rows(P, tc::get(lt.x, src + 1), tc::get(lt.y, src + 1), lane, nrows);
+            const int nblk = tc::get(lt.nblk, src), b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
+            const int h = item % H;
             const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kStageBytes;
             const uint32_t sK = sQ + kQBytes;
             const uint32_t sV = sK + 2 * kBlkBytes;
-            // each lane gathers 4 Q rows (tokens of rows 4*lane .. 4*lane+3); padding
-            // rows read token 0 and are never stored
-            int rows[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const int rr = lane * 4 + u;
-                rows[u] = rr < td.y ? P.perm[td.x + rr] : 0;
-            }
             if (lane == 0) {
+                bars->nload[s] = nload;   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + 2 * nload * kBlkBytes);
                 for (int jb = 0; jb < nload; ++jb) {
-                    const int blk = nblk > 0 ? set[jb] : 0;
+                    const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
                     tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
                     tc::tma_load_2d(sV + jb * kBlkBytes, &tmap_v, h * kHD, blk * kBS, &bars->full[s]);
                 }
@@ -162,16 +170,11 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             __syncwarp();
             return true;
         };
-        for (int item = blockIdx.x, i = 0; item < nitems && ok; item += gridDim.x, ++i) {
+        for (int i = 0; i < nmine && ok; ++i) {
             const int s = i & 1, j = i >> 1;
             if (i > 0 && !issue_o(i - 1)) break;
             if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
-            const int tile = item / H;
-            const int4 td = P.tiles[tile];
-            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
-            int nblk = 0;
-            while (nblk < top && set[nblk] >= 0) ++nblk;
-            const int nload = nblk > 0 ? nblk : 1;
+            const int nload = tc::ld_shared_volatile(&bars->nload[s]);
             tc::tc_fence_after();
             if (lane == 0) {
                 const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
@@ -237,28 +240,33 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                     lse[static_cast<int64_t>(prev_h) * P.n + prev_row] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
             }
         };
-        // per-item row metadata, fetched one item ahead so that its global-load
-        // latency hides behind the current item's softmax
-        struct Meta { int h, nblk, tok, row; float bias; };
-        auto fetch = [&](int item, Meta &m) {
-            const int tile = item / H;
-            m.h = item % H;
-            const int4 td = P.tiles[tile];
-            const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
-            m.nblk = 0;
-            while (m.nblk < top && set[m.nblk] >= 0) ++m.nblk;
-            m.tok = r < td.y ? P.perm[td.x + r] : -1;
-            m.row = td.x + r;
-            m.bias = (m.tok >= 0 && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(td.x + r) * top + jb] * kLog2e : 0.0f;
+        // per-item row metadata: tile fields for 32 items at a time (one per lane),
+        // this thread's row (token, gate bias) one item ahead, so that no global
+        // load latency sits on the softmax path
+        struct Meta { int nblk, tok, row; float bias; };
+        tc::LaneTile lt;
+        auto fetch = [&](int src, Meta &m) {
+            const int x = tc::get(lt.x, src), y = tc::get(lt.y, src);
+            m.nblk = tc::get(lt.nblk, src);
+            m.tok = r < y ? P.perm[x + r] : -1;
+            m.row = x + r;
+            m.bias = (r < y && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(x + r) * top + jb] * kLog2e : 0.0f;
         };
         Meta cur, nxt;
-        if (static_cast<int>(blockIdx.x) < nitems) fetch(blockIdx.x, cur);
         int count = 0;
         bool dead = false;   // a bounded wait gave up: skip work, keep the barrier structure
-        for (int item = blockIdx.x, i = 0; item < nitems; item += gridDim.x, ++i) {
-            const int h = cur.h, nblk = cur.nblk, tok = cur.tok;
+        for (int i = 0; i < nmine; ++i) {
+            const int item = blockIdx.x + i * gridDim.x;
+            const int src = i & 31;
+            if (src == 0) {
+                if (i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
+                fetch(0, cur);
+            } else {
+                cur = nxt;   // prefetched during item i-1
+            }
+            if (src < 31 && i + 1 < nmine) fetch(src + 1, nxt);
+            const int h = item % H, nblk = cur.nblk, tok = cur.tok;
             const float bias = cur.bias;
-            if (item + static_cast<int>(gridDim.x) < nitems) fetch(item + gridDim.x, nxt);
             // the row sum of item i-1 (complete since the second barrier of i-1), read
             // before this item's first barrier lets anyone overwrite it
             if (i > 0) prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
@@ -328,7 +336,6 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             prev_h = h;
             prev_row = cur.row;
             prev_m = m;
-            cur = nxt;
             count = i + 1;
         }
         if (count > 0 && !dead && !*abort_flag) {

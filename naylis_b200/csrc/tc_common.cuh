@@ -228,5 +228,42 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, bool a_mn_ma
            | (static_cast<uint32_t>(M >> 4) << 24);     // M / 16
 }
 
+// ---------------------------------------------------------------- plan metadata
+// The read kernels walk work items whose tile descriptor (P.tiles) and block set
+// (P.keyset) sit behind two dependent global loads. A warp fetches them for 32
+// items at once, item c0 + lane in lane `lane`, and broadcasts one item's fields
+// with get(); a tile's permuted rows then take a single round trip, which the
+// caller issues one item ahead. Sets of at most two blocks (the tensor-core
+// kernels' limit) are held as (nblk, b0, b1).
+struct LaneTile {
+    int x = 0, y = 0, key = -1, nblk = 0, b0 = 0, b1 = 0;
+    template <typename PV>
+    __device__ __forceinline__ void fetch(const PV &P, int tile, int top) {
+        const int4 td = P.tiles[tile];
+        const int *set = P.keyset + static_cast<int64_t>(td.z) * top;
+        const int s0 = set[0], s1 = top > 1 ? set[1] : -1;
+        x = td.x;
+        y = td.y;
+        key = td.z;
+        nblk = s0 < 0 ? 0 : (s1 < 0 ? 1 : 2);
+        b0 = s0 < 0 ? 0 : s0;
+        b1 = s1 < 0 ? 0 : s1;
+    }
+};
+__device__ __forceinline__ int get(int v, int src) { return __shfl_sync(0xffffffffu, v, src); }
+
+// Token of each of the 4 tile rows 4*lane .. 4*lane+3 (row rr < y), else 0:
+// the rows a lane gathers with one tile::gather4 load.
+template <typename PV>
+__device__ __forceinline__ void gather_rows(const PV &P, int x, int y, int lane, int rows[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int rr = lane * 4 + u;
+        rows[u] = rr < y ? P.perm[x + rr] : 0;
+    }
+}
+
+__device__ __forceinline__ int ld_shared_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
 }  // namespace tc
 }  // namespace mom

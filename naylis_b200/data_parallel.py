@@ -23,8 +23,12 @@ import torch.distributed as dist
 
 class GradAllReduce:
     def __init__(self, module: torch.nn.Module, process_group=None, bucket_mb: float = 32.0,
-                 average: bool = True):
+                 average: bool = True, overlap: bool = True):
         self.group = process_group
+        # overlap=False: no collective from the backward's hooks; finish()
+        # exchanges every bucket. For a backward captured in a CUDA graph,
+        # whose replay then runs no collective, with finish() after replay.
+        self.overlap = overlap
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.average = average
         params = [p for p in module.parameters() if p.requires_grad]
@@ -86,7 +90,8 @@ class GradAllReduce:
     def _on_ready(self, p):
         i = self._bucket_of[p]
         self._pending[i] -= 1
-        self._launch_ready()
+        if self.overlap:
+            self._launch_ready()
 
     def finish(self):
         """Launch the remaining buckets, wait for all, average."""
@@ -96,7 +101,7 @@ class GradAllReduce:
         if self.average and self.world > 1:
             for buf in self.flat:
                 buf.div_(self.world)
-        self._works = []
+        self._reset_state()
 
     def remove(self):
         for h in self._hooks:

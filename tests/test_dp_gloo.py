@@ -5,6 +5,8 @@ on world_size-2 gloo process groups on CPU.
   on its own shard of the batch, equals the single-process full-batch
   gradient (mean loss, so the average over ranks is exact up to rounding);
 * parameters that get no gradient in a step do not stall the exchange;
+* with overlap=False (a backward captured in a CUDA graph) finish() alone
+  exchanges every bucket, step after step;
 * failure detection on the host: a rank that dies before the collective makes
   the survivor's next exchange fail within the process-group timeout.
 """
@@ -64,7 +66,9 @@ def _worker(rank, world, port, q, mode):
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timeout)
         from naylis_b200.data_parallel import GradAllReduce
         holder = _build()
-        dp = GradAllReduce(holder, bucket_mb=0.004)      # tiny buckets: several in flight
+        # tiny buckets: several in flight; "deferred": no collective in the
+        # hooks, finish() exchanges everything (the CUDA-graph replay pattern)
+        dp = GradAllReduce(holder, bucket_mb=0.004, overlap=(mode != "deferred"))
         x = _data()
         shard = x.chunk(world, dim=0)[rank]
         if mode == "fault":
@@ -84,8 +88,14 @@ def _worker(rank, world, port, q, mode):
             q.close()
             q.join_thread()       # flush the queue before the hard exit
             os._exit(0)
-        for _ in range(2):   # two steps: zero_grad re-arms the hooks and views
-            dp.zero_grad()
+        for it in range(2):   # two steps: zero_grad re-arms the hooks and views
+            if mode == "deferred" and it > 0:
+                # a graph replay zeroes the buckets on the device and runs no
+                # Python hook or zero_grad; finish() alone must exchange all
+                for buf in dp.flat:
+                    buf.zero_()
+            else:
+                dp.zero_grad()
             _loss(holder, shard).backward()
             dp.finish()
         grads = {n: p.grad.clone() for n, p in holder.named_parameters()}
@@ -115,9 +125,10 @@ def _spawn(world, mode):
     return results
 
 
-def test_grad_allreduce_equals_full_batch_gradient():
+@pytest.mark.parametrize("mode", ["ok", "deferred"])
+def test_grad_allreduce_equals_full_batch_gradient(mode):
     world = 2
-    res = _spawn(world, "ok")
+    res = _spawn(world, mode)
     for r in range(world):
         assert isinstance(res[r], dict), res[r]
     assert res[0]["nbuckets"] > 2
