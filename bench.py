@@ -305,12 +305,13 @@ def measure_kernels(layer, x, M, dout, dev, args):
     lg = gates.clamp_min(1e-9).log().float().contiguous()
     plan = torch.empty(lib.mom_plan_size(N, nb, top), dtype=torch.uint8, device=dev)
     out = torch.empty_like(q)
-    lse = torch.empty(N, H, dtype=torch.float32, device=dev)
+    lse = torch.empty(H, N, dtype=torch.float32, device=dev)
+    q_rows = torch.empty(N, d, dtype=torch.bfloat16, device=dev)
     dq = torch.empty_like(q)
     dk = torch.empty(nb * bs, d, dtype=torch.float32, device=dev)
     dv = torch.empty_like(dk)
     dlg = torch.empty(N, top, dtype=torch.float32, device=dev)
-    ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=dev)
+    ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H, hd), dtype=torch.uint8, device=dev)
     do4 = dout.to(torch.bfloat16).view(B, S, H, hd)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
@@ -318,11 +319,11 @@ def measure_kernels(layer, x, M, dout, dev, args):
         _lib.call("mom_bucket", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
                   plan.numel(), st)
         _lib.call("mom_read_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd, nb,
-                  bs, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(), st)
+                  bs, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(), q_rows.data_ptr(), st)
         _lib.call("mom_read_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                   do4.data_ptr(), lse.data_ptr(), _lib.BF16, B, S, H, hd, nb, bs, top, plan.data_ptr(),
-                  dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(), ws.data_ptr(),
-                  ws.numel(), st)
+                  q_rows.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(),
+                  ws.data_ptr(), ws.numel(), st)
 
     xb = x.detach().contiguous()
     wd = layer.router_down.weight.detach().to(torch.bfloat16).contiguous()

@@ -124,21 +124,26 @@ MOM_API int mom_bucket(const void *top_idx, int idx_dtype, const float *log_gate
  * Gated memory read forward. Replaces mom_kernels/__init__.py:87-102
  * (mom_read) -> mom_kernels/triton_gpu.py:323-356 (_MomReadFunction.forward).
  * q (B,S,H,hd) and out of dtype (BF16); k, v: the shared bank projections
- * (L, H*hd), L = nb*bs; lse (B*S, H) fp32 saved for the backward.
- * `plan` comes from mom_bucket on the same routing. */
+ * (L, H*hd), L = nb*bs; lse (H, B*S) fp32 in routing-plan row order, saved
+ * for the backward. q_rows: a caller buffer of B*S*H*hd elements of dtype,
+ * 16-byte aligned, which this call fills with q's rows in routing-plan row
+ * order (where every tile of the read is contiguous); pass it unchanged to
+ * mom_read_bwd, like lse. `plan` comes from mom_bucket on the same routing. */
 MOM_API int mom_read_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B,
                  int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top,
-                 const void *plan, void *out, float *lse, void *stream);
+                 const void *plan, void *out, float *lse, void *q_rows, void *stream);
 
 /* Gated memory read backward. Replaces mom_kernels/triton_gpu.py:358-409
  * (_MomReadFunction.backward). Produces dq (B,S,H,hd) of dtype, dk_acc and
  * dv_acc (L, H*hd) fp32 (overwritten), dlog_gates (B*S, top) fp32 in the
- * caller's top order (gradient w.r.t. log(max(gate, 1e-9))). */
-MOM_API size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H);
+ * caller's top order (gradient w.r.t. log(max(gate, 1e-9))). q_rows as filled
+ * by mom_read_fwd. The workspace holds delta (H x B*S fp32) and dO in
+ * routing-plan row order (B*S x H*hd of dtype). */
+MOM_API size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd);
 MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void *out,
                  const void *dout, const float *lse, int dtype, int64_t B, int64_t S,
                  int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top,
-                 const void *plan, void *dq, float *dk_acc, float *dv_acc,
+                 const void *plan, const void *q_rows, void *dq, float *dk_acc, float *dv_acc,
                  float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream);
 
 /* mom_read_bwd without a workspace argument: for callers that cannot allocate
@@ -149,13 +154,16 @@ MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void
  * most 1,048,576; larger calls return MOM_ERR_WORKSPACE. It calls no
  * cudaMalloc/cudaFree. Its first call on a device looks the array's address
  * up (make that call before any stream capture). All calls share the array:
- * calls that overlap on the GPU race. Arguments and results as mom_read_bwd. */
+ * calls that overlap on the GPU race. Arguments and results as mom_read_bwd;
+ * dO is read in token order (its rows gathered by the kernels), so nothing
+ * beyond delta needs scratch. */
 MOM_API size_t mom_read_bwd_noalloc_max_bytes(void);
 MOM_API int mom_read_bwd_noalloc(const void *q, const void *k, const void *v, const void *out,
                                  const void *dout, const float *lse, int dtype, int64_t B,
                                  int64_t S, int64_t H, int64_t head_dim, int64_t num_blocks,
-                                 int64_t block_size, int64_t top, const void *plan, void *dq,
-                                 float *dk_acc, float *dv_acc, float *dlog_gates, void *stream);
+                                 int64_t block_size, int64_t top, const void *plan,
+                                 const void *q_rows, void *dq, float *dk_acc, float *dv_acc,
+                                 float *dlog_gates, void *stream);
 
 /* ------------------------------------------------------------------ output scale
  * ReZero output scale of the layer, fused: y = scale[0] * o with y in fp32

@@ -45,13 +45,13 @@ SIGNATURES = {
     "mom_scale_fwd": (_int, [_vp, _int, _i64, _fp, _fp, _vp]),
     "mom_scale_bwd": (_int, [_vp, _int, _vp, _int, _i64, _fp, _vp, _fp, _vp]),
     "mom_read_fwd": (_int, [_vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
-                            _vp, _fp, _vp]),
-    "mom_read_bwd_workspace_size": (_sz, [_i64, _i64, _i64]),
+                            _vp, _fp, _vp, _vp]),
+    "mom_read_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "mom_read_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
-                            _i64, _i64, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
+                            _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
     "mom_read_bwd_noalloc_max_bytes": (_sz, []),
     "mom_read_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
-                                    _i64, _i64, _vp, _vp, _fp, _fp, _fp, _vp]),
+                                    _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp]),
 }
 
 _lock = threading.Lock()

@@ -290,37 +290,36 @@ static int check_read_geometry(int dtype, int64_t B, int64_t S, int64_t H, int64
 
 int mom_read_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B, int64_t S,
                  int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top, const void *plan,
-                 void *out, float *lse, void *stream) {
+                 void *out, float *lse, void *q_rows, void *stream) {
     int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
     if (rc) return rc;
     if (B * S == 0) return MOM_OK;
-    MOM_REQUIRE(q && k && v && plan && out && lse, "null pointer argument");
+    MOM_REQUIRE(q && k && v && plan && out && lse && q_rows, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(q_rows) & 15) == 0,
+                "q and q_rows must be 16-byte aligned");
     if ((rc = check_current_device())) return rc;
     const mom::PlanLayout L = mom::plan_layout(B * S, nb, top);
     const mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
     cudaError_t e = mom::launch_read_fwd(q, k, v, (int)B, (int)S, (int)H, (int)hd, (int)nb, (int)bs,
-                                         (int)top, L, P, out, lse, static_cast<cudaStream_t>(stream));
+                                         (int)top, L, P, out, lse, q_rows, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "read_fwd");
     return MOM_OK;
 }
 
-size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H) {
-    if (B < 0 || S < 0 || H < 0) return 0;
-    return align256(static_cast<size_t>(B) * S * H * 4);
+size_t mom_read_bwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd) {
+    if (B < 0 || S < 0 || H < 0 || hd < 0) return 0;
+    const size_t nh = static_cast<size_t>(B) * S * H;
+    return align256(nh * 4) + align256(nh * hd * 2);
 }
 
-int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, const void *dout,
-                 const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd,
-                 int64_t nb, int64_t bs, int64_t top, const void *plan, void *dq, float *dk_acc,
-                 float *dv_acc, float *dlog_gates, void *workspace, size_t workspace_bytes,
-                 void *stream) {
-    int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
-    if (rc) return rc;
-    MOM_REQUIRE(k && v && dk_acc && dv_acc, "null pointer argument");
-    MOM_REQUIRE(B * S == 0 || (q && out && dout && lse && plan && dq && dlog_gates), "null pointer argument");
-    const size_t need = mom_read_bwd_workspace_size(B, S, H);
-    if (workspace_bytes < need || (need && !workspace))
-        return fail(MOM_ERR_WORKSPACE, "read bwd workspace %zu < %zu bytes", workspace_bytes, need);
+namespace {
+// Shared by mom_read_bwd and mom_read_bwd_noalloc: ws_delta holds H x B*S fp32;
+// do_rows (B*S x H*hd, or null) receives dO in plan order.
+int read_bwd_impl(const void *q, const void *k, const void *v, const void *out, const void *dout,
+                  const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb,
+                  int64_t bs, int64_t top, const void *plan, const void *q_rows, void *dq, float *dk_acc,
+                  float *dv_acc, float *dlog_gates, float *ws_delta, void *do_rows, void *stream) {
+    int rc;
     if ((rc = check_current_device())) return rc;
     if (B * S == 0) {
         const size_t kv = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
@@ -331,12 +330,44 @@ int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, c
     }
     const mom::PlanLayout L = mom::plan_layout(B * S, nb, top);
     const mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
-    cudaError_t e = mom::launch_read_bwd(q, k, v, out, dout, lse, (int)B, (int)S, (int)H, (int)hd,
+    cudaError_t e = mom::launch_read_bwd(q, q_rows, k, v, out, dout, lse, (int)B, (int)S, (int)H, (int)hd,
                                          (int)nb, (int)bs, (int)top, L, P, dq, dk_acc, dv_acc,
-                                         dlog_gates, static_cast<float *>(workspace),
-                                         static_cast<cudaStream_t>(stream));
+                                         dlog_gates, ws_delta, do_rows, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "read_bwd");
     return MOM_OK;
+}
+
+int check_read_bwd_args(int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs,
+                        int64_t top, const void *q, const void *k, const void *v, const void *out,
+                        const void *dout, const float *lse, const void *plan, const void *q_rows, void *dq,
+                        float *dk_acc, float *dv_acc, float *dlog_gates) {
+    int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    MOM_REQUIRE(k && v && dk_acc && dv_acc, "null pointer argument");
+    MOM_REQUIRE(B * S == 0 || (q && out && dout && lse && plan && q_rows && dq && dlog_gates),
+                "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(dout) & 15) == 0,
+                "q_rows and dout must be 16-byte aligned");
+    return MOM_OK;
+}
+}  // namespace
+
+int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, const void *dout,
+                 const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd,
+                 int64_t nb, int64_t bs, int64_t top, const void *plan, const void *q_rows, void *dq,
+                 float *dk_acc, float *dv_acc, float *dlog_gates, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+    int rc = check_read_bwd_args(dtype, B, S, H, hd, nb, bs, top, q, k, v, out, dout, lse, plan, q_rows, dq,
+                                 dk_acc, dv_acc, dlog_gates);
+    if (rc) return rc;
+    const size_t need = mom_read_bwd_workspace_size(B, S, H, hd);
+    if (workspace_bytes < need || (need && !workspace))
+        return fail(MOM_ERR_WORKSPACE, "read bwd workspace %zu < %zu bytes", workspace_bytes, need);
+    char *ws = static_cast<char *>(workspace);
+    float *delta = reinterpret_cast<float *>(ws);
+    void *do_rows = ws + align256(static_cast<size_t>(B) * S * H * 4);
+    return read_bwd_impl(q, k, v, out, dout, lse, dtype, B, S, H, hd, nb, bs, top, plan, q_rows, dq, dk_acc,
+                         dv_acc, dlog_gates, delta, do_rows, stream);
 }
 
 // ------------------------------------------------- read backward, no allocation
@@ -385,21 +416,25 @@ size_t mom_read_bwd_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
 
 int mom_read_bwd_noalloc(const void *q, const void *k, const void *v, const void *out, const void *dout,
                          const float *lse, int dtype, int64_t B, int64_t S, int64_t H, int64_t hd,
-                         int64_t nb, int64_t bs, int64_t top, const void *plan, void *dq, float *dk_acc,
-                         float *dv_acc, float *dlog_gates, void *stream) {
+                         int64_t nb, int64_t bs, int64_t top, const void *plan, const void *q_rows, void *dq,
+                         float *dk_acc, float *dv_acc, float *dlog_gates, void *stream) {
     int rc = check_read_geometry(dtype, B, S, H, hd, nb, bs, top);
     if (rc) return rc;
-    const size_t need = mom_read_bwd_workspace_size(B, S, H);
+    const size_t need = align256(static_cast<size_t>(B) * S * H * 4);
     if (need > kNoAllocScratchBytes)
         return fail(MOM_ERR_WORKSPACE,
                     "mom_read_bwd_noalloc: B*S*H = %lld needs %zu bytes of scratch, over its fixed %zu "
                     "(at most %zu tokens x heads); use mom_read_bwd with a caller workspace",
                     (long long)(B * S * H), need, kNoAllocScratchBytes, kNoAllocScratchBytes / 4);
+    if ((rc = check_read_bwd_args(dtype, B, S, H, hd, nb, bs, top, q, k, v, out, dout, lse, plan, q_rows, dq,
+                                  dk_acc, dv_acc, dlog_gates)))
+        return rc;
     if ((rc = check_current_device())) return rc;
     void *scratch = nullptr;
     if ((rc = noalloc_scratch(&scratch))) return rc;
-    return mom_read_bwd(q, k, v, out, dout, lse, dtype, B, S, H, hd, nb, bs, top, plan, dq, dk_acc, dv_acc,
-                        dlog_gates, scratch, kNoAllocScratchBytes, stream);
+    // dO stays in token order (no scratch for a plan-order copy): the kernels gather its rows
+    return read_bwd_impl(q, k, v, out, dout, lse, dtype, B, S, H, hd, nb, bs, top, plan, q_rows, dq, dk_acc,
+                         dv_acc, dlog_gates, static_cast<float *>(scratch), nullptr, stream);
 }
 
 }  // extern "C"

@@ -64,23 +64,31 @@ cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, con
                              void *d_o, float *d_scale, cudaStream_t st);
 cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
                           const PlanLayout &L, const PlanView &P, cudaStream_t st);
+// Row copy into routing-plan order: dst[r] = src[perm[r]] (rows of row_bytes, a multiple of 16).
+cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, const int *perm, void *dst,
+                                cudaStream_t st);
+// Read forward. q is token-ordered; q_rows (N x H*hd, same dtype) receives q in
+// plan order and is what the tensor-core kernels (and the backward) read.
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
                             int hd, int nb, int bs, int top, const PlanLayout &L,
-                            const PlanView &P, void *out, float *lse, cudaStream_t st);
+                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st);
 bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H);
-cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
+cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st);
 bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,
                            const void *dout, int H);
-cudaError_t launch_read_bwd_tc(const void *q, const void *k, const void *v, const void *dout, const float *lse,
-                               int H, int nb, int top, const PlanLayout &L, const PlanView &P, void *dq,
-                               float *dk_acc, float *dv_acc, float *dlog_gates, float *ws_delta,
-                               cudaStream_t st);
-cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const void *out,
+// do_src: dO in plan order (do_is_rows) or token order (rows gathered by the kernels).
+cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v, const void *do_src,
+                               bool do_is_rows, const float *lse, int H, int nb, int top, const PlanLayout &L,
+                               const PlanView &P, void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
+                               float *ws_delta, cudaStream_t st);
+// Read backward. q_rows: as filled by launch_read_fwd. do_rows: N x H*hd scratch for
+// dO in plan order, or null (the tensor-core kernels then gather dO rows).
+cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, const void *v, const void *out,
                             const void *dout, const float *lse, int B, int S, int H, int hd,
                             int nb, int bs, int top, const PlanLayout &L, const PlanView &P,
                             void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
-                            float *ws_delta, cudaStream_t st);
+                            float *ws_delta, void *do_rows, cudaStream_t st);
 
 }  // namespace mom

@@ -474,11 +474,11 @@ static cudaError_t launch_bwd_t(const void *q, const void *k, const void *v, con
     return cudaSuccess;
 }
 
-cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const void *out,
+cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, const void *v, const void *out,
                             const void *dout, const float *lse, int B, int S, int H, int hd,
                             int nb, int bs, int top, const PlanLayout &L, const PlanView &P,
                             void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
-                            float *ws_delta, cudaStream_t st) {
+                            float *ws_delta, void *do_rows, cudaStream_t st) {
     const size_t kv_bytes = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
     cudaError_t e = cudaMemsetAsync(dk_acc, 0, kv_bytes, st);
     if (e != cudaSuccess) return e;
@@ -488,9 +488,17 @@ cudaError_t launch_read_bwd(const void *q, const void *k, const void *v, const v
     if (L.max_tiles == 0) return cudaSuccess;
     // tensor-core kernels for head_dim 64, 128-slot blocks, top <= 2; other
     // geometries take the warp-level mma kernels below
-    if (read_bwd_tc_supported(hd, bs, top, q, k, v, dout, H))
-        return launch_read_bwd_tc(q, k, v, dout, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
-                                  ws_delta, st);
+    if (read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H)) {
+        if (do_rows) {   // dO in plan order: every tile's rows are one TMA box
+            if ((e = launch_permute_rows(dout, N, static_cast<int64_t>(H) * hd * 2, P.perm, do_rows, st)) !=
+                cudaSuccess)
+                return e;
+            return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
+                                      dlog_gates, ws_delta, st);
+        }
+        return launch_read_bwd_tc(q_rows, k, v, dout, false, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
+                                  dlog_gates, ws_delta, st);
+    }
     if (hd == 64)
         return launch_bwd_t<64>(q, k, v, out, dout, lse, H, nb, bs, top, L, P, dq, dk_acc, dv_acc,
                                 dlog_gates, ws_delta, st);

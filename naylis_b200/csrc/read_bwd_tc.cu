@@ -8,7 +8,7 @@
 // read_bwd_dq_tc_kernel — item = (128-token tile, head), persistent CTAs over
 // contiguous runs of items ordered head-major, so consecutive items usually
 // share their block set and head and reuse the K/V tiles in shared memory.
-//   warp 0     loader: Q, dO rows by TMA gather4; K, V blocks by TMA (on change)
+//   warp 0     loader: Q, dO rows by cp.async; K, V blocks by TMA (on change)
 //   warp 1     MMA: S = Q K^T (TMEM cols 0-255), dP = dO V^T (cols 256-511),
 //              then dQ = dS K (cols 0-63, after the softmax warps drained S)
 //   warps 2-5  pass 1: P = exp2(S*scale + bias - lse) -> bf16 P in smem,
@@ -17,7 +17,7 @@
 //              over P in place; then dQ -> global, delta -> workspace,
 //              gate gradient -> global (fp32 atomics over heads)
 // read_bwd_dkdv_tc_kernel — item = (block, head, split of the block's tiles)
-//   warp 0     loader: K_b, V_b once per item; per tile Q, dO rows (gather4)
+//   warp 0     loader: K_b, V_b once per item (TMA); per tile Q, dO rows (cp.async)
 //              and the tile's per-token lse, delta, bias into shared memory
 //   warp 1     MMA: S^T = K_b Q^T (cols 0-127), dP^T = V_b dO^T (cols 128-255),
 //              then dK += dS^T Q (cols 256-319), dV += P^T dO (cols 320-383)
@@ -65,7 +65,9 @@ struct DqBars {
     uint32_t tmem_base;
     int abort;
     int meta[2];      // per stage: blocks loaded | (K/V reload << 8); written before the stage's barrier
+    int tok[128];     // the loader's row tokens of the tile being copied
 };
+static_assert(sizeof(DqBars) <= 1024, "barrier block");
 constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
 constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
 constexpr uint32_t kDqP = 4 * kRowTile;                          // P / dS [128 x 256] bf16
@@ -74,9 +76,13 @@ constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqP + kDqScratch + 1024 + 1
 }  // namespace
 
 // ============================================================================ dQ
+// kDoRows: dO in plan order (one TMA box per tile, like Q); else dO in token
+// order, its rows gathered with cp.async.
+template <bool kDoRows>
 __global__ void __launch_bounds__(kThreads, 1)
 read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                      const uint16_t *__restrict__ dout,
                       const float *__restrict__ lse, int H, int top, float scale, float scale_log2, PlanView P,
                       uint16_t *__restrict__ dq, float *__restrict__ dlog_gates, float *__restrict__ ws_delta) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -98,7 +104,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(&bars->full[s], 1);
+            // the loader's arrive with the TMA bytes (+ 32 lanes' dO cp.async when gathering)
+            tc::mbar_init(&bars->full[s], kDoRows ? 1 : 33);
             tc::mbar_init(&bars->empty[s], 1);
         }
         tc::mbar_init(&bars->kv_full, 1);
@@ -134,7 +141,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         // committed by the MMA warp when it meets the change).
         tc::LaneTile lt;
         int mh = 0, mreload = 0, prev_key = -1, prev_h = -1;
-        int rows[4], nrows[4];
+        int rows[4];
         int nreload = 0, last_full = -1;
         for (int i = 0; i < nmine; ++i) {
             const int s = i & 1, j = i >> 1, src = i & 31;
@@ -152,25 +159,30 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 mreload = (lt.key != pk || mh != ph) ? 1 : 0;
                 prev_key = tc::get(lt.key, 31);
                 prev_h = tc::get(mh, 31);
-                tc::gather_rows(P, tc::get(lt.x, 0), tc::get(lt.y, 0), lane, nrows);
+                if (!kDoRows) tc::gather_rows(P, tc::get(lt.x, 0), tc::get(lt.y, 0), lane, rows);
             }
-            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) rows[u] = nrows[u];
-            if (src < 31 && i + 1 < nmine) tc::gather_rows(P, tc::get(lt.x, src + 1), tc::get(lt.y, src + 1), lane, nrows);
+            const int x0 = tc::get(lt.x, src);
             const int h = tc::get(mh, src), nblk = tc::get(lt.nblk, src);
             const int b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
             const int reload = tc::get(mreload, src);
+            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
             const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
+            if (!kDoRows) {
+                tc::stage_row_tokens(bars->tok, rows, lane);
+                tc::gather_tile_rows(sD, dout, ld, h * kHD, bars->tok, lane);
+                tc::cp_async_arrive_noinc(&bars->full[s]);
+            }
             if (lane == 0) {
                 bars->meta[s] = nload | (reload << 8);   // released by the arrive below
-                tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
+                tc::mbar_arrive_expect_tx(&bars->full[s], kDoRows ? 2 * kRowTile : kRowTile);
+                tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
+                if (kDoRows) tc::tma_load_2d(sD, &tmap_do, h * kHD, x0, &bars->full[s]);
             }
             __syncwarp();
-            tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
-            tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             last_full = i;
+            if (!kDoRows && src < 31 && i + 1 < nmine)
+                tc::gather_rows(P, tc::get(lt.x, src + 1), tc::get(lt.y, src + 1), lane, rows);
             if (reload) {
                 if (nreload > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
                 if (lane == 0) {
@@ -187,6 +199,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         }
         if (last_full >= 0) tc::mbar_wait_warp(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
         if (nreload > 0) tc::mbar_wait_warp(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
+        tc::cp_async_wait_all();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
@@ -194,6 +207,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         for (int i = 0; i < nmine; ++i) {
             const int s = i & 1, j = i >> 1;
             if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            tc::fence_proxy_async_smem();   // Q / dO rows came through cp.async (generic proxy)
             const int meta = tc::ld_shared_volatile(&bars->meta[s]);
             const int nload = meta & 0xFF;
             if ((meta >> 8) & 1) {
@@ -398,7 +412,9 @@ struct DkvBars {
     uint64_t full[3], empty[3], kv_full, s_full, pds_full, pds_free, acc_full, acc_free, drain;
     uint32_t tmem_base;
     int abort;
+    int tok[128];     // the loader's row tokens of the tile being copied
 };
+static_assert(sizeof(DkvBars) <= 1024, "barrier block");
 constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
 constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
 constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
@@ -406,9 +422,11 @@ constexpr int kDkvStages = 3;
 constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + 2 * (kBS * kTM * 2) + kDkvStages * kMetaBytes + 1024 + 1024;
 }  // namespace
 
+template <bool kDoRows>
 __global__ void __launch_bounds__(kThreads, 1)
 read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                         const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
+                        const uint16_t *__restrict__ dout,
                         const float *__restrict__ lse, const float *__restrict__ ws_delta, int H, int nb, int top,
                         int nsplit, int max_tiles, float scale, float scale_log2, PlanView P,
                         float *__restrict__ dk_acc, float *__restrict__ dv_acc) {
@@ -429,7 +447,9 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDkvStages; ++s) {
-            tc::mbar_init(&bars->full[s], 33);
+            // per lane: the arrive after its metadata stores (lane 0's carries the TMA
+            // bytes), + its dO cp.async when gathering
+            tc::mbar_init(&bars->full[s], kDoRows ? 32 : 64);
             tc::mbar_init(&bars->empty[s], 1);
         }
         tc::mbar_init(&bars->kv_full, 1);
@@ -460,22 +480,25 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         // ------------------------------------------------------------ loader
         // Per item: the tile list entry, tile descriptor and the block's position
         // in the tile's set for 32 tiles at a time (one per lane); per tile the
-        // rows, gate bias, lse and delta (one round trip) one tile ahead.
+        // row tokens, gate bias, lse and delta (one round trip) are loaded right
+        // after the previous tile's copies were issued.
+        const int64_t ld = static_cast<int64_t>(H) * kHD;
         int g = 0, nkv = 0, last = -1;         // g: global tile-step counter of this CTA
         int cx = 0, cy = 0, cjb = 0;           // this lane's tile of the current chunk
-        struct RowPre { int rows[4]; float bias[4], lse2[4], delta[4]; };
-        auto fetch_rows = [&](int src, int h, RowPre &m) {
+        int rows[4];
+        float mbias[4], mlse[4], mdelta[4];
+        auto fetch_rows = [&](int src, int h) {
             const int x = tc::get(cx, src), y = tc::get(cy, src), jb = tc::get(cjb, src);
+            if (!kDoRows) tc::gather_rows(P, x, y, lane, rows);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 // lse and delta are stored in plan-row order: no dependence on perm
                 const int rr = lane * 4 + u;
                 const bool ok = rr < y;
                 const int64_t prow = static_cast<int64_t>(h) * P.n + x + rr;
-                m.rows[u] = ok ? P.perm[x + rr] : 0;
-                m.bias[u] = ok ? P.rowbias[static_cast<int64_t>(x + rr) * top + jb] * kLog2e : 0.0f;
-                m.lse2[u] = ok ? lse[prow] * kLog2e : INFINITY;
-                m.delta[u] = ok ? ws_delta[prow] : 0.0f;
+                mbias[u] = ok ? P.rowbias[static_cast<int64_t>(x + rr) * top + jb] * kLog2e : 0.0f;
+                mlse[u] = ok ? lse[prow] * kLog2e : INFINITY;
+                mdelta[u] = ok ? ws_delta[prow] : 0.0f;
             }
         };
         for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
@@ -492,7 +515,6 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             }
             ++nkv;
             const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
-            RowPre cur, nxt;
             bool stop = false;
             for (int t = 0; t < nt; ++t, ++g) {
                 const int src = t & 31;
@@ -504,33 +526,40 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                         cy = td.y;
                         cjb = (top > 1 && P.keyset[static_cast<int64_t>(td.z) * top] != blk) ? 1 : 0;
                     }
-                    fetch_rows(0, h, cur);
-                } else {
-                    cur = nxt;
+                    fetch_rows(0, h);
                 }
-                if (src < 31 && t + 1 < nt) fetch_rows(src + 1, h, nxt);
                 const int s = g % kDkvStages, j = g / kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) { stop = true; break; }
                 float *mb = meta + s * 3 * kTM;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int rr = lane * 4 + u;
-                    mb[rr] = cur.bias[u];
-                    mb[kTM + rr] = cur.lse2[u];
-                    mb[2 * kTM + rr] = cur.delta[u];
+                    mb[rr] = mbias[u];
+                    mb[kTM + rr] = mlse[u];
+                    mb[2 * kTM + rr] = mdelta[u];
                 }
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
-                if (lane == 0) tc::mbar_arrive_expect_tx(&bars->full[s], 2 * kRowTile);
-                __syncwarp();
-                tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, cur.rows[0], cur.rows[1], cur.rows[2], cur.rows[3], &bars->full[s]);
-                tc::tma_gather4(sD + lane * 512, &tmap_do, h * kHD, cur.rows[0], cur.rows[1], cur.rows[2], cur.rows[3], &bars->full[s]);
-                tc::mbar_arrive(&bars->full[s]);
+                const int x0 = tc::get(cx, src);
+                if (!kDoRows) {
+                    tc::stage_row_tokens(bars->tok, rows, lane);
+                    tc::gather_tile_rows(sD, dout, ld, h * kHD, bars->tok, lane);
+                    tc::cp_async_arrive_noinc(&bars->full[s]);
+                }
+                if (lane == 0) {
+                    tc::mbar_arrive_expect_tx(&bars->full[s], kDoRows ? 2 * kRowTile : kRowTile);
+                    tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
+                    if (kDoRows) tc::tma_load_2d(sD, &tmap_do, h * kHD, x0, &bars->full[s]);
+                } else {
+                    tc::mbar_arrive(&bars->full[s]);
+                }
                 last = g;
+                if (src < 31 && t + 1 < nt) fetch_rows(src + 1, h);
             }
             if (stop || *abort_flag) break;
         }
         if (last >= 0) tc::mbar_wait_warp(&bars->full[last % kDkvStages], (last / kDkvStages) & 1, P.err, 2, abort_flag);
         if (nkv > 0) tc::mbar_wait_warp(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
+        tc::cp_async_wait_all();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kTM, false, false);
@@ -548,6 +577,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             for (int t = 0; t < nt; ++t, ++g) {
                 const int s = g % kDkvStages, j = g / kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
+                tc::fence_proxy_async_smem();   // Q / dO rows came through cp.async (generic proxy)
                 tc::tc_fence_after();
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
                 if (lane == 0) {
@@ -672,37 +702,53 @@ bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k
     return read_fwd_tc_supported(hd, bs, top, q, k, v, H) && (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
 }
 
-cudaError_t launch_read_bwd_tc(const void *q, const void *k, const void *v, const void *dout, const float *lse,
-                               int H, int nb, int top, const PlanLayout &L, const PlanView &P, void *dq,
-                               float *dk_acc, float *dv_acc, float *dlog_gates, float *ws_delta,
-                               cudaStream_t st) {
-    CUtensorMap mk, mv, mq, md;
-    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
-    if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
-        !make_bf16_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1) ||
-        !make_bf16_map(&md, dout, static_cast<uint64_t>(L.N), cols, 1))
-        return cudaErrorInvalidValue;
+template <bool kDoRows>
+static cudaError_t launch_bwd_tc_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mq,
+                                   const CUtensorMap &md, const uint16_t *dout, const float *lse, int H, int nb,
+                                   int top, const PlanLayout &L, const PlanView &P, void *dq, float *dk_acc,
+                                   float *dv_acc, float *dlog_gates, float *ws_delta, cudaStream_t st) {
     const float scale = 1.0f / sqrtf(static_cast<float>(kHD));
     const float scale_log2 = scale * kLog2e;
     const int sms = device_sm_count();
-    cudaError_t e = cudaFuncSetAttribute(read_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kDqSmem);
+    cudaError_t e = cudaFuncSetAttribute(read_bwd_dq_tc_kernel<kDoRows>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDqSmem);
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
     const int grid = static_cast<int>(std::min<int64_t>(items, sms));
-    read_bwd_dq_tc_kernel<<<grid, kThreads, kDqSmem, st>>>(mk, mv, mq, md, lse, H, top, scale, scale_log2, P,
-                                                           static_cast<uint16_t *>(dq), dlog_gates, ws_delta);
+    read_bwd_dq_tc_kernel<kDoRows><<<grid, kThreads, kDqSmem, st>>>(
+        mk, mv, mq, md, dout, lse, H, top, scale, scale_log2, P, static_cast<uint16_t *>(dq), dlog_gates, ws_delta);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDkvSmem);
+    e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel<kDoRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kDkvSmem);
     if (e != cudaSuccess) return e;
     const int nsplit = std::max(1, std::min(16, (2 * sms + nb * H - 1) / (nb * H)));
     const int items2 = nb * H * nsplit;
-    read_bwd_dkdv_tc_kernel<<<std::min(items2, sms), kThreads, kDkvSmem, st>>>(
-        mk, mv, mq, md, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2, P,
-        dk_acc, dv_acc);
+    read_bwd_dkdv_tc_kernel<kDoRows><<<std::min(items2, sms), kThreads, kDkvSmem, st>>>(
+        mk, mv, mq, md, dout, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2,
+        P, dk_acc, dv_acc);
     count_launch();
     return cudaGetLastError();
+}
+
+cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v, const void *do_src,
+                               bool do_is_rows, const float *lse, int H, int nb, int top, const PlanLayout &L,
+                               const PlanView &P, void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
+                               float *ws_delta, cudaStream_t st) {
+    CUtensorMap mk, mv, mq, md;
+    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
+    if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
+        !make_bf16_map(&mq, q_rows, static_cast<uint64_t>(L.N), cols, kTM))
+        return cudaErrorInvalidValue;
+    const uint16_t *do16 = static_cast<const uint16_t *>(do_src);
+    if (do_is_rows) {
+        if (!make_bf16_map(&md, do_src, static_cast<uint64_t>(L.N), cols, kTM)) return cudaErrorInvalidValue;
+        return launch_bwd_tc_t<true>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
+                                     ws_delta, st);
+    }
+    md = mq;   // unused by the gathering variant
+    return launch_bwd_tc_t<false>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
+                                  ws_delta, st);
 }
 
 }  // namespace mom

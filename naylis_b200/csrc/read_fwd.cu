@@ -232,13 +232,16 @@ static cudaError_t launch_fwd_t(const void *q, const void *k, const void *v, int
 
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
                             int hd, int nb, int bs, int top, const PlanLayout &L,
-                            const PlanView &P, void *out, float *lse, cudaStream_t st) {
+                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st) {
     (void)B; (void)S; (void)nb;
     if (L.max_tiles == 0) return cudaSuccess;
+    // q in plan order, for the tensor-core kernels of this call and of the backward
+    cudaError_t e = launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st);
+    if (e != cudaSuccess) return e;
     // the tensor-core kernel covers head_dim 64, 128-slot blocks, top <= 2;
     // other geometries take the warp-level mma kernel below
-    if (read_fwd_tc_supported(hd, bs, top, q, k, v, H))
-        return launch_read_fwd_tc(q, k, v, H, nb, top, L, P, out, lse, st);
+    if (read_fwd_tc_supported(hd, bs, top, q_rows, k, v, H))
+        return launch_read_fwd_tc(q_rows, k, v, H, nb, top, L, P, out, lse, st);
     if (hd == 64) return launch_fwd_t<64>(q, k, v, H, bs, top, L, P, out, lse, st);
     if (hd == 128) return launch_fwd_t<128>(q, k, v, H, bs, top, L, P, out, lse, st);
     return cudaErrorInvalidValue;

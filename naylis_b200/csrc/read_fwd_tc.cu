@@ -7,10 +7,10 @@
 // set, head); CTAs are persistent over items.
 //
 // Warp roles (576 threads):
-//   warp 0     loader: K, V blocks by TMA (SWIZZLE_128B boxes of 128 slots x 64),
-//              the tile's Q rows by TMA tile::gather4 through the permutation;
-//              tile metadata is fetched 32 items at a time (one per lane) and
-//              the rows of item i+1 while item i waits for its stage
+//   warp 0     loader: K, V blocks and the tile's 128 Q rows by TMA (SWIZZLE_128B
+//              boxes of 128 rows x 64); Q is read from its copy in routing-plan
+//              row order (q_rows), where a tile's rows are contiguous; tile
+//              metadata is fetched 32 items at a time (one per lane)
 //   warp 1     TMEM owner and MMA issuer (one elected lane):
 //              S[128 x 256] = Q K^T into TMEM, then O[128 x 64] = P V
 //   warps 2-17 softmax (one TMEM lane = one token row per thread; four warps per
@@ -53,6 +53,7 @@ struct Bars {
     int abort;
     int nload[2];     // blocks loaded into each stage; written before the stage's barrier
 };
+static_assert(sizeof(Bars) <= 1024, "barrier block");
 }  // namespace
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -107,22 +108,14 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     if (warp == 0) {
         // ------------------------------------------------------------ loader
         tc::LaneTile lt;
-        int rows[4], nrows[4];
         int issued = 0;
         for (int i = 0; i < nmine; ++i) {
             const int item = blockIdx.x + i * gridDim.x;
             const int s = i & 1, j = i >> 1, src = i & 31;
-            if (src == 0) {   // metadata of items i .. i+31, then the rows of item i
-                if (i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
-                tc::gather_rows(P, tc::get(lt.x, 0), tc::get(lt.y, 0), lane, nrows);
-            }
-            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-#pragma unroll
-            for (int u = 0; u < 4; ++u) rows[u] = nrows[u];
-            // each lane gathers 4 Q rows (tokens of rows 4*lane .. 4*lane+3); padding
-            // rows read token 0 and are never stored
-            if (src < 31 && i + 1 < nmine) tc::gather_rows(P, tc::get(lt.x, src + 1), tc::get(lt.y, src + 1), lane, nrows);
+            if (src == 0 && i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
+            const int x0 = tc::get(lt.x, src);
             const int nblk = tc::get(lt.nblk, src), b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
+            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
             const int h = item % H;
             const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kStageBytes;
@@ -131,6 +124,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (lane == 0) {
                 bars->nload[s] = nload;   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + 2 * nload * kBlkBytes);
+                // the tile's rows x0 .. x0+127 (rows past the tile are never stored)
+                tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
                 for (int jb = 0; jb < nload; ++jb) {
                     const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
                     tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
@@ -138,7 +133,6 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 }
             }
             __syncwarp();
-            tc::tma_gather4(sQ + lane * 512, &tmap_q, h * kHD, rows[0], rows[1], rows[2], rows[3], &bars->full[s]);
             issued = i + 1;
         }
         // make sure no TMA write is still in flight when the CTA retires
@@ -394,13 +388,13 @@ int device_sm_count() {
     return n;
 }
 
-cudaError_t launch_read_fwd_tc(const void *q, const void *k, const void *v, int H, int nb, int top,
+cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st) {
     CUtensorMap mk, mv, mq;
     const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
     if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
-        !make_bf16_map(&mq, q, static_cast<uint64_t>(L.N), cols, 1))
+        !make_bf16_map(&mq, q_rows, static_cast<uint64_t>(L.N), cols, kTM))
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)kSmemBytes);

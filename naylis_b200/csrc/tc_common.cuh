@@ -90,18 +90,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
         : "memory");
 }
 
-// Four arbitrary rows (y0..y3) of a 2-D map whose box is one row high, placed
-// as four consecutive swizzled 128-B rows at dst.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap *map, int x, int y0, int y1,
-                                            int y2, int y3, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];\n" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3),
-        "r"(smem_u32(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -142,6 +130,17 @@ __device__ __forceinline__ void mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, ui
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: A (128 x 16 bf16, row i in TMEM
+// lane i, two K elements per 32-bit column, 8 columns) read from tensor memory.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on an mbarrier once all previously issued tcgen05.mma of this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -174,6 +173,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+
+// 32 lanes x 8 consecutive 32-bit columns: this thread writes its lane's 8 columns.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(taddr),
+                 "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
 // ------------------------------------------------------------------ misc
 // Named barrier `id` (1..15) over `nthreads` threads (a multiple of 32).
@@ -253,7 +260,7 @@ struct LaneTile {
 __device__ __forceinline__ int get(int v, int src) { return __shfl_sync(0xffffffffu, v, src); }
 
 // Token of each of the 4 tile rows 4*lane .. 4*lane+3 (row rr < y), else 0:
-// the rows a lane gathers with one tile::gather4 load.
+// the four rows whose tokens a lane stages for the tile's row copies.
 template <typename PV>
 __device__ __forceinline__ void gather_rows(const PV &P, int x, int y, int lane, int rows[4]) {
 #pragma unroll
@@ -264,6 +271,47 @@ __device__ __forceinline__ void gather_rows(const PV &P, int x, int y, int lane,
 }
 
 __device__ __forceinline__ int ld_shared_volatile(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
+// ---------------------------------------------------------------- row gathers
+// A tile's Q / dO rows are scattered over the token dimension (the plan's
+// permutation). They are copied with 16-B cp.async, eight lanes per 128-B row
+// slice, four rows per instruction (one TMA tile::gather4 per four rows costs
+// ~60 cycles of the SM's TMA unit each, which made the loader the bottleneck).
+// Completion is signalled on an mbarrier with cp.async.mbarrier.arrive.noinc
+// (one of the barrier's expected arrivals per lane). cp.async writes shared
+// memory through the generic proxy: a consumer that feeds the tile to tcgen05.mma
+// executes fence_proxy_async_smem() after its wait on that barrier.
+__device__ __forceinline__ void cp_async_cg16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// The tile's 128 row tokens (gather_rows' four per lane, rows past the tile's y
+// read token 0, whose results are masked or never stored) go through a 128-int
+// shared buffer, so that a lane holds 4 tokens in registers instead of the 32 of
+// the rows it copies.
+__device__ __forceinline__ void stage_row_tokens(int *s_tok, const int rows[4], int lane) {
+    __syncwarp();   // the previous tile's reads of s_tok are done
+#pragma unroll
+    for (int u = 0; u < 4; ++u) s_tok[lane * 4 + u] = rows[u];
+    __syncwarp();
+}
+
+// Copy columns col0 .. col0+63 (bf16) of the 128 rows into a [128 x 64] tile in
+// the 128-B-swizzled K-major layout (row r at r*128, 16-B chunk c at (c ^ (r & 7))*16):
+// lane copies chunk lane & 7 of rows 4*i + (lane >> 3).
+__device__ __forceinline__ void gather_tile_rows(uint32_t sdst, const uint16_t *src, int64_t ld, int col0,
+                                                 const int *s_tok, int lane) {
+    const int c = lane & 7, rs = lane >> 3;
+    const uint16_t *base = src + col0 + c * 8;
+#pragma unroll 8
+    for (int i = 0; i < 32; ++i) {
+        const int r = 4 * i + rs;
+        cp_async_cg16(sdst + r * 128 + ((c ^ (r & 7)) << 4), base + static_cast<int64_t>(s_tok[r]) * ld);
+    }
+}
 
 }  // namespace tc
 }  // namespace mom

@@ -97,8 +97,9 @@ def announce(backend: str) -> None:
 
 # ====================================================================== read
 class _MomReadFunction(torch.autograd.Function):
-    """Autograd of the sm100 read: saves q, k, v, out, the fp32 log-sum-exp
-    and the routing plan (reference: mom_kernels/triton_gpu.py:323-409)."""
+    """Autograd of the sm100 read: saves q, k, v, out, the fp32 log-sum-exp,
+    the routing plan and q in plan row order (reference:
+    mom_kernels/triton_gpu.py:323-409)."""
 
     @staticmethod
     def forward(ctx, q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
@@ -116,16 +117,19 @@ class _MomReadFunction(torch.autograd.Function):
         _lib.call("mom_bucket", idx.data_ptr(), _lib.I64 if idx.dtype == torch.int64 else _lib.I32,
                   lg.data_ptr(), N, num_blocks, top, plan.data_ptr(), plan.numel(), st)
         out = torch.empty_like(q_sh)
-        lse = torch.empty((N, H), dtype=torch.float32, device=dev)
+        lse = torch.empty((H, N), dtype=torch.float32, device=dev)
+        # q in routing-plan row order, filled by the forward and read again by the backward
+        q_rows = torch.empty((N, H * hd), dtype=q_sh.dtype, device=dev)
         _lib.call("mom_read_fwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd,
-                  num_blocks, block_size, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(), st)
-        ctx.save_for_backward(q_sh, k, v, out, lse, plan)
+                  num_blocks, block_size, top, plan.data_ptr(), out.data_ptr(), lse.data_ptr(),
+                  q_rows.data_ptr(), st)
+        ctx.save_for_backward(q_sh, k, v, out, lse, plan, q_rows)
         ctx.meta = (num_blocks, block_size, top, L)
         return out
 
     @staticmethod
     def backward(ctx, dout):
-        q_sh, k, v, out, lse, plan = ctx.saved_tensors
+        q_sh, k, v, out, lse, plan, q_rows = ctx.saved_tensors
         num_blocks, block_size, top, L = ctx.meta
         B, S, H, hd = q_sh.shape
         N = B * S
@@ -136,11 +140,11 @@ class _MomReadFunction(torch.autograd.Function):
         dk = torch.empty((L, H * hd), dtype=torch.float32, device=dev)
         dv = torch.empty_like(dk)
         dlg = torch.empty((B, S, top), dtype=torch.float32, device=dev)
-        ws = torch.empty(_lib.load().mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=dev)
+        ws = torch.empty(_lib.load().mom_read_bwd_workspace_size(B, S, H, hd), dtype=torch.uint8, device=dev)
         _lib.call("mom_read_bwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
                   dout.data_ptr(), lse.data_ptr(), _lib.BF16, B, S, H, hd, num_blocks, block_size,
-                  top, plan.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(),
-                  ws.data_ptr(), ws.numel(), st)
+                  top, plan.data_ptr(), q_rows.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                  dlg.data_ptr(), ws.data_ptr(), ws.numel(), st)
         return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
 
 

@@ -72,10 +72,15 @@ def test_invalid_arguments_fail_before_device_work(lib):
                            None, None, _lib.I64, None, None, None, None, 0, None)
     assert rc == 1
     # read: head_dim 96 is unsupported (status 2), fp32 is invalid (status 1)
-    rc = lib.mom_read_fwd(None, None, None, _lib.BF16, 1, 1, 2, 96, 4, 64, 2, None, None, None, None)
+    rc = lib.mom_read_fwd(None, None, None, _lib.BF16, 1, 1, 2, 96, 4, 64, 2, None, None, None, None, None)
     assert rc == 2
-    rc = lib.mom_read_fwd(None, None, None, _lib.F32, 1, 1, 2, 64, 4, 64, 2, None, None, None, None)
+    rc = lib.mom_read_fwd(None, None, None, _lib.F32, 1, 1, 2, 64, 4, 64, 2, None, None, None, None, None)
     assert rc == 1
+    # read: a missing q_rows buffer is an invalid argument
+    rc = lib.mom_read_fwd(ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256), _lib.BF16, 1, 4, 2,
+                          64, 4, 64, 2, ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256), None,
+                          None)
+    assert rc == 1 and "null" in _lib.last_error()
     # bucketing: too many routing sets (top-4 of 32 blocks) is reported as unsupported
     rc = lib.mom_bucket(None, _lib.I64, None, 16, 32, 4, None, 0, None)
     assert rc == 2
@@ -88,7 +93,8 @@ def test_invalid_arguments_fail_before_device_work(lib):
 def test_plan_size_grows_with_tokens(lib):
     a, b = lib.mom_plan_size(1024, 8, 2), lib.mom_plan_size(16384, 8, 2)
     assert 0 < a < b
-    assert lib.mom_read_bwd_workspace_size(8, 2048, 16) >= 8 * 2048 * 16 * 4
+    # delta (fp32 per token and head) + dO in plan order (bf16)
+    assert lib.mom_read_bwd_workspace_size(8, 2048, 16, 64) >= 8 * 2048 * 16 * (4 + 64 * 2)
     assert lib.mom_route_workspace_size(8, 2048, 1024, 32, 8, 1) >= 8 * 2048 * 1024 * 2
 
 

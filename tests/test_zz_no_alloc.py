@@ -42,13 +42,14 @@ def _forward(lib, q, k, v, idx, lg, nb, bs, top, st):
     _lib.call("mom_bucket", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
               plan.numel(), st)
     out = torch.empty_like(q)
-    lse = torch.empty((N, H), dtype=torch.float32, device=q.device)
+    lse = torch.empty((H, N), dtype=torch.float32, device=q.device)
+    q_rows = torch.empty((N, H * hd), dtype=q.dtype, device=q.device)
     _lib.call("mom_read_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd, nb, bs, top,
-              plan.data_ptr(), out.data_ptr(), lse.data_ptr(), st)
-    return plan, out, lse
+              plan.data_ptr(), out.data_ptr(), lse.data_ptr(), q_rows.data_ptr(), st)
+    return plan, out, lse, q_rows
 
 
-def _backward(lib, name, q, k, v, out, dout, lse, plan, nb, bs, top, st):
+def _backward(lib, name, q, k, v, out, dout, lse, plan, q_rows, nb, bs, top, st):
     from naylis_b200 import _lib
     B, S, H, hd = q.shape
     dq = torch.empty_like(q)
@@ -56,10 +57,10 @@ def _backward(lib, name, q, k, v, out, dout, lse, plan, nb, bs, top, st):
     dv = torch.empty_like(dk)
     dlg = torch.empty((B * S, top), dtype=torch.float32, device=q.device)
     args = [q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(), lse.data_ptr(),
-            _lib.BF16, B, S, H, hd, nb, bs, top, plan.data_ptr(), dq.data_ptr(), dk.data_ptr(),
-            dv.data_ptr(), dlg.data_ptr()]
+            _lib.BF16, B, S, H, hd, nb, bs, top, plan.data_ptr(), q_rows.data_ptr(), dq.data_ptr(),
+            dk.data_ptr(), dv.data_ptr(), dlg.data_ptr()]
     if name == "mom_read_bwd":
-        ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H), dtype=torch.uint8, device=q.device)
+        ws = torch.empty(lib.mom_read_bwd_workspace_size(B, S, H, hd), dtype=torch.uint8, device=q.device)
         args += [ws.data_ptr(), ws.numel()]
     _lib.call(name, *args, st)
     torch.cuda.synchronize()
@@ -76,7 +77,7 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     H = 16
     S = cap // 4 // H + 1     # one token more than fits, B = 1
     rc = lib.mom_read_bwd_noalloc(None, None, None, None, None, None, _lib.BF16, 1, S, H, 64, 8, 128, 2,
-                                  None, None, None, None, None, None)
+                                  None, None, None, None, None, None, None)
     assert rc == 4, _lib.last_error()   # MOM_ERR_WORKSPACE
     assert "noalloc" in _lib.last_error()
 
@@ -98,9 +99,9 @@ def test_noalloc_matches_read_bwd_on_consecutive_calls():
         seed = c.pop("seed")
         nb, bs, top = c["nb"], c["bs"], c["top"]
         q, k, v, idx, lg, dout = _inputs(**c, seed=seed, dev=dev)
-        plan, out, lse = _forward(lib, q, k, v, idx, lg, nb, bs, top, st)
-        ref = _backward(lib, "mom_read_bwd", q, k, v, out, dout, lse, plan, nb, bs, top, st)
-        got = _backward(lib, "mom_read_bwd_noalloc", q, k, v, out, dout, lse, plan, nb, bs, top, st)
+        plan, out, lse, q_rows = _forward(lib, q, k, v, idx, lg, nb, bs, top, st)
+        ref = _backward(lib, "mom_read_bwd", q, k, v, out, dout, lse, plan, q_rows, nb, bs, top, st)
+        got = _backward(lib, "mom_read_bwd_noalloc", q, k, v, out, dout, lse, plan, q_rows, nb, bs, top, st)
         errs = {key: _scaled_err(got[key], ref[key]) for key in ref}
         assert all(e < TOL for e in errs.values()), (c, errs)
         assert all(np.isfinite(got[key]).all() for key in got)
