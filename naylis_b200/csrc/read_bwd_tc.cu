@@ -408,8 +408,9 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
 
 // ============================================================================ dK / dV
 namespace {
+constexpr int kDkvStages = 4;
 struct DkvBars {
-    uint64_t full[3], empty[3], kv_full, s_full, pds_full, pds_free, acc_full, acc_free, drain;
+    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, s_full[2], pds_full[2], acc_full, acc_free, drain;
     uint32_t tmem_base;
     int abort;
     int tok[128];     // the loader's row tokens of the tile being copied
@@ -418,8 +419,14 @@ static_assert(sizeof(DkvBars) <= 1024, "barrier block");
 constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
 constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
 constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
-constexpr int kDkvStages = 3;
-constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + 2 * (kBS * kTM * 2) + kDkvStages * kMetaBytes + 1024 + 1024;
+constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + kDkvStages * kMetaBytes + 1024 + 1024;
+// A tile's 128 tokens go through the MMAs and the softmax in two steps of 64.
+// TMEM: step buffer b (= step & 1) at column 128*b holds S^T [128 slots x 64
+// tokens] in columns +0..63 and dP^T in +64..127; the softmax overwrites them in
+// place with bf16 P^T and dS^T (softmax group g's 16 tokens packed into the first
+// 8 of its 16 columns), the A operands of dV += P^T dO and dK += dS^T Q. dK is
+// accumulated at columns 256..319, dV at 320..383.
+constexpr int kHalf = 64;
 }  // namespace
 
 template <bool kDoRows>
@@ -435,10 +442,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
     const uint32_t sK = base, sV = base + kKvTile;
-    const uint32_t sStage = base + 2 * kKvTile;                  // [3][Q | dO]
-    const uint32_t sPT = sStage + kDkvStages * kDkvStage;        // P^T  [128 slots x 128 tokens]
-    const uint32_t sDS = sPT + kBS * kTM * 2;                    // dS^T
-    float *meta = reinterpret_cast<float *>(sbase + (sDS + kBS * kTM * 2 - base));   // [3][3][128]
+    const uint32_t sStage = base + 2 * kKvTile;                  // [stages][Q | dO]
+    float *meta = reinterpret_cast<float *>(sbase + 2 * kKvTile + kDkvStages * kDkvStage);   // [stages][3][128]
     DkvBars *bars = reinterpret_cast<DkvBars *>(reinterpret_cast<unsigned char *>(meta) + kDkvStages * kMetaBytes);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -453,9 +458,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             tc::mbar_init(&bars->empty[s], 1);
         }
         tc::mbar_init(&bars->kv_full, 1);
-        tc::mbar_init(&bars->s_full, 1);
-        tc::mbar_init(&bars->pds_full, kSoftThreads);
-        tc::mbar_init(&bars->pds_free, 1);
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&bars->s_full[b], 1);
+            tc::mbar_init(&bars->pds_full[b], kSoftThreads);
+        }
         tc::mbar_init(&bars->acc_full, 1);
         tc::mbar_init(&bars->acc_free, kSoftThreads);
         tc::mbar_init(&bars->drain, 1);
@@ -562,54 +568,85 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         tc::cp_async_wait_all();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kTM, false, false);
+        // Per step (64 tokens of a tile): S^T = K_b Q^T and dP^T = V_b dO^T into the
+        // step's TMEM buffer, issued one step ahead so that they run while the
+        // softmax works on the previous step; then dV += P^T dO and dK += dS^T Q
+        // with P^T / dS^T read from TMEM.
+        const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kHalf, false, false);
         const uint32_t idesc_acc = tc::idesc_bf16_f32(kBS, kHD, false, true);
-        int g = 0, nkv = 0;
+        int g = 0, hs = 0, nkv = 0;       // g: tile (stage) counter, hs: step counter
         bool stop = false;
+        auto issue_s = [&](int gt, int half, int step) {
+            const uint32_t sQ = sStage + (gt % kDkvStages) * kDkvStage + half * (kHalf * 128);
+            const uint32_t sD = sQ + kRowTile;
+            const uint32_t tb = tmem + (step & 1) * 128;
+            if (lane == 0) {
+#pragma unroll
+                for (int kk = 0; kk < kHD / 16; ++kk) {
+                    tc::mma_bf16_ss(tb, tc::smem_desc_sw128(sK + kk * 32, 16, 1024),
+                                    tc::smem_desc_sw128(sQ + kk * 32, 16, 1024), idesc_s, kk > 0);
+                    tc::mma_bf16_ss(tb + kHalf, tc::smem_desc_sw128(sV + kk * 32, 16, 1024),
+                                    tc::smem_desc_sw128(sD + kk * 32, 16, 1024), idesc_s, kk > 0);
+                }
+                tc::mma_commit(&bars->s_full[step & 1]);
+            }
+            __syncwarp();
+        };
+        auto wait_tile = [&](int gt) {
+            if (!tc::mbar_wait_warp(&bars->full[gt % kDkvStages], (gt / kDkvStages) & 1, P.err, 2, abort_flag))
+                return false;
+            tc::fence_proxy_async_smem();   // dO rows may have come through cp.async (generic proxy)
+            tc::tc_fence_after();
+            return true;
+        };
         for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
             const int nt = item_ntile(item);
             if (nt == 0) continue;
             if (!tc::mbar_wait_warp(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
-            // the accumulators are reset by the first MMA of the item; the
-            // epilogue of the previous item must have read them
-            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
-            ++nkv;
-            for (int t = 0; t < nt; ++t, ++g) {
-                const int s = g % kDkvStages, j = g / kDkvStages;
-                if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) { stop = true; break; }
-                tc::fence_proxy_async_smem();   // Q / dO rows came through cp.async (generic proxy)
-                tc::tc_fence_after();
-                const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < kHD / 16; ++kk) {
-                        tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sK + kk * 32, 16, 1024),
-                                        tc::smem_desc_sw128(sQ + kk * 32, 16, 1024), idesc_s, kk > 0);
-                        tc::mma_bf16_ss(tmem + 128, tc::smem_desc_sw128(sV + kk * 32, 16, 1024),
-                                        tc::smem_desc_sw128(sD + kk * 32, 16, 1024), idesc_s, kk > 0);
+            if (!wait_tile(g)) break;
+            issue_s(g, 0, hs);
+            for (int t = 0; t < nt && !stop; ++t, ++g) {
+                for (int half = 0; half < 2; ++half, ++hs) {
+                    const bool last = (t + 1 == nt) && half == 1;
+                    if (!last) {   // the next step's S^T / dP^T
+                        if (half == 1) {
+                            if (!wait_tile(g + 1)) { stop = true; break; }
+                            issue_s(g + 1, 0, hs + 1);
+                        } else {
+                            issue_s(g, 1, hs + 1);
+                        }
                     }
-                    tc::mma_commit(&bars->s_full);
-                }
-                __syncwarp();
-                if (!tc::mbar_wait_warp(&bars->pds_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
-                tc::tc_fence_after();
-                if (lane == 0) {
-#pragma unroll
-                    for (int kk = 0; kk < kTM / 16; ++kk) {
-                        const uint32_t aoff = (kk >> 2) * (kBS * 128) + (kk & 3) * 32;
-                        const uint32_t boff = kk * 2048;
-                        const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-                        tc::mma_bf16_ss(tmem + 256, tc::smem_desc_sw128(sDS + aoff, 16, 1024),
-                                        tc::smem_desc_sw128(sQ + boff, 2 * kRowTile, 1024), idesc_acc, acc);
-                        tc::mma_bf16_ss(tmem + 320, tc::smem_desc_sw128(sPT + aoff, 16, 1024),
-                                        tc::smem_desc_sw128(sD + boff, 2 * kRowTile, 1024), idesc_acc, acc);
+                    if (!tc::mbar_wait_warp(&bars->pds_full[hs & 1], (hs >> 1) & 1, P.err, 2, abort_flag)) {
+                        stop = true;
+                        break;
                     }
-                    tc::mma_commit(&bars->pds_free);
-                    tc::mma_commit(&bars->empty[s]);
-                    if (t + 1 == nt) tc::mma_commit(&bars->acc_full);
+                    // the accumulators are reset by the item's first step; the epilogue
+                    // of the previous item must have read them
+                    if (t == 0 && half == 0 && nkv > 0 &&
+                        !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
+                        const uint32_t sD = sQ + kRowTile;
+                        const uint32_t tb = tmem + (hs & 1) * 128;
+#pragma unroll
+                        for (int kk = 0; kk < kHalf / 16; ++kk) {
+                            const uint32_t acc = (t > 0 || half > 0 || kk > 0) ? 1u : 0u;
+                            tc::mma_bf16_ts(tmem + 256, tb + kHalf + kk * 16,
+                                            tc::smem_desc_sw128(sQ + kk * 2048, 2 * kRowTile, 1024), idesc_acc, acc);
+                            tc::mma_bf16_ts(tmem + 320, tb + kk * 16,
+                                            tc::smem_desc_sw128(sD + kk * 2048, 2 * kRowTile, 1024), idesc_acc, acc);
+                        }
+                        if (half == 1) tc::mma_commit(&bars->empty[g % kDkvStages]);
+                        if (last) tc::mma_commit(&bars->acc_full);
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
+            ++nkv;
         }
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
@@ -617,54 +654,56 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     } else {
         // ------------------------------------------------------------ P^T, dS^T, epilogue
         // 16 warps: warp & 3 = TMEM lane quarter (slot rows), (warp-2) >> 2 = the
-        // 32-token column group this thread handles; no cross-thread reduction.
+        // 16-token group of a 64-token step this thread handles; no cross-thread
+        // reduction.
         const int quarter = warp & 3;
         const int grp = (warp - 2) >> 2;
         const int r = quarter * 32 + lane;                       // slot row within the block
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-        int g = 0, nkv = 0;
+        int g = 0, hs = 0, nkv = 0;
         bool stop = false;
         for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
             const int blk = item / (H * nsplit), h = (item / nsplit) % H;
             const int nt = item_ntile(item);
             if (nt == 0) continue;
-            for (int t = 0; t < nt; ++t, ++g) {
+            for (int t = 0; t < nt && !stop; ++t, ++g) {
                 const int s = g % kDkvStages;
-                if (!tc::mbar_wait_warp(&bars->s_full, g & 1, P.err, 2, abort_flag)) { stop = true; break; }
-                // the smem P^T / dS^T of the previous tile must have been consumed
-                if (g > 0 && !tc::mbar_wait_warp(&bars->pds_free, (g - 1) & 1, P.err, 2, abort_flag)) { stop = true; break; }
                 // the loader's per-token metadata of this stage (acquire it directly)
-                if (!tc::mbar_wait_warp(&bars->full[s], (g / kDkvStages) & 1, P.err, 2, abort_flag)) { stop = true; break; }
-                tc::tc_fence_after();
+                if (!tc::mbar_wait_warp(&bars->full[s], (g / kDkvStages) & 1, P.err, 2, abort_flag)) {
+                    stop = true;
+                    break;
+                }
                 const float *mb = meta + s * 3 * kTM;
-#pragma unroll
-                for (int c = 0; c < 2; ++c) {                    // 16 token columns per step
-                    const int col0 = grp * 32 + c * 16;
+                for (int half = 0; half < 2; ++half, ++hs) {
+                    if (!tc::mbar_wait_warp(&bars->s_full[hs & 1], (hs >> 1) & 1, P.err, 2, abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t tb = trow + (hs & 1) * 128 + grp * 16;
                     uint32_t sv[16], dv[16];
-                    tc::tmem_ld16(trow + col0, sv);
-                    tc::tmem_ld16(trow + 128 + col0, dv);
+                    tc::tmem_ld16(tb, sv);
+                    tc::tmem_ld16(tb + kHalf, dv);
                     tc::tmem_ld_wait();
+                    const int col0 = half * kHalf + grp * 16;        // token within the tile
                     uint32_t pk[8], dk[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const int col = col0 + 2 * e;
                         const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, mb[col]) - mb[kTM + col]);
-                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) - mb[kTM + col + 1]);
+                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) -
+                                                 mb[kTM + col + 1]);
                         pk[e] = pack_bf16x2(p0, p1);
                         dk[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - mb[2 * kTM + col]),
                                             p1 * (__uint_as_float(dv[2 * e + 1]) - mb[2 * kTM + col + 1]));
                     }
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int cg = (col0 >> 3) + u;          // 16-B chunk along the token axis
-                        const uint32_t off = (cg >> 3) * (kBS * 128) + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
-                        st_shared_v4(sPT + off, pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-                        st_shared_v4(sDS + off, dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]);
-                    }
+                    // in place: these columns' S^T / dP^T values are already in registers
+                    tc::tmem_st8(tb, pk);
+                    tc::tmem_st8(tb + kHalf, dk);
+                    tc::tmem_st_wait();
+                    tc::tc_fence_before();
+                    tc::mbar_arrive(&bars->pds_full[hs & 1]);
                 }
-                tc::fence_proxy_async_smem();
-                tc::tc_fence_before();
-                tc::mbar_arrive(&bars->pds_full);
             }
             if (stop) break;
             // epilogue of the item: 16 of the 64 dK columns and 16 of the 64 dV
