@@ -409,8 +409,13 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
 // ============================================================================ dK / dV
 namespace {
 constexpr int kDkvStages = 4;
+// warp 0 loader, warp 1 S^T / dP^T MMAs (and TMEM owner), warp 2 dK / dV MMAs,
+// warps 3-18 softmax + epilogue: one thread issues a tcgen05.mma only every
+// ~100 cycles, so the two GEMM pairs get an issuing warp each.
+constexpr int kDkvThreads = 96 + kSoftThreads;
 struct DkvBars {
-    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, s_full[2], pds_full[2], acc_full, acc_free, drain;
+    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, kv_empty, s_full[2], pds_full[2], buf_free[2], acc_full,
+        acc_free, drain;
     uint32_t tmem_base;
     int abort;
     int tok[128];     // the loader's row tokens of the tile being copied
@@ -430,7 +435,7 @@ constexpr int kHalf = 64;
 }  // namespace
 
 template <bool kDoRows>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDkvThreads, 1)
 read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                         const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                         const uint16_t *__restrict__ dout,
@@ -458,13 +463,15 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             tc::mbar_init(&bars->empty[s], 1);
         }
         tc::mbar_init(&bars->kv_full, 1);
+        tc::mbar_init(&bars->kv_empty, 1);
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&bars->s_full[b], 1);
             tc::mbar_init(&bars->pds_full[b], kSoftThreads);
+            tc::mbar_init(&bars->buf_free[b], 1);
         }
         tc::mbar_init(&bars->acc_full, 1);
         tc::mbar_init(&bars->acc_free, kSoftThreads);
-        tc::mbar_init(&bars->drain, 1);
+        tc::mbar_init(&bars->drain, 2);
         bars->abort = 0;
     }
     if (warp == 1) {
@@ -511,9 +518,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             const int blk = item / (H * nsplit), h = (item / nsplit) % H, split = item % nsplit;
             const int nt = item_ntile(item);
             if (nt == 0) continue;
-            // K_b, V_b: every MMA of the previous item has completed once its
-            // accumulators were committed (acc_full)
-            if (nkv > 0 && !tc::mbar_wait_warp(&bars->acc_full, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
+            // K_b, V_b: every S^T / dP^T MMA of the previous item has completed (kv_empty)
+            if (nkv > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             if (lane == 0) {
                 tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
                 tc::tma_load_2d(sK, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
@@ -567,55 +573,73 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         if (nkv > 0) tc::mbar_wait_warp(&bars->kv_full, (nkv - 1) & 1, P.err, 2, abort_flag);
         tc::cp_async_wait_all();
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+        // ------------------------------------------------------------ S^T / dP^T MMAs
         // Per step (64 tokens of a tile): S^T = K_b Q^T and dP^T = V_b dO^T into the
-        // step's TMEM buffer, issued one step ahead so that they run while the
-        // softmax works on the previous step; then dV += P^T dO and dK += dS^T Q
-        // with P^T / dS^T read from TMEM.
+        // step's TMEM buffer, once the dK / dV MMAs of the step two before have
+        // read that buffer (buf_free); they run while the softmax works on the
+        // previous step.
         const uint32_t idesc_s = tc::idesc_bf16_f32(kBS, kHalf, false, false);
-        const uint32_t idesc_acc = tc::idesc_bf16_f32(kBS, kHD, false, true);
+        const uint64_t dk0 = tc::smem_desc_sw128(sK, 16, 1024), dv0 = tc::smem_desc_sw128(sV, 16, 1024);
         int g = 0, hs = 0, nkv = 0;       // g: tile (stage) counter, hs: step counter
         bool stop = false;
-        auto issue_s = [&](int gt, int half, int step) {
-            const uint32_t sQ = sStage + (gt % kDkvStages) * kDkvStage + half * (kHalf * 128);
-            const uint32_t sD = sQ + kRowTile;
-            const uint32_t tb = tmem + (step & 1) * 128;
-            if (lane == 0) {
-#pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk) {
-                    tc::mma_bf16_ss(tb, tc::smem_desc_sw128(sK + kk * 32, 16, 1024),
-                                    tc::smem_desc_sw128(sQ + kk * 32, 16, 1024), idesc_s, kk > 0);
-                    tc::mma_bf16_ss(tb + kHalf, tc::smem_desc_sw128(sV + kk * 32, 16, 1024),
-                                    tc::smem_desc_sw128(sD + kk * 32, 16, 1024), idesc_s, kk > 0);
-                }
-                tc::mma_commit(&bars->s_full[step & 1]);
-            }
-            __syncwarp();
-        };
-        auto wait_tile = [&](int gt) {
-            if (!tc::mbar_wait_warp(&bars->full[gt % kDkvStages], (gt / kDkvStages) & 1, P.err, 2, abort_flag))
-                return false;
-            tc::fence_proxy_async_smem();   // dO rows may have come through cp.async (generic proxy)
-            tc::tc_fence_after();
-            return true;
-        };
         for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
             const int nt = item_ntile(item);
             if (nt == 0) continue;
             if (!tc::mbar_wait_warp(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
-            if (!wait_tile(g)) break;
-            issue_s(g, 0, hs);
             for (int t = 0; t < nt && !stop; ++t, ++g) {
+                if (!tc::mbar_wait_warp(&bars->full[g % kDkvStages], (g / kDkvStages) & 1, P.err, 2, abort_flag)) {
+                    stop = true;
+                    break;
+                }
+                tc::fence_proxy_async_smem();   // dO rows may have come through cp.async (generic proxy)
+                for (int half = 0; half < 2; ++half, ++hs) {
+                    if (hs >= 2 &&
+                        !tc::mbar_wait_warp(&bars->buf_free[hs & 1], ((hs >> 1) - 1) & 1, P.err, 2, abort_flag)) {
+                        stop = true;
+                        break;
+                    }
+                    tc::tc_fence_after();
+                    const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
+                    const uint64_t dq0 = tc::smem_desc_sw128(sQ, 16, 1024);
+                    const uint64_t dd0 = tc::smem_desc_sw128(sQ + kRowTile, 16, 1024);
+                    const uint32_t tb = tmem + (hs & 1) * 128;
+                    if (lane == 0) {
+#pragma unroll
+                        for (int kk = 0; kk < kHD / 16; ++kk) {   // +32 B per K step: +2 in the address field
+                            tc::mma_bf16_ss(tb, dk0 + 2 * kk, dq0 + 2 * kk, idesc_s, kk > 0);
+                            tc::mma_bf16_ss(tb + kHalf, dv0 + 2 * kk, dd0 + 2 * kk, idesc_s, kk > 0);
+                        }
+                        tc::mma_commit(&bars->s_full[hs & 1]);
+                    }
+                    __syncwarp();
+                }
+            }
+            if (stop) break;
+            if (lane == 0) tc::mma_commit(&bars->kv_empty);   // K_b, V_b free once these complete
+            __syncwarp();
+            ++nkv;
+        }
+        if (lane == 0) tc::mma_commit(&bars->drain);
+        __syncwarp();
+        tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ dK / dV MMAs
+        // dV += P^T dO and dK += dS^T Q per step, P^T / dS^T read from TMEM.
+        const uint32_t idesc_acc = tc::idesc_bf16_f32(kBS, kHD, false, true);
+        int g = 0, hs = 0, nkv = 0;
+        bool stop = false;
+        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+            const int nt = item_ntile(item);
+            if (nt == 0) continue;
+            for (int t = 0; t < nt && !stop; ++t, ++g) {
+                // the stage's Q / dO (acquired directly; the stage is released by this warp)
+                if (!tc::mbar_wait_warp(&bars->full[g % kDkvStages], (g / kDkvStages) & 1, P.err, 2, abort_flag)) {
+                    stop = true;
+                    break;
+                }
+                tc::fence_proxy_async_smem();
                 for (int half = 0; half < 2; ++half, ++hs) {
                     const bool last = (t + 1 == nt) && half == 1;
-                    if (!last) {   // the next step's S^T / dP^T
-                        if (half == 1) {
-                            if (!wait_tile(g + 1)) { stop = true; break; }
-                            issue_s(g + 1, 0, hs + 1);
-                        } else {
-                            issue_s(g, 1, hs + 1);
-                        }
-                    }
                     if (!tc::mbar_wait_warp(&bars->pds_full[hs & 1], (hs >> 1) & 1, P.err, 2, abort_flag)) {
                         stop = true;
                         break;
@@ -628,18 +652,18 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                         break;
                     }
                     tc::tc_fence_after();
+                    const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
+                    const uint64_t bq = tc::smem_desc_sw128(sQ, 2 * kRowTile, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(sQ + kRowTile, 2 * kRowTile, 1024);
+                    const uint32_t tb = tmem + (hs & 1) * 128;
                     if (lane == 0) {
-                        const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
-                        const uint32_t sD = sQ + kRowTile;
-                        const uint32_t tb = tmem + (hs & 1) * 128;
 #pragma unroll
-                        for (int kk = 0; kk < kHalf / 16; ++kk) {
+                        for (int kk = 0; kk < kHalf / 16; ++kk) {   // +16 rows (2048 B) per K step
                             const uint32_t acc = (t > 0 || half > 0 || kk > 0) ? 1u : 0u;
-                            tc::mma_bf16_ts(tmem + 256, tb + kHalf + kk * 16,
-                                            tc::smem_desc_sw128(sQ + kk * 2048, 2 * kRowTile, 1024), idesc_acc, acc);
-                            tc::mma_bf16_ts(tmem + 320, tb + kk * 16,
-                                            tc::smem_desc_sw128(sD + kk * 2048, 2 * kRowTile, 1024), idesc_acc, acc);
+                            tc::mma_bf16_ts(tmem + 256, tb + kHalf + kk * 16, bq + 128 * kk, idesc_acc, acc);
+                            tc::mma_bf16_ts(tmem + 320, tb + kk * 16, bd + 128 * kk, idesc_acc, acc);
                         }
+                        tc::mma_commit(&bars->buf_free[hs & 1]);
                         if (half == 1) tc::mma_commit(&bars->empty[g % kDkvStages]);
                         if (last) tc::mma_commit(&bars->acc_full);
                     }
@@ -653,11 +677,11 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ P^T, dS^T, epilogue
-        // 16 warps: warp & 3 = TMEM lane quarter (slot rows), (warp-2) >> 2 = the
+        // 16 warps: warp & 3 = TMEM lane quarter (slot rows), (warp-3) >> 2 = the
         // 16-token group of a 64-token step this thread handles; no cross-thread
         // reduction.
         const int quarter = warp & 3;
-        const int grp = (warp - 2) >> 2;
+        const int grp = (warp - 3) >> 2;
         const int r = quarter * 32 + lane;                       // slot row within the block
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         int g = 0, hs = 0, nkv = 0;
@@ -763,7 +787,7 @@ static cudaError_t launch_bwd_tc_t(const CUtensorMap &mk, const CUtensorMap &mv,
     if (e != cudaSuccess) return e;
     const int nsplit = std::max(1, std::min(16, (2 * sms + nb * H - 1) / (nb * H)));
     const int items2 = nb * H * nsplit;
-    read_bwd_dkdv_tc_kernel<kDoRows><<<std::min(items2, sms), kThreads, kDkvSmem, st>>>(
+    read_bwd_dkdv_tc_kernel<kDoRows><<<std::min(items2, sms), kDkvThreads, kDkvSmem, st>>>(
         mk, mv, mq, md, dout, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2,
         P, dk_acc, dv_acc);
     count_launch();
