@@ -37,49 +37,36 @@ constexpr int kBS = 128;
 constexpr int kTM = 128;
 constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
 constexpr int kSoftThreads = kSoftWarps * 32;
-constexpr int kThreads = 64 + kSoftThreads;
 constexpr uint32_t kRowTile = kTM * kHD * 2;     // 16 KiB: 128 rows x 64 bf16
 constexpr uint32_t kTmemCols = 512;
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
-                 : "memory");
-}
-__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(addr)
-                 : "memory");
-    return v;
-}
-// byte address of 16-B chunk `cg` of row r in a [128 rows x (8 * nchunk) bf16] K-major
-// operand stored as consecutive [128 x 64] SWIZZLE_128B tiles
-__device__ __forceinline__ uint32_t kmaj_addr(uint32_t base, int r, int cg) {
-    return base + (cg >> 3) * kRowTile + r * 128 + (((cg & 7) ^ (r & 7)) << 4);
-}
-
-// set of a tile, number of live blocks
 struct DqBars {
     uint64_t full[2], empty[2], kv_full, kv_empty, s_full, ds_full, dq_full, dq_free, drain;
     uint32_t tmem_base;
     int abort;
-    int meta[2];      // per stage: blocks loaded | (K/V reload << 8); written before the stage's barrier
+    // per stage: blocks loaded | (K/V reload << 8) | (blocks of the set << 12); written
+    // before the stage's barrier
+    int meta[2];
     int tok[128];     // the loader's row tokens of the tile being copied
 };
 static_assert(sizeof(DqBars) <= 1024, "barrier block");
 constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
 constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
-constexpr uint32_t kDqP = 4 * kRowTile;                          // P / dS [128 x 256] bf16
 constexpr uint32_t kDqScratch = 2 * 2 * 4 * kTM * 4;                // [2 items][P.dP | P][4 groups][128] fp32
-constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqP + kDqScratch + 1024 + 1024;
+constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqScratch + 1024 + 1024;
+// warp 0 loader, warps 1 and 2 MMA issuers (warp 1: S, then dQ over block 0;
+// warp 2: dP, then dQ over block 1; warp 1 owns TMEM), warps 3-18 softmax.
+// TMEM: S at columns 0..255 (dS written back over it as bf16, the A operand of
+// dQ), dP at 256..511, the two dQ partial sums at 256..319 and 320..383 once
+// dP has been consumed.
+constexpr int kDqThreads = 96 + kSoftThreads;
 }  // namespace
 
 // ============================================================================ dQ
 // kDoRows: dO in plan order (one TMA box per tile, like Q); else dO in token
 // order, its rows gathered with cp.async.
 template <bool kDoRows>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kDqThreads, 1)
 read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                       const uint16_t *__restrict__ dout,
@@ -91,9 +78,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
     unsigned char *sbase = smem_raw + (base - raw);
     const uint32_t sKV = base + 2 * kDqStage;
     const uint32_t sK = sKV, sV = sKV + 2 * kRowTile;
-    const uint32_t sP = sKV + kDqKV;
-    float *sPart = reinterpret_cast<float *>(sbase + 2 * kDqStage + kDqKV + kDqP);
-    DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqP + kDqScratch);
+    float *sPart = reinterpret_cast<float *>(sbase + 2 * kDqStage + kDqKV);
+    DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqScratch);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = *P.ntiles;
@@ -106,15 +92,15 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         for (int s = 0; s < 2; ++s) {
             // the loader's arrive with the TMA bytes (+ 32 lanes' dO cp.async when gathering)
             tc::mbar_init(&bars->full[s], kDoRows ? 1 : 33);
-            tc::mbar_init(&bars->empty[s], 1);
+            tc::mbar_init(&bars->empty[s], 2);   // both MMA warps read the stage
         }
         tc::mbar_init(&bars->kv_full, 1);
-        tc::mbar_init(&bars->kv_empty, 1);
-        tc::mbar_init(&bars->s_full, 1);
+        tc::mbar_init(&bars->kv_empty, 2);   // both MMA warps
+        tc::mbar_init(&bars->s_full, 2);
         tc::mbar_init(&bars->ds_full, kSoftThreads);
-        tc::mbar_init(&bars->dq_full, 1);
+        tc::mbar_init(&bars->dq_full, 2);
         tc::mbar_init(&bars->dq_free, kSoftThreads);
-        tc::mbar_init(&bars->drain, 1);
+        tc::mbar_init(&bars->drain, 2);
         bars->abort = 0;
     }
     if (warp == 1) {
@@ -174,7 +160,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 tc::cp_async_arrive_noinc(&bars->full[s]);
             }
             if (lane == 0) {
-                bars->meta[s] = nload | (reload << 8);   // released by the arrive below
+                bars->meta[s] = nload | (reload << 8) | (nblk << 12);   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kDoRows ? 2 * kRowTile : kRowTile);
                 tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
                 if (kDoRows) tc::tma_load_2d(sD, &tmap_do, h * kHD, x0, &bars->full[s]);
@@ -200,37 +186,40 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         if (last_full >= 0) tc::mbar_wait_warp(&bars->full[last_full & 1], (last_full >> 1) & 1, P.err, 2, abort_flag);
         if (nreload > 0) tc::mbar_wait_warp(&bars->kv_full, (nreload - 1) & 1, P.err, 2, abort_flag);
         tc::cp_async_wait_all();
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        // warp 1: S = Q K^T, then dQ_0 = dS[:, block 0] K_0; warp 2: dP = dO V^T, then
+        // dQ_1 = dS[:, block 1] K_1 (dS read from TMEM). Two issuers, because one
+        // thread issues a tcgen05.mma only every ~100 cycles.
+        const bool wa = warp == 1;
         const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
+        const uint64_t bk0 = tc::smem_desc_sw128(sK + (wa ? 0 : kRowTile), 4 * kRowTile, 1024);
         int nreload = 0;
         for (int i = 0; i < nmine; ++i) {
             const int s = i & 1, j = i >> 1;
             if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
-            tc::fence_proxy_async_smem();   // Q / dO rows came through cp.async (generic proxy)
+            tc::fence_proxy_async_smem();   // dO rows may have come through cp.async (generic proxy)
             const int meta = tc::ld_shared_volatile(&bars->meta[s]);
-            const int nload = meta & 0xFF;
+            const int nload = meta & 0xFF, nblk = (meta >> 12) & 0xF;
             if ((meta >> 8) & 1) {
                 // a new (set, head) run: the previous run's K/V are free once every
-                // MMA issued so far has completed
+                // MMA this warp issued so far has completed
                 if (i > 0 && lane == 0) tc::mma_commit(&bars->kv_empty);
                 __syncwarp();
                 if (!tc::mbar_wait_warp(&bars->kv_full, nreload & 1, P.err, 2, abort_flag)) break;
                 ++nreload;
             }
-            // S and dP overwrite TMEM columns that dQ(i-1) used: wait for its epilogue
+            // S / dP overwrite TMEM columns that dQ(i-1) used: wait for its epilogue
             if (i > 0 && !tc::mbar_wait_warp(&bars->dq_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
                 const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
-                const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
+                const uint32_t sA = base + s * kDqStage + (wa ? 0 : kRowTile);   // Q or dO
+                const uint64_t da = tc::smem_desc_sw128(sA, 16, 1024);
+                const uint64_t db = tc::smem_desc_sw128(wa ? sK : sV, 16, 1024);
 #pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk) {
-                    tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sQ + kk * 32, 16, 1024),
-                                    tc::smem_desc_sw128(sK + kk * 32, 16, 1024), idesc_s, kk > 0);
-                    tc::mma_bf16_ss(tmem + 256, tc::smem_desc_sw128(sD + kk * 32, 16, 1024),
-                                    tc::smem_desc_sw128(sV + kk * 32, 16, 1024), idesc_s, kk > 0);
-                }
+                for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
+                    tc::mma_bf16_ss(tmem + (wa ? 0 : 256), da + 2 * kk, db + 2 * kk, idesc_s, kk > 0);
                 tc::mma_commit(&bars->s_full);
                 tc::mma_commit(&bars->empty[s]);
             }
@@ -238,10 +227,14 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             if (!tc::mbar_wait_warp(&bars->ds_full, i & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
-                const int ksteps = nload * (kBS / 16);
-                for (int kk = 0; kk < ksteps; ++kk)
-                    tc::mma_bf16_ss(tmem, tc::smem_desc_sw128(sP + (kk >> 2) * kRowTile + (kk & 3) * 32, 16, 1024),
-                                    tc::smem_desc_sw128(sK + kk * 2048, 4 * kRowTile, 1024), idesc_dq, kk > 0);
+                if (nblk > (wa ? 0 : 1)) {
+#pragma unroll
+                    for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
+                        const int kk = (wa ? 0 : 8) + k8;
+                        tc::mma_bf16_ts(tmem + (wa ? 256 : 320), tmem + 64 * (kk >> 2) + 8 * (kk & 3),
+                                        bk0 + 128 * k8, idesc_dq, k8 > 0);
+                    }
+                }
                 tc::mma_commit(&bars->dq_full);
             }
             __syncwarp();
@@ -251,12 +244,12 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax-backward
-        // 16 warps: warp & 3 = TMEM lane quarter (token rows), grp = (warp-2) >> 2 the
+        // 16 warps: warp & 3 = TMEM lane quarter (token rows), grp = (warp-3) >> 2 the
         // 64-column group of the 256 S / dP columns (block grp >> 1). Partial sums of
         // P*dP and P per group meet in shared memory under named barrier 1 + quarter,
         // which is also where the four warps of a quarter agree to stop on a timeout.
         const int quarter = warp & 3;
-        const int grp = (warp - 2) >> 2;
+        const int grp = (warp - 3) >> 2;
         const int jb = grp >> 1;
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
@@ -299,20 +292,22 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             // warp-uniform: the tcgen05.ld below are warp-collective. Padding rows
             // (tok < 0) have lse2 = +inf and get P = 0 from the same code.
             const bool live = jb < nblk && !dead;
-            // pass 1: P over this thread's 64 columns -> smem (bf16), partial sums
+            // pass 1: P over this thread's 64 columns, 16 at a time, written back to TMEM
+            // as bf16 over S values already read (chunk c's 16 slots packed into
+            // columns grp*64 + 8c .. +7); partial sums of P*dP and P
             float pa = 0.0f, pb = 0.0f;
             if (live) {
                 const float bj = bias - lse2;
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int col0 = grp * 64 + c * 32;
-                    uint32_t sv[32], dv[32];
-                    tc::tmem_ld32(trow + col0, sv);
-                    tc::tmem_ld32(trow + 256 + col0, dv);
+                for (int c = 0; c < 4; ++c) {
+                    const int col0 = grp * 64 + c * 16;
+                    uint32_t sv[16], dv[16];
+                    tc::tmem_ld16(trow + col0, sv);
+                    tc::tmem_ld16(trow + 256 + col0, dv);
                     tc::tmem_ld_wait();
-                    uint32_t pk[16];
+                    uint32_t pk[8];
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) {
+                    for (int e = 0; e < 8; ++e) {
                         const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj));
                         const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj));
                         pa = fmaf(p0, __uint_as_float(dv[2 * e]), pa);
@@ -320,15 +315,9 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                         pb += p0 + p1;
                         pk[e] = pack_bf16x2(p0, p1);
                     }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        st_shared_v4(kmaj_addr(sP, r, col0 / 8 + u), pk[4 * u], pk[4 * u + 1], pk[4 * u + 2],
-                                     pk[4 * u + 3]);
+                    tc::tmem_st8(trow + grp * 64 + c * 8, pk);
                 }
-            } else if (!dead && nblk == 0 && jb == 0) {
-                // empty block set: P = 0, so dS = 0 and dQ = 0
-#pragma unroll
-                for (int u = 0; u < 8; ++u) st_shared_v4(kmaj_addr(sP, r, grp * 8 + u), 0u, 0u, 0u, 0u);
+                tc::tmem_st_wait();
             }
             float *part = sPart + (i & 1) * (2 * 4 * kTM);
             part[grp * kTM + r] = pa;
@@ -336,32 +325,25 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
             const float delta = part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
-            // pass 2: dS = P (dP - delta), in place over P
+            // pass 2: dS = P (dP - delta), in place over P (the A operand of dQ)
             if (live) {
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    const int col0 = grp * 64 + c * 32;
-                    uint32_t dv[32];
-                    tc::tmem_ld32(trow + 256 + col0, dv);
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t pw[8], dv[16];
+                    tc::tmem_ld8(trow + grp * 64 + c * 8, pw);
+                    tc::tmem_ld16(trow + 256 + grp * 64 + c * 16, dv);
                     tc::tmem_ld_wait();
+                    uint32_t ow[8];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const uint32_t addr = kmaj_addr(sP, r, col0 / 8 + u);
-                        const uint4 pv = ld_shared_v4(addr);
-                        const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
-                        uint32_t ow[4];
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const float p0 = __uint_as_float(pw[w] << 16), p1 = __uint_as_float(pw[w] & 0xFFFF0000u);
-                            const int e = u * 8 + w * 2;
-                            ow[w] = pack_bf16x2(p0 * (__uint_as_float(dv[e]) - delta),
-                                                p1 * (__uint_as_float(dv[e + 1]) - delta));
-                        }
-                        st_shared_v4(addr, ow[0], ow[1], ow[2], ow[3]);
+                    for (int e = 0; e < 8; ++e) {
+                        const float p0 = __uint_as_float(pw[e] << 16), p1 = __uint_as_float(pw[e] & 0xFFFF0000u);
+                        ow[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - delta),
+                                            p1 * (__uint_as_float(dv[2 * e + 1]) - delta));
                     }
+                    tc::tmem_st8(trow + grp * 64 + c * 8, ow);
                 }
+                tc::tmem_st_wait();
             }
-            tc::fence_proxy_async_smem();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->ds_full);
             // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
@@ -376,24 +358,38 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                         atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk, fmaf(-delta, Bv[jsel], A[jsel]));
                 }
             }
-            // epilogue: 16 of the 64 dQ columns * scale -> global
+            // epilogue: 16 of the 64 dQ columns, dQ_0 + dQ_1 (the set's blocks) * scale -> global
             if (!tc::mbar_wait_warp(&bars->dq_full, i & 1, P.err, 2, abort_flag)) { dead = true; continue; }
             tc::tc_fence_after();
-            uint32_t o[16];
-            tc::tmem_ld16(trow + grp * 16, o);
-            tc::tmem_ld_wait();
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = 0.0f;
+            if (nblk > 0) {   // warp-uniform
+                uint32_t a0[16];
+                tc::tmem_ld16(trow + 256 + grp * 16, a0);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(a0[e]);
+            }
+            if (nblk > 1) {
+                uint32_t a1[16];
+                tc::tmem_ld16(trow + 320 + grp * 16, a1);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] += __uint_as_float(a1[e]);
+            }
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->dq_free);
             if (tok >= 0) {
                 uint4 v0, v1;
-                v0.x = pack_bf16x2(__uint_as_float(o[0]) * scale, __uint_as_float(o[1]) * scale);
-                v0.y = pack_bf16x2(__uint_as_float(o[2]) * scale, __uint_as_float(o[3]) * scale);
-                v0.z = pack_bf16x2(__uint_as_float(o[4]) * scale, __uint_as_float(o[5]) * scale);
-                v0.w = pack_bf16x2(__uint_as_float(o[6]) * scale, __uint_as_float(o[7]) * scale);
-                v1.x = pack_bf16x2(__uint_as_float(o[8]) * scale, __uint_as_float(o[9]) * scale);
-                v1.y = pack_bf16x2(__uint_as_float(o[10]) * scale, __uint_as_float(o[11]) * scale);
-                v1.z = pack_bf16x2(__uint_as_float(o[12]) * scale, __uint_as_float(o[13]) * scale);
-                v1.w = pack_bf16x2(__uint_as_float(o[14]) * scale, __uint_as_float(o[15]) * scale);
+                v0.x = pack_bf16x2(o[0] * scale, o[1] * scale);
+                v0.y = pack_bf16x2(o[2] * scale, o[3] * scale);
+                v0.z = pack_bf16x2(o[4] * scale, o[5] * scale);
+                v0.w = pack_bf16x2(o[6] * scale, o[7] * scale);
+                v1.x = pack_bf16x2(o[8] * scale, o[9] * scale);
+                v1.y = pack_bf16x2(o[10] * scale, o[11] * scale);
+                v1.z = pack_bf16x2(o[12] * scale, o[13] * scale);
+                v1.w = pack_bf16x2(o[14] * scale, o[15] * scale);
                 uint4 *dst = reinterpret_cast<uint4 *>(dq + tok * ld + h * kHD + grp * 16);
                 dst[0] = v0;
                 dst[1] = v1;
@@ -778,7 +774,7 @@ static cudaError_t launch_bwd_tc_t(const CUtensorMap &mk, const CUtensorMap &mv,
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
     const int grid = static_cast<int>(std::min<int64_t>(items, sms));
-    read_bwd_dq_tc_kernel<kDoRows><<<grid, kThreads, kDqSmem, st>>>(
+    read_bwd_dq_tc_kernel<kDoRows><<<grid, kDqThreads, kDqSmem, st>>>(
         mk, mv, mq, md, dout, lse, H, top, scale, scale_log2, P, static_cast<uint16_t *>(dq), dlog_gates, ws_delta);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
