@@ -410,7 +410,7 @@ constexpr int kDkvStages = 4;
 // ~100 cycles, so the two GEMM pairs get an issuing warp each.
 constexpr int kDkvThreads = 96 + kSoftThreads;
 struct DkvBars {
-    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, kv_empty, s_full[2], pds_full[2], buf_free[2], acc_full,
+    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, kv_empty, s_full[3], pds_full[3], buf_free[3], acc_full,
         acc_free, drain;
     uint32_t tmem_base;
     int abort;
@@ -422,12 +422,16 @@ constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
 constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
 constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + kDkvStages * kMetaBytes + 1024 + 1024;
 // A tile's 128 tokens go through the MMAs and the softmax in two steps of 64.
-// TMEM: step buffer b (= step & 1) at column 128*b holds S^T [128 slots x 64
+// TMEM: step buffer b (= step % 3) at column 128*b holds S^T [128 slots x 64
 // tokens] in columns +0..63 and dP^T in +64..127; the softmax overwrites them in
 // place with bf16 P^T and dS^T (softmax group g's 16 tokens packed into the first
 // 8 of its 16 columns), the A operands of dV += P^T dO and dK += dS^T Q. dK is
-// accumulated at columns 256..319, dV at 320..383.
+// accumulated at columns 384..447, dV at 448..511. Three buffers let the S^T /
+// dP^T MMAs of step s+2 run while the softmax works on step s+1 and the dK / dV
+// MMAs of step s still read their buffer.
 constexpr int kHalf = 64;
+constexpr int kBufs = 3;
+constexpr uint32_t kAccCol = 384;
 }  // namespace
 
 template <bool kDoRows>
@@ -460,7 +464,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         }
         tc::mbar_init(&bars->kv_full, 1);
         tc::mbar_init(&bars->kv_empty, 1);
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kBufs; ++b) {
             tc::mbar_init(&bars->s_full[b], 1);
             tc::mbar_init(&bars->pds_full[b], kSoftThreads);
             tc::mbar_init(&bars->buf_free[b], 1);
@@ -589,8 +593,9 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 }
                 tc::fence_proxy_async_smem();   // dO rows may have come through cp.async (generic proxy)
                 for (int half = 0; half < 2; ++half, ++hs) {
-                    if (hs >= 2 &&
-                        !tc::mbar_wait_warp(&bars->buf_free[hs & 1], ((hs >> 1) - 1) & 1, P.err, 2, abort_flag)) {
+                    const int b = hs % kBufs, use = hs / kBufs;   // buffer, and its use count
+                    if (use > 0 &&
+                        !tc::mbar_wait_warp(&bars->buf_free[b], (use - 1) & 1, P.err, 2, abort_flag)) {
                         stop = true;
                         break;
                     }
@@ -598,14 +603,14 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
                     const uint64_t dq0 = tc::smem_desc_sw128(sQ, 16, 1024);
                     const uint64_t dd0 = tc::smem_desc_sw128(sQ + kRowTile, 16, 1024);
-                    const uint32_t tb = tmem + (hs & 1) * 128;
+                    const uint32_t tb = tmem + b * 128;
                     if (lane == 0) {
 #pragma unroll
                         for (int kk = 0; kk < kHD / 16; ++kk) {   // +32 B per K step: +2 in the address field
                             tc::mma_bf16_ss(tb, dk0 + 2 * kk, dq0 + 2 * kk, idesc_s, kk > 0);
                             tc::mma_bf16_ss(tb + kHalf, dv0 + 2 * kk, dd0 + 2 * kk, idesc_s, kk > 0);
                         }
-                        tc::mma_commit(&bars->s_full[hs & 1]);
+                        tc::mma_commit(&bars->s_full[b]);
                     }
                     __syncwarp();
                 }
@@ -636,7 +641,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 tc::fence_proxy_async_smem();
                 for (int half = 0; half < 2; ++half, ++hs) {
                     const bool last = (t + 1 == nt) && half == 1;
-                    if (!tc::mbar_wait_warp(&bars->pds_full[hs & 1], (hs >> 1) & 1, P.err, 2, abort_flag)) {
+                    const int b = hs % kBufs, use = hs / kBufs;
+                    if (!tc::mbar_wait_warp(&bars->pds_full[b], use & 1, P.err, 2, abort_flag)) {
                         stop = true;
                         break;
                     }
@@ -651,15 +657,15 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
                     const uint64_t bq = tc::smem_desc_sw128(sQ, 2 * kRowTile, 1024);
                     const uint64_t bd = tc::smem_desc_sw128(sQ + kRowTile, 2 * kRowTile, 1024);
-                    const uint32_t tb = tmem + (hs & 1) * 128;
+                    const uint32_t tb = tmem + b * 128;
                     if (lane == 0) {
 #pragma unroll
                         for (int kk = 0; kk < kHalf / 16; ++kk) {   // +16 rows (2048 B) per K step
                             const uint32_t acc = (t > 0 || half > 0 || kk > 0) ? 1u : 0u;
-                            tc::mma_bf16_ts(tmem + 256, tb + kHalf + kk * 16, bq + 128 * kk, idesc_acc, acc);
-                            tc::mma_bf16_ts(tmem + 320, tb + kk * 16, bd + 128 * kk, idesc_acc, acc);
+                            tc::mma_bf16_ts(tmem + kAccCol, tb + kHalf + kk * 16, bq + 128 * kk, idesc_acc, acc);
+                            tc::mma_bf16_ts(tmem + kAccCol + kHD, tb + kk * 16, bd + 128 * kk, idesc_acc, acc);
                         }
-                        tc::mma_commit(&bars->buf_free[hs & 1]);
+                        tc::mma_commit(&bars->buf_free[b]);
                         if (half == 1) tc::mma_commit(&bars->empty[g % kDkvStages]);
                         if (last) tc::mma_commit(&bars->acc_full);
                     }
@@ -695,12 +701,13 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 }
                 const float *mb = meta + s * 3 * kTM;
                 for (int half = 0; half < 2; ++half, ++hs) {
-                    if (!tc::mbar_wait_warp(&bars->s_full[hs & 1], (hs >> 1) & 1, P.err, 2, abort_flag)) {
+                    const int b = hs % kBufs, use = hs / kBufs;
+                    if (!tc::mbar_wait_warp(&bars->s_full[b], use & 1, P.err, 2, abort_flag)) {
                         stop = true;
                         break;
                     }
                     tc::tc_fence_after();
-                    const uint32_t tb = trow + (hs & 1) * 128 + grp * 16;
+                    const uint32_t tb = trow + b * 128 + grp * 16;
                     uint32_t sv[16], dv[16];
                     tc::tmem_ld16(tb, sv);
                     tc::tmem_ld16(tb + kHalf, dv);
@@ -722,7 +729,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     tc::tmem_st8(tb + kHalf, dk);
                     tc::tmem_st_wait();
                     tc::tc_fence_before();
-                    tc::mbar_arrive(&bars->pds_full[hs & 1]);
+                    tc::mbar_arrive(&bars->pds_full[b]);
                 }
             }
             if (stop) break;
@@ -731,8 +738,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             if (!tc::mbar_wait_warp(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             uint32_t kr[16], vr[16];
-            tc::tmem_ld16(trow + 256 + grp * 16, kr);
-            tc::tmem_ld16(trow + 320 + grp * 16, vr);
+            tc::tmem_ld16(trow + kAccCol + grp * 16, kr);
+            tc::tmem_ld16(trow + kAccCol + kHD + grp * 16, vr);
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->acc_free);
