@@ -11,14 +11,16 @@
 //              boxes of 128 rows x 64); Q is read from its copy in routing-plan
 //              row order (q_rows), where a tile's rows are contiguous; tile
 //              metadata is fetched 32 items at a time (one per lane)
-//   warp 1     TMEM owner and MMA issuer (one elected lane):
-//              S[128 x 256] = Q K^T into TMEM, then O[128 x 64] = P V
-//   warps 2-17 softmax (one TMEM lane = one token row per thread; four warps per
+//   warp 1     TMEM owner; S[128 x 256] = Q K^T into TMEM, then O_0 = P[:, block 0] V_0
+//   warp 2     O_1 = P[:, block 1] V_1 (one thread issues a tcgen05.mma only every
+//              ~100 cycles: the two PV halves get an issuing warp each)
+//   warps 3-18 softmax (one TMEM lane = one token row per thread; four warps per
 //              lane quarter, 64 score columns each): row max, exp2, row sum, P as
-//              bf16 into shared memory; then the epilogue O / l -> global,
-//              log-sum-exp -> global
-// Q/K/V stages are double-buffered, O is double-buffered in TMEM, so the
-// epilogue of item i-1 and the loads of item i+1 overlap the softmax of item i.
+//              bf16 written back to TMEM over S (the A operand of PV); then the
+//              epilogue (O_0 + O_1) / l -> global, log-sum-exp -> global
+// TMEM: S at columns 0..255; O_0 / O_1 of item buffer b at 256 + 128b and
+// 320 + 128b. Q/K/V stages and O are double-buffered, so the epilogue of item
+// i-1 and the loads of item i+1 overlap the softmax of item i.
 // All waits are bounded (tc::mbar_wait); a timeout sets bit 1 of the plan's
 // error word and every role unwinds.
 #include <cudaTypedefs.h>
@@ -34,24 +36,20 @@ constexpr int kBS = 128;
 constexpr int kTM = 128;                       // token rows per tile (TMEM lanes)
 constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
 constexpr int kSoftThreads = kSoftWarps * 32;
-constexpr int kThreads = 64 + kSoftThreads;     // loader + MMA + softmax
+constexpr int kThreads = 96 + kSoftThreads;     // loader + 2 MMA issuers + softmax
 constexpr uint32_t kQBytes = kTM * kHD * 2;    // 16 KiB
 constexpr uint32_t kBlkBytes = kBS * kHD * 2;  // 16 KiB per 128-slot block of K or V
 constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) + V(2 blocks)
-// P[128 x 256] bf16 = four 16 KiB K-chunks: chunks 0-2 overlay the item's own Q, K0, K1
-// (dead once S is computed; the stage is refilled only after O(i) completed), chunk 3
-// has its own buffer.
-constexpr uint32_t kPXBytes = kTM * 64 * 2;
 constexpr uint32_t kScratchBytes = 8 * kTM * 4;   // partial row max [4][128], row sums [4][128]
-constexpr uint32_t kSmemBytes = 2 * kStageBytes + kPXBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;                // O buffers at columns 256 and 320
+constexpr uint32_t kOCol = 256;                // O_0 / O_1 of item buffer b at 256 + 128b (+64)
 
 struct Bars {
-    uint64_t full[2], empty[2], s_full, p_full, o_full[2], o_free[2], drain;
+    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full[2], o_free[2], drain;
     uint32_t tmem_base;
     int abort;
-    int nload[2];     // blocks loaded into each stage; written before the stage's barrier
+    int meta[2];      // per stage: blocks loaded | (blocks of the set << 8); written before the stage's barrier
 };
 static_assert(sizeof(Bars) <= 1024, "barrier block");
 }  // namespace
@@ -64,12 +62,9 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
-    const uint32_t sPX = base + 2 * kStageBytes;
-    float *sMax = reinterpret_cast<float *>(sbase + 2 * kStageBytes + kPXBytes);  // [4][128]
-    float *sSum = sMax + 4 * kTM;                                                   // [4][128]
-    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kPXBytes + kScratchBytes);
-    // K-chunk c of P for an item in stage s
-    auto p_chunk = [&](int s, int c) -> uint32_t { return c < 3 ? base + s * kStageBytes + c * (kTM * 128) : sPX; };
+    float *sMax = reinterpret_cast<float *>(sbase + 2 * kStageBytes);   // [4][128]
+    float *sSum = sMax + 4 * kTM;                                        // [4][128]
+    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kScratchBytes);
     volatile int *abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,13 +77,14 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     if (threadIdx.x == 0) {
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&bars->full[s], 1);
-            tc::mbar_init(&bars->empty[s], 1);
-            tc::mbar_init(&bars->o_full[s], 1);
+            tc::mbar_init(&bars->empty[s], 2);    // both MMA warps read the stage
+            tc::mbar_init(&bars->o_full[s], 2);
             tc::mbar_init(&bars->o_free[s], kSoftThreads);
         }
         tc::mbar_init(&bars->s_full, 1);
         tc::mbar_init(&bars->p_full, kSoftThreads);
-        tc::mbar_init(&bars->drain, 1);
+        tc::mbar_init(&bars->pv_done, 2);
+        tc::mbar_init(&bars->drain, 2);
         bars->abort = 0;
     }
     if (warp == 1) {
@@ -122,7 +118,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const uint32_t sK = sQ + kQBytes;
             const uint32_t sV = sK + 2 * kBlkBytes;
             if (lane == 0) {
-                bars->nload[s] = nload;   // released by the arrive below
+                bars->meta[s] = nload | (nblk << 8);   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + 2 * nload * kBlkBytes);
                 // the tile's rows x0 .. x0+127 (rows past the tile are never stored)
                 tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
@@ -140,71 +136,69 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const int i = issued - 1;
             tc::mbar_wait_warp(&bars->full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag);
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------------------ MMA issuers
+        const bool wa = warp == 1;
         const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
-        int prev_nblk = 1, prev_s = 0, count = 0;
-        bool ok = true;
-        auto issue_o = [&](int i) {   // O(i) = P V, stage of item i, buffer i & 1
-            const int b = i & 1;
-            if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) return false;
-            if (!tc::mbar_wait_warp(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) return false;
+        for (int i = 0; i < nmine; ++i) {
+            const int s = i & 1, j = i >> 1, b = i & 1;
+            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            const int meta = tc::ld_shared_volatile(&bars->meta[s]);
+            const int nload = meta & 0xFF, nblk = meta >> 8;
+            const uint32_t sQ = base + s * kStageBytes;
+            const uint32_t sK = sQ + kQBytes;
+            const uint32_t sV = sK + 2 * kBlkBytes;
+            if (wa) {
+                // S(i) overwrites P(i-1): both PV halves of item i-1 must have completed
+                if (i > 0 && !tc::mbar_wait_warp(&bars->pv_done, (i - 1) & 1, P.err, 2, abort_flag)) break;
+                tc::tc_fence_after();
+                if (lane == 0) {
+                    const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
+                    const uint64_t ad = tc::smem_desc_sw128(sQ, 16, 1024), bd = tc::smem_desc_sw128(sK, 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
+                        tc::mma_bf16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc_s, kk > 0);
+                    tc::mma_commit(&bars->s_full);
+                }
+                __syncwarp();
+            }
+            // P(i) written back to TMEM by the softmax; O buffer b read by the epilogue of i-2
+            if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
-                const uint32_t sV = base + prev_s * kStageBytes + kQBytes + 2 * kBlkBytes;
-                const int ksteps = prev_nblk * (kBS / 16);
-                for (int kk = 0; kk < ksteps; ++kk) {
-                    const uint64_t ad = tc::smem_desc_sw128(p_chunk(prev_s, kk >> 2) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(sV + kk * 2048, kBlkBytes * 2, 1024);
-                    tc::mma_bf16_ss(tmem + kOCol + b * kHD, ad, bd, idesc_o, kk > 0);
+                if (nblk > (wa ? 0 : 1)) {
+                    const uint64_t bv = tc::smem_desc_sw128(sV + (wa ? 0 : kBlkBytes), kBlkBytes * 2, 1024);
+#pragma unroll
+                    for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
+                        const int kk = (wa ? 0 : 8) + k8;
+                        tc::mma_bf16_ts(tmem + kOCol + b * 128 + (wa ? 0 : kHD), tmem + 64 * (kk >> 2) + 8 * (kk & 3),
+                                        bv + 128 * k8, idesc_o, k8 > 0);
+                    }
                 }
                 tc::mma_commit(&bars->o_full[b]);
-                tc::mma_commit(&bars->empty[prev_s]);
+                tc::mma_commit(&bars->empty[s]);
+                tc::mma_commit(&bars->pv_done);
             }
             __syncwarp();
-            return true;
-        };
-        for (int i = 0; i < nmine && ok; ++i) {
-            const int s = i & 1, j = i >> 1;
-            if (i > 0 && !issue_o(i - 1)) break;
-            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
-            const int nload = tc::ld_shared_volatile(&bars->nload[s]);
-            tc::tc_fence_after();
-            if (lane == 0) {
-                const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
-                const uint32_t sQ = base + s * kStageBytes;
-                const uint32_t sK = sQ + kQBytes;
-#pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk) {
-                    const uint64_t ad = tc::smem_desc_sw128(sQ + kk * 32, 16, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(sK + kk * 32, 16, 1024);
-                    tc::mma_bf16_ss(tmem, ad, bd, idesc_s, kk > 0);
-                }
-                tc::mma_commit(&bars->s_full);
-            }
-            __syncwarp();
-            prev_nblk = nload;
-            prev_s = s;
-            count = i + 1;
         }
-        if (count > 0 && !*abort_flag) issue_o(count - 1);
         // drain: every MMA this thread issued has completed before TMEM is freed
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
         tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
     } else {
         // ------------------------------------------------------------ softmax + epilogue
-        // 16 warps: warp & 3 is the TMEM lane quarter (hardware rule), (warp-2) >> 2
+        // 16 warps: warp & 3 is the TMEM lane quarter (hardware rule), (warp-3) >> 2
         // the 64-column group of the 256 score columns (block = group >> 1). The
         // four warps of one lane quarter exchange partial row max / sum through
         // shared memory under named barrier 1 + quarter.
         const int quarter = warp & 3;
-        const int grp = (warp - 2) >> 2;
+        const int grp = (warp - 3) >> 2;
         const int jb = grp >> 1;
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const int bar_id = 1 + quarter;
-        int prev_tok = -1, prev_h = 0, prev_row = 0;
+        int prev_tok = -1, prev_h = 0, prev_row = 0, prev_nblk = 0;
         float prev_m = 0.0f;
         float prev_l = 0.0f;
         auto epilogue = [&](int i) {
@@ -212,21 +206,35 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const float l = prev_l;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             tc::tc_fence_after();
-            uint32_t o[16];
-            tc::tmem_ld16(trow + kOCol + b * kHD + grp * 16, o);
-            tc::tmem_ld_wait();
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) o[e] = 0.0f;
+            if (prev_nblk > 0) {   // warp-uniform; O_1 holds block 1 of a two-block set
+                uint32_t a0[16];
+                tc::tmem_ld16(trow + kOCol + b * 128 + grp * 16, a0);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(a0[e]);
+            }
+            if (prev_nblk > 1) {
+                uint32_t a1[16];
+                tc::tmem_ld16(trow + kOCol + b * 128 + kHD + grp * 16, a1);
+                tc::tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] += __uint_as_float(a1[e]);
+            }
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->o_free[b]);
             if (prev_tok >= 0) {
                 uint4 v0, v1;
-                v0.x = pack_bf16x2(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
-                v0.y = pack_bf16x2(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
-                v0.z = pack_bf16x2(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
-                v0.w = pack_bf16x2(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
-                v1.x = pack_bf16x2(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
-                v1.y = pack_bf16x2(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
-                v1.z = pack_bf16x2(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
-                v1.w = pack_bf16x2(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
+                v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+                v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+                v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+                v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+                v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
+                v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
+                v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
+                v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
                 uint4 *dst = reinterpret_cast<uint4 *>(out + prev_tok * ld + prev_h * kHD + grp * 16);
                 dst[0] = v0;
                 dst[1] = v1;
@@ -287,10 +295,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 #pragma unroll
             for (int g = 1; g < 4; ++g) m = fmaxf(m, sMax[g * kTM + r]);
             const float mref = (m == -INFINITY) ? 0.0f : m;
-            // P is free once O(i-1) has consumed it
-            if (!dead && i > 0 && !tc::mbar_wait_warp(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag))
-                dead = true;
-            // pass 2: p = 2^(s*scale + bias - m) -> bf16 P (K-chunk grp), partial row sum
+            // pass 2: p = 2^(s*scale + bias - m) -> bf16 P written back to TMEM over the
+            // S values just read (columns grp*64 + 16c .. +15 for chunk c), partial row sum
             float lpart = 0.0f;
             if (live && !dead) {
                 const float bj = bias - mref;
@@ -307,29 +313,29 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                         lpart += p0 + p1;
                         pk[e] = pack_bf16x2(p0, p1);
                     }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int cw = c * 4 + u;                 // 16-B chunk within the K-chunk
-                        const uint32_t dst = p_chunk(i & 1, grp) + r * 128 + ((cw ^ (r & 7)) << 4);
-                        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(pk[4 * u]),
-                                     "r"(pk[4 * u + 1]), "r"(pk[4 * u + 2]), "r"(pk[4 * u + 3])
-                                     : "memory");
-                    }
+                    tc::tmem_st16(trow + grp * 64 + c * 16, pk);
                 }
+                tc::tmem_st_wait();
             }
             sSum[grp * kTM + r] = lpart;
-            tc::fence_proxy_async_smem();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->p_full);
             // row sums of item i complete; the four warps of this lane quarter agree
             // on stopping together
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
-            if (i > 0) epilogue(i - 1);
+            if (i > 0) {
+                if (!tc::mbar_wait_warp(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag)) {
+                    dead = true;
+                    break;
+                }
+                epilogue(i - 1);
+            }
             prev_tok = tok;
             prev_h = h;
             prev_row = cur.row;
             prev_m = m;
+            prev_nblk = nblk;
             count = i + 1;
         }
         if (count > 0 && !dead && !*abort_flag) {
