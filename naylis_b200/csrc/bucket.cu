@@ -4,9 +4,10 @@
 // selected slots (top*bs per token) instead of all L slots with a mask, as
 // the reference kernels do (mom_kernels/triton_gpu.py:98-133).
 //
-// Three launches, no host synchronisation:
+// Four launches, no host synchronisation:
 //   bucket_keys    per token: validated, sorted set -> key; per-chunk histogram
-//   bucket_scan    one CTA: key totals, offsets, tiles, per-block tile lists
+//   bucket_keyscan per key (one CTA each): offsets of the chunks within the key
+//   bucket_scan    one CTA: key bases, tiles, key sets, per-block tile lists
 //   bucket_scatter per token: stable rank inside its chunk -> permuted row,
 //                  with the row's per-block biases and the caller-order map.
 #include "common.cuh"
@@ -168,52 +169,74 @@ __device__ int block_exclusive_scan(int v, int *s_tmp, int &total) {
     return res;
 }
 
+// Per key: exclusive scan of the chunks' counts -> hist[c][k] = offset of chunk c
+// within key k's rows; keytot[k] = the key's token count.
+__global__ void __launch_bounds__(256)
+bucket_keyscan_kernel(int num_keys, int chunks, PlanView P) {
+    __shared__ int s_tmp[96];
+    const int k = blockIdx.x;
+    int carry = 0;
+    for (int c0 = 0; c0 < chunks; c0 += blockDim.x) {
+        const int c = c0 + threadIdx.x;
+        int *h = P.hist + static_cast<int64_t>(c) * num_keys + k;
+        const int v = c < chunks ? *h : 0;
+        int total;
+        const int ex = block_exclusive_scan(v, s_tmp, total);
+        if (c < chunks) *h = carry + ex;
+        carry += total;
+    }
+    if (threadIdx.x == 0) P.keytot[k] = carry;
+}
+
+// One CTA: key row bases and first tiles (scans over the keys), the tiles, each
+// key's block set, and per block the list of tiles that read it. Dynamic shared
+// memory: per key the block mask (u64), tile count and first tile.
 __global__ void __launch_bounds__(1024)
-bucket_scan_kernel(int64_t N, int nb, int top, int num_keys, int chunks, int max_tiles, PlanView P) {
+bucket_scan_kernel(int nb, int top, int num_keys, int max_tiles, PlanView P) {
+    extern __shared__ __align__(8) unsigned char s_dyn[];
+    uint64_t *s_mask = reinterpret_cast<uint64_t *>(s_dyn);
+    int *s_nt = reinterpret_cast<int *>(s_mask + num_keys);
+    int *s_tb = s_nt + num_keys;
     __shared__ int s_tmp[96];
     const int tid = threadIdx.x;
-    const int per = (num_keys + 1023) / 1024;
+    const int per = (num_keys + 1023) / 1024;          // <= kMaxKeys / 1024 = 8
     const int k0 = min(num_keys, tid * per), k1 = min(num_keys, k0 + per);
-    // key totals and per-chunk offsets (relative to the key's base for now)
     int rows = 0, tiles = 0;
     for (int k = k0; k < k1; ++k) {
-        int run = 0;
-        for (int c = 0; c < chunks; ++c) {
-            int *h = P.hist + static_cast<int64_t>(c) * num_keys + k;
-            const int n = *h;
-            *h = run;
-            run += n;
-        }
-        P.keytot[k] = run;
-        rows += run;
-        tiles += (run + kTileM - 1) / kTileM;
+        const int n = P.keytot[k];
+        s_nt[k] = (n + kTileM - 1) / kTileM;
+        rows += n;
+        tiles += s_nt[k];
     }
     int total_rows, total_tiles;
     int row_base = block_exclusive_scan(rows, s_tmp, total_rows);
     int tile_base = block_exclusive_scan(tiles, s_tmp, total_tiles);
     for (int k = k0; k < k1; ++k) {
         const int n = P.keytot[k];
+        const int nt = s_nt[k];
         P.keybase[k] = row_base;
         P.keytb[k] = tile_base;
-        for (int c = 0; c < chunks; ++c) P.hist[static_cast<int64_t>(c) * num_keys + k] += row_base;
-        const int nt = (n + kTileM - 1) / kTileM;
+        s_tb[k] = tile_base;
         for (int j = 0; j < nt; ++j)
             P.tiles[tile_base + j] = make_int4(row_base + j * kTileM, min(kTileM, n - j * kTileM), k, 0);
         row_base += n;
         tile_base += nt;
         // decode the key into its block set
-        int s = 0;
+        int sz = 0;
         uint64_t off = 0;
-        while (s < top && off + binom(nb, s) <= static_cast<uint64_t>(k)) { off += binom(nb, s); ++s; }
+        while (sz < top && off + binom(nb, sz) <= static_cast<uint64_t>(k)) { off += binom(nb, sz); ++sz; }
         uint64_t rank = static_cast<uint64_t>(k) - off;
         int *set = P.keyset + static_cast<int64_t>(k) * top;
         for (int q = top - 1; q >= 0; --q) set[q] = -1;
-        for (int q = s - 1; q >= 0; --q) {
+        uint64_t mask = 0;
+        for (int q = sz - 1; q >= 0; --q) {
             int b = q;
             while (b + 1 < nb && binom(b + 1, q + 1) <= rank) ++b;
             set[q] = b;
+            mask |= uint64_t(1) << b;
             rank -= binom(b, q + 1);
         }
+        s_mask[k] = mask;
     }
     if (tid == 0) *P.ntiles = total_tiles;
     __syncthreads();
@@ -223,13 +246,7 @@ bucket_scan_kernel(int64_t N, int nb, int top, int num_keys, int chunks, int max
         int count = 0;
         for (int kb = 0; kb < num_keys; kb += 32) {
             const int k = kb + lane;
-            int nt = 0;
-            if (k < num_keys) {
-                const int *set = P.keyset + static_cast<int64_t>(k) * top;
-                bool member = false;
-                for (int q = 0; q < top; ++q) member |= set[q] == b;
-                if (member) nt = (P.keytot[k] + kTileM - 1) / kTileM;
-            }
+            const int nt = (k < num_keys && ((s_mask[k] >> b) & 1)) ? s_nt[k] : 0;
             int incl = nt;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -237,8 +254,7 @@ bucket_scan_kernel(int64_t N, int nb, int top, int num_keys, int chunks, int max
                 if (lane >= o) incl += n;
             }
             const int base = count + incl - nt;
-            for (int j = 0; j < nt; ++j)
-                P.blktiles[static_cast<int64_t>(b) * max_tiles + base + j] = P.keytb[k] + j;
+            for (int j = 0; j < nt; ++j) P.blktiles[static_cast<int64_t>(b) * max_tiles + base + j] = s_tb[k] + j;
             count += __shfl_sync(0xffffffffu, incl, 31);
         }
         if (lane == 0) P.blkcount[b] = count;
@@ -254,11 +270,26 @@ bucket_scatter_kernel(const void *__restrict__ top_idx, int idx64, const float *
     const int64_t t = static_cast<int64_t>(blockIdx.x) * kBucketChunk + threadIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int key = t < N ? P.key[t] : -1;
+    // everything this token needs from global memory, loaded before the rank pass
+    constexpr int kMaxTopB = 8;
+    int bk[kMaxTopB];
+    float lgk[kMaxTopB];
+    int setv[kMaxTopB];
+    int base = 0;
+    if (key >= 0) {
+        base = P.hist[static_cast<int64_t>(blockIdx.x) * num_keys + key] + P.keybase[key];
+#pragma unroll
+        for (int k = 0; k < kMaxTopB; ++k) {
+            bk[k] = k < top ? load_idx(top_idx, idx64, t * top + k) : -1;
+            lgk[k] = k < top ? log_gates[t * top + k] : 0.0f;
+            setv[k] = k < top ? P.keyset[static_cast<int64_t>(key) * top + k] : -1;
+        }
+    }
     const unsigned peers = __match_any_sync(0xffffffffu, key);
     const int rank = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
     int pos = -1;
-    for (int w = 0; w < (kBucketChunk >> 5); ++w) {
+    for (int w = 0; w < (kBucketChunk >> 5); ++w) {   // warps in token order: a stable sort
         if (warp == w && key >= 0) {
             pos = s_run[key] + rank;
             __syncwarp(peers);
@@ -267,20 +298,25 @@ bucket_scatter_kernel(const void *__restrict__ top_idx, int idx64, const float *
         __syncthreads();
     }
     if (t >= N) return;
-    pos += P.hist[static_cast<int64_t>(blockIdx.x) * num_keys + key];
+    pos += base;
     P.perm[pos] = static_cast<int>(t);
-    const int *set = P.keyset + static_cast<int64_t>(key) * top;
     uint32_t kmap = 0xFFFFFFFFu;
-    for (int j = 0; j < top; ++j) P.rowbias[static_cast<int64_t>(pos) * top + j] = 0.0f;
-    for (int k = 0; k < top; ++k) {
-        const int b = load_idx(top_idx, idx64, t * top + k);
-        for (int j = 0; j < top; ++j) {
-            if (set[j] >= 0 && set[j] == b) {
-                P.rowbias[static_cast<int64_t>(pos) * top + j] += log_gates[t * top + k];
+    float bias[kMaxTopB];
+#pragma unroll
+    for (int j = 0; j < kMaxTopB; ++j) bias[j] = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kMaxTopB; ++k) {
+#pragma unroll
+        for (int j = 0; j < kMaxTopB; ++j) {
+            if (k < top && j < top && setv[j] >= 0 && setv[j] == bk[k]) {
+                bias[j] += lgk[k];
                 kmap = (kmap & ~(0xFu << (4 * k))) | (static_cast<uint32_t>(j) << (4 * k));
             }
         }
     }
+#pragma unroll
+    for (int j = 0; j < kMaxTopB; ++j)
+        if (j < top) P.rowbias[static_cast<int64_t>(pos) * top + j] = bias[j];
     P.rowkmap[pos] = kmap;
 }
 
@@ -300,8 +336,15 @@ cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates
     bucket_keys_kernel<<<static_cast<unsigned>(L.chunks), kBucketChunk, smem, st>>>(
         top_idx, idx64, L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk, P); count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    bucket_scan_kernel<<<1, 1024, 0, st>>>(L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk,
-                                           static_cast<int>(L.chunks), static_cast<int>(L.max_tiles), P); count_launch();
+    bucket_keyscan_kernel<<<nk, 256, 0, st>>>(nk, static_cast<int>(L.chunks), P); count_launch();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    const size_t scan_smem = static_cast<size_t>(nk) * 16;
+    if (scan_smem > 48 * 1024) {
+        e = cudaFuncSetAttribute(bucket_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)scan_smem);
+        if (e != cudaSuccess) return e;
+    }
+    bucket_scan_kernel<<<1, 1024, scan_smem, st>>>(static_cast<int>(L.nb), static_cast<int>(L.top), nk,
+                                                   static_cast<int>(L.max_tiles), P); count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     bucket_scatter_kernel<<<static_cast<unsigned>(L.chunks), kBucketChunk, smem, st>>>(
         top_idx, idx64, log_gates, L.N, static_cast<int>(L.nb), static_cast<int>(L.top), nk, P); count_launch();

@@ -13,7 +13,7 @@ uint64_t launches();
 
 constexpr int kTileM = 128;       // tokens per read tile (one routing set per tile)
 constexpr int kMaxKeys = 8192;    // routing sets the bucketing supports
-constexpr int kBucketChunk = 1024;
+constexpr int kBucketChunk = 256;    // tokens per bucketing chunk (one CTA)
 
 // Routing sets of size s <= top over nb blocks, ranked by the combinatorial
 // number system; key = (number of sets of smaller size) + rank.
