@@ -69,6 +69,29 @@ def test_prefix_mean_fp64_mode_dynamic_range_fallback(dtype):
     assert np.array_equal(h.numpy(), ref)
 
 
+def test_prefix_mean_fp64_mode_bf16_special_values():
+    """bf16 inputs enter the fp64 sums through their bit patterns: zeros (both
+    signs), subnormals (below 2^-126, converted), the smallest and largest
+    normals around them and sparse columns must give the sequential fp64 cumsum
+    bit for bit, whichever path (parallel or fallback) a column takes."""
+    torch.manual_seed(5)
+    x = torch.randn(2, 700, 64)
+    x[:, ::3, 0] = 0.0
+    x[:, 1::3, 1] = -0.0
+    x[:, :, 2] = 0.0
+    x[0, 10, 3] = 2.0 ** -130            # bf16 subnormal
+    x[1, 20:40, 4] = -(2.0 ** -133)      # the smallest bf16 subnormal
+    x[0, :, 5] = 2.0 ** -126             # smallest normal, all rows
+    x[1, :, 6] = torch.randn(700) * 1e-20
+    x[0, 300:, 7] = 0.0                  # a column that turns to zeros
+    x[:, :50, 8] = -0.0                  # a prefix of negative zeros (torch's CPU cumsum gives +0.0)
+    x[1, :, 9] = -0.0
+    x = x.to(torch.bfloat16)
+    h = _prefix_mean_gpu(x, "fp64")
+    ref = O.prefix_mean(x.float().numpy(), "fp64")
+    assert np.array_equal(h.numpy().view(np.uint32), ref.astype(np.float32).view(np.uint32))
+
+
 def test_prefix_mean_causality_and_bf16_output():
     torch.manual_seed(1)
     x = torch.randn(3, 700, 64)
