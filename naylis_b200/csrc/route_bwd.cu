@@ -5,9 +5,9 @@
 //             da = dlogits . Wu; dz = da * (1 - act^2)
 //   revscan   u[b,t,:] = sum_{s>=t} dz[b,s,:] / (s+1): the adjoint of the prefix
 //             mean, done in rank-r space (r = 32) instead of d-space (d = 1024)
-//   dx        dx = u . Wd                   (N x r) . (r x d)
-//   dwdown    dWd = u^T . x                 (r x N) . (N x d), split over tokens
-//   dwup      dWu = dlogits^T . act         (nb x N) . (N x r)
+//   dxdw      dx = u . Wd (N x r).(r x d) and dWd = u^T . x (r x N).(N x d) in one
+//             pass over the tokens (x read once, dx written once)
+//   (token)   also dWu = dlogits^T . act    (nb x N).(N x r), per-CTA partial sums
 //
 // Only tolerance-level parity applies to the backward, so the reverse scan is a
 // parallel chunked scan and the two rank-r GEMMs run on the tensor cores with
@@ -24,71 +24,81 @@ constexpr int kMaxRankB = 128;
 }  // namespace
 
 // ---------------------------------------------------------------- per token
+// Warp per token (a persistent grid strides over the tokens): dlogits, dz, and
+// dWu[e, j] += dlogits[t, e] * act[t, j] accumulated in a shared nb x r tile per
+// CTA, added to dw_up once per CTA.
 template <int CDT>
-__global__ void route_bwd_token_kernel(int64_t ntok, int r, int nb, int top,
-                                       const float *__restrict__ probs, const void *__restrict__ top_idx,
-                                       int idx64, const float *__restrict__ gates,
-                                       const typename Elem<CDT>::T *__restrict__ act,
-                                       const typename Elem<CDT>::T *__restrict__ w_up,
-                                       const float *__restrict__ dlog_gates,
-                                       const float *__restrict__ dgates,
-                                       const float *__restrict__ dprobs, float *__restrict__ dlogits,
-                                       float *__restrict__ dz) {
+__global__ void __launch_bounds__(256)
+route_bwd_token_kernel(int64_t ntok, int r, int nb, int top, const float *__restrict__ probs,
+                       const void *__restrict__ top_idx, int idx64, const float *__restrict__ gates,
+                       const typename Elem<CDT>::T *__restrict__ act,
+                       const typename Elem<CDT>::T *__restrict__ w_up,
+                       const float *__restrict__ dlog_gates, const float *__restrict__ dgates,
+                       const float *__restrict__ dprobs, float *__restrict__ dlogits, float *__restrict__ dz,
+                       float *__restrict__ dw_up) {
+    extern __shared__ float s_dwu[];   // [nb][r]
+    for (int i = threadIdx.x; i < nb * r; i += blockDim.x) s_dwu[i] = 0.0f;
+    __syncthreads();
     const int lane = threadIdx.x & 31;
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (t >= ntok) return;
-    float g = 0.0f, dg = 0.0f;
-    int idx = -1;
-    if (lane < top) {
-        g = gates[t * top + lane];
-        if (dlog_gates) dg += (g >= 1e-9f) ? dlog_gates[t * top + lane] / fmaxf(g, 1e-9f) : 0.0f;
-        if (dgates) dg += dgates[t * top + lane];
-        idx = idx64 ? static_cast<int>(reinterpret_cast<const int64_t *>(top_idx)[t * top + lane])
-                    : reinterpret_cast<const int32_t *>(top_idx)[t * top + lane];
-    }
-    const float sgdg = warp_sum(g * dg);
-    const float dtv = g * (dg - sgdg);
-    float sp = 0.0f;
-    if (dprobs) {
-        float part = 0.0f;
-        for (int e = lane; e < nb; e += 32) part += probs[t * nb + e] * dprobs[t * nb + e];
-        sp = warp_sum(part);
-    }
-    // Every shuffle below runs on all 32 lanes: the loops have warp-uniform
-    // trip counts and only the loads/stores are predicated.
-    float dl0 = 0.0f, dl1 = 0.0f;   // dlogits for e = lane and e = lane + 32
+    const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < ntok;
+         t += wstride) {
+        float g = 0.0f, dg = 0.0f;
+        int idx = -1;
+        if (lane < top) {
+            g = gates[t * top + lane];
+            if (dlog_gates) dg += (g >= 1e-9f) ? dlog_gates[t * top + lane] / fmaxf(g, 1e-9f) : 0.0f;
+            if (dgates) dg += dgates[t * top + lane];
+            idx = idx64 ? static_cast<int>(reinterpret_cast<const int64_t *>(top_idx)[t * top + lane])
+                        : reinterpret_cast<const int32_t *>(top_idx)[t * top + lane];
+        }
+        const float sgdg = warp_sum(g * dg);
+        const float dtv = g * (dg - sgdg);
+        float sp = 0.0f;
+        if (dprobs) {
+            float part = 0.0f;
+            for (int e = lane; e < nb; e += 32) part += probs[t * nb + e] * dprobs[t * nb + e];
+            sp = warp_sum(part);
+        }
+        // Every shuffle below runs on all 32 lanes: the loops have warp-uniform
+        // trip counts and only the loads/stores are predicated.
+        float dl0 = 0.0f, dl1 = 0.0f;   // dlogits for e = lane and e = lane + 32
 #pragma unroll
-    for (int half = 0; half < kMaxNbB / 32; ++half) {
-        const int e = half * 32 + lane;
-        float v = 0.0f;
-        for (int k = 0; k < top; ++k) {
-            const int ik = __shfl_sync(0xffffffffu, idx, k);
-            const float dk = __shfl_sync(0xffffffffu, dtv, k);
-            if (ik == e) v += dk;
-        }
-        if (e < nb) {
-            if (dprobs) {
-                const float p = probs[t * nb + e];
-                v += p * (dprobs[t * nb + e] - sp);
+        for (int half = 0; half < kMaxNbB / 32; ++half) {
+            const int e = half * 32 + lane;
+            float v = 0.0f;
+            for (int k = 0; k < top; ++k) {
+                const int ik = __shfl_sync(0xffffffffu, idx, k);
+                const float dk = __shfl_sync(0xffffffffu, dtv, k);
+                if (ik == e) v += dk;
             }
-            dlogits[t * nb + e] = v;
-        } else {
-            v = 0.0f;
+            if (e < nb) {
+                if (dprobs) {
+                    const float p = probs[t * nb + e];
+                    v += p * (dprobs[t * nb + e] - sp);
+                }
+                dlogits[t * nb + e] = v;
+            } else {
+                v = 0.0f;
+            }
+            if (half == 0) dl0 = v; else dl1 = v;
         }
-        if (half == 0) dl0 = v; else dl1 = v;
+        for (int j0 = 0; j0 < r; j0 += 32) {
+            const int j = j0 + lane;
+            const float a = j < r ? Elem<CDT>::load(act, t * r + j) : 0.0f;
+            float da = 0.0f;
+            for (int e = 0; e < nb; ++e) {
+                const float dle = __shfl_sync(0xffffffffu, e < 32 ? dl0 : dl1, e & 31);
+                if (j < r) {
+                    da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
+                    atomicAdd(&s_dwu[e * r + j], dle * a);
+                }
+            }
+            if (j < r) dz[t * r + j] = da * (1.0f - a * a);
+        }
     }
-    for (int j0 = 0; j0 < r; j0 += 32) {
-        const int j = j0 + lane;
-        float da = 0.0f;
-        for (int e = 0; e < nb; ++e) {
-            const float dle = __shfl_sync(0xffffffffu, e < 32 ? dl0 : dl1, e & 31);
-            if (j < r) da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
-        }
-        if (j < r) {
-            const float a = Elem<CDT>::load(act, t * r + j);
-            dz[t * r + j] = da * (1.0f - a * a);
-        }
-    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb * r; i += blockDim.x) atomicAdd(dw_up + i, s_dwu[i]);
 }
 
 // ---------------------------------------------------------------- reverse scan
@@ -113,12 +123,27 @@ route_bwd_revscan_kernel(const float *__restrict__ dz, float *__restrict__ u, in
     }
     s_tot[c][k] = acc;
     __syncthreads();
-    if (k == 0) {   // suffix scan over the chunks of column c
-        float run = 0.0f;
-        for (int kk = kRsChunks - 1; kk >= 0; --kk) {
-            const float v = s_tot[c][kk];
-            s_tot[c][kk] = run;   // exclusive: sum of the chunks after kk
-            run += v;
+    {   // exclusive suffix scan over the 128 chunks of a column: warp w < 8 takes
+        // column w, lane l chunks 4l .. 4l+3
+        static_assert(kRsChunks == 128 && kRsCols <= 32, "suffix-scan layout");
+        const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+        if (w < kRsCols) {
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = s_tot[w][4 * l + q];
+            const float tot = v[0] + v[1] + v[2] + v[3];
+            float incl = tot;   // sum over lanes >= l
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float n = __shfl_down_sync(0xffffffffu, incl, o);
+                if (l + o < 32) incl += n;
+            }
+            float run = incl - tot;   // the chunks after this lane's
+#pragma unroll
+            for (int q = 3; q >= 0; --q) {
+                s_tot[w][4 * l + q] = run;   // exclusive: sum of the chunks after 4l+q
+                run += v[q];
+            }
         }
     }
     __syncthreads();
@@ -138,141 +163,62 @@ __device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) 
     lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
 }
 
-// dx[t, c] (+)= sum_j u[t, j] * Wd[j, c]; CTA tile 64 tokens x 128 columns, 4 warps.
-template <int R, int DXDT>
+// dx[t, c] (+)= sum_j u[t, j] Wd[j, c] and dWd[j, c] += sum_t u[t, j] x[t, c] in one
+// pass over the tokens, so that x is read once and dx written once: CTA = 128
+// columns x kDxdwSteps steps of 64 tokens, 4 warps. Per step the u tile (bf16
+// high and residual parts) and the x tile are staged in shared memory; dx goes
+// out through a shared fp32 tile as 16-B vectors; the dWd partial sums stay in
+// registers across the steps and leave by fp32 reductions at the end.
+constexpr int kDxdwSteps = 4;
+template <int R>
+struct DxdwSmem {
+    static constexpr int kTok = 64, kCols = 128;
+    static constexpr int kUStride = R * 2 + 16, kWStride = kCols * 2 + 16, kXStride = kCols * 2 + 16;
+    static constexpr int kHalf = kCols / 2, kOS = kHalf + 4;
+    static constexpr int kU = kTok * kUStride, kW = R * kWStride, kX = kTok * kXStride, kOut = kTok * kOS * 4;
+    static constexpr int kBytes = 2 * kU + kW + kX + kOut;
+};
+
+template <int R, int XDT, int DXDT>
 __global__ void __launch_bounds__(128)
-route_bwd_dx_mma_kernel(const float *__restrict__ u, const uint16_t *__restrict__ w_down, int64_t ntok,
-                        int d, typename Elem<DXDT>::T *__restrict__ dx, int accumulate) {
-    constexpr int kTok = 64, kCols = 128;
-    constexpr int kUStride = R * 2 + 16;        // bytes per token row (padded)
-    constexpr int kWStride = kCols * 2 + 16;    // bytes per rank row (padded)
-    // one buffer: [u hi | u lo | Wd] while computing, the fp32 output tile after
-    __shared__ __align__(16) unsigned char sBuf[2 * kTok * kUStride + R * kWStride];
-    unsigned char *sUh = sBuf;
-    unsigned char *sUl = sBuf + kTok * kUStride;
-    unsigned char *sW = sBuf + 2 * kTok * kUStride;
+route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restrict__ w_down,
+                          const typename Elem<XDT>::T *__restrict__ x, int64_t ntok, int d,
+                          typename Elem<DXDT>::T *__restrict__ dx, int accumulate, float *__restrict__ dw_down) {
+    using L = DxdwSmem<R>;
+    constexpr int kTok = L::kTok, kCols = L::kCols, MT = R / 16;
+    extern __shared__ __align__(16) unsigned char smem[];
+    unsigned char *sUh = smem;
+    unsigned char *sUl = smem + L::kU;
+    unsigned char *sW = smem + 2 * L::kU;
+    unsigned char *sX = sW + L::kW;
+    float *sOut = reinterpret_cast<float *>(sX + L::kX);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int64_t tok0 = static_cast<int64_t>(blockIdx.x) * kTok;
-    const int c0 = blockIdx.y * kCols;
-    for (int i = tid; i < kTok * R; i += 128) {
-        const int tl = i / R, j = i % R;
-        const int64_t t = tok0 + tl;
-        const float val = t < ntok ? u[t * R + j] : 0.0f;
-        uint16_t hi, lo;
-        split_bf16(val, hi, lo);
-        *reinterpret_cast<uint16_t *>(sUh + tl * kUStride + j * 2) = hi;
-        *reinterpret_cast<uint16_t *>(sUl + tl * kUStride + j * 2) = lo;
-    }
+    const int c0 = blockIdx.x * kCols;
     for (int i = tid; i < R * (kCols / 8); i += 128) {
         const int j = i / (kCols / 8), ch = i % (kCols / 8);
         const int c = c0 + ch * 8;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (c < d) v = *reinterpret_cast<const uint4 *>(w_down + static_cast<int64_t>(j) * d + c);
-        *reinterpret_cast<uint4 *>(sW + j * kWStride + ch * 16) = v;
+        *reinterpret_cast<uint4 *>(sW + j * L::kWStride + ch * 16) = v;
     }
-    __syncthreads();
-    float acc[kCols / 8][4];
-#pragma unroll
-    for (int n = 0; n < kCols / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
-#pragma unroll
-    for (int ks = 0; ks < R / 16; ++ks) {
-        uint32_t ah[4], al[4];
-        const uint32_t aoff = (warp * 16 + (lane & 15)) * kUStride + (ks * 16 + (lane >> 4) * 8) * 2;
-        ldmatrix_x4(ah, smem_u32(sUh) + aoff);
-        ldmatrix_x4(al, smem_u32(sUl) + aoff);
-#pragma unroll
-        for (int p = 0; p < kCols / 16; ++p) {
-            uint32_t bfr[4];
-            const uint32_t boff = (ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kWStride +
-                                  (p * 16 + (lane >> 4) * 8) * 2;
-            ldmatrix_x4_trans(bfr, smem_u32(sW) + boff);
-            mma_bf16_16816(acc[2 * p], ah, bfr[0], bfr[1]);
-            mma_bf16_16816(acc[2 * p + 1], ah, bfr[2], bfr[3]);
-            mma_bf16_16816(acc[2 * p], al, bfr[0], bfr[1]);
-            mma_bf16_16816(acc[2 * p + 1], al, bfr[2], bfr[3]);
-        }
-    }
-    // stage the fp32 tile in shared memory (reusing the operand buffers), 64
-    // columns at a time, then write whole 16-B vectors of dx
-    float *sOut = reinterpret_cast<float *>(sBuf);               // [kTok][kHalf + 4] fp32
-    constexpr int kHalf = kCols / 2, kOS = kHalf + 4;
-    static_assert(kTok * kOS * 4 <= 2 * kTok * kUStride + R * kWStride, "staging buffer");
-    const int g = lane >> 2, q2 = (lane & 3) * 2;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-        __syncthreads();
-#pragma unroll
-        for (int n = 0; n < kHalf / 8; ++n)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int row = warp * 16 + g + h * 8;
-                sOut[row * kOS + n * 8 + q2] = acc[half * (kHalf / 8) + n][2 * h];
-                sOut[row * kOS + n * 8 + q2 + 1] = acc[half * (kHalf / 8) + n][2 * h + 1];
-            }
-        __syncthreads();
-        for (int i = threadIdx.x; i < kTok * (kHalf / 4); i += 128) {
-            const int row = i / (kHalf / 4), c4 = (i % (kHalf / 4)) * 4;
-            const int64_t t = tok0 + row;
-            const int c = c0 + half * kHalf + c4;
-            if (t >= ntok || c >= d) continue;
-            float v[4] = {sOut[row * kOS + c4], sOut[row * kOS + c4 + 1], sOut[row * kOS + c4 + 2],
-                          sOut[row * kOS + c4 + 3]};
-            if (DXDT == MOM_BF16) {
-                uint2 *p = reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(dx) + t * d + c);
-                if (accumulate) {
-                    const uint2 o = *p;
-                    v[0] += __uint_as_float(o.x << 16);
-                    v[1] += __uint_as_float(o.x & 0xFFFF0000u);
-                    v[2] += __uint_as_float(o.y << 16);
-                    v[3] += __uint_as_float(o.y & 0xFFFF0000u);
-                }
-                *p = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
-            } else {
-                float4 *p = reinterpret_cast<float4 *>(reinterpret_cast<float *>(dx) + t * d + c);
-                if (accumulate) {
-                    const float4 o = *p;
-                    v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
-                }
-                *p = make_float4(v[0], v[1], v[2], v[3]);
-            }
-        }
-    }
-}
-
-// dWd[j, c] += sum_{t in chunk} u[t, j] * x[t, c]; CTA: 128 columns x 256 tokens,
-// 4 warps x 32 columns, all R rows; fp32 atomics across token chunks.
-template <int R, int XDT>
-__global__ void __launch_bounds__(128)
-route_bwd_dwdown_mma_kernel(const float *__restrict__ u, const typename Elem<XDT>::T *__restrict__ x,
-                            int64_t ntok, int d, float *__restrict__ dw_down) {
-    constexpr int kTok = 64;                    // tokens per smem step
-    constexpr int kSteps = 4;                   // 256 tokens per CTA
-    constexpr int kCols = 128;
-    constexpr int kUStride = R * 2 + 16;
-    constexpr int kXStride = kCols * 2 + 16;
-    constexpr int MT = R / 16;
-    __shared__ __align__(16) unsigned char sUh[kTok * kUStride];
-    __shared__ __align__(16) unsigned char sUl[kTok * kUStride];
-    __shared__ __align__(16) unsigned char sX[kTok * kXStride];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c0 = blockIdx.x * kCols;
-    float acc[MT][4][4];
+    float accw[MT][4][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
-        for (int n = 0; n < 4; ++n) acc[m][n][0] = acc[m][n][1] = acc[m][n][2] = acc[m][n][3] = 0.0f;
-    for (int st = 0; st < kSteps; ++st) {
-        const int64_t tok0 = (static_cast<int64_t>(blockIdx.y) * kSteps + st) * kTok;
+        for (int n = 0; n < 4; ++n) accw[m][n][0] = accw[m][n][1] = accw[m][n][2] = accw[m][n][3] = 0.0f;
+    const int g = lane >> 2, q2 = (lane & 3) * 2;
+    for (int st = 0; st < kDxdwSteps; ++st) {
+        const int64_t tok0 = (static_cast<int64_t>(blockIdx.y) * kDxdwSteps + st) * kTok;
         if (tok0 >= ntok) break;
-        __syncthreads();
+        __syncthreads();   // the previous step's readers of sU / sX / sOut are done
         for (int i = tid; i < kTok * R; i += 128) {
             const int tl = i / R, j = i % R;
             const int64_t t = tok0 + tl;
             const float val = t < ntok ? u[t * R + j] : 0.0f;
             uint16_t hi, lo;
             split_bf16(val, hi, lo);
-            *reinterpret_cast<uint16_t *>(sUh + tl * kUStride + j * 2) = hi;
-            *reinterpret_cast<uint16_t *>(sUl + tl * kUStride + j * 2) = lo;
+            *reinterpret_cast<uint16_t *>(sUh + tl * L::kUStride + j * 2) = hi;
+            *reinterpret_cast<uint16_t *>(sUl + tl * L::kUStride + j * 2) = lo;
         }
         for (int i = tid; i < kTok * (kCols / 8); i += 128) {
             const int tl = i / (kCols / 8), ch = i % (kCols / 8);
@@ -290,36 +236,98 @@ route_bwd_dwdown_mma_kernel(const float *__restrict__ u, const typename Elem<XDT
                     v.w = pack_bf16x2(xf[6], xf[7]);
                 }
             }
-            *reinterpret_cast<uint4 *>(sX + tl * kXStride + ch * 16) = v;
+            *reinterpret_cast<uint4 *>(sX + tl * L::kXStride + ch * 16) = v;
         }
         __syncthreads();
+        // dx tile: warp = 16 tokens x 128 columns
+        float acc[kCols / 8][4];
+#pragma unroll
+        for (int n = 0; n < kCols / 8; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < R / 16; ++ks) {
+            uint32_t ah[4], al[4];
+            const uint32_t aoff = (warp * 16 + (lane & 15)) * L::kUStride + (ks * 16 + (lane >> 4) * 8) * 2;
+            ldmatrix_x4(ah, smem_u32(sUh) + aoff);
+            ldmatrix_x4(al, smem_u32(sUl) + aoff);
+#pragma unroll
+            for (int p = 0; p < kCols / 16; ++p) {
+                uint32_t bfr[4];
+                const uint32_t boff = (ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * L::kWStride +
+                                      (p * 16 + (lane >> 4) * 8) * 2;
+                ldmatrix_x4_trans(bfr, smem_u32(sW) + boff);
+                mma_bf16_16816(acc[2 * p], ah, bfr[0], bfr[1]);
+                mma_bf16_16816(acc[2 * p + 1], ah, bfr[2], bfr[3]);
+                mma_bf16_16816(acc[2 * p], al, bfr[0], bfr[1]);
+                mma_bf16_16816(acc[2 * p + 1], al, bfr[2], bfr[3]);
+            }
+        }
+        // dWd partial: warp = 32 columns x R ranks, over the step's 64 tokens
 #pragma unroll
         for (int ks = 0; ks < kTok / 16; ++ks) {
             uint32_t bfr[2][4];
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                const uint32_t boff = (ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * kXStride +
+                const uint32_t boff = (ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * L::kXStride +
                                       (warp * 32 + p * 16 + (lane >> 4) * 8) * 2;
                 ldmatrix_x4_trans(bfr[p], smem_u32(sX) + boff);
             }
 #pragma unroll
             for (int m = 0; m < MT; ++m) {
                 uint32_t ah[4], al[4];
-                const uint32_t aoff = (ks * 16 + (lane & 7) + (lane >> 4) * 8) * kUStride +
+                const uint32_t aoff = (ks * 16 + (lane & 7) + (lane >> 4) * 8) * L::kUStride +
                                       (m * 16 + ((lane >> 3) & 1) * 8) * 2;
                 ldmatrix_x4_trans(ah, smem_u32(sUh) + aoff);
                 ldmatrix_x4_trans(al, smem_u32(sUl) + aoff);
 #pragma unroll
                 for (int p = 0; p < 2; ++p) {
-                    mma_bf16_16816(acc[m][2 * p], ah, bfr[p][0], bfr[p][1]);
-                    mma_bf16_16816(acc[m][2 * p + 1], ah, bfr[p][2], bfr[p][3]);
-                    mma_bf16_16816(acc[m][2 * p], al, bfr[p][0], bfr[p][1]);
-                    mma_bf16_16816(acc[m][2 * p + 1], al, bfr[p][2], bfr[p][3]);
+                    mma_bf16_16816(accw[m][2 * p], ah, bfr[p][0], bfr[p][1]);
+                    mma_bf16_16816(accw[m][2 * p + 1], ah, bfr[p][2], bfr[p][3]);
+                    mma_bf16_16816(accw[m][2 * p], al, bfr[p][0], bfr[p][1]);
+                    mma_bf16_16816(accw[m][2 * p + 1], al, bfr[p][2], bfr[p][3]);
+                }
+            }
+        }
+        // dx out: stage the fp32 tile 64 columns at a time, then 16-B vectors
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            if (half) __syncthreads();
+#pragma unroll
+            for (int n = 0; n < L::kHalf / 8; ++n)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int row = warp * 16 + g + h * 8;
+                    sOut[row * L::kOS + n * 8 + q2] = acc[half * (L::kHalf / 8) + n][2 * h];
+                    sOut[row * L::kOS + n * 8 + q2 + 1] = acc[half * (L::kHalf / 8) + n][2 * h + 1];
+                }
+            __syncthreads();
+            for (int i = tid; i < kTok * (L::kHalf / 4); i += 128) {
+                const int row = i / (L::kHalf / 4), c4 = (i % (L::kHalf / 4)) * 4;
+                const int64_t t = tok0 + row;
+                const int c = c0 + half * L::kHalf + c4;
+                if (t >= ntok || c >= d) continue;
+                float v[4] = {sOut[row * L::kOS + c4], sOut[row * L::kOS + c4 + 1], sOut[row * L::kOS + c4 + 2],
+                              sOut[row * L::kOS + c4 + 3]};
+                if (DXDT == MOM_BF16) {
+                    uint2 *pp = reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(dx) + t * d + c);
+                    if (accumulate) {
+                        const uint2 o = *pp;
+                        v[0] += __uint_as_float(o.x << 16);
+                        v[1] += __uint_as_float(o.x & 0xFFFF0000u);
+                        v[2] += __uint_as_float(o.y << 16);
+                        v[3] += __uint_as_float(o.y & 0xFFFF0000u);
+                    }
+                    *pp = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+                } else {
+                    float4 *pp = reinterpret_cast<float4 *>(reinterpret_cast<float *>(dx) + t * d + c);
+                    if (accumulate) {
+                        const float4 o = *pp;
+                        v[0] += o.x; v[1] += o.y; v[2] += o.z; v[3] += o.w;
+                    }
+                    *pp = make_float4(v[0], v[1], v[2], v[3]);
                 }
             }
         }
     }
-    const int g = lane >> 2, q2 = (lane & 3) * 2;
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -329,7 +337,7 @@ route_bwd_dwdown_mma_kernel(const float *__restrict__ u, const typename Elem<XDT
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int j = m * 16 + g + h * 8;
-                red_add_v2(dw_down + static_cast<int64_t>(j) * d + c, acc[m][n][2 * h], acc[m][n][2 * h + 1]);
+                red_add_v2(dw_down + static_cast<int64_t>(j) * d + c, accw[m][n][2 * h], accw[m][n][2 * h + 1]);
             }
         }
 }
@@ -397,39 +405,6 @@ route_bwd_dwdown_simt_kernel(const float *__restrict__ u, const typename Elem<XD
         for (int j = jg, i = 0; j < r; j += 4, ++i) atomicAdd(dw_down + static_cast<int64_t>(j) * d + c, acc[i]);
 }
 
-// dWu[e, j] += sum_t dlogits[t, e] * act[t, j]; CTA = 256 tokens staged in smem.
-template <int CDT>
-__global__ void __launch_bounds__(256)
-route_bwd_dwup_kernel(const float *__restrict__ dlogits, const typename Elem<CDT>::T *__restrict__ act,
-                      int64_t ntok, int r, int nb, float *__restrict__ dw_up) {
-    constexpr int kT = 64;
-    __shared__ float sL[kT * kMaxNbB];
-    __shared__ float sA[kT * kMaxRankB];
-    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * 256;
-    float acc[32];
-    const int nout = nb * r;
-    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-    for (int tb = 0; tb < 256; tb += kT) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kT * nb; i += 256) {
-            const int64_t t = t0 + tb + i / nb;
-            sL[i] = t < ntok ? dlogits[t * nb + i % nb] : 0.0f;
-        }
-        for (int i = threadIdx.x; i < kT * r; i += 256) {
-            const int64_t t = t0 + tb + i / r;
-            sA[i] = t < ntok ? Elem<CDT>::load(act, t * r + i % r) : 0.0f;
-        }
-        __syncthreads();
-        for (int o = threadIdx.x, oi = 0; o < nout; o += 256, ++oi) {
-            const int e = o / r, j = o % r;
-            float a = acc[oi];
-            for (int tt = 0; tt < kT; ++tt) a = fmaf(sL[tt * nb + e], sA[tt * r + j], a);
-            acc[oi] = a;
-        }
-    }
-    for (int o = threadIdx.x, oi = 0; o < nout; o += 256, ++oi) atomicAdd(dw_up + o, acc[oi]);
-}
-
 // ---------------------------------------------------------------- launcher
 cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const void *w_down,
                              const void *w_up, int cdt, int r, int nb, int top, const float *probs,
@@ -444,15 +419,22 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
     if (ntok == 0) return cudaSuccess;
     {
         const int warps = 8;
-        const int grid = static_cast<int>((ntok + warps - 1) / warps);
+        const int grid = static_cast<int>(std::min<int64_t>((ntok + warps - 1) / warps, 2 * 148));
+        const size_t smem = sizeof(float) * nb * r;   // <= 64 x 128 floats
+        if (smem > 48 * 1024) {
+            e = cudaFuncSetAttribute(cdt == MOM_BF16 ? (const void *)route_bwd_token_kernel<MOM_BF16>
+                                                     : (const void *)route_bwd_token_kernel<MOM_F32>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+        }
         if (cdt == MOM_BF16)
-            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, 0, st>>>(
+            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, smem, st>>>(
                 ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const uint16_t *>(act),
-                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
+                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz, dw_up);
         else
-            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, 0, st>>>(
+            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, smem, st>>>(
                 ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const float *>(act),
-                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
+                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz, dw_up);
         count_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
@@ -463,29 +445,26 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
     const bool tc = cdt == MOM_BF16 && (r == 32 || r == 64) && d % 8 == 0 &&
                     (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
     if (tc) {
-        dim3 grid(static_cast<unsigned>((ntok + 63) / 64), (d + 127) / 128);
-#define MOM_DX_TC(R, X)                                                                              \
-    if (r == R && dxdt == X)                                                                         \
-        route_bwd_dx_mma_kernel<R, X><<<grid, 128, 0, st>>>(ws_u, static_cast<const uint16_t *>(w_down), \
-                                                            ntok, d, static_cast<typename Elem<X>::T *>(dx), \
-                                                            accumulate);
-        MOM_DX_TC(32, MOM_BF16)
-        MOM_DX_TC(32, MOM_F32)
-        MOM_DX_TC(64, MOM_BF16)
-        MOM_DX_TC(64, MOM_F32)
-#undef MOM_DX_TC
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        dim3 grid2((d + 127) / 128, static_cast<unsigned>((ntok + 255) / 256));
-#define MOM_DW_TC(R, X)                                                                              \
-    if (r == R && xdt == X)                                                                          \
-        route_bwd_dwdown_mma_kernel<R, X><<<grid2, 128, 0, st>>>(                                    \
-            ws_u, static_cast<const typename Elem<X>::T *>(x), ntok, d, dw_down);
-        MOM_DW_TC(32, MOM_BF16)
-        MOM_DW_TC(32, MOM_F32)
-        MOM_DW_TC(64, MOM_BF16)
-        MOM_DW_TC(64, MOM_F32)
-#undef MOM_DW_TC
+        dim3 grid((d + 127) / 128, static_cast<unsigned>((ntok + 64 * kDxdwSteps - 1) / (64 * kDxdwSteps)));
+#define MOM_DXDW(R, X, D)                                                                                   \
+    if (r == R && xdt == X && dxdt == D) {                                                                 \
+        const int smem = DxdwSmem<R>::kBytes;                                                               \
+        e = cudaFuncSetAttribute(route_bwd_dxdw_mma_kernel<R, X, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                 smem);                                                                     \
+        if (e != cudaSuccess) return e;                                                                     \
+        route_bwd_dxdw_mma_kernel<R, X, D><<<grid, 128, smem, st>>>(                                        \
+            ws_u, static_cast<const uint16_t *>(w_down), static_cast<const typename Elem<X>::T *>(x), ntok, d, \
+            static_cast<typename Elem<D>::T *>(dx), accumulate, dw_down);                                  \
+    }
+        MOM_DXDW(32, MOM_BF16, MOM_BF16)
+        MOM_DXDW(32, MOM_BF16, MOM_F32)
+        MOM_DXDW(32, MOM_F32, MOM_BF16)
+        MOM_DXDW(32, MOM_F32, MOM_F32)
+        MOM_DXDW(64, MOM_BF16, MOM_BF16)
+        MOM_DXDW(64, MOM_BF16, MOM_F32)
+        MOM_DXDW(64, MOM_F32, MOM_BF16)
+        MOM_DXDW(64, MOM_F32, MOM_F32)
+#undef MOM_DXDW
         count_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     } else {
@@ -509,17 +488,6 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
         else
             route_bwd_dwdown_simt_kernel<MOM_F32><<<grid2, 256, 0, st>>>(
                 ws_u, static_cast<const float *>(x), ntok, d, r, dw_down);
-        count_launch();
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    }
-    {
-        const int grid = static_cast<int>((ntok + 255) / 256);
-        if (cdt == MOM_BF16)
-            route_bwd_dwup_kernel<MOM_BF16><<<grid, 256, 0, st>>>(
-                ws_dlogits, static_cast<const uint16_t *>(act), ntok, r, nb, dw_up);
-        else
-            route_bwd_dwup_kernel<MOM_F32><<<grid, 256, 0, st>>>(
-                ws_dlogits, static_cast<const float *>(act), ntok, r, nb, dw_up);
         count_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
