@@ -7,7 +7,7 @@
 //             mean, done in rank-r space (r = 32) instead of d-space (d = 1024)
 //   dxdw      dx = u . Wd (N x r).(r x d) and dWd = u^T . x (r x N).(N x d) in one
 //             pass over the tokens (x read once, dx written once)
-//   (token)   also dWu = dlogits^T . act    (nb x N).(N x r), per-CTA partial sums
+//   dwup      dWu = dlogits^T . act         (nb x N) . (N x r), per-CTA partial sums
 //
 // Only tolerance-level parity applies to the backward, so the reverse scan is a
 // parallel chunked scan and the two rank-r GEMMs run on the tensor cores with
@@ -24,9 +24,7 @@ constexpr int kMaxRankB = 128;
 }  // namespace
 
 // ---------------------------------------------------------------- per token
-// Warp per token (a persistent grid strides over the tokens): dlogits, dz, and
-// dWu[e, j] += dlogits[t, e] * act[t, j] accumulated in a shared nb x r tile per
-// CTA, added to dw_up once per CTA.
+// Warp per token: dlogits and dz.
 template <int CDT>
 __global__ void __launch_bounds__(256)
 route_bwd_token_kernel(int64_t ntok, int r, int nb, int top, const float *__restrict__ probs,
@@ -34,15 +32,11 @@ route_bwd_token_kernel(int64_t ntok, int r, int nb, int top, const float *__rest
                        const typename Elem<CDT>::T *__restrict__ act,
                        const typename Elem<CDT>::T *__restrict__ w_up,
                        const float *__restrict__ dlog_gates, const float *__restrict__ dgates,
-                       const float *__restrict__ dprobs, float *__restrict__ dlogits, float *__restrict__ dz,
-                       float *__restrict__ dw_up) {
-    extern __shared__ float s_dwu[];   // [nb][r]
-    for (int i = threadIdx.x; i < nb * r; i += blockDim.x) s_dwu[i] = 0.0f;
-    __syncthreads();
+                       const float *__restrict__ dprobs, float *__restrict__ dlogits, float *__restrict__ dz) {
     const int lane = threadIdx.x & 31;
-    const int64_t wstride = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < ntok;
-         t += wstride) {
+    {
+        const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (t >= ntok) return;
         float g = 0.0f, dg = 0.0f;
         int idx = -1;
         if (lane < top) {
@@ -89,16 +83,68 @@ route_bwd_token_kernel(int64_t ntok, int r, int nb, int top, const float *__rest
             float da = 0.0f;
             for (int e = 0; e < nb; ++e) {
                 const float dle = __shfl_sync(0xffffffffu, e < 32 ? dl0 : dl1, e & 31);
-                if (j < r) {
-                    da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
-                    atomicAdd(&s_dwu[e * r + j], dle * a);
-                }
+                if (j < r) da = fmaf(dle, Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), da);
             }
             if (j < r) dz[t * r + j] = da * (1.0f - a * a);
         }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < nb * r; i += blockDim.x) atomicAdd(dw_up + i, s_dwu[i]);
+}
+
+// dWu[e, j] += sum_t dlogits[t, e] * act[t, j]: warp = a run of tokens with its
+// partial sums in registers (lane j, all e), 4 tokens' loads in flight at a
+// time; the CTA's 8 warps meet in shared memory, one reduction per CTA.
+template <int CDT, int NB>
+__global__ void __launch_bounds__(256)
+route_bwd_dwup_kernel(const float *__restrict__ dlogits, const typename Elem<CDT>::T *__restrict__ act,
+                      int64_t ntok, int r, int nb, int64_t per_warp, float *__restrict__ dw_up) {
+    __shared__ float s_acc[8][NB][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + warp;
+    const int64_t t0 = gw * per_warp, t1 = min(ntok, t0 + per_warp);
+    for (int j0 = 0; j0 < r; j0 += 32) {
+        const int j = j0 + lane;
+        float acc[NB];
+#pragma unroll
+        for (int e = 0; e < NB; ++e) acc[e] = 0.0f;
+        for (int64_t t = t0; t < t1; t += 4) {
+            float a[4], dl[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool ok = t + u < t1;
+                a[u] = (ok && j < r) ? Elem<CDT>::load(act, (t + u) * r + j) : 0.0f;
+                dl[u] = (ok && lane < nb) ? dlogits[(t + u) * nb + lane] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int e = 0; e < NB; ++e) acc[e] = fmaf(__shfl_sync(0xffffffffu, dl[u], e), a[u], acc[e]);
+        }
+#pragma unroll
+        for (int e = 0; e < NB; ++e) s_acc[warp][e][lane] = acc[e];
+        __syncthreads();
+        for (int i = threadIdx.x; i < NB * 32; i += 256) {
+            const int e = i / 32, jj = i % 32;
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) v += s_acc[w][e][jj];
+            if (e < nb && j0 + jj < r) atomicAdd(dw_up + e * r + j0 + jj, v);
+        }
+        __syncthreads();
+    }
+}
+
+// General (nb > 16) dWu: thread per output element over a token range.
+template <int CDT>
+__global__ void __launch_bounds__(256)
+route_bwd_dwup_any_kernel(const float *__restrict__ dlogits, const typename Elem<CDT>::T *__restrict__ act,
+                          int64_t ntok, int r, int nb, int64_t per_cta, float *__restrict__ dw_up) {
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * per_cta, t1 = min(ntok, t0 + per_cta);
+    for (int o = blockIdx.x * 256 + threadIdx.x; o < nb * r; o += gridDim.x * 256) {
+        const int e = o / r, j = o % r;
+        float acc = 0.0f;
+        for (int64_t t = t0; t < t1; ++t) acc = fmaf(dlogits[t * nb + e], Elem<CDT>::load(act, t * r + j), acc);
+        atomicAdd(dw_up + o, acc);
+    }
 }
 
 // ---------------------------------------------------------------- reverse scan
@@ -419,22 +465,42 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
     if (ntok == 0) return cudaSuccess;
     {
         const int warps = 8;
-        const int grid = static_cast<int>(std::min<int64_t>((ntok + warps - 1) / warps, 2 * 148));
-        const size_t smem = sizeof(float) * nb * r;   // <= 64 x 128 floats
-        if (smem > 48 * 1024) {
-            e = cudaFuncSetAttribute(cdt == MOM_BF16 ? (const void *)route_bwd_token_kernel<MOM_BF16>
-                                                     : (const void *)route_bwd_token_kernel<MOM_F32>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return e;
-        }
+        const int grid = static_cast<int>((ntok + warps - 1) / warps);
         if (cdt == MOM_BF16)
-            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, smem, st>>>(
+            route_bwd_token_kernel<MOM_BF16><<<grid, warps * 32, 0, st>>>(
                 ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const uint16_t *>(act),
-                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz, dw_up);
+                static_cast<const uint16_t *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
         else
-            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, smem, st>>>(
+            route_bwd_token_kernel<MOM_F32><<<grid, warps * 32, 0, st>>>(
                 ntok, r, nb, top, probs, top_idx, idx64, gates, static_cast<const float *>(act),
-                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz, dw_up);
+                static_cast<const float *>(w_up), dlog_gates, dgates, dprobs, ws_dlogits, ws_dz);
+        count_launch();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    {   // dWu = dlogits^T act
+        const int64_t nwarps = 148 * 8;
+        const int64_t per_warp = std::max<int64_t>(4, (ntok + nwarps - 1) / nwarps);
+        const int grid = static_cast<int>((ntok + per_warp * 8 - 1) / (per_warp * 8));
+#define MOM_DWUP(NBV)                                                                                      \
+    if (nb <= NBV) {                                                                                       \
+        if (cdt == MOM_BF16)                                                                               \
+            route_bwd_dwup_kernel<MOM_BF16, NBV><<<grid, 256, 0, st>>>(                                     \
+                ws_dlogits, static_cast<const uint16_t *>(act), ntok, r, nb, per_warp, dw_up);             \
+        else                                                                                               \
+            route_bwd_dwup_kernel<MOM_F32, NBV><<<grid, 256, 0, st>>>(                                      \
+                ws_dlogits, static_cast<const float *>(act), ntok, r, nb, per_warp, dw_up);                \
+    } else
+        MOM_DWUP(8) MOM_DWUP(16) {
+            const int64_t per_cta = 256;
+            dim3 g2((nb * r + 255) / 256, static_cast<unsigned>((ntok + per_cta - 1) / per_cta));
+            if (cdt == MOM_BF16)
+                route_bwd_dwup_any_kernel<MOM_BF16><<<g2, 256, 0, st>>>(
+                    ws_dlogits, static_cast<const uint16_t *>(act), ntok, r, nb, per_cta, dw_up);
+            else
+                route_bwd_dwup_any_kernel<MOM_F32><<<g2, 256, 0, st>>>(
+                    ws_dlogits, static_cast<const float *>(act), ntok, r, nb, per_cta, dw_up);
+        }
+#undef MOM_DWUP
         count_launch();
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }

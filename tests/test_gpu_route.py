@@ -178,9 +178,12 @@ def test_router_noise_goes_into_topk_only():
 
 
 @pytest.mark.parametrize("compute,tol", [("f32", 1e-5), ("bf16", 2e-2)])
-def test_router_backward_matches_oracle(compute, tol):
+@pytest.mark.parametrize("r,nb,top", [(32, 8, 2), (64, 16, 2), (16, 32, 3)])
+def test_router_backward_matches_oracle(compute, tol, r, nb, top):
+    # (32, 8): config 2; (64, 16): rank-64 tensor-core pass, 16-block dW_up;
+    # (16, 32): rank 16 (SIMT dx / dW_down), more blocks than the register dW_up holds
     torch.manual_seed(7)
-    B, S, d, r, nb, top = 2, 384, 256, 32, 8, 2
+    B, S, d = 2, 384, 256
     cd = torch.bfloat16 if compute == "bf16" else torch.float32
     x = torch.randn(B, S, d).to(cd)
     w_down = torch.randn(r, d) * 0.05
