@@ -147,13 +147,17 @@ def run_gpu(args):
     holder.layer = layer
     holder.M = M
     use_graph = not args.no_graph
-    # under a CUDA graph the bucket all-reduces run after each replay (no
-    # collective inside the captured backward)
-    dp = GradAllReduce(holder, overlap=not use_graph) if world > 1 else None
+    # Data parallel: bucketed all-reduces launched from the backward's hooks
+    # (overlapping it) when eager; under a CUDA graph they run after each replay
+    # (measured faster than capturing them with the backward, --dp-in-graph: the
+    # NCCL kernels then share the SMs with the persistent read kernels).
+    dp_in_graph = use_graph and args.dp_in_graph
+    dp = (GradAllReduce(holder, bucket_mb=args.bucket_mb, overlap=(not use_graph) or dp_in_graph)
+          if world > 1 else None)
     mk.resolve_mode(dev, torch.bfloat16, head_dim=c["d"] // c["H"])
     lib = _lib.load()
 
-    def body(xin, gin):
+    def body(xin, gin, with_exchange=False):
         if dp is not None:
             dp.zero_grad()
         else:
@@ -163,6 +167,8 @@ def run_gpu(args):
         with torch.autocast("cuda", dtype=torch.bfloat16):
             out = layer(xin, M)
         out.backward(gin)
+        if with_exchange and dp is not None:
+            dp.finish()
 
     def step(xin, gin):
         body(xin, gin)
@@ -178,19 +184,19 @@ def run_gpu(args):
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(3):
-                body(x, dout)
+                body(x, dout, with_exchange=True)
         torch.cuda.current_stream().wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         l0 = lib.mom_kernel_launches()
         with torch.cuda.graph(graph):
-            body(x, dout)
+            body(x, dout, with_exchange=dp_in_graph)
         launches_per_replay = lib.mom_kernel_launches() - l0
 
         def step(xin, gin):
             assert xin is x and gin is dout, "the graphed step reads the static x / dout"
             graph.replay()
-            if dp is not None:
+            if dp is not None and not dp_in_graph:
                 dp.finish()
 
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)   # 256 MiB > L2
@@ -260,7 +266,9 @@ def run_gpu(args):
             "config": {"workload": WORKLOAD, "global_batch": c["B"] * world, "seq_len": c["S"],
                        "parallelism": f"dp{world}", "l2": "flushed between timed steps (256 MiB write, untimed)",
                        "cuda_graph": ("fwd+bwd captured once, replayed per step"
-                                      + ("; bucket all-reduce after replay" if world > 1 else ""))
+                                      + (("; bucket all-reduces captured with the backward"
+                                          if dp_in_graph else "; bucket all-reduce after replay")
+                                         if world > 1 else ""))
                        if graph is not None else "off (eager launches)"},
             "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
                          "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
@@ -478,6 +486,9 @@ def main():
     ap.add_argument("--cpu-samples", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step eagerly, no CUDA graph")
+    ap.add_argument("--dp-in-graph", action="store_true",
+                    help="N>1 with a graph: capture the bucket all-reduces with the backward")
+    ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
