@@ -16,11 +16,12 @@
 //              ~100 cycles: the two PV halves get an issuing warp each)
 //   warps 3-18 softmax (one TMEM lane = one token row per thread; four warps per
 //              lane quarter, 64 score columns each): row max, exp2, row sum, P as
-//              bf16 written back to TMEM over S (the A operand of PV); then the
-//              epilogue (O_0 + O_1) / l -> global, log-sum-exp -> global
-// TMEM: S at columns 0..255; O_0 / O_1 of item buffer b at 256 + 128b and
-// 320 + 128b. Q/K/V stages and O are double-buffered, so the epilogue of item
-// i-1 and the loads of item i+1 overlap the softmax of item i.
+//              bf16 into TMEM (the A operand of PV); then the epilogue
+//              (O_0 + O_1) / l -> global, log-sum-exp -> global
+// TMEM: S at columns 0..255, P (bf16 pairs) at 256..383, O_0 / O_1 at 384 / 448.
+// P has its own columns so that S(i+1) is issued as soon as the softmax has read
+// S(i), overlapping PV(i); the softmax writes P(i+1) once PV(i) is done
+// (pv_done), PV(i+1) writes O once the epilogue has read O(i) (o_free).
 // All waits are bounded (tc::mbar_wait); a timeout sets bit 1 of the plan's
 // error word and every role unwinds.
 #include <cudaTypedefs.h>
@@ -43,10 +44,11 @@ constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) +
 constexpr uint32_t kScratchBytes = 8 * kTM * 4;   // partial row max [4][128], row sums [4][128]
 constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;                // O_0 / O_1 of item buffer b at 256 + 128b (+64)
+constexpr uint32_t kPCol = 256;                // P: group g's 64 slots at 256 + 32g (bf16 pairs)
+constexpr uint32_t kOCol = 384;                // O_0 at 384, O_1 at 448
 
 struct Bars {
-    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full[2], o_free[2], drain;
+    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full, o_free, drain;
     uint32_t tmem_base;
     int abort;
     int meta[2];      // per stage: blocks loaded | (blocks of the set << 8); written before the stage's barrier
@@ -78,9 +80,9 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         for (int s = 0; s < 2; ++s) {
             tc::mbar_init(&bars->full[s], 1);
             tc::mbar_init(&bars->empty[s], 2);    // both MMA warps read the stage
-            tc::mbar_init(&bars->o_full[s], 2);
-            tc::mbar_init(&bars->o_free[s], kSoftThreads);
         }
+        tc::mbar_init(&bars->o_full, 2);
+        tc::mbar_init(&bars->o_free, kSoftThreads);
         tc::mbar_init(&bars->s_full, 1);
         tc::mbar_init(&bars->p_full, kSoftThreads);
         tc::mbar_init(&bars->pv_done, 2);
@@ -141,7 +143,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         const bool wa = warp == 1;
         const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
         for (int i = 0; i < nmine; ++i) {
-            const int s = i & 1, j = i >> 1, b = i & 1;
+            const int s = i & 1, j = i >> 1;
             if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
             const int meta = tc::ld_shared_volatile(&bars->meta[s]);
             const int nload = meta & 0xFF, nblk = meta >> 8;
@@ -149,8 +151,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const uint32_t sK = sQ + kQBytes;
             const uint32_t sV = sK + 2 * kBlkBytes;
             if (wa) {
-                // S(i) overwrites P(i-1): both PV halves of item i-1 must have completed
-                if (i > 0 && !tc::mbar_wait_warp(&bars->pv_done, (i - 1) & 1, P.err, 2, abort_flag)) break;
+                // S(i) overwrites S(i-1), which the softmax has read once P(i-1) was posted
+                // (p_full of i-1, waited below in the previous iteration)
                 tc::tc_fence_after();
                 if (lane == 0) {
                     const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
@@ -162,9 +164,9 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 }
                 __syncwarp();
             }
-            // P(i) written back to TMEM by the softmax; O buffer b read by the epilogue of i-2
+            // P(i) written to TMEM by the softmax; O read by the epilogue of i-1
             if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
-            if (!tc::mbar_wait_warp(&bars->o_free[b], ((i >> 1) & 1) ^ 1, P.err, 2, abort_flag)) break;
+            if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
                 if (nblk > (wa ? 0 : 1)) {
@@ -172,11 +174,11 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 #pragma unroll
                     for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
                         const int kk = (wa ? 0 : 8) + k8;
-                        tc::mma_bf16_ts(tmem + kOCol + b * 128 + (wa ? 0 : kHD), tmem + 64 * (kk >> 2) + 8 * (kk & 3),
+                        tc::mma_bf16_ts(tmem + kOCol + (wa ? 0 : kHD), tmem + kPCol + 32 * (kk >> 2) + 8 * (kk & 3),
                                         bv + 128 * k8, idesc_o, k8 > 0);
                     }
                 }
-                tc::mma_commit(&bars->o_full[b]);
+                tc::mma_commit(&bars->o_full);
                 tc::mma_commit(&bars->empty[s]);
                 tc::mma_commit(&bars->pv_done);
             }
@@ -202,7 +204,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         float prev_m = 0.0f;
         float prev_l = 0.0f;
         auto epilogue = [&](int i) {
-            const int b = i & 1;
+            (void)i;
             const float l = prev_l;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             tc::tc_fence_after();
@@ -211,20 +213,20 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             for (int e = 0; e < 16; ++e) o[e] = 0.0f;
             if (prev_nblk > 0) {   // warp-uniform; O_1 holds block 1 of a two-block set
                 uint32_t a0[16];
-                tc::tmem_ld16(trow + kOCol + b * 128 + grp * 16, a0);
+                tc::tmem_ld16(trow + kOCol + grp * 16, a0);
                 tc::tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(a0[e]);
             }
             if (prev_nblk > 1) {
                 uint32_t a1[16];
-                tc::tmem_ld16(trow + kOCol + b * 128 + kHD + grp * 16, a1);
+                tc::tmem_ld16(trow + kOCol + kHD + grp * 16, a1);
                 tc::tmem_ld_wait();
 #pragma unroll
                 for (int e = 0; e < 16; ++e) o[e] += __uint_as_float(a1[e]);
             }
             tc::tc_fence_before();
-            tc::mbar_arrive(&bars->o_free[b]);
+            tc::mbar_arrive(&bars->o_free);
             if (prev_tok >= 0) {
                 uint4 v0, v1;
                 v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
@@ -295,8 +297,12 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 #pragma unroll
             for (int g = 1; g < 4; ++g) m = fmaxf(m, sMax[g * kTM + r]);
             const float mref = (m == -INFINITY) ? 0.0f : m;
-            // pass 2: p = 2^(s*scale + bias - m) -> bf16 P written back to TMEM over the
-            // S values just read (columns grp*64 + 16c .. +15 for chunk c), partial row sum
+            // P(i-1) must have been consumed by PV(i-1) before P(i) overwrites it
+            if (!dead && i > 0 && !tc::mbar_wait_warp(&bars->pv_done, (i - 1) & 1, P.err, 2, abort_flag))
+                dead = true;
+            tc::tc_fence_after();
+            // pass 2: p = 2^(s*scale + bias - m) -> bf16 P into TMEM (group grp's 64 slots
+            // at kPCol + 32*grp, chunk c at +16c), partial row sum
             float lpart = 0.0f;
             if (live && !dead) {
                 const float bj = bias - mref;
@@ -313,7 +319,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                         lpart += p0 + p1;
                         pk[e] = pack_bf16x2(p0, p1);
                     }
-                    tc::tmem_st16(trow + grp * 64 + c * 16, pk);
+                    tc::tmem_st16(trow + kPCol + grp * 32 + c * 16, pk);
                 }
                 tc::tmem_st_wait();
             }
@@ -325,7 +331,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
             if (i > 0) {
-                if (!tc::mbar_wait_warp(&bars->o_full[(i - 1) & 1], ((i - 1) >> 1) & 1, P.err, 2, abort_flag)) {
+                if (!tc::mbar_wait_warp(&bars->o_full, (i - 1) & 1, P.err, 2, abort_flag)) {
                     dead = true;
                     break;
                 }
@@ -341,7 +347,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         if (count > 0 && !dead && !*abort_flag) {
             const int i = count - 1;
             prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
-            if (tc::mbar_wait_warp(&bars->o_full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag)) epilogue(i);
+            if (tc::mbar_wait_warp(&bars->o_full, i & 1, P.err, 2, abort_flag)) epilogue(i);
         }
     }
     tc::tc_fence_before();
