@@ -346,8 +346,9 @@ int check_read_bwd_args(int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, 
     MOM_REQUIRE(k && v && dk_acc && dv_acc, "null pointer argument");
     MOM_REQUIRE(B * S == 0 || (q && out && dout && lse && plan && q_rows && dq && dlog_gates),
                 "null pointer argument");
-    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(dout) & 15) == 0,
-                "q_rows and dout must be 16-byte aligned");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(dout) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                "q_rows, out and dout must be 16-byte aligned");
     return MOM_OK;
 }
 }  // namespace

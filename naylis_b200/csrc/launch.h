@@ -67,6 +67,10 @@ cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates
 // Row copy into routing-plan order: dst[r] = src[perm[r]] (rows of row_bytes, a multiple of 16).
 cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, const int *perm, void *dst,
                                 cudaStream_t st);
+// delta[h][r] = <dO, O> of plan row r's token and head h (fp32), dO's row copied to
+// do_rows[r] when do_rows is not null.
+cudaError_t launch_row_delta(const void *dout, const void *out, int64_t N, int H, int hd, const int *perm,
+                             void *do_rows, float *delta, cudaStream_t st);
 // Read forward. q is token-ordered; q_rows (N x H*hd, same dtype) receives q in
 // plan order and is what the tensor-core kernels (and the backward) read.
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,

@@ -489,13 +489,12 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
     // tensor-core kernels for head_dim 64, 128-slot blocks, top <= 2; other
     // geometries take the warp-level mma kernels below
     if (read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H)) {
-        if (do_rows) {   // dO in plan order: every tile's rows are one TMA box
-            if ((e = launch_permute_rows(dout, N, static_cast<int64_t>(H) * hd * 2, P.perm, do_rows, st)) !=
-                cudaSuccess)
-                return e;
+        // delta = <dO, O> per plan row and head, and dO in plan order when there is
+        // room for it (every tile's rows are then one TMA box)
+        if ((e = launch_row_delta(dout, out, N, H, hd, P.perm, do_rows, ws_delta, st)) != cudaSuccess) return e;
+        if (do_rows)
             return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                       dlog_gates, ws_delta, st);
-        }
         return launch_read_bwd_tc(q_rows, k, v, dout, false, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                   dlog_gates, ws_delta, st);
     }

@@ -257,7 +257,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         bool dead = false;
         // per-item row metadata: tile fields 32 items at a time (one per lane),
         // this thread's row (token, bias, lse, caller-slot map) one item ahead
-        struct Meta { int x, nblk, h, tok; float bias, lse2; uint32_t kmap; };
+        struct Meta { int x, nblk, h, tok; float bias, lse2, dlt; uint32_t kmap; };
         tc::LaneTile lt;
         int mh = 0;
         auto fetch = [&](int src, Meta &m) {
@@ -269,6 +269,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             m.tok = in ? P.perm[m.x + r] : -1;
             m.bias = (in && jb < m.nblk) ? P.rowbias[static_cast<int64_t>(m.x + r) * top + jb] * kLog2e : 0.0f;
             m.lse2 = in ? lse[static_cast<int64_t>(m.h) * P.n + m.x + r] * kLog2e : INFINITY;
+            m.dlt = in ? ws_delta[static_cast<int64_t>(m.h) * P.n + m.x + r] : 0.0f;
             m.kmap = (in && grp == 0) ? P.rowkmap[m.x + r] : 0u;
         };
         Meta cur, nxt;
@@ -292,12 +293,14 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             // warp-uniform: the tcgen05.ld below are warp-collective. Padding rows
             // (tok < 0) have lse2 = +inf and get P = 0 from the same code.
             const bool live = jb < nblk && !dead;
-            // pass 1: P over this thread's 64 columns, 16 at a time, written back to TMEM
-            // as bf16 over S values already read (chunk c's 16 slots packed into
-            // columns grp*64 + 8c .. +7); partial sums of P*dP and P
+            // one pass over this thread's 64 columns, 16 at a time: P = exp2(s*scale + bias
+            // - lse), dS = P (dP - delta) with delta = <dO, O> (the row kernel's), written
+            // back to TMEM as bf16 over S values already read (chunk c's 16 slots packed
+            // into columns grp*64 + 8c .. +7: the A operand of dQ); partial sums of P*dP
+            // and P for the gate gradient
             float pa = 0.0f, pb = 0.0f;
             if (live) {
-                const float bj = bias - lse2;
+                const float bj = bias - lse2, dlt = cur.dlt;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int col0 = grp * 64 + c * 16;
@@ -305,50 +308,33 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                     tc::tmem_ld16(trow + col0, sv);
                     tc::tmem_ld16(trow + 256 + col0, dv);
                     tc::tmem_ld_wait();
-                    uint32_t pk[8];
+                    uint32_t ok[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj));
                         const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj));
-                        pa = fmaf(p0, __uint_as_float(dv[2 * e]), pa);
-                        pa = fmaf(p1, __uint_as_float(dv[2 * e + 1]), pa);
+                        const float d0 = __uint_as_float(dv[2 * e]), d1 = __uint_as_float(dv[2 * e + 1]);
+                        pa = fmaf(p0, d0, pa);
+                        pa = fmaf(p1, d1, pa);
                         pb += p0 + p1;
-                        pk[e] = pack_bf16x2(p0, p1);
+                        ok[e] = pack_bf16x2(p0 * (d0 - dlt), p1 * (d1 - dlt));
                     }
-                    tc::tmem_st8(trow + grp * 64 + c * 8, pk);
+                    tc::tmem_st8(trow + grp * 64 + c * 8, ok);
                 }
                 tc::tmem_st_wait();
             }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bars->ds_full);
+            // exact row term sum_j P*dP for the gate gradient (A_j - delta B_j cancels
+            // exactly for a token that reads a single block), off the MMAs' path
             float *part = sPart + (i & 1) * (2 * 4 * kTM);
             part[grp * kTM + r] = pa;
             part[(4 + grp) * kTM + r] = pb;
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
             const float delta = part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
-            // pass 2: dS = P (dP - delta), in place over P (the A operand of dQ)
-            if (live) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t pw[8], dv[16];
-                    tc::tmem_ld8(trow + grp * 64 + c * 8, pw);
-                    tc::tmem_ld16(trow + 256 + grp * 64 + c * 16, dv);
-                    tc::tmem_ld_wait();
-                    uint32_t ow[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float p0 = __uint_as_float(pw[e] << 16), p1 = __uint_as_float(pw[e] & 0xFFFF0000u);
-                        ow[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - delta),
-                                            p1 * (__uint_as_float(dv[2 * e + 1]) - delta));
-                    }
-                    tc::tmem_st8(trow + grp * 64 + c * 8, ow);
-                }
-                tc::tmem_st_wait();
-            }
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bars->ds_full);
-            // gate gradient (sum over heads by fp32 atomics) and delta for the dK/dV kernel
+            // gate gradient (sum over heads by fp32 atomics)
             if (grp == 0 && tok >= 0) {
-                ws_delta[static_cast<int64_t>(h) * P.n + cur.x + r] = delta;
                 const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
                 const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
                 const uint32_t kmap = cur.kmap;
