@@ -4,25 +4,32 @@
 // saved log-sum-exp, dS = P (dP - delta), dq = dS k * scale, dk = dS^T q *
 // scale, dv = P^T do, dlog_gates = per-block sums of dS over slots and heads).
 // Specialised like read_fwd_tc.cu: head_dim 64, 128-slot blocks, top <= 2.
+// Q and dO are read in routing-plan row order (q_rows from the forward, dO
+// copied by the row kernel that also forms delta = <dO, O> per row and head),
+// so every tile is one 2-D TMA box; the no-workspace entry gathers dO's rows
+// from token order with cp.async instead (kDoRows = false).
 //
 // read_bwd_dq_tc_kernel — item = (128-token tile, head), persistent CTAs over
 // contiguous runs of items ordered head-major, so consecutive items usually
 // share their block set and head and reuse the K/V tiles in shared memory.
-//   warp 0     loader: Q, dO rows by cp.async; K, V blocks by TMA (on change)
-//   warp 1     MMA: S = Q K^T (TMEM cols 0-255), dP = dO V^T (cols 256-511),
-//              then dQ = dS K (cols 0-63, after the softmax warps drained S)
-//   warps 2-5  pass 1: P = exp2(S*scale + bias - lse) -> bf16 P in smem,
-//              delta = sum P dP (exact, fp32: no read of O), per-block sums of
-//              P dP and P for the gate gradient; pass 2: dS = P (dP - delta)
-//              over P in place; then dQ -> global, delta -> workspace,
-//              gate gradient -> global (fp32 atomics over heads)
-// read_bwd_dkdv_tc_kernel — item = (block, head, split of the block's tiles)
-//   warp 0     loader: K_b, V_b once per item (TMA); per tile Q, dO rows (cp.async)
-//              and the tile's per-token lse, delta, bias into shared memory
-//   warp 1     MMA: S^T = K_b Q^T (cols 0-127), dP^T = V_b dO^T (cols 128-255),
-//              then dK += dS^T Q (cols 256-319), dV += P^T dO (cols 320-383)
-//   warps 2-5  P^T, dS^T (one slot row per thread) -> bf16 in smem; at the end
-//              of the item dK * scale, dV -> fp32 reductions into global.
+//   warp 0     loader: Q, dO tiles; K, V blocks by TMA when the run changes
+//   warps 1, 2 MMA issuers: S = Q K^T (TMEM cols 0-255) and dP = dO V^T
+//              (cols 256-511), then dQ over block 0 / block 1 (TS form, dS
+//              from TMEM) into cols 256-319 / 320-383
+//   warps 3-18 softmax, one pass: P = exp2(S*scale + bias - lse), dS = P (dP -
+//              delta) as bf16 over the S columns already read; the exact row
+//              sums of P dP and P per block for the gate gradient (fp32 atomics
+//              over heads); then dQ -> global
+// read_bwd_dkdv_tc_kernel — item = (block, head, split of the block's tiles),
+// a tile's tokens in steps of 64
+//   warp 0     loader: K_b, V_b once per item (TMA); per tile Q, dO and the
+//              tile's per-token bias - lse and delta into shared memory
+//   warp 1     MMA: S^T = K_b Q^T, dP^T = V_b dO^T into one of three step
+//              buffers (TMEM cols 128*b, +64)
+//   warp 2     MMA: dK += dS^T Q, dV += P^T dO (TS form) into cols 384 / 448
+//   warps 3-18 P^T, dS^T (one slot row per thread) -> bf16 in TMEM over the
+//              step buffer; at the end of the item dK * scale, dV -> fp32
+//              reductions into global.
 // Every wait is bounded; a timeout sets bit 1 of the plan's error word.
 #include <cudaTypedefs.h>
 
@@ -52,7 +59,8 @@ struct DqBars {
 static_assert(sizeof(DqBars) <= 1024, "barrier block");
 constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
 constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
-constexpr uint32_t kDqScratch = 2 * 2 * 4 * kTM * 4;                // [2 items][P.dP | P][4 groups][128] fp32
+constexpr uint32_t kDqScratch = 2 * 2 * 4 * kTM * 4                 // [2 items][P.dP | P][4 groups][128] fp32
+                                + kTM * kHD * 2 + kTM * 4;          // dQ tile staged for coalesced stores, tokens
 constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqScratch + 1024 + 1024;
 // warp 0 loader, warps 1 and 2 MMA issuers (warp 1: S, then dQ over block 0;
 // warp 2: dP, then dQ over block 1; warp 1 owns TMEM), warps 3-18 softmax.
@@ -79,6 +87,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
     const uint32_t sKV = base + 2 * kDqStage;
     const uint32_t sK = sKV, sV = sKV + 2 * kRowTile;
     float *sPart = reinterpret_cast<float *>(sbase + 2 * kDqStage + kDqKV);
+    uint4 *sOut = reinterpret_cast<uint4 *>(sPart + 2 * 2 * 4 * kTM);      // [128 rows][8 x 16 B]
+    int *sTok = reinterpret_cast<int *>(sOut + kTM * 8);
     DqBars *bars = reinterpret_cast<DqBars *>(sbase + 2 * kDqStage + kDqKV + kDqScratch);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -301,40 +311,49 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             float pa = 0.0f, pb = 0.0f;
             if (live) {
                 const float bj = bias - lse2, dlt = cur.dlt;
+                const uint64_t sc2 = tc::f2(scale_log2, scale_log2), bj2 = tc::f2(bj, bj), dl2 = tc::f2(dlt, dlt);
+                uint64_t pa2 = tc::f2(0.0f, 0.0f), pb2 = pa2;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const int col0 = grp * 64 + c * 16;
                     uint32_t sv[16], dv[16];
                     tc::tmem_ld16(trow + col0, sv);
                     tc::tmem_ld16(trow + 256 + col0, dv);
-                    tc::tmem_ld_wait();
+                    tc::tmem_ld_wait_regs(sv);
+                    tc::tmem_ld_wait_regs(dv);
                     uint32_t ok[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, bj));
-                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, bj));
-                        const float d0 = __uint_as_float(dv[2 * e]), d1 = __uint_as_float(dv[2 * e + 1]);
-                        pa = fmaf(p0, d0, pa);
-                        pa = fmaf(p1, d1, pa);
-                        pb += p0 + p1;
-                        ok[e] = pack_bf16x2(p0 * (d0 - dlt), p1 * (d1 - dlt));
+                        // column pairs: 2 of 8 by the FMA-pipe polynomial, the rest by MUFU
+                        const uint64_t x2 = tc::fma2(tc::f2_bits(sv[2 * e], sv[2 * e + 1]), sc2, bj2);
+                        const uint64_t p2 = (e & 3) == 1 ? tc::ex2_poly2(x2) : tc::ex2_pair(x2);
+                        const uint64_t d2 = tc::f2_bits(dv[2 * e], dv[2 * e + 1]);
+                        pa2 = tc::fma2(p2, d2, pa2);
+                        pb2 = tc::add2(pb2, p2);
+                        const float2 ds = tc::f2_split(tc::mul2(p2, tc::sub2(d2, dl2)));
+                        ok[e] = pack_bf16x2(ds.x, ds.y);
                     }
                     tc::tmem_st8(trow + grp * 64 + c * 8, ok);
                 }
                 tc::tmem_st_wait();
+                const float2 a = tc::f2_split(pa2), bsum = tc::f2_split(pb2);
+                pa = a.x + a.y;
+                pb = bsum.x + bsum.y;
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->ds_full);
-            // exact row term sum_j P*dP for the gate gradient (A_j - delta B_j cancels
-            // exactly for a token that reads a single block), off the MMAs' path
+            // exact row term sum_j P*dP for the gate gradient, off the MMAs' path
             float *part = sPart + (i & 1) * (2 * 4 * kTM);
             part[grp * kTM + r] = pa;
             part[(4 + grp) * kTM + r] = pb;
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
             const float delta = part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
-            // gate gradient (sum over heads by fp32 atomics)
-            if (grp == 0 && tok >= 0) {
+            // gate gradient (sum over heads by fp32 atomics). A set of one block gets
+            // none: its gates shift all of the token's scores alike, which the
+            // softmax cancels, so the gradient is exactly zero (dlog_gates is zeroed
+            // before the kernels run).
+            if (grp == 0 && tok >= 0 && nblk > 1) {
                 const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
                 const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
                 const uint32_t kmap = cur.kmap;
@@ -344,42 +363,36 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                         atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk, fmaf(-delta, Bv[jsel], A[jsel]));
                 }
             }
-            // epilogue: 16 of the 64 dQ columns, dQ_0 + dQ_1 (the set's blocks) * scale -> global
-            if (!tc::mbar_wait_warp(&bars->dq_full, i & 1, P.err, 2, abort_flag)) { dead = true; continue; }
+            // epilogue: 16 of the 64 dQ columns, dQ_0 + dQ_1 (the set's blocks) * scale ->
+            // global through shared memory; the quarter's four warps agree first (the
+            // store's barrier needs all of them)
+            bool bad = !tc::mbar_wait_warp(&bars->dq_full, i & 1, P.err, 2, abort_flag);
+            if (tc::named_bar_or(bar_id, 128, bad)) {
+                dead = true;
+                break;
+            }
             tc::tc_fence_after();
-            float o[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = 0.0f;
-            if (nblk > 0) {   // warp-uniform
-                uint32_t a0[16];
-                tc::tmem_ld16(trow + 256 + grp * 16, a0);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(a0[e]);
-            }
-            if (nblk > 1) {
-                uint32_t a1[16];
-                tc::tmem_ld16(trow + 320 + grp * 16, a1);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] += __uint_as_float(a1[e]);
-            }
+            uint32_t a0[16], a1[16];
+            tc::tmem_ld16(trow + 256 + grp * 16, a0);          // both halves in one round trip
+            tc::tmem_ld16(trow + 320 + grp * 16, a1);
+            tc::tmem_ld_wait_regs(a0);
+            tc::tmem_ld_wait_regs(a1);
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->dq_free);
-            if (tok >= 0) {
-                uint4 v0, v1;
-                v0.x = pack_bf16x2(o[0] * scale, o[1] * scale);
-                v0.y = pack_bf16x2(o[2] * scale, o[3] * scale);
-                v0.z = pack_bf16x2(o[4] * scale, o[5] * scale);
-                v0.w = pack_bf16x2(o[6] * scale, o[7] * scale);
-                v1.x = pack_bf16x2(o[8] * scale, o[9] * scale);
-                v1.y = pack_bf16x2(o[10] * scale, o[11] * scale);
-                v1.z = pack_bf16x2(o[12] * scale, o[13] * scale);
-                v1.w = pack_bf16x2(o[14] * scale, o[15] * scale);
-                uint4 *dst = reinterpret_cast<uint4 *>(dq + tok * ld + h * kHD + grp * 16);
-                dst[0] = v0;
-                dst[1] = v1;
-            }
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+                o[e] = (nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
+            uint4 v0, v1;
+            v0.x = pack_bf16x2(o[0] * scale, o[1] * scale);
+            v0.y = pack_bf16x2(o[2] * scale, o[3] * scale);
+            v0.z = pack_bf16x2(o[4] * scale, o[5] * scale);
+            v0.w = pack_bf16x2(o[6] * scale, o[7] * scale);
+            v1.x = pack_bf16x2(o[8] * scale, o[9] * scale);
+            v1.y = pack_bf16x2(o[10] * scale, o[11] * scale);
+            v1.z = pack_bf16x2(o[12] * scale, o[13] * scale);
+            v1.w = pack_bf16x2(o[14] * scale, o[15] * scale);
+            tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, tok, dq + h * kHD, ld);
         }
     }
     tc::tc_fence_before();
@@ -405,7 +418,7 @@ struct DkvBars {
 static_assert(sizeof(DkvBars) <= 1024, "barrier block");
 constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
 constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
-constexpr uint32_t kMetaBytes = 3 * kTM * 4;                     // bias2, lse2, delta
+constexpr uint32_t kMetaBytes = 2 * kTM * 4;                     // bias2 - lse2, delta
 constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + kDkvStages * kMetaBytes + 1024 + 1024;
 // A tile's 128 tokens go through the MMAs and the softmax in two steps of 64.
 // TMEM: step buffer b (= step % 3) at column 128*b holds S^T [128 slots x 64
@@ -434,7 +447,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     unsigned char *sbase = smem_raw + (base - raw);
     const uint32_t sK = base, sV = base + kKvTile;
     const uint32_t sStage = base + 2 * kKvTile;                  // [stages][Q | dO]
-    float *meta = reinterpret_cast<float *>(sbase + 2 * kKvTile + kDkvStages * kDkvStage);   // [stages][3][128]
+    float *meta = reinterpret_cast<float *>(sbase + 2 * kKvTile + kDkvStages * kDkvStage);   // [stages][2][128]
     DkvBars *bars = reinterpret_cast<DkvBars *>(reinterpret_cast<unsigned char *>(meta) + kDkvStages * kMetaBytes);
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -485,7 +498,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         int g = 0, nkv = 0, last = -1;         // g: global tile-step counter of this CTA
         int cx = 0, cy = 0, cjb = 0;           // this lane's tile of the current chunk
         int rows[4];
-        float mbias[4], mlse[4], mdelta[4];
+        float mcomb[4], mdelta[4];
         auto fetch_rows = [&](int src, int h) {
             const int x = tc::get(cx, src), y = tc::get(cy, src), jb = tc::get(cjb, src);
             if (!kDoRows) tc::gather_rows(P, x, y, lane, rows);
@@ -495,8 +508,9 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 const int rr = lane * 4 + u;
                 const bool ok = rr < y;
                 const int64_t prow = static_cast<int64_t>(h) * P.n + x + rr;
-                mbias[u] = ok ? P.rowbias[static_cast<int64_t>(x + rr) * top + jb] * kLog2e : 0.0f;
-                mlse[u] = ok ? lse[prow] * kLog2e : INFINITY;
+                // the token's exponent offset bias - lse (log2 units); -inf for padding rows
+                mcomb[u] = ok ? P.rowbias[static_cast<int64_t>(x + rr) * top + jb] * kLog2e - lse[prow] * kLog2e
+                              : -INFINITY;
                 mdelta[u] = ok ? ws_delta[prow] : 0.0f;
             }
         };
@@ -528,13 +542,12 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 }
                 const int s = g % kDkvStages, j = g / kDkvStages;
                 if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) { stop = true; break; }
-                float *mb = meta + s * 3 * kTM;
+                float *mb = meta + s * 2 * kTM;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const int rr = lane * 4 + u;
-                    mb[rr] = mbias[u];
-                    mb[kTM + rr] = mlse[u];
-                    mb[2 * kTM + rr] = mdelta[u];
+                    mb[rr] = mcomb[u];
+                    mb[kTM + rr] = mdelta[u];
                 }
                 const uint32_t sQ = sStage + s * kDkvStage, sD = sQ + kRowTile;
                 const int x0 = tc::get(cx, src);
@@ -685,7 +698,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     stop = true;
                     break;
                 }
-                const float *mb = meta + s * 3 * kTM;
+                const float *mb = meta + s * 2 * kTM;
                 for (int half = 0; half < 2; ++half, ++hs) {
                     const int b = hs % kBufs, use = hs / kBufs;
                     if (!tc::mbar_wait_warp(&bars->s_full[b], use & 1, P.err, 2, abort_flag)) {
@@ -699,16 +712,27 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     tc::tmem_ld16(tb + kHalf, dv);
                     tc::tmem_ld_wait();
                     const int col0 = half * kHalf + grp * 16;        // token within the tile
+                    // the 16 tokens' offsets and deltas: 16-B shared loads
+                    float cb[16], dl[16];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const float4 a = reinterpret_cast<const float4 *>(mb + col0)[u];
+                        const float4 d = reinterpret_cast<const float4 *>(mb + kTM + col0)[u];
+                        cb[4 * u] = a.x, cb[4 * u + 1] = a.y, cb[4 * u + 2] = a.z, cb[4 * u + 3] = a.w;
+                        dl[4 * u] = d.x, dl[4 * u + 1] = d.y, dl[4 * u + 2] = d.z, dl[4 * u + 3] = d.w;
+                    }
+                    const uint64_t sc2 = tc::f2(scale_log2, scale_log2);
                     uint32_t pk[8], dk[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
-                        const int col = col0 + 2 * e;
-                        const float p0 = tc::ex2(fmaf(__uint_as_float(sv[2 * e]), scale_log2, mb[col]) - mb[kTM + col]);
-                        const float p1 = tc::ex2(fmaf(__uint_as_float(sv[2 * e + 1]), scale_log2, mb[col + 1]) -
-                                                 mb[kTM + col + 1]);
-                        pk[e] = pack_bf16x2(p0, p1);
-                        dk[e] = pack_bf16x2(p0 * (__uint_as_float(dv[2 * e]) - mb[2 * kTM + col]),
-                                            p1 * (__uint_as_float(dv[2 * e + 1]) - mb[2 * kTM + col + 1]));
+                        const uint64_t x2 = tc::fma2(tc::f2_bits(sv[2 * e], sv[2 * e + 1]), sc2,
+                                                     tc::f2(cb[2 * e], cb[2 * e + 1]));
+                        const uint64_t p2 = tc::ex2_pair(x2);
+                        const float2 p = tc::f2_split(p2);
+                        const float2 ds = tc::f2_split(tc::mul2(
+                            p2, tc::sub2(tc::f2_bits(dv[2 * e], dv[2 * e + 1]), tc::f2(dl[2 * e], dl[2 * e + 1]))));
+                        pk[e] = pack_bf16x2(p.x, p.y);
+                        dk[e] = pack_bf16x2(ds.x, ds.y);
                     }
                     // in place: these columns' S^T / dP^T values are already in registers
                     tc::tmem_st8(tb, pk);

@@ -6,7 +6,7 @@
 // routing set (top-2). A work item is (tile of <= 128 tokens sharing one block
 // set, head); CTAs are persistent over items.
 //
-// Warp roles (576 threads):
+// Warp roles (608 threads):
 //   warp 0     loader: K, V blocks and the tile's 128 Q rows by TMA (SWIZZLE_128B
 //              boxes of 128 rows x 64); Q is read from its copy in routing-plan
 //              row order (q_rows), where a tile's rows are contiguous; tile
@@ -17,7 +17,8 @@
 //   warps 3-18 softmax (one TMEM lane = one token row per thread; four warps per
 //              lane quarter, 64 score columns each): row max, exp2, row sum, P as
 //              bf16 into TMEM (the A operand of PV); then the epilogue
-//              (O_0 + O_1) / l -> global, log-sum-exp -> global
+//              (O_0 + O_1) / l -> shared memory -> global as whole 128-B rows,
+//              log-sum-exp -> global
 // TMEM: S at columns 0..255, P (bf16 pairs) at 256..383, O_0 / O_1 at 384 / 448.
 // P has its own columns so that S(i+1) is issued as soon as the softmax has read
 // S(i), overlapping PV(i); the softmax writes P(i+1) once PV(i) is done
@@ -41,7 +42,8 @@ constexpr int kThreads = 96 + kSoftThreads;     // loader + 2 MMA issuers + soft
 constexpr uint32_t kQBytes = kTM * kHD * 2;    // 16 KiB
 constexpr uint32_t kBlkBytes = kBS * kHD * 2;  // 16 KiB per 128-slot block of K or V
 constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) + V(2 blocks)
-constexpr uint32_t kScratchBytes = 8 * kTM * 4;   // partial row max [4][128], row sums [4][128]
+constexpr uint32_t kOutBytes = kTM * kHD * 2;      // the output tile of one item, staged for coalesced stores
+constexpr uint32_t kScratchBytes = 8 * kTM * 4 + kOutBytes + kTM * 4;   // row max / sums [4][128], O tile, tokens
 constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPCol = 256;                // P: group g's 64 slots at 256 + 32g (bf16 pairs)
@@ -66,6 +68,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     unsigned char *sbase = smem_raw + (base - raw);
     float *sMax = reinterpret_cast<float *>(sbase + 2 * kStageBytes);   // [4][128]
     float *sSum = sMax + 4 * kTM;                                        // [4][128]
+    uint4 *sOut = reinterpret_cast<uint4 *>(sSum + 4 * kTM);            // [128 rows][8 x 16 B], swizzled
+    int *sTok = reinterpret_cast<int *>(sOut + kTM * 8);                 // [128] tokens of the staged rows
     Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kScratchBytes);
     volatile int *abort_flag = &bars->abort;
 
@@ -140,32 +144,40 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         }
     } else if (warp == 1 || warp == 2) {
         // ------------------------------------------------------------ MMA issuers
+        // Warp 1 issues S(i+1) as soon as the softmax has read S(i) (p_full of i),
+        // ahead of its half of PV(i), so that the softmax of i+1 starts while PV(i)
+        // still runs on the tensor pipe.
         const bool wa = warp == 1;
         const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
-        for (int i = 0; i < nmine; ++i) {
+        auto issue_s = [&](int i) -> bool {   // warp 1: S(i) = Q K^T into TMEM columns 0..255
             const int s = i & 1, j = i >> 1;
-            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
-            const int meta = tc::ld_shared_volatile(&bars->meta[s]);
-            const int nload = meta & 0xFF, nblk = meta >> 8;
+            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) return false;
+            const int nload = tc::ld_shared_volatile(&bars->meta[s]) & 0xFF;
             const uint32_t sQ = base + s * kStageBytes;
             const uint32_t sK = sQ + kQBytes;
-            const uint32_t sV = sK + 2 * kBlkBytes;
-            if (wa) {
-                // S(i) overwrites S(i-1), which the softmax has read once P(i-1) was posted
-                // (p_full of i-1, waited below in the previous iteration)
-                tc::tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
-                    const uint64_t ad = tc::smem_desc_sw128(sQ, 16, 1024), bd = tc::smem_desc_sw128(sK, 16, 1024);
+            tc::tc_fence_after();
+            if (lane == 0) {
+                const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
+                const uint64_t ad = tc::smem_desc_sw128(sQ, 16, 1024), bd = tc::smem_desc_sw128(sK, 16, 1024);
 #pragma unroll
-                    for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
-                        tc::mma_bf16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc_s, kk > 0);
-                    tc::mma_commit(&bars->s_full);
-                }
-                __syncwarp();
+                for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
+                    tc::mma_bf16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc_s, kk > 0);
+                tc::mma_commit(&bars->s_full);
             }
-            // P(i) written to TMEM by the softmax; O read by the epilogue of i-1
+            __syncwarp();
+            return true;
+        };
+        bool ok = nmine > 0 && (!wa || issue_s(0));
+        for (int i = 0; ok && i < nmine; ++i) {
+            const int s = i & 1, j = i >> 1;
+            // warp 2 has not waited for the stage yet; warp 1 did so before issuing S(i)
+            if (!wa && !tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
+            const int nblk = tc::ld_shared_volatile(&bars->meta[s]) >> 8;
+            const uint32_t sV = base + s * kStageBytes + kQBytes + 2 * kBlkBytes;
+            // P(i) written to TMEM (and S(i) read) by the softmax
             if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
+            if (wa && i + 1 < nmine && !issue_s(i + 1)) break;
+            // O read by the epilogue of i-1
             if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
@@ -203,46 +215,37 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         int prev_tok = -1, prev_h = 0, prev_row = 0, prev_nblk = 0;
         float prev_m = 0.0f;
         float prev_l = 0.0f;
+        // Epilogue of an item, called by the four warps of a lane quarter together:
+        // O_0 (+ O_1) / l of this thread's 16 columns, stored through shared memory
+        // as whole rows (tc::store_tile_rows).
         auto epilogue = [&](int i) {
             (void)i;
             const float l = prev_l;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             tc::tc_fence_after();
-            float o[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) o[e] = 0.0f;
-            if (prev_nblk > 0) {   // warp-uniform; O_1 holds block 1 of a two-block set
-                uint32_t a0[16];
-                tc::tmem_ld16(trow + kOCol + grp * 16, a0);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = __uint_as_float(a0[e]);
-            }
-            if (prev_nblk > 1) {
-                uint32_t a1[16];
-                tc::tmem_ld16(trow + kOCol + kHD + grp * 16, a1);
-                tc::tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] += __uint_as_float(a1[e]);
-            }
+            uint32_t a0[16], a1[16];
+            tc::tmem_ld16(trow + kOCol + grp * 16, a0);          // both halves in one round trip
+            tc::tmem_ld16(trow + kOCol + kHD + grp * 16, a1);
+            tc::tmem_ld_wait_regs(a0);
+            tc::tmem_ld_wait_regs(a1);
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->o_free);
-            if (prev_tok >= 0) {
-                uint4 v0, v1;
-                v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
-                v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
-                v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
-                v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-                v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
-                v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
-                v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
-                v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
-                uint4 *dst = reinterpret_cast<uint4 *>(out + prev_tok * ld + prev_h * kHD + grp * 16);
-                dst[0] = v0;
-                dst[1] = v1;
-                if (grp == 0)
-                    lse[static_cast<int64_t>(prev_h) * P.n + prev_row] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
-            }
+            float o[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)   // O_1 holds block 1 of a two-block set
+                o[e] = (prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (prev_nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
+            uint4 v0, v1;
+            v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+            v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+            v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+            v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+            v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
+            v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
+            v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
+            v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
+            if (grp == 0 && prev_tok >= 0)
+                lse[static_cast<int64_t>(prev_h) * P.n + prev_row] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
+            tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
         };
         // per-item row metadata: tile fields for 32 items at a time (one per lane),
         // this thread's row (token, gate bias) one item ahead, so that no global
@@ -306,37 +309,52 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             float lpart = 0.0f;
             if (live && !dead) {
                 const float bj = bias - mref;
+                const uint64_t sc2 = tc::f2(scale_log2, scale_log2), bj2 = tc::f2(bj, bj);
+                uint64_t l2 = tc::f2(0.0f, 0.0f);
+                // chunk c: 16 score columns -> 8 bf16 pairs of P at kPCol + 32*grp + 8c
+                auto chunk = [&](const uint32_t (&v)[16], int c) {
+                    uint32_t pk[8];
 #pragma unroll
-                for (int c = 0; c < 2; ++c) {
-                    uint32_t v[32];
-                    tc::tmem_ld32(trow + grp * 64 + c * 32, v);
-                    tc::tmem_ld_wait();
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const float p0 = tc::ex2(fmaf(__uint_as_float(v[2 * e]), scale_log2, bj));
-                        const float p1 = tc::ex2(fmaf(__uint_as_float(v[2 * e + 1]), scale_log2, bj));
-                        lpart += p0 + p1;
-                        pk[e] = pack_bf16x2(p0, p1);
+                    for (int e = 0; e < 8; ++e) {
+                        // column pairs: 3 of 8 by the FMA-pipe polynomial, the rest by MUFU
+                        const uint64_t x2 = tc::fma2(tc::f2_bits(v[2 * e], v[2 * e + 1]), sc2, bj2);
+                        const uint64_t p2 = (e & 1) && e < 7 ? tc::ex2_poly2(x2) : tc::ex2_pair(x2);
+                        l2 = tc::add2(l2, p2);
+                        const float2 p = tc::f2_split(p2);
+                        pk[e] = pack_bf16x2(p.x, p.y);
                     }
-                    tc::tmem_st16(trow + kPCol + grp * 32 + c * 16, pk);
-                }
+                    tc::tmem_st8(trow + kPCol + grp * 32 + c * 8, pk);
+                };
+                // the load of chunk c+1 is in flight while chunk c is computed
+                const uint32_t s0 = trow + grp * 64;
+                uint32_t va[16], vb[16];
+                tc::tmem_ld16(s0, va);
+                tc::tmem_ld_wait_regs(va);
+                tc::tmem_ld16(s0 + 16, vb);
+                chunk(va, 0);
+                tc::tmem_ld_wait_regs(vb);
+                tc::tmem_ld16(s0 + 32, va);
+                chunk(vb, 1);
+                tc::tmem_ld_wait_regs(va);
+                tc::tmem_ld16(s0 + 48, vb);
+                chunk(va, 2);
+                tc::tmem_ld_wait_regs(vb);
+                chunk(vb, 3);
                 tc::tmem_st_wait();
+                const float2 l = tc::f2_split(l2);
+                lpart = l.x + l.y;
             }
             sSum[grp * kTM + r] = lpart;
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->p_full);
+            // O(i-1) complete (PV(i-1)), for the epilogue below
+            if (!dead && i > 0 && !tc::mbar_wait_warp(&bars->o_full, (i - 1) & 1, P.err, 2, abort_flag))
+                dead = true;
             // row sums of item i complete; the four warps of this lane quarter agree
-            // on stopping together
+            // on stopping together (the epilogue's barrier needs all four)
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
-            if (i > 0) {
-                if (!tc::mbar_wait_warp(&bars->o_full, (i - 1) & 1, P.err, 2, abort_flag)) {
-                    dead = true;
-                    break;
-                }
-                epilogue(i - 1);
-            }
+            if (i > 0) epilogue(i - 1);
             prev_tok = tok;
             prev_h = h;
             prev_row = cur.row;
@@ -344,10 +362,11 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             prev_nblk = nblk;
             count = i + 1;
         }
-        if (count > 0 && !dead && !*abort_flag) {
+        if (count > 0 && !dead) {   // uniform over the lane quarter
             const int i = count - 1;
             prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
-            if (tc::mbar_wait_warp(&bars->o_full, i & 1, P.err, 2, abort_flag)) epilogue(i);
+            bool bad = *abort_flag || !tc::mbar_wait_warp(&bars->o_full, i & 1, P.err, 2, abort_flag);
+            if (!tc::named_bar_or(bar_id, 128, bad)) epilogue(i);
         }
     }
     tc::tc_fence_before();

@@ -97,13 +97,18 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
 // partial sum of any subset of them is a multiple of 2^e_min bounded by
 // A = sum |x|; if A < 2^(52 + e_min) all of them are exactly representable in
 // fp64 and ANY summation order returns the exact prefix sums — the values the
-// sequential loop produces. The kernel checks that certificate per column and
-// walks the column sequentially when it fails (tiny or huge dynamic range).
+// sequential loop produces. The kernel checks that certificate per column (A
+// bounded from above by fp32 sums rounded upward) and walks the column
+// sequentially when it fails (tiny or huge dynamic range).
 //
 // CTA = 64 columns (32 pairs) x 32 chunks of the sequence (1024 threads):
-//   phase 1  chunk sums, sums of |x| and min ulp exponent
+//   phase 1  chunk sums, upper bounds of the sums of |x|, min ulp exponent
 //   phase 2  per column: exclusive scan of the chunk sums, certificate
 //   phase 3  each chunk re-walks its rows from its carry and writes h.
+// Rows are read kScanBatch at a time into registers before any of them is
+// used, so every warp keeps that many row loads in flight.
+constexpr int kScanBatch = 8;
+
 template <int XDT>
 __device__ __forceinline__ int ulp_exponent(float v) {
     const uint32_t bits = __float_as_uint(v);
@@ -111,9 +116,7 @@ __device__ __forceinline__ int ulp_exponent(float v) {
     return (e == 0 ? 1 : e) - 127 - (XDT == MOM_BF16 ? 7 : 23);
 }
 
-// Two adjacent columns per thread (one 4-byte bf16 pair or 8-byte fp32 pair per
-// row) and 16 rows in flight per thread: the certificate pass and the output
-// pass are each one streaming read of the CTA's 64 columns.
+// Two adjacent columns per thread (one 4-byte bf16 pair or 8-byte fp32 pair per row).
 template <int XDT> struct Pair;
 template <> struct Pair<MOM_BF16> {
     static __device__ __forceinline__ float2 load(const uint16_t *p) {
@@ -136,12 +139,30 @@ template <> struct PairStore<MOM_F32> {
     }
 };
 
+// RN(c / den) for den = t + 1, a positive integer below 2^24, given y = RN(1 / den).
+// Markstein's correction step (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with q0
+// within one ulp of c/den, the remainder c - den*q0 is exact in one fma and
+// q0 + remainder*y rounded once is the correctly rounded quotient. It holds while
+// the quotient is a normal number, so zero, tiny, infinite and NaN c take the
+// IEEE division instead. Division never lands exactly on a rounding midpoint,
+// so no tie case arises.
+__device__ __forceinline__ float div_by_count(float c, float den, float y) {
+    const uint32_t e = (__float_as_uint(c) >> 23) & 0xFFu;
+    if (e - 25u < 229u) {                      // 2^-102 <= |c| < 2^128
+        const float q0 = __fmul_rn(c, y);
+        const float r = __fmaf_rn(-q0, den, c);
+        return __fmaf_rn(r, y, q0);
+    }
+    return __fdiv_rn(c, den);
+}
+
 template <int XDT, int CDT>
 __global__ void __launch_bounds__(1024)
 route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem<CDT>::T *__restrict__ hq,
                       int S, int d) {
     __shared__ double s_sum[64][33];
-    __shared__ double s_abs[64][33];
+    __shared__ float s_abs[64][33];
     __shared__ int s_emin[64][33];
     __shared__ int s_cert[64];
     const int c2 = threadIdx.x & 31, k = threadIdx.x >> 5;    // column pair, chunk
@@ -149,22 +170,33 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
     const int col = blockIdx.x * 64 + 2 * c2;
     const int len = (S + 31) / 32;
     const int t0 = k * len, t1 = min(S, t0 + len);
-    const typename Elem<XDT>::T *xc = x + static_cast<int64_t>(b) * S * d + col;
-    typename Elem<CDT>::T *hc = hq + static_cast<int64_t>(b) * S * d + col;
     const bool live = col < d;                                   // d % 8 == 0: pairs are whole
-    double sum0 = 0.0, sum1 = 0.0, as0 = 0.0, as1 = 0.0;
+    // lanes past d read (and never write) column pair 0, so that every lane of a
+    // warp runs the same loop and can take part in its shuffles
+    const int64_t cofs = static_cast<int64_t>(b) * S * d + (live ? col : 0);
+    const typename Elem<XDT>::T *xc = x + cofs;
+    typename Elem<CDT>::T *hc = hq + cofs;
+    double sum0 = 0.0, sum1 = 0.0;
+    float as0 = 0.0f, as1 = 0.0f;
     int em0 = 1 << 20, em1 = 1 << 20;
-    if (live) {
-#pragma unroll 16
-        for (int t = t0; t < t1; ++t) {
-            const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
-            sum0 = __dadd_rn(sum0, static_cast<double>(v.x));
-            sum1 = __dadd_rn(sum1, static_cast<double>(v.y));
-            as0 = __dadd_rn(as0, static_cast<double>(fabsf(v.x)));
-            as1 = __dadd_rn(as1, static_cast<double>(fabsf(v.y)));
-            if (v.x != 0.0f) em0 = min(em0, ulp_exponent<XDT>(v.x));
-            if (v.y != 0.0f) em1 = min(em1, ulp_exponent<XDT>(v.y));
+    auto take = [&](float2 v) {
+        sum0 = __dadd_rn(sum0, static_cast<double>(v.x));
+        sum1 = __dadd_rn(sum1, static_cast<double>(v.y));
+        as0 = __fadd_ru(as0, fabsf(v.x));
+        as1 = __fadd_ru(as1, fabsf(v.y));
+        if (v.x != 0.0f) em0 = min(em0, ulp_exponent<XDT>(v.x));
+        if (v.y != 0.0f) em1 = min(em1, ulp_exponent<XDT>(v.y));
+    };
+    {
+        int t = t0;
+        for (; t + kScanBatch <= t1; t += kScanBatch) {
+            float2 v[kScanBatch];
+#pragma unroll
+            for (int u = 0; u < kScanBatch; ++u) v[u] = Pair<XDT>::load(xc + static_cast<int64_t>(t + u) * d);
+#pragma unroll
+            for (int u = 0; u < kScanBatch; ++u) take(v[u]);
         }
+        for (; t < t1; ++t) take(Pair<XDT>::load(xc + static_cast<int64_t>(t) * d));
     }
     s_sum[2 * c2][k] = sum0;
     s_sum[2 * c2 + 1][k] = sum1;
@@ -181,27 +213,38 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
             const double v = s_sum[cc][kk];
             s_sum[cc][kk] = run;
             run = __dadd_rn(run, v);
-            at = __dadd_rn(at, s_abs[cc][kk]);
+            at = __dadd_ru(at, static_cast<double>(s_abs[cc][kk]));   // stays an upper bound of A
             em = min(em, s_emin[cc][kk]);
         }
         // all zero -> trivially exact; else A < 2^(52 + e_min)
         s_cert[cc] = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
     }
     __syncthreads();
-    if (!live) return;
-    const bool ok0 = s_cert[2 * c2], ok1 = s_cert[2 * c2 + 1];
-    if (ok0 && ok1) {
+    const bool fast = live && s_cert[2 * c2] && s_cert[2 * c2 + 1];
+    {
         double r0 = s_sum[2 * c2][k], r1 = s_sum[2 * c2 + 1][k];
-#pragma unroll 16
-        for (int t = t0; t < t1; ++t) {
-            const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
+        auto emit = [&](int t, float2 v, float y) {
             r0 = __dadd_rn(r0, static_cast<double>(v.x));
             r1 = __dadd_rn(r1, static_cast<double>(v.y));
             const float den = static_cast<float>(t + 1);
-            PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, __fdiv_rn(__double2float_rn(r0), den),
-                                  __fdiv_rn(__double2float_rn(r1), den));
+            if (fast)
+                PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, div_by_count(__double2float_rn(r0), den, y),
+                                      div_by_count(__double2float_rn(r1), den, y));
+        };
+        int t = t0;
+        for (; t + kScanBatch <= t1; t += kScanBatch) {
+            float2 v[kScanBatch];
+#pragma unroll
+            for (int u = 0; u < kScanBatch; ++u) v[u] = Pair<XDT>::load(xc + static_cast<int64_t>(t + u) * d);
+            // lane u < kScanBatch holds 1/(t + 1 + u) for the whole warp
+            const float yl = __frcp_rn(static_cast<float>(t + 1 + (c2 & (kScanBatch - 1))));
+#pragma unroll
+            for (int u = 0; u < kScanBatch; ++u) emit(t + u, v[u], __shfl_sync(0xffffffffu, yl, u));
         }
-    } else if (k == 0) {
+        for (; t < t1; ++t)
+            emit(t, Pair<XDT>::load(xc + static_cast<int64_t>(t) * d), __frcp_rn(static_cast<float>(t + 1)));
+    }
+    if (live && !fast && k == 0) {
         // a certificate failed: both columns of the pair walk sequentially
         double a0 = 0.0, a1 = 0.0;
         for (int t = 0; t < S; ++t) {

@@ -162,6 +162,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+// The same wait, with the destination registers of the load it completes as
+// in/out operands: no use of them can be scheduled before it, also when other
+// TMEM loads are issued in between (software pipelining).
+__device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&r)[16]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
+                   "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]),
+                   "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+}
 
 // 32 lanes x 8 consecutive 32-bit columns.
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
@@ -216,12 +227,107 @@ __device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
     return r != 0;
 }
 
+// Stores one item's 128-row x 64-column bf16 tile that the softmax warps hold
+// as 32 bytes per thread (row quarter*32 + lane, columns 16*grp .. +15), to the
+// global rows tok of each row (tok < 0: padding, not stored); dst_col points at
+// the tile's first column, ld is the row pitch in elements. The four warps of a
+// lane quarter call it together (named barrier bar_id over 128 threads): each
+// thread's 32 B go to a shared-memory copy of the quarter's rows (16-B chunks
+// XOR-swizzled by row: conflict-free), then each warp stores 8 whole 128-B rows,
+// 8 lanes per row, so a warp store touches 4 rows instead of 32. sOut holds 128
+// rows x 128 B, sTok 128 ints; the caller keeps another barrier of the quarter
+// between two calls.
+__device__ __forceinline__ void store_tile_rows(uint4 *sOut, int *sTok, int quarter, int grp, int lane, int bar_id,
+                                                uint4 v0, uint4 v1, int tok, uint16_t *dst_col, int64_t ld) {
+    const int r = quarter * 32 + lane;
+    uint4 *srow = sOut + r * 8;
+    srow[(2 * grp) ^ (r & 7)] = v0;
+    srow[(2 * grp + 1) ^ (r & 7)] = v1;
+    if (grp == 0) sTok[r] = tok;
+    named_bar(bar_id, 128);
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+        const int rr = quarter * 32 + grp * 8 + pass * 4 + (lane >> 3), ch = lane & 7;
+        const int t = sTok[rr];
+        if (t >= 0)
+            reinterpret_cast<uint4 *>(dst_col + static_cast<int64_t>(t) * ld)[ch] = sOut[rr * 8 + (ch ^ (rr & 7))];
+    }
+}
+
 // 2^x by the hardware approximation (PTX ex2.approx.ftz.f32); the results
-// feed bf16 operands, far coarser than its error.
+// feed bf16 operands, far coarser than its error. Not volatile: a pure
+// function the compiler may schedule among the TMEM loads.
 __device__ __forceinline__ float ex2(float x) {
     float y;
-    asm volatile("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+    asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
     return y;
+}
+
+// ------------------------------------------------------------------ packed fp32 pairs
+// Two fp32 lanes in one 64-bit register pair (PTX .f32x2 arithmetic, sm_100):
+// one instruction issues both halves.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t f2_bits(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};\n" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 f2_split(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;\n" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;\n" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;\n" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+
+// 2^x for a pair of softmax arguments (x <= ~0) on the FMA pipe, so that part of
+// a row's exponentials leave the MUFU unit: x = n + f with n = RN(x) taken by
+// adding 1.5 * 2^23 (n lands in the low mantissa bits), f = x - n in [-1/2, 1/2],
+// 2^f by a degree-3 polynomial, n added to the exponent field. The coefficients
+// were fitted for this kernel (least squares on 4001 Chebyshev nodes of
+// [-1/2, 1/2], relative error, Lawson reweighting toward minimax): maximum
+// relative error 7.5e-5 in fp32 Horner evaluation, well below the bf16
+// rounding of P. x is clamped at -126, where the result (a zero or denormal
+// exponent field) is negligible next to the row maximum's 1.
+__device__ __forceinline__ uint64_t ex2_poly2(uint64_t x) {
+    const float2 xc = f2_split(x);
+    const uint64_t xk = f2(fmaxf(xc.x, -126.0f), fmaxf(xc.y, -126.0f));
+    const uint64_t shifter = f2(12582912.0f, 12582912.0f);           // 1.5 * 2^23
+    const uint64_t t = add2(xk, shifter);
+    const uint64_t f = sub2(xk, sub2(t, shifter));
+    uint64_t p = fma2(f2(0x1.c3f76p-5f, 0x1.c3f76p-5f), f, f2(0x1.f0de1cp-3f, 0x1.f0de1cp-3f));
+    p = fma2(p, f, f2(0x1.62f31ap-1f, 0x1.62f31ap-1f));
+    p = fma2(p, f, f2(0x1.fff692p-1f, 0x1.fff692p-1f));
+    const float2 pp = f2_split(p), tt = f2_split(t);
+    return f2_bits(__float_as_uint(pp.x) + (__float_as_uint(tt.x) << 23),
+                   __float_as_uint(pp.y) + (__float_as_uint(tt.y) << 23));
+}
+// 2^x for a pair by the hardware approximation.
+__device__ __forceinline__ uint64_t ex2_pair(uint64_t x) {
+    const float2 xc = f2_split(x);
+    return f2(ex2(xc.x), ex2(xc.y));
 }
 
 // ------------------------------------------------------------------ descriptors
