@@ -20,8 +20,9 @@
 //              delta) as bf16 over the S columns already read; the exact row
 //              sums of P dP and P per block for the gate gradient (fp32 atomics
 //              over heads); then dQ -> global
-// read_bwd_dkdv_tc_kernel — item = (block, head, split of the block's tiles),
-// a tile's tokens in steps of 64
+// read_bwd_dkdv_tc_kernel — each CTA an equal contiguous share of the (block,
+// head, tile) units, walked as segments of one (block, head); a tile's tokens
+// in steps of 64
 //   warp 0     loader: K_b, V_b once per item (TMA); per tile Q, dO and the
 //              tile's per-token bias - lse and delta into shared memory
 //   warp 1     MMA: S^T = K_b Q^T, dP^T = V_b dO^T into one of three step
@@ -439,7 +440,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                         const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                         const uint16_t *__restrict__ dout,
                         const float *__restrict__ lse, const float *__restrict__ ws_delta, int H, int nb, int top,
-                        int nsplit, int max_tiles, float scale, float scale_log2, PlanView P,
+                        int max_tiles, float scale, float scale_log2, PlanView P,
                         float *__restrict__ dk_acc, float *__restrict__ dv_acc) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -452,7 +453,6 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     volatile int *abort_flag = &bars->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t ld = static_cast<int64_t>(H) * kHD;
-    const int nitems = nb * H * nsplit;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kDkvStages; ++s) {
@@ -481,16 +481,39 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    // item -> (block, head, split); number of tiles of the item
-    auto item_ntile = [&](int item) {
-        const int blk = item / (H * nsplit), split = item % nsplit;
-        const int count = P.blkcount[blk];
-        return count > split ? (count - split + nsplit - 1) / nsplit : 0;
+    // Work split: the sequence of (block, head, tile of the block's list) units,
+    // block-major, cut into gridDim.x equal contiguous ranges. A CTA walks its
+    // range as segments of one (block, head) (K_b, V_b loaded once, dK / dV
+    // accumulated in TMEM and reduced into global at the segment's end); a
+    // (block, head) cut between two CTAs is reduced by both.
+    int64_t units = 0;
+    for (int b = 0; b < nb; ++b) units += static_cast<int64_t>(P.blkcount[b]) * H;
+    const int64_t u_begin = units * blockIdx.x / gridDim.x, u_end = units * (blockIdx.x + 1) / gridDim.x;
+    struct Seg { int blk, h, t0, nt; };
+    // next segment of [u, u_end); advances u
+    auto next_seg = [&](int64_t &u, Seg &sg) -> bool {
+        if (u >= u_end) return false;
+        int64_t base = 0;
+        int blk = 0;
+        for (; blk < nb - 1; ++blk) {
+            const int64_t span = static_cast<int64_t>(P.blkcount[blk]) * H;
+            if (u < base + span) break;
+            base += span;
+        }
+        const int cnt = P.blkcount[blk];
+        const int64_t rem = u - base;
+        sg.blk = blk;
+        sg.h = static_cast<int>(rem / cnt);
+        sg.t0 = static_cast<int>(rem % cnt);
+        const int64_t end = min(u_end, base + static_cast<int64_t>(sg.h + 1) * cnt);
+        sg.nt = static_cast<int>(end - u);
+        u = end;
+        return true;
     };
 
     if (warp == 0) {
         // ------------------------------------------------------------ loader
-        // Per item: the tile list entry, tile descriptor and the block's position
+        // Per segment: the tile list entry, tile descriptor and the block's position
         // in the tile's set for 32 tiles at a time (one per lane); per tile the
         // row tokens, gate bias, lse and delta (one round trip) are loaded right
         // after the previous tile's copies were issued.
@@ -514,11 +537,11 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 mdelta[u] = ok ? ws_delta[prow] : 0.0f;
             }
         };
-        for (int item = blockIdx.x; item < nitems; item += gridDim.x) {
-            const int blk = item / (H * nsplit), h = (item / nsplit) % H, split = item % nsplit;
-            const int nt = item_ntile(item);
-            if (nt == 0) continue;
-            // K_b, V_b: every S^T / dP^T MMA of the previous item has completed (kv_empty)
+        int64_t u = u_begin;
+        Seg sg;
+        while (next_seg(u, sg)) {
+            const int blk = sg.blk, h = sg.h, nt = sg.nt;
+            // K_b, V_b: every S^T / dP^T MMA of the previous segment has completed (kv_empty)
             if (nkv > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             if (lane == 0) {
                 tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
@@ -532,7 +555,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 const int src = t & 31;
                 if (src == 0) {
                     if (t + lane < nt) {
-                        const int tile = list[split + (t + lane) * nsplit];
+                        const int tile = list[sg.t0 + t + lane];
                         const int4 td = P.tiles[tile];
                         cx = td.x;
                         cy = td.y;
@@ -581,9 +604,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         const uint64_t dk0 = tc::smem_desc_sw128(sK, 16, 1024), dv0 = tc::smem_desc_sw128(sV, 16, 1024);
         int g = 0, hs = 0, nkv = 0;       // g: tile (stage) counter, hs: step counter
         bool stop = false;
-        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
-            const int nt = item_ntile(item);
-            if (nt == 0) continue;
+        int64_t u = u_begin;
+        Seg sg;
+        while (!stop && next_seg(u, sg)) {
+            const int nt = sg.nt;
             if (!tc::mbar_wait_warp(&bars->kv_full, nkv & 1, P.err, 2, abort_flag)) break;
             for (int t = 0; t < nt && !stop; ++t, ++g) {
                 if (!tc::mbar_wait_warp(&bars->full[g % kDkvStages], (g / kDkvStages) & 1, P.err, 2, abort_flag)) {
@@ -628,9 +652,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         const uint32_t idesc_acc = tc::idesc_bf16_f32(kBS, kHD, false, true);
         int g = 0, hs = 0, nkv = 0;
         bool stop = false;
-        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
-            const int nt = item_ntile(item);
-            if (nt == 0) continue;
+        int64_t u = u_begin;
+        Seg sg;
+        while (!stop && next_seg(u, sg)) {
+            const int nt = sg.nt;
             for (int t = 0; t < nt && !stop; ++t, ++g) {
                 // the stage's Q / dO (acquired directly; the stage is released by this warp)
                 if (!tc::mbar_wait_warp(&bars->full[g % kDkvStages], (g / kDkvStages) & 1, P.err, 2, abort_flag)) {
@@ -645,8 +670,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                         stop = true;
                         break;
                     }
-                    // the accumulators are reset by the item's first step; the epilogue
-                    // of the previous item must have read them
+                    // the accumulators are reset by the segment's first step; the
+                    // epilogue of the previous segment must have read them
                     if (t == 0 && half == 0 && nkv > 0 &&
                         !tc::mbar_wait_warp(&bars->acc_free, (nkv - 1) & 1, P.err, 2, abort_flag)) {
                         stop = true;
@@ -687,10 +712,10 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         int g = 0, hs = 0, nkv = 0;
         bool stop = false;
-        for (int item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
-            const int blk = item / (H * nsplit), h = (item / nsplit) % H;
-            const int nt = item_ntile(item);
-            if (nt == 0) continue;
+        int64_t u = u_begin;
+        Seg sg;
+        while (!stop && next_seg(u, sg)) {
+            const int blk = sg.blk, h = sg.h, nt = sg.nt;
             for (int t = 0; t < nt && !stop; ++t, ++g) {
                 const int s = g % kDkvStages;
                 // the loader's per-token metadata of this stage (acquire it directly)
@@ -743,7 +768,7 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 }
             }
             if (stop) break;
-            // epilogue of the item: 16 of the 64 dK columns and 16 of the 64 dV
+            // epilogue of the segment: 16 of the 64 dK columns and 16 of the 64 dV
             // columns per thread -> fp32 reductions
             if (!tc::mbar_wait_warp(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
@@ -798,10 +823,9 @@ static cudaError_t launch_bwd_tc_t(const CUtensorMap &mk, const CUtensorMap &mv,
     e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel<kDoRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kDkvSmem);
     if (e != cudaSuccess) return e;
-    const int nsplit = std::max(1, std::min(16, (2 * sms + nb * H - 1) / (nb * H)));
-    const int items2 = nb * H * nsplit;
-    read_bwd_dkdv_tc_kernel<kDoRows><<<std::min(items2, sms), kDkvThreads, kDkvSmem, st>>>(
-        mk, mv, mq, md, dout, lse, ws_delta, H, nb, top, nsplit, static_cast<int>(L.max_tiles), scale, scale_log2,
+    // one CTA per SM, each over an equal share of the (block, head, tile) units
+    read_bwd_dkdv_tc_kernel<kDoRows><<<sms, kDkvThreads, kDkvSmem, st>>>(
+        mk, mv, mq, md, dout, lse, ws_delta, H, nb, top, static_cast<int>(L.max_tiles), scale, scale_log2,
         P, dk_acc, dv_acc);
     count_launch();
     return cudaGetLastError();

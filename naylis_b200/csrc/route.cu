@@ -264,6 +264,7 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
 constexpr int kHeadTokens = 64;   // tokens per CTA
 constexpr int kHeadThreads = 128; // 4 warps x 16 tokens (mma path)
 constexpr int kHeadKC = 64;       // d-columns per pipeline step
+constexpr int kHeadStages = 4;    // cp.async ring depth of the tensor-core head (3 steps in flight)
 constexpr int kMaxNb = 64;
 constexpr int kMaxTop = 8;
 constexpr int kMaxRank = 128;
@@ -339,7 +340,7 @@ route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restri
     constexpr int kStage = kHqBytes + kWBytes;
     constexpr int NT = RANK / 8;                          // n-tiles of 8
     extern __shared__ __align__(128) unsigned char smem[];
-    float *sA = reinterpret_cast<float *>(smem + 2 * kStage);
+    float *sA = reinterpret_cast<float *>(smem + kHeadStages * kStage);
     float *sLogit = sA + kHeadTokens * RANK;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -348,7 +349,7 @@ route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restri
 
     auto issue = [&](int c) {
         if (c < nchunk) {
-            const uint32_t base = smem_u32(smem + (c & 1) * kStage);
+            const uint32_t base = smem_u32(smem + (c % kHeadStages) * kStage);
             for (int i = tid; i < kHeadTokens * 8; i += kHeadThreads) {
                 const int row = i >> 3, ch = i & 7;
                 const int64_t t = tok0 + row;
@@ -369,13 +370,14 @@ route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restri
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
 
-    issue(0);
+#pragma unroll
+    for (int c = 0; c < kHeadStages - 1; ++c) issue(c);
 #pragma unroll 1
     for (int c = 0; c < nchunk; ++c) {
-        issue(c + 1);
-        cp_async_wait<1>();
-        __syncthreads();
-        const uint32_t sq = smem_u32(smem + (c & 1) * kStage);
+        cp_async_wait<kHeadStages - 2>();
+        __syncthreads();   // step c landed for all threads; step c-1's buffer is no longer read
+        issue(c + kHeadStages - 1);
+        const uint32_t sq = smem_u32(smem + (c % kHeadStages) * kStage);
         const uint32_t sw = sq + kHqBytes;
 #pragma unroll
         for (int ks = 0; ks < kHeadKC / 16; ++ks) {
@@ -391,8 +393,8 @@ route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restri
                 mma_bf16_16816(acc[j + 1], a, bfr[2], bfr[3]);
             }
         }
-        __syncthreads();
     }
+    cp_async_wait<0>();
 
     // z -> act, kept as fp32 values rounded to bf16
     const int g = lane >> 2, q2 = (lane & 3) * 2;
@@ -515,7 +517,7 @@ cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_
                               float *log_gates, void *act, cudaStream_t st) {
     const int grid = static_cast<int>((ntok + kHeadTokens - 1) / kHeadTokens);
     if (cdt == MOM_BF16 && (r == 32 || r == 64) && d % kHeadKC == 0) {
-        const size_t smem = 2 * (kHeadTokens + r) * kHeadKC * 2 +
+        const size_t smem = kHeadStages * (kHeadTokens + r) * kHeadKC * 2 +
                             (kHeadTokens * r + kHeadTokens * kMaxNb) * sizeof(float);
         if (r == 32) {
             auto k = route_head_bf16_kernel<32>;

@@ -211,10 +211,12 @@ __device__ __forceinline__ void split_bf16(float v, uint16_t &hi, uint16_t &lo) 
 
 // dx[t, c] (+)= sum_j u[t, j] Wd[j, c] and dWd[j, c] += sum_t u[t, j] x[t, c] in one
 // pass over the tokens, so that x is read once and dx written once: CTA = 128
-// columns x kDxdwSteps steps of 64 tokens, 4 warps. Per step the u tile (bf16
-// high and residual parts) and the x tile are staged in shared memory; dx goes
-// out through a shared fp32 tile as 16-B vectors; the dWd partial sums stay in
-// registers across the steps and leave by fp32 reductions at the end.
+// columns x kDxdwSteps steps of 64 tokens, 4 warps. The next step's x tile (bf16 x:
+// cp.async into the other of two buffers) and raw fp32 u tile are in flight while a
+// step computes; per step u is split into bf16 high and residual parts in shared
+// memory; dx goes out through a shared fp32 tile (the step's x buffer, once read)
+// as 16-B vectors; the dWd partial sums stay in registers across the steps and
+// leave by fp32 reductions at the end.
 constexpr int kDxdwSteps = 4;
 template <int R>
 struct DxdwSmem {
@@ -222,11 +224,13 @@ struct DxdwSmem {
     static constexpr int kUStride = R * 2 + 16, kWStride = kCols * 2 + 16, kXStride = kCols * 2 + 16;
     static constexpr int kHalf = kCols / 2, kOS = kHalf + 4;
     static constexpr int kU = kTok * kUStride, kW = R * kWStride, kX = kTok * kXStride, kOut = kTok * kOS * 4;
-    static constexpr int kBytes = 2 * kU + kW + kX + kOut;
+    static constexpr int kURaw = kTok * R * 4;
+    static_assert(kOut <= kX, "the dx staging tile reuses an x buffer");
+    static constexpr int kBytes = 2 * kU + kW + 2 * kX + kURaw;
 };
 
 template <int R, int XDT, int DXDT>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(128, 3)
 route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restrict__ w_down,
                           const typename Elem<XDT>::T *__restrict__ x, int64_t ntok, int d,
                           typename Elem<DXDT>::T *__restrict__ dx, int accumulate, float *__restrict__ dw_down) {
@@ -236,8 +240,8 @@ route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restric
     unsigned char *sUh = smem;
     unsigned char *sUl = smem + L::kU;
     unsigned char *sW = smem + 2 * L::kU;
-    unsigned char *sX = sW + L::kW;
-    float *sOut = reinterpret_cast<float *>(sX + L::kX);
+    unsigned char *sXb = sW + L::kW;                                   // [2][kX]
+    float *sURaw = reinterpret_cast<float *>(sXb + 2 * L::kX);         // [kTok][R]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c0 = blockIdx.x * kCols;
     for (int i = tid; i < R * (kCols / 8); i += 128) {
@@ -247,44 +251,69 @@ route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restric
         if (c < d) v = *reinterpret_cast<const uint4 *>(w_down + static_cast<int64_t>(j) * d + c);
         *reinterpret_cast<uint4 *>(sW + j * L::kWStride + ch * 16) = v;
     }
+    auto step_tok0 = [&](int st) { return (static_cast<int64_t>(blockIdx.y) * kDxdwSteps + st) * kTok; };
+    // cp.async of step st's raw u tile (and, for bf16 x, its x tile into buffer st & 1)
+    auto prefetch = [&](int st) {
+        const int64_t tok0 = step_tok0(st);
+        if (st < kDxdwSteps && tok0 < ntok) {
+            const uint32_t su = smem_u32(sURaw);
+            for (int i = tid; i < kTok * R / 4; i += 128) {   // 16-B pieces of a contiguous tile
+                const int64_t t = tok0 + (i * 4) / R;
+                const bool ok = t < ntok;
+                cp_async16(su + i * 16, ok ? u + tok0 * R + i * 4 : u, ok ? 16 : 0);
+            }
+            if (XDT == MOM_BF16) {
+                const uint32_t sx = smem_u32(sXb + (st & 1) * L::kX);
+                for (int i = tid; i < kTok * (kCols / 8); i += 128) {
+                    const int tl = i / (kCols / 8), ch = i % (kCols / 8);
+                    const int64_t t = tok0 + tl;
+                    const int c = c0 + ch * 8;
+                    const bool ok = t < ntok && c < d;
+                    const uint16_t *src = reinterpret_cast<const uint16_t *>(x) + (ok ? t * d + c : 0);
+                    cp_async16(sx + tl * L::kXStride + ch * 16, src, ok ? 16 : 0);
+                }
+            }
+        }
+        cp_async_commit();
+    };
     float accw[MT][4][4];
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
         for (int n = 0; n < 4; ++n) accw[m][n][0] = accw[m][n][1] = accw[m][n][2] = accw[m][n][3] = 0.0f;
     const int g = lane >> 2, q2 = (lane & 3) * 2;
+    prefetch(0);
     for (int st = 0; st < kDxdwSteps; ++st) {
-        const int64_t tok0 = (static_cast<int64_t>(blockIdx.y) * kDxdwSteps + st) * kTok;
+        const int64_t tok0 = step_tok0(st);
         if (tok0 >= ntok) break;
-        __syncthreads();   // the previous step's readers of sU / sX / sOut are done
+        unsigned char *sX = sXb + (st & 1) * L::kX;
+        cp_async_wait<0>();
+        __syncthreads();   // step st's tiles landed; step st-1's readers of sU / its x buffer are done
         for (int i = tid; i < kTok * R; i += 128) {
             const int tl = i / R, j = i % R;
-            const int64_t t = tok0 + tl;
-            const float val = t < ntok ? u[t * R + j] : 0.0f;
             uint16_t hi, lo;
-            split_bf16(val, hi, lo);
+            split_bf16(sURaw[i], hi, lo);
             *reinterpret_cast<uint16_t *>(sUh + tl * L::kUStride + j * 2) = hi;
             *reinterpret_cast<uint16_t *>(sUl + tl * L::kUStride + j * 2) = lo;
         }
-        for (int i = tid; i < kTok * (kCols / 8); i += 128) {
-            const int tl = i / (kCols / 8), ch = i % (kCols / 8);
-            const int64_t t = tok0 + tl;
-            const int c = c0 + ch * 8;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (t < ntok && c < d) {
-                if (XDT == MOM_BF16) {
-                    v = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(x) + t * d + c);
-                } else {
+        if (XDT != MOM_BF16) {
+            for (int i = tid; i < kTok * (kCols / 8); i += 128) {
+                const int tl = i / (kCols / 8), ch = i % (kCols / 8);
+                const int64_t t = tok0 + tl;
+                const int c = c0 + ch * 8;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (t < ntok && c < d) {
                     const float *xf = reinterpret_cast<const float *>(x) + t * d + c;
                     v.x = pack_bf16x2(xf[0], xf[1]);
                     v.y = pack_bf16x2(xf[2], xf[3]);
                     v.z = pack_bf16x2(xf[4], xf[5]);
                     v.w = pack_bf16x2(xf[6], xf[7]);
                 }
+                *reinterpret_cast<uint4 *>(sX + tl * L::kXStride + ch * 16) = v;
             }
-            *reinterpret_cast<uint4 *>(sX + tl * L::kXStride + ch * 16) = v;
         }
-        __syncthreads();
+        __syncthreads();   // sU (and an fp32 x tile) ready; the raw u buffer and the other x buffer are free
+        prefetch(st + 1);
         // dx tile: warp = 16 tokens x 128 columns
         float acc[kCols / 8][4];
 #pragma unroll
@@ -333,10 +362,12 @@ route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restric
                 }
             }
         }
-        // dx out: stage the fp32 tile 64 columns at a time, then 16-B vectors
+        // dx out: stage the fp32 tile 64 columns at a time in this step's x buffer
+        // (every warp has finished reading it), then 16-B vectors
+        float *sOut = reinterpret_cast<float *>(sX);
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-            if (half) __syncthreads();
+            __syncthreads();
 #pragma unroll
             for (int n = 0; n < L::kHalf / 8; ++n)
 #pragma unroll
@@ -374,6 +405,7 @@ route_bwd_dxdw_mma_kernel(const float *__restrict__ u, const uint16_t *__restric
             }
         }
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int m = 0; m < MT; ++m)
 #pragma unroll
@@ -507,9 +539,10 @@ cudaError_t launch_route_bwd(const void *x, int xdt, int B, int S, int d, const 
     route_bwd_revscan_kernel<<<dim3((r + kRsCols - 1) / kRsCols, B), 1024, 0, st>>>(ws_dz, ws_u, S, r);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    // the tensor-core pair stores dx and reads x in 16-B vectors
+    // the tensor-core pass stores dx and reads x and u in 16-B vectors
     const bool tc = cdt == MOM_BF16 && (r == 32 || r == 64) && d % 8 == 0 &&
-                    (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+                    (reinterpret_cast<uintptr_t>(dx) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(ws_u) & 15) == 0;
     if (tc) {
         dim3 grid((d + 127) / 128, static_cast<unsigned>((ntok + 64 * kDxdwSteps - 1) / (64 * kDxdwSteps)));
 #define MOM_DXDW(R, X, D)                                                                                   \
