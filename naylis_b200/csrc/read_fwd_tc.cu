@@ -50,7 +50,7 @@ constexpr uint32_t kPCol = 256;                // P: group g's 64 slots at 256 +
 constexpr uint32_t kOCol = 384;                // O_0 at 384, O_1 at 448
 
 struct Bars {
-    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full, o_free, drain;
+    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full, o_free, drain, s_issued;
     uint32_t tmem_base;
     int abort;
     int meta[2];      // per stage: blocks loaded | (blocks of the set << 8); written before the stage's barrier
@@ -76,8 +76,14 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = *P.ntiles;
     const int nitems = ntiles * H;
-    // items of this CTA: blockIdx.x + i * gridDim.x, i < nmine
-    const int nmine = static_cast<int>(blockIdx.x) < nitems ? (nitems - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
+    // items of this CTA: a contiguous run it0 + i, i < nmine, ordered head-major
+    // (item = head * ntiles + tile), so that consecutive items usually share
+    // their block set and head: a stage keeps its K/V blocks when they repeat
+    const int per = (nitems + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+    const int it0 = static_cast<int>(blockIdx.x) * per;
+    const int nmine = max(0, min(nitems, it0 + per) - it0);
+    auto item_tile = [&](int item) { return item % ntiles; };
+    auto item_head = [&](int item) { return item / ntiles; };
     const int64_t ld = static_cast<int64_t>(H) * kHD;
 
     if (threadIdx.x == 0) {
@@ -91,6 +97,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         tc::mbar_init(&bars->p_full, kSoftThreads);
         tc::mbar_init(&bars->pv_done, 2);
         tc::mbar_init(&bars->drain, 2);
+        tc::mbar_init(&bars->s_issued, 1);
         bars->abort = 0;
     }
     if (warp == 1) {
@@ -111,24 +118,29 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         // ------------------------------------------------------------ loader
         tc::LaneTile lt;
         int issued = 0;
+        int stage_kv[2] = {-1, -1};   // (set, head) whose K/V blocks each stage holds
         for (int i = 0; i < nmine; ++i) {
-            const int item = blockIdx.x + i * gridDim.x;
+            const int item = it0 + i;
             const int s = i & 1, j = i >> 1, src = i & 31;
-            if (src == 0 && i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
+            if (src == 0 && i + lane < nmine) lt.fetch(P, item_tile(item + lane), top);
             const int x0 = tc::get(lt.x, src);
             const int nblk = tc::get(lt.nblk, src), b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
             if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
-            const int h = item % H;
+            const int h = item_head(item);
             const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kStageBytes;
             const uint32_t sK = sQ + kQBytes;
             const uint32_t sV = sK + 2 * kBlkBytes;
+            // the stage's K/V are still those of this set and head (item i-2): keep them
+            const int kv = tc::get(lt.key, src) * H + h;
+            const bool reload = kv != stage_kv[s];
+            stage_kv[s] = kv;
             if (lane == 0) {
                 bars->meta[s] = nload | (nblk << 8);   // released by the arrive below
-                tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + 2 * nload * kBlkBytes);
+                tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + (reload ? 2 * nload * kBlkBytes : 0));
                 // the tile's rows x0 .. x0+127 (rows past the tile are never stored)
                 tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
-                for (int jb = 0; jb < nload; ++jb) {
+                for (int jb = 0; reload && jb < nload; ++jb) {
                     const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
                     tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
                     tc::tma_load_2d(sV + jb * kBlkBytes, &tmap_v, h * kHD, blk * kBS, &bars->full[s]);
@@ -145,8 +157,9 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     } else if (warp == 1 || warp == 2) {
         // ------------------------------------------------------------ MMA issuers
         // Warp 1 issues S(i+1) as soon as the softmax has read S(i) (p_full of i),
-        // ahead of its half of PV(i), so that the softmax of i+1 starts while PV(i)
-        // still runs on the tensor pipe.
+        // ahead of its half of PV(i); warp 2 issues the other half only after that
+        // (s_issued), so S(i+1) runs first on the tensor pipe and the softmax of i+1
+        // starts while PV(i) still runs.
         const bool wa = warp == 1;
         const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
         auto issue_s = [&](int i) -> bool {   // warp 1: S(i) = Q K^T into TMEM columns 0..255
@@ -176,7 +189,14 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const uint32_t sV = base + s * kStageBytes + kQBytes + 2 * kBlkBytes;
             // P(i) written to TMEM (and S(i) read) by the softmax
             if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
-            if (wa && i + 1 < nmine && !issue_s(i + 1)) break;
+            if (wa) {
+                if (i + 1 < nmine && !issue_s(i + 1)) break;
+                // S(i+1) is in the tensor pipe ahead of both PV halves of i
+                if (lane == 0) tc::mbar_arrive(&bars->s_issued);
+                __syncwarp();
+            } else if (!tc::mbar_wait_warp(&bars->s_issued, i & 1, P.err, 2, abort_flag)) {
+                break;
+            }
             // O read by the epilogue of i-1
             if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
@@ -263,16 +283,16 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         int count = 0;
         bool dead = false;   // a bounded wait gave up: skip work, keep the barrier structure
         for (int i = 0; i < nmine; ++i) {
-            const int item = blockIdx.x + i * gridDim.x;
+            const int item = it0 + i;
             const int src = i & 31;
             if (src == 0) {
-                if (i + lane < nmine) lt.fetch(P, (blockIdx.x + (i + lane) * gridDim.x) / H, top);
+                if (i + lane < nmine) lt.fetch(P, item_tile(item + lane), top);
                 fetch(0, cur);
             } else {
                 cur = nxt;   // prefetched during item i-1
             }
             if (src < 31 && i + 1 < nmine) fetch(src + 1, nxt);
-            const int h = item % H, nblk = cur.nblk, tok = cur.tok;
+            const int h = item_head(item), nblk = cur.nblk, tok = cur.tok;
             const float bias = cur.bias;
             // the row sum of item i-1 (complete since the second barrier of i-1), read
             // before this item's first barrier lets anyone overwrite it
@@ -290,7 +310,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                     tc::tmem_ld32(trow + grp * 64 + c * 32, v);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(v[e]));
+                    for (int e = 0; e < 32; e += 2) mx = tc::fmax3(mx, __uint_as_float(v[e]), __uint_as_float(v[e + 1]));
                 }
                 mpart = fmaf(mx, scale_log2, bias);
             }

@@ -263,6 +263,13 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// max of three fp32 values in one instruction (PTX max.f32 with three sources, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;\n" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
 // ------------------------------------------------------------------ packed fp32 pairs
 // Two fp32 lanes in one 64-bit register pair (PTX .f32x2 arithmetic, sm_100):
 // one instruction issues both halves.
