@@ -31,6 +31,11 @@ METRIC = "MoM layer fwd+bwd tokens/s (router + read + projections), BASELINE con
 WORKLOAD = ("cfg2: one MoM layer fwd+bwd per GPU, B=8 S=2048 d=1024, 16x64 heads, "
             "bank 8x128 slots, router rank 32, top-2, bf16 autocast, fp32 master weights")
 
+# DRAM bytes per launch of the read's tensor-core kernels on this workload, measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum; forward 39.1 MB, dQ 85.6 MB, dK/dV 92.2 MB):
+# the roofline's traffic figure.
+READ_TRAFFIC_BYTES = (39.1 + 85.6 + 92.2) * 1e6
+
 
 def read_flops(N, d, top, bs):
     """Algorithmic read FLOPs, active slots only: fwd 4*N*d*La, bwd 8*N*d*La."""
@@ -272,7 +277,11 @@ def run_gpu(args):
                        if graph is not None else "off (eager launches)"},
             "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
                          "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
-                         "traffic": None, "kernel": "MoM read fwd+bwd (bucket + fwd + dq + dkdv)",
+                         "traffic": READ_TRAFFIC_BYTES,
+                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum of the three tensor-core "
+                                          "read kernels (fwd 39.1 + dq 85.6 + dkdv 92.2 MB), one ncu capture "
+                                          "each of this workload; bucketing and row copies not included"),
+                         "kernel": "MoM read fwd+bwd (bucket + fwd + dq + dkdv)",
                          "flops_per_launch": roof["flops"], "ms_per_launch": roof["ms"],
                          "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
             "router": extra["router"],
