@@ -389,34 +389,74 @@ def measure_kernels(layer, x, M, dout, dev, args):
 
 
 def measure_e2e(step, x, dout, dev, args, world, N):
-    """The same step through the public API with host buffers: per step, the
-    inputs (x, upstream grad) come from pinned host memory and dx goes back."""
+    """The same step through the public API with host buffers: every step copies
+    its inputs (x, upstream grad) from pinned host memory and its dx back, all
+    inside the timed region. The copies are pipelined across steps as a training
+    input pipeline would run them: step i+1's inputs travel host -> device on
+    one copy stream (into one of two device staging slots) while step i
+    computes, and step i's dx travels back on another; the compute stream moves
+    a staged slot into the step's own input buffers on the device (static under
+    a CUDA graph) and dx out of the step's gradient buffer."""
     import torch
     import torch.distributed as dist
     xh = x.detach().cpu().pin_memory()
     gh = dout.cpu().pin_memory()
-    dxh = torch.empty_like(xh).pin_memory()
-    xd, gd = x, dout          # the step's own device input buffers (static under a graph)
+    dxh = [torch.empty_like(xh).pin_memory() for _ in range(2)]
+    xd, gd = x, dout          # the step's own device input buffers
+    xs = [torch.empty_like(xd) for _ in range(2)]
+    gs = [torch.empty_like(gd) for _ in range(2)]
+    dxs = [torch.empty_like(xd) for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
+    ev = lambda: [torch.cuda.Event() for _ in range(2)]
+    in_ready, in_free, out_ready, out_free = ev(), ev(), ev(), ev()
     iters = max(5, min(50, args.steps))
 
-    def one():
-        with torch.no_grad():
-            xd.copy_(xh, non_blocking=True)
-            gd.copy_(gh, non_blocking=True)
-        step(xd, gd)
-        dxh.copy_(xd.grad, non_blocking=True)
+    def load(i):              # step i's inputs -> staging slot i % 2
+        k = i % 2
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(in_free[k])                # the slot's previous inputs were moved out
+            xs[k].copy_(xh, non_blocking=True)
+            gs[k].copy_(gh, non_blocking=True)
+            in_ready[k].record(h2d)
 
-    for _ in range(2):
-        one()
+    def run(i):
+        k = i % 2
+        comp.wait_event(in_ready[k])
+        with torch.no_grad():
+            xd.copy_(xs[k])
+            gd.copy_(gs[k])
+        in_free[k].record(comp)
+        step(xd, gd)
+        comp.wait_event(out_free[k])                  # the slot's previous dx reached the host
+        with torch.no_grad():
+            dxs[k].copy_(xd.grad)
+        out_ready[k].record(comp)
+        with torch.cuda.stream(d2h):
+            d2h.wait_event(out_ready[k])
+            dxh[k].copy_(dxs[k], non_blocking=True)
+            out_free[k].record(d2h)
+
+    def steps(n, start_ev=None):
+        if start_ev is not None:
+            h2d.wait_event(start_ev)
+        load(0)
+        for i in range(n):
+            if i + 1 < n:
+                load(i + 1)
+            run(i)
+        comp.wait_stream(d2h)                         # the last dx is on the host
+
+    steps(2)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        one()
-    b.record()
+    a.record(comp)
+    steps(iters, start_ev=a)
+    b.record(comp)
     torch.cuda.synchronize()
     ms = a.elapsed_time(b)
     if world > 1:
@@ -425,7 +465,8 @@ def measure_e2e(step, x, dout, dev, args, world, N):
         ms = float(t.item())
     return {"value": round(world * N * iters / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": xh.numel() * xh.element_size() + gh.numel() * gh.element_size(),
-            "d2h_bytes_per_step": dxh.numel() * dxh.element_size()}
+            "d2h_bytes_per_step": dxh[0].numel() * dxh[0].element_size(),
+            "copies": "pipelined across steps (separate host->device and device->host streams)"}
 
 
 # ------------------------------------------------------------------ CPU arms

@@ -178,14 +178,17 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
     typename Elem<CDT>::T *hc = hq + cofs;
     double sum0 = 0.0, sum1 = 0.0;
     float as0 = 0.0f, as1 = 0.0f;
-    int em0 = 1 << 20, em1 = 1 << 20;
+    // e_min from the smallest non-zero magnitude (finite values: the smallest
+    // magnitude has the smallest exponent field): a running unsigned min of
+    // |bits| - 1, where zero wraps to 0xFFFFFFFF and never wins
+    uint32_t mn0 = 0xFFFFFFFFu, mn1 = 0xFFFFFFFFu;
     auto take = [&](float2 v) {
         sum0 = __dadd_rn(sum0, static_cast<double>(v.x));
         sum1 = __dadd_rn(sum1, static_cast<double>(v.y));
         as0 = __fadd_ru(as0, fabsf(v.x));
         as1 = __fadd_ru(as1, fabsf(v.y));
-        if (v.x != 0.0f) em0 = min(em0, ulp_exponent<XDT>(v.x));
-        if (v.y != 0.0f) em1 = min(em1, ulp_exponent<XDT>(v.y));
+        mn0 = min(mn0, (__float_as_uint(v.x) & 0x7FFFFFFFu) - 1u);
+        mn1 = min(mn1, (__float_as_uint(v.y) & 0x7FFFFFFFu) - 1u);
     };
     {
         int t = t0;
@@ -202,8 +205,11 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
     s_sum[2 * c2 + 1][k] = sum1;
     s_abs[2 * c2][k] = as0;
     s_abs[2 * c2 + 1][k] = as1;
-    s_emin[2 * c2][k] = em0;
-    s_emin[2 * c2 + 1][k] = em1;
+    auto em_of = [](uint32_t mn) -> int {   // ulp exponent of the smallest non-zero element
+        return mn == 0xFFFFFFFFu ? (1 << 20) : ulp_exponent<XDT>(__uint_as_float(mn + 1u));
+    };
+    s_emin[2 * c2][k] = em_of(mn0);
+    s_emin[2 * c2 + 1][k] = em_of(mn1);
     __syncthreads();
     if (threadIdx.x < 64) {                                      // one thread per column
         const int cc = threadIdx.x;

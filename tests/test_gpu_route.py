@@ -163,6 +163,25 @@ def test_router_matches_oracle(compute, x_dtype, B, S, d, r, nb, top):
     assert O.scaled_err(got["gates"], rt["gates"]) < tol
 
 
+def test_router_prefix_certificate_fallback_inside_the_head():
+    """The bf16 router fuses the prefix mean into the head, with exact fp64 chunk
+    carries; columns whose dynamic range fails the certificate (a 1e-30 next to
+    O(1) values, a column scaled by 1e30) take the sequential walk for their
+    carries. Indices must still match the oracle bitwise."""
+    torch.manual_seed(41)
+    x = torch.randn(2, 300, 256)
+    x[0, 17, 5] = 1e-30
+    x[1, :, 77] *= 1e30
+    x = x.to(torch.bfloat16)
+    w_down = torch.randn(32, 256) * 0.02
+    w_up = torch.randn(8, 32) * 0.2
+    got = _route_gpu(x, w_down, w_up, 2, torch.bfloat16)
+    rt = O.router_forward(x.float().numpy(), w_down.numpy(), w_up.numpy(), 2, "bf16")
+    _assert_indices(got["top_idx"], rt, 2, "router with fallback columns")
+    assert O.scaled_err(got["probs"], rt["probs"]) < 2e-2
+    assert O.scaled_err(got["gates"], rt["gates"]) < 2e-2
+
+
 def test_router_noise_goes_into_topk_only():
     torch.manual_seed(3)
     x = torch.randn(2, 256, 512, dtype=torch.bfloat16)
