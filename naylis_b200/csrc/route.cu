@@ -276,30 +276,40 @@ constexpr int kMaxTop = 8;
 constexpr int kMaxRank = 128;
 
 // Epilogue shared by both head variants: sA holds act (fp32 values already
-// rounded to the compute dtype) for kHeadTokens tokens x r.
-template <int CDT>
-__device__ void head_epilogue(const float *sA, float *sLogit, const typename Elem<CDT>::T *w_up,
-                              int r, int nb, int top, int64_t tok0, int64_t ntok,
+// rounded to the compute dtype) for kHeadTokens tokens x r. W_up is staged in
+// shared memory as fp32 (rows padded to r + 1 floats: the warp's 8 blocks hit 8
+// banks), the logits are the same sequential fp32 FMA chains over j as the
+// reference's linear, fully unrolled when the rank is a compile-time R. Per
+// token: top-k on the logits (+ noise), then the softmax with one exp per logit.
+template <int CDT, int R>
+__device__ void head_epilogue(const float *sA, float *sLogit, float *sWu, const typename Elem<CDT>::T *w_up,
+                              int r_rt, int nb, int top, int64_t tok0, int64_t ntok,
                               const float *__restrict__ noise, float *__restrict__ probs,
                               void *__restrict__ top_idx, int idx64, float *__restrict__ gates,
                               float *__restrict__ log_gates) {
+    const int r = R > 0 ? R : r_rt;
+    const int ws = r + 1;
     const int tid = threadIdx.x;
+    for (int i = tid; i < nb * r; i += blockDim.x) sWu[(i / r) * ws + i % r] = Elem<CDT>::load(w_up, i);
+    __syncthreads();
     for (int i = tid; i < kHeadTokens * nb; i += blockDim.x) {
         const int tl = i / nb, e = i % nb;
+        const float *a = sA + tl * r, *w = sWu + e * ws;
         float acc = 0.0f;
-        for (int j = 0; j < r; ++j)
-            acc = __fmaf_rn(sA[tl * r + j], Elem<CDT>::load(w_up, static_cast<int64_t>(e) * r + j), acc);
+        if (R > 0) {
+#pragma unroll
+            for (int j = 0; j < R; ++j) acc = __fmaf_rn(a[j], w[j], acc);
+        } else {
+            for (int j = 0; j < r; ++j) acc = __fmaf_rn(a[j], w[j], acc);
+        }
         sLogit[tl * nb + e] = Elem<CDT>::round(acc);
     }
     __syncthreads();
     if (tid < kHeadTokens && tok0 + tid < ntok) {
         const int64_t t = tok0 + tid;
-        const float *lg = sLogit + tid * nb;
+        float *lg = sLogit + tid * nb;
         float m = -INFINITY;
         for (int e = 0; e < nb; ++e) m = fmaxf(m, lg[e]);
-        float ssum = 0.0f;
-        for (int e = 0; e < nb; ++e) ssum += expf(lg[e] - m);
-        for (int e = 0; e < nb; ++e) probs[t * nb + e] = expf(lg[e] - m) / ssum;
         // top-k by repeated selection: strictly greater wins, so among equal
         // values the lower block index is taken first.
         float vals[kMaxTop];
@@ -317,6 +327,14 @@ __device__ void head_epilogue(const float *sA, float *sLogit, const typename Ele
             vals[k] = best;
             idxs[k] = bi;
         }
+        // softmax over the clean logits, exp once per logit (in place)
+        float ssum = 0.0f;
+        for (int e = 0; e < nb; ++e) {
+            const float x = expf(lg[e] - m);
+            lg[e] = x;
+            ssum += x;
+        }
+        for (int e = 0; e < nb; ++e) probs[t * nb + e] = lg[e] / ssum;
         float gm = vals[0];
         for (int k = 1; k < top; ++k) gm = fmaxf(gm, vals[k]);
         float gs = 0.0f;
@@ -421,8 +439,9 @@ route_head_bf16_kernel(const uint16_t *__restrict__ hq, const uint16_t *__restri
         }
     }
     __syncthreads();
-    head_epilogue<MOM_BF16>(sA, sLogit, w_up, RANK, nb, top, tok0, ntok, noise, probs, top_idx,
-                            idx64, gates, log_gates);
+    // the cp.async ring is idle now: W_up goes there
+    head_epilogue<MOM_BF16, RANK>(sA, sLogit, reinterpret_cast<float *>(smem), w_up, RANK, nb, top, tok0, ntok,
+                                  noise, probs, top_idx, idx64, gates, log_gates);
 }
 
 // Generic SIMT head (fp32 compute dtype, or any rank): fp32 FMA accumulation.
@@ -471,7 +490,8 @@ route_head_simt_kernel(const typename Elem<CDT>::T *__restrict__ hq,
         if (act && t < ntok) Elem<CDT>::store(act, t * r + j, a);
     }
     __syncthreads();
-    head_epilogue<CDT>(sA, sLogit, w_up, r, nb, top, tok0, ntok, noise, probs, top_idx, idx64,
+    // sH and sW (contiguous, nb x (r + 1) floats fit) are idle now: W_up goes there
+    head_epilogue<CDT, 0>(sA, sLogit, sH, w_up, r, nb, top, tok0, ntok, noise, probs, top_idx, idx64,
                        gates, log_gates);
 }
 

@@ -12,8 +12,9 @@ autograd accumulates straight into the communication buffer (no copy). A
 post-accumulate hook marks the parameter ready; buckets are launched as
 asynchronous all-reduces strictly in bucket order (identical on every rank,
 as NCCL requires) as soon as all their parameters are ready, so the exchange
-overlaps the rest of the backward. ``finish()`` launches whatever is left,
-waits, and scales by 1/world.
+overlaps the rest of the backward. ``finish()`` launches whatever is left
+and waits; the average is NCCL's own (``ReduceOp.AVG``), or a division by the
+world size on backends without it.
 """
 from __future__ import annotations
 
@@ -31,6 +32,13 @@ class GradAllReduce:
         self.overlap = overlap
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.average = average
+        # NCCL averages inside the reduction (no extra pass over the buckets);
+        # other backends (gloo) sum, and finish() divides
+        self._op = dist.ReduceOp.SUM
+        self._divide = average and self.world > 1
+        if self._divide and dist.get_backend(process_group) == "nccl":
+            self._op = dist.ReduceOp.AVG
+            self._divide = False
         params = [p for p in module.parameters() if p.requires_grad]
         # gradients arrive roughly in reverse registration order
         params = list(reversed(params))
@@ -84,7 +92,7 @@ class GradAllReduce:
         while self._next < len(self.buckets) and (force or self._pending[self._next] == 0):
             buf = self.flat[self._next]
             if self.world > 1:
-                self._works.append(dist.all_reduce(buf, group=self.group, async_op=True))
+                self._works.append(dist.all_reduce(buf, op=self._op, group=self.group, async_op=True))
             self._next += 1
 
     def _on_ready(self, p):
@@ -98,7 +106,7 @@ class GradAllReduce:
         self._launch_ready(force=True)
         for w in self._works:
             w.wait()
-        if self.average and self.world > 1:
+        if self._divide:
             for buf in self.flat:
                 buf.div_(self.world)
         self._reset_state()
