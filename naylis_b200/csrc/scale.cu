@@ -9,12 +9,14 @@
 
 namespace mom {
 
-template <int ODT>
+// kVec: the arrays are aligned for 4-element vectors (16 B fp32, 8 B bf16);
+// otherwise every element takes the scalar tail loop.
+template <int ODT, bool kVec>
 __global__ void __launch_bounds__(256)
 scale_fwd_kernel(const typename Elem<ODT>::T *__restrict__ o, const float *__restrict__ scale, int64_t n,
                  float *__restrict__ y) {
     const float s = *scale;
-    const int64_t n4 = n / 4;
+    const int64_t n4 = kVec ? n / 4 : 0;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         float4 v;
@@ -32,23 +34,40 @@ scale_fwd_kernel(const typename Elem<ODT>::T *__restrict__ o, const float *__res
         y[i] = s * Elem<ODT>::load(o, i);
 }
 
-template <int ODT, int GDT>
+// elements 4i .. 4i+3 of a 16-B aligned array as fp32
+template <int DT>
+__device__ __forceinline__ void load4(const typename Elem<DT>::T *p, int64_t i, float (&v)[4]) {
+    if (DT == MOM_BF16) {
+        const uint2 raw = reinterpret_cast<const uint2 *>(p)[i];
+        v[0] = __uint_as_float(raw.x << 16);
+        v[1] = __uint_as_float(raw.x & 0xFFFF0000u);
+        v[2] = __uint_as_float(raw.y << 16);
+        v[3] = __uint_as_float(raw.y & 0xFFFF0000u);
+    } else {
+        const float4 f = reinterpret_cast<const float4 *>(p)[i];
+        v[0] = f.x;
+        v[1] = f.y;
+        v[2] = f.z;
+        v[3] = f.w;
+    }
+}
+
+template <int ODT, int GDT, bool kVec>
 __global__ void __launch_bounds__(256)
 scale_bwd_kernel(const typename Elem<GDT>::T *__restrict__ g, const typename Elem<ODT>::T *__restrict__ o,
                  const float *__restrict__ scale, int64_t n, typename Elem<ODT>::T *__restrict__ d_o,
                  float *__restrict__ d_scale) {
     const float s = *scale;
     float acc = 0.0f;
-    const int64_t n4 = n / 4;
+    const int64_t n4 = kVec ? n / 4 : 0;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        // four elements per thread, as one 16-B (fp32) or 8-B (bf16) vector per operand
         float gv[4], ov[4];
+        load4<GDT>(g, i, gv);
+        load4<ODT>(o, i, ov);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            gv[k] = Elem<GDT>::load(g, 4 * i + k);
-            ov[k] = Elem<ODT>::load(o, 4 * i + k);
-            acc = fmaf(gv[k], ov[k], acc);
-        }
+        for (int k = 0; k < 4; ++k) acc = fmaf(gv[k], ov[k], acc);
         if (ODT == MOM_BF16) {
             uint2 w;
             w.x = pack_bf16x2(s * gv[0], s * gv[1]);
@@ -80,12 +99,20 @@ static int scale_grid(int64_t n) {
     return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, 148 * 8)));
 }
 
+static bool vec_ok(const void *p, int dt) {
+    return (reinterpret_cast<uintptr_t>(p) & (dt == MOM_BF16 ? 7u : 15u)) == 0;
+}
+
 cudaError_t launch_scale_fwd(const void *o, int odt, const float *scale, int64_t n, float *y, cudaStream_t st) {
     if (n == 0) return cudaSuccess;
-    if (odt == MOM_BF16)
-        scale_fwd_kernel<MOM_BF16><<<scale_grid(n), 256, 0, st>>>(static_cast<const uint16_t *>(o), scale, n, y);
-    else
-        scale_fwd_kernel<MOM_F32><<<scale_grid(n), 256, 0, st>>>(static_cast<const float *>(o), scale, n, y);
+    const bool v = vec_ok(o, odt) && vec_ok(y, MOM_F32);
+    if (odt == MOM_BF16) {
+        if (v) scale_fwd_kernel<MOM_BF16, true><<<scale_grid(n), 256, 0, st>>>(static_cast<const uint16_t *>(o), scale, n, y);
+        else scale_fwd_kernel<MOM_BF16, false><<<scale_grid(n), 256, 0, st>>>(static_cast<const uint16_t *>(o), scale, n, y);
+    } else {
+        if (v) scale_fwd_kernel<MOM_F32, true><<<scale_grid(n), 256, 0, st>>>(static_cast<const float *>(o), scale, n, y);
+        else scale_fwd_kernel<MOM_F32, false><<<scale_grid(n), 256, 0, st>>>(static_cast<const float *>(o), scale, n, y);
+    }
     count_launch();
     return cudaGetLastError();
 }
@@ -94,11 +121,18 @@ cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, con
                              void *d_o, float *d_scale, cudaStream_t st) {
     cudaError_t e = cudaMemsetAsync(d_scale, 0, sizeof(float), st);
     if (e != cudaSuccess || n == 0) return e;
+    const bool v = vec_ok(g, gdt) && vec_ok(o, odt) && vec_ok(d_o, odt);
 #define MOM_SB(O, G)                                                                                   \
-    if (odt == O && gdt == G)                                                                          \
-        scale_bwd_kernel<O, G><<<scale_grid(n), 256, 0, st>>>(                                         \
-            static_cast<const typename Elem<G>::T *>(g), static_cast<const typename Elem<O>::T *>(o), scale, \
-            n, static_cast<typename Elem<O>::T *>(d_o), d_scale);
+    if (odt == O && gdt == G) {                                                                        \
+        if (v)                                                                                         \
+            scale_bwd_kernel<O, G, true><<<scale_grid(n), 256, 0, st>>>(                               \
+                static_cast<const typename Elem<G>::T *>(g), static_cast<const typename Elem<O>::T *>(o), scale, \
+                n, static_cast<typename Elem<O>::T *>(d_o), d_scale);                                  \
+        else                                                                                           \
+            scale_bwd_kernel<O, G, false><<<scale_grid(n), 256, 0, st>>>(                              \
+                static_cast<const typename Elem<G>::T *>(g), static_cast<const typename Elem<O>::T *>(o), scale, \
+                n, static_cast<typename Elem<O>::T *>(d_o), d_scale);                                  \
+    }
     MOM_SB(MOM_BF16, MOM_F32)
     MOM_SB(MOM_BF16, MOM_BF16)
     MOM_SB(MOM_F32, MOM_F32)

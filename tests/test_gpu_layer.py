@@ -106,15 +106,19 @@ def test_resolve_mode_contract_on_gpu():
 
 
 @pytest.mark.parametrize("g_dtype", [torch.float32, torch.bfloat16])
-def test_fused_output_scale_matches_torch(g_dtype):
+@pytest.mark.parametrize("offset", [0, 1])
+def test_fused_output_scale_matches_torch(g_dtype, offset):
     """mom_scale (model.py:239 fused): fp32 y = s * o from bf16 o; backward
-    d_o = s * g in bf16 and d_s = sum(g * o), against torch's own mul."""
+    d_o = s * g in bf16 and d_s = sum(g * o), against torch's own mul. offset 1
+    starts o and g one element into their storage (not vector-aligned: the
+    kernels' scalar path)."""
     from naylis_b200 import mom_kernels as mk
     torch.manual_seed(0)
     dev = torch.device("cuda")
-    o = torch.randn(3, 257, 64, device=dev).to(torch.bfloat16).requires_grad_(True)
+    n = 3 * 257 * 64
+    o = torch.randn(n + offset, device=dev).to(torch.bfloat16)[offset:].view(3, 257, 64).requires_grad_(True)
     s = torch.tensor([0.37], device=dev, requires_grad=True)
-    g = torch.randn(3, 257, 64, device=dev).to(g_dtype)
+    g = torch.randn(n + offset, device=dev).to(g_dtype)[offset:].view(3, 257, 64)
     y = mk.mom_scale(o, s)
     y.backward(g)
     o2 = o.detach().clone().requires_grad_(True)
