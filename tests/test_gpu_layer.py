@@ -128,3 +128,25 @@ def test_fused_output_scale_matches_torch(g_dtype, offset):
     assert y.dtype == torch.float32 and torch.equal(y, y2)
     assert torch.equal(o.grad, o2.grad)
     assert abs(float(s.grad) - float(s2.grad)) <= 1e-5 * abs(float(s2.grad))
+
+
+def test_layer_grad_checkpoint_recompute_matches():
+    """mom_grad_ckpt (model.py:233-238): the read runs under
+    torch.utils.checkpoint, so its forward kernels run a second time during the
+    backward. The forward kernels are deterministic: output and routing equal
+    the run without checkpointing bitwise; the gradients, which sum fp32
+    partials by atomics in an order that varies between runs, agree to a
+    scaled 1e-4. Config-2 geometry at 2 x 512 tokens, so the tensor-core read
+    kernels are the ones recomputed."""
+    geo = dict(gi.SMALL_BF16)
+    geo.update(B=2, S=512, d=1024, H=16, nb=8, bs=128, top=2, r=32, seed=77)
+    res = []
+    for ckpt in (False, True):
+        layer, inp = _layer(geo)
+        layer.mom_grad_ckpt = ckpt
+        res.append(_run(layer, inp, gi.upstream_grad(geo)))
+    for key in ("out", "top_idx"):
+        assert np.array_equal(res[0][key], res[1][key]), key
+    errs = {k: O.scaled_err(res[1][k], res[0][k]) for k in res[0] if k not in ("out", "top_idx")}
+    assert all(e < 1e-4 for e in errs.values()), errs
+
