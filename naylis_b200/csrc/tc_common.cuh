@@ -44,9 +44,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same test with a suspend-time hint: the thread is suspended in hardware
+// until the phase completes or `hint_ns` nanoseconds pass, so a waiting warp
+// does not take issue slots from the warps still computing on its SM
+// sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Upper bound of one wait, in SM clock cycles (~1 s at 1.9 GHz): far above any
 // legitimate wait in these kernels, far below a hang.
 constexpr long long kWaitLimitCycles = 2000000000LL;
+// Suspend hint of one try (ns): the abort flag and the time limit are checked
+// between tries, so another role's abort is seen within about this time.
+constexpr uint32_t kWaitSuspendNs = 200000;
 
 // Wait for the phase of `parity` to complete. Returns false (and sets bit
 // `err_bit` of *err, and *abort) on timeout or when another role aborted.
@@ -54,11 +73,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
                                           volatile int *abort) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    int spins = 0;
     while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_suspend(bar, parity, kWaitSuspendNs)) return true;
         if (*abort) return false;
-        if (++spins > 32) __nanosleep(64);
         if (clock64() - t0 > kWaitLimitCycles) {
             atomicOr(err, err_bit);
             *abort = 1;
