@@ -165,6 +165,42 @@ MOM_API int mom_read_bwd_noalloc(const void *q, const void *k, const void *v, co
                                  const void *q_rows, void *dq, float *dk_acc, float *dv_acc,
                                  float *dlog_gates, void *stream);
 
+/* ------------------------------------------------------------------ block-split read
+ * The same read (mom_kernels/__init__.py:87-102 -> triton_gpu.py:323-409) for
+ * top-k routing whose block sets are more than the set bucketing holds
+ * (mom_plan_size() returns 0 there: top-4 of 32 blocks has 35,960 sets). Each
+ * (token, k) pair becomes a row of a top-1 plan that reads its one block; a
+ * token's rows are combined by their log-sum-exp into the softmax over the
+ * union of its blocks, the reference's result. A block chosen twice by a token
+ * is read once with the sum of its log-gates, as in the reference's bias.
+ *
+ * Plan: mom_plan_split_size() bytes, filled by mom_bucket_split from top_idx
+ * (N, top) and log_gates (N, top). mom_plan_check(plan, N*top, nb, 1) reads its
+ * error word. Forward: out (B,S,H,hd) of dtype; lse_rows (H, B*S*top) fp32 and
+ * weights (B*S*top, H) fp32 (the rows' share of each token's softmax), both
+ * saved for the backward; q_rows: B*S*top*H*hd elements of dtype, filled here;
+ * workspace: the rows' outputs. Backward: as mom_read_bwd, dlog_gates (B*S, top)
+ * in the caller's top order. No counterpart entry in the reference. */
+MOM_API size_t mom_plan_split_size(int64_t N, int64_t nb, int64_t top);
+MOM_API int mom_bucket_split(const void *top_idx, int idx_dtype, const float *log_gates, int64_t N,
+                             int64_t nb, int64_t top, void *plan, size_t plan_bytes, void *stream);
+MOM_API size_t mom_read_split_fwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd,
+                                                 int64_t top);
+MOM_API int mom_read_split_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B,
+                               int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top,
+                               const void *top_idx, int idx_dtype, const void *plan, void *out,
+                               float *lse_rows, float *weights, void *q_rows, void *workspace,
+                               size_t workspace_bytes, void *stream);
+MOM_API size_t mom_read_split_bwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd,
+                                                 int64_t top);
+MOM_API int mom_read_split_bwd(const void *q, const void *k, const void *v, const void *out,
+                               const void *dout, const float *lse_rows, const float *weights,
+                               int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb,
+                               int64_t bs, int64_t top, const void *top_idx, int idx_dtype,
+                               const void *plan, const void *q_rows, void *dq, float *dk_acc,
+                               float *dv_acc, float *dlog_gates, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------ output scale
  * ReZero output scale of the layer, fused: y = scale[0] * o with y in fp32
  * (model.py:239, `self.mom_scale * out`: a (1,) fp32 parameter times the bf16

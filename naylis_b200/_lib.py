@@ -49,6 +49,14 @@ SIGNATURES = {
     "mom_read_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "mom_read_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                             _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
+    "mom_plan_split_size": (_sz, [_i64, _i64, _i64]),
+    "mom_bucket_split": (_int, [_vp, _int, _fp, _i64, _i64, _i64, _vp, _sz, _vp]),
+    "mom_read_split_fwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mom_read_split_fwd": (_int, [_vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                  _int, _vp, _vp, _fp, _fp, _vp, _vp, _sz, _vp]),
+    "mom_read_split_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mom_read_split_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
+                                  _i64, _i64, _vp, _int, _vp, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
     "mom_read_bwd_noalloc_max_bytes": (_sz, []),
     "mom_read_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp]),

@@ -371,6 +371,140 @@ int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, c
                          dv_acc, dlog_gates, delta, do_rows, stream);
 }
 
+// ------------------------------------------------------------------ block-split read
+// Top-k routing with more block sets than the set bucketing holds: every
+// (token, k) pair is a row of a top-1 plan over B*S*top rows, read by the same
+// kernels with PlanView::rows_per_q = top, then combined per token (split.cu).
+namespace {
+size_t split_tail_offset(int64_t M, int64_t nb) { return align256(mom::plan_layout(M, nb, 1).total); }
+
+int check_split_geometry(int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs,
+                         int64_t top) {
+    MOM_REQUIRE(top > 0 && top <= mom::kMaxTop && top <= nb, "bad (num_blocks, top)");
+    MOM_REQUIRE(B >= 0 && S >= 0 && B * S * top < (int64_t(1) << 31), "B*S*top too large");
+    return check_read_geometry(dtype, 1, B * S * top, H, hd, nb, bs, 1);
+}
+}  // namespace
+
+size_t mom_plan_split_size(int64_t N, int64_t nb, int64_t top) {
+    if (N < 0 || nb <= 0 || nb > 64 || top <= 0 || top > mom::kMaxTop || top > nb) return 0;
+    const int64_t M = N * top;
+    if (M >= (int64_t(1) << 31)) return 0;
+    return split_tail_offset(M, nb) + align256(static_cast<size_t>(M) * 4);
+}
+
+int mom_bucket_split(const void *top_idx, int idx_dtype, const float *log_gates, int64_t N, int64_t nb,
+                     int64_t top, void *plan, size_t plan_bytes, void *stream) {
+    MOM_REQUIRE(N >= 0 && nb > 0 && nb <= 64 && top > 0 && top <= mom::kMaxTop && top <= nb,
+                "bad (tokens, num_blocks, top)");
+    MOM_REQUIRE(N * top < (int64_t(1) << 31), "token count out of range");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(plan, "null plan");
+    const size_t need = mom_plan_split_size(N, nb, top);
+    if (plan_bytes < need) return fail(MOM_ERR_WORKSPACE, "plan %zu < %zu bytes", plan_bytes, need);
+    MOM_REQUIRE(N == 0 || (top_idx && log_gates), "null routing tensors");
+    int rc = check_current_device();
+    if (rc) return rc;
+    const int64_t M = N * top;
+    const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
+    const mom::PlanView P = mom::plan_view(plan, L);
+    float *lg_rows = reinterpret_cast<float *>(static_cast<char *>(plan) + split_tail_offset(M, nb));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int idx64 = idx_dtype == MOM_I64;
+    cudaError_t e = mom::launch_split_prep(top_idx, idx64, log_gates, N, (int)top, lg_rows, st);
+    if (e == cudaSuccess) e = mom::launch_bucket(top_idx, idx64, lg_rows, L, P, st);
+    if (e != cudaSuccess) return cuda_fail(e, "bucket_split");
+    return MOM_OK;
+}
+
+size_t mom_read_split_fwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd, int64_t top) {
+    if (B < 0 || S < 0 || H < 0 || hd < 0 || top < 0) return 0;
+    return align256(static_cast<size_t>(B) * S * top * H * hd * 2);
+}
+
+int mom_read_split_fwd(const void *q, const void *k, const void *v, int dtype, int64_t B, int64_t S, int64_t H,
+                       int64_t hd, int64_t nb, int64_t bs, int64_t top, const void *top_idx, int idx_dtype,
+                       const void *plan, void *out, float *lse_rows, float *weights, void *q_rows,
+                       void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_split_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(q && k && v && top_idx && plan && out && lse_rows && weights && q_rows, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q) & 15) == 0 && (reinterpret_cast<uintptr_t>(q_rows) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                "q, q_rows and out must be 16-byte aligned");
+    const size_t need = mom_read_split_fwd_workspace_size(B, S, H, hd, top);
+    if (workspace_bytes < need || !workspace)
+        return fail(MOM_ERR_WORKSPACE, "split read fwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    const int64_t N = B * S, M = N * top;
+    const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
+    mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    P.rows_per_q = (int)top;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = mom::launch_read_fwd(q, k, v, 1, (int)M, (int)H, (int)hd, (int)nb, (int)bs, 1, L, P, workspace,
+                                         lse_rows, q_rows, st);
+    if (e == cudaSuccess)
+        e = mom::launch_split_combine(workspace, lse_rows, P.perm, top_idx, idx_dtype == MOM_I64, N, (int)top, (int)H,
+                                      (int)hd, weights, out, st);
+    if (e != cudaSuccess) return cuda_fail(e, "read_split_fwd");
+    return MOM_OK;
+}
+
+size_t mom_read_split_bwd_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd, int64_t top) {
+    if (B < 0 || S < 0 || H < 0 || hd < 0 || top < 0) return 0;
+    const size_t M = static_cast<size_t>(B) * S * top;
+    return align256(M * H * 4) + 3 * align256(M * H * hd * 2);
+}
+
+int mom_read_split_bwd(const void *q, const void *k, const void *v, const void *out, const void *dout,
+                       const float *lse_rows, const float *weights, int dtype, int64_t B, int64_t S, int64_t H,
+                       int64_t hd, int64_t nb, int64_t bs, int64_t top, const void *top_idx, int idx_dtype,
+                       const void *plan, const void *q_rows, void *dq, float *dk_acc, float *dv_acc,
+                       float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_split_geometry(dtype, B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    MOM_REQUIRE(k && v && dk_acc && dv_acc, "null pointer argument");
+    MOM_REQUIRE(B * S == 0 || (q && out && dout && lse_rows && weights && top_idx && plan && q_rows && dq &&
+                               dlog_gates),
+                "null pointer argument");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(q_rows) & 15) == 0 && (reinterpret_cast<uintptr_t>(dout) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (reinterpret_cast<uintptr_t>(dq) & 15) == 0,
+                "q_rows, out, dout and dq must be 16-byte aligned");
+    const size_t need = mom_read_split_bwd_workspace_size(B, S, H, hd, top);
+    if (workspace_bytes < need || (need && !workspace))
+        return fail(MOM_ERR_WORKSPACE, "split read bwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t N = B * S, M = N * top;
+    if (N == 0) {
+        const size_t kv = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
+        cudaError_t e = cudaMemsetAsync(dk_acc, 0, kv, st);
+        if (e == cudaSuccess) e = cudaMemsetAsync(dv_acc, 0, kv, st);
+        return e == cudaSuccess ? MOM_OK : cuda_fail(e, "read_split_bwd");
+    }
+    const size_t rows_bytes = align256(static_cast<size_t>(M) * H * hd * 2);
+    char *ws = static_cast<char *>(workspace);
+    float *delta = reinterpret_cast<float *>(ws);
+    char *g = ws + align256(static_cast<size_t>(M) * H * 4);
+    char *dq_rows = g + rows_bytes;
+    char *do_rows = dq_rows + rows_bytes;
+    const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
+    mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    P.rows_per_q = (int)top;
+    const int idx64 = idx_dtype == MOM_I64;
+    cudaError_t e = mom::launch_split_gate_do(dout, weights, N, (int)top, (int)H, (int)hd, g, st);
+    if (e == cudaSuccess)
+        e = mom::launch_read_bwd(q, q_rows, k, v, out, g, lse_rows, 1, (int)M, (int)H, (int)hd, (int)nb, (int)bs, 1,
+                                 L, P, dq_rows, dk_acc, dv_acc, dlog_gates, delta, do_rows, st);
+    if (e == cudaSuccess)
+        e = mom::launch_split_dq_sum(dq_rows, top_idx, idx64, N, (int)top, (int)H, (int)hd, dq, dlog_gates, st);
+    if (e != cudaSuccess) return cuda_fail(e, "read_split_bwd");
+    return MOM_OK;
+}
+
 // ------------------------------------------------- read backward, no allocation
 // mom_read_bwd_noalloc runs mom_read_bwd with its workspace (the per-row delta,
 // H x B*S fp32) in a fixed device array of this library instead of caller

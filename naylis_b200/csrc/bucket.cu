@@ -77,6 +77,7 @@ PlanView plan_view(void *plan, const PlanLayout &L) {
     v.tiles = reinterpret_cast<int4 *>(p + L.off_tiles);
     v.blkcount = reinterpret_cast<int *>(p + L.off_blkcount);
     v.blktiles = reinterpret_cast<int *>(p + L.off_blktiles);
+    v.rows_per_q = 1;
     return v;
 }
 

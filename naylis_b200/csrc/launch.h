@@ -14,6 +14,7 @@ uint64_t launches();
 constexpr int kTileM = 128;       // tokens per read tile (one routing set per tile)
 constexpr int kMaxKeys = 8192;    // routing sets the bucketing supports
 constexpr int kBucketChunk = 256;    // tokens per bucketing chunk (one CTA)
+constexpr int kMaxTop = 8;        // top_blocks the library takes
 
 // Routing sets of size s <= top over nb blocks, ranked by the combinatorial
 // number system; key = (number of sets of smaller size) + rank.
@@ -44,6 +45,11 @@ struct PlanView {
     int4 *tiles;         // [max_tiles] {first row, rows, key, 0}
     int *blkcount;       // [nb]
     int *blktiles;       // [nb][max_tiles] tiles whose set contains block b
+    // Rows of q (and, in the backward, of the output O used for delta) are
+    // perm[r] / rows_per_q: 1 for a plan over tokens; `top` for a plan over
+    // (token, k) pairs, where every token's q row serves its `top` rows while
+    // the per-row outputs, dO and dQ stay indexed by perm[r].
+    int rows_per_q;
 };
 PlanView plan_view(void *plan, const PlanLayout &L);
 
@@ -65,12 +71,13 @@ cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, con
 cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
                           const PlanLayout &L, const PlanView &P, cudaStream_t st);
 // Row copy into routing-plan order: dst[r] = src[perm[r]] (rows of row_bytes, a multiple of 16).
+// rows_per_src: dst[r] = src[perm[r] / rows_per_src] (a plan over (token, k) rows).
 cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, const int *perm, void *dst,
-                                cudaStream_t st);
+                                cudaStream_t st, int rows_per_src = 1);
 // delta[h][r] = <dO, O> of plan row r's token and head h (fp32), dO's row copied to
 // do_rows[r] when do_rows is not null.
 cudaError_t launch_row_delta(const void *dout, const void *out, int64_t N, int H, int hd, const int *perm,
-                             void *do_rows, float *delta, cudaStream_t st);
+                             void *do_rows, float *delta, cudaStream_t st, int rows_per_out = 1);
 // Read forward. q is token-ordered; q_rows (N x H*hd, same dtype) receives q in
 // plan order and is what the tensor-core kernels (and the backward) read.
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
@@ -87,6 +94,19 @@ cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v,
                                bool do_is_rows, const float *lse, int H, int nb, int top, const PlanLayout &L,
                                const PlanView &P, void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
                                float *ws_delta, cudaStream_t st);
+// Block-split read (split.cu): rows are (token, k) pairs of a top-1 plan built
+// over N*top rows with PlanView::rows_per_q = top.
+cudaError_t launch_split_prep(const void *top_idx, int idx64, const float *log_gates, int64_t N, int top,
+                              float *lg_rows, cudaStream_t st);
+// weights (N*top, H) fp32: a_k = exp(lse_k - logsumexp over the token's live rows);
+// out (N, H*hd) = sum_k a_k out_rows[t*top + k] (bf16).
+cudaError_t launch_split_combine(const void *out_rows, const float *lse_rows, const int *perm, const void *top_idx,
+                                 int idx64, int64_t N, int top, int H, int hd, float *weights, void *out,
+                                 cudaStream_t st);
+cudaError_t launch_split_gate_do(const void *dout, const float *weights, int64_t N, int top, int H, int hd, void *g,
+                                 cudaStream_t st);
+cudaError_t launch_split_dq_sum(const void *dq_rows, const void *top_idx, int idx64, int64_t N, int top, int H,
+                                int hd, void *dq, float *dlog_gates, cudaStream_t st);
 // Read backward. q_rows: as filled by launch_read_fwd. do_rows: N x H*hd scratch for
 // dO in plan order, or null (the tensor-core kernels then gather dO rows).
 cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, const void *v, const void *out,

@@ -77,10 +77,11 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
             const int r = i / kChunks, ch = i % kChunks;
             const int tok = sTok[r];
             const int64_t off = tok >= 0 ? tok * ld + h * HD + ch * 8 : 0;
+            const int64_t offq = tok >= 0 ? (tok / P.rows_per_q) * ld + h * HD + ch * 8 : 0;
             const int nbytes = tok >= 0 ? 16 : 0;
-            cp_async16(smem_u32(sQ) + swz(r, ch, kRowB), q + off, nbytes);
+            cp_async16(smem_u32(sQ) + swz(r, ch, kRowB), q + offq, nbytes);
             cp_async16(smem_u32(sdO) + swz(r, ch, kRowB), dout + off, nbytes);
-            cp_async16(smem_u32(sO) + swz(r, ch, kRowB), o + off, nbytes);
+            cp_async16(smem_u32(sO) + swz(r, ch, kRowB), o + offq, nbytes);
         }
         cp_async_commit();
         auto issue = [&](int c) {
@@ -227,7 +228,9 @@ read_bwd_dq_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ 
                 sa += dba[r][jj];
                 sb += dbb[r][jj];
             }
-            const float delta_row = sb > 0.0f ? sa / sb : 0.0f;
+            // a plan over (token, k) rows reads one block per row: its gate term
+            // needs the whole token's delta (from the combined O), not the block's
+            const float delta_row = P.rows_per_q > 1 ? (r == 0 ? dl0 : dl1) : (sb > 0.0f ? sa / sb : 0.0f);
 #pragma unroll
             for (int jj = 0; jj < kMaxTopBwd; ++jj) dbacc[r][jj] += fmaf(-delta_row, dbb[r][jj], dba[r][jj]);
         }
@@ -334,7 +337,8 @@ read_bwd_dkdv_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict_
                 const int r = e / kChunks, ch = e % kChunks;
                 const int tok = sTok[buf * kTileM + r];
                 const int64_t off = tok >= 0 ? tok * ld + h * HD + ch * 8 : 0;
-                cp_async16(sq + swz(r, ch, kRowB), q + off, tok >= 0 ? 16 : 0);
+                const int64_t offq = tok >= 0 ? (tok / P.rows_per_q) * ld + h * HD + ch * 8 : 0;
+                cp_async16(sq + swz(r, ch, kRowB), q + offq, tok >= 0 ? 16 : 0);
                 cp_async16(sd + swz(r, ch, kRowB), dout + off, tok >= 0 ? 16 : 0);
             }
         }
@@ -491,7 +495,8 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
     if (read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H)) {
         // delta = <dO, O> per plan row and head, and dO in plan order when there is
         // room for it (every tile's rows are then one TMA box)
-        if ((e = launch_row_delta(dout, out, N, H, hd, P.perm, do_rows, ws_delta, st)) != cudaSuccess) return e;
+        if ((e = launch_row_delta(dout, out, L.N, H, hd, P.perm, do_rows, ws_delta, st, P.rows_per_q)) != cudaSuccess)
+            return e;
         if (do_rows)
             return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                       dlog_gates, ws_delta, st);

@@ -349,12 +349,15 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             part[(4 + grp) * kTM + r] = pb;
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
-            const float delta = part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
+            // a plan over (token, k) rows reads one block per row: its gate term
+            // needs the whole token's delta (the row kernel's, from the combined O)
+            const bool pseudo = P.rows_per_q > 1;
+            const float delta = pseudo ? cur.dlt : part[r] + part[kTM + r] + part[2 * kTM + r] + part[3 * kTM + r];
             // gate gradient (sum over heads by fp32 atomics). A set of one block gets
             // none: its gates shift all of the token's scores alike, which the
             // softmax cancels, so the gradient is exactly zero (dlog_gates is zeroed
             // before the kernels run).
-            if (grp == 0 && tok >= 0 && nblk > 1) {
+            if (grp == 0 && tok >= 0 && (nblk > 1 || pseudo)) {
                 const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
                 const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
                 const uint32_t kmap = cur.kmap;

@@ -49,7 +49,7 @@ read_fwd_kernel(const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
     for (int i = tid; i < kTileM * kChunks; i += kReadThreads) {
         const int r = i / kChunks, ch = i % kChunks;
         const int tok = sTok[r];
-        const uint16_t *src = tok >= 0 ? q + tok * ld + h * HD + ch * 8 : q;
+        const uint16_t *src = tok >= 0 ? q + (tok / P.rows_per_q) * ld + h * HD + ch * 8 : q;
         cp_async16(smem_u32(sQ) + swz(r, ch, kRowB), src, tok >= 0 ? 16 : 0);
     }
     cp_async_commit();
@@ -236,7 +236,7 @@ cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, 
     (void)B; (void)S; (void)nb;
     if (L.max_tiles == 0) return cudaSuccess;
     // q in plan order, for the tensor-core kernels of this call and of the backward
-    cudaError_t e = launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st);
+    cudaError_t e = launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st, P.rows_per_q);
     if (e != cudaSuccess) return e;
     // the tensor-core kernel covers head_dim 64, 128-slot blocks, top <= 2;
     // other geometries take the warp-level mma kernel below

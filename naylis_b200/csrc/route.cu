@@ -272,7 +272,6 @@ constexpr int kHeadThreads = 128; // 4 warps x 16 tokens (mma path)
 constexpr int kHeadKC = 64;       // d-columns per pipeline step
 constexpr int kHeadStages = 4;    // cp.async ring depth of the tensor-core head (3 steps in flight)
 constexpr int kMaxNb = 64;
-constexpr int kMaxTop = 8;
 constexpr int kMaxRank = 128;
 
 // Epilogue shared by both head variants: sA holds act (fp32 values already

@@ -14,11 +14,11 @@ namespace mom {
 // One warp per row, 16-B vectors; row_bytes is a multiple of 16.
 __global__ void __launch_bounds__(256)
 permute_rows_kernel(const uint4 *__restrict__ src, const int *__restrict__ perm, int64_t N, int vec_per_row,
-                    uint4 *__restrict__ dst) {
+                    int rows_per_src, uint4 *__restrict__ dst) {
     const int lane = threadIdx.x & 31;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < N; r += nwarps) {
-        const int64_t t = perm[r];
+        const int64_t t = perm[r] / rows_per_src;
         const uint4 *s = src + t * vec_per_row;
         uint4 *d = dst + r * vec_per_row;
         for (int i = lane; i < vec_per_row; i += 32) d[i] = s[i];
@@ -26,14 +26,15 @@ permute_rows_kernel(const uint4 *__restrict__ src, const int *__restrict__ perm,
 }
 
 cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, const int *perm, void *dst,
-                                cudaStream_t st) {
+                                cudaStream_t st, int rows_per_src) {
     if (N == 0) return cudaSuccess;
     if (row_bytes % 16 != 0 || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
         return cudaErrorInvalidValue;
     const int64_t want = (N + 7) / 8;
     const int grid = static_cast<int>(std::min<int64_t>(want, 148 * 16));
     permute_rows_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4 *>(src), perm, N,
-                                              static_cast<int>(row_bytes / 16), static_cast<uint4 *>(dst));
+                                              static_cast<int>(row_bytes / 16), rows_per_src,
+                                              static_cast<uint4 *>(dst));
     count_launch();
     return cudaGetLastError();
 }
@@ -45,14 +46,14 @@ cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, c
 // lanes that share a head combine their partial sums by shuffles.
 __global__ void __launch_bounds__(256)
 row_delta_kernel(const uint4 *__restrict__ dout, const uint4 *__restrict__ out, const int *__restrict__ perm,
-                 int64_t N, int H, int hd, uint4 *__restrict__ do_rows, float *__restrict__ delta) {
+                 int64_t N, int H, int hd, int rows_per_out, uint4 *__restrict__ do_rows, float *__restrict__ delta) {
     const int lane = threadIdx.x & 31;
     const int vpr = H * hd / 8, vph = hd / 8;            // 16-B vectors per row / per head
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < N; r += nwarps) {
         const int64_t t = perm[r];
         const uint4 *dr = dout + t * vpr;
-        const uint4 *orow = out + t * vpr;
+        const uint4 *orow = out + (t / rows_per_out) * vpr;
         for (int v0 = 0; v0 < vpr; v0 += 32) {
             const int v = v0 + lane;
             float acc = 0.0f;
@@ -73,7 +74,7 @@ row_delta_kernel(const uint4 *__restrict__ dout, const uint4 *__restrict__ out, 
 }
 
 cudaError_t launch_row_delta(const void *dout, const void *out, int64_t N, int H, int hd, const int *perm,
-                             void *do_rows, float *delta, cudaStream_t st) {
+                             void *do_rows, float *delta, cudaStream_t st, int rows_per_out) {
     if (N == 0) return cudaSuccess;
     if ((hd % 8) || (32 % (hd / 8)) || (reinterpret_cast<uintptr_t>(dout) & 15) ||
         (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(do_rows) & 15))
@@ -81,7 +82,7 @@ cudaError_t launch_row_delta(const void *dout, const void *out, int64_t N, int H
     const int64_t want = (N + 7) / 8;
     const int grid = static_cast<int>(std::min<int64_t>(want, 148 * 16));
     row_delta_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4 *>(dout), static_cast<const uint4 *>(out), perm,
-                                           N, H, hd, static_cast<uint4 *>(do_rows), delta);
+                                           N, H, hd, rows_per_out, static_cast<uint4 *>(do_rows), delta);
     count_launch();
     return cudaGetLastError();
 }

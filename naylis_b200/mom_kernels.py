@@ -148,6 +148,64 @@ class _MomReadFunction(torch.autograd.Function):
         return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
 
 
+class _MomReadSplitFunction(torch.autograd.Function):
+    """The same read for top-k routing with more block sets than the set
+    bucketing holds (``mom_plan_size`` is 0: top-4 of 32 blocks): every
+    (token, k) pair is a row of a top-1 plan, and each token's rows are
+    combined by their log-sum-exp (csrc/split.cu). Saves q, k, v, out, the
+    rows' lse and softmax shares, the plan and q in plan order."""
+
+    @staticmethod
+    def forward(ctx, q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
+        B, S, H, hd = q_sh.shape
+        L = k.shape[0]
+        N, top = B * S, top_idx.shape[-1]
+        M = N * top
+        dev = q_sh.device
+        st = _stream(dev)
+        lib = _lib.load()
+        idx = top_idx.reshape(N, top)
+        if idx.dtype not in (torch.int64, torch.int32):
+            idx = idx.to(torch.int64)
+        idx = idx.contiguous()
+        lg = log_gates.reshape(N, top).to(torch.float32).contiguous()
+        plan = torch.empty(lib.mom_plan_split_size(N, num_blocks, top), dtype=torch.uint8, device=dev)
+        idt = _lib.I64 if idx.dtype == torch.int64 else _lib.I32
+        _lib.call("mom_bucket_split", idx.data_ptr(), idt, lg.data_ptr(), N, num_blocks, top, plan.data_ptr(),
+                  plan.numel(), st)
+        out = torch.empty_like(q_sh)
+        lse_rows = torch.empty((H, M), dtype=torch.float32, device=dev)
+        weights = torch.empty((M, H), dtype=torch.float32, device=dev)
+        q_rows = torch.empty((M, H * hd), dtype=q_sh.dtype, device=dev)
+        ws = torch.empty(lib.mom_read_split_fwd_workspace_size(B, S, H, hd, top), dtype=torch.uint8, device=dev)
+        _lib.call("mom_read_split_fwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd,
+                  num_blocks, block_size, top, idx.data_ptr(), idt, plan.data_ptr(), out.data_ptr(),
+                  lse_rows.data_ptr(), weights.data_ptr(), q_rows.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        ctx.save_for_backward(q_sh, k, v, out, lse_rows, weights, idx, plan, q_rows)
+        ctx.meta = (num_blocks, block_size, top, L, idt)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q_sh, k, v, out, lse_rows, weights, idx, plan, q_rows = ctx.saved_tensors
+        num_blocks, block_size, top, L, idt = ctx.meta
+        B, S, H, hd = q_sh.shape
+        dev = q_sh.device
+        st = _stream(dev)
+        dout = dout.to(torch.bfloat16).contiguous()
+        dq = torch.empty_like(q_sh)
+        dk = torch.empty((L, H * hd), dtype=torch.float32, device=dev)
+        dv = torch.empty_like(dk)
+        dlg = torch.empty((B, S, top), dtype=torch.float32, device=dev)
+        ws = torch.empty(_lib.load().mom_read_split_bwd_workspace_size(B, S, H, hd, top), dtype=torch.uint8,
+                         device=dev)
+        _lib.call("mom_read_split_bwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                  dout.data_ptr(), lse_rows.data_ptr(), weights.data_ptr(), _lib.BF16, B, S, H, hd, num_blocks,
+                  block_size, top, idx.data_ptr(), idt, plan.data_ptr(), q_rows.data_ptr(), dq.data_ptr(),
+                  dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
+
+
 def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: str = MODE):
     """MoM memory read with the per-token gate bias (reference door:
     mom_kernels/__init__.py:87-102; contract of mom_kernels/triton_gpu.py:412-439).
@@ -176,8 +234,11 @@ def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: st
     if top_idx.shape != top_gates.shape or top_idx.shape[:2] != (B, S):
         raise RuntimeError("sm100 mom_read: top_idx / top_gates must be (B, S, top)")
     log_gates = top_gates.clamp_min(1e-9).log().float()
-    return _MomReadFunction.apply(q_sh.contiguous(), k.contiguous(), v.contiguous(), top_idx,
-                                  log_gates, int(num_blocks), int(block_size))
+    top = top_idx.shape[-1]
+    # routing sets beyond what the set bucketing holds: the block-split read
+    fn = _MomReadFunction if _lib.load().mom_plan_size(B * S, int(num_blocks), top) else _MomReadSplitFunction
+    return fn.apply(q_sh.contiguous(), k.contiguous(), v.contiguous(), top_idx, log_gates, int(num_blocks),
+                    int(block_size))
 
 
 # ====================================================================== router

@@ -78,6 +78,26 @@ def test_layer_config2_geometry_matches_oracle():
     assert all(e < TOL for e in errs.values()), errs
 
 
+def test_layer_top4_of_32_geometry_matches_oracle():
+    # d=2048, 16x128 heads, bank 32x128, rank 64, top-4: 35,960 block sets, so
+    # the read takes the block-split path; one 512-token sequence for the oracle
+    geo = dict(B=1, S=512, d=2048, H=16, nb=32, bs=128, top=4, r=64, seed=3, x_std=1.0,
+               m_std=0.02, w_std=0.02, mom_scale=1.0)
+    layer, inp = _layer(geo)
+    dout = gi.upstream_grad(geo)
+    got = _run(layer, inp, dout)
+    P = gi.oracle_params(inp, geo)
+    f = O.layer_forward(inp["x"].numpy(), P, geo["H"], geo["nb"], geo["bs"], geo["top"], "bf16")
+    mism = np.any(got["top_idx"].reshape(f["router"]["top_idx"].shape) != f["router"]["top_idx"], -1)
+    assert not mism.any(), f"{int(mism.sum())} routing mismatches"
+    b = O.layer_backward(f, inp["x"].numpy(), P, dout.numpy(), geo["H"], geo["nb"], geo["bs"])
+    pairs = [("out", f["out"]), ("dx", b["dx"]), ("dM_blocks", b["dM_blocks"]),
+             ("d_router_down", b["dw_down"]), ("d_router_up", b["dw_up"]), ("d_q_proj", b["dwq"]),
+             ("d_k_proj", b["dwk"]), ("d_v_proj", b["dwv"]), ("d_o_proj", b["dwo"])]
+    errs = {k: O.scaled_err(got[k], ref) for k, ref in pairs}
+    assert all(e < TOL for e in errs.values()), errs
+
+
 def test_layer_kernel_path_is_causal():
     geo = dict(B=2, S=512, d=256, H=4, nb=8, bs=64, top=2, r=32, seed=3, x_std=1.0,
                m_std=1.0, w_std=0.06, mom_scale=1.0)

@@ -38,12 +38,16 @@ def _mk(B, S, H, hd, nb, bs, top, seed, routing="random", dup=False):
     return bf(q), bf(k), bf(v), idx, gates, bf(dout)
 
 
-def _run_gpu(q, k, v, idx, gates, dout, nb, bs):
+def _run_gpu(q, k, v, idx, gates, dout, nb, bs, split=False):
     from naylis_b200 import mom_kernels as mk
     dev = torch.device("cuda")
-    qd, kd, vd = (t.to(dev).requires_grad_(True) for t in (q, k, v))
-    gd = gates.to(dev).requires_grad_(True)
-    out = mk.mom_read(qd, kd, vd, idx.to(dev), gd, num_blocks=nb, block_size=bs, mode="sm100")
+    qd, kd, vd = (t.detach().to(dev).requires_grad_(True) for t in (q, k, v))
+    gd = gates.detach().to(dev).requires_grad_(True)
+    if split:   # the block-split read on a geometry the set bucketing also takes
+        lg = gd.clamp_min(1e-9).log().float()
+        out = mk._MomReadSplitFunction.apply(qd, kd, vd, idx.to(dev), lg, nb, bs)
+    else:
+        out = mk.mom_read(qd, kd, vd, idx.to(dev), gd, num_blocks=nb, block_size=bs, mode="sm100")
     out.backward(dout.to(dev))
     torch.cuda.synchronize()
     return {"out": out.detach().float().cpu().numpy(), "dq": qd.grad.float().cpu().numpy(),
@@ -102,6 +106,111 @@ def test_read_matches_oracle(case):
     got = _run_gpu(q, k, v, idx, gates, dout, case["nb"], case["bs"])
     ref = _oracle(q, k, v, idx, gates, dout, case["nb"], case["bs"])
     _compare(got, ref)
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=1, S=300, H=2, hd=128, nb=32, bs=128, top=4, seed=21),          # top-4 of 32 blocks, head_dim 128
+    dict(B=2, S=200, H=2, hd=64, nb=32, bs=128, top=4, seed=22),           # tensor-core geometry, split rows
+    dict(B=2, S=150, H=3, hd=64, nb=24, bs=64, top=4, seed=23, dup=True),  # repeated block ids
+    dict(B=1, S=130, H=2, hd=64, nb=20, bs=48, top=5, seed=24),            # top-5, block not a multiple of 64
+])
+def test_read_split_matches_oracle(case):
+    """Routing with more block sets than the set bucketing holds takes the
+    block-split read ((token, k) rows combined by log-sum-exp)."""
+    from naylis_b200 import _lib
+    case = dict(case)
+    dup = case.pop("dup", False)
+    seed = case.pop("seed")
+    assert _lib.load().mom_plan_size(case["B"] * case["S"], case["nb"], case["top"]) == 0
+    q, k, v, idx, gates, dout = _mk(**case, seed=seed, dup=dup)
+    if dup:   # a block three times in one token's top list
+        idx[:, 1::4, 2] = idx[:, 1::4, 0]
+        idx[:, 1::4, 3] = idx[:, 1::4, 0]
+    got = _run_gpu(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    ref = _oracle(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    _compare(got, ref)
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=2, S=300, H=4, hd=64, nb=8, bs=128, top=2, seed=31),
+    dict(B=1, S=200, H=2, hd=128, nb=8, bs=64, top=3, seed=32, dup=True),
+])
+def test_read_split_matches_oracle_where_sets_fit(case):
+    case = dict(case)
+    dup = case.pop("dup", False)
+    seed = case.pop("seed")
+    q, k, v, idx, gates, dout = _mk(**case, seed=seed, dup=dup)
+    got = _run_gpu(q, k, v, idx, gates, dout, case["nb"], case["bs"], split=True)
+    ref = _oracle(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    _compare(got, ref)
+
+
+def _dense_read_fp32(q, k, v, idx, gates, dout, nb, bs):
+    """Plain PyTorch fp32 read and gradients on the GPU, one head at a time
+    (the same decomposition as the oracle's read_backward)."""
+    B, S, H, hd = q.shape
+    N, L, top = B * S, k.shape[0], idx.shape[-1]
+    scale = hd ** -0.5
+    qf = q.reshape(N, H, hd).float()
+    kf = k.reshape(L, H, hd).float()
+    vf = v.reshape(L, H, hd).float()
+    do = dout.reshape(N, H, hd).float()
+    lg = gates.reshape(N, top).clamp_min(1e-9).log().float()
+    ix = idx.reshape(N, top).long()
+    bias = torch.zeros(N, nb, device=q.device).scatter_add_(1, ix, lg)
+    sel = torch.zeros(N, nb, dtype=torch.bool, device=q.device).scatter_(1, ix, True)
+    bias = bias.masked_fill(~sel, float("-inf")).repeat_interleave(bs, 1)
+    out = torch.empty(N, H, hd, device=q.device)
+    dq = torch.empty_like(out)
+    dk = torch.empty(L, H, hd, device=q.device)
+    dv = torch.empty_like(dk)
+    dbias = torch.zeros(N, nb, device=q.device)
+    for h in range(H):
+        p = torch.softmax(qf[:, h] @ kf[:, h].T * scale + bias, -1)
+        o = p @ vf[:, h]
+        out[:, h] = o
+        ds = p * (do[:, h] @ vf[:, h].T - (do[:, h] * o).sum(-1, keepdim=True))
+        dq[:, h] = ds @ kf[:, h] * scale
+        dk[:, h] = ds.T @ qf[:, h] * scale
+        dv[:, h] = p.T @ do[:, h]
+        dbias += ds.reshape(N, nb, bs).sum(-1)
+    dlg = torch.gather(dbias, 1, ix)
+    return {"out": out.reshape(B, S, H, hd), "dq": dq.reshape(B, S, H, hd), "dk": dk.reshape(L, H * hd),
+            "dv": dv.reshape(L, H * hd), "dgates": (dlg / gates.reshape(N, top).clamp_min(1e-9)).reshape(B, S, top)}
+
+
+def test_read_split_full_size_top4_of_32():
+    """The top-4-of-32 geometry at full size (4 x 4096 tokens, 16 heads of 128,
+    32 blocks of 128 slots) against a plain PyTorch fp32 read on the GPU."""
+    B, S, H, hd, nb, bs, top = 4, 4096, 16, 128, 32, 128, 4
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(41)
+    q = (torch.randn(B, S, H, hd, generator=g, device=dev) * 0.7).bfloat16()
+    k = (torch.randn(nb * bs, H * hd, generator=g, device=dev) * 0.4).bfloat16()
+    v = (torch.randn(nb * bs, H * hd, generator=g, device=dev) * 0.4).bfloat16()
+    gates = torch.softmax(torch.randn(B, S, top, generator=g, device=dev), -1)
+    idx = torch.argsort(torch.rand(B, S, nb, generator=g, device=dev), -1)[..., :top]
+    dout = torch.randn(B, S, H, hd, generator=g, device=dev).bfloat16()
+    got = _run_gpu(q, k, v, idx, gates, dout, nb, bs)
+    with torch.no_grad():
+        ref = {key: t.cpu().numpy() for key, t in _dense_read_fp32(q, k, v, idx, gates, dout, nb, bs).items()}
+    _compare(got, ref)
+
+
+def test_bucket_split_flags_out_of_range_index():
+    from naylis_b200 import _lib
+    dev = torch.device("cuda")
+    N, nb, top = 100, 32, 4
+    idx = torch.argsort(torch.rand(N, nb, device=dev), -1)[:, :top].contiguous()
+    idx[17, 1] = -2   # out of range: must be reported, never read
+    lg = torch.zeros(N, top, device=dev)
+    plan = torch.empty(_lib.load().mom_plan_split_size(N, nb, top), dtype=torch.uint8, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.call("mom_bucket_split", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
+              plan.numel(), st)
+    with pytest.raises(_lib.MomError) as ei:
+        _lib.call("mom_plan_check", plan.data_ptr(), N * top, nb, 1, st)
+    assert ei.value.status == 7
 
 
 def test_read_is_deterministic_forward_and_dq():
