@@ -93,6 +93,35 @@ MOM_API int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int6
                   float *log_gates, void *act, void *workspace, size_t workspace_bytes,
                   void *stream);
 
+/* Sequence-sharded router forward (long-context prefill split by sequence over
+ * ranks; the reference has no such split). Each rank holds rows
+ * [t_base, t_base + S) of every sequence; the prefix mean at global row t
+ * divides by t + 1, so t_base + S < 2^24. The results equal mom_route_fwd over
+ * the whole sequence bit for bit, given the scan state entering the shard:
+ *
+ * scan_mode FP64, carry double[2][B][d]: [0] the sum of the earlier rows,
+ *   [1] 1.0 where the whole sequence's exactness certificate holds. Recipe:
+ *   mom_route_shard_stats on each shard (stats double[3][B][d]: sum, an upper
+ *   bound of sum |x|, smallest ulp exponent), all-gather them in rank order
+ *   (W x 3 x B x d), mom_route_shard_carry. Certified columns are exact in any
+ *   order, so all shards run at once. When *uncertified > 0 (tiny or huge
+ *   dynamic range) those columns need the sequential sum: run the shards in
+ *   rank order, each passing its carry_out (same layout) as the next carry_in.
+ * scan_mode FP32 (the sequential fp32 scan): carry float[B][d], always passed
+ *   shard to shard in rank order.
+ * carry_in may be NULL only for t_base = 0 in FP64 mode with a whole
+ * sequence; carry_out may be NULL. Other arguments as mom_route_fwd. */
+MOM_API int mom_route_shard_stats(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d,
+                                  double *stats, void *stream);
+MOM_API int mom_route_shard_carry(const double *stats_all, int64_t world, int64_t rank, int64_t B,
+                                  int64_t d, double *carry, int *uncertified, void *stream);
+MOM_API int mom_route_fwd_shard(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d,
+                                const void *w_down, const void *w_up, int compute_dtype, int64_t r,
+                                int64_t nb, int64_t top, const float *noise, int scan_mode,
+                                int64_t t_base, const void *carry_in, void *carry_out, float *probs,
+                                void *top_idx, int idx_dtype, float *gates, float *log_gates,
+                                void *act, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Router backward: autograd of the block above (model.py:186-220).
  * dlog_gates (B,S,top): gradient w.r.t. log_gates, or NULL; dgates: w.r.t. gates,
  * or NULL; dprobs (B,S,nb): w.r.t. probs (the aux load-balance loss), or NULL.

@@ -35,6 +35,10 @@ SIGNATURES = {
     "mom_route_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64, _int]),
     "mom_route_fwd": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _int, _i64, _i64, _i64, _fp,
                              _int, _fp, _vp, _int, _fp, _fp, _vp, _vp, _sz, _vp]),
+    "mom_route_shard_stats": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp]),
+    "mom_route_shard_carry": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp]),
+    "mom_route_fwd_shard": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _int, _i64, _i64, _i64, _fp,
+                                   _int, _i64, _vp, _vp, _fp, _vp, _int, _fp, _fp, _vp, _vp, _sz, _vp]),
     "mom_route_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "mom_route_bwd": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _vp, _int, _i64, _i64, _i64, _fp,
                              _vp, _int, _fp, _vp, _fp, _fp, _fp, _vp, _int, _int, _fp, _fp, _vp,

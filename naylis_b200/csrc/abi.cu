@@ -133,17 +133,20 @@ size_t mom_route_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int6
     return align256(static_cast<size_t>(B) * S * d * dt_size(compute_dtype));
 }
 
-int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
-                  const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
-                  const float *noise, int scan_mode, float *probs, void *top_idx, int idx_dtype,
-                  float *gates, float *log_gates, void *act, void *workspace,
-                  size_t workspace_bytes, void *stream) {
+namespace {
+int route_fwd_impl(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
+                   const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top, const float *noise,
+                   int scan_mode, float *probs, void *top_idx, int idx_dtype, float *gates, float *log_gates,
+                   void *act, void *workspace, size_t workspace_bytes, const mom::ScanShard &sh, void *stream) {
     int rc = check_router_geometry(B, S, d, r, nb, top);
     if (rc) return rc;
     MOM_REQUIRE(is_float_dtype(x_dtype), "x dtype must be F32 or BF16");
     MOM_REQUIRE(is_float_dtype(compute_dtype), "compute dtype must be F32 or BF16");
     MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
     MOM_REQUIRE(scan_mode == MOM_SCAN_FP64 || scan_mode == MOM_SCAN_FP32, "unknown scan mode %d", scan_mode);
+    MOM_REQUIRE(sh.t_base >= 0 && sh.t_base + S < (int64_t(1) << 24),
+                "shard offset %lld + length %lld: positions must stay below 2^24 (fp32 divisor)",
+                (long long)sh.t_base, (long long)S);
     const int64_t N = B * S;
     if (N == 0) return MOM_OK;
     MOM_REQUIRE(x && w_down && w_up && probs && top_idx && gates, "null pointer argument");
@@ -153,13 +156,74 @@ int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, c
     if ((rc = check_current_device())) return rc;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = mom::launch_route_scan(x, x_dtype, workspace, compute_dtype, (int)B, (int)S, (int)d,
-                                           scan_mode, st);
+                                           scan_mode, st, sh);
     if (e != cudaSuccess) return cuda_fail(e, "route_scan");
     e = mom::launch_route_head(workspace, w_down, w_up, compute_dtype, N, (int)d, (int)r, (int)nb,
                                (int)top, noise, probs, top_idx, idx_dtype == MOM_I64, gates,
                                log_gates, act, st);
     if (e != cudaSuccess) return cuda_fail(e, "route_head");
     return MOM_OK;
+}
+}  // namespace
+
+int mom_route_fwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
+                  const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
+                  const float *noise, int scan_mode, float *probs, void *top_idx, int idx_dtype,
+                  float *gates, float *log_gates, void *act, void *workspace,
+                  size_t workspace_bytes, void *stream) {
+    return route_fwd_impl(x, x_dtype, B, S, d, w_down, w_up, compute_dtype, r, nb, top, noise, scan_mode, probs,
+                          top_idx, idx_dtype, gates, log_gates, act, workspace, workspace_bytes, mom::ScanShard(),
+                          stream);
+}
+
+// ------------------------------------------------------------------ sequence shards
+int mom_route_shard_stats(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, double *stats,
+                          void *stream) {
+    MOM_REQUIRE(B >= 0 && S >= 0 && B * S < (int64_t(1) << 31), "bad B, S");
+    MOM_REQUIRE(d > 0 && d % 8 == 0, "d_model must be a positive multiple of 8 (got %lld)", (long long)d);
+    MOM_REQUIRE(is_float_dtype(x_dtype), "x dtype must be F32 or BF16");
+    MOM_REQUIRE(stats && (S == 0 || x), "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    if (B == 0) return MOM_OK;
+    // an empty shard (S = 0) reads nothing and reports sum 0, bound 0, no element
+    cudaError_t e = mom::launch_route_shard_stats(x, x_dtype, (int)B, (int)S, (int)d, stats,
+                                                  static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "route_shard_stats");
+}
+
+int mom_route_shard_carry(const double *stats_all, int64_t world, int64_t rank, int64_t B, int64_t d,
+                          double *carry, int *uncertified, void *stream) {
+    MOM_REQUIRE(world > 0 && world <= 65536 && rank >= 0 && rank < world, "bad (world, rank)");
+    MOM_REQUIRE(B >= 0 && d > 0 && B * d < (int64_t(1) << 31), "bad B, d");
+    MOM_REQUIRE(stats_all && carry && uncertified, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_route_shard_carry(stats_all, (int)world, (int)rank, (int)B, (int)d, carry,
+                                                  uncertified, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "route_shard_carry");
+}
+
+int mom_route_fwd_shard(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
+                        const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
+                        const float *noise, int scan_mode, int64_t t_base, const void *carry_in, void *carry_out,
+                        float *probs, void *top_idx, int idx_dtype, float *gates, float *log_gates, void *act,
+                        void *workspace, size_t workspace_bytes, void *stream) {
+    MOM_REQUIRE(carry_in || t_base == 0, "a shard that does not start at row 0 needs carry_in");
+    mom::ScanShard sh;
+    sh.t_base = t_base;
+    sh.carry_in = carry_in;
+    sh.carry_out = carry_out;
+    if (carry_out && B * S == 0 && B > 0 && d > 0) {   // nothing to walk: the state passes through
+        MOM_REQUIRE(carry_in, "carry_out of an empty first shard: pass a zero carry_in");
+        const size_t bytes = (scan_mode == MOM_SCAN_FP64 ? 2 * sizeof(double) : sizeof(float)) *
+                             static_cast<size_t>(B) * d;
+        cudaError_t e = cudaMemcpyAsync(carry_out, carry_in, bytes, cudaMemcpyDeviceToDevice,
+                                        static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return cuda_fail(e, "route_fwd_shard");
+    }
+    return route_fwd_impl(x, x_dtype, B, S, d, w_down, w_up, compute_dtype, r, nb, top, noise, scan_mode, probs,
+                          top_idx, idx_dtype, gates, log_gates, act, workspace, workspace_bytes, sh, stream);
 }
 
 size_t mom_route_bwd_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, int64_t nb) {

@@ -20,6 +20,18 @@ constexpr int kMaxTop = 8;        // top_blocks the library takes
 // number system; key = (number of sets of smaller size) + rank.
 int64_t num_route_keys(int64_t nb, int64_t top);
 
+// A shard of the sequence for the router scan: rows [t_base, t_base + S) of
+// every batch row. carry_in (may be null: t_base = 0, nothing before) is the
+// running state entering the shard; carry_out (may be null) receives it after
+// the shard's last row. Layouts: exact fp64 mode double[2][B][d] ([0] the sum of
+// the rows before, [1] 1.0 where the whole sequence's exactness certificate
+// holds); fp32 mode float[B][d] (the sequential fp32 sum).
+struct ScanShard {
+    int64_t t_base = 0;
+    const void *carry_in = nullptr;
+    void *carry_out = nullptr;
+};
+
 struct PlanLayout {
     int64_t N = 0, nb = 0, top = 0, num_keys = 0, chunks = 0, max_tiles = 0;
     size_t off_err = 0, off_ntiles = 0, off_key = 0, off_hist = 0, off_keytot = 0,
@@ -54,7 +66,18 @@ struct PlanView {
 PlanView plan_view(void *plan, const PlanLayout &L);
 
 cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, int S, int d,
-                              int mode, cudaStream_t st);
+                              int mode, cudaStream_t st,
+                              const ScanShard &sh = ScanShard());
+// Per (b, column) state of a sequence shard for the exact fp64 scan:
+// stats double[3][B][d] = its sum, an upper bound of its sum of |x|, the ulp
+// exponent of its smallest non-zero element (1 << 20 when all are zero).
+cudaError_t launch_route_shard_stats(const void *x, int xdt, int B, int S, int d, double *stats, cudaStream_t st);
+// From all shards' stats (W x [3][B][d], rank order): carry double[2][B][d] for
+// shard `rank` and, in *uncertified, the number of (b, column) whose whole-
+// sequence certificate fails (those need the sequential carry of the previous
+// shard instead of the sum).
+cudaError_t launch_route_shard_carry(const double *stats_all, int W, int rank, int B, int d, double *carry,
+                                     int *uncertified, cudaStream_t st);
 cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_up, int cdt,
                               int64_t ntok, int d, int r, int nb, int top, const float *noise,
                               float *probs, void *top_idx, int idx64, float *gates,

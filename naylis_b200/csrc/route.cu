@@ -21,7 +21,7 @@ constexpr int kScanStages = 8;   // ring depth
 template <int XDT, int CDT, int MODE>
 __global__ void __launch_bounds__(kScanCols)
 route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
-                  typename Elem<CDT>::T *__restrict__ hq, int S, int d) {
+                  typename Elem<CDT>::T *__restrict__ hq, int S, int d, ScanShard sh) {
     using XT = typename Elem<XDT>::T;
     constexpr int kRowBytes = kScanCols * sizeof(XT);
     constexpr int kChunksPerRow = kRowBytes / 16;
@@ -59,8 +59,10 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
 #pragma unroll 1
     for (int s = 0; s < kScanStages - 1; ++s) issue(s);
 
+    // a shard of the sequence starts from the running sum of the rows before it
     double acc64 = 0.0;
-    float acc32 = 0.0f;
+    float acc32 = (sh.carry_in && col < d) ? static_cast<const float *>(sh.carry_in)[static_cast<int64_t>(b) * d + col]
+                                           : 0.0f;
     typename Elem<CDT>::T *out = hq + static_cast<int64_t>(b) * S * d + col;
 #pragma unroll 1
     for (int s = 0; s < nstage; ++s) {
@@ -82,12 +84,14 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
                     acc32 = __fadd_rn(acc32, v);
                     cs = acc32;
                 }
-                const float h = __fdiv_rn(cs, static_cast<float>(t0 + r + 1));
+                const float h = __fdiv_rn(cs, static_cast<float>(sh.t_base + t0 + r + 1));
                 Elem<CDT>::store(out, static_cast<int64_t>(t0 + r) * d, h);
             }
         }
     }
     cp_async_wait<0>();
+    if (MODE == MOM_SCAN_FP32 && sh.carry_out && col < d)
+        static_cast<float *>(sh.carry_out)[static_cast<int64_t>(b) * d + col] = acc32;
 }
 
 // ------------------------------------------------------------ parallel exact fp64 scan
@@ -160,7 +164,7 @@ __device__ __forceinline__ float div_by_count(float c, float den, float y) {
 template <int XDT, int CDT>
 __global__ void __launch_bounds__(1024)
 route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem<CDT>::T *__restrict__ hq,
-                      int S, int d) {
+                      int S, int d, ScanShard sh) {
     __shared__ double s_sum[64][33];
     __shared__ float s_abs[64][33];
     __shared__ int s_emin[64][33];
@@ -211,9 +215,15 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
     s_emin[2 * c2][k] = em_of(mn0);
     s_emin[2 * c2 + 1][k] = em_of(mn1);
     __syncthreads();
+    // a shard of the sequence: carry [0][b][col] = the sum of the rows before it,
+    // [1][b][col] = the whole sequence's certificate (so every shard decides alike)
+    const double *cin = static_cast<const double *>(sh.carry_in);
+    const int64_t bd = static_cast<int64_t>(gridDim.y) * d;
     if (threadIdx.x < 64) {                                      // one thread per column
         const int cc = threadIdx.x;
-        double run = 0.0, at = 0.0;
+        const int ccol = blockIdx.x * 64 + cc;
+        const int64_t ci = static_cast<int64_t>(b) * d + ccol;
+        double run = (cin && ccol < d) ? cin[ci] : 0.0, at = 0.0;
         int em = 1 << 20;
         for (int kk = 0; kk < 32; ++kk) {
             const double v = s_sum[cc][kk];
@@ -223,7 +233,8 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
             em = min(em, s_emin[cc][kk]);
         }
         // all zero -> trivially exact; else A < 2^(52 + e_min)
-        s_cert[cc] = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
+        s_cert[cc] = cin ? (ccol < d && cin[bd + ci] != 0.0)
+                         : ((em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em)));
     }
     __syncthreads();
     const bool fast = live && s_cert[2 * c2] && s_cert[2 * c2 + 1];
@@ -232,7 +243,7 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
         auto emit = [&](int t, float2 v, float y) {
             r0 = __dadd_rn(r0, static_cast<double>(v.x));
             r1 = __dadd_rn(r1, static_cast<double>(v.y));
-            const float den = static_cast<float>(t + 1);
+            const float den = static_cast<float>(sh.t_base + t + 1);
             if (fast)
                 PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, div_by_count(__double2float_rn(r0), den, y),
                                       div_by_count(__double2float_rn(r1), den, y));
@@ -243,24 +254,116 @@ route_scan_par_kernel(const typename Elem<XDT>::T *__restrict__ x, typename Elem
 #pragma unroll
             for (int u = 0; u < kScanBatch; ++u) v[u] = Pair<XDT>::load(xc + static_cast<int64_t>(t + u) * d);
             // lane u < kScanBatch holds 1/(t + 1 + u) for the whole warp
-            const float yl = __frcp_rn(static_cast<float>(t + 1 + (c2 & (kScanBatch - 1))));
+            const float yl = __frcp_rn(static_cast<float>(sh.t_base + t + 1 + (c2 & (kScanBatch - 1))));
 #pragma unroll
             for (int u = 0; u < kScanBatch; ++u) emit(t + u, v[u], __shfl_sync(0xffffffffu, yl, u));
         }
         for (; t < t1; ++t)
-            emit(t, Pair<XDT>::load(xc + static_cast<int64_t>(t) * d), __frcp_rn(static_cast<float>(t + 1)));
+            emit(t, Pair<XDT>::load(xc + static_cast<int64_t>(t) * d),
+                 __frcp_rn(static_cast<float>(sh.t_base + t + 1)));
+        // the last chunk ends at row S - 1: its running sums are the shard's exact end state
+        if (fast && k == 31 && sh.carry_out) {
+            double *co = static_cast<double *>(sh.carry_out) + static_cast<int64_t>(b) * d + col;
+            co[0] = r0;
+            co[1] = r1;
+            co[bd] = 1.0;
+            co[bd + 1] = 1.0;
+        }
     }
     if (live && !fast && k == 0) {
         // a certificate failed: both columns of the pair walk sequentially
-        double a0 = 0.0, a1 = 0.0;
+        const int64_t ci = static_cast<int64_t>(b) * d + col;
+        double a0 = cin ? cin[ci] : 0.0, a1 = cin ? cin[ci + 1] : 0.0;
         for (int t = 0; t < S; ++t) {
             const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
             a0 = __dadd_rn(a0, static_cast<double>(v.x));
             a1 = __dadd_rn(a1, static_cast<double>(v.y));
-            const float den = static_cast<float>(t + 1);
+            const float den = static_cast<float>(sh.t_base + t + 1);
             PairStore<CDT>::store(hc + static_cast<int64_t>(t) * d, __fdiv_rn(__double2float_rn(a0), den),
                                   __fdiv_rn(__double2float_rn(a1), den));
         }
+        if (sh.carry_out) {
+            double *co = static_cast<double *>(sh.carry_out) + ci;
+            co[0] = a0;
+            co[1] = a1;
+            co[bd] = s_cert[2 * c2] ? 1.0 : 0.0;
+            co[bd + 1] = s_cert[2 * c2 + 1] ? 1.0 : 0.0;
+        }
+    }
+}
+
+// Per-shard totals for a sequence split across ranks: the par kernel's phase 1
+// over the shard's rows, reduced per column (the sum is exact whenever the whole
+// sequence's certificate holds, since the shard's elements are a subset).
+template <int XDT>
+__global__ void __launch_bounds__(1024)
+route_scan_stats_kernel(const typename Elem<XDT>::T *__restrict__ x, int S, int d, double *__restrict__ stats) {
+    __shared__ double s_sum[64][33];
+    __shared__ float s_abs[64][33];
+    __shared__ int s_emin[64][33];
+    const int c2 = threadIdx.x & 31, k = threadIdx.x >> 5;
+    const int b = blockIdx.y;
+    const int col = blockIdx.x * 64 + 2 * c2;
+    const int len = (S + 31) / 32;
+    const int t0 = k * len, t1 = min(S, t0 + len);
+    const bool live = col < d;
+    const typename Elem<XDT>::T *xc = x + static_cast<int64_t>(b) * S * d + (live ? col : 0);
+    double sum0 = 0.0, sum1 = 0.0;
+    float as0 = 0.0f, as1 = 0.0f;
+    uint32_t mn0 = 0xFFFFFFFFu, mn1 = 0xFFFFFFFFu;
+    for (int t = t0; t < t1; ++t) {
+        const float2 v = Pair<XDT>::load(xc + static_cast<int64_t>(t) * d);
+        sum0 = __dadd_rn(sum0, static_cast<double>(v.x));
+        sum1 = __dadd_rn(sum1, static_cast<double>(v.y));
+        as0 = __fadd_ru(as0, fabsf(v.x));
+        as1 = __fadd_ru(as1, fabsf(v.y));
+        mn0 = min(mn0, (__float_as_uint(v.x) & 0x7FFFFFFFu) - 1u);
+        mn1 = min(mn1, (__float_as_uint(v.y) & 0x7FFFFFFFu) - 1u);
+    }
+    auto em_of = [](uint32_t mn) -> int {
+        return mn == 0xFFFFFFFFu ? (1 << 20) : ulp_exponent<XDT>(__uint_as_float(mn + 1u));
+    };
+    s_sum[2 * c2][k] = sum0;
+    s_sum[2 * c2 + 1][k] = sum1;
+    s_abs[2 * c2][k] = as0;
+    s_abs[2 * c2 + 1][k] = as1;
+    s_emin[2 * c2][k] = em_of(mn0);
+    s_emin[2 * c2 + 1][k] = em_of(mn1);
+    __syncthreads();
+    const int cc = threadIdx.x;
+    const int ccol = blockIdx.x * 64 + cc;
+    if (cc < 64 && ccol < d) {
+        double run = 0.0, at = 0.0;
+        int em = 1 << 20;
+        for (int kk = 0; kk < 32; ++kk) {
+            run = __dadd_rn(run, s_sum[cc][kk]);
+            at = __dadd_ru(at, static_cast<double>(s_abs[cc][kk]));
+            em = min(em, s_emin[cc][kk]);
+        }
+        const int64_t bd = static_cast<int64_t>(gridDim.y) * d, i = static_cast<int64_t>(b) * d + ccol;
+        stats[i] = run;
+        stats[bd + i] = at;
+        stats[2 * bd + i] = static_cast<double>(em);
+    }
+}
+
+__global__ void __launch_bounds__(256)
+route_shard_carry_kernel(const double *__restrict__ all, int W, int rank, int64_t bd, double *__restrict__ carry,
+                         int *__restrict__ uncertified) {
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < bd;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        double run = 0.0, at = 0.0;
+        int em = 1 << 20;
+        for (int j = 0; j < W; ++j) {
+            const double *st = all + static_cast<int64_t>(j) * 3 * bd;
+            if (j < rank) run = __dadd_rn(run, st[i]);
+            at = __dadd_ru(at, st[bd + i]);                 // stays an upper bound of A
+            em = min(em, static_cast<int>(st[2 * bd + i]));
+        }
+        const bool cert = (em == (1 << 20)) || (em > -1000 && at < ldexp(1.0, 52 + em));
+        carry[i] = run;
+        carry[bd + i] = cert ? 1.0 : 0.0;
+        if (!cert) atomicAdd(uncertified, 1);
     }
 }
 
@@ -496,7 +599,8 @@ route_head_simt_kernel(const typename Elem<CDT>::T *__restrict__ hq,
 
 // ============================================================ host launchers
 template <int XDT, int CDT, int MODE>
-static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
+static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st,
+                                 const ScanShard &sh) {
     using XT = typename Elem<XDT>::T;
     const size_t smem = kScanStages * kScanRows * kScanCols * sizeof(XT);
     auto k = route_scan_kernel<XDT, CDT, MODE>;
@@ -504,36 +608,60 @@ static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, c
     if (e != cudaSuccess) return e;
     dim3 grid((d + kScanCols - 1) / kScanCols, B);
     k<<<grid, kScanCols, smem, st>>>(static_cast<const XT *>(x),
-                                     static_cast<typename Elem<CDT>::T *>(hq), S, d); count_launch();
+                                     static_cast<typename Elem<CDT>::T *>(hq), S, d, sh); count_launch();
     return cudaGetLastError();
 }
 
 template <int XDT, int CDT>
-static cudaError_t launch_scan_par_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st) {
+static cudaError_t launch_scan_par_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st,
+                                     const ScanShard &sh) {
     dim3 grid((d + 63) / 64, B);
     route_scan_par_kernel<XDT, CDT><<<grid, 1024, 0, st>>>(static_cast<const typename Elem<XDT>::T *>(x),
-                                                          static_cast<typename Elem<CDT>::T *>(hq), S, d);
+                                                          static_cast<typename Elem<CDT>::T *>(hq), S, d, sh);
     count_launch();
     return cudaGetLastError();
 }
 
 cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, int S, int d,
-                              int mode, cudaStream_t st) {
+                              int mode, cudaStream_t st, const ScanShard &sh) {
     if (mode == MOM_SCAN_FP64) {
-        if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_par_t<MOM_BF16, MOM_BF16>(x, hq, B, S, d, st);
-        if (xdt == MOM_BF16 && cdt == MOM_F32) return launch_scan_par_t<MOM_BF16, MOM_F32>(x, hq, B, S, d, st);
-        if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_par_t<MOM_F32, MOM_BF16>(x, hq, B, S, d, st);
-        if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_par_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st);
+        if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_par_t<MOM_BF16, MOM_BF16>(x, hq, B, S, d, st, sh);
+        if (xdt == MOM_BF16 && cdt == MOM_F32) return launch_scan_par_t<MOM_BF16, MOM_F32>(x, hq, B, S, d, st, sh);
+        if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_par_t<MOM_F32, MOM_BF16>(x, hq, B, S, d, st, sh);
+        if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_par_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st, sh);
         return cudaErrorInvalidValue;
     }
 #define MOM_SCAN_CASE(X, C, M)                                                       \
-    if (xdt == X && cdt == C && mode == M) return launch_scan_t<X, C, M>(x, hq, B, S, d, st);
+    if (xdt == X && cdt == C && mode == M) return launch_scan_t<X, C, M>(x, hq, B, S, d, st, sh);
     MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP32)
     MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP32)
     MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP32)
     MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP32)
 #undef MOM_SCAN_CASE
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_route_shard_stats(const void *x, int xdt, int B, int S, int d, double *stats, cudaStream_t st) {
+    dim3 grid((d + 63) / 64, B);
+    if (xdt == MOM_BF16)
+        route_scan_stats_kernel<MOM_BF16><<<grid, 1024, 0, st>>>(static_cast<const uint16_t *>(x), S, d, stats);
+    else if (xdt == MOM_F32)
+        route_scan_stats_kernel<MOM_F32><<<grid, 1024, 0, st>>>(static_cast<const float *>(x), S, d, stats);
+    else
+        return cudaErrorInvalidValue;
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_shard_carry(const double *stats_all, int W, int rank, int B, int d, double *carry,
+                                     int *uncertified, cudaStream_t st) {
+    const int64_t bd = static_cast<int64_t>(B) * d;
+    cudaError_t e = cudaMemsetAsync(uncertified, 0, sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((bd + 255) / 256, 148 * 8)));
+    route_shard_carry_kernel<<<grid, 256, 0, st>>>(stats_all, W, rank, bd, carry, uncertified);
+    count_launch();
+    return cudaGetLastError();
 }
 
 cudaError_t launch_route_head(const void *hq, const void *w_down, const void *w_up, int cdt,

@@ -164,10 +164,10 @@ def test_router_matches_oracle(compute, x_dtype, B, S, d, r, nb, top):
 
 
 def test_router_prefix_certificate_fallback_inside_the_head():
-    """The bf16 router fuses the prefix mean into the head, with exact fp64 chunk
-    carries; columns whose dynamic range fails the certificate (a 1e-30 next to
-    O(1) values, a column scaled by 1e30) take the sequential walk for their
-    carries. Indices must still match the oracle bitwise."""
+    """The router's prefix mean runs exact fp64 chunk carries; columns whose
+    dynamic range fails the certificate (a 1e-30 next to O(1) values, a column
+    scaled by 1e30) take the sequential walk. Indices must still match the
+    oracle bitwise."""
     torch.manual_seed(41)
     x = torch.randn(2, 300, 256)
     x[0, 17, 5] = 1e-30
@@ -180,6 +180,67 @@ def test_router_prefix_certificate_fallback_inside_the_head():
     _assert_indices(got["top_idx"], rt, 2, "router with fallback columns")
     assert O.scaled_err(got["probs"], rt["probs"]) < 2e-2
     assert O.scaled_err(got["gates"], rt["gates"]) < 2e-2
+
+
+def _route_shards_in_one_process(x, w_down, w_up, top, compute_dtype, sizes, scan_mode, noise=None):
+    """The sequence-sharded router's exchange, its ranks emulated in rank order
+    in one process (the all-gather is a stack; the chain passes carry_out on)."""
+    from naylis_b200.sequence_parallel import CudaShardOps
+    xd = x.cuda()
+    starts = np.concatenate([[0], np.cumsum(sizes)[:-1]]).tolist()
+    shards = [xd[:, s0:s0 + n].contiguous() for s0, n in zip(starts, sizes)]
+    noises = [None if noise is None else noise.cuda()[:, s0:s0 + n] for s0, n in zip(starts, sizes)]
+    ops = [CudaShardOps(w_down.cuda(), w_up.cuda(), top, nz, compute_dtype) for nz in noises]
+    W = len(sizes)
+    outs, chained = [], False
+    if scan_mode == "fp64":
+        stats_all = torch.stack([o.stats(xs) for o, xs in zip(ops, shards)])
+        carries = [o.carry(stats_all, W, j) for j, o in enumerate(ops)]
+        assert len({u for _, u in carries}) == 1        # every rank takes the same branch
+        chained = carries[0][1] > 0
+        carry = carries[0][0]
+        for j in range(W):
+            c_in = carry if chained else carries[j][0]
+            p, i, g, c_out = ops[j].route(shards[j], starts[j], c_in, chained, scan_mode)
+            outs.append((p, i, g))
+            carry = c_out
+    else:
+        chained = True
+        carry = ops[0].zero_carry(shards[0], scan_mode)
+        for j in range(W):
+            p, i, g, carry = ops[j].route(shards[j], starts[j], carry, True, scan_mode)
+            outs.append((p, i, g))
+    torch.cuda.synchronize()
+    cat = lambda k: torch.cat([o[k] for o in outs], 1).cpu().numpy()
+    return {"probs": cat(0), "top_idx": cat(1), "gates": cat(2)}, chained
+
+
+@pytest.mark.parametrize("scan_mode,extreme,x_dtype,compute", [
+    ("fp64", False, torch.bfloat16, torch.bfloat16),
+    ("fp64", False, torch.float32, torch.float32),
+    ("fp64", True, torch.bfloat16, torch.bfloat16),
+    ("fp32", False, torch.bfloat16, torch.bfloat16),
+    ("fp32", False, torch.float32, torch.float32),
+])
+def test_router_sequence_shards_equal_the_whole_sequence_bitwise(scan_mode, extreme, x_dtype, compute):
+    """Rows split over 5 shards of unequal length (one empty): every output of
+    the shards, concatenated, equals the single-call router bit for bit. With
+    columns that fail the exactness certificate the shards run as a chain."""
+    torch.manual_seed(7)
+    B, d, sizes = 2, 256, [300, 1, 0, 257, 466]
+    x = torch.randn(B, sum(sizes), d)
+    if extreme:
+        x[0, 17, 5] = 1e-30
+        x[1, :, 77] *= 1e30
+    x = x.to(x_dtype)
+    w_down = torch.randn(32, d) * 0.02
+    w_up = torch.randn(8, 32) * 0.2
+    noise = torch.randn(B, sum(sizes), 8)
+    whole = _route_gpu(x, w_down, w_up, 2, compute, noise=noise, scan_mode=scan_mode)
+    got, chained = _route_shards_in_one_process(x, w_down, w_up, 2, compute, sizes, scan_mode, noise)
+    assert chained == (extreme or scan_mode == "fp32")
+    for k in ("probs", "top_idx", "gates"):
+        assert np.array_equal(got[k], whole[k]), k
 
 
 def test_router_noise_goes_into_topk_only():
