@@ -107,7 +107,7 @@ cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, 
                             int hd, int nb, int bs, int top, const PlanLayout &L,
                             const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st);
 bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H);
-cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int H, int nb, int top,
+cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int hd, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
                                cudaStream_t st);
 bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,

@@ -803,7 +803,9 @@ int device_sm_count();
 
 bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,
                            const void *dout, int H) {
-    return read_fwd_tc_supported(hd, bs, top, q, k, v, H) && (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
+    // the backward kernels are written for head_dim 64 only
+    return hd == kHD && read_fwd_tc_supported(hd, bs, top, q, k, v, H) &&
+           (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
 }
 
 template <bool kDoRows>

@@ -241,7 +241,7 @@ cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, 
     // the tensor-core kernel covers head_dim 64, 128-slot blocks, top <= 2;
     // other geometries take the warp-level mma kernel below
     if (read_fwd_tc_supported(hd, bs, top, q_rows, k, v, H))
-        return launch_read_fwd_tc(q_rows, k, v, H, nb, top, L, P, out, lse, st);
+        return launch_read_fwd_tc(q_rows, k, v, hd, H, nb, top, L, P, out, lse, st);
     if (hd == 64) return launch_fwd_t<64>(q, k, v, H, bs, top, L, P, out, lse, st);
     if (hd == 128) return launch_fwd_t<128>(q, k, v, H, bs, top, L, P, out, lse, st);
     return cudaErrorInvalidValue;

@@ -33,21 +33,35 @@
 namespace mom {
 
 namespace {
-constexpr int kHD = 64;
 constexpr int kBS = 128;
 constexpr int kTM = 128;                       // token rows per tile (TMEM lanes)
 constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
 constexpr int kSoftThreads = kSoftWarps * 32;
 constexpr int kThreads = 96 + kSoftThreads;     // loader + 2 MMA issuers + softmax
-constexpr uint32_t kQBytes = kTM * kHD * 2;    // 16 KiB
-constexpr uint32_t kBlkBytes = kBS * kHD * 2;  // 16 KiB per 128-slot block of K or V
-constexpr uint32_t kStageBytes = kQBytes + 4 * kBlkBytes;   // Q + K(2 blocks) + V(2 blocks)
-constexpr uint32_t kOutBytes = kTM * kHD * 2;      // the output tile of one item, staged for coalesced stores
-constexpr uint32_t kScratchBytes = 8 * kTM * 4 + kOutBytes + kTM * 4;   // row max / sums [4][128], O tile, tokens
-constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
+constexpr uint32_t kBoxBytes = 128 * 128;      // one TMA box: 128 rows x 64 bf16 columns (128-B swizzle)
+constexpr uint32_t kOutBytes = kTM * 64 * 2;   // 64 output columns of the tile, staged for coalesced stores
+constexpr uint32_t kScratchBytes = 8 * kTM * 4 + kOutBytes + kTM * 4;   // row max / sums [4][128], O cols, tokens
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPCol = 256;                // P: group g's 64 slots at 256 + 32g (bf16 pairs)
-constexpr uint32_t kOCol = 384;                // O_0 at 384, O_1 at 448
+constexpr uint32_t kOCol = 384;                // head_dim 64: O_0 at 384, O_1 at 448; head_dim 128: O at 384
+
+// head_dim 64: sets of up to two blocks (S 256 columns, two O halves).
+// head_dim 128: one block per row (the block-split plan): S 128, O 128 columns.
+// Rows of Q / K / V are 64-column TMA boxes side by side (kBoxBytes apart).
+template <int HD>
+struct Fwd {
+    static constexpr int kHD = HD;
+    static constexpr int kMaxBlk = HD == 64 ? 2 : 1;
+    static constexpr int kBoxes = HD / 64;
+    static constexpr uint32_t kQBytes = kTM * HD * 2;
+    static constexpr uint32_t kBlkBytes = kBS * HD * 2;     // one 128-slot block of K or V
+    static constexpr uint32_t kStageBytes = kQBytes + 2 * kMaxBlk * kBlkBytes;   // Q + K blocks + V blocks
+    static constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
+    // V as the MN-major B operand of PV: N-atoms of 64 columns kBoxBytes apart
+    // (head_dim 64 has one atom; its value is what the validated kernel used)
+    static constexpr uint32_t kVLbo = HD == 64 ? 2 * kBlkBytes : kBoxBytes;
+    static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
 
 struct Bars {
     uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full, o_free, drain, s_issued;
@@ -58,10 +72,14 @@ struct Bars {
 static_assert(sizeof(Bars) <= 1024, "barrier block");
 }  // namespace
 
+template <int HD>
 __global__ void __launch_bounds__(kThreads, 1)
 read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                    const __grid_constant__ CUtensorMap tmap_q, int H, int top, float scale_log2, PlanView P,
                    uint16_t *__restrict__ out, float *__restrict__ lse) {
+    using C = Fwd<HD>;
+    constexpr int kHD = C::kHD;
+    constexpr uint32_t kQBytes = C::kQBytes, kBlkBytes = C::kBlkBytes, kStageBytes = C::kStageBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -130,7 +148,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const int nload = nblk > 0 ? nblk : 1;
             const uint32_t sQ = base + s * kStageBytes;
             const uint32_t sK = sQ + kQBytes;
-            const uint32_t sV = sK + 2 * kBlkBytes;
+            const uint32_t sV = sK + C::kMaxBlk * kBlkBytes;
             // the stage's K/V are still those of this set and head (item i-2): keep them
             const int kv = tc::get(lt.key, src) * H + h;
             const bool reload = kv != stage_kv[s];
@@ -139,11 +157,18 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 bars->meta[s] = nload | (nblk << 8);   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + (reload ? 2 * nload * kBlkBytes : 0));
                 // the tile's rows x0 .. x0+127 (rows past the tile are never stored)
-                tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
+#pragma unroll
+                for (int c = 0; c < C::kBoxes; ++c)
+                    tc::tma_load_2d(sQ + c * kBoxBytes, &tmap_q, h * kHD + 64 * c, x0, &bars->full[s]);
                 for (int jb = 0; reload && jb < nload; ++jb) {
                     const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
-                    tc::tma_load_2d(sK + jb * kBlkBytes, &tmap_k, h * kHD, blk * kBS, &bars->full[s]);
-                    tc::tma_load_2d(sV + jb * kBlkBytes, &tmap_v, h * kHD, blk * kBS, &bars->full[s]);
+#pragma unroll
+                    for (int c = 0; c < C::kBoxes; ++c) {
+                        tc::tma_load_2d(sK + jb * kBlkBytes + c * kBoxBytes, &tmap_k, h * kHD + 64 * c, blk * kBS,
+                                        &bars->full[s]);
+                        tc::tma_load_2d(sV + jb * kBlkBytes + c * kBoxBytes, &tmap_v, h * kHD + 64 * c, blk * kBS,
+                                        &bars->full[s]);
+                    }
                 }
             }
             __syncwarp();
@@ -173,8 +198,12 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
                 const uint64_t ad = tc::smem_desc_sw128(sQ, 16, 1024), bd = tc::smem_desc_sw128(sK, 16, 1024);
 #pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
-                    tc::mma_bf16_ss(tmem, ad + 2 * kk, bd + 2 * kk, idesc_s, kk > 0);
+                for (int kk = 0; kk < kHD / 16; ++kk) {
+                    // +32 B per K step within a 64-column box (+2 in the address field),
+                    // +kBoxBytes (+1024) to the next box
+                    const uint64_t step = 1024u * (kk >> 2) + 2u * (kk & 3);
+                    tc::mma_bf16_ss(tmem, ad + step, bd + step, idesc_s, kk > 0);
+                }
                 tc::mma_commit(&bars->s_full);
             }
             __syncwarp();
@@ -186,7 +215,7 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             // warp 2 has not waited for the stage yet; warp 1 did so before issuing S(i)
             if (!wa && !tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
             const int nblk = tc::ld_shared_volatile(&bars->meta[s]) >> 8;
-            const uint32_t sV = base + s * kStageBytes + kQBytes + 2 * kBlkBytes;
+            const uint32_t sV = base + s * kStageBytes + kQBytes + C::kMaxBlk * kBlkBytes;
             // P(i) written to TMEM (and S(i) read) by the softmax
             if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
             if (wa) {
@@ -201,8 +230,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
-                if (nblk > (wa ? 0 : 1)) {
-                    const uint64_t bv = tc::smem_desc_sw128(sV + (wa ? 0 : kBlkBytes), kBlkBytes * 2, 1024);
+                if (nblk > (wa ? 0 : 1) && (wa || C::kMaxBlk > 1)) {
+                    const uint64_t bv = tc::smem_desc_sw128(sV + (wa ? 0 : kBlkBytes), C::kVLbo, 1024);
 #pragma unroll
                     for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
                         const int kk = (wa ? 0 : 8) + k8;
@@ -243,29 +272,53 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             const float l = prev_l;
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
             tc::tc_fence_after();
+            // head_dim 64: O_0 and O_1 (the set's two blocks) at +0 / +64, summed;
+            // head_dim 128: columns 16g.. and 64+16g.. of the one O
             uint32_t a0[16], a1[16];
-            tc::tmem_ld16(trow + kOCol + grp * 16, a0);          // both halves in one round trip
-            tc::tmem_ld16(trow + kOCol + kHD + grp * 16, a1);
+            tc::tmem_ld16(trow + kOCol + grp * 16, a0);          // both in one round trip
+            tc::tmem_ld16(trow + kOCol + 64 + grp * 16, a1);
             tc::tmem_ld_wait_regs(a0);
             tc::tmem_ld_wait_regs(a1);
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->o_free);
+            auto pack16 = [&](const float (&o)[16], uint4 &v0, uint4 &v1) {
+                v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+                v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+                v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
+                v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
+                v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
+                v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
+                v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
+                v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
+            };
+            auto put_lse = [&]() {
+                if (grp == 0 && prev_tok >= 0)
+                    lse[static_cast<int64_t>(prev_h) * P.n + prev_row] =
+                        l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
+            };
             float o[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e)   // O_1 holds block 1 of a two-block set
-                o[e] = (prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (prev_nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
             uint4 v0, v1;
-            v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
-            v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
-            v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
-            v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-            v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
-            v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
-            v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
-            v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
-            if (grp == 0 && prev_tok >= 0)
-                lse[static_cast<int64_t>(prev_h) * P.n + prev_row] = l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
-            tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
+            if constexpr (HD == 64) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)   // O_1 holds block 1 of a two-block set
+                    o[e] = (prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) +
+                           (prev_nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
+                pack16(o, v0, v1);
+                put_lse();
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f;
+                pack16(o, v0, v1);
+                put_lse();
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
+                tc::named_bar(bar_id, 128);   // the staging rows are read out before they are rewritten
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = prev_nblk > 0 ? __uint_as_float(a1[e]) : 0.0f;
+                pack16(o, v0, v1);
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok,
+                                    out + prev_h * kHD + 64, ld);
+            }
         };
         // per-item row metadata: tile fields for 32 items at a time (one per lane),
         // this thread's row (token, gate bias) one item ahead, so that no global
@@ -422,10 +475,12 @@ bool make_bf16_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t co
     return r == CUDA_SUCCESS;
 }
 
+// head_dim 64 with sets of up to two blocks; head_dim 128 with one block per row
+// (the block-split plan)
 bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H) {
-    return hd == kHD && bs == kBS && top >= 1 && top <= 2 && (reinterpret_cast<uintptr_t>(k) % 16) == 0 &&
-           (reinterpret_cast<uintptr_t>(v) % 16) == 0 && (reinterpret_cast<uintptr_t>(q) % 16) == 0 &&
-           (H * kHD * 2) % 16 == 0 && encode_fn() != nullptr;
+    return ((hd == 64 && top >= 1 && top <= 2) || (hd == 128 && top == 1)) && bs == kBS &&
+           (reinterpret_cast<uintptr_t>(k) % 16) == 0 && (reinterpret_cast<uintptr_t>(v) % 16) == 0 &&
+           (reinterpret_cast<uintptr_t>(q) % 16) == 0 && (H * hd * 2) % 16 == 0 && encode_fn() != nullptr;
 }
 
 int device_sm_count() {
@@ -439,24 +494,33 @@ int device_sm_count() {
     return n;
 }
 
-cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int H, int nb, int top,
-                               const PlanLayout &L, const PlanView &P, void *out, float *lse,
-                               cudaStream_t st) {
+template <int HD>
+static cudaError_t launch_fwd_tc_t(const void *q_rows, const void *k, const void *v, int H, int nb, int top,
+                                   const PlanLayout &L, const PlanView &P, void *out, float *lse, cudaStream_t st) {
     CUtensorMap mk, mv, mq;
-    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
+    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * HD;
     if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
         !make_bf16_map(&mq, q_rows, static_cast<uint64_t>(L.N), cols, kTM))
         return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemBytes);
+    constexpr uint32_t smem = Fwd<HD>::kSmemBytes;
+    cudaError_t e = cudaFuncSetAttribute(read_fwd_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
     const int grid = static_cast<int>(std::min<int64_t>(items, device_sm_count()));
-    const float scale_log2 = kLog2e / sqrtf(static_cast<float>(kHD));
-    read_fwd_tc_kernel<<<grid, kThreads, kSmemBytes, st>>>(mk, mv, mq, H, top,
-                                                          scale_log2, P, static_cast<uint16_t *>(out), lse);
+    const float scale_log2 = kLog2e / sqrtf(static_cast<float>(HD));
+    read_fwd_tc_kernel<HD><<<grid, kThreads, smem, st>>>(mk, mv, mq, H, top, scale_log2, P,
+                                                         static_cast<uint16_t *>(out), lse);
     count_launch();
     return cudaGetLastError();
+}
+
+cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int hd, int H, int nb, int top,
+                               const PlanLayout &L, const PlanView &P, void *out, float *lse,
+                               cudaStream_t st) {
+    if (hd == 64) return launch_fwd_tc_t<64>(q_rows, k, v, H, nb, top, L, P, out, lse, st);
+    if (hd == 128 && top == 1) return launch_fwd_tc_t<128>(q_rows, k, v, H, nb, top, L, P, out, lse, st);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace mom

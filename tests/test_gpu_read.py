@@ -96,6 +96,7 @@ def test_read_matches_reference_golden():
     dict(B=1, S=257, H=2, hd=64, nb=6, bs=48, top=2, seed=5),             # block not a multiple of 64
     dict(B=2, S=333, H=2, hd=64, nb=8, bs=128, top=2, seed=6, routing="skewed"),  # one dominant set
     dict(B=2, S=150, H=2, hd=64, nb=4, bs=64, top=2, seed=7, dup=True),   # repeated block ids
+    dict(B=1, S=300, H=3, hd=128, nb=8, bs=128, top=1, seed=8),           # head_dim 128, top-1 (tensor cores)
 ])
 def test_read_matches_oracle(case):
     case = dict(case)
