@@ -114,7 +114,7 @@ bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k
                            const void *dout, int H);
 // do_src: dO in plan order (do_is_rows) or token order (rows gathered by the kernels).
 cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v, const void *do_src,
-                               bool do_is_rows, const float *lse, int H, int nb, int top, const PlanLayout &L,
+                               bool do_is_rows, const float *lse, int hd, int H, int nb, int top, const PlanLayout &L,
                                const PlanView &P, void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
                                float *ws_delta, cudaStream_t st);
 // Block-split read (split.cu): rows are (token, k) pairs of a top-1 plan built

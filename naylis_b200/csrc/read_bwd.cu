@@ -490,17 +490,18 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
     const int64_t N = static_cast<int64_t>(B) * S;
     if ((e = cudaMemsetAsync(dlog_gates, 0, sizeof(float) * N * top, st)) != cudaSuccess) return e;
     if (L.max_tiles == 0) return cudaSuccess;
-    // tensor-core kernels for head_dim 64, 128-slot blocks, top <= 2; other
-    // geometries take the warp-level mma kernels below
+    // tensor-core kernels for 128-slot blocks with head_dim 64 (top <= 2) or
+    // head_dim 128 (top 1: block-split plans); other geometries take the
+    // warp-level mma kernels below
     if (read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H)) {
         // delta = <dO, O> per plan row and head, and dO in plan order when there is
         // room for it (every tile's rows are then one TMA box)
         if ((e = launch_row_delta(dout, out, L.N, H, hd, P.perm, do_rows, ws_delta, st, P.rows_per_q)) != cudaSuccess)
             return e;
         if (do_rows)
-            return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
+            return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, hd, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                       dlog_gates, ws_delta, st);
-        return launch_read_bwd_tc(q_rows, k, v, dout, false, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
+        return launch_read_bwd_tc(q_rows, k, v, dout, false, lse, hd, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                   dlog_gates, ws_delta, st);
     }
     if (hd == 64)

@@ -3,7 +3,8 @@
 // Reference semantics: mom_kernels/triton_gpu.py:143-409 (P rebuilt from the
 // saved log-sum-exp, dS = P (dP - delta), dq = dS k * scale, dk = dS^T q *
 // scale, dv = P^T do, dlog_gates = per-block sums of dS over slots and heads).
-// Specialised like read_fwd_tc.cu: head_dim 64, 128-slot blocks, top <= 2.
+// Specialised like read_fwd_tc.cu: 128-slot blocks; head_dim 64 with top <= 2,
+// head_dim 128 with one block per row (block-split plans).
 // Q and dO are read in routing-plan row order (q_rows from the forward, dO
 // copied by the row kernel that also forms delta = <dO, O> per row and head),
 // so every tile is one 2-D TMA box; the no-workspace entry gathers dO's rows
@@ -40,13 +41,25 @@
 namespace mom {
 
 namespace {
-constexpr int kHD = 64;
 constexpr int kBS = 128;
 constexpr int kTM = 128;
 constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
 constexpr int kSoftThreads = kSoftWarps * 32;
-constexpr uint32_t kRowTile = kTM * kHD * 2;     // 16 KiB: 128 rows x 64 bf16
+constexpr uint32_t kBoxBytes = 128 * 128;      // one TMA box: 128 rows x 64 bf16 columns (128-B swizzle)
 constexpr uint32_t kTmemCols = 512;
+// Rows of Q / dO / K / V are 64-column TMA boxes side by side (kBoxBytes apart):
+// one box at head_dim 64, two at head_dim 128.
+template <int HD> struct Geo {
+    static constexpr int kBoxes = HD / 64;
+    static constexpr uint32_t kRowTile = kTM * HD * 2;   // 128 rows x HD bf16
+    // K / V / Q / dO as the MN-major B operand (N = HD): N-atoms of 64 columns
+    // kBoxBytes apart (head_dim 64 has one atom; its value is what the validated
+    // kernels used)
+    __host__ __device__ static constexpr uint32_t kLbo(uint32_t hd64_value) { return HD == 64 ? hd64_value : kBoxBytes; }
+};
+// K-step kk of an MMA whose K dimension is head_dim: +32 B within a 64-column
+// box (+2 in the descriptor's address field), +kBoxBytes (+1024) per box
+__device__ __forceinline__ uint64_t hd_step(int kk) { return 1024u * (kk >> 2) + 2u * (kk & 3); }
 
 struct DqBars {
     uint64_t full[2], empty[2], kv_full, kv_empty, s_full, ds_full, dq_full, dq_free, drain;
@@ -58,11 +71,19 @@ struct DqBars {
     int tok[128];     // the loader's row tokens of the tile being copied
 };
 static_assert(sizeof(DqBars) <= 1024, "barrier block");
-constexpr uint32_t kDqStage = 2 * kRowTile;                      // Q + dO
-constexpr uint32_t kDqKV = 4 * kRowTile;                         // K (2 blocks) + V (2 blocks)
-constexpr uint32_t kDqScratch = 2 * 2 * 4 * kTM * 4                 // [2 items][P.dP | P][4 groups][128] fp32
-                                + kTM * kHD * 2 + kTM * 4;          // dQ tile staged for coalesced stores, tokens
-constexpr uint32_t kDqSmem = 2 * kDqStage + kDqKV + kDqScratch + 1024 + 1024;
+// head_dim 64: sets of up to two blocks; head_dim 128: one block per row (the
+// block-split plan), so K / V hold one block and dQ is one 128-column sum.
+template <int HD> struct Dq {
+    static constexpr int kMaxBlk = HD == 64 ? 2 : 1;
+    static constexpr uint32_t kRowTile = Geo<HD>::kRowTile;
+    static constexpr uint32_t kBlkBytes = kBS * HD * 2;
+    static constexpr uint32_t kStage = 2 * kRowTile;                       // Q + dO
+    static constexpr uint32_t kKV = 2 * kMaxBlk * kBlkBytes;               // K blocks + V blocks
+    static constexpr uint32_t kScratch = 2 * 2 * 4 * kTM * 4               // [2 items][P.dP | P][4 groups][128] fp32
+                                         + kTM * 64 * 2 + kTM * 4;         // 64 dQ columns staged, tokens
+    static constexpr uint32_t kSmem = 2 * kStage + kKV + kScratch + 1024 + 1024;
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+};
 // warp 0 loader, warps 1 and 2 MMA issuers (warp 1: S, then dQ over block 0;
 // warp 2: dP, then dQ over block 1; warp 1 owns TMEM), warps 3-18 softmax.
 // TMEM: S at columns 0..255 (dS written back over it as bf16, the A operand of
@@ -74,19 +95,23 @@ constexpr int kDqThreads = 96 + kSoftThreads;
 // ============================================================================ dQ
 // kDoRows: dO in plan order (one TMA box per tile, like Q); else dO in token
 // order, its rows gathered with cp.async.
-template <bool kDoRows>
+template <int HD, bool kDoRows>
 __global__ void __launch_bounds__(kDqThreads, 1)
 read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                       const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
                       const uint16_t *__restrict__ dout,
                       const float *__restrict__ lse, int H, int top, float scale, float scale_log2, PlanView P,
                       uint16_t *__restrict__ dq, float *__restrict__ dlog_gates, float *__restrict__ ws_delta) {
+    using C = Dq<HD>;
+    constexpr int kHD = HD;
+    constexpr uint32_t kRowTile = C::kRowTile, kDqStage = C::kStage, kDqKV = C::kKV, kDqScratch = C::kScratch;
+    constexpr uint32_t kBlkBytes = C::kBlkBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
     const uint32_t sKV = base + 2 * kDqStage;
-    const uint32_t sK = sKV, sV = sKV + 2 * kRowTile;
+    const uint32_t sK = sKV, sV = sKV + C::kMaxBlk * kBlkBytes;
     float *sPart = reinterpret_cast<float *>(sbase + 2 * kDqStage + kDqKV);
     uint4 *sOut = reinterpret_cast<uint4 *>(sPart + 2 * 2 * 4 * kTM);      // [128 rows][8 x 16 B]
     int *sTok = reinterpret_cast<int *>(sOut + kTM * 8);
@@ -167,14 +192,20 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             const uint32_t sQ = base + s * kDqStage, sD = sQ + kRowTile;
             if (!kDoRows) {
                 tc::stage_row_tokens(bars->tok, rows, lane);
-                tc::gather_tile_rows(sD, dout, ld, h * kHD, bars->tok, lane);
+#pragma unroll
+                for (int c = 0; c < Geo<HD>::kBoxes; ++c)
+                    tc::gather_tile_rows(sD + c * kBoxBytes, dout, ld, h * kHD + 64 * c, bars->tok, lane);
                 tc::cp_async_arrive_noinc(&bars->full[s]);
             }
             if (lane == 0) {
                 bars->meta[s] = nload | (reload << 8) | (nblk << 12);   // released by the arrive below
                 tc::mbar_arrive_expect_tx(&bars->full[s], kDoRows ? 2 * kRowTile : kRowTile);
-                tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
-                if (kDoRows) tc::tma_load_2d(sD, &tmap_do, h * kHD, x0, &bars->full[s]);
+#pragma unroll
+                for (int c = 0; c < Geo<HD>::kBoxes; ++c) {
+                    tc::tma_load_2d(sQ + c * kBoxBytes, &tmap_q, h * kHD + 64 * c, x0, &bars->full[s]);
+                    if (kDoRows)
+                        tc::tma_load_2d(sD + c * kBoxBytes, &tmap_do, h * kHD + 64 * c, x0, &bars->full[s]);
+                }
             }
             __syncwarp();
             last_full = i;
@@ -183,11 +214,16 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             if (reload) {
                 if (nreload > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nreload - 1) & 1, P.err, 2, abort_flag)) break;
                 if (lane == 0) {
-                    tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kRowTile);
+                    tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * nload * kBlkBytes);
                     for (int jb = 0; jb < nload; ++jb) {
                         const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
-                        tc::tma_load_2d(sK + jb * kRowTile, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
-                        tc::tma_load_2d(sV + jb * kRowTile, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
+#pragma unroll
+                        for (int c = 0; c < Geo<HD>::kBoxes; ++c) {
+                            tc::tma_load_2d(sK + jb * kBlkBytes + c * kBoxBytes, &tmap_k, h * kHD + 64 * c,
+                                            blk * kBS, &bars->kv_full);
+                            tc::tma_load_2d(sV + jb * kBlkBytes + c * kBoxBytes, &tmap_v, h * kHD + 64 * c,
+                                            blk * kBS, &bars->kv_full);
+                        }
                     }
                 }
                 __syncwarp();
@@ -204,7 +240,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
         // thread issues a tcgen05.mma only every ~100 cycles.
         const bool wa = warp == 1;
         const uint32_t idesc_dq = tc::idesc_bf16_f32(kTM, kHD, false, true);
-        const uint64_t bk0 = tc::smem_desc_sw128(sK + (wa ? 0 : kRowTile), 4 * kRowTile, 1024);
+        const uint64_t bk0 = tc::smem_desc_sw128(sK + (wa ? 0 : kBlkBytes), Geo<HD>::kLbo(4 * kRowTile), 1024);
         int nreload = 0;
         for (int i = 0; i < nmine; ++i) {
             const int s = i & 1, j = i >> 1;
@@ -229,8 +265,8 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 const uint64_t da = tc::smem_desc_sw128(sA, 16, 1024);
                 const uint64_t db = tc::smem_desc_sw128(wa ? sK : sV, 16, 1024);
 #pragma unroll
-                for (int kk = 0; kk < kHD / 16; ++kk)   // +32 B per K step: +2 in the address field
-                    tc::mma_bf16_ss(tmem + (wa ? 0 : 256), da + 2 * kk, db + 2 * kk, idesc_s, kk > 0);
+                for (int kk = 0; kk < kHD / 16; ++kk)
+                    tc::mma_bf16_ss(tmem + (wa ? 0 : 256), da + hd_step(kk), db + hd_step(kk), idesc_s, kk > 0);
                 tc::mma_commit(&bars->s_full);
                 tc::mma_commit(&bars->empty[s]);
             }
@@ -238,7 +274,7 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             if (!tc::mbar_wait_warp(&bars->ds_full, i & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
             if (lane == 0) {
-                if (nblk > (wa ? 0 : 1)) {
+                if (nblk > (wa ? 0 : 1) && (wa || C::kMaxBlk > 1)) {
 #pragma unroll
                     for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
                         const int kk = (wa ? 0 : 8) + k8;
@@ -376,27 +412,44 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
                 break;
             }
             tc::tc_fence_after();
+            // head_dim 64: dQ_0 + dQ_1 (the set's blocks) at 256 / 320; head_dim 128:
+            // columns 16g.. and 64+16g.. of the one dQ at 256
             uint32_t a0[16], a1[16];
-            tc::tmem_ld16(trow + 256 + grp * 16, a0);          // both halves in one round trip
+            tc::tmem_ld16(trow + 256 + grp * 16, a0);          // both in one round trip
             tc::tmem_ld16(trow + 320 + grp * 16, a1);
             tc::tmem_ld_wait_regs(a0);
             tc::tmem_ld_wait_regs(a1);
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->dq_free);
+            auto pack16 = [&](const float (&o)[16], uint4 &v0, uint4 &v1) {
+                v0.x = pack_bf16x2(o[0] * scale, o[1] * scale);
+                v0.y = pack_bf16x2(o[2] * scale, o[3] * scale);
+                v0.z = pack_bf16x2(o[4] * scale, o[5] * scale);
+                v0.w = pack_bf16x2(o[6] * scale, o[7] * scale);
+                v1.x = pack_bf16x2(o[8] * scale, o[9] * scale);
+                v1.y = pack_bf16x2(o[10] * scale, o[11] * scale);
+                v1.z = pack_bf16x2(o[12] * scale, o[13] * scale);
+                v1.w = pack_bf16x2(o[14] * scale, o[15] * scale);
+            };
             float o[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e)
-                o[e] = (nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
             uint4 v0, v1;
-            v0.x = pack_bf16x2(o[0] * scale, o[1] * scale);
-            v0.y = pack_bf16x2(o[2] * scale, o[3] * scale);
-            v0.z = pack_bf16x2(o[4] * scale, o[5] * scale);
-            v0.w = pack_bf16x2(o[6] * scale, o[7] * scale);
-            v1.x = pack_bf16x2(o[8] * scale, o[9] * scale);
-            v1.y = pack_bf16x2(o[10] * scale, o[11] * scale);
-            v1.z = pack_bf16x2(o[12] * scale, o[13] * scale);
-            v1.w = pack_bf16x2(o[14] * scale, o[15] * scale);
-            tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, tok, dq + h * kHD, ld);
+            if constexpr (HD == 64) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    o[e] = (nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
+                pack16(o, v0, v1);
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, tok, dq + h * kHD, ld);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = nblk > 0 ? __uint_as_float(a0[e]) : 0.0f;
+                pack16(o, v0, v1);
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, tok, dq + h * kHD, ld);
+                tc::named_bar(bar_id, 128);   // the staging rows are read out before they are rewritten
+#pragma unroll
+                for (int e = 0; e < 16; ++e) o[e] = nblk > 0 ? __uint_as_float(a1[e]) : 0.0f;
+                pack16(o, v0, v1);
+                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, tok, dq + h * kHD + 64, ld);
+            }
         }
     }
     tc::tc_fence_before();
@@ -407,37 +460,46 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
 
 // ============================================================================ dK / dV
 namespace {
-constexpr int kDkvStages = 4;
+constexpr int kDkvMaxStages = 4;
 // warp 0 loader, warp 1 S^T / dP^T MMAs (and TMEM owner), warp 2 dK / dV MMAs,
 // warps 3-18 softmax + epilogue: one thread issues a tcgen05.mma only every
 // ~100 cycles, so the two GEMM pairs get an issuing warp each.
 constexpr int kDkvThreads = 96 + kSoftThreads;
 struct DkvBars {
-    uint64_t full[kDkvStages], empty[kDkvStages], kv_full, kv_empty, s_full[3], pds_full[3], buf_free[3], acc_full,
-        acc_free, drain;
+    uint64_t full[kDkvMaxStages], empty[kDkvMaxStages], kv_full, kv_empty, s_full[3], pds_full[3], buf_free[3],
+        acc_full, acc_free, drain;
     uint32_t tmem_base;
     int abort;
     int tok[128];     // the loader's row tokens of the tile being copied
 };
 static_assert(sizeof(DkvBars) <= 1024, "barrier block");
-constexpr uint32_t kKvTile = kBS * kHD * 2;                      // 16 KiB
-constexpr uint32_t kDkvStage = 2 * kRowTile;                     // Q + dO
 constexpr uint32_t kMetaBytes = 2 * kTM * 4;                     // bias2 - lse2, delta
-constexpr uint32_t kDkvSmem = 2 * kKvTile + kDkvStages * kDkvStage + kDkvStages * kMetaBytes + 1024 + 1024;
 // A tile's 128 tokens go through the MMAs and the softmax in two steps of 64.
-// TMEM: step buffer b (= step % 3) at column 128*b holds S^T [128 slots x 64
+// TMEM: step buffer b (= step % kBufs) at column 128*b holds S^T [128 slots x 64
 // tokens] in columns +0..63 and dP^T in +64..127; the softmax overwrites them in
 // place with bf16 P^T and dS^T (softmax group g's 16 tokens packed into the first
 // 8 of its 16 columns), the A operands of dV += P^T dO and dK += dS^T Q. dK is
-// accumulated at columns 384..447, dV at 448..511. Three buffers let the S^T /
-// dP^T MMAs of step s+2 run while the softmax works on step s+1 and the dK / dV
-// MMAs of step s still read their buffer.
+// accumulated at columns kAccCol.., dV at kAccCol + HD... head_dim 64: three
+// buffers (0..383), dK / dV at 384 / 448, four Q / dO stages; the S^T / dP^T
+// MMAs of step s+2 run while the softmax works on step s+1 and the dK / dV MMAs
+// of step s still read their buffer. head_dim 128: the two 128-column
+// accumulators at 256 / 384 leave room for two buffers, and shared memory for
+// two stages.
 constexpr int kHalf = 64;
-constexpr int kBufs = 3;
-constexpr uint32_t kAccCol = 384;
+template <int HD> struct Dkv {
+    static constexpr int kStages = HD == 64 ? 4 : 2;
+    static constexpr int kBufs = HD == 64 ? 3 : 2;
+    static constexpr uint32_t kAccCol = HD == 64 ? 384 : 256;
+    static constexpr uint32_t kRowTile = Geo<HD>::kRowTile;
+    static constexpr uint32_t kKvTile = kBS * HD * 2;                 // one block of K or V
+    static constexpr uint32_t kStage = 2 * kRowTile;                  // Q + dO
+    static constexpr uint32_t kSmem = 2 * kKvTile + kStages * kStage + kStages * kMetaBytes + 1024 + 1024;
+    static_assert(kSmem <= 227 * 1024, "shared memory");
+    static_assert(kStages <= kDkvMaxStages && kBufs <= 3 && kAccCol + 2 * HD <= kTmemCols, "layout");
+};
 }  // namespace
 
-template <bool kDoRows>
+template <int HD, bool kDoRows>
 __global__ void __launch_bounds__(kDkvThreads, 1)
 read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
                         const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_do,
@@ -445,6 +507,9 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                         const float *__restrict__ lse, const float *__restrict__ ws_delta, int H, int nb, int top,
                         int max_tiles, float scale, float scale_log2, PlanView P,
                         float *__restrict__ dk_acc, float *__restrict__ dv_acc) {
+    using C = Dkv<HD>;
+    constexpr int kHD = HD, kDkvStages = C::kStages, kBufs = C::kBufs;
+    constexpr uint32_t kRowTile = C::kRowTile, kKvTile = C::kKvTile, kDkvStage = C::kStage, kAccCol = C::kAccCol;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -548,8 +613,11 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
             if (nkv > 0 && !tc::mbar_wait_warp(&bars->kv_empty, (nkv - 1) & 1, P.err, 2, abort_flag)) break;
             if (lane == 0) {
                 tc::mbar_arrive_expect_tx(&bars->kv_full, 2 * kKvTile);
-                tc::tma_load_2d(sK, &tmap_k, h * kHD, blk * kBS, &bars->kv_full);
-                tc::tma_load_2d(sV, &tmap_v, h * kHD, blk * kBS, &bars->kv_full);
+#pragma unroll
+                for (int c = 0; c < Geo<HD>::kBoxes; ++c) {
+                    tc::tma_load_2d(sK + c * kBoxBytes, &tmap_k, h * kHD + 64 * c, blk * kBS, &bars->kv_full);
+                    tc::tma_load_2d(sV + c * kBoxBytes, &tmap_v, h * kHD + 64 * c, blk * kBS, &bars->kv_full);
+                }
             }
             ++nkv;
             const int *list = P.blktiles + static_cast<int64_t>(blk) * max_tiles;
@@ -579,13 +647,19 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 const int x0 = tc::get(cx, src);
                 if (!kDoRows) {
                     tc::stage_row_tokens(bars->tok, rows, lane);
-                    tc::gather_tile_rows(sD, dout, ld, h * kHD, bars->tok, lane);
+#pragma unroll
+                    for (int c = 0; c < Geo<HD>::kBoxes; ++c)
+                        tc::gather_tile_rows(sD + c * kBoxBytes, dout, ld, h * kHD + 64 * c, bars->tok, lane);
                     tc::cp_async_arrive_noinc(&bars->full[s]);
                 }
                 if (lane == 0) {
                     tc::mbar_arrive_expect_tx(&bars->full[s], kDoRows ? 2 * kRowTile : kRowTile);
-                    tc::tma_load_2d(sQ, &tmap_q, h * kHD, x0, &bars->full[s]);
-                    if (kDoRows) tc::tma_load_2d(sD, &tmap_do, h * kHD, x0, &bars->full[s]);
+#pragma unroll
+                    for (int c = 0; c < Geo<HD>::kBoxes; ++c) {
+                        tc::tma_load_2d(sQ + c * kBoxBytes, &tmap_q, h * kHD + 64 * c, x0, &bars->full[s]);
+                        if (kDoRows)
+                            tc::tma_load_2d(sD + c * kBoxBytes, &tmap_do, h * kHD + 64 * c, x0, &bars->full[s]);
+                    }
                 } else {
                     tc::mbar_arrive(&bars->full[s]);
                 }
@@ -632,9 +706,9 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     const uint32_t tb = tmem + b * 128;
                     if (lane == 0) {
 #pragma unroll
-                        for (int kk = 0; kk < kHD / 16; ++kk) {   // +32 B per K step: +2 in the address field
-                            tc::mma_bf16_ss(tb, dk0 + 2 * kk, dq0 + 2 * kk, idesc_s, kk > 0);
-                            tc::mma_bf16_ss(tb + kHalf, dv0 + 2 * kk, dd0 + 2 * kk, idesc_s, kk > 0);
+                        for (int kk = 0; kk < kHD / 16; ++kk) {
+                            tc::mma_bf16_ss(tb, dk0 + hd_step(kk), dq0 + hd_step(kk), idesc_s, kk > 0);
+                            tc::mma_bf16_ss(tb + kHalf, dv0 + hd_step(kk), dd0 + hd_step(kk), idesc_s, kk > 0);
                         }
                         tc::mma_commit(&bars->s_full[b]);
                     }
@@ -682,8 +756,8 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                     }
                     tc::tc_fence_after();
                     const uint32_t sQ = sStage + (g % kDkvStages) * kDkvStage + half * (kHalf * 128);
-                    const uint64_t bq = tc::smem_desc_sw128(sQ, 2 * kRowTile, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(sQ + kRowTile, 2 * kRowTile, 1024);
+                    const uint64_t bq = tc::smem_desc_sw128(sQ, Geo<HD>::kLbo(2 * kRowTile), 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(sQ + kRowTile, Geo<HD>::kLbo(2 * kRowTile), 1024);
                     const uint32_t tb = tmem + b * 128;
                     if (lane == 0) {
 #pragma unroll
@@ -771,23 +845,29 @@ read_bwd_dkdv_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid
                 }
             }
             if (stop) break;
-            // epilogue of the segment: 16 of the 64 dK columns and 16 of the 64 dV
-            // columns per thread -> fp32 reductions
+            // epilogue of the segment: 16 columns of dK and of dV per 64-column box
+            // and thread -> fp32 reductions
             if (!tc::mbar_wait_warp(&bars->acc_full, nkv & 1, P.err, 2, abort_flag)) break;
             tc::tc_fence_after();
-            uint32_t kr[16], vr[16];
-            tc::tmem_ld16(trow + kAccCol + grp * 16, kr);
-            tc::tmem_ld16(trow + kAccCol + kHD + grp * 16, vr);
+            uint32_t kr[Geo<HD>::kBoxes][16], vr[Geo<HD>::kBoxes][16];
+#pragma unroll
+            for (int c = 0; c < Geo<HD>::kBoxes; ++c) {
+                tc::tmem_ld16(trow + kAccCol + 64 * c + grp * 16, kr[c]);
+                tc::tmem_ld16(trow + kAccCol + kHD + 64 * c + grp * 16, vr[c]);
+            }
             tc::tmem_ld_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->acc_free);
             ++nkv;
-            float *dkr = dk_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + grp * 16;
-            float *dvr = dv_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + grp * 16;
 #pragma unroll
-            for (int c = 0; c < 16; c += 2) {
-                red_add_v2(dkr + c, __uint_as_float(kr[c]) * scale, __uint_as_float(kr[c + 1]) * scale);
-                red_add_v2(dvr + c, __uint_as_float(vr[c]), __uint_as_float(vr[c + 1]));
+            for (int cb = 0; cb < Geo<HD>::kBoxes; ++cb) {
+                float *dkr = dk_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + 64 * cb + grp * 16;
+                float *dvr = dv_acc + (static_cast<int64_t>(blk) * kBS + r) * ld + h * kHD + 64 * cb + grp * 16;
+#pragma unroll
+                for (int c = 0; c < 16; c += 2) {
+                    red_add_v2(dkr + c, __uint_as_float(kr[cb][c]) * scale, __uint_as_float(kr[cb][c + 1]) * scale);
+                    red_add_v2(dvr + c, __uint_as_float(vr[cb][c]), __uint_as_float(vr[cb][c + 1]));
+                }
             }
         }
     }
@@ -803,57 +883,71 @@ int device_sm_count();
 
 bool read_bwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v,
                            const void *dout, int H) {
-    // the backward kernels are written for head_dim 64 only
-    return hd == kHD && read_fwd_tc_supported(hd, bs, top, q, k, v, H) &&
-           (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
+    // head_dim 64 with sets of up to two blocks, head_dim 128 with one block per row
+    return read_fwd_tc_supported(hd, bs, top, q, k, v, H) && (reinterpret_cast<uintptr_t>(dout) % 16) == 0;
 }
 
-template <bool kDoRows>
+template <int HD, bool kDoRows>
 static cudaError_t launch_bwd_tc_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mq,
                                    const CUtensorMap &md, const uint16_t *dout, const float *lse, int H, int nb,
                                    int top, const PlanLayout &L, const PlanView &P, void *dq, float *dk_acc,
                                    float *dv_acc, float *dlog_gates, float *ws_delta, cudaStream_t st) {
-    const float scale = 1.0f / sqrtf(static_cast<float>(kHD));
+    const float scale = 1.0f / sqrtf(static_cast<float>(HD));
     const float scale_log2 = scale * kLog2e;
     const int sms = device_sm_count();
-    cudaError_t e = cudaFuncSetAttribute(read_bwd_dq_tc_kernel<kDoRows>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDqSmem);
+    constexpr uint32_t dq_smem = Dq<HD>::kSmem, dkv_smem = Dkv<HD>::kSmem;
+    cudaError_t e = cudaFuncSetAttribute(read_bwd_dq_tc_kernel<HD, kDoRows>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq_smem);
     if (e != cudaSuccess) return e;
     const int64_t items = L.max_tiles * H;
     const int grid = static_cast<int>(std::min<int64_t>(items, sms));
-    read_bwd_dq_tc_kernel<kDoRows><<<grid, kDqThreads, kDqSmem, st>>>(
+    read_bwd_dq_tc_kernel<HD, kDoRows><<<grid, kDqThreads, dq_smem, st>>>(
         mk, mv, mq, md, dout, lse, H, top, scale, scale_log2, P, static_cast<uint16_t *>(dq), dlog_gates, ws_delta);
     count_launch();
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel<kDoRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kDkvSmem);
+    e = cudaFuncSetAttribute(read_bwd_dkdv_tc_kernel<HD, kDoRows>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)dkv_smem);
     if (e != cudaSuccess) return e;
     // one CTA per SM, each over an equal share of the (block, head, tile) units
-    read_bwd_dkdv_tc_kernel<kDoRows><<<sms, kDkvThreads, kDkvSmem, st>>>(
+    read_bwd_dkdv_tc_kernel<HD, kDoRows><<<sms, kDkvThreads, dkv_smem, st>>>(
         mk, mv, mq, md, dout, lse, ws_delta, H, nb, top, static_cast<int>(L.max_tiles), scale, scale_log2,
         P, dk_acc, dv_acc);
     count_launch();
     return cudaGetLastError();
 }
 
-cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v, const void *do_src,
-                               bool do_is_rows, const float *lse, int H, int nb, int top, const PlanLayout &L,
-                               const PlanView &P, void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
-                               float *ws_delta, cudaStream_t st) {
+template <int HD>
+static cudaError_t launch_read_bwd_tc_hd(const void *q_rows, const void *k, const void *v, const void *do_src,
+                                         bool do_is_rows, const float *lse, int H, int nb, int top,
+                                         const PlanLayout &L, const PlanView &P, void *dq, float *dk_acc,
+                                         float *dv_acc, float *dlog_gates, float *ws_delta, cudaStream_t st) {
     CUtensorMap mk, mv, mq, md;
-    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * kHD;
+    const uint64_t rows = static_cast<uint64_t>(nb) * kBS, cols = static_cast<uint64_t>(H) * HD;
     if (!make_bf16_map(&mk, k, rows, cols, kBS) || !make_bf16_map(&mv, v, rows, cols, kBS) ||
         !make_bf16_map(&mq, q_rows, static_cast<uint64_t>(L.N), cols, kTM))
         return cudaErrorInvalidValue;
     const uint16_t *do16 = static_cast<const uint16_t *>(do_src);
     if (do_is_rows) {
         if (!make_bf16_map(&md, do_src, static_cast<uint64_t>(L.N), cols, kTM)) return cudaErrorInvalidValue;
-        return launch_bwd_tc_t<true>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
-                                     ws_delta, st);
+        return launch_bwd_tc_t<HD, true>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc,
+                                         dlog_gates, ws_delta, st);
     }
     md = mq;   // unused by the gathering variant
-    return launch_bwd_tc_t<false>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
-                                  ws_delta, st);
+    return launch_bwd_tc_t<HD, false>(mk, mv, mq, md, do16, lse, H, nb, top, L, P, dq, dk_acc, dv_acc, dlog_gates,
+                                      ws_delta, st);
+}
+
+cudaError_t launch_read_bwd_tc(const void *q_rows, const void *k, const void *v, const void *do_src,
+                               bool do_is_rows, const float *lse, int hd, int H, int nb, int top,
+                               const PlanLayout &L, const PlanView &P, void *dq, float *dk_acc, float *dv_acc,
+                               float *dlog_gates, float *ws_delta, cudaStream_t st) {
+    if (hd == 64)
+        return launch_read_bwd_tc_hd<64>(q_rows, k, v, do_src, do_is_rows, lse, H, nb, top, L, P, dq, dk_acc,
+                                         dv_acc, dlog_gates, ws_delta, st);
+    if (hd == 128 && top == 1)
+        return launch_read_bwd_tc_hd<128>(q_rows, k, v, do_src, do_is_rows, lse, H, nb, top, L, P, dq, dk_acc,
+                                          dv_acc, dlog_gates, ws_delta, st);
+    return cudaErrorInvalidValue;
 }
 
 }  // namespace mom

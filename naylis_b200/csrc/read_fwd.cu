@@ -238,8 +238,9 @@ cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, 
     // q in plan order, for the tensor-core kernels of this call and of the backward
     cudaError_t e = launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st, P.rows_per_q);
     if (e != cudaSuccess) return e;
-    // the tensor-core kernel covers head_dim 64, 128-slot blocks, top <= 2;
-    // other geometries take the warp-level mma kernel below
+    // the tensor-core kernel covers 128-slot blocks with head_dim 64 (top <= 2)
+    // or head_dim 128 (top 1: block-split plans); other geometries take the
+    // warp-level mma kernel below
     if (read_fwd_tc_supported(hd, bs, top, q_rows, k, v, H))
         return launch_read_fwd_tc(q_rows, k, v, hd, H, nb, top, L, P, out, lse, st);
     if (hd == 64) return launch_fwd_t<64>(q, k, v, H, bs, top, L, P, out, lse, st);

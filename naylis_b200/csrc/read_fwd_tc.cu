@@ -2,8 +2,9 @@
 //
 // Same math as read_fwd.cu (reference: mom_kernels/reference.py:39-61 with the
 // bias of :14-29, triton_gpu.py:64-141), specialised for the shapes of the
-// Naylis configurations: head_dim 64, 128-slot blocks, at most two blocks per
-// routing set (top-2). A work item is (tile of <= 128 tokens sharing one block
+// Naylis configurations: 128-slot blocks; head_dim 64 with at most two blocks
+// per routing set (top-2), or head_dim 128 with one block per row (the
+// block-split plan of top-k routing with many blocks). A work item is (tile of <= 128 tokens sharing one block
 // set, head); CTAs are persistent over items.
 //
 // Warp roles (608 threads):
