@@ -527,6 +527,79 @@ def run_reference(args):
     }), flush=True)
 
 
+# ------------------------------------------------------------------ config-3 read
+CFG3 = dict(B=4, S=4096, H=16, hd=128, nb=32, bs=128, top=4)
+METRIC3 = "MoM read fwd+bwd tokens/s, BASELINE config 3 geometry (top-4 of 32 blocks, 16x128 heads)"
+
+
+def run_read_top4of32(args):
+    """The read alone on BASELINE config 3's geometry (x [4, 4096], 16 heads of
+    128, bank 32 x 128 slots, top-4): 35,960 block sets, so the door takes the
+    block-split read. One step = mom_read forward + backward through the door
+    on resident inputs, L2 flushed before each timed step."""
+    import torch
+    from naylis_b200 import _lib
+    from naylis_b200 import mom_kernels as mk
+    c = CFG3
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    B, S, H, hd, nb, bs, top = c["B"], c["S"], c["H"], c["hd"], c["nb"], c["bs"], c["top"]
+    q = (torch.randn(B, S, H, hd, generator=g, device=dev) * 0.7).bfloat16().requires_grad_(True)
+    k = (torch.randn(nb * bs, H * hd, generator=g, device=dev) * 0.4).bfloat16().requires_grad_(True)
+    v = (torch.randn(nb * bs, H * hd, generator=g, device=dev) * 0.4).bfloat16().requires_grad_(True)
+    gates = torch.softmax(torch.randn(B, S, top, generator=g, device=dev), -1).requires_grad_(True)
+    idx = torch.argsort(torch.rand(B, S, nb, generator=g, device=dev), -1)[..., :top]
+    dout = torch.randn(B, S, H, hd, generator=g, device=dev).bfloat16()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+
+    def step():
+        for t in (q, k, v, gates):
+            t.grad = None
+        out = mk.mom_read(q, k, v, idx, gates, num_blocks=nb, block_size=bs)
+        out.backward(dout)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(0)
+    clocks.start()
+    t_wall0 = time.time()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    l0 = lib.mom_kernel_launches()
+    for i in range(args.steps):
+        flush.zero_()
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    launches = lib.mom_kernel_launches() - l0
+    clocks.window = (t_wall0, time.time())
+    clocks.stop()
+    total_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    N = B * S
+    fwd_flops, bwd_flops = read_flops(N, H * hd, top, bs)   # over the selected blocks only
+    flops = fwd_flops + bwd_flops
+    ms = total_ms / args.steps
+    pk = peaks()
+    tflops = flops / (ms / 1e3) / 1e12
+    print(json.dumps({
+        "metric": METRIC3, "value": round(N / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) q/k/v scaled 0.7/0.4/0.4, random distinct top-4 blocks, softmax gates)",
+        "config": {"workload": "cfg3-read: mom_read fwd+bwd, B=4 S=4096, 16x128 heads, bank 32x128 slots, top-4 "
+                               "(block-split read)", "l2": "flushed between timed steps (256 MiB write, untimed)"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["bf16"], "unit": "TFLOP/s",
+                     "frac": round(tflops / pk["bf16"], 4), "traffic": None,
+                     "kernel": "MoM read fwd+bwd, block-split (bucket, row passes, fwd, dq, dkdv, combine)",
+                     "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
+        "gpu_launches": int(launches), "clocks": clocks.summary(),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -539,11 +612,15 @@ def main():
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
+    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "read-top4of32"],
+                    help="cfg2: the headline layer step; read-top4of32: the read alone on config 3's geometry")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "read-top4of32":
+        run_read_top4of32(args)
     else:
         run_gpu(args)
 

@@ -440,7 +440,11 @@ int mom_read_bwd(const void *q, const void *k, const void *v, const void *out, c
 // (token, k) pair is a row of a top-1 plan over B*S*top rows, read by the same
 // kernels with PlanView::rows_per_q = top, then combined per token (split.cu).
 namespace {
+// tail of a block-split plan: the rows' log-gates (M fp32), then iperm (M int32)
 size_t split_tail_offset(int64_t M, int64_t nb) { return align256(mom::plan_layout(M, nb, 1).total); }
+size_t split_iperm_offset(int64_t M, int64_t nb) {
+    return split_tail_offset(M, nb) + align256(static_cast<size_t>(M) * 4);
+}
 
 int check_split_geometry(int dtype, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs,
                          int64_t top) {
@@ -454,7 +458,7 @@ size_t mom_plan_split_size(int64_t N, int64_t nb, int64_t top) {
     if (N < 0 || nb <= 0 || nb > 64 || top <= 0 || top > mom::kMaxTop || top > nb) return 0;
     const int64_t M = N * top;
     if (M >= (int64_t(1) << 31)) return 0;
-    return split_tail_offset(M, nb) + align256(static_cast<size_t>(M) * 4);
+    return split_iperm_offset(M, nb) + align256(static_cast<size_t>(M) * 4);
 }
 
 int mom_bucket_split(const void *top_idx, int idx_dtype, const float *log_gates, int64_t N, int64_t nb,
@@ -475,8 +479,10 @@ int mom_bucket_split(const void *top_idx, int idx_dtype, const float *log_gates,
     float *lg_rows = reinterpret_cast<float *>(static_cast<char *>(plan) + split_tail_offset(M, nb));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const int idx64 = idx_dtype == MOM_I64;
+    int *iperm = reinterpret_cast<int *>(static_cast<char *>(plan) + split_iperm_offset(M, nb));
     cudaError_t e = mom::launch_split_prep(top_idx, idx64, log_gates, N, (int)top, lg_rows, st);
     if (e == cudaSuccess) e = mom::launch_bucket(top_idx, idx64, lg_rows, L, P, st);
+    if (e == cudaSuccess) e = mom::launch_split_iperm(P.perm, M, iperm, st);
     if (e != cudaSuccess) return cuda_fail(e, "bucket_split");
     return MOM_OK;
 }
@@ -506,9 +512,10 @@ int mom_read_split_fwd(const void *q, const void *k, const void *v, int dtype, i
     const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
     mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
     P.rows_per_q = (int)top;
+    const int *iperm = reinterpret_cast<const int *>(static_cast<const char *>(plan) + split_iperm_offset(M, nb));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     cudaError_t e = mom::launch_read_fwd(q, k, v, 1, (int)M, (int)H, (int)hd, (int)nb, (int)bs, 1, L, P, workspace,
-                                         lse_rows, q_rows, st);
+                                         lse_rows, q_rows, st, iperm);
     if (e == cudaSuccess)
         e = mom::launch_split_combine(workspace, lse_rows, P.perm, top_idx, idx_dtype == MOM_I64, N, (int)top, (int)H,
                                       (int)hd, weights, out, st);
@@ -559,10 +566,18 @@ int mom_read_split_bwd(const void *q, const void *k, const void *v, const void *
     mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
     P.rows_per_q = (int)top;
     const int idx64 = idx_dtype == MOM_I64;
-    cudaError_t e = mom::launch_split_gate_do(dout, weights, N, (int)top, (int)H, (int)hd, g, st);
-    if (e == cudaSuccess)
-        e = mom::launch_read_bwd(q, q_rows, k, v, out, g, lse_rows, 1, (int)M, (int)H, (int)hd, (int)nb, (int)bs, 1,
-                                 L, P, dq_rows, dk_acc, dv_acc, dlog_gates, delta, do_rows, st);
+    cudaError_t e = cudaSuccess;
+    if (mom::read_bwd_tc_supported((int)hd, (int)bs, 1, q_rows, k, v, dout, (int)H)) {
+        // the rows' dO = weight x dO, formed by the tensor-core path's row copy
+        const int *iperm = reinterpret_cast<const int *>(static_cast<const char *>(plan) + split_iperm_offset(M, nb));
+        e = mom::launch_read_bwd(q, q_rows, k, v, out, dout, lse_rows, 1, (int)M, (int)H, (int)hd, (int)nb, (int)bs,
+                                 1, L, P, dq_rows, dk_acc, dv_acc, dlog_gates, delta, do_rows, st, weights, iperm);
+    } else {
+        e = mom::launch_split_gate_do(dout, weights, N, (int)top, (int)H, (int)hd, g, st);
+        if (e == cudaSuccess)
+            e = mom::launch_read_bwd(q, q_rows, k, v, out, g, lse_rows, 1, (int)M, (int)H, (int)hd, (int)nb,
+                                     (int)bs, 1, L, P, dq_rows, dk_acc, dv_acc, dlog_gates, delta, do_rows, st);
+    }
     if (e == cudaSuccess)
         e = mom::launch_split_dq_sum(dq_rows, top_idx, idx64, N, (int)top, (int)H, (int)hd, dq, dlog_gates, st);
     if (e != cudaSuccess) return cuda_fail(e, "read_split_bwd");

@@ -100,12 +100,15 @@ cudaError_t launch_permute_rows(const void *src, int64_t N, int64_t row_bytes, c
 // delta[h][r] = <dO, O> of plan row r's token and head h (fp32), dO's row copied to
 // do_rows[r] when do_rows is not null.
 cudaError_t launch_row_delta(const void *dout, const void *out, int64_t N, int H, int hd, const int *perm,
-                             void *do_rows, float *delta, cudaStream_t st, int rows_per_out = 1);
+                             void *do_rows, float *delta, cudaStream_t st, int rows_per_out = 1,
+                             const float *row_w = nullptr);
 // Read forward. q is token-ordered; q_rows (N x H*hd, same dtype) receives q in
 // plan order and is what the tensor-core kernels (and the backward) read.
+// iperm (block-split plans, rows_per_q > 1): q_rows is filled token-major.
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
                             int hd, int nb, int bs, int top, const PlanLayout &L,
-                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st);
+                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st,
+                            const int *iperm = nullptr);
 bool read_fwd_tc_supported(int hd, int bs, int top, const void *q, const void *k, const void *v, int H);
 cudaError_t launch_read_fwd_tc(const void *q_rows, const void *k, const void *v, int hd, int H, int nb, int top,
                                const PlanLayout &L, const PlanView &P, void *out, float *lse,
@@ -126,16 +129,29 @@ cudaError_t launch_split_prep(const void *top_idx, int idx64, const float *log_g
 cudaError_t launch_split_combine(const void *out_rows, const float *lse_rows, const int *perm, const void *top_idx,
                                  int idx64, int64_t N, int top, int H, int hd, float *weights, void *out,
                                  cudaStream_t st);
+// iperm[perm[r]] = r over the M = N*top rows of a block-split plan.
+cudaError_t launch_split_iperm(const int *perm, int64_t M, int *iperm, cudaStream_t st);
+// q_rows[iperm[t*top + k]] = q[t]: q in plan order, each token's row read once.
+cudaError_t launch_split_permute_q(const void *q, const int *iperm, int64_t N, int top, int64_t row_bytes,
+                                   void *q_rows, cudaStream_t st);
+// The tensor-core backward's row copy for a block-split plan, token-major:
+// do_rows[iperm[t*top+k]] = bf16(w[t*top+k][h] dO[t]), delta per row and head.
+cudaError_t launch_split_row_delta(const void *dout, const void *out, const float *weights, const int *iperm,
+                                   int64_t N, int top, int H, int hd, void *do_rows, float *delta, cudaStream_t st);
 cudaError_t launch_split_gate_do(const void *dout, const float *weights, int64_t N, int top, int H, int hd, void *g,
                                  cudaStream_t st);
 cudaError_t launch_split_dq_sum(const void *dq_rows, const void *top_idx, int idx64, int64_t N, int top, int H,
                                 int hd, void *dq, float *dlog_gates, cudaStream_t st);
 // Read backward. q_rows: as filled by launch_read_fwd. do_rows: N x H*hd scratch for
 // dO in plan order, or null (the tensor-core kernels then gather dO rows).
+// row_w (a block-split plan on the tensor-core path, with do_rows): dout is the
+// token-order dO of the combined output and row r's dO is row_w[perm[r]][h] times
+// it, formed while dO is copied into plan order (no separate weighted copy).
 cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, const void *v, const void *out,
                             const void *dout, const float *lse, int B, int S, int H, int hd,
                             int nb, int bs, int top, const PlanLayout &L, const PlanView &P,
                             void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
-                            float *ws_delta, void *do_rows, cudaStream_t st);
+                            float *ws_delta, void *do_rows, cudaStream_t st, const float *row_w = nullptr,
+                            const int *iperm = nullptr);
 
 }  // namespace mom

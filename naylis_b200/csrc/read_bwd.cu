@@ -482,7 +482,8 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
                             const void *dout, const float *lse, int B, int S, int H, int hd,
                             int nb, int bs, int top, const PlanLayout &L, const PlanView &P,
                             void *dq, float *dk_acc, float *dv_acc, float *dlog_gates,
-                            float *ws_delta, void *do_rows, cudaStream_t st) {
+                            float *ws_delta, void *do_rows, cudaStream_t st, const float *row_w,
+                            const int *iperm) {
     const size_t kv_bytes = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
     cudaError_t e = cudaMemsetAsync(dk_acc, 0, kv_bytes, st);
     if (e != cudaSuccess) return e;
@@ -493,11 +494,17 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
     // tensor-core kernels for 128-slot blocks with head_dim 64 (top <= 2) or
     // head_dim 128 (top 1: block-split plans); other geometries take the
     // warp-level mma kernels below
-    if (read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H)) {
+    const bool tc = read_bwd_tc_supported(hd, bs, top, q_rows, k, v, dout, H);
+    // weighted rows are formed only by the row copy of the tensor-core path
+    if (row_w && (!tc || !do_rows)) return cudaErrorInvalidValue;
+    if (tc) {
         // delta = <dO, O> per plan row and head, and dO in plan order when there is
         // room for it (every tile's rows are then one TMA box)
-        if ((e = launch_row_delta(dout, out, L.N, H, hd, P.perm, do_rows, ws_delta, st, P.rows_per_q)) != cudaSuccess)
-            return e;
+        e = (row_w && iperm)
+                ? launch_split_row_delta(dout, out, row_w, iperm, L.N / P.rows_per_q, P.rows_per_q, H, hd, do_rows,
+                                         ws_delta, st)
+                : launch_row_delta(dout, out, L.N, H, hd, P.perm, do_rows, ws_delta, st, P.rows_per_q, row_w);
+        if (e != cudaSuccess) return e;
         if (do_rows)
             return launch_read_bwd_tc(q_rows, k, v, do_rows, true, lse, hd, H, nb, top, L, P, dq, dk_acc, dv_acc,
                                       dlog_gates, ws_delta, st);

@@ -232,11 +232,15 @@ static cudaError_t launch_fwd_t(const void *q, const void *k, const void *v, int
 
 cudaError_t launch_read_fwd(const void *q, const void *k, const void *v, int B, int S, int H,
                             int hd, int nb, int bs, int top, const PlanLayout &L,
-                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st) {
+                            const PlanView &P, void *out, float *lse, void *q_rows, cudaStream_t st,
+                            const int *iperm) {
     (void)B; (void)S; (void)nb;
     if (L.max_tiles == 0) return cudaSuccess;
     // q in plan order, for the tensor-core kernels of this call and of the backward
-    cudaError_t e = launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st, P.rows_per_q);
+    cudaError_t e = iperm ? launch_split_permute_q(q, iperm, L.N / P.rows_per_q, P.rows_per_q,
+                                                   static_cast<int64_t>(H) * hd * 2, q_rows, st)
+                          : launch_permute_rows(q, L.N, static_cast<int64_t>(H) * hd * 2, P.perm, q_rows, st,
+                                                P.rows_per_q);
     if (e != cudaSuccess) return e;
     // the tensor-core kernel covers 128-slot blocks with head_dim 64 (top <= 2)
     // or head_dim 128 (top 1: block-split plans); other geometries take the

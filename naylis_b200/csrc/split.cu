@@ -14,7 +14,9 @@
 //   gate_do  g_k = a_k dO, the backward's per-row dO. With it, and delta taken
 //            from the combined output (rows_per_q again), every dS = P (dP - delta)
 //            of the split rows equals the full softmax's, so dK, dV and the
-//            per-row gate gradient come out exact, with no extra term.
+//            per-row gate gradient come out exact, with no extra term. (The
+//            tensor-core path forms g_k inside its row copy of dO instead, rows.cu;
+//            this kernel serves the warp-level kernels, which read dO per token.)
 //   dq_sum   dQ = sum_k dQ_k, and the dead rows' gate gradient = their first
 //            occurrence's (d bias / d log_gate = 1 for both).
 //
@@ -104,16 +106,22 @@ split_combine_kernel(const uint4 *__restrict__ out_rows, const void *__restrict_
         __syncwarp();
         for (int v = lane; v < vpr; v += 32) {
             const int h = v / vph;
+            // all rows' vectors in flight before any is used
+            float a[kMaxTop];
+            uint4 x[kMaxTop];
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k) {
+                a[k] = k < top ? wt[k * H + h] : 0.0f;
+                x[k] = a[k] != 0.0f ? out_rows[(t * top + k) * vpr + v] : make_uint4(0u, 0u, 0u, 0u);
+            }
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int k = 0; k < top; ++k) {
-                const float a = wt[k * H + h];
-                if (a == 0.0f) continue;
-                const uint4 x = out_rows[(t * top + k) * vpr + v];
-                const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k) {
+                const uint32_t xw[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    acc[2 * q] = fmaf(a, bf_lo(xw[q]), acc[2 * q]);
-                    acc[2 * q + 1] = fmaf(a, bf_hi(xw[q]), acc[2 * q + 1]);
+                    acc[2 * q] = fmaf(a[k], bf_lo(xw[q]), acc[2 * q]);
+                    acc[2 * q + 1] = fmaf(a[k], bf_hi(xw[q]), acc[2 * q + 1]);
                 }
             }
             out[t * vpr + v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
@@ -154,10 +162,14 @@ split_dq_sum_kernel(const uint4 *__restrict__ dq_rows, const void *__restrict__ 
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
         for (int v = lane; v < vpr; v += 32) {
+            uint4 x[kMaxTop];
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k)
+                x[k] = k < top ? dq_rows[(t * top + k) * vpr + v] : make_uint4(0u, 0u, 0u, 0u);
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (int k = 0; k < top; ++k) {
-                const uint4 x = dq_rows[(t * top + k) * vpr + v];
-                const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k) {
+                const uint32_t xw[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                     acc[2 * q] += bf_lo(xw[q]);
@@ -172,6 +184,82 @@ split_dq_sum_kernel(const uint4 *__restrict__ dq_rows, const void *__restrict__ 
             const uint32_t dead = dead_mask(idx, idx64, t, top, first);
             for (int k = 0; k < top; ++k)
                 if ((dead >> k) & 1) dlog_gates[t * top + k] = dlog_gates[t * top + first[k]];
+        }
+    }
+}
+
+// iperm[perm[r]] = r: each (token, k) row's position in plan order.
+__global__ void __launch_bounds__(256)
+split_iperm_kernel(const int *__restrict__ perm, int64_t M, int *__restrict__ iperm) {
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < M;
+         r += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        iperm[perm[r]] = static_cast<int>(r);
+}
+
+// Warp per token: q[t] read once, copied to the plan rows of its top (token, k) rows.
+__global__ void __launch_bounds__(256)
+split_permute_q_kernel(const uint4 *__restrict__ q, const int *__restrict__ iperm, int64_t N, int top, int vpr,
+                       uint4 *__restrict__ q_rows) {
+    const int lane = threadIdx.x & 31;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
+        int64_t dst[kMaxTop];
+#pragma unroll
+        for (int k = 0; k < kMaxTop; ++k) dst[k] = k < top ? static_cast<int64_t>(iperm[t * top + k]) * vpr : 0;
+        for (int v = lane; v < vpr; v += 32) {
+            const uint4 x = q[t * vpr + v];
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k)
+                if (k < top) q_rows[dst[k] + v] = x;
+        }
+    }
+}
+
+// Warp per token, the block-split backward's row copy on the tensor-core path:
+// for each of the token's rows p = t*top + k, do_rows[iperm[p]] = bf16(w_k dO[t])
+// (zero where w_k = 0) and delta[h][iperm[p]] = <that row, O[t]> per head (fp32
+// sums of the bf16 products, as rows.cu's row_delta_kernel forms them). dO[t] and
+// O[t] are read once per token instead of once per row.
+__global__ void __launch_bounds__(256)
+split_row_delta_kernel(const uint4 *__restrict__ dout, const uint4 *__restrict__ out,
+                       const float *__restrict__ w, const int *__restrict__ iperm, int64_t N, int top, int H,
+                       int hd, uint4 *__restrict__ do_rows, float *__restrict__ delta) {
+    const int lane = threadIdx.x & 31;
+    const int vph = hd / 8, vpr = H * vph;
+    const int64_t M = N * top;
+    const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
+        int64_t row[kMaxTop];
+#pragma unroll
+        for (int k = 0; k < kMaxTop; ++k) row[k] = k < top ? iperm[t * top + k] : 0;
+        for (int v0 = 0; v0 < vpr; v0 += 32) {
+            const int v = v0 + lane;
+            const bool in = v < vpr;
+            const int h = in ? v / vph : 0;
+            uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
+            if (in) {
+                a = dout[t * vpr + v];
+                b = out[t * vpr + v];
+            }
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int k = 0; k < kMaxTop; ++k) {
+                if (k >= top) break;
+                const float wk = in ? w[(t * top + k) * H + h] : 0.0f;
+                uint32_t g[4] = {0u, 0u, 0u, 0u};
+                float acc = 0.0f;
+                if (wk != 0.0f) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        g[q] = pack_bf16x2(wk * bf_lo(aw[q]), wk * bf_hi(aw[q]));
+                        acc = fmaf(bf_lo(g[q]), bf_lo(bw[q]), acc);
+                        acc = fmaf(bf_hi(g[q]), bf_hi(bw[q]), acc);
+                    }
+                }
+                if (in) do_rows[row[k] * vpr + v] = make_uint4(g[0], g[1], g[2], g[3]);
+                for (int o = 1; o < vph; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (in && (v % vph) == 0) delta[static_cast<int64_t>(h) * M + row[k]] = acc;
+            }
         }
     }
 }
@@ -206,6 +294,38 @@ cudaError_t launch_split_combine(const void *out_rows, const float *lse_rows, co
     if (e != cudaSuccess) return e;
     split_combine_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(out_rows), top_idx, idx64, N,
                                                          top, H, hd, weights, static_cast<uint4 *>(out));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_split_iperm(const int *perm, int64_t M, int *iperm, cudaStream_t st) {
+    if (M == 0) return cudaSuccess;
+    split_iperm_kernel<<<grid_for(M, 256), 256, 0, st>>>(perm, M, iperm);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_split_permute_q(const void *q, const int *iperm, int64_t N, int top, int64_t row_bytes,
+                                   void *q_rows, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    if (top < 1 || top > kMaxTop || row_bytes % 16 || !aligned16(q) || !aligned16(q_rows))
+        return cudaErrorInvalidValue;
+    split_permute_q_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(q), iperm, N, top,
+                                                           static_cast<int>(row_bytes / 16),
+                                                           static_cast<uint4 *>(q_rows));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_split_row_delta(const void *dout, const void *out, const float *weights, const int *iperm,
+                                   int64_t N, int top, int H, int hd, void *do_rows, float *delta, cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    if (top < 1 || top > kMaxTop || hd % 8 || (32 % (hd / 8)) || !aligned16(dout) || !aligned16(out) ||
+        !aligned16(do_rows))
+        return cudaErrorInvalidValue;
+    split_row_delta_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(dout),
+                                                           static_cast<const uint4 *>(out), weights, iperm, N, top,
+                                                           H, hd, static_cast<uint4 *>(do_rows), delta);
     count_launch();
     return cudaGetLastError();
 }

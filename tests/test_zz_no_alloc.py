@@ -92,6 +92,7 @@ def test_noalloc_matches_read_bwd_on_consecutive_calls():
         dict(B=2, S=512, H=4, hd=64, nb=8, bs=128, top=2, seed=21),
         dict(B=8, S=8192, H=16, hd=64, nb=8, bs=128, top=2, seed=22),   # B*S*H at the scratch limit
         dict(B=1, S=300, H=2, hd=128, nb=8, bs=128, top=2, seed=23),    # ragged S, head_dim 128
+        dict(B=1, S=300, H=2, hd=128, nb=8, bs=128, top=1, seed=24),    # head_dim 128 on the tensor cores
     ]
     assert 8 * 8192 * 16 * 4 == lib.mom_read_bwd_noalloc_max_bytes()
     for c in cases:
