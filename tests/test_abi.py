@@ -90,6 +90,47 @@ def test_invalid_arguments_fail_before_device_work(lib):
     assert rc == 4
 
 
+def test_block_split_and_shard_entries_validate_first(lib):
+    from naylis_b200 import _lib
+    # the block-split plan takes what set bucketing cannot (top-4 of 32 blocks) ...
+    N, nb, top = 16384, 32, 4
+    assert lib.mom_plan_size(N, nb, top) == 0
+    split = lib.mom_plan_split_size(N, nb, top)
+    # ... a top-1 plan over N*top rows plus the rows' log-gates and inverse permutation
+    assert split >= lib.mom_plan_size(N * top, nb, 1) + 2 * 4 * N * top
+    assert lib.mom_plan_split_size(N, nb, 9) == 0 and lib.mom_plan_split_size(N, 4, 5) == 0
+    # workspaces: the rows' outputs (fwd); delta + weighted dO + dQ rows + dO rows (bwd)
+    rows = N * top * 16 * 128 * 2
+    assert lib.mom_read_split_fwd_workspace_size(4, 4096, 16, 128, top) >= rows
+    assert lib.mom_read_split_bwd_workspace_size(4, 4096, 16, 128, top) >= 3 * rows + N * top * 16 * 4
+    # argument errors come before any device work
+    rc = lib.mom_bucket_split(None, _lib.I64, None, 16, 32, 9, None, 0, None)
+    assert rc == 1
+    rc = lib.mom_bucket_split(None, _lib.I64, None, 1024, 32, 4, ctypes.c_void_p(256), 16, None)
+    assert rc == 4
+    rc = lib.mom_read_split_fwd(None, None, None, _lib.BF16, 1, 4, 2, 96, 32, 128, 4, None, _lib.I64, None,
+                                None, None, None, None, None, 0, None)
+    assert rc == 2      # head_dim 96
+    rc = lib.mom_read_split_fwd(ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256), _lib.BF16, 1, 4,
+                                2, 64, 32, 128, 4, ctypes.c_void_p(256), _lib.I64, ctypes.c_void_p(256),
+                                ctypes.c_void_p(256), ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                ctypes.c_void_p(256), None, 0, None)
+    assert rc == 4      # no workspace
+    # sequence shards: bad (world, rank), bad d, and a later shard without a carry
+    rc = lib.mom_route_shard_carry(ctypes.c_void_p(256), 4, 4, 1, 64, ctypes.c_void_p(256), ctypes.c_void_p(256),
+                                   None)
+    assert rc == 1
+    rc = lib.mom_route_shard_stats(ctypes.c_void_p(256), _lib.BF16, 1, 8, 12, ctypes.c_void_p(256), None)
+    assert rc == 1
+    rc = lib.mom_route_fwd_shard(None, _lib.BF16, 1, 4, 64, None, None, _lib.BF16, 32, 8, 2, None, 0, 128,
+                                 None, None, None, None, _lib.I64, None, None, None, None, 0, None)
+    assert rc == 1 and "carry_in" in _lib.last_error()
+    rc = lib.mom_route_fwd_shard(None, _lib.BF16, 1, 4, 64, None, None, _lib.BF16, 32, 8, 2, None, 0,
+                                 (1 << 24) - 2, ctypes.c_void_p(256), None, None, None, _lib.I64, None, None, None,
+                                 None, 0, None)
+    assert rc == 1 and "2^24" in _lib.last_error()
+
+
 def test_plan_size_grows_with_tokens(lib):
     a, b = lib.mom_plan_size(1024, 8, 2), lib.mom_plan_size(16384, 8, 2)
     assert 0 < a < b
