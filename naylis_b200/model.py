@@ -98,8 +98,11 @@ class MoMLayer(nn.Module):
         noise = None
         if self.training and self.noise_scale > 0:
             noise = mom_kernels.gumbel_noise((B, S, self.num_blocks), x.device, self.noise_scale)
-        return mom_kernels.mom_route(x, self.router_down.weight, self.router_up.weight,
-                                     self.top_blocks, noise, scan_mode=self.scan_mode)
+        # probs, top_idx, top_gates and log(max(top_gates, 1e-9)) from the router kernel:
+        # the read takes the log-gates (the gradient flows back into the router kernel
+        # without torch's clamp / log ops)
+        return mom_kernels.mom_route_log_gates(x, self.router_down.weight, self.router_up.weight,
+                                               self.top_blocks, noise, scan_mode=self.scan_mode)
 
     def forward(self, x, M_blocks):
         if self.use_kernel:
@@ -109,23 +112,25 @@ class MoMLayer(nn.Module):
         else:
             mode = None
         if mode is not None:
-            router_probs, top_idx, top_gates = self._route_kernel(x)
+            router_probs, top_idx, _, gate_in = self._route_kernel(x)
         else:
-            router_probs, top_idx, top_gates = self._route_eager(x)
+            router_probs, top_idx, gate_in = self._route_eager(x)
         if self.training:
             self.last_router_probs = router_probs.reshape(-1, self.num_blocks)
             self.last_top_idx = top_idx.reshape(-1, self.top_blocks)
         if self.mom_grad_ckpt and self.training and torch.is_grad_enabled():
             out = torch.utils.checkpoint.checkpoint(
-                self._read, x, top_idx, top_gates, M_blocks, mode,
+                self._read, x, top_idx, gate_in, M_blocks, mode,
                 use_reentrant=False, preserve_rng_state=False)
         else:
-            out = self._read(x, top_idx, top_gates, M_blocks, mode)
+            out = self._read(x, top_idx, gate_in, M_blocks, mode)
         if mode is not None and torch.result_type(self.mom_scale, out) == torch.float32:
             return mom_kernels.mom_scale(out, self.mom_scale)
         return self.mom_scale * out
 
-    def _read(self, x, top_idx, top_gates, M_blocks, mode=None):
+    def _read(self, x, top_idx, gate_in, M_blocks, mode=None):
+        """gate_in: the log-gates on the kernel path (mode set), the gates on the
+        reference's eager path."""
         B, S, D = x.shape
         q_sh = self.q_proj(x).view(B, S, self.n_heads, self.head_dim)
         L = self.mem_slots
@@ -133,11 +138,11 @@ class MoMLayer(nn.Module):
         k_shared = self.k_proj(slots)
         v_shared = self.v_proj(slots)
         if mode is not None:
-            out = mom_kernels.mom_read(q_sh, k_shared, v_shared, top_idx, top_gates,
-                                       num_blocks=self.num_blocks, block_size=self.block_size,
-                                       mode=mode)
+            out = mom_kernels.mom_read_log_gates(q_sh, k_shared, v_shared, top_idx, gate_in,
+                                                 num_blocks=self.num_blocks, block_size=self.block_size,
+                                                 mode=mode)
         else:
-            bias = _gate_bias_eager(top_idx, top_gates, self.num_blocks, self.block_size, q_sh.dtype)
+            bias = _gate_bias_eager(top_idx, gate_in, self.num_blocks, self.block_size, q_sh.dtype)
             q = q_sh.transpose(1, 2)
             k = k_shared.view(1, L, self.n_heads, self.head_dim).transpose(1, 2).expand(B, -1, -1, -1)
             v = v_shared.view(1, L, self.n_heads, self.head_dim).transpose(1, 2).expand(B, -1, -1, -1)

@@ -206,15 +206,7 @@ class _MomReadSplitFunction(torch.autograd.Function):
         return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
 
 
-def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: str = MODE):
-    """MoM memory read with the per-token gate bias (reference door:
-    mom_kernels/__init__.py:87-102; contract of mom_kernels/triton_gpu.py:412-439).
-
-    q_sh (B, S, H, hd) bf16; shared k, v (L, H*hd) bf16 with L = num_blocks *
-    block_size; top_idx (B, S, top) block ids; top_gates (B, S, top) fp32
-    softmax gates. Returns (B, S, H, hd). Gradients reach q, k, v and the
-    gates (through log(clamp_min(g, 1e-9)), as the reference bias does).
-    """
+def _check_read_args(q_sh, k, v, top_idx, top_gates, num_blocks, block_size, mode):
     if mode != MODE:
         raise RuntimeError(f"unknown kernel mode {mode!r} (this door serves {MODE!r})")
     if k.dim() != 2 or v.dim() != 2:
@@ -233,12 +225,37 @@ def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: st
         raise RuntimeError(f"sm100 mom_read: k/v must be (L, {H * hd}), got {tuple(k.shape)}, {tuple(v.shape)}")
     if top_idx.shape != top_gates.shape or top_idx.shape[:2] != (B, S):
         raise RuntimeError("sm100 mom_read: top_idx / top_gates must be (B, S, top)")
-    log_gates = top_gates.clamp_min(1e-9).log().float()
+
+
+def _read_apply(q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
+    B, S = q_sh.shape[:2]
     top = top_idx.shape[-1]
     # routing sets beyond what the set bucketing holds: the block-split read
     fn = _MomReadFunction if _lib.load().mom_plan_size(B * S, int(num_blocks), top) else _MomReadSplitFunction
     return fn.apply(q_sh.contiguous(), k.contiguous(), v.contiguous(), top_idx, log_gates, int(num_blocks),
                     int(block_size))
+
+
+def mom_read_log_gates(q_sh, k, v, top_idx, log_gates, *, num_blocks, block_size, mode: str = MODE):
+    """``mom_read`` taking log(max(gates, 1e-9)) directly (fp32, (B, S, top)),
+    e.g. the fourth output of ``mom_route_log_gates``; the gradient is returned
+    for log_gates. Not in the reference door (its mom_read takes the gates)."""
+    _check_read_args(q_sh, k, v, top_idx, log_gates, num_blocks, block_size, mode)
+    return _read_apply(q_sh, k, v, top_idx, log_gates.float(), num_blocks, block_size)
+
+
+def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: str = MODE):
+    """MoM memory read with the per-token gate bias (reference door:
+    mom_kernels/__init__.py:87-102; contract of mom_kernels/triton_gpu.py:412-439).
+
+    q_sh (B, S, H, hd) bf16; shared k, v (L, H*hd) bf16 with L = num_blocks *
+    block_size; top_idx (B, S, top) block ids; top_gates (B, S, top) fp32
+    softmax gates. Returns (B, S, H, hd). Gradients reach q, k, v and the
+    gates (through log(clamp_min(g, 1e-9)), as the reference bias does).
+    """
+    _check_read_args(q_sh, k, v, top_idx, top_gates, num_blocks, block_size, mode)
+    log_gates = top_gates.clamp_min(1e-9).log().float()
+    return _read_apply(q_sh, k, v, top_idx, log_gates, num_blocks, block_size)
 
 
 # ====================================================================== router
@@ -274,6 +291,7 @@ class _MomRouteFunction(torch.autograd.Function):
         probs = torch.empty((B, S, nb), dtype=torch.float32, device=dev)
         top_idx = torch.empty((B, S, top), dtype=torch.int64, device=dev)
         gates = torch.empty((B, S, top), dtype=torch.float32, device=dev)
+        log_gates = torch.empty((B, S, top), dtype=torch.float32, device=dev)
         act = torch.empty((B, S, r), dtype=compute_dtype, device=dev)
         cd = _dt_code(compute_dtype)
         ws = torch.empty(_lib.load().mom_route_workspace_size(B, S, d, r, nb, cd), dtype=torch.uint8, device=dev)
@@ -282,15 +300,15 @@ class _MomRouteFunction(torch.autograd.Function):
             nz = noise.to(torch.float32).contiguous()
         _lib.call("mom_route_fwd", x_c.data_ptr(), _dt_code(x.dtype), B, S, d, wd.data_ptr(),
                   wu.data_ptr(), cd, r, nb, top, _ptr(nz), _lib.SCAN_MODES[scan_mode],
-                  probs.data_ptr(), top_idx.data_ptr(), _lib.I64, gates.data_ptr(), None,
+                  probs.data_ptr(), top_idx.data_ptr(), _lib.I64, gates.data_ptr(), log_gates.data_ptr(),
                   act.data_ptr(), ws.data_ptr(), ws.numel(), st)
         ctx.save_for_backward(x_c, wd, wu, probs, top_idx, gates, act)
         ctx.meta = (top, cd, w_down.dtype, w_up.dtype)
         ctx.mark_non_differentiable(top_idx)
-        return probs, top_idx, gates
+        return probs, top_idx, gates, log_gates
 
     @staticmethod
-    def backward(ctx, dprobs, _didx, dgates):
+    def backward(ctx, dprobs, _didx, dgates, dlog_gates):
         x, wd, wu, probs, top_idx, gates, act = ctx.saved_tensors
         top, cd, wd_dtype, wu_dtype = ctx.meta
         B, S, d = x.shape
@@ -299,13 +317,14 @@ class _MomRouteFunction(torch.autograd.Function):
         st = _stream(dev)
         dp = None if dprobs is None else dprobs.to(torch.float32).contiguous()
         dg = None if dgates is None else dgates.to(torch.float32).contiguous()
+        dlg = None if dlog_gates is None else dlog_gates.to(torch.float32).contiguous()
         dx = torch.empty_like(x)
         dw_down = torch.empty((r, d), dtype=torch.float32, device=dev)
         dw_up = torch.empty((nb, r), dtype=torch.float32, device=dev)
         ws = torch.empty(_lib.load().mom_route_bwd_workspace_size(B, S, d, r, nb), dtype=torch.uint8, device=dev)
         _lib.call("mom_route_bwd", x.data_ptr(), _dt_code(x.dtype), B, S, d, wd.data_ptr(),
                   wu.data_ptr(), cd, r, nb, top, probs.data_ptr(), top_idx.data_ptr(), _lib.I64,
-                  gates.data_ptr(), act.data_ptr(), None, _ptr(dg), _ptr(dp), dx.data_ptr(),
+                  gates.data_ptr(), act.data_ptr(), _ptr(dlg), _ptr(dg), _ptr(dp), dx.data_ptr(),
                   _dt_code(x.dtype), 0, dw_down.data_ptr(), dw_up.data_ptr(), ws.data_ptr(),
                   ws.numel(), st)
         return dx, dw_down.to(wd_dtype), dw_up.to(wu_dtype), None, None, None, None
@@ -329,6 +348,24 @@ def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=Non
         raise RuntimeError(
             f"sm100 mom_route: shapes x {tuple(x.shape)}, w_down {tuple(w_down.shape)}, "
             f"w_up {tuple(w_up.shape)} disagree")
+    if scan_mode not in _lib.SCAN_MODES:
+        raise RuntimeError(f"sm100 mom_route: scan_mode must be one of {sorted(_lib.SCAN_MODES)}")
+    cd = compute_dtype or _compute_dtype(w_down)
+    probs, idx, gates, _ = _MomRouteFunction.apply(x, w_down, w_up, noise, int(top_blocks), cd, scan_mode)
+    return probs, idx, gates
+
+
+def mom_route_log_gates(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
+                        scan_mode: str = "fp64"):
+    """``mom_route`` that also returns log(max(top_gates, 1e-9)) as a fourth,
+    differentiable output, computed by the router kernel; its gradient goes
+    into the router backward directly (the kernel applies the clamp / log
+    derivative). For callers that feed the read with log-gates
+    (``mom_read_log_gates``), as the MoM layer does: the same values as the
+    reference's bias (mom_kernels/reference.py:14-29) without the torch
+    clamp / log ops and their backward."""
+    if not x.is_cuda:
+        raise RuntimeError("sm100 mom_route: x must be on a CUDA device")
     if scan_mode not in _lib.SCAN_MODES:
         raise RuntimeError(f"sm100 mom_route: scan_mode must be one of {sorted(_lib.SCAN_MODES)}")
     cd = compute_dtype or _compute_dtype(w_down)
