@@ -56,8 +56,13 @@ struct Fwd {
     static constexpr int kBoxes = HD / 64;
     static constexpr uint32_t kQBytes = kTM * HD * 2;
     static constexpr uint32_t kBlkBytes = kBS * HD * 2;     // one 128-slot block of K or V
-    static constexpr uint32_t kStageBytes = kQBytes + 2 * kMaxBlk * kBlkBytes;   // Q + K blocks + V blocks
-    static constexpr uint32_t kSmemBytes = 2 * kStageBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
+    // Q tiles in a ring of kQStages; the set's K and V blocks in kKvBufs buffers,
+    // loaded once per run of items with the same (set, head)
+    static constexpr int kQStages = 4;
+    static constexpr int kKvBufs = HD == 64 ? 2 : 1;
+    static constexpr uint32_t kKvBytes = 2 * kMaxBlk * kBlkBytes;   // K blocks + V blocks
+    static constexpr uint32_t kRingBytes = kQStages * kQBytes + kKvBufs * kKvBytes;
+    static constexpr uint32_t kSmemBytes = kRingBytes + kScratchBytes + 1024 /*barriers*/ + 1024 /*align*/;
     // V as the MN-major B operand of PV: N-atoms of 64 columns kBoxBytes apart
     // (head_dim 64 has one atom; its value is what the validated kernel used)
     static constexpr uint32_t kVLbo = HD == 64 ? 2 * kBlkBytes : kBoxBytes;
@@ -65,10 +70,13 @@ struct Fwd {
 };
 
 struct Bars {
-    uint64_t full[2], empty[2], s_full, p_full, pv_done, o_full, o_free, drain, s_issued;
+    uint64_t q_full[4], q_empty[4], kv_full[2], kv_empty[2], s_full, p_full, pv_done, o_full, o_free, drain,
+        s_issued;
     uint32_t tmem_base;
     int abort;
-    int meta[2];      // per stage: blocks loaded | (blocks of the set << 8); written before the stage's barrier
+    // per Q stage: blocks loaded | (blocks of the set << 8) | (new K/V load << 16);
+    // written before the stage's barrier
+    int meta[4];
 };
 static_assert(sizeof(Bars) <= 1024, "barrier block");
 }  // namespace
@@ -79,17 +87,18 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                    const __grid_constant__ CUtensorMap tmap_q, int H, int top, float scale_log2, PlanView P,
                    uint16_t *__restrict__ out, float *__restrict__ lse) {
     using C = Fwd<HD>;
-    constexpr int kHD = C::kHD;
-    constexpr uint32_t kQBytes = C::kQBytes, kBlkBytes = C::kBlkBytes, kStageBytes = C::kStageBytes;
+    constexpr int kHD = C::kHD, kQStages = C::kQStages, kKvBufs = C::kKvBufs;
+    constexpr uint32_t kQBytes = C::kQBytes, kBlkBytes = C::kBlkBytes, kKvBytes = C::kKvBytes;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char *sbase = smem_raw + (base - raw);
-    float *sMax = reinterpret_cast<float *>(sbase + 2 * kStageBytes);   // [4][128]
+    const uint32_t kvbase = base + kQStages * kQBytes;                 // [kKvBufs][K blocks | V blocks]
+    float *sMax = reinterpret_cast<float *>(sbase + C::kRingBytes);     // [4][128]
     float *sSum = sMax + 4 * kTM;                                        // [4][128]
     uint4 *sOut = reinterpret_cast<uint4 *>(sSum + 4 * kTM);            // [128 rows][8 x 16 B], swizzled
     int *sTok = reinterpret_cast<int *>(sOut + kTM * 8);                 // [128] tokens of the staged rows
-    Bars *bars = reinterpret_cast<Bars *>(sbase + 2 * kStageBytes + kScratchBytes);
+    Bars *bars = reinterpret_cast<Bars *>(sbase + C::kRingBytes + kScratchBytes);
     volatile int *abort_flag = &bars->abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -106,9 +115,14 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     const int64_t ld = static_cast<int64_t>(H) * kHD;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(&bars->full[s], 1);
-            tc::mbar_init(&bars->empty[s], 2);    // both MMA warps read the stage
+        for (int s = 0; s < kQStages; ++s) {
+            tc::mbar_init(&bars->q_full[s], 1);
+            tc::mbar_init(&bars->q_empty[s], 2);    // both MMA warps release a stage (meta is read by both)
+        }
+        for (int b = 0; b < kKvBufs; ++b) {
+            tc::mbar_init(&bars->kv_full[b], 1);
+            // the warps whose MMAs read K/V: warp 1 (S, PV of block 0), warp 2 (PV of block 1)
+            tc::mbar_init(&bars->kv_empty[b], C::kMaxBlk > 1 ? 2 : 1);
         }
         tc::mbar_init(&bars->o_full, 2);
         tc::mbar_init(&bars->o_free, kSoftThreads);
@@ -135,65 +149,94 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
 
     if (warp == 0) {
         // ------------------------------------------------------------ loader
+        // Per item: its Q tile into the next ring stage, with the stage's meta; when
+        // the (set, head) changes, then the set's K/V blocks into the next K/V buffer
+        // once the MMAs that read that buffer's previous load are done (kv_empty).
+        // Q and meta go first: the MMA warps release a K/V buffer when they meet the
+        // item that starts the next load.
         tc::LaneTile lt;
-        int issued = 0;
-        int stage_kv[2] = {-1, -1};   // (set, head) whose K/V blocks each stage holds
+        int issued = 0, nkv = 0, cur_kv = -1;
         for (int i = 0; i < nmine; ++i) {
             const int item = it0 + i;
-            const int s = i & 1, j = i >> 1, src = i & 31;
+            const int s = i % kQStages, j = i / kQStages, src = i & 31;
             if (src == 0 && i + lane < nmine) lt.fetch(P, item_tile(item + lane), top);
             const int x0 = tc::get(lt.x, src);
             const int nblk = tc::get(lt.nblk, src), b0 = tc::get(lt.b0, src), b1 = tc::get(lt.b1, src);
-            if (!tc::mbar_wait_warp(&bars->empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->q_empty[s], (j & 1) ^ 1, P.err, 2, abort_flag)) break;
             const int h = item_head(item);
             const int nload = nblk > 0 ? nblk : 1;
-            const uint32_t sQ = base + s * kStageBytes;
-            const uint32_t sK = sQ + kQBytes;
-            const uint32_t sV = sK + C::kMaxBlk * kBlkBytes;
-            // the stage's K/V are still those of this set and head (item i-2): keep them
+            const uint32_t sQ = base + s * kQBytes;
             const int kv = tc::get(lt.key, src) * H + h;
-            const bool reload = kv != stage_kv[s];
-            stage_kv[s] = kv;
+            const bool reload = kv != cur_kv;
+            cur_kv = kv;
             if (lane == 0) {
-                bars->meta[s] = nload | (nblk << 8);   // released by the arrive below
-                tc::mbar_arrive_expect_tx(&bars->full[s], kQBytes + (reload ? 2 * nload * kBlkBytes : 0));
+                bars->meta[s] = nload | (nblk << 8) | (reload ? 1 << 16 : 0);   // released by the arrive below
+                tc::mbar_arrive_expect_tx(&bars->q_full[s], kQBytes);
                 // the tile's rows x0 .. x0+127 (rows past the tile are never stored)
 #pragma unroll
                 for (int c = 0; c < C::kBoxes; ++c)
-                    tc::tma_load_2d(sQ + c * kBoxBytes, &tmap_q, h * kHD + 64 * c, x0, &bars->full[s]);
-                for (int jb = 0; reload && jb < nload; ++jb) {
-                    const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
-#pragma unroll
-                    for (int c = 0; c < C::kBoxes; ++c) {
-                        tc::tma_load_2d(sK + jb * kBlkBytes + c * kBoxBytes, &tmap_k, h * kHD + 64 * c, blk * kBS,
-                                        &bars->full[s]);
-                        tc::tma_load_2d(sV + jb * kBlkBytes + c * kBoxBytes, &tmap_v, h * kHD + 64 * c, blk * kBS,
-                                        &bars->full[s]);
-                    }
-                }
+                    tc::tma_load_2d(sQ + c * kBoxBytes, &tmap_q, h * kHD + 64 * c, x0, &bars->q_full[s]);
             }
             __syncwarp();
             issued = i + 1;
+            if (reload) {
+                const int b = nkv % kKvBufs, u = nkv / kKvBufs;
+                if (u > 0 && !tc::mbar_wait_warp(&bars->kv_empty[b], (u - 1) & 1, P.err, 2, abort_flag)) break;
+                const uint32_t sK = kvbase + b * kKvBytes, sV = sK + C::kMaxBlk * kBlkBytes;
+                if (lane == 0) {
+                    tc::mbar_arrive_expect_tx(&bars->kv_full[b], 2 * nload * kBlkBytes);
+                    for (int jb = 0; jb < nload; ++jb) {
+                        const int blk = nblk > 0 ? (jb == 0 ? b0 : b1) : 0;
+#pragma unroll
+                        for (int c = 0; c < C::kBoxes; ++c) {
+                            tc::tma_load_2d(sK + jb * kBlkBytes + c * kBoxBytes, &tmap_k, h * kHD + 64 * c,
+                                            blk * kBS, &bars->kv_full[b]);
+                            tc::tma_load_2d(sV + jb * kBlkBytes + c * kBoxBytes, &tmap_v, h * kHD + 64 * c,
+                                            blk * kBS, &bars->kv_full[b]);
+                        }
+                    }
+                }
+                __syncwarp();
+                ++nkv;
+            }
         }
         // make sure no TMA write is still in flight when the CTA retires
         if (issued > 0) {
             const int i = issued - 1;
-            tc::mbar_wait_warp(&bars->full[i & 1], (i >> 1) & 1, P.err, 2, abort_flag);
+            tc::mbar_wait_warp(&bars->q_full[i % kQStages], (i / kQStages) & 1, P.err, 2, abort_flag);
         }
+        if (nkv > 0)
+            tc::mbar_wait_warp(&bars->kv_full[(nkv - 1) % kKvBufs], ((nkv - 1) / kKvBufs) & 1, P.err, 2, abort_flag);
     } else if (warp == 1 || warp == 2) {
         // ------------------------------------------------------------ MMA issuers
         // Warp 1 issues S(i+1) as soon as the softmax has read S(i) (p_full of i),
         // ahead of its half of PV(i); warp 2 issues the other half only after that
         // (s_issued), so S(i+1) runs first on the tensor pipe and the softmax of i+1
-        // starts while PV(i) still runs.
+        // starts while PV(i) still runs. K/V loads: each warp counts the loads it has
+        // switched to (nkv); load n sits in buffer n % kKvBufs. A warp releases a
+        // buffer (kv_empty) after its last MMA that reads it. With one buffer, the
+        // item that starts a new load has its S issued after PV of the item before
+        // (both read the buffer), so warp 1 then issues PV(i) first.
         const bool wa = warp == 1;
         const uint32_t idesc_o = tc::idesc_bf16_f32(kTM, kHD, false, true);
-        auto issue_s = [&](int i) -> bool {   // warp 1: S(i) = Q K^T into TMEM columns 0..255
-            const int s = i & 1, j = i >> 1;
-            if (!tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) return false;
-            const int nload = tc::ld_shared_volatile(&bars->meta[s]) & 0xFF;
-            const uint32_t sQ = base + s * kStageBytes;
-            const uint32_t sK = sQ + kQBytes;
+        int nkv = 0;
+        // wait for item i's Q stage; its meta
+        auto stage_meta = [&](int i, int &meta) -> bool {
+            if (!tc::mbar_wait_warp(&bars->q_full[i % kQStages], (i / kQStages) & 1, P.err, 2, abort_flag))
+                return false;
+            meta = tc::ld_shared_volatile(&bars->meta[i % kQStages]);
+            return true;
+        };
+        // the next K/V load has landed (this warp's nkv-th switch)
+        auto kv_switch = [&]() -> bool {
+            const int n = nkv++;
+            return tc::mbar_wait_warp(&bars->kv_full[n % kKvBufs], (n / kKvBufs) & 1, P.err, 2, abort_flag);
+        };
+        // warp 1: S(i) = Q K^T into TMEM columns 0..255, K from buffer kb
+        auto issue_s = [&](int i, int meta, int kb) {
+            const int nload = meta & 0xFF;
+            const uint32_t sQ = base + (i % kQStages) * kQBytes;
+            const uint32_t sK = kvbase + kb * kKvBytes;
             tc::tc_fence_after();
             if (lane == 0) {
                 const uint32_t idesc_s = tc::idesc_bf16_f32(kTM, nload * kBS, false, false);
@@ -208,30 +251,13 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                 tc::mma_commit(&bars->s_full);
             }
             __syncwarp();
-            return true;
         };
-        bool ok = nmine > 0 && (!wa || issue_s(0));
-        for (int i = 0; ok && i < nmine; ++i) {
-            const int s = i & 1, j = i >> 1;
-            // warp 2 has not waited for the stage yet; warp 1 did so before issuing S(i)
-            if (!wa && !tc::mbar_wait_warp(&bars->full[s], j & 1, P.err, 2, abort_flag)) break;
-            const int nblk = tc::ld_shared_volatile(&bars->meta[s]) >> 8;
-            const uint32_t sV = base + s * kStageBytes + kQBytes + C::kMaxBlk * kBlkBytes;
-            // P(i) written to TMEM (and S(i) read) by the softmax
-            if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
-            if (wa) {
-                if (i + 1 < nmine && !issue_s(i + 1)) break;
-                // S(i+1) is in the tensor pipe ahead of both PV halves of i
-                if (lane == 0) tc::mbar_arrive(&bars->s_issued);
-                __syncwarp();
-            } else if (!tc::mbar_wait_warp(&bars->s_issued, i & 1, P.err, 2, abort_flag)) {
-                break;
-            }
-            // O read by the epilogue of i-1
-            if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
+        // PV of item i's block (warp 1: block 0, warp 2: block 1), V from buffer kb
+        auto issue_pv = [&](int i, int nblk, int kb) {
             tc::tc_fence_after();
             if (lane == 0) {
                 if (nblk > (wa ? 0 : 1) && (wa || C::kMaxBlk > 1)) {
+                    const uint32_t sV = kvbase + kb * kKvBytes + C::kMaxBlk * kBlkBytes;
                     const uint64_t bv = tc::smem_desc_sw128(sV + (wa ? 0 : kBlkBytes), C::kVLbo, 1024);
 #pragma unroll
                     for (int k8 = 0; k8 < 8; ++k8) {   // the block's 128 slots, 16 per step
@@ -241,10 +267,68 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
                     }
                 }
                 tc::mma_commit(&bars->o_full);
-                tc::mma_commit(&bars->empty[s]);
+                tc::mma_commit(&bars->q_empty[i % kQStages]);
                 tc::mma_commit(&bars->pv_done);
             }
             __syncwarp();
+        };
+        auto release = [&](int kb) {
+            if (lane == 0) tc::mma_commit(&bars->kv_empty[kb]);
+            __syncwarp();
+        };
+        if (wa) {
+            int meta_next = 0, kb_next = 0;
+            bool ok = nmine > 0 && stage_meta(0, meta_next) && kv_switch();
+            if (ok) {
+                kb_next = (nkv - 1) % kKvBufs;
+                issue_s(0, meta_next, kb_next);
+            }
+            for (int i = 0; ok && i < nmine; ++i) {
+                const int meta_i = meta_next, kb_i = kb_next;
+                // P(i) written to TMEM (and S(i) read) by the softmax
+                if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
+                const bool next = i + 1 < nmine;
+                if (next && !stage_meta(i + 1, meta_next)) break;
+                const bool sw = next && ((meta_next >> 16) & 1);
+                const bool pv_first = sw && kKvBufs == 1;
+                if (next && !pv_first) {
+                    if (sw && !kv_switch()) break;
+                    kb_next = (nkv - 1) % kKvBufs;
+                    issue_s(i + 1, meta_next, kb_next);
+                }
+                if (!pv_first) {
+                    // S(i+1) is in the tensor pipe ahead of both PV halves of i
+                    if (lane == 0) tc::mbar_arrive(&bars->s_issued);
+                    __syncwarp();
+                }
+                // O read by the epilogue of i-1
+                if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
+                issue_pv(i, (meta_i >> 8) & 0xFF, kb_i);
+                if (sw) release(kb_i);   // this warp's last MMA on item i's K/V load
+                if (pv_first) {
+                    if (!kv_switch()) break;
+                    kb_next = (nkv - 1) % kKvBufs;
+                    issue_s(i + 1, meta_next, kb_next);
+                    if (lane == 0) tc::mbar_arrive(&bars->s_issued);
+                    __syncwarp();
+                }
+            }
+        } else {
+            int kb = 0;
+            for (int i = 0; i < nmine; ++i) {
+                int meta = 0;
+                if (!stage_meta(i, meta)) break;
+                if (C::kMaxBlk > 1 && ((meta >> 16) & 1)) {
+                    // a new K/V load: PV(i-1), this warp's last read of the previous one, is issued
+                    if (i > 0) release(kb);
+                    if (!kv_switch()) break;
+                    kb = (nkv - 1) % kKvBufs;
+                }
+                if (!tc::mbar_wait_warp(&bars->p_full, i & 1, P.err, 2, abort_flag)) break;
+                if (!tc::mbar_wait_warp(&bars->s_issued, i & 1, P.err, 2, abort_flag)) break;
+                if (i > 0 && !tc::mbar_wait_warp(&bars->o_free, (i - 1) & 1, P.err, 2, abort_flag)) break;
+                issue_pv(i, (meta >> 8) & 0xFF, kb);
+            }
         }
         // drain: every MMA this thread issued has completed before TMEM is freed
         if (lane == 0) tc::mma_commit(&bars->drain);
