@@ -31,19 +31,23 @@ __device__ __forceinline__ int64_t load_idx(const void *idx, int idx64, int64_t 
     return idx64 ? static_cast<const int64_t *>(idx)[i] : static_cast<const int32_t *>(idx)[i];
 }
 
-// bit k set: slot k repeats a block chosen at an earlier slot of the same token
-__device__ __forceinline__ uint32_t dead_mask(const void *idx, int idx64, int64_t t, int top, int *first) {
-    int64_t b[kMaxTop];
+// bit k set: slot k repeats a block chosen at an earlier slot of the same token;
+// first[k] = the earliest slot with slot k's block. Unrolled over TOPM >= top so
+// that the arrays stay in registers.
+template <int TOPM>
+__device__ __forceinline__ uint32_t dead_mask(const void *idx, int idx64, int64_t t, int top, int (&first)[TOPM]) {
+    int64_t b[TOPM];
+#pragma unroll
+    for (int k = 0; k < TOPM; ++k) b[k] = k < top ? load_idx(idx, idx64, t * top + k) : 0;
     uint32_t m = 0;
-    for (int k = 0; k < top; ++k) {
-        b[k] = load_idx(idx, idx64, t * top + k);
-        first[k] = k;
-        for (int j = 0; j < k; ++j)
-            if (b[j] == b[k]) {
-                first[k] = j;
-                m |= 1u << k;
-                break;
-            }
+#pragma unroll
+    for (int k = 0; k < TOPM; ++k) {
+        int f = k;
+#pragma unroll
+        for (int j = k - 1; j >= 0; --j)
+            if (b[j] == b[k]) f = j;
+        first[k] = f;
+        if (k < top && f != k) m |= 1u << k;
     }
     return m;
 }
@@ -57,7 +61,7 @@ split_prep_kernel(const void *__restrict__ idx, int idx64, const float *__restri
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < N;
          t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
         int first[kMaxTop];
-        const uint32_t dead = dead_mask(idx, idx64, t, top, first);
+        const uint32_t dead = dead_mask<kMaxTop>(idx, idx64, t, top, first);
         for (int k = 0; k < top; ++k) {
             float s = lg[t * top + k];
             if (!((dead >> k) & 1))
@@ -80,7 +84,10 @@ split_lse_scatter_kernel(const float *__restrict__ lse_rows, const int *__restri
 }
 
 // Warp per token. w holds the rows' lse on entry and the weights a_k on exit
-// (each (token, head) entry read and rewritten by the same lane).
+// (each (token, head) entry read and rewritten by the same lane). TOPM >= top is
+// the unroll bound; each lane combines two 16-B vectors per step with all rows'
+// loads in flight first.
+template <int TOPM>
 __global__ void __launch_bounds__(256)
 split_combine_kernel(const uint4 *__restrict__ out_rows, const void *__restrict__ idx, int idx64, int64_t N,
                      int top, int H, int hd, float *__restrict__ w, uint4 *__restrict__ out) {
@@ -88,44 +95,61 @@ split_combine_kernel(const uint4 *__restrict__ out_rows, const void *__restrict_
     const int vph = hd / 8, vpr = H * vph;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
-        int first[kMaxTop];
-        const uint32_t dead = dead_mask(idx, idx64, t, top, first);
+        int first[TOPM];
+        const uint32_t dead = dead_mask<TOPM>(idx, idx64, t, top, first);
         float *wt = w + t * top * H;
         for (int h = lane; h < H; h += 32) {
+            float lv[TOPM];
             float m = -INFINITY;
-            for (int k = 0; k < top; ++k)
-                if (!((dead >> k) & 1)) m = fmaxf(m, wt[k * H + h]);
-            float e[kMaxTop], s = 0.0f;
-            for (int k = 0; k < top; ++k) {
-                e[k] = (((dead >> k) & 1) || m == -INFINITY) ? 0.0f : expf(wt[k * H + h] - m);
-                s += e[k];
+#pragma unroll
+            for (int k = 0; k < TOPM; ++k) {
+                const bool live = k < top && !((dead >> k) & 1);
+                lv[k] = k < top ? wt[k * H + h] : -INFINITY;
+                if (live) m = fmaxf(m, lv[k]);
             }
-            const float inv = s > 0.0f ? 1.0f / s : 0.0f;
-            for (int k = 0; k < top; ++k) wt[k * H + h] = e[k] * inv;
+            float e[TOPM], sum = 0.0f;
+#pragma unroll
+            for (int k = 0; k < TOPM; ++k) {
+                const bool live = k < top && !((dead >> k) & 1);
+                e[k] = (live && m != -INFINITY) ? expf(lv[k] - m) : 0.0f;
+                sum += e[k];
+            }
+            const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+#pragma unroll
+            for (int k = 0; k < TOPM; ++k)
+                if (k < top) wt[k * H + h] = e[k] * inv;
         }
         __syncwarp();
-        for (int v = lane; v < vpr; v += 32) {
-            const int h = v / vph;
-            // all rows' vectors in flight before any is used
-            float a[kMaxTop];
-            uint4 x[kMaxTop];
+        for (int v0 = lane; v0 < vpr; v0 += 64) {
+            float a[2][TOPM];
+            uint4 x[2][TOPM];
 #pragma unroll
-            for (int k = 0; k < kMaxTop; ++k) {
-                a[k] = k < top ? wt[k * H + h] : 0.0f;
-                x[k] = a[k] != 0.0f ? out_rows[(t * top + k) * vpr + v] : make_uint4(0u, 0u, 0u, 0u);
-            }
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int u = 0; u < 2; ++u) {
+                const int v = v0 + 32 * u;
+                const int h = (v < vpr ? v : v0) / vph;
 #pragma unroll
-            for (int k = 0; k < kMaxTop; ++k) {
-                const uint32_t xw[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc[2 * q] = fmaf(a[k], bf_lo(xw[q]), acc[2 * q]);
-                    acc[2 * q + 1] = fmaf(a[k], bf_hi(xw[q]), acc[2 * q + 1]);
+                for (int k = 0; k < TOPM; ++k) {
+                    a[u][k] = (k < top && v < vpr) ? wt[k * H + h] : 0.0f;
+                    x[u][k] = a[u][k] != 0.0f ? out_rows[(t * top + k) * vpr + v] : make_uint4(0u, 0u, 0u, 0u);
                 }
             }
-            out[t * vpr + v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
-                                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int v = v0 + 32 * u;
+                if (v >= vpr) break;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int k = 0; k < TOPM; ++k) {
+                    const uint32_t xw[4] = {x[u][k].x, x[u][k].y, x[u][k].z, x[u][k].w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        acc[2 * q] = fmaf(a[u][k], bf_lo(xw[q]), acc[2 * q]);
+                        acc[2 * q + 1] = fmaf(a[u][k], bf_hi(xw[q]), acc[2 * q + 1]);
+                    }
+                }
+                out[t * vpr + v] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]),
+                                              pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
+            }
         }
         __syncwarp();
     }
@@ -155,6 +179,7 @@ split_gate_do_kernel(const uint4 *__restrict__ dout, const float *__restrict__ w
 
 // Warp per token: dq[t] = sum_k dq_rows[t*top + k] (fp32 sum, bf16 out); the
 // dead slots' gate gradient copied from their first occurrence.
+template <int TOPM>
 __global__ void __launch_bounds__(256)
 split_dq_sum_kernel(const uint4 *__restrict__ dq_rows, const void *__restrict__ idx, int idx64, int64_t N, int top,
                     int vpr, uint4 *__restrict__ dq, float *__restrict__ dlog_gates) {
@@ -162,13 +187,13 @@ split_dq_sum_kernel(const uint4 *__restrict__ dq_rows, const void *__restrict__ 
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
         for (int v = lane; v < vpr; v += 32) {
-            uint4 x[kMaxTop];
+            uint4 x[TOPM];
 #pragma unroll
-            for (int k = 0; k < kMaxTop; ++k)
+            for (int k = 0; k < TOPM; ++k)
                 x[k] = k < top ? dq_rows[(t * top + k) * vpr + v] : make_uint4(0u, 0u, 0u, 0u);
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int k = 0; k < kMaxTop; ++k) {
+            for (int k = 0; k < TOPM; ++k) {
                 const uint32_t xw[4] = {x[k].x, x[k].y, x[k].z, x[k].w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -180,9 +205,10 @@ split_dq_sum_kernel(const uint4 *__restrict__ dq_rows, const void *__restrict__ 
                                          pack_bf16x2(acc[4], acc[5]), pack_bf16x2(acc[6], acc[7]));
         }
         if (lane == 0) {
-            int first[kMaxTop];
-            const uint32_t dead = dead_mask(idx, idx64, t, top, first);
-            for (int k = 0; k < top; ++k)
+            int first[TOPM];
+            const uint32_t dead = dead_mask<TOPM>(idx, idx64, t, top, first);
+#pragma unroll
+            for (int k = 0; k < TOPM; ++k)
                 if ((dead >> k) & 1) dlog_gates[t * top + k] = dlog_gates[t * top + first[k]];
         }
     }
@@ -220,6 +246,7 @@ split_permute_q_kernel(const uint4 *__restrict__ q, const int *__restrict__ iper
 // (zero where w_k = 0) and delta[h][iperm[p]] = <that row, O[t]> per head (fp32
 // sums of the bf16 products, as rows.cu's row_delta_kernel forms them). dO[t] and
 // O[t] are read once per token instead of once per row.
+template <int TOPM>
 __global__ void __launch_bounds__(256)
 split_row_delta_kernel(const uint4 *__restrict__ dout, const uint4 *__restrict__ out,
                        const float *__restrict__ w, const int *__restrict__ iperm, int64_t N, int top, int H,
@@ -229,36 +256,47 @@ split_row_delta_kernel(const uint4 *__restrict__ dout, const uint4 *__restrict__
     const int64_t M = N * top;
     const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < N; t += nwarps) {
-        int64_t row[kMaxTop];
+        int row[TOPM];
 #pragma unroll
-        for (int k = 0; k < kMaxTop; ++k) row[k] = k < top ? iperm[t * top + k] : 0;
-        for (int v0 = 0; v0 < vpr; v0 += 32) {
-            const int v = v0 + lane;
-            const bool in = v < vpr;
-            const int h = in ? v / vph : 0;
-            uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a;
-            if (in) {
-                a = dout[t * vpr + v];
-                b = out[t * vpr + v];
-            }
-            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+        for (int k = 0; k < TOPM; ++k) row[k] = k < top ? iperm[t * top + k] : 0;
+        // two 16-B vectors per lane and step (v0 and v0 + 32), both loaded first
+        for (int v0 = 0; v0 < vpr; v0 += 64) {
+            uint4 a[2], b[2];
 #pragma unroll
-            for (int k = 0; k < kMaxTop; ++k) {
-                if (k >= top) break;
-                const float wk = in ? w[(t * top + k) * H + h] : 0.0f;
-                uint32_t g[4] = {0u, 0u, 0u, 0u};
-                float acc = 0.0f;
-                if (wk != 0.0f) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        g[q] = pack_bf16x2(wk * bf_lo(aw[q]), wk * bf_hi(aw[q]));
-                        acc = fmaf(bf_lo(g[q]), bf_lo(bw[q]), acc);
-                        acc = fmaf(bf_hi(g[q]), bf_hi(bw[q]), acc);
-                    }
+            for (int u = 0; u < 2; ++u) {
+                const int v = v0 + 32 * u + lane;
+                a[u] = make_uint4(0u, 0u, 0u, 0u);
+                b[u] = a[u];
+                if (v < vpr) {
+                    a[u] = dout[t * vpr + v];
+                    b[u] = out[t * vpr + v];
                 }
-                if (in) do_rows[row[k] * vpr + v] = make_uint4(g[0], g[1], g[2], g[3]);
-                for (int o = 1; o < vph; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                if (in && (v % vph) == 0) delta[static_cast<int64_t>(h) * M + row[k]] = acc;
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                if (v0 + 32 * u >= vpr) break;   // warp-uniform
+                const int v = v0 + 32 * u + lane;
+                const bool in = v < vpr;
+                const int h = in ? v / vph : 0;
+                const uint32_t aw[4] = {a[u].x, a[u].y, a[u].z, a[u].w}, bw[4] = {b[u].x, b[u].y, b[u].z, b[u].w};
+#pragma unroll
+                for (int k = 0; k < TOPM; ++k) {
+                    if (k >= top) break;
+                    const float wk = in ? w[(t * top + k) * H + h] : 0.0f;
+                    uint32_t g[4] = {0u, 0u, 0u, 0u};
+                    float acc = 0.0f;
+                    if (wk != 0.0f) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            g[q] = pack_bf16x2(wk * bf_lo(aw[q]), wk * bf_hi(aw[q]));
+                            acc = fmaf(bf_lo(g[q]), bf_lo(bw[q]), acc);
+                            acc = fmaf(bf_hi(g[q]), bf_hi(bw[q]), acc);
+                        }
+                    }
+                    if (in) do_rows[static_cast<int64_t>(row[k]) * vpr + v] = make_uint4(g[0], g[1], g[2], g[3]);
+                    for (int o = 1; o < vph; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (in && (v % vph) == 0) delta[static_cast<int64_t>(h) * M + row[k]] = acc;
+                }
             }
         }
     }
@@ -292,8 +330,9 @@ cudaError_t launch_split_combine(const void *out_rows, const float *lse_rows, co
     count_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    split_combine_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(out_rows), top_idx, idx64, N,
-                                                         top, H, hd, weights, static_cast<uint4 *>(out));
+    auto kern = top <= 4 ? split_combine_kernel<4> : split_combine_kernel<kMaxTop>;
+    kern<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(out_rows), top_idx, idx64, N, top, H, hd, weights,
+                                         static_cast<uint4 *>(out));
     count_launch();
     return cudaGetLastError();
 }
@@ -323,9 +362,9 @@ cudaError_t launch_split_row_delta(const void *dout, const void *out, const floa
     if (top < 1 || top > kMaxTop || hd % 8 || (32 % (hd / 8)) || !aligned16(dout) || !aligned16(out) ||
         !aligned16(do_rows))
         return cudaErrorInvalidValue;
-    split_row_delta_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(dout),
-                                                           static_cast<const uint4 *>(out), weights, iperm, N, top,
-                                                           H, hd, static_cast<uint4 *>(do_rows), delta);
+    auto kern = top <= 4 ? split_row_delta_kernel<4> : split_row_delta_kernel<kMaxTop>;
+    kern<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(dout), static_cast<const uint4 *>(out), weights,
+                                         iperm, N, top, H, hd, static_cast<uint4 *>(do_rows), delta);
     count_launch();
     return cudaGetLastError();
 }
@@ -345,8 +384,9 @@ cudaError_t launch_split_dq_sum(const void *dq_rows, const void *top_idx, int id
                                 int hd, void *dq, float *dlog_gates, cudaStream_t st) {
     if (N == 0) return cudaSuccess;
     if (top < 1 || top > kMaxTop || hd % 8 || !aligned16(dq_rows) || !aligned16(dq)) return cudaErrorInvalidValue;
-    split_dq_sum_kernel<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(dq_rows), top_idx, idx64, N, top,
-                                                        H * hd / 8, static_cast<uint4 *>(dq), dlog_gates);
+    auto kern = top <= 4 ? split_dq_sum_kernel<4> : split_dq_sum_kernel<kMaxTop>;
+    kern<<<grid_for(N, 8), 256, 0, st>>>(static_cast<const uint4 *>(dq_rows), top_idx, idx64, N, top, H * hd / 8,
+                                         static_cast<uint4 *>(dq), dlog_gates);
     count_launch();
     return cudaGetLastError();
 }
