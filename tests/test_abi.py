@@ -156,6 +156,14 @@ def test_door_fails_loud_off_gpu():
                     num_blocks=4, block_size=64)
     with pytest.raises(RuntimeError):
         mk.mom_route(torch.zeros(1, 4, 64), torch.zeros(8, 64), torch.zeros(4, 8), 2)
+    # the log-gate variants fail the same way off the GPU
+    with pytest.raises(RuntimeError):
+        mk.mom_read_log_gates(q, k, k, torch.zeros(1, 4, 2, dtype=torch.int64), torch.zeros(1, 4, 2),
+                              num_blocks=4, block_size=64)
+    with pytest.raises(RuntimeError):
+        mk.mom_route_log_gates(torch.zeros(1, 4, 64), torch.zeros(8, 64), torch.zeros(4, 8), 2)
+    with pytest.raises(RuntimeError):
+        mk.mom_route_log_gates(torch.zeros(1, 4, 64), torch.zeros(8, 64), torch.zeros(4, 8), 2, scan_mode="fp16")
 
 
 def test_layer_eager_path_matches_reference_semantics():
