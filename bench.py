@@ -527,20 +527,20 @@ def run_reference(args):
     }), flush=True)
 
 
-# ------------------------------------------------------------------ config-3 read
-CFG3 = dict(B=4, S=4096, H=16, hd=128, nb=32, bs=128, top=4)
-METRIC3 = "MoM read fwd+bwd tokens/s, BASELINE config 3 geometry (top-4 of 32 blocks, 16x128 heads)"
+# ------------------------------------------------------------------ config-4 read
+CFG4 = dict(B=4, S=4096, H=16, hd=128, nb=32, bs=128, top=4)
+METRIC4 = "MoM read fwd+bwd tokens/s, BASELINE config 4 geometry (top-4 of 32 blocks, 16x128 heads)"
 
 
 def run_read_top4of32(args):
-    """The read alone on BASELINE config 3's geometry (x [4, 4096], 16 heads of
+    """The read alone on BASELINE config 4's geometry (configs[3]: x [4, 4096], 16 heads of
     128, bank 32 x 128 slots, top-4): 35,960 block sets, so the door takes the
     block-split read. One step = mom_read forward + backward through the door
     on resident inputs, L2 flushed before each timed step."""
     import torch
     from naylis_b200 import _lib
     from naylis_b200 import mom_kernels as mk
-    c = CFG3
+    c = CFG4
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(1234)
@@ -586,11 +586,11 @@ def run_read_top4of32(args):
     pk = peaks()
     tflops = flops / (ms / 1e3) / 1e12
     print(json.dumps({
-        "metric": METRIC3, "value": round(N / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
+        "metric": METRIC4, "value": round(N / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) q/k/v scaled 0.7/0.4/0.4, random distinct top-4 blocks, softmax gates)",
-        "config": {"workload": "cfg3-read: mom_read fwd+bwd, B=4 S=4096, 16x128 heads, bank 32x128 slots, top-4 "
+        "config": {"workload": "cfg4-read: mom_read fwd+bwd, B=4 S=4096, 16x128 heads, bank 32x128 slots, top-4 "
                                "(block-split read)", "l2": "flushed between timed steps (256 MiB write, untimed)"},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": pk["bf16"], "unit": "TFLOP/s",
                      "frac": round(tflops / pk["bf16"], 4), "traffic": None,
@@ -613,7 +613,7 @@ def main():
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
     ap.add_argument("--workload", default="cfg2", choices=["cfg2", "read-top4of32"],
-                    help="cfg2: the headline layer step; read-top4of32: the read alone on config 3's geometry")
+                    help="cfg2: the headline layer step; read-top4of32: the read alone on config 4's geometry")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
