@@ -157,3 +157,21 @@ def test_sharded_router_exchange_equals_whole_sequence(scan_mode, extreme):
     # in a chain every rank but the last hands its end state on
     chain = extreme or scan_mode == "fp32"
     assert [res[r]["chained"] for r in range(world)] == [chain] * (world - 1) + [False]
+
+
+def test_sharded_router_rejects_bad_calls_before_any_exchange():
+    """Argument errors are raised on the host before any collective runs (a
+    single gloo rank, so nothing could hang on a missing peer)."""
+    import torch.distributed as dist
+    from naylis_b200.sequence_parallel import route_sequence_sharded
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("gloo", rank=0, world_size=1, timeout=datetime.timedelta(seconds=30))
+    try:
+        x = torch.zeros(1, 4, 16)
+        with pytest.raises(RuntimeError, match="scan_mode"):
+            route_sequence_sharded(x, torch.zeros(4, 16), torch.zeros(6, 4), 2, scan_mode="fp16")
+        with pytest.raises(RuntimeError, match="CUDA"):
+            route_sequence_sharded(x, torch.zeros(4, 16), torch.zeros(6, 4), 2)
+    finally:
+        dist.destroy_process_group()
