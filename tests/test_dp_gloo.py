@@ -98,7 +98,9 @@ def _worker(rank, world, port, q, mode):
                 dp.zero_grad()
             _loss(holder, shard).backward()
             dp.finish()
-        grads = {n: p.grad.clone() for n, p in holder.named_parameters()}
+        # numpy copies travel by value; torch tensors would be shared through file
+        # descriptors that vanish when this process exits before the parent reads them
+        grads = {n: p.grad.detach().numpy().copy() for n, p in holder.named_parameters()}
         q.put((rank, {"grads": grads, "nbuckets": len(dp.buckets)}))
         dist.barrier()
         dist.destroy_process_group()
@@ -139,11 +141,11 @@ def test_grad_allreduce_equals_full_batch_gradient(mode):
     for n, p in holder.named_parameters():
         ref = p.grad if p.grad is not None else torch.zeros_like(p)
         for r in range(world):
-            got = res[r]["grads"][n]
+            got = torch.from_numpy(res[r]["grads"][n])
             assert torch.allclose(got, ref, rtol=1e-4, atol=1e-6), (n, (got - ref).abs().max())
     # the shared bank gets its gradient once, summed over all uses, then averaged
-    assert float(res[0]["grads"]["M"].abs().sum()) > 0
-    assert torch.equal(res[0]["grads"]["unused"], torch.zeros(3))
+    assert float(abs(res[0]["grads"]["M"]).sum()) > 0
+    assert torch.equal(torch.from_numpy(res[0]["grads"]["unused"]), torch.zeros(3))
 
 
 def test_rank_failure_is_detected_on_the_host():
