@@ -4,14 +4,16 @@
 // bias of :14-29, triton_gpu.py:64-141), specialised for the shapes of the
 // Naylis configurations: 128-slot blocks; head_dim 64 with at most two blocks
 // per routing set (top-2), or head_dim 128 with one block per row (the
-// block-split plan of top-k routing with many blocks). A work item is (tile of <= 128 tokens sharing one block
-// set, head); CTAs are persistent over items.
+// block-split plan of top-k routing with many blocks). A work item is (tile of
+// <= 128 tokens sharing one block set, head); CTAs are persistent over items.
 //
 // Warp roles (608 threads):
-//   warp 0     loader: K, V blocks and the tile's 128 Q rows by TMA (SWIZZLE_128B
-//              boxes of 128 rows x 64); Q is read from its copy in routing-plan
-//              row order (q_rows), where a tile's rows are contiguous; tile
-//              metadata is fetched 32 items at a time (one per lane)
+//   warp 0     loader: the tile's 128 Q rows by TMA (SWIZZLE_128B boxes of 128
+//              rows x 64) into a 4-stage ring, from Q's copy in routing-plan row
+//              order (q_rows), where a tile's rows are contiguous; the set's K, V
+//              blocks into K/V buffers (two at head_dim 64, one at 128) once per
+//              run of items with the same (set, head); tile metadata 32 items at
+//              a time (one per lane)
 //   warp 1     TMEM owner; S[128 x 256] = Q K^T into TMEM, then O_0 = P[:, block 0] V_0
 //   warp 2     O_1 = P[:, block 1] V_1 (one thread issues a tcgen05.mma only every
 //              ~100 cycles: the two PV halves get an issuing warp each)
@@ -20,7 +22,8 @@
 //              bf16 into TMEM (the A operand of PV); then the epilogue
 //              (O_0 + O_1) / l -> shared memory -> global as whole 128-B rows,
 //              log-sum-exp -> global
-// TMEM: S at columns 0..255, P (bf16 pairs) at 256..383, O_0 / O_1 at 384 / 448.
+// TMEM: S at columns 0..255, P (bf16 pairs) at 256..383, O_0 / O_1 at 384 / 448
+// (head_dim 128: S 0..127, P 256..319, O 384..511).
 // P has its own columns so that S(i+1) is issued as soon as the softmax has read
 // S(i), overlapping PV(i); the softmax writes P(i+1) once PV(i) is done
 // (pv_done), PV(i+1) writes O once the epilogue has read O(i) (o_free).
