@@ -16,7 +16,8 @@
 //   warp 0     loader: Q, dO tiles; K, V blocks by TMA when the run changes
 //   warps 1, 2 MMA issuers: S = Q K^T (TMEM cols 0-255) and dP = dO V^T
 //              (cols 256-511), then dQ over block 0 / block 1 (TS form, dS
-//              from TMEM) into cols 256-319 / 320-383
+//              from TMEM) into cols 256-319 / 320-383 (head_dim 128: S 0-127,
+//              dP then the one 128-column dQ at 256-383)
 //   warps 3-18 softmax, one pass: P = exp2(S*scale + bias - lse), dS = P (dP -
 //              delta) as bf16 over the S columns already read; the exact row
 //              sums of P dP and P per block for the gate gradient (fp32 atomics
@@ -27,8 +28,9 @@
 //   warp 0     loader: K_b, V_b once per item (TMA); per tile Q, dO and the
 //              tile's per-token bias - lse and delta into shared memory
 //   warp 1     MMA: S^T = K_b Q^T, dP^T = V_b dO^T into one of three step
-//              buffers (TMEM cols 128*b, +64)
+//              buffers (TMEM cols 128*b, +64; two buffers at head_dim 128)
 //   warp 2     MMA: dK += dS^T Q, dV += P^T dO (TS form) into cols 384 / 448
+//              (head_dim 128: 256 / 384, 128 columns each)
 //   warps 3-18 P^T, dS^T (one slot row per thread) -> bf16 in TMEM over the
 //              step buffer; at the end of the item dK * scale, dV -> fp32
 //              reductions into global.
