@@ -181,3 +181,25 @@ def test_layer_eager_path_matches_reference_semantics():
         out = layer(inp["x"], inp["M"])
     g = np.load(os.path.join(ROOT, "tests", "golden", "small_f32.npz"))
     assert O.scaled_err(out.numpy(), g["out"]) < 1e-6
+
+
+def test_ctypes_signatures_match_the_header():
+    """Every binding in naylis_b200/_lib.py has the argument count and return
+    type class of its declaration in include/naylis_mom.h (a mismatch would pass
+    arguments in the wrong registers without any error)."""
+    import ctypes
+    from naylis_b200 import _lib
+    src = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    decls = {}
+    for ret, name, args in re.findall(r"MOM_API\s+((?:const\s+)?\w+\s*\*?)\s*(mom_\w+)\s*\(([^;]*?)\)\s*;", src,
+                                      flags=re.S):
+        args = " ".join(args.split())
+        n = 0 if args in ("", "void") else args.count(",") + 1
+        decls[name] = (ret.replace(" ", ""), n)
+    assert set(decls) == set(_lib.SIGNATURES)
+    for name, (res, argtypes) in _lib.SIGNATURES.items():
+        ret, n = decls[name]
+        assert len(argtypes) == n, f"{name}: {len(argtypes)} ctypes args, header has {n}"
+        want = {"int": ctypes.c_int, "size_t": ctypes.c_size_t, "uint64_t": ctypes.c_uint64,
+                "constchar*": ctypes.c_char_p}[ret]
+        assert res is want, f"{name}: restype {res}, header returns {ret}"
