@@ -194,12 +194,18 @@ def test_ctypes_signatures_match_the_header():
     for ret, name, args in re.findall(r"MOM_API\s+((?:const\s+)?\w+\s*\*?)\s*(mom_\w+)\s*\(([^;]*?)\)\s*;", src,
                                       flags=re.S):
         args = " ".join(args.split())
-        n = 0 if args in ("", "void") else args.count(",") + 1
-        decls[name] = (ret.replace(" ", ""), n)
+        kinds = []
+        for a in ([] if args in ("", "void") else args.split(",")):
+            a = a.strip()
+            kinds.append("ptr" if "*" in a else a.split()[-2] if len(a.split()) > 1 else a)
+        decls[name] = (ret.replace(" ", ""), kinds)
     assert set(decls) == set(_lib.SIGNATURES)
+    arg_type = {"ptr": ctypes.c_void_p, "int": ctypes.c_int, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t}
     for name, (res, argtypes) in _lib.SIGNATURES.items():
-        ret, n = decls[name]
-        assert len(argtypes) == n, f"{name}: {len(argtypes)} ctypes args, header has {n}"
+        ret, kinds = decls[name]
+        assert len(argtypes) == len(kinds), f"{name}: {len(argtypes)} ctypes args, header has {len(kinds)}"
+        for i, (got, kind) in enumerate(zip(argtypes, kinds)):
+            assert got is arg_type[kind], f"{name} argument {i}: ctypes {got}, header {kind}"
         want = {"int": ctypes.c_int, "size_t": ctypes.c_size_t, "uint64_t": ctypes.c_uint64,
                 "constchar*": ctypes.c_char_p}[ret]
         assert res is want, f"{name}: restype {res}, header returns {ret}"
