@@ -351,9 +351,9 @@ def measure_kernels(layer, x, M, dout, dev, args):
     act_o = torch.empty(N, r, dtype=torch.bfloat16, device=dev)
     rws = torch.empty(lib.mom_route_workspace_size(B, S, d, r, nb, _lib.BF16), dtype=torch.uint8, device=dev)
 
-    def route_once():
+    def route_once(mode=_lib.SCAN_MODES["fp32"]):
         _lib.call("mom_route_fwd", xb.data_ptr(), _lib.BF16, B, S, d, wd.data_ptr(), wu.data_ptr(),
-                  _lib.BF16, r, nb, top, None, 0, probs_o.data_ptr(), idx_o.data_ptr(), _lib.I64,
+                  _lib.BF16, r, nb, top, None, mode, probs_o.data_ptr(), idx_o.data_ptr(), _lib.I64,
                   gates_o.data_ptr(), None, act_o.data_ptr(), rws.data_ptr(), rws.numel(), st)
 
     def timed(fn, iters):
@@ -374,6 +374,7 @@ def measure_kernels(layer, x, M, dout, dev, args):
     iters = max(10, min(100, args.steps))
     t_read = timed(read_once, iters)
     t_route = timed(route_once, iters)
+    t_route64 = timed(lambda: route_once(_lib.SCAN_MODES["fp64"]), iters)
     fwd_f, bwd_f = read_flops(N, d, top, bs)
     rb = router_bytes(N, d, nb, top, r)
     pk = peaks()
@@ -384,7 +385,8 @@ def measure_kernels(layer, x, M, dout, dev, args):
         "router": {"ms": round(t_route, 4), "bytes": rb,
                    "gbs": round(rb / (t_route / 1e3) / 1e9, 1),
                    "frac_of_hbm": round(rb / (t_route / 1e3) / 1e9 / pk["hbm"], 4),
-                   "hbm_peak_gbs": pk["hbm"]},
+                   "hbm_peak_gbs": pk["hbm"], "scan_mode": "fp32 (torch CUDA cumsum; the layer default)",
+                   "fp64_scan_ms": round(t_route64, 4)},
     }
 
 
@@ -506,9 +508,9 @@ def run_reference(args):
     S_sample = 2048
     O, x, P, g = _cpu_step_inputs(S_sample)
     c = CFG
-    for _ in range(min(args.warmup, 1)):
+    for _ in range(args.warmup):
         O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])
-    steps = args.steps if args.steps <= 5 else 5
+    steps = args.steps
     t = time.perf_counter()
     for _ in range(steps):
         O.layer_step_fp32(x, P, g, c["H"], c["nb"], c["bs"], c["top"])
@@ -516,7 +518,7 @@ def run_reference(args):
     val = round(S_sample / dt, 1)
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
-        "steps": steps, "warmup": min(args.warmup, 1), "ms_per_step": round(dt * 1e3, 2),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": S_sample,
                                         "parallelism": "cpu"},

@@ -10,6 +10,9 @@
 #include <atomic>
 #include <mutex>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "launch.h"
 
@@ -597,7 +600,10 @@ int mom_read_split_bwd(const void *q, const void *k, const void *v, const void *
 // until the process exits. In host code `g_read_bwd_scratch` only names the
 // symbol; its device address comes from cudaGetSymbolAddress, looked up once
 // per device with that device current, on the first call made on it (make
-// that first call before any stream capture). All calls share the one array
+// that first call before any stream capture), and again whenever the device's
+// current context is another one than at the last look-up (after a
+// cudaDeviceReset the runtime loads the module anew, at a new address). All
+// calls share the one array
 // and it keeps the last call's contents; nothing in it has to start at zero
 // (the dQ pass writes every delta entry that the dK/dV pass reads), but calls
 // that overlap on the GPU (two streams, or two threads) race on it.
@@ -606,20 +612,38 @@ constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 constexpr int kNoAllocMaxDevices = 64;
 __device__ __align__(256) unsigned char g_read_bwd_scratch[kNoAllocScratchBytes];
 
+// The driver's cuCtxGetCurrent, through the runtime's entry-point query (no
+// link against libcuda): the context the cached address belongs to.
+PFN_cuCtxGetCurrent_v4000 ctx_get_current_fn() {
+    static PFN_cuCtxGetCurrent_v4000 fn = [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        return static_cast<PFN_cuCtxGetCurrent_v4000>(nullptr);
+    }();
+    return fn;
+}
+
 int noalloc_scratch(void **ptr) {
     static std::mutex mu;
     static void *addr[kNoAllocMaxDevices] = {};
+    static CUcontext owner[kNoAllocMaxDevices] = {};
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
     if (dev < 0 || dev >= kNoAllocMaxDevices)
         return fail(MOM_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kNoAllocMaxDevices);
+    CUcontext ctx = nullptr;
+    if (PFN_cuCtxGetCurrent_v4000 get = ctx_get_current_fn()) get(&ctx);
     std::lock_guard<std::mutex> lk(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || owner[dev] != ctx) {
         void *p = nullptr;
         if ((e = cudaGetSymbolAddress(&p, g_read_bwd_scratch)) != cudaSuccess)
             return cuda_fail(e, "cudaGetSymbolAddress(read bwd scratch)");
         addr[dev] = p;
+        owner[dev] = ctx;
     }
     *ptr = addr[dev];
     return MOM_OK;

@@ -15,8 +15,21 @@ as NCCL requires) as soon as all their parameters are ready, so the exchange
 overlaps the rest of the backward. ``finish()`` launches whatever is left
 and waits; the average is NCCL's own (``ReduceOp.AVG``), or a division by the
 world size on backends without it.
+
+Gradient accumulation (the reference's ``[train] grad_accum``, pretrain.py:795
+under DDP): run every micro-batch but the last inside ``no_sync()``, which
+keeps the hooks from launching, then the last backward and ``finish()`` once.
+A second backward before ``finish()`` outside ``no_sync()`` would add into
+buckets already on the wire, so it raises instead.
+
+``comm_dtype=torch.bfloat16`` sends each bucket as bf16 (half the bytes on
+NVLink): the fp32 bucket is rounded into a bf16 twin on the compute stream
+before its all-reduce, and the averaged result is written back into the fp32
+bucket by ``finish()``.
 """
 from __future__ import annotations
+
+import contextlib
 
 import torch
 import torch.distributed as dist
@@ -24,12 +37,16 @@ import torch.distributed as dist
 
 class GradAllReduce:
     def __init__(self, module: torch.nn.Module, process_group=None, bucket_mb: float = 32.0,
-                 average: bool = True, overlap: bool = True):
+                 average: bool = True, overlap: bool = True, comm_dtype=None):
         self.group = process_group
         # overlap=False: no collective from the backward's hooks; finish()
         # exchanges every bucket. For a backward captured in a CUDA graph,
         # whose replay then runs no collective, with finish() after replay.
         self.overlap = overlap
+        self._sync = True
+        if comm_dtype not in (None, torch.float32, torch.bfloat16):
+            raise ValueError(f"GradAllReduce: comm_dtype must be fp32 or bf16, got {comm_dtype}")
+        self.comm_dtype = None if comm_dtype in (None, torch.float32) else comm_dtype
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.average = average
         # NCCL averages inside the reduction (no extra pass over the buckets);
@@ -68,6 +85,8 @@ class GradAllReduce:
                 off += p.numel()
                 self._bucket_of[p] = i
             self.flat.append(buf)
+        self.wire = [torch.empty(b.numel(), dtype=self.comm_dtype, device=b.device) for b in self.flat] \
+            if self.comm_dtype is not None and self.world > 1 else None
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_ready) for p in params]
         self._reset_state()
 
@@ -88,15 +107,36 @@ class GradAllReduce:
                 off += p.numel()
         self._reset_state()
 
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backwards inside this context only accumulate into the buckets; the
+        exchange happens after the next backward outside it, at ``finish()``."""
+        prev = self._sync
+        self._sync = False
+        try:
+            yield
+        finally:
+            self._sync = prev
+
     def _launch_ready(self, force: bool = False):
         while self._next < len(self.buckets) and (force or self._pending[self._next] == 0):
             buf = self.flat[self._next]
             if self.world > 1:
+                if self.wire is not None:
+                    self.wire[self._next].copy_(buf)
+                    buf = self.wire[self._next]
                 self._works.append(dist.all_reduce(buf, op=self._op, group=self.group, async_op=True))
             self._next += 1
 
     def _on_ready(self, p):
+        if not self._sync:
+            return
         i = self._bucket_of[p]
+        if i < self._next or self._pending[i] <= 0:
+            raise RuntimeError(
+                "GradAllReduce: a gradient arrived for a bucket that has already been exchanged or "
+                "counted in this step (a second backward before finish()). Run the accumulation "
+                "micro-batches inside no_sync() and call finish() after the last backward.")
         self._pending[i] -= 1
         if self.overlap:
             self._launch_ready()
@@ -106,6 +146,9 @@ class GradAllReduce:
         self._launch_ready(force=True)
         for w in self._works:
             w.wait()
+        if self.wire is not None:
+            for buf, w in zip(self.flat, self.wire):
+                buf.copy_(w)
         if self._divide:
             for buf in self.flat:
                 buf.div_(self.world)

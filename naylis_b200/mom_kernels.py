@@ -54,16 +54,29 @@ def preflight(device_type: str) -> None:
     _device_ok(torch.device("cuda", torch.cuda.current_device()))
 
 
+def _read_dtype(dtype):
+    """The dtype the read's activations will have. The reference resolves with
+    the dtype of the layer input x (model.py:164-165), which is fp32 under
+    bf16 autocast (the residual stream keeps the fp32 master dtype); the q
+    projection then runs in bf16, so the read gets bf16 activations."""
+    if dtype == torch.float32 and torch.is_autocast_enabled("cuda") \
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        return torch.bfloat16
+    return dtype
+
+
 def resolve_mode(device, dtype, *, head_dim=None) -> str:
     """Pick the kernel backend and check its contract (reference:
     mom_kernels/__init__.py:56-84). Only ``"sm100"`` is served here: bf16
-    activations and head_dim 64 or 128 on an sm_100 device; anything else
-    raises instead of falling back."""
+    activations (bf16 tensors, or fp32 ones inside a CUDA bf16 autocast
+    region) and head_dim 64 or 128 on an sm_100 device; anything else raises
+    instead of falling back."""
     device_type = _device_type(device)
     if device_type != "cuda":
         raise RuntimeError(
             f"use_kernel=true: no sm100 kernel backend for device {device_type!r} "
             f"(the sm100 backend runs on CUDA B200 only).")
+    dtype = _read_dtype(dtype)
     if dtype != torch.bfloat16:
         raise RuntimeError(
             f"use_kernel=true (sm100) requires bf16 activations (the repo AMP dtype; "
@@ -331,15 +344,16 @@ class _MomRouteFunction(torch.autograd.Function):
 
 
 def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
-              scan_mode: str = "fp64"):
+              scan_mode: str = "fp32"):
     """Fused causal router: returns (router_probs, top_idx, top_gates).
 
     x (B, S, d) fp32/bf16 on CUDA; w_down (r, d) and w_up (nb, r) are the
     router_down / router_up weights (any float dtype; they are cast to the
     compute dtype — autocast's when enabled, as nn.Linear would be). noise
     (B, S, nb): the already-scaled Gumbel noise added before top-k, or None.
-    scan_mode "fp64" reproduces torch's CPU cumsum bit-for-bit, "fp32" its
-    CUDA cumsum.
+    scan_mode "fp32" (default) reproduces torch's CUDA cumsum bit for bit — what
+    the reference's eager router computes on the same GPU — and "fp64" its
+    CPU cumsum.
     """
     if not x.is_cuda:
         raise RuntimeError("sm100 mom_route: x must be on a CUDA device")
@@ -356,7 +370,7 @@ def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=Non
 
 
 def mom_route_log_gates(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
-                        scan_mode: str = "fp64"):
+                        scan_mode: str = "fp32"):
     """``mom_route`` that also returns log(max(top_gates, 1e-9)) as a fourth,
     differentiable output, computed by the router kernel; its gradient goes
     into the router backward directly (the kernel applies the clamp / log

@@ -23,6 +23,9 @@ SMALL_F32 = dict(B=2, S=64, d=32, H=2, nb=4, bs=16, top=2, r=8,
 # A head_dim-64 geometry with a ragged sequence length, bf16 autocast.
 SMALL_BF16 = dict(B=2, S=96, d=128, H=2, nb=4, bs=64, top=2, r=8,
                   seed=21, x_std=1.0, m_std=1.0, w_std=0.09, mom_scale=0.5)
+# BASELINE config 2 at full size (B=8 x S=2048): the benchmarked layer.
+CFG2 = dict(B=8, S=2048, d=1024, H=16, nb=8, bs=128, top=2, r=32,
+            seed=2, x_std=1.0, m_std=0.02, w_std=0.02, mom_scale=1.0)
 # Read-only cases (q, k, v, routing given directly).
 READ = dict(B=2, S=80, H=2, hd=64, nb=4, bs=64, top=2, seed=5)
 

@@ -22,6 +22,12 @@ Cases:
   read_f32/bf16   read only (build_gate_bias + mom_attention_reference), with
                   gradients w.r.t. q, k, v and the gates.
   scan            prefix mean h at (2, 1024, 64), fp32 and bf16 input: SHA-256.
+  cfg2_layer      BASELINE config 2 at full size (B=8, S=2048): layer
+                  forward+backward under CPU bf16 autocast, Gumbel off. Stored:
+                  every token's top-2 ids, every token's logit margin between
+                  its 2nd and 3rd block (0 = a tie), the logits of the tied
+                  tokens, and seeded
+                  subsamples of the output and of every gradient.
 """
 import argparse
 import hashlib
@@ -107,6 +113,42 @@ def run_layer_small(model_mod, autocast: bool):
     return res
 
 
+def run_cfg2(model_mod):
+    import torch
+    geo = gi.CFG2
+    layer = build_layer(model_mod, geo)
+    inp = gi.layer_inputs(geo, layer)
+    layer.train()
+    layer.noise_scale = 0.0
+    x = inp["x"].clone().requires_grad_(True)
+    M = inp["M"].clone().requires_grad_(True)
+    dout = gi.upstream_grad(geo)
+    with torch.autocast("cpu", dtype=torch.bfloat16):
+        out = layer(x, M)
+    out.backward(dout)
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16):
+        logits = layer._router_logits(inp["x"])
+    top_idx = layer.last_top_idx.reshape(geo["B"], geo["S"], -1)
+    srt = torch.sort(logits, dim=-1, descending=True).values
+    margin = (srt[..., geo["top"] - 1] - srt[..., geo["top"]]).reshape(-1)
+    rng = np.random.default_rng(4321)
+    res = dict(input_sha=np.array(gi.input_digest(inp)),
+               top_idx=to_np(top_idx).astype(np.uint8), margin=to_np(margin))
+    ties = torch.nonzero(margin == 0).reshape(-1)
+    res["tie_tokens"] = to_np(ties).astype(np.int64)
+    res["tie_logits"] = to_np(logits.reshape(-1, geo["nb"])[ties])
+    tensors = dict(out=out, dx=x.grad, dM_blocks=M.grad)
+    for name, p in layer.named_parameters():
+        tensors["d_" + name.replace(".weight", "")] = p.grad
+    for name, t in tensors.items():
+        flat = to_np(t).reshape(-1)
+        sub = np.sort(rng.choice(flat.size, size=min(flat.size, 8192), replace=False))
+        res[name + "_idx"] = sub.astype(np.int64)
+        res[name] = flat[sub]
+        res[name + "_absmax"] = np.array(np.abs(flat).max())
+    return res
+
+
 def run_read(reference, dtype_name: str):
     import torch
     geo = gi.READ
@@ -137,6 +179,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--cases", default="", help="comma-separated subset of the cases (default: all)")
     args = ap.parse_args()
     sys.path.insert(0, os.path.abspath(args.reference))
     import torch
@@ -151,8 +194,10 @@ def main():
         "read_f32": lambda: run_read(reference, "f32"),
         "read_bf16": lambda: run_read(reference, "bf16"),
         "scan": lambda: run_scan(reference),
+        "cfg2_layer": lambda: run_cfg2(model_mod),
     }
-    for name, fn in cases.items():
+    ap_cases = [c for c in args.cases.split(",") if c] if args.cases else list(cases)
+    for name, fn in ((n, cases[n]) for n in ap_cases):
         res = fn()
         path = os.path.join(args.out, f"{name}.npz")
         np.savez_compressed(path, **res)

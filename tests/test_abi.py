@@ -166,21 +166,36 @@ def test_door_fails_loud_off_gpu():
         mk.mom_route_log_gates(torch.zeros(1, 4, 64), torch.zeros(8, 64), torch.zeros(4, 8), 2, scan_mode="fp16")
 
 
-def test_layer_eager_path_matches_reference_semantics():
-    """use_kernel=False is the reference's eager path: it must equal the oracle
-    on the reference test-suite geometry (fp32)."""
-    import numpy as np
-    import golden_inputs as gi
-    import mom_oracle as O
+def test_layer_is_a_drop_in_for_the_reference_module():
+    """naylis_b200.model.MoMLayer takes the reference's constructor arguments,
+    raises its ValueErrors and has its parameter names and shapes, so a
+    reference checkpoint loads into it (checked against the reference's own
+    model.MoMLayer where the reference checkout is importable)."""
     from naylis_b200.model import MoMLayer
-    geo = gi.SMALL_F32
-    layer = MoMLayer(geo["d"], geo["H"], geo["nb"] * geo["bs"], geo["bs"], geo["top"], geo["r"])
-    inp = gi.layer_inputs(geo, layer)
-    layer.eval()
-    with torch.no_grad():
-        out = layer(inp["x"], inp["M"])
-    g = np.load(os.path.join(ROOT, "tests", "golden", "small_f32.npz"))
-    assert O.scaled_err(out.numpy(), g["out"]) < 1e-6
+    args = dict(d_model=256, n_heads=4, mem_size=1024, block_size=128, top_blocks=2, router_rank=32)
+    ours = MoMLayer(**args)
+    assert ours.head_dim == 64 and ours.num_blocks == 8 and ours.scan_mode == "fp32"
+    for bad in (dict(args, n_heads=3), dict(args, mem_size=1000), dict(args, top_blocks=9)):
+        with pytest.raises(ValueError):
+            MoMLayer(**bad)
+    with pytest.raises(ValueError, match="eager"):
+        MoMLayer(**args, use_kernel=False)
+    ref_root = os.environ.get("NAYLIS_REFERENCE", "/root/reference")
+    if not os.path.exists(os.path.join(ref_root, "model.py")):
+        pytest.skip("reference checkout not importable here")
+    import importlib
+    import sys as _sys
+    _sys.path.insert(0, ref_root)
+    try:
+        ref_model = importlib.import_module("model")
+    finally:
+        _sys.path.remove(ref_root)
+    ref = ref_model.MoMLayer(**args)
+    assert {k: tuple(v.shape) for k, v in ref.state_dict().items()} == \
+        {k: tuple(v.shape) for k, v in ours.state_dict().items()}
+    ours.load_state_dict(ref.state_dict())
+    for name in ("num_blocks", "block_size", "top_blocks", "mem_slots", "n_heads", "head_dim", "noise_scale"):
+        assert getattr(ours, name) == getattr(ref, name), name
 
 
 def test_ctypes_signatures_match_the_header():

@@ -280,3 +280,86 @@ def test_router_backward_matches_oracle(compute, tol, r, nb, top):
     for key in ("dx", "dw_down", "dw_up"):
         err = O.scaled_err(got[key], ref[key])
         assert err < tol, f"{key}: {err:.3e}"
+
+
+@pytest.mark.parametrize("compute", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("top", [1, 2, 3])
+def test_topk_tie_order_matches_torch_cuda(compute, top):
+    """torch.topk leaves the order of equal values to the implementation. On
+    CUDA, the reference's eager router (model.py:214) runs torch's CUDA topk;
+    the kernel takes the lower block id first. With W_up = 0 the logits are
+    exactly 0 and the noisy logits equal the noise, which here takes values
+    in {1, 2, 3} only, so nearly every token has ties at the 1st/2nd and at
+    the k-th/(k+1)-th boundary. Indices must equal torch.topk's on this GPU."""
+    torch.manual_seed(11 + top)
+    B, S, d, r, nb = 4, 512, 64, 8, 8
+    x = torch.randn(B, S, d)
+    w_down = torch.randn(r, d) * 0.1
+    w_up = torch.zeros(nb, r)
+    noise = torch.randint(1, 4, (B, S, nb)).float()
+    got = _route_gpu(x, w_down, w_up, top, compute, noise=noise, scan_mode="fp32")
+    ref_v, ref_i = torch.topk(noise.cuda(), top, dim=-1)
+    ref_i = ref_i.cpu().numpy()
+    tied = (noise.sort(-1, descending=True).values[..., :top + 1].diff(dim=-1) == 0).any(-1)
+    assert float(tied.float().mean()) > 0.5          # the case really is tie-heavy
+    mism = np.any(got["top_idx"] != ref_i, axis=-1)
+    assert not mism.any(), (f"{int(mism.sum())} of {mism.size} tokens differ from torch.topk on CUDA; "
+                            f"first: noise {noise.reshape(-1, nb)[mism.reshape(-1)][:3].tolist()}, "
+                            f"kernel {got['top_idx'].reshape(-1, top)[mism.reshape(-1)][:3].tolist()}, "
+                            f"torch {ref_i.reshape(-1, top)[mism.reshape(-1)][:3].tolist()}")
+
+
+def _torch_cuda_router(x, w_down, w_up, top, noise=None):
+    """The reference's eager router (model.py:169-220) as torch runs it on this
+    GPU under bf16 autocast with fp32 master weights: CUDA cumsum (sequential
+    fp32 per column), IEEE division by t+1, cuBLAS bf16 linears, tanh, fp32
+    softmax, torch's CUDA topk."""
+    import torch.nn.functional as F
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        cs = torch.cumsum(x.float(), dim=1)
+        h = cs / torch.arange(1, x.shape[1] + 1, device=x.device, dtype=cs.dtype).view(1, -1, 1)
+        logits = F.linear(torch.tanh(F.linear(h.to(w_down.dtype), w_down)), w_up).float()
+    noisy = logits if noise is None else logits + noise
+    probs = torch.softmax(logits, -1)
+    vals, idx = noisy.topk(top, dim=-1)
+    return logits, probs, idx, torch.softmax(vals, -1)
+
+
+@pytest.mark.parametrize("noise_on", [False, True])
+def test_router_fp32_scan_matches_torch_cuda_eager_router(noise_on):
+    """The default scan mode ("fp32") against the reference's eager router
+    math run by torch on this B200 at BASELINE config 2's full size (x bf16
+    (8, 2048, 1024), rank 32, 8 blocks, top-2). The prefix means are bitwise
+    equal (tested above); the bf16 logits can differ only where cuBLAS and the
+    kernel accumulate the rank-32 / d=1024 dot products in different orders and
+    the fp32 sums round to different bf16 values. So every token must route
+    alike except tokens whose torch top-k margin is within one bf16 rounding of
+    the logits (at most 4 ulps of the k-th logit), and those stay rare."""
+    torch.manual_seed(2024)
+    B, S, d, r, nb, top = 8, 2048, 1024, 32, 8, 2
+    x = torch.randn(B, S, d).to(torch.bfloat16)
+    w_down = torch.randn(r, d) * 0.02
+    w_up = torch.randn(nb, r) * 0.02
+    noise = None
+    if noise_on:
+        from naylis_b200 import mom_kernels as mk
+        torch.manual_seed(5)
+        noise = mk.gumbel_noise((B, S, nb), torch.device("cuda"), 1.0).cpu()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        got = _route_gpu(x, w_down, w_up, top, torch.bfloat16, noise=noise, scan_mode="fp32")
+    xd, wd, wu = x.cuda(), w_down.cuda(), w_up.cuda()
+    logits, probs, idx, gates = _torch_cuda_router(xd, wd, wu, top, None if noise is None else noise.cuda())
+    ref_i = idx.cpu().numpy()
+    mism = np.any(got["top_idx"] != ref_i, axis=-1).reshape(-1)
+    noisy = (logits if noise is None else logits + noise.cuda()).reshape(-1, nb)
+    srt = noisy.sort(-1, descending=True).values
+    margin = (srt[:, top - 1] - srt[:, top]).cpu().numpy()
+    # a bf16 value has 8 significant bits: 4 ulps of the k-th logit ~ 4 * |v| * 2^-7
+    kth = np.abs(srt[:, top - 1].cpu().numpy())
+    allowed = margin <= 4 * kth * 2.0 ** -7
+    assert not (mism & ~allowed).any(), \
+        f"{int((mism & ~allowed).sum())} tokens differ with torch margins {margin[mism & ~allowed][:8]}"
+    assert mism.mean() < 2e-3, f"{int(mism.sum())} of {mism.size} tokens differ (all near ties)"
+    assert O.scaled_err(got["probs"].reshape(-1, nb), probs.reshape(-1, nb).cpu().numpy()) < 2e-2
+    ok = ~mism
+    assert O.scaled_err(got["gates"].reshape(-1, top)[ok], gates.reshape(-1, top).cpu().numpy()[ok]) < 2e-2

@@ -4,15 +4,26 @@ device array of the library, for callers that cannot allocate device memory.
 The GPU test calls it through the C ABI several times in a row (different
 geometries, so each call meets the previous call's leftovers in the shared
 scratch, one of them at the largest size the array takes) and checks each
-result against mom_read_bwd with a caller workspace, within the bf16 read
-tolerance of the other tests (scaled max error < 2e-2). The file is named to
-be collected last; it also passes alone in a fresh process.
+result against mom_read_bwd with a caller workspace:
+
+* dq bit for bit: both entry points run the same MMAs on the same values (the
+  no-alloc one only fetches dO rows by gather instead of from a plan-order
+  copy), and each dQ tile is summed in one fixed order;
+* dk, dv and dlog_gates to a scaled 1e-5: the kernels sum them with fp32
+  atomics, whose order changes from run to run (two runs of mom_read_bwd
+  differ in the same way);
+* on the smallest case also against the oracle's fp64 read backward, within
+  the bf16 read tolerance of the other tests (scaled 2e-2).
+
+The file is named to be collected last; it also passes alone in a fresh
+process.
 """
 import numpy as np
 import pytest
 import torch
 
-TOL = 2e-2
+TOL = 2e-2          # bf16 read against the fp64 oracle
+ATOMIC_TOL = 1e-5   # the same fp32 sums taken in another order
 
 
 def _scaled_err(a, b):
@@ -103,6 +114,20 @@ def test_noalloc_matches_read_bwd_on_consecutive_calls():
         plan, out, lse, q_rows = _forward(lib, q, k, v, idx, lg, nb, bs, top, st)
         ref = _backward(lib, "mom_read_bwd", q, k, v, out, dout, lse, plan, q_rows, nb, bs, top, st)
         got = _backward(lib, "mom_read_bwd_noalloc", q, k, v, out, dout, lse, plan, q_rows, nb, bs, top, st)
-        errs = {key: _scaled_err(got[key], ref[key]) for key in ref}
-        assert all(e < TOL for e in errs.values()), (c, errs)
         assert all(np.isfinite(got[key]).all() for key in got)
+        assert np.array_equal(got["dq"], ref["dq"]), (c, _scaled_err(got["dq"], ref["dq"]))
+        errs = {key: _scaled_err(got[key], ref[key]) for key in ("dk", "dv", "dlog_gates")}
+        assert all(e < ATOMIC_TOL for e in errs.values()), (c, errs)
+        if seed == 21:
+            _check_against_oracle(got, q, k, v, idx, lg, dout, nb, bs)
+
+
+def _check_against_oracle(got, q, k, v, idx, lg, dout, nb, bs):
+    import mom_oracle as O
+    f = lambda t: t.float().cpu().numpy()
+    ref = O.read_backward(f(q), f(k), f(v), idx.cpu().numpy(), lg.cpu().numpy(), f(dout), nb, bs)
+    B, S, H, hd = q.shape
+    pairs = {"dq": (got["dq"], ref["dq"]), "dk": (got["dk"], ref["dk"]), "dv": (got["dv"], ref["dv"]),
+             "dlog_gates": (got["dlog_gates"].reshape(B, S, -1), ref["dlog_gates"])}
+    errs = {k: _scaled_err(a.reshape(b.shape), b) for k, (a, b) in pairs.items()}
+    assert all(e < TOL for e in errs.values()), errs
