@@ -1,17 +1,25 @@
 #!/usr/bin/env python3
 """Benchmark of the sm100 MoM hot path (one JSON line on rank 0).
 
-Workload: one MoM layer forward+backward — fused router,
-q/k/v/o projections, the bucketed memory read — on B=8 x S=2048 tokens per
-GPU, d=1024, 16x64 heads, bank 8x128 slots, router rank 32, top-2, bf16
-autocast with fp32 master weights, Gumbel exploration on (training mode).
-At N>1 every rank runs its own 8x2048 shard (weak scaling) and the gradients
-are averaged with the bucketed NCCL all-reduce of naylis_b200.data_parallel.
+Default workload: the 300M-class Naylis decoder training
+step — 20 layers, d=1024, 16x64 heads, SwiGLU 2816, vocab 32000, RoPE, RMSNorm,
+a MoM read (fused router + bucketed read on this package's sm_100a kernels) in
+every layer sharing one 8x128x1024 bank, router rank 32, top-2, aux 0.01 —
+forward + backward + fused AdamW, bf16 autocast with fp32 master weights, on
+B=8 x S=2048 token ids per GPU. At N>1 every rank trains its own 8x2048 batch
+(weak scaling) and the gradients are averaged by the bucketed NCCL all-reduce
+of naylis_b200.data_parallel, launched from the backward's hooks so it
+overlaps the backward. The line also carries the MoM read (fwd+bwd) and the
+router forward on BASELINE config 2's geometry, timed alone through the C ABI:
+the dominant kernels of this library and their rooflines.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sm100|reference]
+                    [--workload cfg3|cfg2|read-top4of32]
 
+``--workload cfg2`` times one MoM layer forward+backward (config 2) as a CUDA
+graph; ``read-top4of32`` the read alone on config 4's geometry.
 ``--impl reference`` times the CPU restatement of the reference's eager path
-(oracle/mom_oracle.py: layer_step_fp32) on this host's cores, same metric.
+(oracle/) on this host's cores for the same workload and metric.
 """
 from __future__ import annotations
 
@@ -27,6 +35,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 CFG = dict(B=8, S=2048, d=1024, H=16, nb=8, bs=128, top=2, r=32)
+CFG3 = dict(B=8, S=2048)
+METRIC3 = "Naylis 300M decoder training tokens/s (fwd+bwd+AdamW, all GPUs), BASELINE config 3"
+WORKLOAD3 = ("cfg3: 20-layer Naylis decoder (d 1024, 16x64 heads, SwiGLU 2816, vocab 32000, RoPE, RMSNorm, "
+             "MoM in every layer sharing one 8x128x1024 bank, rank 32, top-2, aux 0.01), B=8 x S=2048 "
+             "token ids per GPU, bf16 autocast, fp32 master weights, fused AdamW")
 METRIC = "MoM layer fwd+bwd tokens/s (router + read + projections), BASELINE config 2"
 WORKLOAD = ("cfg2: one MoM layer fwd+bwd per GPU, B=8 S=2048 d=1024, 16x64 heads, "
             "bank 8x128 slots, router rank 32, top-2, bf16 autocast, fp32 master weights")
@@ -115,7 +128,7 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ GPU arm
-def run_gpu(args):
+def run_layer_cfg2(args):
     import torch
     import torch.distributed as dist
     from naylis_b200 import _lib
@@ -299,6 +312,183 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_model_cfg3(args):
+    """the decoder's training step on every GPU."""
+    import torch
+    import torch.distributed as dist
+    from naylis_b200 import _lib
+    from naylis_b200.data_parallel import GradAllReduce
+    from naylis_b200.decoder import NaylisConfig, NaylisForCausalLM, flops_per_token, param_count
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    B, S = CFG3["B"], CFG3["S"]
+    cfg = NaylisConfig()
+    torch.manual_seed(1234)                       # every replica starts from the same weights
+    model = NaylisForCausalLM(cfg).to(dev).train()
+    comm = torch.bfloat16 if args.bf16_grads else None
+    dp = GradAllReduce(model, bucket_mb=args.bucket_mb, comm_dtype=comm)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1, fused=True)
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), device=dev, generator=g)
+    lib = _lib.load()
+
+    def step(batch):
+        dp.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(batch, labels=batch)
+        loss.backward()
+        dp.finish()
+        opt.step()
+        return loss
+
+    for _ in range(args.warmup):
+        step(ids)
+    torch.cuda.synchronize()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.5)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = lib.mom_kernel_launches()
+    t_wall0 = time.time()
+    for i in range(args.steps):
+        flush.fill_(float(i))                     # evict L2 between timed steps (untimed)
+        starts[i].record()
+        step(ids)
+        ends[i].record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t_wall1 = time.time()
+    launches = lib.mom_kernel_launches() - l0
+    total_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    if clocks:
+        clocks.window = (t_wall0, t_wall1)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    tokens_per_s = world * B * S * args.steps / (total_ms / 1e3)
+
+    # end to end through the public API: the token ids travel from pinned host
+    # memory every step, the loss comes back every step
+    ids_host = ids.cpu().pin_memory()
+    loss_host = torch.empty(max(1, min(args.steps, 20)), dtype=torch.float32).pin_memory()
+    dev_ids = torch.empty_like(ids)
+    n_e2e = loss_host.numel()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(n_e2e):
+        dev_ids.copy_(ids_host, non_blocking=True)
+        loss = step(dev_ids)
+        loss_host[i:i + 1].copy_(loss.detach().float().reshape(1), non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(world * B * S * n_e2e / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": ids_host.numel() * ids_host.element_size(), "d2h_bytes_per_step": 4,
+           "loss_last": round(float(loss_host[-1]), 4)}
+
+    extra = {}
+    if rank == 0:
+        layer, x, M, dout = cfg2_layer_inputs(dev)
+        extra = measure_kernels(layer, x, M, dout, dev, args)
+    if clocks:
+        clocks.stop()
+    if rank == 0:
+        pk = peaks()
+        roof = extra["read"]
+        fpt = 3 * flops_per_token(cfg, S, B * S)
+        per_gpu = tokens_per_s / world
+        line = {
+            "metric": METRIC3,
+            "value": round(tokens_per_s, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (token ids uniform in [0, 32000), seeded per rank; random-init weights as the "
+                    "reference initialises them)",
+            "config": {"workload": WORKLOAD3, "global_batch": B * world, "seq_len": S, "parallelism": f"dp{world}",
+                       "params": param_count(model),
+                       "l2": "flushed between timed steps (256 MiB write, untimed); the step's working set "
+                             "(weights, optimizer state, activations) is far above L2 as well",
+                       "grad_exchange": (f"bucketed NCCL AVG all-reduce ({args.bucket_mb:g} MiB buckets, "
+                                         f"{'bf16' if comm is not None else 'fp32'} on the wire) launched from the "
+                                         "backward's hooks" if world > 1 else "none (one GPU)")},
+            "tokens_per_s_per_gpu": round(per_gpu, 1),
+            "model_flops_per_token": fpt,
+            "mfu": round(per_gpu * fpt / (pk["bf16_sust"] * 1e12), 4),
+            "mfu_peak": f"{pk['src']} bf16 sustained {pk['bf16_sust']} TFLOP/s (MEASURED_PEAKS.json)",
+            "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
+                         "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
+                         "traffic": READ_TRAFFIC_BYTES,
+                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum of the three tensor-core "
+                                          "read kernels (fwd 39.1 + dq 85.6 + dkdv 92.2 MB), one ncu capture "
+                                          "each on config 2; bucketing and row copies not included"),
+                         "kernel": "MoM read fwd+bwd on BASELINE config 2 (bucket + fwd + dq + dkdv), C ABI",
+                         "flops_per_launch": roof["flops"], "ms_per_launch": roof["ms"],
+                         "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
+            "router": extra["router"],
+            "read": roof,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "gpu_launches_per_step": round(launches / args.steps, 1),
+            "clocks": clocks.summary() if clocks else None,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_model(args)
+        print(json.dumps(line), flush=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cfg2_layer_inputs(dev, seed=4321):
+    """A config-2 MoM layer (N(0, 0.02) weights, bank and mom_scale 1), x and
+    an upstream gradient, for timing the library's kernels on their own."""
+    import torch
+    from naylis_b200.model import MoMLayer
+    c = CFG
+    torch.manual_seed(seed)
+    layer = MoMLayer(c["d"], c["H"], c["nb"] * c["bs"], c["bs"], c["top"], c["r"])
+    with torch.no_grad():
+        for p in layer.parameters():
+            p.normal_(0.0, 0.02)
+        layer.mom_scale.fill_(1.0)
+    layer = layer.to(dev)
+    M = torch.randn(c["nb"], c["bs"] * c["d"], device=dev) * 0.02
+    x = torch.randn(c["B"], c["S"], c["d"], device=dev).to(torch.bfloat16)
+    dout = torch.randn(c["B"], c["S"], c["d"], device=dev)
+    return layer, x, M, dout
 
 
 def measure_kernels(layer, x, M, dout, dev, args):
@@ -500,6 +690,71 @@ def cpu_baseline(samples=3, S_sample=2048):
                       f"(oracle/mom_oracle.py layer_step_fp32; BLAS threads = all cores)"}
 
 
+CPU_SAMPLE3 = dict(B=1, S=512)
+
+
+def _decoder_oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import decoder_oracle as D
+    return D
+
+
+def cpu_baseline_model(args, samples=3):
+    """The oracle's CPU restatement of the reference's decoder training step
+    (fwd + bwd + AdamW, fp32, config-3 architecture) on this host's cores, a
+    bounded sample of the workload: one 1 x 512-token sequence per step."""
+    import torch
+    D = _decoder_oracle()
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    B, S = CPU_SAMPLE3["B"], CPU_SAMPLE3["S"]
+    step = D.train_step_timer(D.CONFIG3, B, S, threads=threads)
+    step()                                            # warm-up
+    t = time.perf_counter()
+    for _ in range(samples):
+        step()
+    dt = (time.perf_counter() - t) / samples
+    return {"value": round(B * S / dt, 1), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{samples} steps of one {B}x{S}-token sequence: the config-3 decoder (20 layers, d 1024, "
+                      f"vocab 32000) fwd + bwd + AdamW in fp32 torch on the host (oracle/decoder_oracle.py, "
+                      f"pinned to the reference's NaylisLlamaForCausalLM)"}
+
+
+def run_reference_model(args):
+    """--impl reference for config 3: the CPU restatement of the reference's
+    training step, timed on this host's cores, --warmup then --steps steps of a
+    bounded sample (one 1 x 512-token sequence per step). Rank 0 only."""
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    D = _decoder_oracle()
+    threads = os.cpu_count()
+    torch.set_num_threads(threads)
+    B, S = CPU_SAMPLE3["B"], CPU_SAMPLE3["S"]
+    step = D.train_step_timer(D.CONFIG3, B, S, threads=threads)
+    for _ in range(args.warmup):
+        step()
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t) / args.steps
+    val = round(B * S / dt, 1)
+    sample = (f"one {B}x{S}-token sequence per step: the config-3 decoder fwd + bwd + AdamW in fp32 torch on the "
+              f"host (oracle/decoder_oracle.py, the CPU restatement pinned to the reference's "
+              f"NaylisLlamaForCausalLM)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC3, "value": val, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD3, "global_batch": B, "seq_len": S, "parallelism": "cpu",
+                   "sample_of": f"{CFG3['B']}x{CFG3['S']} tokens per GPU"},
+        "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -605,7 +860,7 @@ def run_read_top4of32(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="sm100", choices=["sm100", "reference"])
     ap.add_argument("--cpu-samples", type=int, default=3)
@@ -614,17 +869,21 @@ def main():
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
-    ap.add_argument("--workload", default="cfg2", choices=["cfg2", "read-top4of32"],
-                    help="cfg2: the headline layer step; read-top4of32: the read alone on config 4's geometry")
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg2", "read-top4of32"],
+                    help="cfg3: the decoder training step (default); cfg2: one MoM layer step; "
+                         "read-top4of32: the read alone on config 4's geometry")
+    ap.add_argument("--bf16-grads", action="store_true", help="N>1: all-reduce the gradient buckets in bf16")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
-        run_reference(args)
+        run_reference_model(args) if args.workload == "cfg3" else run_reference(args)
     elif args.workload == "read-top4of32":
         run_read_top4of32(args)
+    elif args.workload == "cfg2":
+        run_layer_cfg2(args)
     else:
-        run_gpu(args)
+        run_model_cfg3(args)
 
 
 if __name__ == "__main__":

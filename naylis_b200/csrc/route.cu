@@ -9,46 +9,81 @@
 namespace mom {
 
 // ============================================================ prefix scan
-// One thread per column of one batch row walks t in order with the carry in a
-// register: the only association that reproduces torch.cumsum bit-for-bit
-// (sequential fp64 on CPU, sequential fp32 on CUDA). Rows are streamed through
-// a ring of shared-memory stages filled by cp.async so that each SM keeps tens
-// of KB of x in flight while the carry chain runs.
-constexpr int kScanCols = 64;    // columns per CTA (one thread each)
-constexpr int kScanRows = 32;    // rows per stage
-constexpr int kScanStages = 8;   // ring depth
+// Sequential fp32 accumulation per column is torch's CUDA cumsum
+// (tensor_kernel_scan_outer_dim): no re-association reproduces its bits, so one
+// thread walks each column in order with the carry in a register. The adds are
+// cheap (a 4-cycle dependent chain per row); what costs is the correctly rounded
+// division h = c / (t+1) and the stores. So the work is split by warp:
+//   warp 0      the 32 column chains of this CTA over a stage of kSeqRows rows,
+//               writing the running sums to shared memory;
+//   warps 1..8  one stage behind, RN(c / (t+1)) by Markstein's correction from
+//               the row's reciprocal, 4 columns of a row per thread (one 16-B
+//               shared load, one 8- or 16-B store); they also form the next
+//               stage's row reciprocals.
+// x streams through a ring of shared-memory stages filled by cp.async, kept
+// kSeqStages-1 stages ahead. (The fp64 mode is the parallel exact scan below.)
+constexpr int kSeqCols = 32;       // columns per CTA (one chain lane each)
+constexpr int kSeqRows = 64;       // rows per stage
+constexpr int kSeqStages = 8;      // ring depth
+constexpr int kSeqDivWarps = 8;
+constexpr int kSeqThreads = 32 * (1 + kSeqDivWarps);
+constexpr int kSeqBatch = 16;      // rows loaded into registers at a time by the chain warp
 
-template <int XDT, int CDT, int MODE>
-__global__ void __launch_bounds__(kScanCols)
+template <int XDT>
+constexpr size_t seq_scan_smem() {
+    return size_t(kSeqStages) * kSeqRows * kSeqCols * sizeof(typename Elem<XDT>::T) +
+           2 * size_t(kSeqRows) * kSeqCols * sizeof(float) + 2 * size_t(kSeqRows) * sizeof(float);
+}
+
+__device__ __forceinline__ float div_by_count(float c, float den, float y);
+
+template <int CDT> struct Store4;
+template <> struct Store4<MOM_BF16> {
+    static __device__ __forceinline__ void store(uint16_t *p, float4 v) {
+        *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    }
+    static __device__ __forceinline__ void store1(uint16_t *p, float v) { *p = f32_to_bf16_bits(v); }
+};
+template <> struct Store4<MOM_F32> {
+    static __device__ __forceinline__ void store(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+    static __device__ __forceinline__ void store1(float *p, float v) { *p = v; }
+};
+
+template <int XDT, int CDT>
+__global__ void __launch_bounds__(kSeqThreads)
 route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
                   typename Elem<CDT>::T *__restrict__ hq, int S, int d, ScanShard sh) {
     using XT = typename Elem<XDT>::T;
-    constexpr int kRowBytes = kScanCols * sizeof(XT);
+    using CT = typename Elem<CDT>::T;
+    constexpr int kRowBytes = kSeqCols * sizeof(XT);
     constexpr int kChunksPerRow = kRowBytes / 16;
-    constexpr int kStageBytes = kScanRows * kRowBytes;
+    constexpr int kStageBytes = kSeqRows * kRowBytes;
+    constexpr int kGroups = kSeqCols / 4;                 // 4-column groups per row
     extern __shared__ __align__(128) unsigned char smem[];
+    float *csum = reinterpret_cast<float *>(smem + kSeqStages * kStageBytes);   // [2][kSeqRows][kSeqCols]
+    float *rcp = csum + 2 * kSeqRows * kSeqCols;                                 // [2][kSeqRows]
 
     const int tid = threadIdx.x;
-    const int c0 = blockIdx.x * kScanCols;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int c0 = blockIdx.x * kSeqCols;
     const int b = blockIdx.y;
-    const int col = c0 + tid;
     const XT *xb = x + static_cast<int64_t>(b) * S * d;
-    const int nstage = (S + kScanRows - 1) / kScanRows;
-    const int valid_cols = min(kScanCols, d - c0);
+    CT *hb = hq + static_cast<int64_t>(b) * S * d;
+    const int nstage = (S + kSeqRows - 1) / kSeqRows;
+    const int valid_cols = min(kSeqCols, d - c0);
     const int valid_bytes = valid_cols * static_cast<int>(sizeof(XT));
 
     auto issue = [&](int s) {
         if (s < nstage) {
-            const uint32_t base = smem_u32(smem + (s % kScanStages) * kStageBytes);
-            for (int i = tid; i < kScanRows * kChunksPerRow; i += kScanCols) {
+            const uint32_t base = smem_u32(smem + (s % kSeqStages) * kStageBytes);
+            for (int i = tid; i < kSeqRows * kChunksPerRow; i += kSeqThreads) {
                 const int r = i / kChunksPerRow, ch = i % kChunksPerRow;
-                const int t = s * kScanRows + r;
+                const int t = s * kSeqRows + r;
                 int nbytes = 0;
                 const XT *src = xb;
                 if (t < S) {
                     nbytes = min(16, max(0, valid_bytes - ch * 16));
-                    src = xb + static_cast<int64_t>(t) * d + c0 + ch * (16 / sizeof(XT));
-                    if (nbytes == 0) src = xb;
+                    if (nbytes) src = xb + static_cast<int64_t>(t) * d + c0 + ch * (16 / sizeof(XT));
                 }
                 cp_async16(base + r * kRowBytes + ch * 16, src, nbytes);
             }
@@ -57,41 +92,79 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
     };
 
 #pragma unroll 1
-    for (int s = 0; s < kScanStages - 1; ++s) issue(s);
+    for (int s = 0; s < kSeqStages - 1; ++s) issue(s);
 
-    // a shard of the sequence starts from the running sum of the rows before it
-    double acc64 = 0.0;
-    float acc32 = (sh.carry_in && col < d) ? static_cast<const float *>(sh.carry_in)[static_cast<int64_t>(b) * d + col]
-                                           : 0.0f;
-    typename Elem<CDT>::T *out = hq + static_cast<int64_t>(b) * S * d + col;
+    // a shard of the sequence continues from the running sum of the rows before it
+    const int col = c0 + lane;
+    float acc = (warp == 0 && sh.carry_in && col < d)
+                    ? static_cast<const float *>(sh.carry_in)[static_cast<int64_t>(b) * d + col] : 0.0f;
+    // a division thread's 4-column group and its first row in a stage
+    const int dt = tid - 32;
+    const int grp = dt % kGroups, row0 = dt / kGroups;
+    constexpr int kRowStep = (kSeqThreads - 32) / kGroups;   // 32 rows per pass
+    const bool vec_ok = 4 * grp + 4 <= valid_cols && (d % 4) == 0 &&
+                        (reinterpret_cast<uintptr_t>(hq) % (4 * sizeof(CT))) == 0;
 #pragma unroll 1
-    for (int s = 0; s < nstage; ++s) {
-        cp_async_wait<kScanStages - 2>();
+    for (int s = 0; s <= nstage; ++s) {
+        cp_async_wait<kSeqStages - 2>();
         __syncthreads();
-        issue(s + kScanStages - 1);
-        const XT *stage = reinterpret_cast<const XT *>(smem + (s % kScanStages) * kStageBytes);
-        const int t0 = s * kScanRows;
-        const int rows = min(kScanRows, S - t0);
-        if (col < d) {
-#pragma unroll 8
-            for (int r = 0; r < rows; ++r) {
-                const float v = Elem<XDT>::load(stage, r * kScanCols + tid);
-                float cs;
-                if (MODE == MOM_SCAN_FP64) {
-                    acc64 = __dadd_rn(acc64, static_cast<double>(v));
-                    cs = __double2float_rn(acc64);
-                } else {
-                    acc32 = __fadd_rn(acc32, v);
-                    cs = acc32;
+        issue(s + kSeqStages - 1);
+        if (warp == 0) {
+            if (s < nstage) {
+                const XT *stage = reinterpret_cast<const XT *>(smem + (s % kSeqStages) * kStageBytes);
+                float *cs = csum + (s & 1) * kSeqRows * kSeqCols;
+                const int rows = min(kSeqRows, S - s * kSeqRows);
+                // a batch of rows is read into registers before the adds use any of
+                // them: only the 4-cycle add chain stays serial, not the loads
+#pragma unroll 1
+                for (int r0 = 0; r0 < rows; r0 += kSeqBatch) {
+                    float v[kSeqBatch];
+#pragma unroll
+                    for (int j = 0; j < kSeqBatch; ++j)
+                        v[j] = r0 + j < rows ? Elem<XDT>::load(stage, (r0 + j) * kSeqCols + lane) : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < kSeqBatch; ++j) {
+                        acc = r0 + j < rows ? __fadd_rn(acc, v[j]) : acc;
+                        v[j] = acc;
+                    }
+#pragma unroll
+                    for (int j = 0; j < kSeqBatch; ++j)
+                        if (r0 + j < rows) cs[(r0 + j) * kSeqCols + lane] = v[j];
                 }
-                const float h = __fdiv_rn(cs, static_cast<float>(sh.t_base + t0 + r + 1));
-                Elem<CDT>::store(out, static_cast<int64_t>(t0 + r) * d, h);
+            }
+        } else {
+            // the reciprocals of stage s's rows, read at the next iteration
+            if (s < nstage && dt < kSeqRows)
+                rcp[(s & 1) * kSeqRows + dt] = __frcp_rn(static_cast<float>(sh.t_base + s * kSeqRows + dt + 1));
+            if (s > 0) {
+                const int sp = s - 1;
+                const float *cs = csum + (sp & 1) * kSeqRows * kSeqCols;
+                const float *yv = rcp + (sp & 1) * kSeqRows;
+                const int t0 = sp * kSeqRows;
+                const int rows = min(kSeqRows, S - t0);
+#pragma unroll
+                for (int r = row0; r < kSeqRows; r += kRowStep) {
+                    if (r >= rows) break;
+                    const float4 c = *reinterpret_cast<const float4 *>(cs + r * kSeqCols + 4 * grp);
+                    const float y = yv[r];
+                    const float den = static_cast<float>(sh.t_base + t0 + r + 1);
+                    const float4 h = make_float4(div_by_count(c.x, den, y), div_by_count(c.y, den, y),
+                                                 div_by_count(c.z, den, y), div_by_count(c.w, den, y));
+                    CT *dst = hb + static_cast<int64_t>(t0 + r) * d + c0 + 4 * grp;
+                    if (vec_ok) {
+                        Store4<CDT>::store(dst, h);
+                    } else {
+                        const float hv[4] = {h.x, h.y, h.z, h.w};
+                        for (int j = 0; j < 4; ++j)
+                            if (4 * grp + j < valid_cols) Store4<CDT>::store1(dst + j, hv[j]);
+                    }
+                }
             }
         }
     }
     cp_async_wait<0>();
-    if (MODE == MOM_SCAN_FP32 && sh.carry_out && col < d)
-        static_cast<float *>(sh.carry_out)[static_cast<int64_t>(b) * d + col] = acc32;
+    if (warp == 0 && sh.carry_out && col < d)
+        static_cast<float *>(sh.carry_out)[static_cast<int64_t>(b) * d + col] = acc;
 }
 
 // ------------------------------------------------------------ parallel exact fp64 scan
@@ -369,7 +442,7 @@ route_shard_carry_kernel(const double *__restrict__ all, int W, int rank, int64_
 
 // ============================================================ router head
 // Per token: z = round(hq . Wd^T), act = round(tanh z), logits = round(act . Wu^T),
-// then softmax, top-k (value desc, lower index on ties) and the gate softmax.
+// then softmax, top-k (value desc; torch's CUDA order on ties) and the gate softmax.
 constexpr int kHeadTokens = 64;   // tokens per CTA
 constexpr int kHeadThreads = 128; // 4 warps x 16 tokens (mma path)
 constexpr int kHeadKC = 64;       // d-columns per pipeline step
@@ -383,6 +456,53 @@ constexpr int kMaxRank = 128;
 // banks), the logits are the same sequential fp32 FMA chains over j as the
 // reference's linear, fully unrolled when the rank is a compile-time R. Per
 // token: top-k on the logits (+ noise), then the softmax with one exp per logit.
+// Order of the selected top-k as torch's CUDA topk returns it when selected
+// values are equal (measured on B200 against torch.topk for 8 / 16 / 32 blocks,
+// k = 1..8, fp32 and bf16, by an exhaustive comparison over recorded outputs).
+// torch gathers the selection as (values above the k-th value, in index order)
+// then (values equal to it, in index order), and sorts that list with a
+// 32-wide bitonic network (Batcher) whose compare-exchange, descending, also
+// exchanges equal keys; unused slots sort to the end. The network is run here
+// on the same list, so ties come out in the same order. Only tokens with equal
+// selected values take this path (about 1 % of tokens with bf16 logits).
+__device__ __noinline__ void torch_cuda_topk_order(const float *lg, const float *noise_row, int nb, int top,
+                                                   uint64_t taken, float *vals, int *idxs) {
+    constexpr int P = 32;
+    float key[P];
+    int val[P];
+    bool ok[P];
+    const float kth = vals[top - 1];
+    int n = 0;
+    for (int pass = 0; pass < 2; ++pass)
+        for (int e = 0; e < nb; ++e) {
+            if (!((taken >> e) & 1ull)) continue;
+            const float v = noise_row ? lg[e] + noise_row[e] : lg[e];
+            if (pass == 0 ? v > kth : v == kth) { key[n] = v; val[n] = e; ok[n] = true; ++n; }
+        }
+    for (int i = n; i < P; ++i) { key[i] = 0.0f; val[i] = -1; ok[i] = false; }
+    auto cmpx = [&](int a, int b, bool dir) {
+        const bool greater = ok[a] && ok[b] && key[a] > key[b];
+        const bool swap = greater || !ok[b];
+        if (swap == dir) {
+            const float tk = key[a]; key[a] = key[b]; key[b] = tk;
+            const int tv = val[a]; val[a] = val[b]; val[b] = tv;
+            const bool to = ok[a]; ok[a] = ok[b]; ok[b] = to;
+        }
+    };
+    for (int size = 2; size < P; size <<= 1)
+        for (int stride = size >> 1; stride > 0; stride >>= 1)
+            for (int i = 0; i < P / 2; ++i) {
+                const int pos = 2 * i - (i & (stride - 1));
+                cmpx(pos, pos + stride, (i & (size >> 1)) != 0);
+            }
+    for (int stride = P >> 1; stride > 0; stride >>= 1)
+        for (int i = 0; i < P / 2; ++i) {
+            const int pos = 2 * i - (i & (stride - 1));
+            cmpx(pos, pos + stride, false);
+        }
+    for (int k = 0; k < top; ++k) { vals[k] = key[k]; idxs[k] = val[k]; }
+}
+
 template <int CDT, int R>
 __device__ void head_epilogue(const float *sA, float *sLogit, float *sWu, const typename Elem<CDT>::T *w_up,
                               int r_rt, int nb, int top, int64_t tok0, int64_t ntok,
@@ -413,7 +533,7 @@ __device__ void head_epilogue(const float *sA, float *sLogit, float *sWu, const 
         float m = -INFINITY;
         for (int e = 0; e < nb; ++e) m = fmaxf(m, lg[e]);
         // top-k by repeated selection: strictly greater wins, so among equal
-        // values the lower block index is taken first.
+        // values the lower block ids are the ones selected at the k-th boundary.
         float vals[kMaxTop];
         int idxs[kMaxTop];
         uint64_t taken = 0;
@@ -429,6 +549,12 @@ __device__ void head_epilogue(const float *sA, float *sLogit, float *sWu, const 
             vals[k] = best;
             idxs[k] = bi;
         }
+        // Output order as torch's CUDA topk gives it (the reference's eager
+        // router on the GPU, model.py:214). Distinct values come out by value
+        // descending whatever the method; only equal selected values need care.
+        bool tied = false;
+        for (int a = 1; a < top; ++a) tied |= vals[a] == vals[a - 1];
+        if (tied) torch_cuda_topk_order(lg, noise ? noise + t * nb : nullptr, nb, top, taken, vals, idxs);
         // softmax over the clean logits, exp once per logit (in place)
         float ssum = 0.0f;
         for (int e = 0; e < nb; ++e) {
@@ -598,17 +724,17 @@ route_head_simt_kernel(const typename Elem<CDT>::T *__restrict__ hq,
 }
 
 // ============================================================ host launchers
-template <int XDT, int CDT, int MODE>
+template <int XDT, int CDT>
 static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st,
                                  const ScanShard &sh) {
     using XT = typename Elem<XDT>::T;
-    const size_t smem = kScanStages * kScanRows * kScanCols * sizeof(XT);
-    auto k = route_scan_kernel<XDT, CDT, MODE>;
+    const size_t smem = seq_scan_smem<XDT>();
+    auto k = route_scan_kernel<XDT, CDT>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((d + kScanCols - 1) / kScanCols, B);
-    k<<<grid, kScanCols, smem, st>>>(static_cast<const XT *>(x),
-                                     static_cast<typename Elem<CDT>::T *>(hq), S, d, sh); count_launch();
+    dim3 grid((d + kSeqCols - 1) / kSeqCols, B);
+    k<<<grid, kSeqThreads, smem, st>>>(static_cast<const XT *>(x),
+                                       static_cast<typename Elem<CDT>::T *>(hq), S, d, sh); count_launch();
     return cudaGetLastError();
 }
 
@@ -631,13 +757,11 @@ cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, 
         if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_par_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st, sh);
         return cudaErrorInvalidValue;
     }
-#define MOM_SCAN_CASE(X, C, M)                                                       \
-    if (xdt == X && cdt == C && mode == M) return launch_scan_t<X, C, M>(x, hq, B, S, d, st, sh);
-    MOM_SCAN_CASE(MOM_BF16, MOM_BF16, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_F32, MOM_BF16, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_F32, MOM_F32, MOM_SCAN_FP32)
-    MOM_SCAN_CASE(MOM_BF16, MOM_F32, MOM_SCAN_FP32)
-#undef MOM_SCAN_CASE
+    if (mode != MOM_SCAN_FP32) return cudaErrorInvalidValue;
+    if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_t<MOM_BF16, MOM_BF16>(x, hq, B, S, d, st, sh);
+    if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_t<MOM_F32, MOM_BF16>(x, hq, B, S, d, st, sh);
+    if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st, sh);
+    if (xdt == MOM_BF16 && cdt == MOM_F32) return launch_scan_t<MOM_BF16, MOM_F32>(x, hq, B, S, d, st, sh);
     return cudaErrorInvalidValue;
 }
 

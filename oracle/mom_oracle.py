@@ -135,11 +135,62 @@ def softmax64(a, axis=-1) -> np.ndarray:
     return e / e.sum(axis=axis, keepdims=True)
 
 
-def topk_lowest_index(values, k: int):
-    """Top-k along the last axis: value descending, ties -> lower index first."""
-    v = np.asarray(values)
-    order = np.argsort(-v.astype(f64), axis=-1, kind="stable")[..., :k]
-    return order.astype(np.int64), np.take_along_axis(v, order, axis=-1)
+def _bitonic32_desc(keys):
+    """Order of a list of at most 32 keys under a 32-wide Batcher bitonic
+    network sorting descending whose compare-exchange also exchanges equal
+    keys, unused slots last: how torch's CUDA topk sorts its gathered
+    selection. Returns the permutation of positions."""
+    P = 32
+    key = list(keys) + [None] * (P - len(keys))
+    pos_of = list(range(len(keys))) + [-1] * (P - len(keys))
+
+    def cmpx(a, b, direction):
+        va, vb = key[a] is not None, key[b] is not None
+        swap = (va and vb and key[a] > key[b]) or not vb
+        if swap == direction:
+            key[a], key[b] = key[b], key[a]
+            pos_of[a], pos_of[b] = pos_of[b], pos_of[a]
+
+    size = 2
+    while size < P:
+        stride = size // 2
+        while stride:
+            for i in range(P // 2):
+                cmpx(2 * i - (i & (stride - 1)), 2 * i - (i & (stride - 1)) + stride, (i & (size // 2)) != 0)
+            stride //= 2
+        size *= 2
+    stride = P // 2
+    while stride:
+        for i in range(P // 2):
+            cmpx(2 * i - (i & (stride - 1)), 2 * i - (i & (stride - 1)) + stride, False)
+        stride //= 2
+    return pos_of[:len(keys)]
+
+
+def topk_cuda_order(values, k: int):
+    """Top-k along the last axis as torch's CUDA topk returns it (the
+    reference's eager router on a GPU, model.py:214): the k largest values,
+    the lower indices winning among equal values at the k-th boundary. Without
+    equal selected values the order is by value descending. With them, torch
+    gathers (values above the k-th, index order) then (values equal to it,
+    index order) and sorts that with a 32-wide bitonic network that exchanges
+    equal keys; that network is run here (tests/golden/topk_cuda_ties.npz holds
+    torch.topk outputs recorded on a B200 that pin this rule). torch's CPU
+    topk follows no index rule on ties."""
+    v = np.asarray(values).astype(f64)
+    chosen = np.argsort(-v, axis=-1, kind="stable")[..., :k].astype(np.int64)
+    flat_v = v.reshape(-1, v.shape[-1])
+    flat_c = chosen.reshape(-1, k)
+    for r in range(flat_c.shape[0]):
+        sel = flat_v[r, flat_c[r]]
+        if k > 1 and np.any(sel[1:] == sel[:-1]):
+            kth = sel[-1]
+            cols = np.sort(flat_c[r])
+            gathered = [int(c) for c in cols if flat_v[r, c] > kth] + [int(c) for c in cols if flat_v[r, c] == kth]
+            perm = _bitonic32_desc([flat_v[r, c] for c in gathered])
+            flat_c[r] = [gathered[p] for p in perm]
+    chosen = flat_c.reshape(chosen.shape)
+    return chosen, np.take_along_axis(np.asarray(values), chosen, axis=-1)
 
 
 def router_forward(x, w_down, w_up, top_k: int, compute: str = "f32",
@@ -153,7 +204,7 @@ def router_forward(x, w_down, w_up, top_k: int, compute: str = "f32",
     logits = linear(a, w_up, compute).astype(f32)      # (B,S,nb), .float()
     probs = softmax64(logits).astype(f32)
     noisy = logits if noise is None else (logits + np.asarray(noise, f32)).astype(f32)
-    top_idx, top_vals = topk_lowest_index(noisy, top_k)
+    top_idx, top_vals = topk_cuda_order(noisy, top_k)
     gates = softmax64(top_vals).astype(f32)
     log_gates = np.log(np.maximum(gates.astype(f64), 1e-9)).astype(f32)
     return dict(h=h, hq=hq, z=z, a=a, logits=logits, noisy=noisy, probs=probs,

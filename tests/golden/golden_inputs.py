@@ -101,3 +101,62 @@ def scan_input(dtype_name: str):
     if dtype_name == "bf16":
         x = x.to(torch.bfloat16)
     return x
+
+
+# A small Naylis decoder (BASELINE config 3's architecture at reduced size):
+# 2 layers, d=256, 4 heads of 64, SwiGLU 512, vocab 512, bank 8 x 128 slots,
+# router rank 32, top-2, RoPE theta 5e5, RMSNorm eps 1e-5, tied LM head.
+DECODER = dict(B=2, S=256, vocab=512, d=256, ffn=512, layers=2, H=4, nb=8, bs=128, top=2, r=32,
+               rope_theta=500000.0, eps=1e-5, aux=0.01, seed=31)
+
+
+def decoder_param_shapes(geo: dict) -> list:
+    """(name, shape) of every parameter of the reference's NaylisLlamaForCausalLM
+    (model.py:350-470 with transformers' Llama modules), lm_head tied."""
+    d, f, r, nb, bs = geo["d"], geo["ffn"], geo["r"], geo["nb"], geo["bs"]
+    out = [("model.M_blocks", (nb, bs * d)), ("model.embed_tokens.weight", (geo["vocab"], d))]
+    for i in range(geo["layers"]):
+        p = f"model.layers.{i}."
+        out += [(p + "self_attn.q_proj.weight", (d, d)), (p + "self_attn.k_proj.weight", (d, d)),
+                (p + "self_attn.v_proj.weight", (d, d)), (p + "self_attn.o_proj.weight", (d, d)),
+                (p + "mlp.gate_proj.weight", (f, d)), (p + "mlp.up_proj.weight", (f, d)),
+                (p + "mlp.down_proj.weight", (d, f)), (p + "input_layernorm.weight", (d,)),
+                (p + "post_attention_layernorm.weight", (d,)), (p + "mom_norm.weight", (d,)),
+                (p + "mom.mom_scale", (1,)), (p + "mom.router_down.weight", (r, d)),
+                (p + "mom.router_up.weight", (nb, r)), (p + "mom.q_proj.weight", (d, d)),
+                (p + "mom.k_proj.weight", (d, d)), (p + "mom.v_proj.weight", (d, d)),
+                (p + "mom.o_proj.weight", (d, d))]
+    return out + [("model.norm.weight", (d,))]
+
+
+def decoder_state(geo: dict) -> dict:
+    """A deterministic parameter set for the decoder, in the reference's names:
+    matrices and the bank N(0, 0.02), norm weights 1 + N(0, 0.1), mom_scale 1
+    (so the memory read reaches the output), plus lm_head.weight tied to the
+    embedding. Drawn in decoder_param_shapes order from one CPU generator."""
+    torch = _torch()
+    g = torch.Generator().manual_seed(geo["seed"])
+    sd = {}
+    for name, shape in decoder_param_shapes(geo):
+        if name.endswith("mom_scale"):
+            sd[name] = torch.ones(shape)
+        elif len(shape) == 1:
+            sd[name] = 1.0 + 0.1 * torch.randn(shape, generator=g)
+        else:
+            sd[name] = 0.02 * torch.randn(shape, generator=g)
+    sd["lm_head.weight"] = sd["model.embed_tokens.weight"]
+    return sd
+
+
+def decoder_tokens(geo: dict):
+    torch = _torch()
+    g = torch.Generator().manual_seed(geo["seed"] + 1)
+    return torch.randint(0, geo["vocab"], (geo["B"], geo["S"]), generator=g)
+
+
+def state_digest(sd: dict) -> str:
+    h = hashlib.sha256()
+    for k in sorted(sd):
+        h.update(k.encode())
+        h.update(sd[k].contiguous().numpy().tobytes())
+    return h.hexdigest()

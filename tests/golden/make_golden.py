@@ -22,11 +22,16 @@ Cases:
   read_f32/bf16   read only (build_gate_bias + mom_attention_reference), with
                   gradients w.r.t. q, k, v and the gates.
   scan            prefix mean h at (2, 1024, 64), fp32 and bf16 input: SHA-256.
+  decoder_small   the reference's NaylisLlamaForCausalLM (2 layers, d=256,
+                  4x64 heads, SwiGLU 512, vocab 512, bank 8x128, top-2) under
+                  CPU bf16 autocast in training mode, Gumbel off: loss,
+                  gradient subsamples, logits subsample, every layer's routing.
+  decoder_small_f32  the same in fp32 (no autocast): pins oracle/decoder_oracle.py.
   cfg2_layer      BASELINE config 2 at full size (B=8, S=2048): layer
                   forward+backward under CPU bf16 autocast, Gumbel off. Stored:
                   every token's top-2 ids, every token's logit margin between
-                  its 2nd and 3rd block (0 = a tie), the logits of the tied
-                  tokens, and seeded
+                  its 2nd and 3rd block, the tokens with equal values among
+                  their top 3 logits with those logits, and seeded
                   subsamples of the output and of every gradient.
 """
 import argparse
@@ -134,7 +139,9 @@ def run_cfg2(model_mod):
     rng = np.random.default_rng(4321)
     res = dict(input_sha=np.array(gi.input_digest(inp)),
                top_idx=to_np(top_idx).astype(np.uint8), margin=to_np(margin))
-    ties = torch.nonzero(margin == 0).reshape(-1)
+    # tokens with two equal values anywhere among their top (k + 1) logits
+    top3 = srt[..., :geo["top"] + 1].reshape(-1, geo["top"] + 1)
+    ties = torch.nonzero((top3[:, 1:] == top3[:, :-1]).any(-1)).reshape(-1)
     res["tie_tokens"] = to_np(ties).astype(np.int64)
     res["tie_logits"] = to_np(logits.reshape(-1, geo["nb"])[ties])
     tensors = dict(out=out, dx=x.grad, dM_blocks=M.grad)
@@ -146,6 +153,57 @@ def run_cfg2(model_mod):
         res[name + "_idx"] = sub.astype(np.int64)
         res[name] = flat[sub]
         res[name + "_absmax"] = np.array(np.abs(flat).max())
+    return res
+
+
+def run_decoder(model_mod, autocast=True):
+    """The reference's NaylisLlamaForCausalLM (transformers Llama trunk, MoM
+    layers, tied head, aux loss) at golden_inputs.DECODER under CPU bf16
+    autocast, training mode without Gumbel noise: the loss and its gradient,
+    the logits, and every layer's routing."""
+    import torch
+    from transformers import LlamaConfig
+    geo = gi.DECODER
+    cfg = LlamaConfig(vocab_size=geo["vocab"], hidden_size=geo["d"], intermediate_size=geo["ffn"],
+                      num_hidden_layers=geo["layers"], num_attention_heads=geo["H"],
+                      num_key_value_heads=geo["H"], max_position_embeddings=geo["S"],
+                      rms_norm_eps=geo["eps"], rope_theta=geo["rope_theta"], attention_bias=False,
+                      tie_word_embeddings=True, attn_implementation="sdpa", use_cache=False)
+    model = model_mod.NaylisLlamaForCausalLM(cfg, mem_size=geo["nb"] * geo["bs"], mom_block_size=geo["bs"],
+                                             mom_top_blocks=geo["top"], mom_router_rank=geo["r"],
+                                             mom_aux_weight=geo["aux"])
+    sd = gi.decoder_state(geo)
+    missing, unexpected = model.load_state_dict(sd, strict=False)
+    assert not unexpected and all("rotary" in m for m in missing), (missing, unexpected)
+    moms = [m for m in model.modules() if isinstance(m, model_mod.MoMLayer)]
+    for m in moms:
+        m.noise_scale = 0.0
+    model.train()
+    ids = gi.decoder_tokens(geo)
+    with torch.autocast("cpu", dtype=torch.bfloat16, enabled=autocast):
+        out = model(input_ids=ids, labels=ids)
+    routing = np.stack([to_np(m.last_top_idx) for m in moms]).astype(np.int64) if moms[0].last_top_idx \
+        is not None else None
+    out.loss.backward()
+    res = dict(state_sha=np.array(gi.state_digest(sd)), loss=np.array(float(out.loss)))
+    rng = np.random.default_rng(77)
+    for name, p in model.named_parameters():
+        flat = to_np(p.grad).reshape(-1)
+        sub = np.sort(rng.choice(flat.size, size=min(flat.size, 2048), replace=False))
+        res["g_" + name + "_idx"] = sub.astype(np.int64)
+        res["g_" + name] = flat[sub]
+        res["g_" + name + "_absmax"] = np.array(np.abs(flat).max())
+    model.zero_grad(set_to_none=True)
+    with torch.no_grad(), torch.autocast("cpu", dtype=torch.bfloat16, enabled=autocast):
+        logits = model(input_ids=ids).logits
+    res["routing"] = np.stack([to_np(m.last_top_idx) for m in moms]).astype(np.int8)
+    flat = to_np(logits).reshape(-1)
+    sub = np.sort(rng.choice(flat.size, size=8192, replace=False))
+    res["logits_idx"] = sub.astype(np.int64)
+    res["logits"] = flat[sub]
+    res["logits_absmax"] = np.array(np.abs(flat).max())
+    if routing is not None:
+        assert np.array_equal(routing, res["routing"])
     return res
 
 
@@ -195,6 +253,8 @@ def main():
         "read_bf16": lambda: run_read(reference, "bf16"),
         "scan": lambda: run_scan(reference),
         "cfg2_layer": lambda: run_cfg2(model_mod),
+        "decoder_small": lambda: run_decoder(model_mod),
+        "decoder_small_f32": lambda: run_decoder(model_mod, autocast=False),
     }
     ap_cases = [c for c in args.cases.split(",") if c] if args.cases else list(cases)
     for name, fn in ((n, cases[n]) for n in ap_cases):

@@ -42,15 +42,20 @@ def test_prefix_mean_fp64_mode_bitwise_vs_reference(name):
     assert hashlib.sha256(h.numpy().tobytes()).hexdigest() == str(g[f"h_sha_{name}"])
 
 
+@pytest.mark.parametrize("shape", [(2, 2048, 1024), (3, 1000, 104), (1, 1, 40), (1, 65, 24), (2, 4097, 64)])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_prefix_mean_fp32_mode_bitwise_vs_torch_cuda(dtype):
+def test_prefix_mean_fp32_mode_bitwise_vs_torch_cuda(dtype, shape):
+    """fp32 mode = torch's CUDA cumsum divided by t+1, bit for bit; ragged
+    shapes cover partial column groups and partial row stages."""
     torch.manual_seed(0)
-    x = torch.randn(2, 2048, 1024).to(dtype)
+    x = (torch.randn(*shape) * torch.exp(torch.randn(*shape) * 3)).to(dtype)
     h = _prefix_mean_gpu(x, "fp32")
     xc = x.cuda()
-    ref = torch.cumsum(xc.float(), dim=1) / torch.arange(1, 2049, device="cuda",
+    ref = torch.cumsum(xc.float(), dim=1) / torch.arange(1, shape[1] + 1, device="cuda",
                                                           dtype=torch.float32).view(1, -1, 1)
     assert torch.equal(h, ref.cpu())
+    hb = _prefix_mean_gpu(x, "fp32", torch.bfloat16)
+    assert torch.equal(hb, ref.cpu().to(torch.bfloat16))
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
@@ -283,16 +288,16 @@ def test_router_backward_matches_oracle(compute, tol, r, nb, top):
 
 
 @pytest.mark.parametrize("compute", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("top", [1, 2, 3])
-def test_topk_tie_order_matches_torch_cuda(compute, top):
+@pytest.mark.parametrize("nb,top", [(8, 1), (8, 2), (8, 3), (8, 4), (32, 2), (32, 4), (32, 5)])
+def test_topk_tie_order_matches_torch_cuda(compute, nb, top):
     """torch.topk leaves the order of equal values to the implementation. On
     CUDA, the reference's eager router (model.py:214) runs torch's CUDA topk;
-    the kernel takes the lower block id first. With W_up = 0 the logits are
-    exactly 0 and the noisy logits equal the noise, which here takes values
-    in {1, 2, 3} only, so nearly every token has ties at the 1st/2nd and at
-    the k-th/(k+1)-th boundary. Indices must equal torch.topk's on this GPU."""
-    torch.manual_seed(11 + top)
-    B, S, d, r, nb = 4, 512, 64, 8, 8
+    the kernel reproduces its choice and order on ties. With W_up = 0 the
+    logits are exactly 0 and the noisy logits equal the noise, which here takes
+    values in {1, 2, 3} only, so nearly every token has ties at every boundary.
+    Indices must equal torch.topk's on this GPU, token for token."""
+    torch.manual_seed(11 + top + nb)
+    B, S, d, r = 4, 512, 64, 8
     x = torch.randn(B, S, d)
     w_down = torch.randn(r, d) * 0.1
     w_up = torch.zeros(nb, r)
@@ -307,6 +312,7 @@ def test_topk_tie_order_matches_torch_cuda(compute, top):
                             f"first: noise {noise.reshape(-1, nb)[mism.reshape(-1)][:3].tolist()}, "
                             f"kernel {got['top_idx'].reshape(-1, top)[mism.reshape(-1)][:3].tolist()}, "
                             f"torch {ref_i.reshape(-1, top)[mism.reshape(-1)][:3].tolist()}")
+    assert np.array_equal(got["top_idx"], O.topk_cuda_order(noise.numpy(), top)[0])
 
 
 def _torch_cuda_router(x, w_down, w_up, top, noise=None):

@@ -125,12 +125,39 @@ def test_suffix_scaled_sum_is_adjoint_of_prefix_mean():
     assert abs(lhs - rhs) < 1e-4 * max(1.0, abs(lhs))
 
 
-def test_topk_rule_lowest_index_on_ties():
+def test_topk_rule_matches_torch_cuda_on_ties():
+    """The oracle's tie rule is torch's CUDA topk as measured on B200 (the
+    rows below are cases recorded there): lower indices win at the k-th
+    boundary, equal values are listed by descending index."""
     v = np.array([[0.5, 1.0, 1.0, 1.0, 0.2, 1.0, 0.1, 0.0],
-                  [0.5, 1.0, 0.7, 0.7, 0.2, 0.7, 0.1, 0.0]], np.float32)
-    idx, vals = O.topk_lowest_index(v, 2)
-    assert idx.tolist() == [[1, 2], [1, 2]]
-    assert vals.tolist() == [[1.0, 1.0], [1.0, np.float32(0.7)]]
+                  [0.5, 1.0, 0.7, 0.7, 0.2, 0.7, 0.1, 0.0],
+                  [2, 3, 2, 3, 3, 2, 3, 1],
+                  [1, 2, 3, 2, 1, 3, 2, 2]], np.float32)
+    idx, vals = O.topk_cuda_order(v, 2)
+    assert idx.tolist() == [[2, 1], [1, 2], [3, 1], [5, 2]]
+    assert vals.tolist() == [[1.0, 1.0], [1.0, np.float32(0.7)], [3, 3], [3, 3]]
+    v3 = np.array([[2, 3, 3, 2, 2, 2, 1, 2], [1, 3, 2, 2, 2, 2, 2, 3], [3, 1, 2, 2, 3, 2, 1, 3]], np.float32)
+    assert O.topk_cuda_order(v3, 3)[0].tolist() == [[2, 1, 0], [7, 1, 2], [7, 4, 0]]
+
+
+def test_topk_rule_reproduces_recorded_torch_cuda_topk():
+    """torch.topk outputs recorded on a B200 (tests/golden/make_topk_ties.py)
+    over tie-heavy inputs, 8 / 16 / 32 columns, k = 1..8: the oracle's rule
+    gives the same indices in the same order on every row."""
+    path = os.path.join(GOLDEN, "topk_cuda_ties.npz")
+    if not os.path.exists(path):
+        pytest.skip("topk_cuda_ties.npz not recorded yet")
+    g = np.load(path)
+    rows = 0
+    for key in g.files:
+        if not key.startswith("v_"):
+            continue
+        v = g[key].astype(np.float32)
+        want = g[key.replace("v_", "i_")].astype(np.int64)
+        got = O.topk_cuda_order(v, want.shape[1])[0]
+        assert np.array_equal(got, want), key
+        rows += v.shape[0]
+    assert rows >= 6000
 
 
 def test_bf16_round_matches_torch():
@@ -139,3 +166,31 @@ def test_bf16_round_matches_torch():
     a = (rng.standard_normal(100000) * np.exp(rng.uniform(-20, 20, 100000))).astype(np.float32)
     ref = torch.from_numpy(a).to(torch.bfloat16).float().numpy()
     assert np.array_equal(O.bf16_round(a), ref)
+
+
+def test_decoder_oracle_matches_reference_fp32():
+    """oracle/decoder_oracle.py (the CPU restatement of the reference's decoder
+    training forward) against the reference's own NaylisLlamaForCausalLM in
+    fp32: loss to 1e-5 relative, gradients and logits to 1e-4 of their largest
+    magnitude, every layer's routing equal."""
+    import torch
+    import decoder_oracle as D
+    g = _load("decoder_small_f32")
+    geo = dict(gi.DECODER)
+    sd = gi.decoder_state(geo)
+    assert gi.state_digest(sd) == str(g["state_sha"])
+    p = {k: v.clone().requires_grad_(True) for k, v in sd.items() if k != "lm_head.weight"}
+    ids = gi.decoder_tokens(geo)
+    loss, stats = D.forward(ids, p, geo, labels=ids)
+    loss.backward()
+    assert abs(float(loss) - float(g["loss"])) <= 1e-5 * abs(float(g["loss"]))
+    routing = np.stack([idx.numpy() for _, idx in stats])
+    assert np.array_equal(routing.reshape(g["routing"].shape), g["routing"].astype(np.int64))
+    for name, t in p.items():
+        got = t.grad.reshape(-1).numpy()[g["g_" + name + "_idx"]]
+        err = np.abs(got - g["g_" + name]).max() / max(float(g["g_" + name + "_absmax"]), 1e-30)
+        assert err < 1e-4, (name, err)
+    with torch.no_grad():
+        logits, _ = D.forward(ids, p, geo)
+    got = logits.reshape(-1).numpy()[g["logits_idx"]]
+    assert np.abs(got - g["logits"]).max() / g["logits_absmax"] < 1e-4

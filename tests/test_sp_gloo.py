@@ -87,7 +87,7 @@ def _numpy_ops(w_down, w_up):
             act = O.round_to(np.tanh(z.astype(f64)), "f32")
             logits = O.linear(act, w_up, "f32").astype(f32)
             probs = O.softmax64(logits).astype(f32)
-            idx, vals = O.topk_lowest_index(logits, TOP)
+            idx, vals = O.topk_cuda_order(logits, TOP)
             gates = O.softmax64(vals).astype(f32)
             out = None
             if want_carry_out:
