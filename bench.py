@@ -502,7 +502,10 @@ def measure_kernels(layer, x, M, dout, dev, args):
     hd = d // H
     N = B * S
     lib = _lib.load()
-    st = torch.cuda.current_stream(dev).cuda_stream
+
+    def cur():   # the launching stream, looked up at call time (a capture switches it)
+        return torch.cuda.current_stream(dev).cuda_stream
+
     with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         probs, idx, gates = mk.mom_route(x, layer.router_down.weight, layer.router_up.weight, top)
         q = layer.q_proj(x).view(B, S, H, hd).contiguous()
@@ -523,6 +526,7 @@ def measure_kernels(layer, x, M, dout, dev, args):
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     def read_once():
+        st = cur()
         _lib.call("mom_bucket", idx.data_ptr(), _lib.I64, lg.data_ptr(), N, nb, top, plan.data_ptr(),
                   plan.numel(), st)
         _lib.call("mom_read_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), _lib.BF16, B, S, H, hd, nb,
@@ -544,21 +548,35 @@ def measure_kernels(layer, x, M, dout, dev, args):
     def route_once(mode=_lib.SCAN_MODES["fp32"]):
         _lib.call("mom_route_fwd", xb.data_ptr(), _lib.BF16, B, S, d, wd.data_ptr(), wu.data_ptr(),
                   _lib.BF16, r, nb, top, None, mode, probs_o.data_ptr(), idx_o.data_ptr(), _lib.I64,
-                  gates_o.data_ptr(), None, act_o.data_ptr(), rws.data_ptr(), rws.numel(), st)
+                  gates_o.data_ptr(), None, act_o.data_ptr(), rws.data_ptr(), rws.numel(), cur())
 
     def timed(fn, iters):
-        for _ in range(3):
+        """One call captured in a CUDA graph (the entry points only launch kernels
+        on the stream they are given), replayed per timed iteration after an L2
+        flush: the host's launch cost stays outside the events."""
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
             fn()
+        for _ in range(3):
+            graph.replay()
         times = []
         for i in range(iters):
             flush.fill_(float(i))
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record()
-            fn()
+            graph.replay()
             b.record()
             times.append((a, b))
         torch.cuda.synchronize()
+        del graph
         return sum(a.elapsed_time(b) for a, b in times) / iters
 
     iters = max(10, min(100, args.steps))

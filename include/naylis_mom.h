@@ -175,6 +175,29 @@ MOM_API int mom_read_bwd(const void *q, const void *k, const void *v, const void
                  const void *plan, const void *q_rows, void *dq, float *dk_acc, float *dv_acc,
                  float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ------------------------------------------------------------------ fp32 read
+ * The same read for fp32 activations (q, k, v, out, dout all fp32), computed with
+ * fp32 FMA throughout: the reference's fp32 read (mom_kernels/reference.py:14-61,
+ * held to 1e-5 in tests/test_parity.py:138-188), reached through the same door
+ * (mom_kernels/__init__.py:87-102) when the tensors are fp32. It runs on the
+ * block-split plan: build it with mom_bucket_split first (any top <= 8, repeated
+ * block ids summed as the reference's bias sums them). head_dim 16, 32, 64 or
+ * 128 (the reference's powers of two); any block size. lse is (B*S, H) fp32 in token order (saved for the backward).
+ * Workspace: mom_read_f32_workspace_size bytes, for either call. The backward
+ * zeroes and then accumulates dq (B*S x H*hd), dk, dv (L x H*hd) and dlog_gates
+ * (B*S x top), all fp32. */
+MOM_API size_t mom_read_f32_workspace_size(int64_t B, int64_t S, int64_t H, int64_t head_dim, int64_t top);
+MOM_API int mom_read_f32_fwd(const float *q, const float *k, const float *v, int64_t B, int64_t S, int64_t H,
+                             int64_t head_dim, int64_t num_blocks, int64_t block_size, int64_t top,
+                             const void *top_idx, int idx_dtype, const void *plan, float *out, float *lse,
+                             void *workspace, size_t workspace_bytes, void *stream);
+MOM_API int mom_read_f32_bwd(const float *q, const float *k, const float *v, const float *out,
+                             const float *dout, const float *lse, int64_t B, int64_t S, int64_t H,
+                             int64_t head_dim, int64_t num_blocks, int64_t block_size, int64_t top,
+                             const void *top_idx, int idx_dtype, const void *plan, float *dq, float *dk,
+                             float *dv, float *dlog_gates, void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 /* mom_read_bwd without a workspace argument: for callers that cannot allocate
  * device memory (a plugin whose host framework's caching allocator owns the
  * device, or an FFI caller with no device allocator). It has no counterpart

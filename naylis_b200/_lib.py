@@ -61,6 +61,11 @@ SIGNATURES = {
     "mom_read_split_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "mom_read_split_bwd": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                                   _i64, _i64, _vp, _int, _vp, _vp, _vp, _fp, _fp, _fp, _vp, _sz, _vp]),
+    "mom_read_f32_workspace_size": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "mom_read_f32_fwd": (_int, [_fp, _fp, _fp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _int, _vp, _fp,
+                                _fp, _vp, _sz, _vp]),
+    "mom_read_f32_bwd": (_int, [_fp, _fp, _fp, _fp, _fp, _fp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                _int, _vp, _fp, _fp, _fp, _fp, _vp, _sz, _vp]),
     "mom_read_bwd_noalloc_max_bytes": (_sz, []),
     "mom_read_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp]),

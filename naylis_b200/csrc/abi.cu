@@ -587,6 +587,90 @@ int mom_read_split_bwd(const void *q, const void *k, const void *v, const void *
     return MOM_OK;
 }
 
+// ------------------------------------------------------------------ fp32 read
+namespace {
+int check_f32_read(int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs, int64_t top) {
+    MOM_REQUIRE(B >= 0 && S >= 0 && B * S * top < (int64_t(1) << 31), "bad B, S");
+    MOM_REQUIRE(H > 0 && H <= 1024, "bad n_heads %lld", (long long)H);
+    if (hd != 16 && hd != 32 && hd != 64 && hd != 128)
+        return fail(MOM_ERR_UNSUPPORTED, "head_dim %lld: the fp32 read takes 16, 32, 64 or 128", (long long)hd);
+    MOM_REQUIRE(nb > 0 && nb <= 64 && top > 0 && top <= mom::kMaxTop && top <= nb, "bad (num_blocks, top)");
+    MOM_REQUIRE(bs > 0 && nb * bs < (int64_t(1) << 24), "bad block_size %lld", (long long)bs);
+    return MOM_OK;
+}
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+}  // namespace
+
+size_t mom_read_f32_workspace_size(int64_t B, int64_t S, int64_t H, int64_t hd, int64_t top) {
+    if (B < 0 || S < 0 || H < 0 || hd < 0 || top < 0) return 0;
+    const size_t M = static_cast<size_t>(B) * S * top;
+    const size_t fwd = align256(M * H * hd * 4) + align256(M * H * 4);
+    const size_t bwd = align256(static_cast<size_t>(B) * S * H * 4);
+    return fwd > bwd ? fwd : bwd;
+}
+
+int mom_read_f32_fwd(const float *q, const float *k, const float *v, int64_t B, int64_t S, int64_t H, int64_t hd,
+                     int64_t nb, int64_t bs, int64_t top, const void *top_idx, int idx_dtype, const void *plan,
+                     float *out, float *lse, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_f32_read(B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(q && k && v && top_idx && plan && out && lse && workspace, "null pointer argument");
+    MOM_REQUIRE(al16(q) && al16(k) && al16(v) && al16(out), "q, k, v and out must be 16-byte aligned");
+    const size_t need = mom_read_f32_workspace_size(B, S, H, hd, top);
+    if (workspace_bytes < need)
+        return fail(MOM_ERR_WORKSPACE, "fp32 read fwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    const int64_t N = B * S, M = N * top;
+    const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
+    mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+    P.rows_per_q = (int)top;
+    const int *iperm = reinterpret_cast<const int *>(static_cast<const char *>(plan) + split_iperm_offset(M, nb));
+    float *o_rows = static_cast<float *>(workspace);
+    float *lse_rows = reinterpret_cast<float *>(static_cast<char *>(workspace) + align256(M * H * hd * 4));
+    cudaError_t e = mom::launch_read_f32_fwd(q, k, v, N, (int)H, (int)hd, (int)nb, (int)bs, (int)top, L, P, top_idx,
+                                             idx_dtype == MOM_I64, iperm, o_rows, lse_rows, out, lse,
+                                             static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "read_f32_fwd");
+    return MOM_OK;
+}
+
+int mom_read_f32_bwd(const float *q, const float *k, const float *v, const float *out, const float *dout,
+                     const float *lse, int64_t B, int64_t S, int64_t H, int64_t hd, int64_t nb, int64_t bs,
+                     int64_t top, const void *top_idx, int idx_dtype, const void *plan, float *dq, float *dk,
+                     float *dv, float *dlog_gates, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_f32_read(B, S, H, hd, nb, bs, top);
+    if (rc) return rc;
+    MOM_REQUIRE(k && v && dk && dv, "null pointer argument");
+    MOM_REQUIRE(B * S == 0 || (q && out && dout && lse && top_idx && plan && dq && dlog_gates && workspace),
+                "null pointer argument");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(B * S == 0 || (al16(q) && al16(k) && al16(v) && al16(out) && al16(dout)),
+                "q, k, v, out and dout must be 16-byte aligned");
+    const size_t need = mom_read_f32_workspace_size(B, S, H, hd, top);
+    if (B * S > 0 && workspace_bytes < need)
+        return fail(MOM_ERR_WORKSPACE, "fp32 read bwd workspace %zu < %zu bytes", workspace_bytes, need);
+    if ((rc = check_current_device())) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int64_t N = B * S, M = N * top;
+    const size_t kv = sizeof(float) * static_cast<size_t>(nb) * bs * H * hd;
+    cudaError_t e = cudaMemsetAsync(dk, 0, kv, st);
+    if (e == cudaSuccess) e = cudaMemsetAsync(dv, 0, kv, st);
+    if (e == cudaSuccess && N > 0) e = cudaMemsetAsync(dq, 0, sizeof(float) * static_cast<size_t>(N) * H * hd, st);
+    if (e == cudaSuccess && N > 0) e = cudaMemsetAsync(dlog_gates, 0, sizeof(float) * static_cast<size_t>(N) * top, st);
+    if (e == cudaSuccess && N > 0) {
+        const mom::PlanLayout L = mom::plan_layout(M, nb, 1);
+        mom::PlanView P = mom::plan_view(const_cast<void *>(plan), L);
+        P.rows_per_q = (int)top;
+        e = mom::launch_read_f32_bwd(q, k, v, out, dout, lse, N, (int)H, (int)hd, (int)bs, (int)top, L, P, top_idx,
+                                     idx_dtype == MOM_I64, static_cast<float *>(workspace), dq, dk, dv, dlog_gates,
+                                     st);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "read_f32_bwd");
+    return MOM_OK;
+}
+
 // ------------------------------------------------- read backward, no allocation
 // mom_read_bwd_noalloc runs mom_read_bwd with its workspace (the per-row delta,
 // H x B*S fp32) in a fixed device array of this library instead of caller

@@ -154,4 +154,17 @@ cudaError_t launch_read_bwd(const void *q, const void *q_rows, const void *k, co
                             float *ws_delta, void *do_rows, cudaStream_t st, const float *row_w = nullptr,
                             const int *iperm = nullptr);
 
+// fp32 read (read_f32.cu) on a block-split plan (rows = (token, k) pairs, PlanView
+// over N*top rows with rows_per_q = top). Forward: o_rows (M x H x hd) and lse_rows
+// (M x H) scratch, out (N, H, hd) and lse (N, H) token order. Backward: delta (N x H)
+// scratch; dq, dk_acc, dv_acc and dlog_gates are accumulated into (zero them first).
+cudaError_t launch_read_f32_fwd(const float *q, const float *k, const float *v, int64_t N, int H, int hd, int nb,
+                                int bs, int top, const PlanLayout &L, const PlanView &P, const void *idx, int idx64,
+                                const int *iperm, float *o_rows, float *lse_rows, float *out, float *lse,
+                                cudaStream_t st);
+cudaError_t launch_read_f32_bwd(const float *q, const float *k, const float *v, const float *out, const float *dout,
+                                const float *lse, int64_t N, int H, int hd, int bs, int top, const PlanLayout &L,
+                                const PlanView &P, const void *idx, int idx64, float *delta, float *dq,
+                                float *dk_acc, float *dv_acc, float *dlog_gates, cudaStream_t st);
+
 }  // namespace mom

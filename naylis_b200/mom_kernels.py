@@ -69,25 +69,30 @@ def resolve_mode(device, dtype, *, head_dim=None) -> str:
     """Pick the kernel backend and check its contract (reference:
     mom_kernels/__init__.py:56-84). Only ``"sm100"`` is served here: bf16
     activations (bf16 tensors, or fp32 ones inside a CUDA bf16 autocast
-    region) and head_dim 64 or 128 on an sm_100 device; anything else raises
-    instead of falling back."""
+    region, which the read receives as bf16), fp32 activations outside
+    autocast (the fp32 read), and head_dim 64 or 128 on an sm_100 device;
+    anything else raises instead of falling back."""
     device_type = _device_type(device)
     if device_type != "cuda":
         raise RuntimeError(
             f"use_kernel=true: no sm100 kernel backend for device {device_type!r} "
             f"(the sm100 backend runs on CUDA B200 only).")
     dtype = _read_dtype(dtype)
-    if dtype != torch.bfloat16:
+    if dtype not in (torch.bfloat16, torch.float32):
         raise RuntimeError(
-            f"use_kernel=true (sm100) requires bf16 activations (the repo AMP dtype; "
-            f"fp16 is unsupported); got {dtype}.")
+            f"use_kernel=true (sm100) requires bf16 activations (the repo AMP dtype) or fp32 "
+            f"(the fp32 read); fp16 is unsupported; got {dtype}.")
     if head_dim is not None:
         if head_dim > 128 or head_dim & (head_dim - 1) != 0:
             raise RuntimeError(
                 f"use_kernel=true (sm100): head_dim {head_dim} must be a power of two <= 128.")
-        if head_dim not in (64, 128):
+        if dtype == torch.bfloat16 and head_dim not in (64, 128):
             raise RuntimeError(
-                f"use_kernel=true (sm100): the read kernels implement head_dim 64 and 128; "
+                f"use_kernel=true (sm100): the bf16 read kernels implement head_dim 64 and 128; "
+                f"got {head_dim}.")
+        if dtype == torch.float32 and head_dim not in (16, 32, 64, 128):
+            raise RuntimeError(
+                f"use_kernel=true (sm100): the fp32 read implements head_dim 16, 32, 64 and 128; "
                 f"got {head_dim}.")
     _lib.load()
     dev = torch.device(device) if not isinstance(device, torch.device) else device
@@ -219,13 +224,64 @@ class _MomReadSplitFunction(torch.autograd.Function):
         return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
 
 
+class _MomReadF32Function(torch.autograd.Function):
+    """The read for fp32 activations (csrc/read_f32.cu): fp32 FMA throughout, the
+    reference's fp32 results to ~1e-6. Runs on the block-split plan for any top;
+    saves q, k, v, out, the token-order log-sum-exp, the routing ids and the plan."""
+
+    @staticmethod
+    def forward(ctx, q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
+        B, S, H, hd = q_sh.shape
+        N, top = B * S, top_idx.shape[-1]
+        dev = q_sh.device
+        st = _stream(dev)
+        lib = _lib.load()
+        idx = top_idx.reshape(N, top)
+        if idx.dtype not in (torch.int64, torch.int32):
+            idx = idx.to(torch.int64)
+        idx = idx.contiguous()
+        idt = _lib.I64 if idx.dtype == torch.int64 else _lib.I32
+        lg = log_gates.reshape(N, top).to(torch.float32).contiguous()
+        plan = torch.empty(lib.mom_plan_split_size(N, num_blocks, top), dtype=torch.uint8, device=dev)
+        _lib.call("mom_bucket_split", idx.data_ptr(), idt, lg.data_ptr(), N, num_blocks, top, plan.data_ptr(),
+                  plan.numel(), st)
+        out = torch.empty_like(q_sh)
+        lse = torch.empty((N, H), dtype=torch.float32, device=dev)
+        ws = torch.empty(lib.mom_read_f32_workspace_size(B, S, H, hd, top), dtype=torch.uint8, device=dev)
+        _lib.call("mom_read_f32_fwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), B, S, H, hd, num_blocks,
+                  block_size, top, idx.data_ptr(), idt, plan.data_ptr(), out.data_ptr(), lse.data_ptr(),
+                  ws.data_ptr(), ws.numel(), st)
+        ctx.save_for_backward(q_sh, k, v, out, lse, idx, plan)
+        ctx.meta = (num_blocks, block_size, top, idt)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q_sh, k, v, out, lse, idx, plan = ctx.saved_tensors
+        num_blocks, block_size, top, idt = ctx.meta
+        B, S, H, hd = q_sh.shape
+        dev = q_sh.device
+        st = _stream(dev)
+        lib = _lib.load()
+        dout = dout.to(torch.float32).contiguous()
+        dq = torch.empty_like(q_sh)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        dlg = torch.empty((B, S, top), dtype=torch.float32, device=dev)
+        ws = torch.empty(lib.mom_read_f32_workspace_size(B, S, H, hd, top), dtype=torch.uint8, device=dev)
+        _lib.call("mom_read_f32_bwd", q_sh.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                  lse.data_ptr(), B, S, H, hd, num_blocks, block_size, top, idx.data_ptr(), idt, plan.data_ptr(),
+                  dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(), ws.data_ptr(), ws.numel(), st)
+        return dq, dk, dv, None, dlg, None, None
+
+
 def _check_read_args(q_sh, k, v, top_idx, top_gates, num_blocks, block_size, mode):
     if mode != MODE:
         raise RuntimeError(f"unknown kernel mode {mode!r} (this door serves {MODE!r})")
     if k.dim() != 2 or v.dim() != 2:
         raise RuntimeError("sm100 mom_read: shared K/V (L, D) only, got batched inputs")
-    if q_sh.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
-        raise RuntimeError(f"sm100 mom_read requires bf16 activations, got q {q_sh.dtype}, "
+    if not (q_sh.dtype == k.dtype == v.dtype) or q_sh.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError(f"sm100 mom_read requires bf16 (or all-fp32) activations, got q {q_sh.dtype}, "
                            f"k {k.dtype}, v {v.dtype}")
     if not q_sh.is_cuda:
         raise RuntimeError("sm100 mom_read: tensors must be on a CUDA device")
@@ -243,8 +299,13 @@ def _check_read_args(q_sh, k, v, top_idx, top_gates, num_blocks, block_size, mod
 def _read_apply(q_sh, k, v, top_idx, log_gates, num_blocks, block_size):
     B, S = q_sh.shape[:2]
     top = top_idx.shape[-1]
+    if q_sh.dtype == torch.float32:
+        fn = _MomReadF32Function
     # routing sets beyond what the set bucketing holds: the block-split read
-    fn = _MomReadFunction if _lib.load().mom_plan_size(B * S, int(num_blocks), top) else _MomReadSplitFunction
+    elif _lib.load().mom_plan_size(B * S, int(num_blocks), top):
+        fn = _MomReadFunction
+    else:
+        fn = _MomReadSplitFunction
     return fn.apply(q_sh.contiguous(), k.contiguous(), v.contiguous(), top_idx, log_gates, int(num_blocks),
                     int(block_size))
 
@@ -263,7 +324,8 @@ def mom_read(q_sh, k, v, top_idx, top_gates, *, num_blocks, block_size, mode: st
 
     q_sh (B, S, H, hd) bf16; shared k, v (L, H*hd) bf16 with L = num_blocks *
     block_size; top_idx (B, S, top) block ids; top_gates (B, S, top) fp32
-    softmax gates. Returns (B, S, H, hd). Gradients reach q, k, v and the
+    softmax gates. Returns (B, S, H, hd). With q, k, v all fp32 the read runs
+    in fp32 (csrc/read_f32.cu) and returns fp32. Gradients reach q, k, v and the
     gates (through log(clamp_min(g, 1e-9)), as the reference bias does).
     """
     _check_read_args(q_sh, k, v, top_idx, top_gates, num_blocks, block_size, mode)

@@ -12,9 +12,14 @@ common shift) and the probabilities (taken from the clean logits) do not
 change. Without that, a bf16 logit tie or 1-ulp near-tie that the CPU and the
 GPU round differently would send a token to another block, and the output of
 that token would differ by the whole read, not by rounding. What is left is
-bf16 arithmetic in a different order: loss within 1e-2 relative, logits and
-every gradient within 2e-2 of the largest magnitude (the reference's bf16
-bar, tests/test_parity.py:477-490).
+bf16 arithmetic in a different order through two layers: loss within 1e-2
+relative and logits within 2e-2 of the largest magnitude (the reference's
+bf16 bar, tests/test_parity.py:477-490); gradients within 1e-1 of their
+largest magnitude, the bar the reference holds its own kernels' gradients to
+at real shape (mom_kernels/probe.py:107-154: 2e-1 absolute). The tight check
+is the fp32 run: the same model with the fp32 read, fp32 GEMMs (TF32 off) and
+fp32 attention against the reference's fp32 golden (decoder_small_f32.npz):
+loss within 1e-5 relative, logits and every gradient within 1e-4.
 """
 import os
 
@@ -27,6 +32,7 @@ from conftest import GOLDEN
 
 pytestmark = pytest.mark.gpu
 TOL = 2e-2
+GRAD_TOL_BF16 = 1e-1
 SHIFT = 0.25
 
 
@@ -60,9 +66,9 @@ def _pin_routing(monkeypatch, routing, nb):
     monkeypatch.setattr(mk, "gumbel_noise", shift)
 
 
-def test_decoder_matches_reference_golden(monkeypatch):
+def _check_against_golden(monkeypatch, golden, bf16):
     geo = gi.DECODER
-    g = np.load(os.path.join(GOLDEN, "decoder_small.npz"))
+    g = np.load(os.path.join(GOLDEN, golden))
     model, sd = _model()
     assert gi.state_digest(sd) == str(g["state_sha"])
     dev = torch.device("cuda")
@@ -71,24 +77,38 @@ def test_decoder_matches_reference_golden(monkeypatch):
         m.noise_scale = 1.0
     _pin_routing(monkeypatch, g["routing"], geo["nb"])
     ids = gi.decoder_tokens(geo).to(dev)
-    with torch.autocast("cuda", dtype=torch.bfloat16):
-        loss = model(ids, labels=ids)
-    loss.backward()
-    torch.cuda.synchronize()
-    assert abs(float(loss) - float(g["loss"])) <= 1e-2 * abs(float(g["loss"])), (float(loss), float(g["loss"]))
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        with torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
+            loss = model(ids, labels=ids)
+        loss.backward()
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16, enabled=bf16):
+            logits = model(ids)
+        torch.cuda.synchronize()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    loss_tol, logit_tol, grad_tol = (1e-2, TOL, GRAD_TOL_BF16) if bf16 else (1e-5, 1e-4, 1e-4)
+    assert abs(float(loss) - float(g["loss"])) <= loss_tol * abs(float(g["loss"])), (float(loss), float(g["loss"]))
     errs = {}
     for name, p in model.named_parameters():
         got = p.grad.float().reshape(-1).cpu().numpy()[g["g_" + name + "_idx"]]
         errs[name] = float(np.abs(got - g["g_" + name]).max() / max(float(g["g_" + name + "_absmax"]), 1e-30))
-    bad = {k: v for k, v in errs.items() if v >= TOL}
-    assert not bad, bad
-
-    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
-        logits = model(ids)
+    bad = {k: v for k, v in errs.items() if v >= grad_tol}
+    assert not bad, (bad, errs)
     routing = np.stack([m.last_top_idx.cpu().numpy() for m in model.mom_layers()])
     assert np.array_equal(np.sort(routing, -1), np.sort(g["routing"].astype(np.int64), -1))
     got = logits.float().reshape(-1).cpu().numpy()[g["logits_idx"]]
-    assert float(np.abs(got - g["logits"]).max() / g["logits_absmax"]) < TOL
+    assert float(np.abs(got - g["logits"]).max() / g["logits_absmax"]) < logit_tol
+    return errs
+
+
+def test_decoder_matches_reference_golden(monkeypatch):
+    _check_against_golden(monkeypatch, "decoder_small.npz", bf16=True)
+
+
+def test_decoder_matches_reference_golden_fp32(monkeypatch):
+    _check_against_golden(monkeypatch, "decoder_small_f32.npz", bf16=False)
 
 
 def test_decoder_trains_one_step_with_fused_adamw():

@@ -60,6 +60,40 @@ def test_layer_matches_reference_golden_bf16():
     assert abs(got["d_mom_scale"][0] - g["d_mom_scale"][0]) <= TOL * abs(g["d_mom_scale"][0])
 
 
+def test_layer_matches_reference_golden_fp32():
+    """The whole layer in fp32 (no autocast): fp32 router head, the fp32 read,
+    fp32 projections (TF32 off), against the reference's fp32 layer: output
+    and every gradient within 1e-5 of the largest magnitude (the reference's
+    fp32 bar), routing bitwise."""
+    geo = gi.SMALL_F32
+    g = np.load(os.path.join(GOLDEN, "small_f32.npz"))
+    layer, inp = _layer(geo)
+    assert gi.input_digest(inp) == str(g["input_sha"])
+    dev = torch.device("cuda")
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        layer = layer.to(dev).train()
+        layer.noise_scale = 0.0
+        x = inp["x"].to(dev).requires_grad_(True)
+        M = inp["M"].to(dev).requires_grad_(True)
+        out = layer(x, M)
+        out.backward(gi.upstream_grad(geo).to(dev))
+        torch.cuda.synchronize()
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert out.dtype == torch.float32
+    assert np.array_equal(layer.last_top_idx.cpu().numpy().reshape(g["top_idx"].shape), g["top_idx"])
+    got = {"out": out.detach().cpu().numpy(), "dx": x.grad.cpu().numpy(), "dM_blocks": M.grad.cpu().numpy()}
+    for name, p in layer.named_parameters():
+        got["d_" + name.replace(".weight", "")] = p.grad.cpu().numpy()
+    keys = ["out", "dx", "dM_blocks", "d_router_down", "d_router_up", "d_q_proj", "d_k_proj", "d_v_proj",
+            "d_o_proj"]
+    errs = {k: O.scaled_err(got[k], g[k]) for k in keys}
+    assert all(e < 1e-5 for e in errs.values()), errs
+    assert abs(got["d_mom_scale"][0] - g["d_mom_scale"][0]) <= 1e-5 * abs(g["d_mom_scale"][0])
+
+
 def test_layer_config2_full_size_matches_reference_golden(monkeypatch):
     """BASELINE config 2 at the benchmarked size (B=8 x S=2048, d=1024, 16x64
     heads, bank 8x128, rank 32, top-2) against what the reference's own
@@ -192,8 +226,9 @@ def test_resolve_mode_contract_on_gpu():
     from naylis_b200 import mom_kernels as mk
     assert mk.resolve_mode("cuda", torch.bfloat16, head_dim=64) == "sm100"
     assert mk.resolve_mode(torch.device("cuda", 0), torch.bfloat16, head_dim=128) == "sm100"
+    assert mk.resolve_mode("cuda", torch.float32, head_dim=64) == "sm100"   # the fp32 read
     with pytest.raises(RuntimeError):
-        mk.resolve_mode("cuda", torch.float32, head_dim=64)
+        mk.resolve_mode("cuda", torch.float16, head_dim=64)
     # the reference resolves with x.dtype (model.py:164-165): fp32 inside a bf16
     # autocast region, where the q projection, and so the read, runs in bf16
     with torch.autocast("cuda", dtype=torch.bfloat16):

@@ -265,3 +265,42 @@ def test_read_rejects_contract_violations():
         mk.mom_read(q.bfloat16(), k, k, idx, g, num_blocks=3, block_size=64)   # L mismatch
     with pytest.raises(RuntimeError):
         mk.mom_read(q.bfloat16(), k.unsqueeze(0), k.unsqueeze(0), idx, g, num_blocks=4, block_size=64)
+
+
+# ---------------------------------------------------------------------- fp32 read
+TOL_F32 = 1e-5     # the reference's fp32 bar (tests/test_parity.py:138-188)
+
+
+def _to_f32(*ts):
+    return tuple(t.float() for t in ts)
+
+
+def test_read_f32_matches_reference_golden():
+    """fp32 q, k, v through the door take the fp32 read; against what the
+    reference's own build_gate_bias + SDPA read gave in fp32."""
+    geo = gi.READ
+    g = np.load(os.path.join(GOLDEN, "read_f32.npz"))
+    q, k, v, top, gates, dout = gi.read_inputs(geo, "f32")
+    got = _run_gpu(q, k, v, top, gates, dout, geo["nb"], geo["bs"])
+    _compare(got, {k_: g[k_] for k_ in ("out", "dq", "dk", "dv", "dgates")}, tol=TOL_F32)
+
+
+@pytest.mark.parametrize("case", [
+    dict(B=2, S=300, H=4, hd=64, nb=8, bs=128, top=2, seed=51),            # config-2 geometry
+    dict(B=1, S=200, H=2, hd=128, nb=8, bs=128, top=2, seed=52),           # head_dim 128
+    dict(B=2, S=129, H=2, hd=64, nb=4, bs=64, top=1, seed=53),             # top-1
+    dict(B=1, S=157, H=3, hd=64, nb=6, bs=48, top=3, seed=54, dup=True),   # top-3, block 48, repeated ids
+    dict(B=1, S=130, H=2, hd=128, nb=32, bs=128, top=4, seed=55),          # top-4 of 32
+])
+def test_read_f32_matches_oracle(case):
+    case = dict(case)
+    dup = case.pop("dup", False)
+    seed = case.pop("seed")
+    q, k, v, idx, gates, dout = _mk(**case, seed=seed, dup=dup)
+    g = torch.Generator().manual_seed(seed + 100)      # fp32 values, not bf16-rounded ones
+    q = q.float() + 1e-3 * torch.randn(q.shape, generator=g)
+    k, v, dout = _to_f32(k, v, dout)
+    got = _run_gpu(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    assert got["out"].dtype == np.float32
+    ref = _oracle(q, k, v, idx, gates, dout, case["nb"], case["bs"])
+    _compare(got, ref, tol=TOL_F32)
