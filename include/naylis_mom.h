@@ -198,6 +198,48 @@ MOM_API int mom_read_f32_bwd(const float *q, const float *k, const float *v, con
                              float *dv, float *dlog_gates, void *workspace, size_t workspace_bytes,
                              void *stream);
 
+/* ------------------------------------------------------------------ decoder trunk
+ * bf16 kernels of the trunk around the MoM layer (the caller that BASELINE
+ * config 3 trains), with the rounding points of the reference's trunk under bf16
+ * autocast (transformers' Llama apply_rotary_pos_emb and LlamaMLP, wired by
+ * model.py:280-348).
+ * mom_rope_qkv_fwd: qkv (B*S, 3*H*hd) bf16, the fused q/k/v projection output
+ * ([q | k | v], H heads of hd each); cos, sin (S, hd) fp32 -> q, k with the
+ * rotary embedding (fp32 math, bf16 result) and v, each (B, S, H, hd) bf16
+ * (attention takes them as (B, H, S, hd) views). mom_rope_qkv_bwd: the attention
+ * gradients dq, dk, dv in that (B, S, H, hd) layout -> dqkv (B*S, 3*H*hd) bf16. Replace the reference's
+ * q/k/v views, apply_rotary_pos_emb and their autograd. */
+MOM_API int mom_rope_qkv_fwd(const void *qkv, const float *cos, const float *sin, int64_t B, int64_t S, int64_t H,
+                             int64_t head_dim, void *q, void *k, void *v, void *stream);
+MOM_API int mom_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, const float *cos, const float *sin,
+                             int64_t B, int64_t S, int64_t H, int64_t head_dim, void *dqkv, void *stream);
+/* mom_swiglu_fwd: gu (N, 2f) bf16, the fused gate/up projection output ([g | u])
+ * -> h = bf16(bf16(silu(g)) * u), (N, f). mom_swiglu_bwd: dh (N, f), gu ->
+ * dgu (N, 2f) = [dg | du], bf16. Replace LlamaMLP's act_fn(gate) * up and its
+ * autograd. f even, buffers 4-byte aligned. */
+MOM_API int mom_swiglu_fwd(const void *gu, int64_t N, int64_t f, void *h, void *stream);
+MOM_API int mom_swiglu_bwd(const void *dh, const void *gu, int64_t N, int64_t f, void *dgu, void *stream);
+
+/* mom_add_rmsnorm_fwd: the residual add before a Llama RMSNorm fused with it:
+ * x_out = x + s * delta (s = *delta_scale when given, else 1; delta bf16 or fp32,
+ * or NULL for no add), then y = w * (x_out * rsqrt(mean(x_out^2) + eps)) as bf16
+ * (y_bf16, the next projection's input) and, when y_f32 is not NULL, fp32 (the
+ * MoM router's input); rstd (N) per token for the backward. x, x_out, w fp32;
+ * rows of d = a multiple of 32 up to 2048. Replaces the reference's
+ * `residual + hidden_states` and LlamaRMSNorm (model.py:319-345) and, with
+ * delta_scale = mom_scale, `mom_scale * o_proj(out)` (model.py:239).
+ * mom_add_rmsnorm_bwd: from dy (bf16 and/or fp32) and dx_in (the residual
+ * stream's own gradient, may be NULL): dx (fp32), ddelta = s * dx in delta's
+ * dtype, dw (d, zeroed then accumulated) and, when ddelta_scale is given,
+ * d s = sum(dx * delta). */
+MOM_API int mom_add_rmsnorm_fwd(const float *x, const void *delta, int delta_dtype, const float *delta_scale,
+                                const float *w, int64_t N, int64_t d, double eps, float *x_out, void *y_bf16,
+                                float *y_f32, float *rstd, void *stream);
+MOM_API int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, const void *delta,
+                                int delta_dtype, const float *delta_scale, const void *dy_bf16, const float *dy_f32,
+                                const float *dx_in, int64_t N, int64_t d, float *dx, void *ddelta, float *dw,
+                                float *ddelta_scale, void *stream);
+
 /* mom_read_bwd without a workspace argument: for callers that cannot allocate
  * device memory (a plugin whose host framework's caching allocator owns the
  * device, or an FFI caller with no device allocator). It has no counterpart

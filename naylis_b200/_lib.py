@@ -66,6 +66,13 @@ SIGNATURES = {
                                 _fp, _vp, _sz, _vp]),
     "mom_read_f32_bwd": (_int, [_fp, _fp, _fp, _fp, _fp, _fp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                                 _int, _vp, _fp, _fp, _fp, _fp, _vp, _sz, _vp]),
+    "mom_rope_qkv_fwd": (_int, [_vp, _fp, _fp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "mom_rope_qkv_bwd": (_int, [_vp, _vp, _vp, _fp, _fp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "mom_swiglu_fwd": (_int, [_vp, _i64, _i64, _vp, _vp]),
+    "mom_swiglu_bwd": (_int, [_vp, _vp, _i64, _i64, _vp, _vp]),
+    "mom_add_rmsnorm_fwd": (_int, [_fp, _vp, _int, _fp, _fp, _i64, _i64, _c.c_double, _fp, _vp, _fp, _fp, _vp]),
+    "mom_add_rmsnorm_bwd": (_int, [_fp, _fp, _fp, _vp, _int, _fp, _vp, _fp, _fp, _i64, _i64, _fp, _vp, _fp, _fp,
+                                   _vp]),
     "mom_read_bwd_noalloc_max_bytes": (_sz, []),
     "mom_read_bwd_noalloc": (_int, [_vp, _vp, _vp, _vp, _vp, _fp, _int, _i64, _i64, _i64, _i64, _i64,
                                     _i64, _i64, _vp, _vp, _vp, _fp, _fp, _fp, _vp]),

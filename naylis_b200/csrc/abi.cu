@@ -671,6 +671,99 @@ int mom_read_f32_bwd(const float *q, const float *k, const float *v, const float
     return MOM_OK;
 }
 
+// ------------------------------------------------------------------ decoder trunk
+int mom_rope_qkv_fwd(const void *qkv, const float *cosv, const float *sinv, int64_t B, int64_t S, int64_t H,
+                     int64_t hd, void *q, void *k, void *v, void *stream) {
+    MOM_REQUIRE(B >= 0 && S >= 0 && H > 0 && hd > 0 && hd % 2 == 0 && hd <= 256, "bad rope geometry");
+    MOM_REQUIRE(B * S * H * hd < (int64_t(1) << 40), "rope size out of range");
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(qkv && cosv && sinv && q && k && v, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_rope_qkv_fwd(qkv, cosv, sinv, (int)B, (int)S, (int)H, (int)hd, q, k, v,
+                                             static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "rope_qkv_fwd");
+}
+
+int mom_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, const float *cosv, const float *sinv, int64_t B,
+                     int64_t S, int64_t H, int64_t hd, void *dqkv, void *stream) {
+    MOM_REQUIRE(B >= 0 && S >= 0 && H > 0 && hd > 0 && hd % 2 == 0 && hd <= 256, "bad rope geometry");
+    if (B * S == 0) return MOM_OK;
+    MOM_REQUIRE(dq && dk && dv && cosv && sinv && dqkv, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_rope_qkv_bwd(dq, dk, dv, cosv, sinv, (int)B, (int)S, (int)H, (int)hd, dqkv,
+                                             static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "rope_qkv_bwd");
+}
+
+int mom_swiglu_fwd(const void *gu, int64_t N, int64_t f, void *h, void *stream) {
+    MOM_REQUIRE(N >= 0 && f > 0 && f % 2 == 0 && f < (int64_t(1) << 30), "bad swiglu geometry");
+    if (N == 0) return MOM_OK;
+    MOM_REQUIRE(gu && h, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(gu) & 3) == 0 && (reinterpret_cast<uintptr_t>(h) & 3) == 0,
+                "gu and h must be 4-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_swiglu_fwd(gu, N, (int)f, h, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "swiglu_fwd");
+}
+
+int mom_swiglu_bwd(const void *dh, const void *gu, int64_t N, int64_t f, void *dgu, void *stream) {
+    MOM_REQUIRE(N >= 0 && f > 0 && f % 2 == 0 && f < (int64_t(1) << 30), "bad swiglu geometry");
+    if (N == 0) return MOM_OK;
+    MOM_REQUIRE(dh && gu && dgu, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(dh) & 3) == 0 && (reinterpret_cast<uintptr_t>(gu) & 3) == 0 &&
+                    (reinterpret_cast<uintptr_t>(dgu) & 3) == 0,
+                "dh, gu and dgu must be 4-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_swiglu_bwd(dh, gu, N, (int)f, dgu, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "swiglu_bwd");
+}
+
+namespace {
+int delta_code(int delta_dtype, const void *delta) {
+    if (!delta) return 0;
+    if (delta_dtype == MOM_BF16) return 1;
+    if (delta_dtype == MOM_F32) return 2;
+    return -1;
+}
+}  // namespace
+
+int mom_add_rmsnorm_fwd(const float *x, const void *delta, int delta_dtype, const float *delta_scale, const float *w,
+                        int64_t N, int64_t d, double eps, float *x_out, void *y_bf16, float *y_f32, float *rstd,
+                        void *stream) {
+    const int ddt = delta_code(delta_dtype, delta);
+    MOM_REQUIRE(ddt >= 0, "delta dtype must be F32 or BF16");
+    MOM_REQUIRE(N >= 0 && d > 0 && d % 32 == 0 && d <= 2048, "d must be a multiple of 32 up to 2048");
+    if (N == 0) return MOM_OK;
+    MOM_REQUIRE(x && w && x_out && y_bf16 && rstd, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_add_rmsnorm_fwd(x, delta, ddt, delta_scale, w, N, (int)d, static_cast<float>(eps), x_out,
+                                                y_bf16, y_f32, rstd, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "add_rmsnorm_fwd");
+}
+
+int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, const void *delta, int delta_dtype,
+                        const float *delta_scale, const void *dy_bf16, const float *dy_f32, const float *dx_in,
+                        int64_t N, int64_t d, float *dx, void *ddelta, float *dw, float *ddelta_scale, void *stream) {
+    const int ddt = delta_code(delta_dtype, delta);
+    MOM_REQUIRE(ddt >= 0, "delta dtype must be F32 or BF16");
+    MOM_REQUIRE(N >= 0 && d > 0 && d % 32 == 0 && d <= 2048, "d must be a multiple of 32 up to 2048");
+    MOM_REQUIRE(w && dw, "null pointer argument");
+    MOM_REQUIRE(N == 0 || (x_new && rstd && dx && (dy_bf16 || dy_f32) && (ddt == 0 || ddelta)),
+                "null pointer argument");
+    MOM_REQUIRE(!ddelta_scale || (ddt != 0 && delta_scale), "a scale gradient needs a scaled delta");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_add_rmsnorm_bwd(x_new, rstd, w, delta, ddt, delta_scale, dy_bf16, dy_f32, dx_in, N,
+                                                (int)d, dx, ddelta, dw, ddelta_scale,
+                                                static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "add_rmsnorm_bwd");
+}
+
 // ------------------------------------------------- read backward, no allocation
 // mom_read_bwd_noalloc runs mom_read_bwd with its workspace (the per-row delta,
 // H x B*S fp32) in a fixed device array of this library instead of caller

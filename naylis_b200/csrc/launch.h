@@ -167,4 +167,23 @@ cudaError_t launch_read_f32_bwd(const float *q, const float *k, const float *v, 
                                 const PlanView &P, const void *idx, int idx64, float *delta, float *dq,
                                 float *dk_acc, float *dv_acc, float *dlog_gates, cudaStream_t st);
 
+// Decoder trunk (trunk.cu): rotary embedding of the fused q/k/v projection output
+// (B*S, 3*H*hd) bf16 into (B, S, H, hd) bf16 q / k / v, and back; SwiGLU of the fused
+// gate/up output (N, 2f) bf16, and back.
+cudaError_t launch_rope_qkv_fwd(const void *qkv, const float *cosv, const float *sinv, int B, int S, int H, int hd,
+                                void *q, void *k, void *v, cudaStream_t st);
+cudaError_t launch_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, const float *cosv, const float *sinv,
+                                int B, int S, int H, int hd, void *dqkv, cudaStream_t st);
+cudaError_t launch_swiglu_fwd(const void *gu, int64_t N, int f, void *h, cudaStream_t st);
+cudaError_t launch_swiglu_bwd(const void *dh, const void *gu, int64_t N, int f, void *dgu, cudaStream_t st);
+// Residual add + RMSNorm (ddt: 0 no delta, 1 bf16, 2 fp32 delta; dscale: optional
+// device scalar multiplying delta); y16 bf16 always, y32 fp32 optional; rstd per token.
+cudaError_t launch_add_rmsnorm_fwd(const float *x, const void *delta, int ddt, const float *dscale, const float *w,
+                                   int64_t N, int d, float eps, float *x_out, void *y16, float *y32, float *rstd,
+                                   cudaStream_t st);
+cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, const void *delta, int ddt,
+                                   const float *dscale_in, const void *dy16, const float *dy32, const float *dx_in,
+                                   int64_t N, int d, float *dx, void *ddelta, float *dw, float *dscale,
+                                   cudaStream_t st);
+
 }  // namespace mom

@@ -1,0 +1,385 @@
+// Fused bf16 kernels for the decoder trunk around the MoM read (the caller
+// BASELINE config 3 trains): rotary embedding of the fused q/k/v projection and
+// the SwiGLU gate, forward and backward, each one pass over HBM.
+//
+// Numerics follow what the reference's trunk computes under bf16 autocast
+// (transformers' Llama: apply_rotary_pos_emb and LlamaMLP, as wired by
+// model.py:280-348 of the reference):
+//   RoPE     q, k come out of the projection in bf16; the rotation runs in fp32
+//            with fp32 cos / sin (t * cos + rotate_half(t) * sin, each product
+//            rounded, then the sum), and attention receives the result rounded
+//            to bf16. Backward: dt = dout * cos + (rotate_half^T of dout * sin),
+//            in fp32 from the bf16 attention gradient, rounded to bf16.
+//   SwiGLU   a = bf16(silu(g)) with silu(x) = x / (1 + exp(-x)) in fp32, then
+//            h = bf16(a * u). Backward: da = bf16(dh * u), du = bf16(dh * a),
+//            dg = bf16(da * s * (1 + g * (1 - s))) with s = 1 / (1 + exp(-g)).
+// No fused multiply-add is allowed to merge the rounded steps (explicit _rn
+// intrinsics).
+#include <algorithm>
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace mom {
+namespace {
+
+__device__ __forceinline__ float bf(uint16_t b) { return bf16_bits_to_f32(b); }
+__device__ __forceinline__ uint16_t tobf(float f) { return f32_to_bf16_bits(f); }
+
+// Forward. qkv: (B*S, 3*H*hd) bf16, rows = tokens, columns [q | k | v], each H
+// heads of hd. cos/sin: (S, hd) fp32. Out: q, k, v as (B, S, H, hd) bf16 (the
+// token-major layout attention takes as a (B, H, S, hd) view).
+// One thread per (token, head, pair i < hd/2): dims i and i + hd/2.
+__global__ void __launch_bounds__(256)
+rope_qkv_fwd_kernel(const uint16_t *__restrict__ qkv, const float *__restrict__ cosv, const float *__restrict__ sinv,
+                    int B, int S, int H, int hd, uint16_t *__restrict__ q, uint16_t *__restrict__ k,
+                    uint16_t *__restrict__ v) {
+    const int half = hd / 2;
+    const int64_t total = static_cast<int64_t>(B) * S * H * half;
+    const int64_t d3 = 3LL * H * hd;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i % half);
+        const int64_t th = i / half;
+        const int h = static_cast<int>(th % H);
+        const int64_t tok = th / H;
+        const int s = static_cast<int>(tok % S);
+        const uint16_t *row = qkv + tok * d3 + static_cast<int64_t>(h) * hd;
+        const float c1 = cosv[static_cast<int64_t>(s) * hd + p], c2 = cosv[static_cast<int64_t>(s) * hd + p + half];
+        const float s1 = sinv[static_cast<int64_t>(s) * hd + p], s2 = sinv[static_cast<int64_t>(s) * hd + p + half];
+        const int64_t o = (tok * H + h) * hd;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {   // q, then k
+            const uint16_t *src = row + static_cast<int64_t>(w) * H * hd;
+            const float x1 = bf(src[p]), x2 = bf(src[p + half]);
+            // out[p] = x1*cos - x2*sin ; out[p+half] = x2*cos + x1*sin
+            const float y1 = __fadd_rn(__fmul_rn(x1, c1), __fmul_rn(-x2, s1));
+            const float y2 = __fadd_rn(__fmul_rn(x2, c2), __fmul_rn(x1, s2));
+            uint16_t *dst = (w == 0 ? q : k) + o;
+            dst[p] = tobf(y1);
+            dst[p + half] = tobf(y2);
+        }
+        const uint16_t *vs = row + 2LL * H * hd;
+        v[o + p] = vs[p];
+        v[o + p + half] = vs[p + half];
+    }
+}
+
+// Backward: dq, dk, dv (B, S, H, hd) bf16 -> dqkv (B*S, 3*H*hd) bf16.
+__global__ void __launch_bounds__(256)
+rope_qkv_bwd_kernel(const uint16_t *__restrict__ dq, const uint16_t *__restrict__ dk, const uint16_t *__restrict__ dv,
+                    const float *__restrict__ cosv, const float *__restrict__ sinv, int B, int S, int H, int hd,
+                    uint16_t *__restrict__ dqkv) {
+    const int half = hd / 2;
+    const int64_t total = static_cast<int64_t>(B) * S * H * half;
+    const int64_t d3 = 3LL * H * hd;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i % half);
+        const int64_t th = i / half;
+        const int h = static_cast<int>(th % H);
+        const int64_t tok = th / H;
+        const int s = static_cast<int>(tok % S);
+        uint16_t *row = dqkv + tok * d3 + static_cast<int64_t>(h) * hd;
+        const float c1 = cosv[static_cast<int64_t>(s) * hd + p], c2 = cosv[static_cast<int64_t>(s) * hd + p + half];
+        const float s1 = sinv[static_cast<int64_t>(s) * hd + p], s2 = sinv[static_cast<int64_t>(s) * hd + p + half];
+        const int64_t o = (tok * H + h) * hd;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const uint16_t *g = (w == 0 ? dq : dk) + o;
+            const float g1 = bf(g[p]), g2 = bf(g[p + half]);
+            // dx1 = g1*cos1 + g2*sin2 ; dx2 = g2*cos2 - g1*sin1
+            const float d1 = __fadd_rn(__fmul_rn(g1, c1), __fmul_rn(g2, s2));
+            const float d2 = __fadd_rn(__fmul_rn(g2, c2), -__fmul_rn(g1, s1));
+            uint16_t *dst = row + static_cast<int64_t>(w) * H * hd;
+            dst[p] = tobf(d1);
+            dst[p + half] = tobf(d2);
+        }
+        uint16_t *dvd = row + 2LL * H * hd;
+        dvd[p] = dv[o + p];
+        dvd[p + half] = dv[o + p + half];
+    }
+}
+
+__device__ __forceinline__ float silu_f(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
+
+// gu: (N, 2f) bf16 rows [g | u] -> h (N, f) bf16. Two columns per thread.
+__global__ void __launch_bounds__(256)
+swiglu_fwd_kernel(const uint32_t *__restrict__ gu, int64_t N, int f, uint32_t *__restrict__ h) {
+    const int fp = f / 2;
+    const int64_t total = N * fp;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / fp;
+        const int c = static_cast<int>(i - t * fp);
+        const uint32_t gw = gu[t * 2 * fp + c], uw = gu[t * 2 * fp + fp + c];
+        float r[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float g = j ? __uint_as_float(gw & 0xFFFF0000u) : __uint_as_float(gw << 16);
+            const float u = j ? __uint_as_float(uw & 0xFFFF0000u) : __uint_as_float(uw << 16);
+            const float a = bf(tobf(silu_f(g)));
+            r[j] = __fmul_rn(a, u);
+        }
+        h[t * fp + c] = pack_bf16x2(r[0], r[1]);
+    }
+}
+
+// dh (N, f) bf16, gu (N, 2f) -> dgu (N, 2f) bf16 rows [dg | du].
+__global__ void __launch_bounds__(256)
+swiglu_bwd_kernel(const uint32_t *__restrict__ dh, const uint32_t *__restrict__ gu, int64_t N, int f,
+                  uint32_t *__restrict__ dgu) {
+    const int fp = f / 2;
+    const int64_t total = N * fp;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / fp;
+        const int c = static_cast<int>(i - t * fp);
+        const uint32_t gw = gu[t * 2 * fp + c], uw = gu[t * 2 * fp + fp + c], dw = dh[t * fp + c];
+        float dg[2], du[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float g = j ? __uint_as_float(gw & 0xFFFF0000u) : __uint_as_float(gw << 16);
+            const float u = j ? __uint_as_float(uw & 0xFFFF0000u) : __uint_as_float(uw << 16);
+            const float d = j ? __uint_as_float(dw & 0xFFFF0000u) : __uint_as_float(dw << 16);
+            const float a = bf(tobf(silu_f(g)));
+            const float da = bf(tobf(__fmul_rn(d, u)));
+            du[j] = __fmul_rn(d, a);
+            const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)));
+            dg[j] = __fmul_rn(__fmul_rn(da, sg), __fadd_rn(1.0f, __fmul_rn(g, __fsub_rn(1.0f, sg))));
+        }
+        dgu[t * 2 * fp + c] = pack_bf16x2(dg[0], dg[1]);
+        dgu[t * 2 * fp + fp + c] = pack_bf16x2(du[0], du[1]);
+    }
+}
+
+int grid_of(int64_t work) { return static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 16)); }
+
+// ------------------------------------------------------------------ residual add + RMSNorm
+// x_new = x + scale * delta (the sublayer's output added to the fp32 residual
+// stream; scale is a device scalar or absent), then the Llama RMSNorm of x_new:
+// y = w * (x_new * rsqrt(mean(x_new^2) + eps)), returned as bf16 (the next GEMM's
+// input) and, when asked, as fp32 (the MoM router's input). A warp per token,
+// d / 32 values per lane in registers; r = rsqrt(...) saved per token.
+constexpr int kNormWarps = 8;
+
+template <int DDT>   // delta: 0 none, 1 bf16, 2 fp32
+__device__ __forceinline__ float load_delta(const void *delta, int64_t i) {
+    if (DDT == 1) return bf16_bits_to_f32(static_cast<const uint16_t *>(delta)[i]);
+    if (DDT == 2) return static_cast<const float *>(delta)[i];
+    return 0.0f;
+}
+
+template <int DDT, int VPL>
+__global__ void __launch_bounds__(32 * kNormWarps)
+add_rmsnorm_fwd_kernel(const float *__restrict__ x, const void *__restrict__ delta, const float *__restrict__ dscale,
+                       const float *__restrict__ w, int64_t N, int d, float eps, float *__restrict__ x_out,
+                       uint16_t *__restrict__ y16, float *__restrict__ y32, float *__restrict__ rstd) {
+    const int lane = threadIdx.x & 31;
+    const float sc = (DDT != 0 && dscale) ? *dscale : 1.0f;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5); t < N;
+         t += static_cast<int64_t>(gridDim.x) * kNormWarps) {
+        const int64_t base = t * d;
+        float v[VPL];
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            float a = 0.0f;
+            if (c < d) {
+                a = x[base + c];
+                if (DDT != 0) {
+                    float dd = load_delta<DDT>(delta, base + c);
+                    if (dscale) dd = __fmul_rn(sc, dd);
+                    a = __fadd_rn(a, dd);
+                }
+                x_out[base + c] = a;
+            }
+            v[j] = a;
+            ss = __fmaf_rn(a, a, ss);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps));
+        if (lane == 0) rstd[t] = r;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c < d) {
+                const float yv = __fmul_rn(w[c], __fmul_rn(v[j], r));
+                y16[base + c] = f32_to_bf16_bits(yv);
+                if (y32) y32[base + c] = yv;
+            }
+        }
+    }
+}
+
+// Backward of add_rmsnorm. dy = dy16 (+ dy32), g = dy * w, xh = x_new * r:
+//   d(x_new) = dx_in + r * (g - xh * mean(g * xh))      (dx_in: the residual's own gradient)
+//   dx = d(x_new), d(delta) = scale * d(x_new), dw += dy * xh, dscale += sum d(x_new) * delta
+// dw / dscale are reduced per CTA in shared memory and added with one atomic each.
+template <int DDT, int VPL>
+__global__ void __launch_bounds__(32 * kNormWarps)
+add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict__ rstd, const float *__restrict__ w,
+                       const void *__restrict__ delta, const float *__restrict__ dscale_in,
+                       const uint16_t *__restrict__ dy16, const float *__restrict__ dy32,
+                       const float *__restrict__ dx_in, int64_t N, int d, float *__restrict__ dx,
+                       void *__restrict__ ddelta, float *__restrict__ dw, float *__restrict__ dscale) {
+    extern __shared__ float sdw[];                  // [d] + [1]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int c = threadIdx.x; c <= d; c += blockDim.x) sdw[c] = 0.0f;
+    __syncthreads();
+    const float sc = (DDT != 0 && dscale_in) ? *dscale_in : 1.0f;
+    float acc_w[VPL];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) acc_w[j] = 0.0f;
+    float acc_s = 0.0f;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kNormWarps + warp; t < N;
+         t += static_cast<int64_t>(gridDim.x) * kNormWarps) {
+        const int64_t base = t * d;
+        const float r = rstd[t];
+        float xh[VPL], g[VPL];
+        float dot = 0.0f;
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            xh[j] = 0.0f;
+            g[j] = 0.0f;
+            if (c < d) {
+                float dyv = dy16 ? bf16_bits_to_f32(dy16[base + c]) : 0.0f;
+                if (dy32) dyv += dy32[base + c];
+                xh[j] = x_new[base + c] * r;
+                g[j] = dyv * w[c];
+                acc_w[j] = fmaf(dyv, xh[j], acc_w[j]);
+                dot = fmaf(g[j], xh[j], dot);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float mean = dot / static_cast<float>(d);
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) {
+            const int c = lane + 32 * j;
+            if (c < d) {
+                float gx = r * (g[j] - xh[j] * mean);
+                if (dx_in) gx += dx_in[base + c];
+                dx[base + c] = gx;
+                if (DDT == 1) {
+                    static_cast<uint16_t *>(ddelta)[base + c] = f32_to_bf16_bits(dscale_in ? sc * gx : gx);
+                    if (dscale) acc_s = fmaf(gx, bf16_bits_to_f32(static_cast<const uint16_t *>(delta)[base + c]), acc_s);
+                } else if (DDT == 2) {
+                    static_cast<float *>(ddelta)[base + c] = dscale_in ? sc * gx : gx;
+                    if (dscale) acc_s = fmaf(gx, static_cast<const float *>(delta)[base + c], acc_s);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+        const int c = lane + 32 * j;
+        if (c < d) atomicAdd(&sdw[c], acc_w[j]);
+    }
+    if (DDT != 0 && dscale) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc_s += __shfl_xor_sync(0xffffffffu, acc_s, o);
+        if (lane == 0) atomicAdd(&sdw[d], acc_s);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < d; c += blockDim.x) atomicAdd(dw + c, sdw[c]);
+    if (DDT != 0 && dscale && threadIdx.x == 0) atomicAdd(dscale, sdw[d]);
+}
+
+}  // namespace
+
+cudaError_t launch_rope_qkv_fwd(const void *qkv, const float *cosv, const float *sinv, int B, int S, int H, int hd,
+                                void *q, void *k, void *v, cudaStream_t st) {
+    const int64_t work = static_cast<int64_t>(B) * S * H * (hd / 2);
+    if (work == 0) return cudaSuccess;
+    rope_qkv_fwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint16_t *>(qkv), cosv, sinv, B, S, H, hd,
+                                                       static_cast<uint16_t *>(q), static_cast<uint16_t *>(k),
+                                                       static_cast<uint16_t *>(v));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, const float *cosv, const float *sinv,
+                                int B, int S, int H, int hd, void *dqkv, cudaStream_t st) {
+    const int64_t work = static_cast<int64_t>(B) * S * H * (hd / 2);
+    if (work == 0) return cudaSuccess;
+    rope_qkv_bwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint16_t *>(dq),
+                                                       static_cast<const uint16_t *>(dk),
+                                                       static_cast<const uint16_t *>(dv), cosv, sinv, B, S, H, hd,
+                                                       static_cast<uint16_t *>(dqkv));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_fwd(const void *gu, int64_t N, int f, void *h, cudaStream_t st) {
+    const int64_t work = N * (f / 2);
+    if (work == 0) return cudaSuccess;
+    swiglu_fwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint32_t *>(gu), N, f,
+                                                     static_cast<uint32_t *>(h));
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu_bwd(const void *dh, const void *gu, int64_t N, int f, void *dgu, cudaStream_t st) {
+    const int64_t work = N * (f / 2);
+    if (work == 0) return cudaSuccess;
+    swiglu_bwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint32_t *>(dh),
+                                                     static_cast<const uint32_t *>(gu), N, f,
+                                                     static_cast<uint32_t *>(dgu));
+    count_launch();
+    return cudaGetLastError();
+}
+
+// d must be a multiple of 32 and at most 32 * 64 (values per lane in registers).
+cudaError_t launch_add_rmsnorm_fwd(const float *x, const void *delta, int ddt, const float *dscale, const float *w,
+                                   int64_t N, int d, float eps, float *x_out, void *y16, float *y32, float *rstd,
+                                   cudaStream_t st) {
+    if (N == 0) return cudaSuccess;
+    if (d % 32 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
+    const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 8));
+    auto out16 = static_cast<uint16_t *>(y16);
+#define MOM_NORM_F(DDT, VPL)                                                                                   \
+    add_rmsnorm_fwd_kernel<DDT, VPL><<<blocks, 32 * kNormWarps, 0, st>>>(x, delta, dscale, w, N, d, eps, x_out, \
+                                                                         out16, y32, rstd)
+    const int vpl = d / 32;
+    if (vpl <= 32) {
+        if (ddt == 0) MOM_NORM_F(0, 32); else if (ddt == 1) MOM_NORM_F(1, 32); else MOM_NORM_F(2, 32);
+    } else {
+        if (ddt == 0) MOM_NORM_F(0, 64); else if (ddt == 1) MOM_NORM_F(1, 64); else MOM_NORM_F(2, 64);
+    }
+#undef MOM_NORM_F
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, const void *delta, int ddt,
+                                   const float *dscale_in, const void *dy16, const float *dy32, const float *dx_in,
+                                   int64_t N, int d, float *dx, void *ddelta, float *dw, float *dscale,
+                                   cudaStream_t st) {
+    if (d % 32 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(dw, 0, sizeof(float) * d, st);
+    if (e == cudaSuccess && dscale) e = cudaMemsetAsync(dscale, 0, sizeof(float), st);
+    if (e != cudaSuccess) return e;
+    if (N == 0) return cudaSuccess;
+    const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 2));
+    const size_t smem = sizeof(float) * (d + 1);
+    auto g16 = static_cast<const uint16_t *>(dy16);
+#define MOM_NORM_B(DDT, VPL)                                                                                     \
+    add_rmsnorm_bwd_kernel<DDT, VPL><<<blocks, 32 * kNormWarps, smem, st>>>(x_new, rstd, w, delta, dscale_in, g16, \
+                                                                            dy32, dx_in, N, d, dx, ddelta, dw,  \
+                                                                            dscale)
+    const int vpl = d / 32;
+    if (vpl <= 32) {
+        if (ddt == 0) MOM_NORM_B(0, 32); else if (ddt == 1) MOM_NORM_B(1, 32); else MOM_NORM_B(2, 32);
+    } else {
+        if (ddt == 0) MOM_NORM_B(0, 64); else if (ddt == 1) MOM_NORM_B(1, 64); else MOM_NORM_B(2, 64);
+    }
+#undef MOM_NORM_B
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace mom

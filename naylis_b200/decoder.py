@@ -22,10 +22,16 @@ reference checkpoint loads with ``load_state_dict``.
 
 The trunk runs on torch's CUDA kernels (cuBLAS GEMMs, the flash attention
 backend of scaled_dot_product_attention); the MoM router and read run on this
-package's sm_100a kernels. Two layout choices differ from a module-by-module
+package's sm_100a kernels. Layout choices that differ from a module-by-module
 port: q/k/v and gate/up each run as ONE GEMM over their concatenated weights
-(wider N per tensor-core launch; the weights stay separate parameters), and the
-rotary embedding tables are built once per forward for all layers.
+(wider N per tensor-core launch; the weights stay separate parameters); in bf16
+the rotary embedding, the SwiGLU gate and every residual add with the RMSNorm
+after it are fused kernels (csrc/trunk.cu) with the reference's rounding
+points: the rotation writes q/k/v straight into the token-major layout
+attention reads, the add + norm writes the fp32 residual stream and the bf16
+input of the next projection in one pass, and the layer's mom_scale factor
+rides on the add that follows the memory read. The rotary tables are built
+once per forward for all layers.
 """
 from __future__ import annotations
 
@@ -37,6 +43,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 import torch.utils.checkpoint
 
+from . import trunk
 from .model import MoMLayer
 
 
@@ -113,10 +120,15 @@ class SelfAttention(nn.Module):
     def forward(self, x, cos, sin):
         B, S, d = x.shape
         w = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), dim=0)
-        qkv = F.linear(x, w).view(B, S, 3, self.n_heads, self.head_dim)
-        q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
-        q = apply_rope(q, cos, sin)
-        k = apply_rope(k, cos, sin)
+        qkv = F.linear(x, w)
+        if qkv.is_cuda and qkv.dtype == torch.bfloat16:
+            # fused rotary embedding into attention's layout (csrc/trunk.cu)
+            q, k, v = trunk.rope_qkv(qkv, cos, sin, self.n_heads)
+        else:
+            qkv = qkv.view(B, S, 3, self.n_heads, self.head_dim)
+            q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+            q = apply_rope(q, cos, sin)
+            k = apply_rope(k, cos, sin)
         o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
         return self.o_proj(o.transpose(1, 2).reshape(B, S, d))
 
@@ -131,6 +143,8 @@ class SwiGLU(nn.Module):
 
     def forward(self, x):
         gu = F.linear(x, torch.cat((self.gate_proj.weight, self.up_proj.weight), dim=0))
+        if gu.is_cuda and gu.dtype == torch.bfloat16:
+            return self.down_proj(trunk.swiglu(gu))      # fused (csrc/trunk.cu)
         g, u = gu.chunk(2, dim=-1)
         return self.down_proj(F.silu(g) * u)
 
@@ -158,6 +172,20 @@ class DecoderLayer(nn.Module):
         x = x + self.mom(self.mom_norm(x), M_blocks)
         return x + self._ckpt(lambda h: self.mlp(self.post_attention_layernorm(h)), x)
 
+    def forward_fused(self, x, pending, pending_scale, M_blocks, cos, sin):
+        """bf16 path: each residual add runs inside the RMSNorm that follows it
+        (csrc/trunk.cu add_rmsnorm). x is the residual stream before `pending`,
+        the previous sublayer's output (times pending_scale), is added; returns
+        the stream and this layer's MLP output, still to be added."""
+        eps = self.input_layernorm.eps
+        x, y = trunk.add_rmsnorm(x, pending, self.input_layernorm.weight, eps, scale=pending_scale)
+        a = self.self_attn(y, cos, sin)
+        x, y16, y32 = trunk.add_rmsnorm(x, a, self.mom_norm.weight, eps, want_f32=True)
+        o = self.mom.forward_unscaled(y32, M_blocks, x_lowp=y16)
+        # mom_scale * o_proj(read) folded into the add (model.py:239 of the reference)
+        x, y = trunk.add_rmsnorm(x, o, self.post_attention_layernorm.weight, eps, scale=self.mom.mom_scale)
+        return x, self.mlp(y)
+
 
 class NaylisModel(nn.Module):
     def __init__(self, cfg: NaylisConfig):
@@ -174,6 +202,14 @@ class NaylisModel(nn.Module):
     def forward(self, input_ids):
         x = self.embed_tokens(input_ids)
         cos, sin = rope_tables(input_ids.shape[1], self.cfg.head_dim, self.cfg.rope_theta, x.device)
+        fused = (x.is_cuda and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda")
+                 and torch.get_autocast_dtype("cuda") == torch.bfloat16 and not self.cfg.grad_ckpt)
+        if fused:
+            pending = None
+            for layer in self.layers:
+                x, pending = layer.forward_fused(x, pending, None, self.M_blocks, cos, sin)
+            _, y = trunk.add_rmsnorm(x, pending, self.norm.weight, self.norm.eps)
+            return y
         for layer in self.layers:
             x = layer(x, self.M_blocks, cos, sin)
         return self.norm(x)

@@ -74,6 +74,17 @@ class MoMLayer(nn.Module):
     def forward(self, x, M_blocks):
         """x (B, S, d_model), M_blocks (num_blocks, block_size * d_model) ->
         mom_scale * o_proj(read) (B, S, d_model), fp32 when mom_scale is."""
+        out = self.forward_unscaled(x, M_blocks)
+        if torch.result_type(self.mom_scale, out) == torch.float32:
+            return mom_kernels.mom_scale(out, self.mom_scale)
+        return self.mom_scale * out
+
+    def forward_unscaled(self, x, M_blocks, x_lowp=None):
+        """o_proj(read) before the mom_scale factor, for a caller that folds the
+        factor into the residual add that follows (the decoder's fused add +
+        RMSNorm). x feeds the router (its prefix scan sees x's own values);
+        x_lowp, when given, is the same activations already in bf16 for the q
+        projection."""
         mode = self._resolve(x)
         B, S, _ = x.shape
         noise = None
@@ -87,16 +98,13 @@ class MoMLayer(nn.Module):
         if self.training:
             self.last_router_probs = probs.reshape(-1, self.num_blocks)
             self.last_top_idx = top_idx.reshape(-1, self.top_blocks)
+        xq = x if x_lowp is None else x_lowp
         if self.mom_grad_ckpt and self.training and torch.is_grad_enabled():
             # the read holds no RNG draw, so its recompute is exact
-            out = torch.utils.checkpoint.checkpoint(
-                self._read, x, top_idx, log_gates, M_blocks, mode,
+            return torch.utils.checkpoint.checkpoint(
+                self._read, xq, top_idx, log_gates, M_blocks, mode,
                 use_reentrant=False, preserve_rng_state=False)
-        else:
-            out = self._read(x, top_idx, log_gates, M_blocks, mode)
-        if torch.result_type(self.mom_scale, out) == torch.float32:
-            return mom_kernels.mom_scale(out, self.mom_scale)
-        return self.mom_scale * out
+        return self._read(xq, top_idx, log_gates, M_blocks, mode)
 
     def _read(self, x, top_idx, log_gates, M_blocks, mode):
         B, S, D = x.shape

@@ -1,0 +1,159 @@
+"""Autograd wrappers of the decoder trunk's fused bf16 kernels (csrc/trunk.cu):
+the rotary embedding of the fused q/k/v projection and the SwiGLU gate.
+
+Both reproduce the rounding points of the reference's trunk under bf16
+autocast (transformers' Llama apply_rotary_pos_emb and LlamaMLP); they take
+and return bf16 CUDA tensors only and raise otherwise (the decoder keeps
+torch's ops for fp32 runs).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_bf16(*ts):
+    for t in ts:
+        if not (t.is_cuda and t.dtype == torch.bfloat16):
+            raise RuntimeError(f"naylis_b200 trunk kernels take bf16 CUDA tensors, got {t.dtype} on {t.device}")
+
+
+class _RopeQKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, cos, sin, n_heads):
+        B, S, d3 = qkv.shape
+        hd = d3 // (3 * n_heads)
+        qkv = qkv.contiguous()
+        cos = cos.float().contiguous()
+        sin = sin.float().contiguous()
+        q = torch.empty(B, S, n_heads, hd, dtype=torch.bfloat16, device=qkv.device)
+        k = torch.empty_like(q)
+        v = torch.empty_like(q)
+        _lib.call("mom_rope_qkv_fwd", qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), B, S, n_heads, hd,
+                  q.data_ptr(), k.data_ptr(), v.data_ptr(), _stream(qkv))
+        ctx.save_for_backward(cos, sin)
+        ctx.meta = (B, S, n_heads, hd)
+        # attention's (B, H, S, hd) views over the token-major buffers
+        return q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        cos, sin = ctx.saved_tensors
+        B, S, H, hd = ctx.meta
+        tok = [t.to(torch.bfloat16).transpose(1, 2).contiguous() for t in (dq, dk, dv)]
+        dqkv = torch.empty(B, S, 3 * H * hd, dtype=torch.bfloat16, device=cos.device)
+        _lib.call("mom_rope_qkv_bwd", tok[0].data_ptr(), tok[1].data_ptr(), tok[2].data_ptr(), cos.data_ptr(),
+                  sin.data_ptr(), B, S, H, hd, dqkv.data_ptr(), _stream(dqkv))
+        return dqkv, None, None, None
+
+
+def rope_qkv(qkv, cos, sin, n_heads: int):
+    """qkv (B, S, 3*H*hd) bf16 -> q, k, v as (B, H, S, hd) bf16 views, q and k
+    rotated (fp32 math with fp32 cos / sin (S, hd), rounded to bf16)."""
+    _need_bf16(qkv)
+    if qkv.shape[-1] % (6 * n_heads):
+        raise RuntimeError("rope_qkv: last dimension must be 3 * n_heads * (even head_dim)")
+    return _RopeQKV.apply(qkv, cos, sin, int(n_heads))
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        gu = gu.contiguous()
+        f = gu.shape[-1] // 2
+        N = gu.numel() // gu.shape[-1]
+        h = torch.empty(*gu.shape[:-1], f, dtype=torch.bfloat16, device=gu.device)
+        _lib.call("mom_swiglu_fwd", gu.data_ptr(), N, f, h.data_ptr(), _stream(gu))
+        ctx.save_for_backward(gu)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gu,) = ctx.saved_tensors
+        f = gu.shape[-1] // 2
+        N = gu.numel() // gu.shape[-1]
+        dh = dh.to(torch.bfloat16).contiguous()
+        dgu = torch.empty_like(gu)
+        _lib.call("mom_swiglu_bwd", dh.data_ptr(), gu.data_ptr(), N, f, dgu.data_ptr(), _stream(gu))
+        return dgu
+
+
+def swiglu(gu):
+    """gu (..., 2f) bf16 = [gate | up] -> bf16(bf16(silu(gate)) * up) (..., f)."""
+    _need_bf16(gu)
+    if gu.shape[-1] % 4:
+        raise RuntimeError("swiglu: the gate/up width 2f must have f even")
+    return _SwiGLU.apply(gu)
+
+
+__all__ = ["rope_qkv", "swiglu"]
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    """x_new = x + s * delta, y = RMSNorm(x_new) (bf16, and fp32 when asked)."""
+
+    @staticmethod
+    def forward(ctx, x, delta, scale, weight, eps, want_f32):
+        x = x.contiguous()
+        d = x.shape[-1]
+        N = x.numel() // d
+        x_out = torch.empty_like(x)
+        y16 = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        y32 = torch.empty_like(x) if want_f32 else None
+        rstd = torch.empty(N, dtype=torch.float32, device=x.device)
+        dcode = _lib.F32
+        if delta is not None:
+            delta = delta.contiguous()
+            dcode = _lib.BF16 if delta.dtype == torch.bfloat16 else _lib.F32
+        sc = None if scale is None else scale.detach().float().contiguous()
+        w = weight.detach().float().contiguous()
+        _lib.call("mom_add_rmsnorm_fwd", x.data_ptr(), None if delta is None else delta.data_ptr(), dcode,
+                  None if sc is None else sc.data_ptr(), w.data_ptr(), N, d, float(eps), x_out.data_ptr(),
+                  y16.data_ptr(), None if y32 is None else y32.data_ptr(), rstd.data_ptr(), _stream(x))
+        ctx.save_for_backward(x_out, rstd, w, delta, sc)
+        ctx.meta = (dcode, delta is not None, scale is not None, scale.dtype if scale is not None else None,
+                    weight.dtype)
+        if want_f32:
+            return x_out, y16, y32
+        return x_out, y16
+
+    @staticmethod
+    def backward(ctx, dx_out, dy16, dy32=None):
+        x_out, rstd, w, delta, sc = ctx.saved_tensors
+        dcode, has_delta, has_scale, scale_dtype, w_dtype = ctx.meta
+        d = x_out.shape[-1]
+        N = x_out.numel() // d
+        g16 = None if dy16 is None else dy16.to(torch.bfloat16).contiguous()
+        g32 = None if dy32 is None else dy32.float().contiguous()
+        gx = None if dx_out is None else dx_out.float().contiguous()
+        dx = torch.empty_like(x_out)
+        ddelta = torch.empty_like(delta) if has_delta else None
+        dw = torch.empty(d, dtype=torch.float32, device=x_out.device)
+        dsc = torch.empty(1, dtype=torch.float32, device=x_out.device) if has_scale else None
+        if g16 is None and g32 is None:
+            g32 = torch.zeros_like(x_out)
+        _lib.call("mom_add_rmsnorm_bwd", x_out.data_ptr(), rstd.data_ptr(), w.data_ptr(),
+                  None if delta is None else delta.data_ptr(), dcode, None if sc is None else sc.data_ptr(),
+                  None if g16 is None else g16.data_ptr(), None if g32 is None else g32.data_ptr(),
+                  None if gx is None else gx.data_ptr(), N, d, dx.data_ptr(),
+                  None if ddelta is None else ddelta.data_ptr(), dw.data_ptr(),
+                  None if dsc is None else dsc.data_ptr(), _stream(x_out))
+        return (dx, ddelta, None if dsc is None else dsc.to(scale_dtype), dw.to(w_dtype), None, None)
+
+
+def add_rmsnorm(x, delta, weight, eps: float, scale=None, want_f32: bool = False):
+    """The residual add fused with the RMSNorm that follows it:
+    x_new = x + scale * delta (delta bf16 / fp32 or None, scale a (1,) tensor or
+    None), y = weight * x_new / sqrt(mean(x_new^2) + eps). Returns (x_new fp32,
+    y bf16) or, with want_f32, (x_new, y bf16, y fp32)."""
+    if not (x.is_cuda and x.dtype == torch.float32):
+        raise RuntimeError("add_rmsnorm: x must be an fp32 CUDA tensor (the residual stream)")
+    return _AddRMSNorm.apply(x, delta, scale, weight, float(eps), bool(want_f32))
+
+
+__all__ = ["rope_qkv", "swiglu", "add_rmsnorm"]
