@@ -225,7 +225,7 @@ MOM_API int mom_swiglu_bwd(const void *dh, const void *gu, int64_t N, int64_t f,
  * or NULL for no add), then y = w * (x_out * rsqrt(mean(x_out^2) + eps)) as bf16
  * (y_bf16, the next projection's input) and, when y_f32 is not NULL, fp32 (the
  * MoM router's input); rstd (N) per token for the backward. x, x_out, w fp32;
- * rows of d = a multiple of 32 up to 2048. Replaces the reference's
+ * rows of d = 128, 256, 512, 1024 or 2048, 16-byte (fp32) / 8-byte (bf16) aligned. Replaces the reference's
  * `residual + hidden_states` and LlamaRMSNorm (model.py:319-345) and, with
  * delta_scale = mom_scale, `mom_scale * o_proj(out)` (model.py:239).
  * mom_add_rmsnorm_bwd: from dy (bf16 and/or fp32) and dx_in (the residual

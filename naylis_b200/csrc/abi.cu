@@ -736,9 +736,13 @@ int mom_add_rmsnorm_fwd(const float *x, const void *delta, int delta_dtype, cons
                         void *stream) {
     const int ddt = delta_code(delta_dtype, delta);
     MOM_REQUIRE(ddt >= 0, "delta dtype must be F32 or BF16");
-    MOM_REQUIRE(N >= 0 && d > 0 && d % 32 == 0 && d <= 2048, "d must be a multiple of 32 up to 2048");
+    MOM_REQUIRE(N >= 0 && (d == 128 || d == 256 || d == 512 || d == 1024 || d == 2048),
+                "d must be 128, 256, 512, 1024 or 2048");
     if (N == 0) return MOM_OK;
     MOM_REQUIRE(x && w && x_out && y_bf16 && rstd, "null pointer argument");
+    MOM_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(x_out) | reinterpret_cast<uintptr_t>(w) |
+                  reinterpret_cast<uintptr_t>(y_f32)) & 15) == 0 && ((reinterpret_cast<uintptr_t>(y_bf16) |
+                  reinterpret_cast<uintptr_t>(delta)) & 7) == 0, "rows must be 16-byte (fp32) / 8-byte (bf16) aligned");
     int rc = check_current_device();
     if (rc) return rc;
     cudaError_t e = mom::launch_add_rmsnorm_fwd(x, delta, ddt, delta_scale, w, N, (int)d, static_cast<float>(eps), x_out,
@@ -751,7 +755,8 @@ int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, c
                         int64_t N, int64_t d, float *dx, void *ddelta, float *dw, float *ddelta_scale, void *stream) {
     const int ddt = delta_code(delta_dtype, delta);
     MOM_REQUIRE(ddt >= 0, "delta dtype must be F32 or BF16");
-    MOM_REQUIRE(N >= 0 && d > 0 && d % 32 == 0 && d <= 2048, "d must be a multiple of 32 up to 2048");
+    MOM_REQUIRE(N >= 0 && (d == 128 || d == 256 || d == 512 || d == 1024 || d == 2048),
+                "d must be 128, 256, 512, 1024 or 2048");
     MOM_REQUIRE(w && dw, "null pointer argument");
     MOM_REQUIRE(N == 0 || (x_new && rstd && dx && (dy_bf16 || dy_f32) && (ddt == 0 || ddelta)),
                 "null pointer argument");

@@ -159,57 +159,79 @@ int grid_of(int64_t work) { return static_cast<int>(std::min<int64_t>((work + 25
 // x_new = x + scale * delta (the sublayer's output added to the fp32 residual
 // stream; scale is a device scalar or absent), then the Llama RMSNorm of x_new:
 // y = w * (x_new * rsqrt(mean(x_new^2) + eps)), returned as bf16 (the next GEMM's
-// input) and, when asked, as fp32 (the MoM router's input). A warp per token,
-// d / 32 values per lane in registers; r = rsqrt(...) saved per token.
+// input) and, when asked, as fp32 (the MoM router's input). A warp per token;
+// each lane holds NV vectors of 4 columns (columns 4*lane + 128*j), and every
+// load of a token is issued before any of its values is used (the loads, not
+// the arithmetic, bound this kernel). r = rsqrt(...) is saved per token.
 constexpr int kNormWarps = 8;
 
 template <int DDT>   // delta: 0 none, 1 bf16, 2 fp32
-__device__ __forceinline__ float load_delta(const void *delta, int64_t i) {
-    if (DDT == 1) return bf16_bits_to_f32(static_cast<const uint16_t *>(delta)[i]);
-    if (DDT == 2) return static_cast<const float *>(delta)[i];
-    return 0.0f;
+__device__ __forceinline__ float4 load_delta4(const void *delta, int64_t i) {
+    if (DDT == 1) {
+        const uint2 w = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(delta) + i);
+        return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u),
+                           __uint_as_float(w.y << 16), __uint_as_float(w.y & 0xFFFF0000u));
+    }
+    if (DDT == 2) return *reinterpret_cast<const float4 *>(static_cast<const float *>(delta) + i);
+    return make_float4(0.f, 0.f, 0.f, 0.f);
 }
 
-template <int DDT, int VPL>
+__device__ __forceinline__ float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ void st4(float *p, float4 v) { *reinterpret_cast<float4 *>(p) = v; }
+__device__ __forceinline__ float4 bf4(const uint16_t *p) {
+    const uint2 w = *reinterpret_cast<const uint2 *>(p);
+    return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xFFFF0000u), __uint_as_float(w.y << 16),
+                       __uint_as_float(w.y & 0xFFFF0000u));
+}
+__device__ __forceinline__ void stbf4(uint16_t *p, float4 v) {
+    *reinterpret_cast<uint2 *>(p) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+}
+
+template <int DDT, int NV>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_rmsnorm_fwd_kernel(const float *__restrict__ x, const void *__restrict__ delta, const float *__restrict__ dscale,
                        const float *__restrict__ w, int64_t N, int d, float eps, float *__restrict__ x_out,
                        uint16_t *__restrict__ y16, float *__restrict__ y32, float *__restrict__ rstd) {
     const int lane = threadIdx.x & 31;
     const float sc = (DDT != 0 && dscale) ? *dscale : 1.0f;
+    float4 wv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) wv[j] = ld4(w + 4 * lane + 128 * j);
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * kNormWarps + (threadIdx.x >> 5); t < N;
          t += static_cast<int64_t>(gridDim.x) * kNormWarps) {
-        const int64_t base = t * d;
-        float v[VPL];
+        const int64_t base = t * d + 4 * lane;
+        float4 a[NV], b[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            a[j] = ld4(x + base + 128 * j);
+            b[j] = load_delta4<DDT>(delta, base + 128 * j);
+        }
         float ss = 0.0f;
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            float a = 0.0f;
-            if (c < d) {
-                a = x[base + c];
-                if (DDT != 0) {
-                    float dd = load_delta<DDT>(delta, base + c);
-                    if (dscale) dd = __fmul_rn(sc, dd);
-                    a = __fadd_rn(a, dd);
-                }
-                x_out[base + c] = a;
+        for (int j = 0; j < NV; ++j) {
+            if (DDT != 0) {
+                float4 dd = b[j];
+                if (dscale) dd = make_float4(__fmul_rn(sc, dd.x), __fmul_rn(sc, dd.y), __fmul_rn(sc, dd.z),
+                                             __fmul_rn(sc, dd.w));
+                a[j] = make_float4(__fadd_rn(a[j].x, dd.x), __fadd_rn(a[j].y, dd.y), __fadd_rn(a[j].z, dd.z),
+                                   __fadd_rn(a[j].w, dd.w));
             }
-            v[j] = a;
-            ss = __fmaf_rn(a, a, ss);
+            st4(x_out + base + 128 * j, a[j]);
+            ss = __fmaf_rn(a[j].x, a[j].x, ss);
+            ss = __fmaf_rn(a[j].y, a[j].y, ss);
+            ss = __fmaf_rn(a[j].z, a[j].z, ss);
+            ss = __fmaf_rn(a[j].w, a[j].w, ss);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float r = rsqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps));
         if (lane == 0) rstd[t] = r;
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < d) {
-                const float yv = __fmul_rn(w[c], __fmul_rn(v[j], r));
-                y16[base + c] = f32_to_bf16_bits(yv);
-                if (y32) y32[base + c] = yv;
-            }
+        for (int j = 0; j < NV; ++j) {
+            const float4 yv = make_float4(__fmul_rn(wv[j].x, __fmul_rn(a[j].x, r)), __fmul_rn(wv[j].y, __fmul_rn(a[j].y, r)),
+                                          __fmul_rn(wv[j].z, __fmul_rn(a[j].z, r)), __fmul_rn(wv[j].w, __fmul_rn(a[j].w, r)));
+            stbf4(y16 + base + 128 * j, yv);
+            if (y32) st4(y32 + base + 128 * j, yv);
         }
     }
 }
@@ -217,8 +239,9 @@ add_rmsnorm_fwd_kernel(const float *__restrict__ x, const void *__restrict__ del
 // Backward of add_rmsnorm. dy = dy16 (+ dy32), g = dy * w, xh = x_new * r:
 //   d(x_new) = dx_in + r * (g - xh * mean(g * xh))      (dx_in: the residual's own gradient)
 //   dx = d(x_new), d(delta) = scale * d(x_new), dw += dy * xh, dscale += sum d(x_new) * delta
-// dw / dscale are reduced per CTA in shared memory and added with one atomic each.
-template <int DDT, int VPL>
+// dw and dscale are kept per lane across the warp's tokens, reduced per CTA in
+// shared memory and added to global memory with one atomic each.
+template <int DDT, int NV>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict__ rstd, const float *__restrict__ w,
                        const void *__restrict__ delta, const float *__restrict__ dscale_in,
@@ -230,54 +253,66 @@ add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict_
     for (int c = threadIdx.x; c <= d; c += blockDim.x) sdw[c] = 0.0f;
     __syncthreads();
     const float sc = (DDT != 0 && dscale_in) ? *dscale_in : 1.0f;
-    float acc_w[VPL];
+    float4 wv[NV], aw[NV];
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) acc_w[j] = 0.0f;
+    for (int j = 0; j < NV; ++j) {
+        wv[j] = ld4(w + 4 * lane + 128 * j);
+        aw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     float acc_s = 0.0f;
     for (int64_t t = static_cast<int64_t>(blockIdx.x) * kNormWarps + warp; t < N;
          t += static_cast<int64_t>(gridDim.x) * kNormWarps) {
-        const int64_t base = t * d;
+        const int64_t base = t * d + 4 * lane;
         const float r = rstd[t];
-        float xh[VPL], g[VPL];
+        float4 xv[NV], gv[NV], rv[NV], dl[NV];
+#pragma unroll
+        for (int j = 0; j < NV; ++j) {
+            const int64_t o = base + 128 * j;
+            xv[j] = ld4(x_new + o);
+            gv[j] = dy16 ? bf4(dy16 + o) : make_float4(0.f, 0.f, 0.f, 0.f);
+            rv[j] = dy32 ? ld4(dy32 + o) : make_float4(0.f, 0.f, 0.f, 0.f);
+            dl[j] = dx_in ? ld4(dx_in + o) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         float dot = 0.0f;
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            xh[j] = 0.0f;
-            g[j] = 0.0f;
-            if (c < d) {
-                float dyv = dy16 ? bf16_bits_to_f32(dy16[base + c]) : 0.0f;
-                if (dy32) dyv += dy32[base + c];
-                xh[j] = x_new[base + c] * r;
-                g[j] = dyv * w[c];
-                acc_w[j] = fmaf(dyv, xh[j], acc_w[j]);
-                dot = fmaf(g[j], xh[j], dot);
-            }
+        for (int j = 0; j < NV; ++j) {
+            float4 dyv = make_float4(gv[j].x + rv[j].x, gv[j].y + rv[j].y, gv[j].z + rv[j].z, gv[j].w + rv[j].w);
+            const float4 xh = make_float4(xv[j].x * r, xv[j].y * r, xv[j].z * r, xv[j].w * r);
+            aw[j].x = fmaf(dyv.x, xh.x, aw[j].x); aw[j].y = fmaf(dyv.y, xh.y, aw[j].y);
+            aw[j].z = fmaf(dyv.z, xh.z, aw[j].z); aw[j].w = fmaf(dyv.w, xh.w, aw[j].w);
+            gv[j] = make_float4(dyv.x * wv[j].x, dyv.y * wv[j].y, dyv.z * wv[j].z, dyv.w * wv[j].w);
+            xv[j] = xh;
+            dot = fmaf(gv[j].x, xh.x, fmaf(gv[j].y, xh.y, fmaf(gv[j].z, xh.z, fmaf(gv[j].w, xh.w, dot))));
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
         const float mean = dot / static_cast<float>(d);
 #pragma unroll
-        for (int j = 0; j < VPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < d) {
-                float gx = r * (g[j] - xh[j] * mean);
-                if (dx_in) gx += dx_in[base + c];
-                dx[base + c] = gx;
-                if (DDT == 1) {
-                    static_cast<uint16_t *>(ddelta)[base + c] = f32_to_bf16_bits(dscale_in ? sc * gx : gx);
-                    if (dscale) acc_s = fmaf(gx, bf16_bits_to_f32(static_cast<const uint16_t *>(delta)[base + c]), acc_s);
-                } else if (DDT == 2) {
-                    static_cast<float *>(ddelta)[base + c] = dscale_in ? sc * gx : gx;
-                    if (dscale) acc_s = fmaf(gx, static_cast<const float *>(delta)[base + c], acc_s);
+        for (int j = 0; j < NV; ++j) {
+            const int64_t o = base + 128 * j;
+            const float4 gx = make_float4(fmaf(r, gv[j].x - xv[j].x * mean, dl[j].x),
+                                          fmaf(r, gv[j].y - xv[j].y * mean, dl[j].y),
+                                          fmaf(r, gv[j].z - xv[j].z * mean, dl[j].z),
+                                          fmaf(r, gv[j].w - xv[j].w * mean, dl[j].w));
+            st4(dx + o, gx);
+            if (DDT != 0) {
+                const float4 dd = dscale_in ? make_float4(sc * gx.x, sc * gx.y, sc * gx.z, sc * gx.w) : gx;
+                if (dscale) {
+                    const float4 dv = load_delta4<DDT>(delta, o);
+                    acc_s = fmaf(gx.x, dv.x, fmaf(gx.y, dv.y, fmaf(gx.z, dv.z, fmaf(gx.w, dv.w, acc_s))));
                 }
+                if (DDT == 1) stbf4(static_cast<uint16_t *>(ddelta) + o, dd);
+                else st4(static_cast<float *>(ddelta) + o, dd);
             }
         }
     }
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-        const int c = lane + 32 * j;
-        if (c < d) atomicAdd(&sdw[c], acc_w[j]);
+    for (int j = 0; j < NV; ++j) {
+        const int c = 4 * lane + 128 * j;
+        atomicAdd(&sdw[c], aw[j].x);
+        atomicAdd(&sdw[c + 1], aw[j].y);
+        atomicAdd(&sdw[c + 2], aw[j].z);
+        atomicAdd(&sdw[c + 3], aw[j].w);
     }
     if (DDT != 0 && dscale) {
 #pragma unroll
@@ -333,23 +368,23 @@ cudaError_t launch_swiglu_bwd(const void *dh, const void *gu, int64_t N, int f, 
     return cudaGetLastError();
 }
 
-// d must be a multiple of 32 and at most 32 * 64 (values per lane in registers).
+// d = 128, 256, 512, 1024 or 2048: d / 128 vectors of 4 columns per lane in registers.
 cudaError_t launch_add_rmsnorm_fwd(const float *x, const void *delta, int ddt, const float *dscale, const float *w,
                                    int64_t N, int d, float eps, float *x_out, void *y16, float *y32, float *rstd,
                                    cudaStream_t st) {
     if (N == 0) return cudaSuccess;
-    if (d % 32 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
+    if (d % 128 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
     const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 8));
     auto out16 = static_cast<uint16_t *>(y16);
-#define MOM_NORM_F(DDT, VPL)                                                                                   \
-    add_rmsnorm_fwd_kernel<DDT, VPL><<<blocks, 32 * kNormWarps, 0, st>>>(x, delta, dscale, w, N, d, eps, x_out, \
+    const int nv = d / 128;
+#define MOM_NORM_F(DDT, NVV)                                                                                   \
+    add_rmsnorm_fwd_kernel<DDT, NVV><<<blocks, 32 * kNormWarps, 0, st>>>(x, delta, dscale, w, N, d, eps, x_out, \
                                                                          out16, y32, rstd)
-    const int vpl = d / 32;
-    if (vpl <= 32) {
-        if (ddt == 0) MOM_NORM_F(0, 32); else if (ddt == 1) MOM_NORM_F(1, 32); else MOM_NORM_F(2, 32);
-    } else {
-        if (ddt == 0) MOM_NORM_F(0, 64); else if (ddt == 1) MOM_NORM_F(1, 64); else MOM_NORM_F(2, 64);
-    }
+#define MOM_NORM_FD(NVV) \
+    if (ddt == 0) MOM_NORM_F(0, NVV); else if (ddt == 1) MOM_NORM_F(1, NVV); else MOM_NORM_F(2, NVV);
+    if (nv == 8) { MOM_NORM_FD(8) } else if (nv == 16) { MOM_NORM_FD(16) } else if (nv == 4) { MOM_NORM_FD(4) }
+    else if (nv == 2) { MOM_NORM_FD(2) } else if (nv == 1) { MOM_NORM_FD(1) } else { return cudaErrorInvalidValue; }
+#undef MOM_NORM_FD
 #undef MOM_NORM_F
     count_launch();
     return cudaGetLastError();
@@ -359,24 +394,24 @@ cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const 
                                    const float *dscale_in, const void *dy16, const float *dy32, const float *dx_in,
                                    int64_t N, int d, float *dx, void *ddelta, float *dw, float *dscale,
                                    cudaStream_t st) {
-    if (d % 32 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
+    if (d % 128 || d > 2048 || ddt < 0 || ddt > 2) return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(dw, 0, sizeof(float) * d, st);
     if (e == cudaSuccess && dscale) e = cudaMemsetAsync(dscale, 0, sizeof(float), st);
     if (e != cudaSuccess) return e;
     if (N == 0) return cudaSuccess;
-    const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 2));
+    const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 4));
     const size_t smem = sizeof(float) * (d + 1);
     auto g16 = static_cast<const uint16_t *>(dy16);
-#define MOM_NORM_B(DDT, VPL)                                                                                     \
-    add_rmsnorm_bwd_kernel<DDT, VPL><<<blocks, 32 * kNormWarps, smem, st>>>(x_new, rstd, w, delta, dscale_in, g16, \
+    const int nv = d / 128;
+#define MOM_NORM_B(DDT, NVV)                                                                                     \
+    add_rmsnorm_bwd_kernel<DDT, NVV><<<blocks, 32 * kNormWarps, smem, st>>>(x_new, rstd, w, delta, dscale_in, g16, \
                                                                             dy32, dx_in, N, d, dx, ddelta, dw,  \
                                                                             dscale)
-    const int vpl = d / 32;
-    if (vpl <= 32) {
-        if (ddt == 0) MOM_NORM_B(0, 32); else if (ddt == 1) MOM_NORM_B(1, 32); else MOM_NORM_B(2, 32);
-    } else {
-        if (ddt == 0) MOM_NORM_B(0, 64); else if (ddt == 1) MOM_NORM_B(1, 64); else MOM_NORM_B(2, 64);
-    }
+#define MOM_NORM_BD(NVV) \
+    if (ddt == 0) MOM_NORM_B(0, NVV); else if (ddt == 1) MOM_NORM_B(1, NVV); else MOM_NORM_B(2, NVV);
+    if (nv == 8) { MOM_NORM_BD(8) } else if (nv == 16) { MOM_NORM_BD(16) } else if (nv == 4) { MOM_NORM_BD(4) }
+    else if (nv == 2) { MOM_NORM_BD(2) } else if (nv == 1) { MOM_NORM_BD(1) } else { return cudaErrorInvalidValue; }
+#undef MOM_NORM_BD
 #undef MOM_NORM_B
     count_launch();
     return cudaGetLastError();

@@ -203,7 +203,8 @@ class NaylisModel(nn.Module):
         x = self.embed_tokens(input_ids)
         cos, sin = rope_tables(input_ids.shape[1], self.cfg.head_dim, self.cfg.rope_theta, x.device)
         fused = (x.is_cuda and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda")
-                 and torch.get_autocast_dtype("cuda") == torch.bfloat16 and not self.cfg.grad_ckpt)
+                 and torch.get_autocast_dtype("cuda") == torch.bfloat16 and not self.cfg.grad_ckpt
+                 and self.cfg.hidden_size in (128, 256, 512, 1024, 2048))
         if fused:
             pending = None
             for layer in self.layers:
