@@ -19,14 +19,18 @@
 //              ~100 cycles: the two PV halves get an issuing warp each)
 //   warps 3-18 softmax (one TMEM lane = one token row per thread; four warps per
 //              lane quarter, 64 score columns each): row max, exp2, row sum, P as
-//              bf16 into TMEM (the A operand of PV); then the epilogue
+//              bf16 into TMEM (the A operand of PV); the rows' max, sum and token
+//              go to the epilogue through a two-item ring in shared memory
+//   warps 19-22 epilogue, one per TMEM lane quarter, one item behind the softmax:
 //              (O_0 + O_1) / l -> shared memory -> global as whole 128-B rows,
-//              log-sum-exp -> global
+//              log-sum-exp -> global. O is read out of TMEM first and released
+//              (o_free) before the stores, so PV(i+1) does not wait for them.
 // TMEM: S at columns 0..255, P (bf16 pairs) at 256..383, O_0 / O_1 at 384 / 448
 // (head_dim 128: S 0..127, P 256..319, O 384..511).
 // P has its own columns so that S(i+1) is issued as soon as the softmax has read
 // S(i), overlapping PV(i); the softmax writes P(i+1) once PV(i) is done
-// (pv_done), PV(i+1) writes O once the epilogue has read O(i) (o_free).
+// (pv_done), PV(i+1) writes O once the epilogue warps have read O(i) (o_free),
+// and the softmax of i+1 runs while the epilogue of i stores.
 // All waits are bounded (tc::mbar_wait); a timeout sets bit 1 of the plan's
 // error word and every role unwinds.
 #include <cudaTypedefs.h>
@@ -41,10 +45,15 @@ constexpr int kBS = 128;
 constexpr int kTM = 128;                       // token rows per tile (TMEM lanes)
 constexpr int kSoftWarps = 16;                 // 4 per SM sub-partition
 constexpr int kSoftThreads = kSoftWarps * 32;
-constexpr int kThreads = 96 + kSoftThreads;     // loader + 2 MMA issuers + softmax
+constexpr int kEpiWarp0 = 3 + kSoftWarps;       // first epilogue warp (warp & 3 = its lane quarter)
+constexpr int kEpiThreads = 4 * 32;
+constexpr int kThreads = 96 + kSoftThreads + kEpiThreads;   // loader + 2 MMA issuers + softmax + epilogue
 constexpr uint32_t kBoxBytes = 128 * 128;      // one TMA box: 128 rows x 64 bf16 columns (128-B swizzle)
 constexpr uint32_t kOutBytes = kTM * 64 * 2;   // 64 output columns of the tile, staged for coalesced stores
-constexpr uint32_t kScratchBytes = 8 * kTM * 4 + kOutBytes + kTM * 4;   // row max / sums [4][128], O cols, tokens
+// row max / sums [4][128]; O staging [128 rows][128 B]; the epilogue ring: two
+// items of {row max, row sum, token} [128] and {head, blocks, first plan row}
+constexpr uint32_t kRingItemBytes = 3 * kTM * 4 + 16;
+constexpr uint32_t kScratchBytes = 8 * kTM * 4 + kOutBytes + 2 * kRingItemBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kPCol = 256;                // P: group g's 64 slots at 256 + 32g (bf16 pairs)
 constexpr uint32_t kOCol = 384;                // head_dim 64: O_0 at 384, O_1 at 448; head_dim 128: O at 384
@@ -74,7 +83,7 @@ struct Fwd {
 
 struct Bars {
     uint64_t q_full[4], q_empty[4], kv_full[2], kv_empty[2], s_full, p_full, pv_done, o_full, o_free, drain,
-        s_issued;
+        s_issued, stats_full[2], stats_free[2];
     uint32_t tmem_base;
     int abort;
     // per Q stage: blocks loaded | (blocks of the set << 8) | (new K/V load << 16);
@@ -100,7 +109,12 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
     float *sMax = reinterpret_cast<float *>(sbase + C::kRingBytes);     // [4][128]
     float *sSum = sMax + 4 * kTM;                                        // [4][128]
     uint4 *sOut = reinterpret_cast<uint4 *>(sSum + 4 * kTM);            // [128 rows][8 x 16 B], swizzled
-    int *sTok = reinterpret_cast<int *>(sOut + kTM * 8);                 // [128] tokens of the staged rows
+    // epilogue ring, item parity p: eM[p][128], eL[p][128], eTok[p][128], eInfo[p][4]
+    unsigned char *sRing = reinterpret_cast<unsigned char *>(sOut + kTM * 8);
+    auto eM = [&](int p) { return reinterpret_cast<float *>(sRing + p * kRingItemBytes); };
+    auto eL = [&](int p) { return eM(p) + kTM; };
+    auto eTok = [&](int p) { return reinterpret_cast<int *>(eM(p) + 2 * kTM); };
+    auto eInfo = [&](int p) { return eTok(p) + kTM; };
     Bars *bars = reinterpret_cast<Bars *>(sbase + C::kRingBytes + kScratchBytes);
     volatile int *abort_flag = &bars->abort;
 
@@ -128,7 +142,11 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             tc::mbar_init(&bars->kv_empty[b], C::kMaxBlk > 1 ? 2 : 1);
         }
         tc::mbar_init(&bars->o_full, 2);
-        tc::mbar_init(&bars->o_free, kSoftThreads);
+        tc::mbar_init(&bars->o_free, kEpiThreads);
+        for (int p = 0; p < 2; ++p) {
+            tc::mbar_init(&bars->stats_full[p], kSoftThreads);
+            tc::mbar_init(&bars->stats_free[p], kEpiThreads);
+        }
         tc::mbar_init(&bars->s_full, 1);
         tc::mbar_init(&bars->p_full, kSoftThreads);
         tc::mbar_init(&bars->pv_done, 2);
@@ -337,8 +355,8 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         if (lane == 0) tc::mma_commit(&bars->drain);
         __syncwarp();
         tc::mbar_wait_warp(&bars->drain, 0, P.err, 2, abort_flag);
-    } else {
-        // ------------------------------------------------------------ softmax + epilogue
+    } else if (warp < kEpiWarp0) {
+        // ------------------------------------------------------------ softmax
         // 16 warps: warp & 3 is the TMEM lane quarter (hardware rule), (warp-3) >> 2
         // the 64-column group of the 256 score columns (block = group >> 1). The
         // four warps of one lane quarter exchange partial row max / sum through
@@ -349,65 +367,6 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
         const int r = quarter * 32 + lane;
         const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         const int bar_id = 1 + quarter;
-        int prev_tok = -1, prev_h = 0, prev_row = 0, prev_nblk = 0;
-        float prev_m = 0.0f;
-        float prev_l = 0.0f;
-        // Epilogue of an item, called by the four warps of a lane quarter together:
-        // O_0 (+ O_1) / l of this thread's 16 columns, stored through shared memory
-        // as whole rows (tc::store_tile_rows).
-        auto epilogue = [&](int i) {
-            (void)i;
-            const float l = prev_l;
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            tc::tc_fence_after();
-            // head_dim 64: O_0 and O_1 (the set's two blocks) at +0 / +64, summed;
-            // head_dim 128: columns 16g.. and 64+16g.. of the one O
-            uint32_t a0[16], a1[16];
-            tc::tmem_ld16(trow + kOCol + grp * 16, a0);          // both in one round trip
-            tc::tmem_ld16(trow + kOCol + 64 + grp * 16, a1);
-            tc::tmem_ld_wait_regs(a0);
-            tc::tmem_ld_wait_regs(a1);
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bars->o_free);
-            auto pack16 = [&](const float (&o)[16], uint4 &v0, uint4 &v1) {
-                v0.x = pack_bf16x2(o[0] * inv, o[1] * inv);
-                v0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
-                v0.z = pack_bf16x2(o[4] * inv, o[5] * inv);
-                v0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-                v1.x = pack_bf16x2(o[8] * inv, o[9] * inv);
-                v1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
-                v1.z = pack_bf16x2(o[12] * inv, o[13] * inv);
-                v1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
-            };
-            auto put_lse = [&]() {
-                if (grp == 0 && prev_tok >= 0)
-                    lse[static_cast<int64_t>(prev_h) * P.n + prev_row] =
-                        l > 0.0f ? (prev_m + log2f(l)) * kLn2 : -INFINITY;
-            };
-            float o[16];
-            uint4 v0, v1;
-            if constexpr (HD == 64) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e)   // O_1 holds block 1 of a two-block set
-                    o[e] = (prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) +
-                           (prev_nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
-                pack16(o, v0, v1);
-                put_lse();
-                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = prev_nblk > 0 ? __uint_as_float(a0[e]) : 0.0f;
-                pack16(o, v0, v1);
-                put_lse();
-                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok, out + prev_h * kHD, ld);
-                tc::named_bar(bar_id, 128);   // the staging rows are read out before they are rewritten
-#pragma unroll
-                for (int e = 0; e < 16; ++e) o[e] = prev_nblk > 0 ? __uint_as_float(a1[e]) : 0.0f;
-                pack16(o, v0, v1);
-                tc::store_tile_rows(sOut, sTok, quarter, grp, lane, bar_id, v0, v1, prev_tok,
-                                    out + prev_h * kHD + 64, ld);
-            }
-        };
         // per-item row metadata: tile fields for 32 items at a time (one per lane),
         // this thread's row (token, gate bias) one item ahead, so that no global
         // load latency sits on the softmax path
@@ -435,9 +394,6 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             if (src < 31 && i + 1 < nmine) fetch(src + 1, nxt);
             const int h = item_head(item), nblk = cur.nblk, tok = cur.tok;
             const float bias = cur.bias;
-            // the row sum of item i-1 (complete since the second barrier of i-1), read
-            // before this item's first barrier lets anyone overwrite it
-            if (i > 0) prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
             if (!dead && !tc::mbar_wait_warp(&bars->s_full, i & 1, P.err, 2, abort_flag)) dead = true;
             const bool live = jb < nblk && !dead;
             tc::tc_fence_after();
@@ -508,26 +464,126 @@ read_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_cons
             sSum[grp * kTM + r] = lpart;
             tc::tc_fence_before();
             tc::mbar_arrive(&bars->p_full);
-            // O(i-1) complete (PV(i-1)), for the epilogue below
-            if (!dead && i > 0 && !tc::mbar_wait_warp(&bars->o_full, (i - 1) & 1, P.err, 2, abort_flag))
-                dead = true;
             // row sums of item i complete; the four warps of this lane quarter agree
-            // on stopping together (the epilogue's barrier needs all four)
+            // on stopping together
             dead = tc::named_bar_or(bar_id, 128, dead);
             if (dead) break;
-            if (i > 0) epilogue(i - 1);
-            prev_tok = tok;
-            prev_h = h;
-            prev_row = cur.row;
-            prev_m = m;
-            prev_nblk = nblk;
+            // item i's rows (max, sum, token) to the epilogue warps, ring slot i & 1,
+            // once the epilogue has read the slot's previous item (stats_free)
+            const int ps = i & 1;
+            if (grp == 0) {
+                const bool ok = i < 2 || tc::mbar_wait_warp(&bars->stats_free[ps], ((i >> 1) - 1) & 1, P.err, 2,
+                                                            abort_flag);
+                if (ok) {
+                    eM(ps)[r] = m;
+                    eL(ps)[r] = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
+                    eTok(ps)[r] = tok;
+                    if (r == 0) {
+                        eInfo(ps)[0] = h;
+                        eInfo(ps)[1] = nblk;
+                        eInfo(ps)[2] = cur.row;   // the tile's first plan row (this is row 0)
+                    }
+                }
+            }
+            tc::mbar_arrive(&bars->stats_full[ps]);
             count = i + 1;
         }
-        if (count > 0 && !dead) {   // uniform over the lane quarter
-            const int i = count - 1;
-            prev_l = sSum[r] + sSum[kTM + r] + sSum[2 * kTM + r] + sSum[3 * kTM + r];
-            bool bad = *abort_flag || !tc::mbar_wait_warp(&bars->o_full, i & 1, P.err, 2, abort_flag);
-            if (!tc::named_bar_or(bar_id, 128, bad)) epilogue(i);
+        (void)count;
+    } else {
+        // ------------------------------------------------------------ epilogue
+        // One warp per TMEM lane quarter (warp & 3), one item behind the softmax:
+        // O(i) out of TMEM (both halves of a two-block set summed), released to
+        // PV(i+1) (o_free), then scaled by 1/l, packed to bf16, staged as whole
+        // 128-B rows in shared memory and stored; the log-sum-exp per row.
+        const int quarter = warp & 3;
+        const int r = quarter * 32 + lane;
+        const uint32_t trow = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        uint4 *srow = sOut + r * 8;                       // this thread's staging row
+        const int64_t n_rows = P.n;
+        // rows quarter*32 .. +31 of the staging buffer to global, 4 rows per store
+        auto store_rows = [&](int tok, uint16_t *dst_col) {
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int rr = k * 4 + (lane >> 3), ch = lane & 7;
+                const int t = __shfl_sync(0xffffffffu, tok, rr);
+                const int row = quarter * 32 + rr;
+                if (t >= 0 && t < n_rows)
+                    reinterpret_cast<uint4 *>(dst_col + static_cast<int64_t>(t) * ld)[ch] = sOut[row * 8 + (ch ^ (row & 7))];
+            }
+            __syncwarp();
+        };
+        for (int i = 0; i < nmine; ++i) {
+            const int ps = i & 1;
+            if (!tc::mbar_wait_warp(&bars->stats_full[ps], (i >> 1) & 1, P.err, 2, abort_flag)) break;
+            if (!tc::mbar_wait_warp(&bars->o_full, i & 1, P.err, 2, abort_flag)) break;
+            const float m = eM(ps)[r], l = eL(ps)[r];
+            const int tok = eTok(ps)[r];
+            const int h = eInfo(ps)[0], nblk = eInfo(ps)[1], row0 = eInfo(ps)[2];
+            tc::mbar_arrive(&bars->stats_free[ps]);
+            if (*abort_flag || h < 0 || h >= H) break;
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            tc::tc_fence_after();
+            uint16_t *dst = out + static_cast<int64_t>(h) * kHD;
+            auto pack8 = [&](const float (&o)[16], int c, uint32_t (&pk)[8]) {
+                (void)c;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) pk[e] = pack_bf16x2(o[2 * e] * inv, o[2 * e + 1] * inv);
+            };
+            auto stage = [&](int c, const uint32_t (&pk)[8]) {
+                srow[(2 * c) ^ (r & 7)] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                srow[(2 * c + 1) ^ (r & 7)] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+            };
+            if constexpr (HD == 64) {
+                // O_0 at 384, O_1 at 448: the set's two blocks, summed
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t a0[16], a1[16];
+                    tc::tmem_ld16(trow + kOCol + 16 * c, a0);
+                    tc::tmem_ld16(trow + kOCol + 64 + 16 * c, a1);
+                    tc::tmem_ld_wait_regs(a0);
+                    tc::tmem_ld_wait_regs(a1);
+                    float o[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        o[e] = (nblk > 0 ? __uint_as_float(a0[e]) : 0.0f) + (nblk > 1 ? __uint_as_float(a1[e]) : 0.0f);
+                    uint32_t pk[8];
+                    pack8(o, c, pk);
+                    stage(c, pk);
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bars->o_free);
+                store_rows(tok, dst);
+            } else {
+                // one O of 128 columns: the first 64 staged and stored, the second
+                // kept in registers until O is released
+                uint32_t hi[4][8];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t a0[16], a1[16];
+                    tc::tmem_ld16(trow + kOCol + 16 * c, a0);
+                    tc::tmem_ld16(trow + kOCol + 64 + 16 * c, a1);
+                    tc::tmem_ld_wait_regs(a0);
+                    tc::tmem_ld_wait_regs(a1);
+                    float o[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) o[e] = nblk > 0 ? __uint_as_float(a0[e]) : 0.0f;
+                    uint32_t pk[8];
+                    pack8(o, c, pk);
+                    stage(c, pk);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) o[e] = nblk > 0 ? __uint_as_float(a1[e]) : 0.0f;
+                    pack8(o, c, hi[c]);
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bars->o_free);
+                store_rows(tok, dst);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) stage(c, hi[c]);
+                store_rows(tok, dst + 64);
+            }
+            if (tok >= 0 && row0 + r < n_rows)
+                lse[static_cast<int64_t>(h) * n_rows + row0 + r] = l > 0.0f ? (m + log2f(l)) * kLn2 : -INFINITY;
         }
     }
     tc::tc_fence_before();
