@@ -155,6 +155,162 @@ swiglu_bwd_kernel(const uint32_t *__restrict__ dh, const uint32_t *__restrict__ 
 
 int grid_of(int64_t work) { return static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 16)); }
 
+// ---- 16-byte forms of the same kernels (8 bf16 per access), used when the
+// widths are multiples of 8 and the rows 16-byte aligned; same arithmetic.
+__device__ __forceinline__ void unpack8(uint4 w, float (&f)[8]) {
+    const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(a[i] << 16);
+        f[2 * i + 1] = __uint_as_float(a[i] & 0xFFFF0000u);
+    }
+}
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+}
+
+// one thread per (token, head, 8 pairs)
+__global__ void __launch_bounds__(256)
+rope_qkv_fwd_v8_kernel(const uint16_t *__restrict__ qkv, const float *__restrict__ cosv, const float *__restrict__ sinv,
+                       int B, int S, int H, int hd, uint16_t *__restrict__ q, uint16_t *__restrict__ k,
+                       uint16_t *__restrict__ v) {
+    const int half = hd / 2, ng = half / 8;
+    const int64_t total = static_cast<int64_t>(B) * S * H * ng;
+    const int64_t d3 = 3LL * H * hd;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i % ng) * 8;
+        const int64_t th = i / ng;
+        const int h = static_cast<int>(th % H);
+        const int64_t tok = th / H;
+        const int s = static_cast<int>(tok % S);
+        const uint16_t *row = qkv + tok * d3 + static_cast<int64_t>(h) * hd;
+        const float *cs = cosv + static_cast<int64_t>(s) * hd, *sn = sinv + static_cast<int64_t>(s) * hd;
+        float c1[8], c2[8], s1[8], s2[8];
+#pragma unroll
+        for (int j = 0; j < 8; j += 4) {
+            *reinterpret_cast<float4 *>(c1 + j) = *reinterpret_cast<const float4 *>(cs + p + j);
+            *reinterpret_cast<float4 *>(c2 + j) = *reinterpret_cast<const float4 *>(cs + p + half + j);
+            *reinterpret_cast<float4 *>(s1 + j) = *reinterpret_cast<const float4 *>(sn + p + j);
+            *reinterpret_cast<float4 *>(s2 + j) = *reinterpret_cast<const float4 *>(sn + p + half + j);
+        }
+        const int64_t o = (tok * H + h) * hd;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const uint16_t *src = row + static_cast<int64_t>(w) * H * hd;
+            float x1[8], x2[8], y1[8], y2[8];
+            unpack8(*reinterpret_cast<const uint4 *>(src + p), x1);
+            unpack8(*reinterpret_cast<const uint4 *>(src + p + half), x2);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                y1[j] = __fadd_rn(__fmul_rn(x1[j], c1[j]), __fmul_rn(-x2[j], s1[j]));
+                y2[j] = __fadd_rn(__fmul_rn(x2[j], c2[j]), __fmul_rn(x1[j], s2[j]));
+            }
+            uint16_t *dst = (w == 0 ? q : k) + o;
+            *reinterpret_cast<uint4 *>(dst + p) = pack8(y1);
+            *reinterpret_cast<uint4 *>(dst + p + half) = pack8(y2);
+        }
+        const uint16_t *vs = row + 2LL * H * hd;
+        *reinterpret_cast<uint4 *>(v + o + p) = *reinterpret_cast<const uint4 *>(vs + p);
+        *reinterpret_cast<uint4 *>(v + o + p + half) = *reinterpret_cast<const uint4 *>(vs + p + half);
+    }
+}
+
+__global__ void __launch_bounds__(256)
+rope_qkv_bwd_v8_kernel(const uint16_t *__restrict__ dq, const uint16_t *__restrict__ dk,
+                       const uint16_t *__restrict__ dv, const float *__restrict__ cosv,
+                       const float *__restrict__ sinv, int B, int S, int H, int hd, uint16_t *__restrict__ dqkv) {
+    const int half = hd / 2, ng = half / 8;
+    const int64_t total = static_cast<int64_t>(B) * S * H * ng;
+    const int64_t d3 = 3LL * H * hd;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int p = static_cast<int>(i % ng) * 8;
+        const int64_t th = i / ng;
+        const int h = static_cast<int>(th % H);
+        const int64_t tok = th / H;
+        const int s = static_cast<int>(tok % S);
+        uint16_t *row = dqkv + tok * d3 + static_cast<int64_t>(h) * hd;
+        const float *cs = cosv + static_cast<int64_t>(s) * hd, *sn = sinv + static_cast<int64_t>(s) * hd;
+        float c1[8], c2[8], s1[8], s2[8];
+#pragma unroll
+        for (int j = 0; j < 8; j += 4) {
+            *reinterpret_cast<float4 *>(c1 + j) = *reinterpret_cast<const float4 *>(cs + p + j);
+            *reinterpret_cast<float4 *>(c2 + j) = *reinterpret_cast<const float4 *>(cs + p + half + j);
+            *reinterpret_cast<float4 *>(s1 + j) = *reinterpret_cast<const float4 *>(sn + p + j);
+            *reinterpret_cast<float4 *>(s2 + j) = *reinterpret_cast<const float4 *>(sn + p + half + j);
+        }
+        const int64_t o = (tok * H + h) * hd;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+            const uint16_t *g = (w == 0 ? dq : dk) + o;
+            float g1[8], g2[8], d1[8], d2[8];
+            unpack8(*reinterpret_cast<const uint4 *>(g + p), g1);
+            unpack8(*reinterpret_cast<const uint4 *>(g + p + half), g2);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                d1[j] = __fadd_rn(__fmul_rn(g1[j], c1[j]), __fmul_rn(g2[j], s2[j]));
+                d2[j] = __fadd_rn(__fmul_rn(g2[j], c2[j]), -__fmul_rn(g1[j], s1[j]));
+            }
+            uint16_t *dst = row + static_cast<int64_t>(w) * H * hd;
+            *reinterpret_cast<uint4 *>(dst + p) = pack8(d1);
+            *reinterpret_cast<uint4 *>(dst + p + half) = pack8(d2);
+        }
+        uint16_t *dvd = row + 2LL * H * hd;
+        *reinterpret_cast<uint4 *>(dvd + p) = *reinterpret_cast<const uint4 *>(dv + o + p);
+        *reinterpret_cast<uint4 *>(dvd + p + half) = *reinterpret_cast<const uint4 *>(dv + o + p + half);
+    }
+}
+
+// 8 columns per thread
+__global__ void __launch_bounds__(256)
+swiglu_fwd_v8_kernel(const uint4 *__restrict__ gu, int64_t N, int f, uint4 *__restrict__ h) {
+    const int fv = f / 8;
+    const int64_t total = N * fv;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / fv;
+        const int c = static_cast<int>(i - t * fv);
+        float g[8], u[8], r[8];
+        unpack8(gu[t * 2 * fv + c], g);
+        unpack8(gu[t * 2 * fv + fv + c], u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) r[j] = __fmul_rn(bf(tobf(silu_f(g[j]))), u[j]);
+        h[t * fv + c] = pack8(r);
+    }
+}
+
+__global__ void __launch_bounds__(256)
+swiglu_bwd_v8_kernel(const uint4 *__restrict__ dh, const uint4 *__restrict__ gu, int64_t N, int f,
+                     uint4 *__restrict__ dgu) {
+    const int fv = f / 8;
+    const int64_t total = N * fv;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / fv;
+        const int c = static_cast<int>(i - t * fv);
+        float g[8], u[8], d[8], dg[8], du[8];
+        unpack8(gu[t * 2 * fv + c], g);
+        unpack8(gu[t * 2 * fv + fv + c], u);
+        unpack8(dh[t * fv + c], d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            // one exp per element: silu(g) = g / (1 + e^-g), sigmoid = 1 / (1 + e^-g)
+            const float den = __fadd_rn(1.0f, expf(-g[j]));
+            const float a = bf(tobf(__fdiv_rn(g[j], den)));
+            const float da = bf(tobf(__fmul_rn(d[j], u[j])));
+            du[j] = __fmul_rn(d[j], a);
+            const float sg = __fdiv_rn(1.0f, den);
+            dg[j] = __fmul_rn(__fmul_rn(da, sg), __fadd_rn(1.0f, __fmul_rn(g[j], __fsub_rn(1.0f, sg))));
+        }
+        dgu[t * 2 * fv + c] = pack8(dg);
+        dgu[t * 2 * fv + fv + c] = pack8(du);
+    }
+}
+
+bool al16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 // ------------------------------------------------------------------ residual add + RMSNorm
 // x_new = x + scale * delta (the sublayer's output added to the fp32 residual
 // stream; scale is a device scalar or absent), then the Llama RMSNorm of x_new:
@@ -330,6 +486,13 @@ cudaError_t launch_rope_qkv_fwd(const void *qkv, const float *cosv, const float 
                                 void *q, void *k, void *v, cudaStream_t st) {
     const int64_t work = static_cast<int64_t>(B) * S * H * (hd / 2);
     if (work == 0) return cudaSuccess;
+    if (hd % 16 == 0 && al16(qkv) && al16(q) && al16(k) && al16(v) && al16(cosv) && al16(sinv)) {
+        rope_qkv_fwd_v8_kernel<<<grid_of(work / 8), 256, 0, st>>>(
+            static_cast<const uint16_t *>(qkv), cosv, sinv, B, S, H, hd, static_cast<uint16_t *>(q),
+            static_cast<uint16_t *>(k), static_cast<uint16_t *>(v));
+        count_launch();
+        return cudaGetLastError();
+    }
     rope_qkv_fwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint16_t *>(qkv), cosv, sinv, B, S, H, hd,
                                                        static_cast<uint16_t *>(q), static_cast<uint16_t *>(k),
                                                        static_cast<uint16_t *>(v));
@@ -341,6 +504,13 @@ cudaError_t launch_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, 
                                 int B, int S, int H, int hd, void *dqkv, cudaStream_t st) {
     const int64_t work = static_cast<int64_t>(B) * S * H * (hd / 2);
     if (work == 0) return cudaSuccess;
+    if (hd % 16 == 0 && al16(dq) && al16(dk) && al16(dv) && al16(dqkv) && al16(cosv) && al16(sinv)) {
+        rope_qkv_bwd_v8_kernel<<<grid_of(work / 8), 256, 0, st>>>(
+            static_cast<const uint16_t *>(dq), static_cast<const uint16_t *>(dk), static_cast<const uint16_t *>(dv),
+            cosv, sinv, B, S, H, hd, static_cast<uint16_t *>(dqkv));
+        count_launch();
+        return cudaGetLastError();
+    }
     rope_qkv_bwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint16_t *>(dq),
                                                        static_cast<const uint16_t *>(dk),
                                                        static_cast<const uint16_t *>(dv), cosv, sinv, B, S, H, hd,
@@ -352,6 +522,12 @@ cudaError_t launch_rope_qkv_bwd(const void *dq, const void *dk, const void *dv, 
 cudaError_t launch_swiglu_fwd(const void *gu, int64_t N, int f, void *h, cudaStream_t st) {
     const int64_t work = N * (f / 2);
     if (work == 0) return cudaSuccess;
+    if (f % 8 == 0 && al16(gu) && al16(h)) {
+        swiglu_fwd_v8_kernel<<<grid_of(work / 4), 256, 0, st>>>(static_cast<const uint4 *>(gu), N, f,
+                                                                 static_cast<uint4 *>(h));
+        count_launch();
+        return cudaGetLastError();
+    }
     swiglu_fwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint32_t *>(gu), N, f,
                                                      static_cast<uint32_t *>(h));
     count_launch();
@@ -361,6 +537,13 @@ cudaError_t launch_swiglu_fwd(const void *gu, int64_t N, int f, void *h, cudaStr
 cudaError_t launch_swiglu_bwd(const void *dh, const void *gu, int64_t N, int f, void *dgu, cudaStream_t st) {
     const int64_t work = N * (f / 2);
     if (work == 0) return cudaSuccess;
+    if (f % 8 == 0 && al16(dh) && al16(gu) && al16(dgu)) {
+        swiglu_bwd_v8_kernel<<<grid_of(work / 4), 256, 0, st>>>(static_cast<const uint4 *>(dh),
+                                                                 static_cast<const uint4 *>(gu), N, f,
+                                                                 static_cast<uint4 *>(dgu));
+        count_launch();
+        return cudaGetLastError();
+    }
     swiglu_bwd_kernel<<<grid_of(work), 256, 0, st>>>(static_cast<const uint32_t *>(dh),
                                                      static_cast<const uint32_t *>(gu), N, f,
                                                      static_cast<uint32_t *>(dgu));

@@ -6,6 +6,8 @@ attention) and the SwiGLU gate (LlamaMLP's silu(gate) * up in bf16), forward
 and backward.
 
 RoPE is bit-exact (the same fp32 products and sums, no fused multiply-add).
+Both kernels have a 16-byte vector form and an element form (head_dim not a
+multiple of 16, gate width not a multiple of 8): the shapes cover both.
 SwiGLU goes through expf and one division like torch's kernels; a result
 may still land one bf16 rounding step apart where torch's exp differs in the
 last fp32 bit, so it is held to at most one bf16 ulp, on under 0.1 % of the
@@ -27,7 +29,7 @@ def _rope_ref(qkv, cos, sin, H):
     return apply_rope(q, cos, sin).bfloat16(), apply_rope(k, cos, sin).bfloat16(), v
 
 
-@pytest.mark.parametrize("B,S,H,hd", [(2, 300, 4, 64), (1, 128, 2, 128), (1, 17, 3, 32)])
+@pytest.mark.parametrize("B,S,H,hd", [(2, 300, 4, 64), (1, 128, 2, 128), (1, 17, 3, 32), (1, 9, 2, 24)])
 def test_rope_qkv_matches_torch_bitwise(B, S, H, hd):
     from naylis_b200 import trunk
     from naylis_b200.decoder import rope_tables
@@ -46,7 +48,7 @@ def test_rope_qkv_matches_torch_bitwise(B, S, H, hd):
     assert torch.equal(qkv.grad, qkv2.grad)
 
 
-@pytest.mark.parametrize("N,f", [(4096, 2816), (333, 64)])
+@pytest.mark.parametrize("N,f", [(4096, 2816), (333, 64), (50, 36)])
 def test_swiglu_matches_torch(N, f):
     from naylis_b200 import trunk
     torch.manual_seed(1)
