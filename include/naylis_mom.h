@@ -240,6 +240,21 @@ MOM_API int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const flo
                                 const float *dx_in, int64_t N, int64_t d, float *dx, void *ddelta, float *dw,
                                 float *ddelta_scale, void *stream);
 
+/* mom_xent_fwd: the causal-LM loss of model.py:539-551 (NaylisLlamaForCausalLM:
+ * cross_entropy(logits.float(), labels, reduction="sum") over the shifted rows,
+ * then divided by the count of labels != ignore_index) without materialising the
+ * fp32 logits: logits (R, V) bf16 as the LM head's autocast GEMM writes them,
+ * labels (R) int64; row_loss (R) fp32 = logsumexp(row) - row[label] (0 where
+ * label == ignore_index, NaN where the label is outside [0, V)), lse (R) fp32
+ * for the backward. The caller sums row_loss and divides.
+ * mom_xent_bwd: dlogits (R, V) bf16 = ((softmax(row) - onehot(label)) * *grad)
+ * rounded to bf16, 0 on ignored rows; grad is a device scalar, the gradient of
+ * the sum of row_loss. */
+MOM_API int mom_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int64_t V, int64_t ignore_index,
+                         float *row_loss, float *lse, void *stream);
+MOM_API int mom_xent_bwd(const void *logits, const int64_t *labels, const float *lse, const float *grad, int64_t R,
+                         int64_t V, int64_t ignore_index, void *dlogits, void *stream);
+
 /* mom_read_bwd without a workspace argument: for callers that cannot allocate
  * device memory (a plugin whose host framework's caching allocator owns the
  * device, or an FFI caller with no device allocator). It has no counterpart

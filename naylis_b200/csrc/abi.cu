@@ -769,6 +769,33 @@ int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, c
     return e == cudaSuccess ? MOM_OK : cuda_fail(e, "add_rmsnorm_bwd");
 }
 
+int mom_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int64_t V, int64_t ignore_index,
+                 float *row_loss, float *lse, void *stream) {
+    MOM_REQUIRE(R >= 0 && V > 0 && V < (int64_t(1) << 31), "bad cross-entropy geometry");
+    if (R == 0) return MOM_OK;
+    MOM_REQUIRE(logits && labels && row_loss && lse, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(logits) & 1) == 0, "logits must be 2-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_xent_fwd(logits, labels, R, (int)V, ignore_index, row_loss, lse,
+                                         static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "xent_fwd");
+}
+
+int mom_xent_bwd(const void *logits, const int64_t *labels, const float *lse, const float *grad, int64_t R, int64_t V,
+                 int64_t ignore_index, void *dlogits, void *stream) {
+    MOM_REQUIRE(R >= 0 && V > 0 && V < (int64_t(1) << 31), "bad cross-entropy geometry");
+    if (R == 0) return MOM_OK;
+    MOM_REQUIRE(logits && labels && lse && grad && dlogits, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(logits) & 1) == 0 && (reinterpret_cast<uintptr_t>(dlogits) & 1) == 0,
+                "logits and dlogits must be 2-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_xent_bwd(logits, labels, lse, grad, R, (int)V, ignore_index, dlogits,
+                                         static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "xent_bwd");
+}
+
 // ------------------------------------------------- read backward, no allocation
 // mom_read_bwd_noalloc runs mom_read_bwd with its workspace (the per-row delta,
 // H x B*S fp32) in a fixed device array of this library instead of caller

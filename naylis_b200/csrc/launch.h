@@ -185,5 +185,11 @@ cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const 
                                    const float *dscale_in, const void *dy16, const float *dy32, const float *dx_in,
                                    int64_t N, int d, float *dx, void *ddelta, float *dw, float *dscale,
                                    cudaStream_t st);
+// LM-head cross-entropy over bf16 logits (R, V): per-row loss (0 on ignored rows)
+// and log-sum-exp; backward dlogits = bf16((softmax - onehot) * (*grad)).
+cudaError_t launch_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int V, int64_t ignore_index,
+                            float *row_loss, float *lse, cudaStream_t st);
+cudaError_t launch_xent_bwd(const void *logits, const int64_t *labels, const float *lse, const float *grad, int64_t R,
+                            int V, int64_t ignore_index, void *dlogits, cudaStream_t st);
 
 }  // namespace mom

@@ -480,6 +480,140 @@ add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict_
     if (DDT != 0 && dscale && threadIdx.x == 0) atomicAdd(dscale, sdw[d]);
 }
 
+// ---------------------------------------------------------------- LM-head cross-entropy
+// The reference's loss (model.py:539-551): the LM head's logits (R, V) as the
+// bf16 autocast GEMM leaves them, upcast to fp32, cross_entropy(reduction="sum")
+// over the rows whose label is not ignore_index, divided by their count (the
+// division stays in torch). Forward, one CTA per row: each thread keeps a running
+// (max m, sum s of e^(x - m)) over 16-byte vectors of the row, the CTA combines
+// them, lse = m + ln(s), row loss = lse - x[label] (0 on ignored rows, NaN when
+// the label is outside [0, V)). The row is read once; the fp32 log-softmax torch
+// materialises (and its cast) are never formed. Backward: dlogits =
+// bf16((e^(x - lse) - [j == label]) * g) with g the gradient of the sum, 0 on
+// ignored rows (what torch's log-softmax / nll backward and the cast to the
+// GEMM's bf16 give).
+constexpr int kXentThreads = 256;
+
+__device__ __forceinline__ void xent_merge(float &m, float &s, float m2, float s2) {
+    const float mm = fmaxf(m, m2);
+    if (mm == -INFINITY) return;   // both empty
+    s = s * exp2f((m - mm) * kLog2e) + s2 * exp2f((m2 - mm) * kLog2e);
+    m = mm;
+}
+
+__device__ __forceinline__ void xent_add(float &m, float &s, const float (&x)[8]) {
+    float mx = x[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, x[i]);
+    if (mx > m) {
+        s = (m == -INFINITY) ? 0.0f : s * exp2f((m - mx) * kLog2e);
+        m = mx;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += exp2f((x[i] - m) * kLog2e);
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kXentThreads)
+xent_fwd_kernel(const uint16_t *__restrict__ logits, const int64_t *__restrict__ labels, int64_t R, int V,
+                int64_t ignore_index, float *__restrict__ row_loss, float *__restrict__ lse_out) {
+    __shared__ float sm[kXentThreads / 32], ss[kXentThreads / 32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+        const uint16_t *row = logits + r * V;
+        float m = -INFINITY, s = 0.0f;
+        if constexpr (kVec) {
+            const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+            const int nv = V / 8;
+            int j = threadIdx.x;
+            // two vectors in flight per thread
+            for (; j + kXentThreads < nv; j += 2 * kXentThreads) {
+                const uint4 a = __ldcs(rv + j), b = __ldcs(rv + j + kXentThreads);
+                float xa[8], xb[8];
+                unpack8(a, xa);
+                unpack8(b, xb);
+                xent_add(m, s, xa);
+                xent_add(m, s, xb);
+            }
+            if (j < nv) {
+                float xa[8];
+                unpack8(__ldcs(rv + j), xa);
+                xent_add(m, s, xa);
+            }
+        } else {
+            for (int j = threadIdx.x; j < V; j += kXentThreads) {
+                const float x = bf(row[j]);
+                if (x > m) {
+                    s = (m == -INFINITY) ? 0.0f : s * exp2f((m - x) * kLog2e);
+                    m = x;
+                }
+                s += exp2f((x - m) * kLog2e);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+            xent_merge(m, s, m2, s2);
+        }
+        if (lane == 0) {
+            sm[warp] = m;
+            ss[warp] = s;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float M = sm[0], Ssum = ss[0];
+            for (int w = 1; w < kXentThreads / 32; ++w) xent_merge(M, Ssum, sm[w], ss[w]);
+            const float l = M + logf(Ssum);
+            const int64_t lab = labels[r];
+            float loss = 0.0f;
+            if (lab != ignore_index) loss = (lab >= 0 && lab < V) ? l - bf(row[lab]) : __int_as_float(0x7fc00000);
+            row_loss[r] = loss;
+            lse_out[r] = l;
+        }
+        __syncthreads();
+    }
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kXentThreads)
+xent_bwd_kernel(const uint16_t *__restrict__ logits, const int64_t *__restrict__ labels,
+                const float *__restrict__ lse, const float *__restrict__ grad, int64_t R, int V, int64_t ignore_index,
+                uint16_t *__restrict__ dlogits) {
+    const float g = *grad;
+    for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+        const int64_t lab = labels[r];
+        const bool ignored = lab == ignore_index;
+        const bool bad = !ignored && (lab < 0 || lab >= V);
+        const float l = lse[r];
+        const uint16_t *row = logits + r * V;
+        uint16_t *drow = dlogits + r * V;
+        auto grad_of = [&](float x, int j) -> float {
+            if (ignored) return 0.0f;
+            if (bad) return __int_as_float(0x7fc00000);
+            // x - lse first (exact when they are close, where p - 1 cancels), then the exponential
+            const float p = exp2f((x - l) * kLog2e);
+            return (j == lab ? p - 1.0f : p) * g;
+        };
+        if constexpr (kVec) {
+            const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+            uint4 *dv = reinterpret_cast<uint4 *>(drow);
+            const int nv = V / 8;
+            for (int j = threadIdx.x; j < nv; j += kXentThreads) {
+                float x[8];
+                unpack8(__ldcs(rv + j), x);
+                uint32_t o[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    o[i] = static_cast<uint32_t>(tobf(grad_of(x[2 * i], 8 * j + 2 * i))) |
+                           (static_cast<uint32_t>(tobf(grad_of(x[2 * i + 1], 8 * j + 2 * i + 1))) << 16);
+                __stcs(dv + j, make_uint4(o[0], o[1], o[2], o[3]));
+            }
+        } else {
+            for (int j = threadIdx.x; j < V; j += kXentThreads) drow[j] = tobf(grad_of(bf(row[j]), j));
+        }
+    }
+}
+
 }  // namespace
 
 cudaError_t launch_rope_qkv_fwd(const void *qkv, const float *cosv, const float *sinv, int B, int S, int H, int hd,
@@ -596,6 +730,33 @@ cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const 
     else if (nv == 2) { MOM_NORM_BD(2) } else if (nv == 1) { MOM_NORM_BD(1) } else { return cudaErrorInvalidValue; }
 #undef MOM_NORM_BD
 #undef MOM_NORM_B
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int V, int64_t ignore_index,
+                            float *row_loss, float *lse, cudaStream_t st) {
+    if (R == 0) return cudaSuccess;
+    const int grid = static_cast<int>(std::min<int64_t>(R, 148 * 64));
+    auto lg = static_cast<const uint16_t *>(logits);
+    if (V % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0)
+        xent_fwd_kernel<true><<<grid, kXentThreads, 0, st>>>(lg, labels, R, V, ignore_index, row_loss, lse);
+    else
+        xent_fwd_kernel<false><<<grid, kXentThreads, 0, st>>>(lg, labels, R, V, ignore_index, row_loss, lse);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t launch_xent_bwd(const void *logits, const int64_t *labels, const float *lse, const float *grad, int64_t R,
+                            int V, int64_t ignore_index, void *dlogits, cudaStream_t st) {
+    if (R == 0) return cudaSuccess;
+    const int grid = static_cast<int>(std::min<int64_t>(R, 148 * 64));
+    auto lg = static_cast<const uint16_t *>(logits);
+    auto dl = static_cast<uint16_t *>(dlogits);
+    if (V % 8 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (reinterpret_cast<uintptr_t>(dlogits) & 15) == 0)
+        xent_bwd_kernel<true><<<grid, kXentThreads, 0, st>>>(lg, labels, lse, grad, R, V, ignore_index, dl);
+    else
+        xent_bwd_kernel<false><<<grid, kXentThreads, 0, st>>>(lg, labels, lse, grad, R, V, ignore_index, dl);
     count_launch();
     return cudaGetLastError();
 }

@@ -31,7 +31,9 @@ points: the rotation writes q/k/v straight into the token-major layout
 attention reads, the add + norm writes the fp32 residual stream and the bf16
 input of the next projection in one pass, and the layer's mom_scale factor
 rides on the add that follows the memory read. The rotary tables are built
-once per forward for all layers.
+once per forward for all layers. The loss reads the LM head's bf16 logits once
+(csrc/trunk.cu, cross-entropy): the fp32 copy of the logits and torch's fp32
+log-softmax are never formed.
 """
 from __future__ import annotations
 
@@ -276,7 +278,11 @@ class NaylisForCausalLM(nn.Module):
         shift_h = h[:, :-1].reshape(-1, h.shape[-1])
         shift_labels = labels[:, 1:].reshape(-1)
         logits = self.lm_head(shift_h)
-        loss = F.cross_entropy(logits.float(), shift_labels, reduction="sum")
+        if logits.is_cuda and logits.dtype == torch.bfloat16:
+            # fused (csrc/trunk.cu): the same fp32 math on the bf16 logits, no fp32 copy
+            loss = trunk.cross_entropy_sum(logits, shift_labels)
+        else:
+            loss = F.cross_entropy(logits.float(), shift_labels, reduction="sum")
         loss = loss / (shift_labels != -100).sum().clamp_min(1)
         if self.training:
             loss = loss + self.mom_aux_weight * self.mom_aux_loss(h.device)

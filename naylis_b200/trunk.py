@@ -1,5 +1,6 @@
 """Autograd wrappers of the decoder trunk's fused bf16 kernels (csrc/trunk.cu):
-the rotary embedding of the fused q/k/v projection and the SwiGLU gate.
+the rotary embedding of the fused q/k/v projection, the SwiGLU gate, the
+residual add + RMSNorm and the LM head's cross-entropy.
 
 Both reproduce the rounding points of the reference's trunk under bf16
 autocast (transformers' Llama apply_rotary_pos_emb and LlamaMLP); they take
@@ -91,9 +92,6 @@ def swiglu(gu):
     return _SwiGLU.apply(gu)
 
 
-__all__ = ["rope_qkv", "swiglu"]
-
-
 class _AddRMSNorm(torch.autograd.Function):
     """x_new = x + s * delta, y = RMSNorm(x_new) (bf16, and fp32 when asked)."""
 
@@ -156,4 +154,40 @@ def add_rmsnorm(x, delta, weight, eps: float, scale=None, want_f32: bool = False
     return _AddRMSNorm.apply(x, delta, scale, weight, float(eps), bool(want_f32))
 
 
-__all__ = ["rope_qkv", "swiglu", "add_rmsnorm"]
+class _CrossEntropySum(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, logits, labels, ignore_index):
+        R, V = logits.shape
+        logits = logits.contiguous()
+        labels = labels.to(torch.int64).contiguous()
+        row_loss = torch.empty(R, dtype=torch.float32, device=logits.device)
+        lse = torch.empty(R, dtype=torch.float32, device=logits.device)
+        _lib.call("mom_xent_fwd", logits.data_ptr(), labels.data_ptr(), R, V, int(ignore_index),
+                  row_loss.data_ptr(), lse.data_ptr(), _stream(logits))
+        ctx.save_for_backward(logits, labels, lse)
+        ctx.ignore_index = int(ignore_index)
+        return row_loss.sum()
+
+    @staticmethod
+    def backward(ctx, grad):
+        logits, labels, lse = ctx.saved_tensors
+        R, V = logits.shape
+        g = grad.detach().to(torch.float32).reshape(1).contiguous()
+        dlogits = torch.empty_like(logits)
+        _lib.call("mom_xent_bwd", logits.data_ptr(), labels.data_ptr(), lse.data_ptr(), g.data_ptr(), R, V,
+                  ctx.ignore_index, dlogits.data_ptr(), _stream(logits))
+        return dlogits, None, None
+
+
+def cross_entropy_sum(logits, labels, ignore_index: int = -100):
+    """sum over rows of cross_entropy(logits.float(), labels) for bf16 logits
+    (R, V) and int labels (R), rows with label == ignore_index counting 0: the
+    reference's loss before its division by the count of valid labels, without
+    the fp32 copy of the logits. Its gradient is bf16, like the LM head's."""
+    _need_bf16(logits)
+    if logits.dim() != 2 or labels.shape != logits.shape[:1]:
+        raise RuntimeError("cross_entropy_sum: logits (R, V) and labels (R,)")
+    return _CrossEntropySum.apply(logits, labels, int(ignore_index))
+
+
+__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum"]

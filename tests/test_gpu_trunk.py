@@ -120,3 +120,31 @@ def test_add_rmsnorm_matches_torch(delta_dtype, scaled, want_f32):
         assert err(delta.grad, dr.grad) < tol
     if scaled:
         assert abs(float(s.grad) - float(sr.grad)) <= 1e-4 * abs(float(sr.grad))
+
+
+@pytest.mark.parametrize("R,V,scale", [(300, 32000, 1.0), (257, 1000, 30.0), (64, 1003, 3.0), (5, 8, 1.0)])
+def test_cross_entropy_matches_torch(R, V, scale):
+    """The LM head's loss (the reference's cross_entropy(logits.float(), labels,
+    reduction="sum"), labels -100 ignored) from bf16 logits against torch on
+    the same values: the loss within 1e-5 relative (the kernel sums e^(x - m)
+    in another order and through exp2), the bf16 logit gradient within one bf16
+    rounding step of torch's fp32 gradient cast to bf16. V = 1003 takes the
+    element form of the kernels; scale 30 makes the running maximum move."""
+    from naylis_b200 import trunk
+    torch.manual_seed(3)
+    dev = torch.device("cuda")
+    logits = (scale * torch.randn(R, V, device=dev)).bfloat16().requires_grad_(True)
+    labels = torch.randint(0, V, (R,), device=dev)
+    labels[::7] = -100
+    loss = trunk.cross_entropy_sum(logits, labels)
+    ref_in = logits.detach().float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(ref_in, labels, reduction="sum")
+    assert abs(float(loss) - float(ref)) <= 1e-5 * abs(float(ref)) + 1e-5
+    g = 0.37
+    (loss * g).backward()
+    (ref * g).backward()
+    got = logits.grad.float()
+    want = ref_in.grad
+    assert torch.all(got[labels == -100] == 0)
+    # one bf16 step of the fp32 value, or an fp32 ulp-level absolute floor
+    assert ((got - want).abs() <= want.abs() * 2.0 ** -7 + 1e-7).all()
