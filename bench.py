@@ -44,10 +44,18 @@ METRIC = "MoM layer fwd+bwd tokens/s (router + read + projections), BASELINE con
 WORKLOAD = ("cfg2: one MoM layer fwd+bwd per GPU, B=8 S=2048 d=1024, 16x64 heads, "
             "bank 8x128 slots, router rank 32, top-2, bf16 autocast, fp32 master weights")
 
-# DRAM bytes per launch of the read's tensor-core kernels on this workload, measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum; forward 39.1 MB, dQ 85.6 MB, dK/dV 92.2 MB):
-# the roofline's traffic figure.
-READ_TRAFFIC_BYTES = (39.1 + 85.6 + 92.2) * 1e6
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum, MB) per launch of every kernel on
+# the read path at config 2, medians of one ncu capture (profiles/read_path_dram_bytes_cfg2.md):
+# the roofline's traffic figure covers the whole read, bucketing and row passes included.
+READ_TRAFFIC_MB = {"bucket (4 kernels)": 1.26, "permute_rows (q -> plan order)": 33.65,
+                   "read_fwd_tc": 39.42, "row_delta (dO copy + delta)": 70.24, "read_bwd_dq_tc": 79.93,
+                   "read_bwd_dkdv_tc": 86.34}
+READ_TRAFFIC_BYTES = sum(READ_TRAFFIC_MB.values()) * 1e6
+# Algorithmic bytes of the read fwd + bwd at config 2 (N = 16384 tokens, H*hd = 1024 bf16,
+# bank 1024 slots): forward Q + K + V in, O + lse out; backward Q, K, V, O (for delta), dO,
+# lse in, dQ, fp32 dK / dV out.
+READ_ALGO_BYTES = ((16384 * 2048) * 2 + 4 * 1024 * 1024 + 16384 * 16 * 4
+                   + (16384 * 2048) * 4 + 4 * 1024 * 1024 + 16384 * 16 * 4 + 8 * 1024 * 1024)
 
 
 def read_flops(N, d, top, bs):
@@ -291,9 +299,11 @@ def run_layer_cfg2(args):
             "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
                          "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
                          "traffic": READ_TRAFFIC_BYTES,
-                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum of the three tensor-core "
-                                          "read kernels (fwd 39.1 + dq 85.6 + dkdv 92.2 MB), one ncu capture "
-                                          "each of this workload; bucketing and row copies not included"),
+                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum summed over every kernel "
+                                          "of the read path on config 2 (ncu medians, MB): "
+                                          + ", ".join(f"{k} {v}" for k, v in READ_TRAFFIC_MB.items())),
+                         "algorithmic_bytes": READ_ALGO_BYTES,
+                         "traffic_over_algorithmic": round(READ_TRAFFIC_BYTES / READ_ALGO_BYTES, 2),
                          "kernel": "MoM read fwd+bwd (bucket + fwd + dq + dkdv)",
                          "flops_per_launch": roof["flops"], "ms_per_launch": roof["ms"],
                          "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
@@ -450,9 +460,11 @@ def run_model_cfg3(args):
             "roofline": {"bound": "tensor", "achieved": roof["tflops"], "peak": pk["bf16"],
                          "unit": "TFLOP/s", "frac": round(roof["tflops"] / pk["bf16"], 4),
                          "traffic": READ_TRAFFIC_BYTES,
-                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum of the three tensor-core "
-                                          "read kernels (fwd 39.1 + dq 85.6 + dkdv 92.2 MB), one ncu capture "
-                                          "each on config 2; bucketing and row copies not included"),
+                         "traffic_note": ("dram__bytes_read.sum + dram__bytes_write.sum summed over every kernel "
+                                          "of the read path on config 2 (ncu medians, MB): "
+                                          + ", ".join(f"{k} {v}" for k, v in READ_TRAFFIC_MB.items())),
+                         "algorithmic_bytes": READ_ALGO_BYTES,
+                         "traffic_over_algorithmic": round(READ_TRAFFIC_BYTES / READ_ALGO_BYTES, 2),
                          "kernel": "MoM read fwd+bwd on BASELINE config 2 (bucket + fwd + dq + dkdv), C ABI",
                          "flops_per_launch": roof["flops"], "ms_per_launch": roof["ms"],
                          "peak_source": f"{pk['src']} bf16 burst (MEASURED_PEAKS.json bf16_tflops)"},
@@ -802,6 +814,84 @@ def run_reference(args):
     }), flush=True)
 
 
+# ------------------------------------------------------------------ decoder trunk kernels
+def run_trunk(args):
+    """The decoder trunk's fused kernels (csrc/trunk.cu) alone at BASELINE
+    config 3's sizes (B=8 x S=2048 tokens, d=1024, 16x64 heads, SwiGLU 2816),
+    each timed with CUDA events on the launching stream over --steps calls
+    after --warmup, L2 flushed before each call; achieved = algorithmic bytes
+    (each input read once, each output written once) / time, against the
+    measured HBM copy bandwidth. These kernels move bytes only."""
+    import torch
+    from naylis_b200 import _lib
+    from naylis_b200.decoder import rope_tables
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S, d, H, f = CFG3["B"], CFG3["S"], 1024, 16, 2816
+    hd, N = d // H, B * S
+    g = torch.Generator(device=dev).manual_seed(5)
+    bf = torch.bfloat16
+    qkv = torch.randn(N, 3 * d, generator=g, device=dev).to(bf)
+    q, k, v = (torch.empty(N, d, dtype=bf, device=dev) for _ in range(3))
+    dqkv = torch.empty_like(qkv)
+    cos, sin = rope_tables(S, hd, 500000.0, dev)
+    gu = torch.randn(N, 2 * f, generator=g, device=dev).to(bf)
+    h = torch.empty(N, f, dtype=bf, device=dev)
+    dh = torch.randn(N, f, generator=g, device=dev).to(bf)
+    dgu = torch.empty_like(gu)
+    x = torch.randn(N, d, generator=g, device=dev)
+    delta = torch.randn(N, d, generator=g, device=dev).to(bf)
+    w = torch.ones(d, device=dev)
+    x_out, dx_in, dx = (torch.empty(N, d, device=dev) for _ in range(3))
+    y16, ddelta, dy16 = (torch.empty(N, d, dtype=bf, device=dev) for _ in range(3))
+    dy16.normal_()
+    dx_in.normal_()
+    rstd = torch.empty(N, device=dev)
+    dw = torch.empty(d, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    st = lambda: torch.cuda.current_stream(dev).cuda_stream
+    ops = {
+        "rope_qkv_fwd": (lambda: _lib.call("mom_rope_qkv_fwd", qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), B, S,
+                                           H, hd, q.data_ptr(), k.data_ptr(), v.data_ptr(), st()), 6 * N * d * 2),
+        "rope_qkv_bwd": (lambda: _lib.call("mom_rope_qkv_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                           cos.data_ptr(), sin.data_ptr(), B, S, H, hd, dqkv.data_ptr(), st()),
+                         6 * N * d * 2),
+        "swiglu_fwd": (lambda: _lib.call("mom_swiglu_fwd", gu.data_ptr(), N, f, h.data_ptr(), st()), 3 * N * f * 2),
+        "swiglu_bwd": (lambda: _lib.call("mom_swiglu_bwd", dh.data_ptr(), gu.data_ptr(), N, f, dgu.data_ptr(), st()),
+                       5 * N * f * 2),
+        "add_rmsnorm_fwd": (lambda: _lib.call("mom_add_rmsnorm_fwd", x.data_ptr(), delta.data_ptr(), _lib.BF16, None,
+                                              w.data_ptr(), N, d, 1e-5, x_out.data_ptr(), y16.data_ptr(), None,
+                                              rstd.data_ptr(), st()), N * d * 12),
+        "add_rmsnorm_bwd": (lambda: _lib.call("mom_add_rmsnorm_bwd", x_out.data_ptr(), rstd.data_ptr(), w.data_ptr(),
+                                              delta.data_ptr(), _lib.BF16, None, dy16.data_ptr(), None,
+                                              dx_in.data_ptr(), N, d, dx.data_ptr(), ddelta.data_ptr(),
+                                              dw.data_ptr(), None, st()), N * d * 16),
+    }
+    pk = peaks()
+    res = {}
+    for name, (fn, nbytes) in ops.items():
+        for _ in range(args.warmup):
+            fn()
+        ev = []
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            ev.append((a, b))
+        torch.cuda.synchronize()
+        us = sum(a.elapsed_time(b) for a, b in ev) / args.steps * 1e3
+        gbs = nbytes / (us / 1e6) / 1e9
+        res[name] = {"us": round(us, 2), "bytes": nbytes, "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / pk["hbm"], 4)}
+    print(json.dumps({"metric": "decoder trunk kernels, achieved HBM GB/s (BASELINE config 3 sizes)",
+                      "unit": "GB/s", "steps": args.steps, "warmup": args.warmup, "kernels": res,
+                      "hbm_peak_gbs": pk["hbm"], "peak_source": pk["src"],
+                      "config": {"workload": "trunk: N=16384 tokens, d=1024, 16x64 heads, SwiGLU 2816, bf16",
+                                 "l2": "flushed before each call (256 MiB write, untimed)"}}), flush=True)
+
+
 # ------------------------------------------------------------------ config-4 read
 CFG4 = dict(B=4, S=4096, H=16, hd=128, nb=32, bs=128, top=4)
 METRIC4 = "MoM read fwd+bwd tokens/s, BASELINE config 4 geometry (top-4 of 32 blocks, 16x128 heads)"
@@ -887,9 +977,10 @@ def main():
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
-    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg2", "read-top4of32"],
+    ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg2", "read-top4of32", "trunk"],
                     help="cfg3: the decoder training step (default); cfg2: one MoM layer step; "
-                         "read-top4of32: the read alone on config 4's geometry")
+                         "read-top4of32: the read alone on config 4's geometry; trunk: the decoder's fused "
+                         "trunk kernels alone")
     ap.add_argument("--bf16-grads", action="store_true", help="N>1: all-reduce the gradient buckets in bf16")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -898,6 +989,8 @@ def main():
         run_reference_model(args) if args.workload == "cfg3" else run_reference(args)
     elif args.workload == "read-top4of32":
         run_read_top4of32(args)
+    elif args.workload == "trunk":
+        run_trunk(args)
     elif args.workload == "cfg2":
         run_layer_cfg2(args)
     else:

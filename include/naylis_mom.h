@@ -122,6 +122,18 @@ MOM_API int mom_route_fwd_shard(const void *x, int x_dtype, int64_t B, int64_t S
                                 void *top_idx, int idx_dtype, float *gates, float *log_gates,
                                 void *act, void *workspace, size_t workspace_bytes, void *stream);
 
+/* The MoM load-balancing aux loss of one layer and its router logs
+ * (NaylisLlamaModel._collect_mom_aux_loss, model.py:476-517) from the router's
+ * probs (N, nb) fp32 and top_idx (N, top): out[0] = nb * sum_e frac_e * mean_e
+ * (frac_e = share of tokens that selected block e, mean_e = mean of probs[:, e]),
+ * out[1] = router entropy -mean_t sum_e p log(max(p, 1e-9)), out[2] = share of
+ * blocks no token selected, out[3 + e] = frac_e (the gradient of out[0] w.r.t.
+ * probs[t, e] is nb * frac_e / N). Deterministic (a fixed summation order); nb <= 256;
+ * out holds 3 + nb floats; the workspace is mom_router_aux_workspace_size bytes. */
+MOM_API size_t mom_router_aux_workspace_size(int64_t N, int64_t nb);
+MOM_API int mom_router_aux(const float *probs, const void *top_idx, int idx_dtype, int64_t N, int64_t nb,
+                           int64_t top, void *workspace, size_t workspace_bytes, float *out, void *stream);
+
 /* Router backward: autograd of the block above (model.py:186-220).
  * dlog_gates (B,S,top): gradient w.r.t. log_gates, or NULL; dgates: w.r.t. gates,
  * or NULL; dprobs (B,S,nb): w.r.t. probs (the aux load-balance loss), or NULL.

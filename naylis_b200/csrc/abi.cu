@@ -236,6 +236,24 @@ size_t mom_route_bwd_workspace_size(int64_t B, int64_t S, int64_t d, int64_t r, 
     return align256(N * nb * 4) + 2 * align256(N * r * 4);
 }
 
+size_t mom_router_aux_workspace_size(int64_t N, int64_t nb) {
+    if (N < 1 || nb < 1 || nb > 256) return 0;
+    return mom::router_aux_workspace_size(N, (int)nb);
+}
+
+int mom_router_aux(const float *probs, const void *top_idx, int idx_dtype, int64_t N, int64_t nb, int64_t top,
+                   void *workspace, size_t workspace_bytes, float *out, void *stream) {
+    MOM_REQUIRE(N > 0 && nb >= 1 && nb <= 256 && top >= 1 && top <= nb, "bad router geometry");
+    MOM_REQUIRE(is_idx_dtype(idx_dtype), "index dtype must be I32 or I64");
+    MOM_REQUIRE(probs && top_idx && out && workspace, "null pointer argument");
+    MOM_REQUIRE(workspace_bytes >= mom::router_aux_workspace_size(N, (int)nb), "workspace too small");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_router_aux(probs, top_idx, idx_dtype == MOM_I64, N, (int)nb, (int)top,
+                                           static_cast<float *>(workspace), out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "router_aux");
+}
+
 int mom_route_bwd(const void *x, int x_dtype, int64_t B, int64_t S, int64_t d, const void *w_down,
                   const void *w_up, int compute_dtype, int64_t r, int64_t nb, int64_t top,
                   const float *probs, const void *top_idx, int idx_dtype, const float *gates,

@@ -71,6 +71,11 @@ cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, 
 // Per (b, column) state of a sequence shard for the exact fp64 scan:
 // stats double[3][B][d] = its sum, an upper bound of its sum of |x|, the ulp
 // exponent of its smallest non-zero element (1 << 20 when all are zero).
+// The aux loss, router entropy and dead-block fraction of one MoM layer from its
+// router outputs; out = [aux, entropy, dead, frac_0 .. frac_{nb-1}].
+size_t router_aux_workspace_size(int64_t N, int nb);
+cudaError_t launch_router_aux(const float *probs, const void *top_idx, bool idx64, int64_t N, int nb, int top,
+                              float *ws, float *out, cudaStream_t st);
 cudaError_t launch_route_shard_stats(const void *x, int xdt, int B, int S, int d, double *stats, cudaStream_t st);
 // From all shards' stats (W x [3][B][d], rank order): carry double[2][B][d] for
 // shard `rank` and, in *uncertified, the number of (b, column) whose whole-

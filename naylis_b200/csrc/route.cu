@@ -805,6 +805,132 @@ cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, 
     return cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------------ aux-loss statistics
+// The reference's load-balancing aux loss and router logs per MoM layer
+// (model.py:476-517) from the stashed probs (N, nb) fp32 and top_idx (N, top):
+//   frac_e = (tokens that selected block e) / N, mean_e = sum_t probs[t, e] / N,
+//   aux = nb * sum_e frac_e * mean_e, entropy = -sum_t sum_e p log(max(p, 1e-9)) / N,
+//   dead = (blocks no token selected) / nb.
+// Two launches with a fixed reduction order (deterministic): each CTA of the
+// first owns a contiguous token range, thread j takes block e = j % nb of tokens
+// j / nb, j / nb + per, ...; it writes its partial sums [sum_e (nb) | sel_e (nb)
+// | entropy] to the workspace. One CTA then adds the partials in CTA order.
+// out = [aux, entropy, dead, frac_0 .. frac_{nb-1}] (frac is what the backward needs).
+constexpr int kAuxThreads = 256;
+
+template <bool kI64>
+__global__ void __launch_bounds__(kAuxThreads)
+router_aux_part_kernel(const float *__restrict__ probs, const void *__restrict__ top_idx, int64_t N, int nb, int top,
+                       int64_t tok_per_cta, float *__restrict__ part) {
+    __shared__ float s_sum[kAuxThreads], s_sel[kAuxThreads], s_ent[kAuxThreads];
+    const int per = kAuxThreads / nb;              // tokens per pass
+    const int j = threadIdx.x;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * tok_per_cta;
+    const int64_t t1 = min(N, t0 + tok_per_cta);
+    float psum = 0.0f, sel = 0.0f, ent = 0.0f;
+    if (j < per * nb) {
+        const int e = j % nb;
+#pragma unroll 4
+        for (int64_t t = t0 + j / nb; t < t1; t += per) {
+            const float p = probs[t * nb + e];
+            psum += p;
+            ent -= p * logf(fmaxf(p, 1e-9f));
+            bool hit = false;
+            for (int k = 0; k < top; ++k) {
+                const int64_t id = kI64 ? static_cast<const int64_t *>(top_idx)[t * top + k]
+                                        : static_cast<const int32_t *>(top_idx)[t * top + k];
+                hit |= id == e;
+            }
+            sel += hit ? 1.0f : 0.0f;
+        }
+    }
+    s_sum[j] = psum;
+    s_sel[j] = sel;
+    s_ent[j] = ent;
+    __syncthreads();
+    float *mine = part + static_cast<int64_t>(blockIdx.x) * (2 * nb + 1);
+    if (j < nb) {
+        float a = 0.0f, c = 0.0f;
+        for (int g = 0; g < per; ++g) {
+            a += s_sum[g * nb + j];
+            c += s_sel[g * nb + j];
+        }
+        mine[j] = a;
+        mine[nb + j] = c;
+    }
+    if (j == 0) {
+        float en = 0.0f;
+        for (int i = 0; i < per * nb; ++i) en += s_ent[i];
+        mine[2 * nb] = en;
+    }
+}
+
+__global__ void __launch_bounds__(kAuxThreads)
+router_aux_final_kernel(const float *__restrict__ part, int nparts, int64_t N, int nb, float *__restrict__ out) {
+    __shared__ float s_sum[1024], s_sel[1024];
+    __shared__ float s_ent;
+    const float inv = 1.0f / static_cast<float>(N);
+    for (int e = threadIdx.x; e <= nb; e += blockDim.x) {
+        float a = 0.0f, c = 0.0f;
+        for (int g = 0; g < nparts; ++g) {
+            const float *pg = part + static_cast<int64_t>(g) * (2 * nb + 1);
+            if (e < nb) {
+                a += pg[e];
+                c += pg[nb + e];
+            } else {
+                a += pg[2 * nb];
+            }
+        }
+        if (e < nb) {
+            s_sum[e] = a;
+            s_sel[e] = c;
+        } else {
+            s_ent = a;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float aux = 0.0f;
+        int dead = 0;
+        for (int e = 0; e < nb; ++e) {
+            const float frac = s_sel[e] * inv;
+            aux += frac * (s_sum[e] * inv);
+            dead += s_sel[e] == 0.0f;
+            out[3 + e] = frac;
+        }
+        out[0] = static_cast<float>(nb) * aux;
+        out[1] = s_ent * inv;
+        out[2] = static_cast<float>(dead) / static_cast<float>(nb);
+    }
+}
+
+int64_t router_aux_parts(int64_t N, int nb) {
+    const int per = std::max(1, kAuxThreads / nb);
+    // about 4 passes of `per` tokens per CTA, at most 296 CTAs
+    return std::max<int64_t>(1, std::min<int64_t>(296, (N + 4 * per - 1) / (4 * per)));
+}
+
+size_t router_aux_workspace_size(int64_t N, int nb) {
+    return sizeof(float) * static_cast<size_t>(router_aux_parts(N, nb)) * (2 * nb + 1);
+}
+
+cudaError_t launch_router_aux(const float *probs, const void *top_idx, bool idx64, int64_t N, int nb, int top,
+                              float *ws, float *out, cudaStream_t st) {
+    if (nb < 1 || nb > kAuxThreads || N < 1) return cudaErrorInvalidValue;
+    const int64_t parts = router_aux_parts(N, nb);
+    const int64_t tok = (N + parts - 1) / parts;
+    if (idx64)
+        router_aux_part_kernel<true><<<static_cast<int>(parts), kAuxThreads, 0, st>>>(probs, top_idx, N, nb, top,
+                                                                                      tok, ws);
+    else
+        router_aux_part_kernel<false><<<static_cast<int>(parts), kAuxThreads, 0, st>>>(probs, top_idx, N, nb, top,
+                                                                                       tok, ws);
+    count_launch();
+    router_aux_final_kernel<<<1, kAuxThreads, 0, st>>>(ws, static_cast<int>(parts), N, nb, out);
+    count_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_route_shard_stats(const void *x, int xdt, int B, int S, int d, double *stats, cudaStream_t st) {
     dim3 grid((d + 63) / 64, B);
     if (xdt == MOM_BF16)

@@ -45,6 +45,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 import torch.utils.checkpoint
 
+from . import mom_kernels as mk
 from . import trunk
 from .model import MoMLayer
 
@@ -255,6 +256,16 @@ class NaylisForCausalLM(nn.Module):
         count = 0
         for m in self.mom_layers():
             if m.last_router_probs is None or m.last_top_idx is None:
+                continue
+            if m.last_router_probs.is_cuda:
+                # one fused kernel per layer (csrc/route.cu, router_aux)
+                st = mk.router_aux(m.last_router_probs, m.last_top_idx, m.num_blocks)
+                aux = aux + st[0]
+                m.last_entropy = st[1].detach()
+                m.last_dead_frac = st[2].detach()
+                m.last_router_probs = None
+                m.last_top_idx = None
+                count += 1
                 continue
             probs = m.last_router_probs.float()
             blocks = torch.arange(m.num_blocks, device=probs.device)

@@ -485,6 +485,45 @@ def mom_scale(o, scale):
     return _MomScaleFunction.apply(o, scale)
 
 
+class _RouterAuxFunction(torch.autograd.Function):
+    """The load-balancing aux loss of one MoM layer and its router logs
+    (reference: model.py:476-517) in one deterministic kernel. Returns the
+    (3 + nb,) buffer [aux, entropy, dead_frac, frac_0 ..]; only aux carries a
+    gradient: d aux / d probs[t, e] = nb * frac_e / N."""
+
+    @staticmethod
+    def forward(ctx, probs, top_idx, nb):
+        p = probs.detach().to(torch.float32).contiguous()
+        idx = top_idx.contiguous()
+        N = p.numel() // nb
+        out = torch.empty(3 + nb, dtype=torch.float32, device=p.device)
+        ws = torch.empty(_lib.load().mom_router_aux_workspace_size(N, nb), dtype=torch.uint8, device=p.device)
+        code = _lib.I64 if idx.dtype == torch.int64 else _lib.I32
+        _lib.call("mom_router_aux", p.data_ptr(), idx.data_ptr(), code, N, nb, idx.shape[-1], ws.data_ptr(),
+                  ws.numel(), out.data_ptr(), _stream(p.device))
+        ctx.save_for_backward(out)
+        ctx.meta = (N, nb, probs.shape, probs.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        (out,) = ctx.saved_tensors
+        N, nb, shape, dtype = ctx.meta
+        row = grad[0] * (nb / N) * out[3:]
+        return row.repeat(N, 1).reshape(shape).to(dtype), None, None
+
+
+def router_aux(probs, top_idx, num_blocks: int):
+    """(3 + nb,) fp32 [aux, entropy, dead_frac, frac_e ...] of one MoM layer from
+    its stashed router_probs (N, nb) and top_idx (N, top) on a CUDA device:
+    aux = nb * sum_e frac_e * mean_t probs[t, e] (differentiable w.r.t. probs),
+    entropy = -mean_t sum_e p log(max(p, 1e-9)), dead_frac = share of blocks no
+    token selected (reference: model.py:476-517)."""
+    if not probs.is_cuda or top_idx.dtype not in (torch.int32, torch.int64):
+        raise RuntimeError("router_aux: CUDA probs and int32/int64 top_idx")
+    return _RouterAuxFunction.apply(probs, top_idx, int(num_blocks))
+
+
 def gumbel_noise(shape, device, noise_scale: float):
     """Scaled Gumbel noise drawn exactly as the reference draws it
     (model.py:209-213: torch.rand_like on the fp32 logits)."""
@@ -492,5 +531,5 @@ def gumbel_noise(shape, device, noise_scale: float):
     return noise_scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
 
 
-__all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "mom_scale",
+__all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "mom_scale", "router_aux",
            "gumbel_noise"]

@@ -369,3 +369,33 @@ def test_router_fp32_scan_matches_torch_cuda_eager_router(noise_on):
     assert O.scaled_err(got["probs"].reshape(-1, nb), probs.reshape(-1, nb).cpu().numpy()) < 2e-2
     ok = ~mism
     assert O.scaled_err(got["gates"].reshape(-1, top)[ok], gates.reshape(-1, top).cpu().numpy()[ok]) < 2e-2
+
+
+@pytest.mark.parametrize("N,nb,top,idx_dtype", [(16384, 8, 2, torch.int64), (1000, 20, 4, torch.int32),
+                                                (77, 32, 3, torch.int64)])
+def test_router_aux_matches_reference_formula(N, nb, top, idx_dtype):
+    """The fused aux loss / entropy / dead fraction of a layer against the
+    reference's torch expressions (model.py:476-517) on the same router outputs,
+    and the aux gradient w.r.t. probs against torch autograd. Block 0 is never
+    selected, so the dead fraction is non-zero."""
+    from naylis_b200 import mom_kernels as mk
+    torch.manual_seed(7)
+    dev = torch.device("cuda")
+    probs = torch.softmax(torch.randn(N, nb, device=dev), -1).requires_grad_(True)
+    idx = torch.argsort(torch.rand(N, nb, device=dev), -1)[:, :top]
+    idx = torch.where(idx == 0, torch.full_like(idx, nb - 1), idx).to(idx_dtype)   # repeats allowed
+    out = mk.router_aux(probs, idx, nb)
+    pr = probs.detach().clone().requires_grad_(True)
+    blocks = torch.arange(nb, device=dev)
+    sel = (idx.long().unsqueeze(2) == blocks.view(1, 1, -1)).any(1)
+    frac = sel.float().mean(0)
+    aux = nb * (frac * pr.mean(0)).sum()
+    ent = -(pr * pr.clamp_min(1e-9).log()).sum(-1).mean()
+    dead = (~sel.any(0)).float().mean()
+    assert torch.allclose(out[0], aux, rtol=1e-5, atol=1e-7)
+    assert torch.allclose(out[1], ent, rtol=1e-5, atol=1e-6)
+    assert float(out[2]) == float(dead) and float(dead) > 0
+    assert torch.equal(out[3:], frac)
+    (out[0] * 0.3).backward()
+    (aux * 0.3).backward()
+    assert torch.allclose(probs.grad, pr.grad, rtol=1e-6, atol=1e-9)
