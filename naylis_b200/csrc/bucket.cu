@@ -114,11 +114,32 @@ __device__ TokenSet token_set(const void *top_idx, int idx64, int64_t t, int nb,
     return s;
 }
 
-__device__ int set_key(const TokenSet &s, int nb) {
-    uint64_t off = 0;
-    for (int q = 0; q < s.n; ++q) off += binom(nb, q);
-    uint64_t rank = 0;
-    for (int q = 0; q < s.n; ++q) rank += binom(s.blk[q], q + 1);
+// Binomial coefficients C(n, k), n <= 64, k <= 8, as a shared-memory table built
+// by one warp from Pascal's rule (no integer division on the token path). Values
+// saturate at 2^31 - 1: every coefficient a key or its decoding uses is at most
+// the number of keys (<= kMaxKeys).
+constexpr int kBinomN = 65, kBinomK = 9;
+__device__ void build_binom(uint32_t *tab) {
+    if (threadIdx.x >= 32) return;
+    const int k = threadIdx.x;
+    uint32_t c = k == 0 ? 1u : 0u;   // row n = 0
+    for (int n = 0; n < kBinomN; ++n) {
+        if (k < kBinomK) tab[n * kBinomK + k] = c;
+        const uint32_t left = __shfl_up_sync(0xffffffffu, c, 1);
+        const uint64_t next = static_cast<uint64_t>(c) + (k > 0 ? left : 0u);
+        c = next > 0x7FFFFFFFu ? 0x7FFFFFFFu : static_cast<uint32_t>(next);
+    }
+}
+__device__ __forceinline__ uint32_t binom_tab(const uint32_t *tab, int n, int k) {
+    return (k < 0 || k >= kBinomK || n < 0 || n >= kBinomN || k > n) ? 0u : tab[n * kBinomK + k];
+}
+
+__device__ int set_key(const TokenSet &s, int nb, const uint32_t *tab) {
+    uint32_t off = 0, rank = 0;
+    for (int q = 0; q < s.n; ++q) {
+        off += binom_tab(tab, nb, q);
+        rank += binom_tab(tab, s.blk[q], q + 1);
+    }
     return static_cast<int>(off + rank);
 }
 
@@ -126,13 +147,15 @@ __global__ void __launch_bounds__(kBucketChunk)
 bucket_keys_kernel(const void *__restrict__ top_idx, int idx64, int64_t N, int nb, int top,
                    int num_keys, PlanView P) {
     extern __shared__ int s_hist[];
+    __shared__ uint32_t s_binom[kBinomN * kBinomK];
     for (int i = threadIdx.x; i < num_keys; i += blockDim.x) s_hist[i] = 0;
+    build_binom(s_binom);
     __syncthreads();
     const int64_t t = static_cast<int64_t>(blockIdx.x) * kBucketChunk + threadIdx.x;
     if (t < N) {
         const TokenSet s = token_set(top_idx, idx64, t, nb, top);
         if (s.bad) atomicOr(P.err, 1);
-        const int key = set_key(s, nb);
+        const int key = set_key(s, nb, s_binom);
         P.key[t] = key;
         atomicAdd(&s_hist[key], 1);
     }
@@ -199,6 +222,9 @@ bucket_scan_kernel(int nb, int top, int num_keys, int max_tiles, PlanView P) {
     int *s_nt = reinterpret_cast<int *>(s_mask + num_keys);
     int *s_tb = s_nt + num_keys;
     __shared__ int s_tmp[96];
+    __shared__ uint32_t s_binom[kBinomN * kBinomK];
+    build_binom(s_binom);
+    __syncthreads();
     const int tid = threadIdx.x;
     const int per = (num_keys + 1023) / 1024;          // <= kMaxKeys / 1024 = 8
     const int k0 = min(num_keys, tid * per), k1 = min(num_keys, k0 + per);
@@ -224,18 +250,21 @@ bucket_scan_kernel(int nb, int top, int num_keys, int max_tiles, PlanView P) {
         tile_base += nt;
         // decode the key into its block set
         int sz = 0;
-        uint64_t off = 0;
-        while (sz < top && off + binom(nb, sz) <= static_cast<uint64_t>(k)) { off += binom(nb, sz); ++sz; }
-        uint64_t rank = static_cast<uint64_t>(k) - off;
+        uint32_t off = 0;
+        while (sz < top && off + binom_tab(s_binom, nb, sz) <= static_cast<uint32_t>(k)) {
+            off += binom_tab(s_binom, nb, sz);
+            ++sz;
+        }
+        uint32_t rank = static_cast<uint32_t>(k) - off;
         int *set = P.keyset + static_cast<int64_t>(k) * top;
         for (int q = top - 1; q >= 0; --q) set[q] = -1;
         uint64_t mask = 0;
         for (int q = sz - 1; q >= 0; --q) {
             int b = q;
-            while (b + 1 < nb && binom(b + 1, q + 1) <= rank) ++b;
+            while (b + 1 < nb && binom_tab(s_binom, b + 1, q + 1) <= rank) ++b;
             set[q] = b;
             mask |= uint64_t(1) << b;
-            rank -= binom(b, q + 1);
+            rank -= binom_tab(s_binom, b, q + 1);
         }
         s_mask[k] = mask;
     }
