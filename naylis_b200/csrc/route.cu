@@ -3,8 +3,11 @@
 //
 // Reference semantics: model.py:169-220 (MoMLayer._prefix_mean,
 // _router_logits, forward's softmax/topk/gates block).
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "launch.h"
+#include "tc_common.cuh"
 
 namespace mom {
 
@@ -165,6 +168,160 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
     cp_async_wait<0>();
     if (warp == 0 && sh.carry_out && col < d)
         static_cast<float *>(sh.carry_out)[static_cast<int64_t>(b) * d + col] = acc;
+}
+
+// ------------------------------------------------------------ fp32 scan, TMA-fed
+// The same sequential fp32 chains and the same division as route_scan_kernel,
+// decoupled by mbarriers instead of a CTA barrier per stage, so that the chain
+// warp runs as far ahead as the ring allows:
+//   warp 0      producer: each stage (kTRows rows x 32 columns of one batch row)
+//               by one 3-D TMA box into a ring of kTStages slots (rows past S
+//               and columns past d arrive as zeros);
+//   warp 1      the 32 column chains: running sums of a stage into one of two
+//               shared fp32 buffers, then the x slot goes back to the producer;
+//   warps 2..9  RN(c / (t+1)) of a finished buffer (Markstein's correction from
+//               the row's reciprocal), 16-B loads, 8- or 16-B stores.
+// Every wait is bounded; on a timeout the CTA stops and its rows of h are left
+// as NaN (written up front), so a stuck scan shows in the router's outputs.
+constexpr int kTRows = 64;
+constexpr int kTStages = 8;
+constexpr int kTDivWarps = 8;
+constexpr int kTThreads = 32 * (2 + kTDivWarps);
+
+template <int XDT>
+constexpr size_t tma_scan_smem() {
+    return size_t(kTStages) * kTRows * kSeqCols * sizeof(typename Elem<XDT>::T) +
+           2 * size_t(kTRows) * kSeqCols * sizeof(float) + 256 /*barriers*/ + 128 /*align*/;
+}
+
+template <int XDT, int CDT>
+__global__ void __launch_bounds__(kTThreads)
+route_scan_tma_kernel(const __grid_constant__ CUtensorMap xmap, typename Elem<CDT>::T *__restrict__ hq, int S,
+                      int d, ScanShard sh) {
+    using XT = typename Elem<XDT>::T;
+    using CT = typename Elem<CDT>::T;
+    constexpr uint32_t kStageBytes = kTRows * kSeqCols * sizeof(XT);
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    unsigned char *smem = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
+    const XT *ring = reinterpret_cast<const XT *>(smem);
+    float *csum = reinterpret_cast<float *>(smem + kTStages * kStageBytes);     // [2][kTRows][32]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(csum + 2 * kTRows * kSeqCols);
+    uint64_t *full = bars, *empty = bars + kTStages, *cfull = bars + 2 * kTStages, *cempty = cfull + 2;
+    int *flags = reinterpret_cast<int *>(cempty + 2);                           // [0] error bits, [1] abort
+    volatile int *abort_flag = flags + 1;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c0 = blockIdx.x * kSeqCols, b = blockIdx.y;
+    const int nstage = (S + kTRows - 1) / kTRows;
+    const int valid_cols = min(kSeqCols, d - c0);
+    CT *hb = hq + static_cast<int64_t>(b) * S * d;
+    if (tid == 0) {
+        for (int i = 0; i < kTStages; ++i) {
+            tc::mbar_init(&full[i], 1);
+            tc::mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            tc::mbar_init(&cfull[i], 32);
+            tc::mbar_init(&cempty[i], 32 * kTDivWarps);
+        }
+        flags[0] = 0;
+        flags[1] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tc::prefetch_tensormap(&xmap);
+            for (int s = 0; s < nstage; ++s) {
+                const int slot = s % kTStages;
+                if (s >= kTStages &&
+                    !tc::mbar_wait(&empty[slot], ((s / kTStages) - 1) & 1, flags, 2, abort_flag))
+                    break;
+                tc::mbar_arrive_expect_tx(&full[slot], kStageBytes);
+                tc::tma_load_3d(smem_u32(smem + slot * kStageBytes), &xmap, c0, s * kTRows, b, &full[slot]);
+            }
+            // the last copies have landed before the CTA may exit
+            for (int s = max(0, nstage - kTStages); s < nstage; ++s)
+                tc::mbar_wait(&full[s % kTStages], (s / kTStages) & 1, flags, 2, abort_flag);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ chain warp
+        const int col = c0 + lane;
+        float acc = (sh.carry_in && col < d) ? static_cast<const float *>(sh.carry_in)[static_cast<int64_t>(b) * d + col]
+                                             : 0.0f;
+        bool ok = true;
+        for (int s = 0; s < nstage && ok; ++s) {
+            const int slot = s % kTStages;
+            float *cs = csum + (s & 1) * kTRows * kSeqCols;
+            ok = tc::mbar_wait_warp(&full[slot], (s / kTStages) & 1, flags, 2, abort_flag);
+            if (ok && s >= 2) ok = tc::mbar_wait_warp(&cempty[s & 1], ((s >> 1) - 1) & 1, flags, 2, abort_flag);
+            if (!ok) break;
+            const XT *st = ring + slot * kTRows * kSeqCols;
+            const int rows = min(kTRows, S - s * kTRows);
+#pragma unroll 1
+            for (int r0 = 0; r0 < rows; r0 += kSeqBatch) {
+                float v[kSeqBatch];
+#pragma unroll
+                for (int j = 0; j < kSeqBatch; ++j) v[j] = Elem<XDT>::load(st, (r0 + j) * kSeqCols + lane);
+#pragma unroll
+                for (int j = 0; j < kSeqBatch; ++j) {
+                    acc = r0 + j < rows ? __fadd_rn(acc, v[j]) : acc;
+                    v[j] = acc;
+                }
+#pragma unroll
+                for (int j = 0; j < kSeqBatch; ++j)
+                    if (r0 + j < rows) cs[(r0 + j) * kSeqCols + lane] = v[j];
+            }
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&empty[slot]);
+            tc::mbar_arrive(&cfull[s & 1]);
+        }
+        if (ok && sh.carry_out && col < d)
+            static_cast<float *>(sh.carry_out)[static_cast<int64_t>(b) * d + col] = acc;
+    } else {
+        // ------------------------------------------------------------ division warps
+        constexpr int kGroups = kSeqCols / 4;
+        constexpr int kRowStep = 32 * kTDivWarps / kGroups;
+        const int dt = tid - 64;
+        const int grp = dt % kGroups, row0 = dt / kGroups;
+        const bool vec_ok = 4 * grp + 4 <= valid_cols && (d % 4) == 0 &&
+                            (reinterpret_cast<uintptr_t>(hq) % (4 * sizeof(CT))) == 0;
+        for (int s = 0; s < nstage; ++s) {
+            if (!tc::mbar_wait_warp(&cfull[s & 1], (s >> 1) & 1, flags, 2, abort_flag)) break;
+            const float *cs = csum + (s & 1) * kTRows * kSeqCols;
+            const int t0 = s * kTRows;
+            const int rows = min(kTRows, S - t0);
+#pragma unroll
+            for (int r = row0; r < kTRows; r += kRowStep) {
+                if (r >= rows) break;
+                const float4 c = *reinterpret_cast<const float4 *>(cs + r * kSeqCols + 4 * grp);
+                const float den = static_cast<float>(sh.t_base + t0 + r + 1);
+                const float y = __frcp_rn(den);
+                const float4 h = make_float4(div_by_count(c.x, den, y), div_by_count(c.y, den, y),
+                                             div_by_count(c.z, den, y), div_by_count(c.w, den, y));
+                CT *dst = hb + static_cast<int64_t>(t0 + r) * d + c0 + 4 * grp;
+                if (vec_ok) {
+                    Store4<CDT>::store(dst, h);
+                } else {
+                    const float hv[4] = {h.x, h.y, h.z, h.w};
+                    for (int j = 0; j < 4; ++j)
+                        if (4 * grp + j < valid_cols) Store4<CDT>::store1(dst + j, hv[j]);
+                }
+            }
+            tc::mbar_arrive(&cempty[s & 1]);
+        }
+    }
+    __syncthreads();
+    if (flags[0]) {
+        // a wait gave up: this CTA's columns of h become NaN
+        const float nanv = __int_as_float(0x7fc00000);
+        for (int i = tid; i < S * kSeqCols; i += blockDim.x) {
+            const int t = i / kSeqCols, c = i % kSeqCols;
+            if (c < valid_cols) Store4<CDT>::store1(hb + static_cast<int64_t>(t) * d + c0 + c, nanv);
+        }
+    }
 }
 
 // ------------------------------------------------------------ parallel exact fp64 scan
@@ -778,6 +935,43 @@ static cudaError_t launch_scan_t(const void *x, void *hq, int B, int S, int d, c
     return cudaGetLastError();
 }
 
+// 3-D tensor map over x (B, S, d) with a box of 32 columns x kTRows rows of one
+// batch row; false when TMA cannot address x (alignment) or the driver entry
+// point is missing, and the cp.async kernel is used instead.
+static bool make_scan_map(CUtensorMap *map, const void *x, int xdt, int B, int S, int d) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    const uint64_t es = xdt == MOM_F32 ? 4 : 2;
+    if (!fn || (reinterpret_cast<uintptr_t>(x) % 16) != 0 || (static_cast<uint64_t>(d) * es) % 16 != 0) return false;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(S), static_cast<cuuint64_t>(B)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(d) * es, static_cast<cuuint64_t>(S) * d * es};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(kSeqCols), static_cast<cuuint32_t>(kTRows), 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType ty = xdt == MOM_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    return fn(map, ty, 3, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int XDT, int CDT>
+static cudaError_t launch_scan_tma_t(const CUtensorMap &map, void *hq, int B, int S, int d, cudaStream_t st,
+                                     const ScanShard &sh) {
+    const size_t smem = tma_scan_smem<XDT>();
+    auto k = route_scan_tma_kernel<XDT, CDT>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((d + kSeqCols - 1) / kSeqCols, B);
+    k<<<grid, kTThreads, smem, st>>>(map, static_cast<typename Elem<CDT>::T *>(hq), S, d, sh);
+    count_launch();
+    return cudaGetLastError();
+}
+
 template <int XDT, int CDT>
 static cudaError_t launch_scan_par_t(const void *x, void *hq, int B, int S, int d, cudaStream_t st,
                                      const ScanShard &sh) {
@@ -798,6 +992,14 @@ cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, 
         return cudaErrorInvalidValue;
     }
     if (mode != MOM_SCAN_FP32) return cudaErrorInvalidValue;
+    CUtensorMap map;
+    if (S > 0 && B > 0 && d > 0 && (xdt == MOM_BF16 || xdt == MOM_F32) && (cdt == MOM_BF16 || cdt == MOM_F32) &&
+        make_scan_map(&map, x, xdt, B, S, d)) {
+        if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_tma_t<MOM_BF16, MOM_BF16>(map, hq, B, S, d, st, sh);
+        if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_tma_t<MOM_F32, MOM_BF16>(map, hq, B, S, d, st, sh);
+        if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_tma_t<MOM_F32, MOM_F32>(map, hq, B, S, d, st, sh);
+        return launch_scan_tma_t<MOM_BF16, MOM_F32>(map, hq, B, S, d, st, sh);
+    }
     if (xdt == MOM_BF16 && cdt == MOM_BF16) return launch_scan_t<MOM_BF16, MOM_BF16>(x, hq, B, S, d, st, sh);
     if (xdt == MOM_F32 && cdt == MOM_BF16) return launch_scan_t<MOM_F32, MOM_BF16>(x, hq, B, S, d, st, sh);
     if (xdt == MOM_F32 && cdt == MOM_F32) return launch_scan_t<MOM_F32, MOM_F32>(x, hq, B, S, d, st, sh);
