@@ -396,13 +396,16 @@ read_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_c
             // softmax cancels, so the gradient is exactly zero (dlog_gates is zeroed
             // before the kernels run).
             if (grp == 0 && tok >= 0 && (nblk > 1 || pseudo)) {
-                const float A[2] = {part[r] + part[kTM + r], part[2 * kTM + r] + part[3 * kTM + r]};
-                const float Bv[2] = {part[4 * kTM + r] + part[5 * kTM + r], part[6 * kTM + r] + part[7 * kTM + r]};
+                // per block of the set: A = sum P*dP, B = sum P (selected by value, not by
+                // a dynamically indexed array, which would live in local memory)
+                const float A0 = part[r] + part[kTM + r], A1 = part[2 * kTM + r] + part[3 * kTM + r];
+                const float B0 = part[4 * kTM + r] + part[5 * kTM + r], B1 = part[6 * kTM + r] + part[7 * kTM + r];
                 const uint32_t kmap = cur.kmap;
                 for (int kk = 0; kk < top; ++kk) {
                     const int jsel = (kmap >> (4 * kk)) & 0xF;
                     if (jsel < nblk && jsel < 2)
-                        atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk, fmaf(-delta, Bv[jsel], A[jsel]));
+                        atomicAdd(dlog_gates + static_cast<int64_t>(tok) * top + kk,
+                                  fmaf(-delta, jsel ? B1 : B0, jsel ? A1 : A0));
                 }
             }
             // epilogue: 16 of the 64 dQ columns, dQ_0 + dQ_1 (the set's blocks) * scale ->

@@ -177,12 +177,15 @@ route_scan_kernel(const typename Elem<XDT>::T *__restrict__ x,
 //   warp 0      producer: each stage (kTRows rows x 32 columns of one batch row)
 //               by one 3-D TMA box into a ring of kTStages slots (rows past S
 //               and columns past d arrive as zeros);
-//   warp 1      the 32 column chains: running sums of a stage into one of two
-//               shared fp32 buffers, then the x slot goes back to the producer;
-//   warps 2..9  RN(c / (t+1)) of a finished buffer (Markstein's correction from
-//               the row's reciprocal), 16-B loads, 8- or 16-B stores.
+//   warp 1      the 32 column chains (lane = column): running sums of a stage
+//               into one of two shared fp32 buffers (row-major), then the x slot
+//               goes back to the producer; full stages take an unpredicated loop
+//               (one load, one add, one store per row);
+//   warps 2..9  RN(c / (t+1)) by Markstein's correction from the row's
+//               reciprocal, 4 columns of a row per thread (one 16-B shared load,
+//               one 8- or 16-B store).
 // Every wait is bounded; on a timeout the CTA stops and its rows of h are left
-// as NaN (written up front), so a stuck scan shows in the router's outputs.
+// as NaN (written at the end), so a stuck scan shows in the router's outputs.
 constexpr int kTRows = 64;
 constexpr int kTStages = 8;
 constexpr int kTDivWarps = 8;
@@ -254,25 +257,29 @@ route_scan_tma_kernel(const __grid_constant__ CUtensorMap xmap, typename Elem<CD
         bool ok = true;
         for (int s = 0; s < nstage && ok; ++s) {
             const int slot = s % kTStages;
-            float *cs = csum + (s & 1) * kTRows * kSeqCols;
+            float *cs = csum + (s & 1) * kTRows * kSeqCols + lane;              // this lane's column
             ok = tc::mbar_wait_warp(&full[slot], (s / kTStages) & 1, flags, 2, abort_flag);
             if (ok && s >= 2) ok = tc::mbar_wait_warp(&cempty[s & 1], ((s >> 1) - 1) & 1, flags, 2, abort_flag);
             if (!ok) break;
-            const XT *st = ring + slot * kTRows * kSeqCols;
+            const XT *st = ring + slot * kTRows * kSeqCols + lane;
             const int rows = min(kTRows, S - s * kTRows);
-#pragma unroll 1
-            for (int r0 = 0; r0 < rows; r0 += kSeqBatch) {
-                float v[kSeqBatch];
+            if (rows == kTRows) {
+#pragma unroll 2
+                for (int r0 = 0; r0 < kTRows; r0 += kSeqBatch) {
+                    float v[kSeqBatch];
 #pragma unroll
-                for (int j = 0; j < kSeqBatch; ++j) v[j] = Elem<XDT>::load(st, (r0 + j) * kSeqCols + lane);
+                    for (int j = 0; j < kSeqBatch; ++j) v[j] = Elem<XDT>::load(st, (r0 + j) * kSeqCols);
 #pragma unroll
-                for (int j = 0; j < kSeqBatch; ++j) {
-                    acc = r0 + j < rows ? __fadd_rn(acc, v[j]) : acc;
-                    v[j] = acc;
+                    for (int j = 0; j < kSeqBatch; ++j) {
+                        acc = __fadd_rn(acc, v[j]);
+                        cs[(r0 + j) * kSeqCols] = acc;
+                    }
                 }
-#pragma unroll
-                for (int j = 0; j < kSeqBatch; ++j)
-                    if (r0 + j < rows) cs[(r0 + j) * kSeqCols + lane] = v[j];
+            } else {
+                for (int r = 0; r < rows; ++r) {
+                    acc = __fadd_rn(acc, Elem<XDT>::load(st, r * kSeqCols));
+                    cs[r * kSeqCols] = acc;
+                }
             }
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&empty[slot]);
