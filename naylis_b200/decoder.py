@@ -109,6 +109,12 @@ def apply_rope(t, cos, sin):
     return t * cos + rot * sin
 
 
+def _bf16_path(x) -> bool:
+    """The decoder's bf16 kernel path: CUDA activations in bf16 under CUDA bf16
+    autocast (the residual stream's RMSNorm kernels hand bf16 to every projection)."""
+    return x.is_cuda and x.dtype == torch.bfloat16 and torch.is_autocast_enabled("cuda")
+
+
 class SelfAttention(nn.Module):
     def __init__(self, cfg: NaylisConfig):
         super().__init__()
@@ -122,10 +128,15 @@ class SelfAttention(nn.Module):
 
     def forward(self, x, cos, sin):
         B, S, d = x.shape
+        if _bf16_path(x):
+            qkv = trunk.linear_f32grad(x, self.q_proj.weight, self.k_proj.weight, self.v_proj.weight)
+            # fused rotary embedding into attention's layout (csrc/trunk.cu)
+            q, k, v = trunk.rope_qkv(qkv, cos, sin, self.n_heads)
+            o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            return trunk.linear_f32grad(o.transpose(1, 2).reshape(B, S, d), self.o_proj.weight)
         w = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), dim=0)
         qkv = F.linear(x, w)
         if qkv.is_cuda and qkv.dtype == torch.bfloat16:
-            # fused rotary embedding into attention's layout (csrc/trunk.cu)
             q, k, v = trunk.rope_qkv(qkv, cos, sin, self.n_heads)
         else:
             qkv = qkv.view(B, S, 3, self.n_heads, self.head_dim)
@@ -145,6 +156,9 @@ class SwiGLU(nn.Module):
         self.down_proj = nn.Linear(f, d, bias=False)
 
     def forward(self, x):
+        if _bf16_path(x):
+            gu = trunk.linear_f32grad(x, self.gate_proj.weight, self.up_proj.weight)
+            return trunk.linear_f32grad(trunk.swiglu(gu), self.down_proj.weight)   # fused (csrc/trunk.cu)
         gu = F.linear(x, torch.cat((self.gate_proj.weight, self.up_proj.weight), dim=0))
         if gu.is_cuda and gu.dtype == torch.bfloat16:
             return self.down_proj(trunk.swiglu(gu))      # fused (csrc/trunk.cu)
@@ -288,7 +302,10 @@ class NaylisForCausalLM(nn.Module):
             return self.lm_head(h)
         shift_h = h[:, :-1].reshape(-1, h.shape[-1])
         shift_labels = labels[:, 1:].reshape(-1)
-        logits = self.lm_head(shift_h)
+        if _bf16_path(shift_h):
+            logits = trunk.linear_f32grad(shift_h, self.lm_head.weight)
+        else:
+            logits = self.lm_head(shift_h)
         if logits.is_cuda and logits.dtype == torch.bfloat16:
             # fused (csrc/trunk.cu): the same fp32 math on the bf16 logits, no fp32 copy
             loss = trunk.cross_entropy_sum(logits, shift_labels)

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from . import mom_kernels
+from . import mom_kernels, trunk
 
 
 class MoMLayer(nn.Module):
@@ -106,13 +106,21 @@ class MoMLayer(nn.Module):
                 use_reentrant=False, preserve_rng_state=False)
         return self._read(xq, top_idx, log_gates, M_blocks, mode)
 
+    @staticmethod
+    def _proj(lin, x):
+        """lin(x); under CUDA bf16 autocast the bf16 GEMM with fp32 weight
+        gradients (trunk.linear_f32grad) instead of autocast's cast + linear."""
+        if x.is_cuda and torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+            return trunk.linear_f32grad(x, lin.weight)
+        return lin(x)
+
     def _read(self, x, top_idx, log_gates, M_blocks, mode):
         B, S, D = x.shape
-        q_sh = self.q_proj(x).view(B, S, self.n_heads, self.head_dim)
+        q_sh = self._proj(self.q_proj, x).view(B, S, self.n_heads, self.head_dim)
         slots = M_blocks.view(self.mem_slots, D)
-        k_shared = self.k_proj(slots)
-        v_shared = self.v_proj(slots)
+        k_shared = self._proj(self.k_proj, slots)
+        v_shared = self._proj(self.v_proj, slots)
         out = mom_kernels.mom_read_log_gates(q_sh, k_shared, v_shared, top_idx, log_gates,
                                              num_blocks=self.num_blocks, block_size=self.block_size,
                                              mode=mode)
-        return self.o_proj(out.reshape(B, S, D))
+        return self._proj(self.o_proj, out.reshape(B, S, D))

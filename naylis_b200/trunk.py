@@ -154,6 +154,49 @@ def add_rmsnorm(x, delta, weight, eps: float, scale=None, want_f32: bool = False
     return _AddRMSNorm.apply(x, delta, scale, weight, float(eps), bool(want_f32))
 
 
+class _LinearF32Grad(torch.autograd.Function):
+    """y = x @ cat(weights)^T in bf16. The weights are cast into one bf16 buffer
+    (no fp32 concatenation); the backward gives dx in bf16 and the weights'
+    gradients from one GEMM with fp32 output, split per weight."""
+
+    @staticmethod
+    def forward(ctx, x, *weights):
+        rows = [w.shape[0] for w in weights]
+        w16 = torch.empty(sum(rows), weights[0].shape[1], dtype=torch.bfloat16, device=x.device)
+        o = 0
+        for w, n in zip(weights, rows):
+            w16[o:o + n].copy_(w.detach())
+            o += n
+        x16 = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+        y = torch.nn.functional.linear(x16, w16)
+        ctx.save_for_backward(x16, w16)
+        ctx.rows = rows
+        ctx.wdtypes = [w.dtype for w in weights]
+        ctx.x_dtype = x.dtype
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x16, w16 = ctx.saved_tensors
+        dy = dy.to(torch.bfloat16)
+        dx = torch.matmul(dy, w16)
+        dw = torch.mm(dy.reshape(-1, dy.shape[-1]).t(), x16.reshape(-1, x16.shape[-1]), out_dtype=torch.float32)
+        grads, o = [], 0
+        for n, dt in zip(ctx.rows, ctx.wdtypes):
+            grads.append(dw[o:o + n] if dt == torch.float32 else dw[o:o + n].to(dt))
+            o += n
+        return (dx.to(ctx.x_dtype), *grads)
+
+
+def linear_f32grad(x, *weights):
+    """bf16 x @ cat(weights)^T on CUDA (fp32 master weights cast once per call)
+    whose weight gradients are computed in fp32 by the GEMM itself; the
+    reference's autocast linear rounds them to bf16 and casts them back."""
+    if not x.is_cuda:
+        raise RuntimeError("linear_f32grad: CUDA tensors only")
+    return _LinearF32Grad.apply(x, *weights)
+
+
 class _CrossEntropySum(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, labels, ignore_index):
@@ -190,4 +233,4 @@ def cross_entropy_sum(logits, labels, ignore_index: int = -100):
     return _CrossEntropySum.apply(logits, labels, int(ignore_index))
 
 
-__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum"]
+__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum", "linear_f32grad"]
