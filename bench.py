@@ -39,7 +39,7 @@ CFG3 = dict(B=8, S=2048)
 METRIC3 = "Naylis 300M decoder training tokens/s (fwd+bwd+AdamW, all GPUs), BASELINE config 3"
 WORKLOAD3 = ("cfg3: 20-layer Naylis decoder (d 1024, 16x64 heads, SwiGLU 2816, vocab 32000, RoPE, RMSNorm, "
              "MoM in every layer sharing one 8x128x1024 bank, rank 32, top-2, aux 0.01), B=8 x S=2048 "
-             "token ids per GPU, bf16 autocast, fp32 master weights, fused AdamW")
+             "token ids per GPU, bf16 autocast, fp32 master weights, AdamW")
 METRIC = "MoM layer fwd+bwd tokens/s (router + read + projections), BASELINE config 2"
 WORKLOAD = ("cfg2: one MoM layer fwd+bwd per GPU, B=8 S=2048 d=1024, 16x64 heads, "
             "bank 8x128 slots, router rank 32, top-2, bf16 autocast, fp32 master weights")
@@ -346,7 +346,12 @@ def run_model_cfg3(args):
     model = NaylisForCausalLM(cfg).to(dev).train()
     comm = torch.bfloat16 if args.bf16_grads else None
     dp = GradAllReduce(model, bucket_mb=args.bucket_mb, comm_dtype=comm)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1, fused=True)
+    if args.optim == "torch":
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1, fused=True)
+    else:
+        # one launch over every parameter, writing the bf16 weight copies the next forward reads
+        from naylis_b200.optim import AdamW
+        opt = AdamW(model.parameters(), lr=3e-4, weight_decay=0.1)
     g = torch.Generator(device=dev).manual_seed(77 + rank)
     ids = torch.randint(0, cfg.vocab_size, (B, S), device=dev, generator=g)
     lib = _lib.load()
@@ -977,6 +982,8 @@ def main():
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
+    ap.add_argument("--optim", default="naylis", choices=["naylis", "torch"],
+                    help="cfg3 optimizer: this package's one-launch AdamW (default) or torch's fused AdamW")
     ap.add_argument("--workload", default="cfg3", choices=["cfg3", "cfg2", "read-top4of32", "trunk"],
                     help="cfg3: the decoder training step (default); cfg2: one MoM layer step; "
                          "read-top4of32: the read alone on config 4's geometry; trunk: the decoder's fused "

@@ -252,6 +252,18 @@ MOM_API int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const flo
                                 const float *dx_in, int64_t N, int64_t d, float *dx, void *ddelta, float *dw,
                                 float *ddelta_scale, void *stream);
 
+/* AdamW over many fp32 parameter tensors in one launch (the reference's
+ * optimizer, torch.optim.AdamW with decoupled weight decay, as
+ * pretrain.py's HF Trainer runs it), writing each updated parameter's bf16 copy
+ * in the same pass when the table entry asks for one.
+ * tensors: ntensors entries of {float *p; const float *g; float *m; float *v;
+ * uint16_t *p16 (bf16 copy of p, or NULL); int64_t n} (48 bytes each, device
+ * memory); chunks: nchunks {int32 tensor, int32 chunk} pairs covering every
+ * tensor in chunks of 65,536 elements. step >= 1 is the step count after this
+ * update (bias corrections 1 - beta^step). */
+MOM_API int mom_adamw_step(const void *tensors, int64_t ntensors, const void *chunks, int64_t nchunks, double lr,
+                           double beta1, double beta2, double eps, double weight_decay, int64_t step, void *stream);
+
 /* mom_xent_fwd: the causal-LM loss of model.py:539-551 (NaylisLlamaForCausalLM:
  * cross_entropy(logits.float(), labels, reduction="sum") over the shifted rows,
  * then divided by the count of labels != ignore_index) without materialising the

@@ -75,6 +75,8 @@ SIGNATURES = {
                                    _vp]),
     "mom_router_aux_workspace_size": (_sz, [_i64, _i64]),
     "mom_router_aux": (_int, [_fp, _vp, _int, _i64, _i64, _i64, _vp, _sz, _fp, _vp]),
+    "mom_adamw_step": (_int, [_vp, _i64, _vp, _i64, _c.c_double, _c.c_double, _c.c_double, _c.c_double, _c.c_double,
+                              _i64, _vp]),
     "mom_xent_fwd": (_int, [_vp, _vp, _i64, _i64, _i64, _fp, _fp, _vp]),
     "mom_xent_bwd": (_int, [_vp, _vp, _fp, _fp, _i64, _i64, _i64, _vp, _vp]),
     "mom_read_bwd_noalloc_max_bytes": (_sz, []),

@@ -4,6 +4,7 @@
 // with a thread-local message, and forwards to the launchers. It allocates
 // nothing and never synchronises the host, except mom_plan_check, whose job
 // is to read the plan's device error word.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -785,6 +786,24 @@ int mom_add_rmsnorm_bwd(const float *x_new, const float *rstd, const float *w, c
                                                 (int)d, dx, ddelta, dw, ddelta_scale,
                                                 static_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? MOM_OK : cuda_fail(e, "add_rmsnorm_bwd");
+}
+
+int mom_adamw_step(const void *tensors, int64_t ntensors, const void *chunks, int64_t nchunks, double lr,
+                   double beta1, double beta2, double eps, double weight_decay, int64_t step, void *stream) {
+    MOM_REQUIRE(ntensors >= 0 && nchunks >= 0 && step >= 1, "bad optimizer arguments");
+    if (nchunks == 0) return MOM_OK;
+    MOM_REQUIRE(tensors && chunks, "null pointer argument");
+    MOM_REQUIRE((reinterpret_cast<uintptr_t>(tensors) & 7) == 0 && (reinterpret_cast<uintptr_t>(chunks) & 7) == 0,
+                "tables must be 8-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    const double bc1 = 1.0 - std::pow(beta1, static_cast<double>(step));
+    const double bc2 = 1.0 - std::pow(beta2, static_cast<double>(step));
+    cudaError_t e = mom::launch_adamw_multi(static_cast<const mom::OptTensor *>(tensors),
+                                            static_cast<const int2 *>(chunks), nchunks, (float)lr, (float)beta1,
+                                            (float)beta2, (float)eps, (float)weight_decay, (float)bc1, (float)bc2,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "adamw_step");
 }
 
 int mom_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int64_t V, int64_t ignore_index,

@@ -192,6 +192,19 @@ cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const 
                                    cudaStream_t st);
 // LM-head cross-entropy over bf16 logits (R, V): per-row loss (0 on ignored rows)
 // and log-sum-exp; backward dlogits = bf16((softmax - onehot) * (*grad)).
+// AdamW over a table of fp32 tensors (one launch), with optional bf16 copies.
+struct OptTensor {
+    float *p;
+    const float *g;
+    float *m;
+    float *v;
+    uint16_t *p16;   // may be null
+    int64_t n;
+};
+constexpr int kOptChunk = 65536;   // elements per CTA
+constexpr int kOptThreads = 256;
+cudaError_t launch_adamw_multi(const OptTensor *tensors, const int2 *chunks, int64_t nchunks, float lr, float b1,
+                               float b2, float eps, float wd, float bc1, float bc2, cudaStream_t st);
 cudaError_t launch_xent_fwd(const void *logits, const int64_t *labels, int64_t R, int V, int64_t ignore_index,
                             float *row_loss, float *lse, cudaStream_t st);
 cudaError_t launch_xent_bwd(const void *logits, const int64_t *labels, const float *lse, const float *grad, int64_t R,

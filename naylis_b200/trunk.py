@@ -10,6 +10,7 @@ torch's ops for fp32 runs).
 from __future__ import annotations
 
 import torch
+from torch.utils.weak import WeakIdKeyDictionary
 
 from . import _lib
 
@@ -154,19 +155,66 @@ def add_rmsnorm(x, delta, weight, eps: float, scale=None, want_f32: bool = False
     return _AddRMSNorm.apply(x, delta, scale, weight, float(eps), bool(want_f32))
 
 
+# parameter -> [group buffer, its rows (a view), the parameter's _version when the
+# rows were written]; weak keys, so the buffers go with the parameters and are
+# not part of what a parameter pickles
+_SHADOWS = WeakIdKeyDictionary()
+_SHADOW_GEN = [0]   # bumped whenever rows are (re)registered, so holders of pointers can re-read them
+
+
+def _bf16_weights(weights):
+    """One bf16 buffer holding cat(weights) for the GEMM, kept per parameter and
+    reused while every weight's `_version` matches the one its rows were written
+    at. The optimizer of this package rewrites the rows in its update and marks
+    them fresh (`mark_bf16_fresh`); any other in-place change of a weight makes
+    the next call recast it."""
+    rows = sum(w.shape[0] for w in weights)
+    ent = [_SHADOWS.get(w) for w in weights]
+    buf = ent[0][0] if ent[0] is not None else None
+    if buf is None or any(e is None or e[0] is not buf for e in ent) or buf.shape[0] != rows or \
+            buf.device != weights[0].device:
+        buf = torch.empty(rows, weights[0].shape[1], dtype=torch.bfloat16, device=weights[0].device)
+        o = 0
+        for w in weights:
+            _SHADOWS[w] = [buf, buf[o:o + w.shape[0]], -1]
+            o += w.shape[0]
+        _SHADOW_GEN[0] += 1
+    for w in weights:
+        e = _SHADOWS[w]
+        if e[2] != w._version:
+            e[1].copy_(w.detach())
+            e[2] = w._version
+    return buf
+
+
+def bf16_generation() -> int:
+    """A counter that changes whenever a parameter's bf16 rows are (re)registered."""
+    return _SHADOW_GEN[0]
+
+
+def bf16_copy(param):
+    """The bf16 rows registered for `param` by the bf16 projections, or None."""
+    e = _SHADOWS.get(param)
+    return None if e is None else e[1]
+
+
+def mark_bf16_fresh(param) -> None:
+    """Record that `param`'s bf16 rows were rewritten from its current values."""
+    e = _SHADOWS.get(param)
+    if e is not None:
+        e[2] = param._version
+
+
 class _LinearF32Grad(torch.autograd.Function):
-    """y = x @ cat(weights)^T in bf16. The weights are cast into one bf16 buffer
-    (no fp32 concatenation); the backward gives dx in bf16 and the weights'
-    gradients from one GEMM with fp32 output, split per weight."""
+    """y = x @ cat(weights)^T in bf16 from the weights' bf16 buffer (no fp32
+    concatenation, no cast when the buffer is fresh); the backward gives dx in
+    bf16 and the weights' gradients from one GEMM with fp32 output, split per
+    weight."""
 
     @staticmethod
     def forward(ctx, x, *weights):
         rows = [w.shape[0] for w in weights]
-        w16 = torch.empty(sum(rows), weights[0].shape[1], dtype=torch.bfloat16, device=x.device)
-        o = 0
-        for w, n in zip(weights, rows):
-            w16[o:o + n].copy_(w.detach())
-            o += n
+        w16 = _bf16_weights(weights)
         x16 = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
         y = torch.nn.functional.linear(x16, w16)
         ctx.save_for_backward(x16, w16)

@@ -44,3 +44,33 @@ def test_config3_size_and_flops():
     assert abs(param_count(NaylisForCausalLM(cfg)) - 375.33e6) < 0.01e6
     # 20 layers x 35.46 MFLOP + the 65.5 MFLOP head per token forward; x3 per training token
     assert abs(3 * flops_per_token(cfg, 2048, 16384) - 2.324e9) < 0.001e9
+
+
+def test_bf16_weight_buffer_is_reused_until_a_weight_changes():
+    """The bf16 projections keep one bf16 buffer per group of weights (q/k/v,
+    gate/up, ...): reused while no weight changed, rewritten after an in-place
+    update (the version counter), and shared by the group's rows."""
+    import torch
+    from naylis_b200 import trunk
+    w = torch.nn.Parameter(torch.randn(4, 3))
+    w2 = torch.nn.Parameter(torch.randn(2, 3))
+    b = trunk._bf16_weights([w, w2])
+    assert b.shape == (6, 3) and torch.equal(b, torch.cat([w, w2]).detach().bfloat16())
+    assert trunk.bf16_copy(w).data_ptr() == b.data_ptr()
+    assert trunk._bf16_weights([w, w2]) is b
+    with torch.no_grad():
+        w2.mul_(2)
+    b2 = trunk._bf16_weights([w, w2])
+    assert b2 is b and torch.equal(b2[4:], w2.detach().bfloat16())
+
+
+def test_optimizer_table_layout():
+    """The one-launch AdamW's device table: 48-byte entries of five 64-bit
+    addresses and an int64 count, in the order csrc/launch.h's OptTensor
+    declares them."""
+    import struct
+    from naylis_b200.optim import _pack_entries
+    raw = _pack_entries([(1, 2, 3, 4, 0, 70000), (0x7FFF00001000, 6, 7, 8, 9, 5)])
+    assert len(raw) == 96
+    assert struct.unpack("<5Qq", raw[:48]) == (1, 2, 3, 4, 0, 70000)
+    assert struct.unpack("<5Qq", raw[48:]) == (0x7FFF00001000, 6, 7, 8, 9, 5)
