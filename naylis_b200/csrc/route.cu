@@ -1023,7 +1023,7 @@ cudaError_t launch_route_scan(const void *x, int xdt, void *hq, int cdt, int B, 
 // Two launches with a fixed reduction order (deterministic): each CTA of the
 // first owns a contiguous token range, thread j takes block e = j % nb of tokens
 // j / nb, j / nb + per, ...; it writes its partial sums [sum_e (nb) | sel_e (nb)
-// | entropy] to the workspace. One CTA then adds the partials in CTA order.
+// | entropy] to the workspace. One CTA then adds the partials, a warp per column.
 // out = [aux, entropy, dead, frac_0 .. frac_{nb-1}] (frac is what the backward needs).
 constexpr int kAuxThreads = 256;
 
@@ -1074,41 +1074,36 @@ router_aux_part_kernel(const float *__restrict__ probs, const void *__restrict__
     }
 }
 
-__global__ void __launch_bounds__(kAuxThreads)
+// One warp per column of the partials ([sum_e | sel_e | entropy], 2 nb + 1 of
+// them): lane l adds parts l, l + 32, ... and the warp combines its lanes by a
+// fixed shuffle tree, so the order, and the result, are the same every run.
+constexpr int kAuxFinalThreads = 1024;
+
+__global__ void __launch_bounds__(kAuxFinalThreads)
 router_aux_final_kernel(const float *__restrict__ part, int nparts, int64_t N, int nb, float *__restrict__ out) {
-    __shared__ float s_sum[1024], s_sel[1024];
-    __shared__ float s_ent;
-    const float inv = 1.0f / static_cast<float>(N);
-    for (int e = threadIdx.x; e <= nb; e += blockDim.x) {
-        float a = 0.0f, c = 0.0f;
-        for (int g = 0; g < nparts; ++g) {
-            const float *pg = part + static_cast<int64_t>(g) * (2 * nb + 1);
-            if (e < nb) {
-                a += pg[e];
-                c += pg[nb + e];
-            } else {
-                a += pg[2 * nb];
-            }
-        }
-        if (e < nb) {
-            s_sum[e] = a;
-            s_sel[e] = c;
-        } else {
-            s_ent = a;
-        }
+    __shared__ float s_col[2 * kAuxThreads + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ncols = 2 * nb + 1;
+    for (int col = warp; col < ncols; col += kAuxFinalThreads / 32) {
+        float a = 0.0f;
+        for (int g = lane; g < nparts; g += 32) a += part[static_cast<int64_t>(g) * ncols + col];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) s_col[col] = a;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
+        const float inv = 1.0f / static_cast<float>(N);
         float aux = 0.0f;
         int dead = 0;
         for (int e = 0; e < nb; ++e) {
-            const float frac = s_sel[e] * inv;
-            aux += frac * (s_sum[e] * inv);
-            dead += s_sel[e] == 0.0f;
+            const float frac = s_col[nb + e] * inv;
+            aux += frac * (s_col[e] * inv);
+            dead += s_col[nb + e] == 0.0f;
             out[3 + e] = frac;
         }
         out[0] = static_cast<float>(nb) * aux;
-        out[1] = s_ent * inv;
+        out[1] = s_col[2 * nb] * inv;
         out[2] = static_cast<float>(dead) / static_cast<float>(nb);
     }
 }
@@ -1135,7 +1130,7 @@ cudaError_t launch_router_aux(const float *probs, const void *top_idx, bool idx6
         router_aux_part_kernel<false><<<static_cast<int>(parts), kAuxThreads, 0, st>>>(probs, top_idx, N, nb, top,
                                                                                        tok, ws);
     count_launch();
-    router_aux_final_kernel<<<1, kAuxThreads, 0, st>>>(ws, static_cast<int>(parts), N, nb, out);
+    router_aux_final_kernel<<<1, kAuxFinalThreads, 0, st>>>(ws, static_cast<int>(parts), N, nb, out);
     count_launch();
     return cudaGetLastError();
 }
