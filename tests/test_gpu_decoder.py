@@ -130,3 +130,57 @@ def test_decoder_trains_one_step_with_fused_adamw():
         opt.step()
         losses.append(float(loss))
     assert all(np.isfinite(losses)) and losses[-1] < losses[0], losses
+
+
+def test_decoder_gradients_through_the_buckets_equal_plain_backward():
+    """GradAllReduce on one process (no exchange) with the bf16 path: every
+    parameter's .grad is a view of its bucket, accumulated there by autograd,
+    and equals a plain backward's within 2e-2 of its largest magnitude, the
+    reference's bf16 bar (the read's dK / dV are fp32 atomic sums rounded to
+    bf16 before the k/v projections' backward, so the bank gradient, a sum of
+    2 x layers such terms, differs between any two runs by ~1e-3 of its largest
+    value; a lost or doubled contribution is O(1)), and stays so on a second
+    step after zero_grad. Then the package's AdamW trains on them."""
+    from naylis_b200.data_parallel import GradAllReduce
+    from naylis_b200.optim import AdamW
+    geo = gi.DECODER
+    dev = torch.device("cuda")
+    model, _ = _model()
+    model = model.to(dev).train()
+    ids = gi.decoder_tokens(geo).to(dev)
+
+    for p in model.parameters():
+        p.grad = None
+    torch.manual_seed(5)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = model(ids, labels=ids)
+    loss.backward()
+    ref = {n: (p.grad.clone() if p.grad is not None else None) for n, p in model.named_parameters()}
+
+    dp = GradAllReduce(model)
+    for _ in range(2):
+        dp.zero_grad()
+        torch.manual_seed(5)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(ids, labels=ids)
+        loss.backward()
+        dp.finish()
+        for n, p in model.named_parameters():
+            want = ref[n] if ref[n] is not None else torch.zeros_like(p)
+            err = float((p.grad - want).abs().max())
+            assert err <= 2e-2 * float(want.abs().max()) + 1e-12, (n, err)
+    flat = {b.data_ptr(): b for b in dp.flat}
+    assert all(any(b.data_ptr() <= p.grad.data_ptr() < b.data_ptr() + 4 * b.numel() for b in flat.values())
+               for p in model.parameters())
+    opt = AdamW(model.parameters(), lr=1e-3)
+    losses = []
+    for _ in range(4):
+        dp.zero_grad()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = model(ids, labels=ids)
+        loss.backward()
+        dp.finish()
+        opt.step()
+        losses.append(float(loss))
+    assert all(np.isfinite(losses)) and losses[-1] < losses[0], losses
+    dp.remove()
