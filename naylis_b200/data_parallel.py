@@ -7,13 +7,21 @@ run_biggpu.sh:16-42): one process per GPU, the batch sharded by sequence
 and every gradient — the shared bank ``M_blocks`` (summed over all layers
 first), the router and the q/k/v/o projections — averaged across ranks.
 
-Design: each parameter's ``.grad`` is a view into a flat fp32 bucket, so
-autograd accumulates straight into the communication buffer (no copy). A
-post-accumulate hook marks the parameter ready; buckets are launched as
-asynchronous all-reduces strictly in bucket order (identical on every rank,
-as NCCL requires) as soon as all their parameters are ready, so the exchange
-overlaps the rest of the backward. ``finish()`` launches whatever is left
-and waits; the average is NCCL's own (``ReduceOp.AVG``), or a division by the
+Design: each parameter owns a slot in a flat fp32 bucket, and after the
+backward its ``.grad`` is a view of that slot, so the all-reduce runs on the
+gradients in place. ``zero_grad()`` clears the gradients to None instead of
+zeroing the buckets: the decoder's bf16 projections (``trunk.linear_f32grad``)
+write their weight-gradient GEMM's fp32 output straight into the slots, which
+autograd adopts as ``.grad`` (no fill, no add); any other gradient is copied
+into its slot by the post-accumulate hook, which then marks the parameter
+ready. Parameters that one GEMM produces gradients for together (``groups``,
+or the module's ``grad_groups()``: the fused q/k/v and gate/up projections)
+sit next to each other in one bucket, in the GEMM's row order. Buckets are
+launched as asynchronous all-reduces strictly in bucket order (identical on
+every rank, as NCCL requires) as soon as all their parameters are ready, so
+the exchange overlaps the rest of the backward. ``finish()`` zero-fills the
+slots of parameters that got no gradient, launches whatever is left and
+waits; the average is NCCL's own (``ReduceOp.AVG``), or a division by the
 world size on backends without it.
 
 Gradient accumulation (the reference's ``[train] grad_accum``, pretrain.py:795
@@ -34,10 +42,12 @@ import contextlib
 import torch
 import torch.distributed as dist
 
+from . import trunk
+
 
 class GradAllReduce:
     def __init__(self, module: torch.nn.Module, process_group=None, bucket_mb: float = 32.0,
-                 average: bool = True, overlap: bool = True, comm_dtype=None):
+                 average: bool = True, overlap: bool = True, comm_dtype=None, groups=None):
         self.group = process_group
         # overlap=False: no collective from the backward's hooks; finish()
         # exchanges every bucket. For a backward captured in a CUDA graph,
@@ -57,31 +67,53 @@ class GradAllReduce:
             self._op = dist.ReduceOp.AVG
             self._divide = False
         params = [p for p in module.parameters() if p.requires_grad]
-        # gradients arrive roughly in reverse registration order
-        params = list(reversed(params))
-        cap = int(bucket_mb * (1 << 20) // 4)
-        self.buckets = []
-        cur = []
-        size = 0
         for p in params:
             if p.dtype != torch.float32:
                 raise RuntimeError("GradAllReduce keeps fp32 master gradients; got "
                                    f"a {p.dtype} parameter")
-            if cur and size + p.numel() > cap:
+        if groups is None:
+            groups = module.grad_groups() if hasattr(module, "grad_groups") else []
+        members = {id(p) for p in params}
+        group_of = {}
+        for g in groups:
+            g = tuple(g)
+            if all(id(p) in members for p in g) and not any(id(p) in group_of for p in g):
+                for p in g:
+                    group_of[id(p)] = g
+        # gradients arrive roughly in reverse registration order; a group is placed,
+        # in its own order, where its first member appears
+        units, placed = [], set()
+        for p in reversed(params):
+            g = group_of.get(id(p), (p,))
+            if id(g[0]) not in placed:
+                units.append(g)
+                placed.update(id(q) for q in g)
+        cap = int(bucket_mb * (1 << 20) // 4)
+        self.buckets = []
+        cur = []
+        size = 0
+        for g in units:
+            n = sum(p.numel() for p in g)
+            if cur and size + n > cap:
                 self.buckets.append(cur)
                 cur, size = [], 0
-            cur.append(p)
-            size += p.numel()
+            cur.extend(g)
+            size += n
         if cur:
             self.buckets.append(cur)
+        self.params = [p for ps in self.buckets for p in ps]
         self.flat = []
         self._bucket_of = {}
+        self._slot = {}
         for i, ps in enumerate(self.buckets):
             n = sum(p.numel() for p in ps)
             buf = torch.zeros(n, dtype=torch.float32, device=ps[0].device)
             off = 0
             for p in ps:
-                p.grad = buf[off:off + p.numel()].view_as(p)
+                view = buf[off:off + p.numel()].view_as(p)
+                p.grad = view
+                self._slot[p] = view
+                trunk.register_grad_slot(p, buf, off)
                 off += p.numel()
                 self._bucket_of[p] = i
             self.flat.append(buf)
@@ -96,16 +128,26 @@ class GradAllReduce:
         self._works = []
 
     def zero_grad(self):
-        for buf in self.flat:
-            buf.zero_()
-        for i, ps in enumerate(self.buckets):
-            # an optimizer may have replaced .grad; re-attach the views
-            off = 0
-            for p in ps:
-                if p.grad is None or p.grad.data_ptr() != self.flat[i].data_ptr() + off * 4:
-                    p.grad = self.flat[i][off:off + p.numel()].view_as(p)
-                off += p.numel()
+        """Clear every gradient to None (no device work): the next backward writes
+        or copies each gradient into its slot, and ``finish()`` zero-fills the slots
+        of parameters that got none."""
+        for p in self.params:
+            p.grad = None
+        trunk.release_grad_slots(self.params)
         self._reset_state()
+
+    def _place(self, p):
+        """Make p.grad the view of its slot, copying the gradient in if autograd
+        left it elsewhere (or zero-filling the slot when there is none)."""
+        slot = self._slot[p]
+        g = p.grad
+        if g is None:
+            slot.zero_()
+        elif g.data_ptr() != slot.data_ptr() or g.stride() != slot.stride():
+            slot.copy_(g)
+        else:
+            return
+        p.grad = slot
 
     @contextlib.contextmanager
     def no_sync(self):
@@ -120,6 +162,9 @@ class GradAllReduce:
 
     def _launch_ready(self, force: bool = False):
         while self._next < len(self.buckets) and (force or self._pending[self._next] == 0):
+            for p in self.buckets[self._next]:
+                if p.grad is None:
+                    self._place(p)
             buf = self.flat[self._next]
             if self.world > 1:
                 if self.wire is not None:
@@ -129,6 +174,7 @@ class GradAllReduce:
             self._next += 1
 
     def _on_ready(self, p):
+        self._place(p)
         if not self._sync:
             return
         i = self._bucket_of[p]
@@ -158,3 +204,4 @@ class GradAllReduce:
         for h in self._hooks:
             h.remove()
         self._hooks = []
+        trunk.unregister_grad_slots(self.params)

@@ -189,6 +189,11 @@ class DecoderLayer(nn.Module):
         x = x + self.mom(self.mom_norm(x), M_blocks)
         return x + self._ckpt(lambda h: self.mlp(self.post_attention_layernorm(h)), x)
 
+    def grad_groups(self):
+        """Weights whose gradients one GEMM produces, in that GEMM's row order."""
+        a, m = self.self_attn, self.mlp
+        return [(a.q_proj.weight, a.k_proj.weight, a.v_proj.weight), (m.gate_proj.weight, m.up_proj.weight)]
+
     def forward_fused(self, x, pending, pending_scale, M_blocks, cos, sin):
         """bf16 path: each residual add runs inside the RMSNorm that follows it
         (csrc/trunk.cu add_rmsnorm). x is the residual stream before `pending`,
@@ -215,6 +220,9 @@ class NaylisModel(nn.Module):
         self.layers = nn.ModuleList([DecoderLayer(cfg) for _ in range(cfg.num_hidden_layers)])
         self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         self.cfg = cfg
+
+    def grad_groups(self):
+        return [g for layer in self.layers for g in layer.grad_groups()]
 
     def forward(self, input_ids):
         x = self.embed_tokens(input_ids)
@@ -258,6 +266,12 @@ class NaylisForCausalLM(nn.Module):
             elif isinstance(m, MoMLayer):
                 m.mom_scale.zero_()
         self.model.M_blocks.normal_(0.0, 0.02)
+
+    def grad_groups(self):
+        """Parameter groups a gradient bucketing wrapper keeps contiguous and in
+        order (data_parallel.GradAllReduce), so the fused q/k/v and gate/up
+        weight-gradient GEMMs can write into the buckets directly."""
+        return self.model.grad_groups()
 
     def mom_layers(self):
         return [layer.mom for layer in self.model.layers]

@@ -205,11 +205,57 @@ def mark_bf16_fresh(param) -> None:
         e[2] = param._version
 
 
+# parameter -> [flat fp32 gradient buffer, element offset of the parameter's slot in it,
+# claimed]: registered by a gradient bucketing wrapper (data_parallel.GradAllReduce).
+# While a parameter's .grad is None and its slot is unclaimed, the weight-gradient GEMM
+# of linear_f32grad writes straight into the slot and hands autograd a view of it, which
+# AccumulateGrad then adopts as .grad (no zero fill, no add, no copy).
+_GRAD_SLOTS = WeakIdKeyDictionary()
+
+
+def register_grad_slot(param, flat, offset: int) -> None:
+    """Declare flat[offset : offset + param.numel()] as `param`'s gradient storage."""
+    _GRAD_SLOTS[param] = [flat, int(offset), False]
+
+
+def release_grad_slots(params) -> None:
+    """Re-arm the slots of `params` (their gradients were cleared to None)."""
+    for p in params:
+        e = _GRAD_SLOTS.get(p)
+        if e is not None:
+            e[2] = False
+
+
+def unregister_grad_slots(params) -> None:
+    for p in params:
+        _GRAD_SLOTS.pop(p, None)
+
+
+def _claim_grad_rows(weights, cols):
+    """The (sum of rows, cols) fp32 view of the slots that hold cat(weights)' gradients,
+    claimed for this backward, or None: every weight needs an unclaimed slot, no
+    .grad yet, fp32, and the slots must follow each other in the weights' order."""
+    ents = [_GRAD_SLOTS.get(w) for w in weights]
+    if any(e is None or e[2] for e in ents):
+        return None
+    if any(w.grad is not None or w.dtype != torch.float32 for w in weights):
+        return None
+    flat, start = ents[0][0], ents[0][1]
+    o = start
+    for w, e in zip(weights, ents):
+        if e[0] is not flat or e[1] != o:
+            return None
+        o += w.numel()
+    for e in ents:
+        e[2] = True
+    return flat[start:o].view(-1, cols)
+
+
 class _LinearF32Grad(torch.autograd.Function):
     """y = x @ cat(weights)^T in bf16 from the weights' bf16 buffer (no fp32
     concatenation, no cast when the buffer is fresh); the backward gives dx in
     bf16 and the weights' gradients from one GEMM with fp32 output, split per
-    weight."""
+    weight — written into the weights' gradient slots when they have them."""
 
     @staticmethod
     def forward(ctx, x, *weights):
@@ -219,7 +265,7 @@ class _LinearF32Grad(torch.autograd.Function):
         y = torch.nn.functional.linear(x16, w16)
         ctx.save_for_backward(x16, w16)
         ctx.rows = rows
-        ctx.wdtypes = [w.dtype for w in weights]
+        ctx.weights = weights
         ctx.x_dtype = x.dtype
         return y
 
@@ -227,13 +273,19 @@ class _LinearF32Grad(torch.autograd.Function):
     def backward(ctx, dy):
         x16, w16 = ctx.saved_tensors
         dy = dy.to(torch.bfloat16)
-        dx = torch.matmul(dy, w16)
-        dw = torch.mm(dy.reshape(-1, dy.shape[-1]).t(), x16.reshape(-1, x16.shape[-1]), out_dtype=torch.float32)
+        dx = torch.matmul(dy, w16) if ctx.needs_input_grad[0] else None
+        dy2 = dy.reshape(-1, dy.shape[-1]).t()
+        x2 = x16.reshape(-1, x16.shape[-1])
+        slot = _claim_grad_rows(ctx.weights, x2.shape[1])
+        if slot is not None:
+            dw = torch.mm(dy2, x2, out_dtype=torch.float32, out=slot)
+        else:
+            dw = torch.mm(dy2, x2, out_dtype=torch.float32)
         grads, o = [], 0
-        for n, dt in zip(ctx.rows, ctx.wdtypes):
-            grads.append(dw[o:o + n] if dt == torch.float32 else dw[o:o + n].to(dt))
+        for n, w in zip(ctx.rows, ctx.weights):
+            grads.append(dw[o:o + n] if w.dtype == torch.float32 else dw[o:o + n].to(w.dtype))
             o += n
-        return (dx.to(ctx.x_dtype), *grads)
+        return (None if dx is None else dx.to(ctx.x_dtype), *grads)
 
 
 def linear_f32grad(x, *weights):
@@ -281,4 +333,5 @@ def cross_entropy_sum(logits, labels, ignore_index: int = -100):
     return _CrossEntropySum.apply(logits, labels, int(ignore_index))
 
 
-__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum", "linear_f32grad"]
+__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum", "linear_f32grad", "register_grad_slot",
+           "release_grad_slots", "unregister_grad_slots"]

@@ -74,3 +74,60 @@ def test_optimizer_table_layout():
     assert len(raw) == 96
     assert struct.unpack("<5Qq", raw[:48]) == (1, 2, 3, 4, 0, 70000)
     assert struct.unpack("<5Qq", raw[48:]) == (0x7FFF00001000, 6, 7, 8, 9, 5)
+
+
+def test_gradient_buckets_keep_fused_projection_groups_contiguous():
+    """GradAllReduce lays the decoder's q/k/v and gate/up weights next to each
+    other in one bucket in the fused GEMM's row order, registers every slot, and
+    zero_grad clears the gradients to None; finish() gives a parameter that got
+    no gradient its zero-filled slot."""
+    import torch
+    from naylis_b200 import trunk
+    from naylis_b200.data_parallel import GradAllReduce
+    from naylis_b200.decoder import NaylisConfig, NaylisForCausalLM
+    cfg = NaylisConfig(vocab_size=64, hidden_size=32, intermediate_size=48, num_hidden_layers=2,
+                       num_attention_heads=2, mem_size=32, mom_block_size=8, mom_top_blocks=2, mom_router_rank=4)
+    model = NaylisForCausalLM(cfg)
+    dp = GradAllReduce(model, bucket_mb=0.01)
+    try:
+        assert len(dp.buckets) > 2
+        for g in model.grad_groups():
+            ents = [trunk._GRAD_SLOTS[w] for w in g]
+            assert all(e[0] is ents[0][0] for e in ents)
+            offs = [e[1] for e in ents]
+            assert offs == [offs[0] + sum(w.numel() for w in g[:i]) for i in range(len(g))]
+        assert sum(b.numel() for b in dp.flat) == sum(p.numel() for p in model.parameters())
+        dp.zero_grad()
+        assert all(p.grad is None for p in model.parameters())
+        dp.finish()
+        assert all(p.grad is not None and not p.grad.any() for p in model.parameters())
+    finally:
+        dp.remove()
+    assert all(w not in trunk._GRAD_SLOTS for w in model.parameters())
+
+
+def test_gradient_slot_claims():
+    """A fused GEMM may write a group's gradients into their slots only when the
+    slots follow each other in order, no weight has a gradient yet and no other
+    GEMM of this backward claimed them; release re-arms them."""
+    import torch
+    from naylis_b200 import trunk
+    flat = torch.zeros(40)
+    a, b, c = (torch.nn.Parameter(torch.randn(2, 4)) for _ in range(3))
+    trunk.register_grad_slot(a, flat, 0)
+    trunk.register_grad_slot(b, flat, 8)
+    trunk.register_grad_slot(c, flat, 24)
+    try:
+        assert trunk._claim_grad_rows([b, a], 4) is None          # out of order
+        assert trunk._claim_grad_rows([a, c], 4) is None          # not adjacent
+        rows = trunk._claim_grad_rows([a, b], 4)
+        assert rows.shape == (4, 4) and rows.data_ptr() == flat.data_ptr()
+        assert trunk._claim_grad_rows([a, b], 4) is None          # claimed in this backward
+        c.grad = torch.zeros(2, 4)
+        assert trunk._claim_grad_rows([c], 4) is None             # already has a gradient
+        trunk.release_grad_slots([a, b, c])
+        c.grad = None
+        assert trunk._claim_grad_rows([c], 4).data_ptr() == flat[24:].data_ptr()
+        assert trunk._claim_grad_rows([a, b], 4) is not None
+    finally:
+        trunk.unregister_grad_slots([a, b, c])

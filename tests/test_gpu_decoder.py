@@ -23,6 +23,8 @@ loss within 1e-5 relative, logits and every gradient within 1e-4.
 """
 import os
 
+import contextlib
+
 import numpy as np
 import pytest
 import torch
@@ -134,13 +136,17 @@ def test_decoder_trains_one_step_with_fused_adamw():
 
 def test_decoder_gradients_through_the_buckets_equal_plain_backward():
     """GradAllReduce on one process (no exchange) with the bf16 path: every
-    parameter's .grad is a view of its bucket, accumulated there by autograd,
+    parameter's .grad is a view of its bucket slot (the projections' weight
+    gradients written there by their GEMM, the others copied in by the hook),
     and equals a plain backward's within 2e-2 of its largest magnitude, the
     reference's bf16 bar (the read's dK / dV are fp32 atomic sums rounded to
     bf16 before the k/v projections' backward, so the bank gradient, a sum of
     2 x layers such terms, differs between any two runs by ~1e-3 of its largest
     value; a lost or doubled contribution is O(1)), and stays so on a second
-    step after zero_grad. Then the package's AdamW trains on them."""
+    step after zero_grad and, doubled, after two micro-batches (the first inside
+    no_sync, the second adding onto the slots). Then the package's AdamW trains
+    on them."""
+    from naylis_b200 import trunk
     from naylis_b200.data_parallel import GradAllReduce
     from naylis_b200.optim import AdamW
     geo = gi.DECODER
@@ -164,11 +170,27 @@ def test_decoder_gradients_through_the_buckets_equal_plain_backward():
         with torch.autocast("cuda", dtype=torch.bfloat16):
             loss = model(ids, labels=ids)
         loss.backward()
+        # the fused q/k/v and gate/up GEMMs wrote straight into their slots
+        for g in model.grad_groups():
+            assert all(trunk._GRAD_SLOTS[w][2] for w in g)
         dp.finish()
         for n, p in model.named_parameters():
             want = ref[n] if ref[n] is not None else torch.zeros_like(p)
             err = float((p.grad - want).abs().max())
             assert err <= 2e-2 * float(want.abs().max()) + 1e-12, (n, err)
+    dp.zero_grad()
+    for i in range(2):
+        ctx = dp.no_sync() if i == 0 else contextlib.nullcontext()
+        with ctx:
+            torch.manual_seed(5)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = model(ids, labels=ids)
+            loss.backward()
+    dp.finish()
+    for n, p in model.named_parameters():
+        want = 2 * ref[n] if ref[n] is not None else torch.zeros_like(p)
+        err = float((p.grad - want).abs().max())
+        assert err <= 2e-2 * float(want.abs().max()) + 1e-12, (n, err)
     flat = {b.data_ptr(): b for b in dp.flat}
     assert all(any(b.data_ptr() <= p.grad.data_ptr() < b.data_ptr() + 4 * b.numel() for b in flat.values())
                for p in model.parameters())
