@@ -390,7 +390,8 @@ def run_model_cfg3(args):
         dist.barrier()
     t_wall1 = time.time()
     launches = lib.mom_kernel_launches() - l0
-    total_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    each_ms = sorted(a.elapsed_time(b) for a, b in zip(starts, ends))
+    total_ms = sum(each_ms)
     if clocks:
         clocks.window = (t_wall0, t_wall1)
     if world > 1:
@@ -445,6 +446,8 @@ def run_model_cfg3(args):
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 3),
+            "step_ms_rank0": {"min": round(each_ms[0], 3), "median": round(each_ms[len(each_ms) // 2], 3),
+                              "max": round(each_ms[-1], 3)},
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,

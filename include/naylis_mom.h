@@ -344,6 +344,12 @@ MOM_API int mom_scale_fwd(const void *o, int o_dtype, int64_t n, const float *sc
 MOM_API int mom_scale_bwd(const void *g, int g_dtype, const void *o, int o_dtype, int64_t n,
                           const float *scale, void *d_o, float *d_scale, void *stream);
 
+/* Router Gumbel noise from uniform draws u (fp32, n values; torch.rand): out =
+ * noise_scale * -log(-log(u + 1e-9) + 1e-9), bit for bit the reference's
+ * expression (model.py:209-213) evaluated by torch's fp32 kernels. out may be u.
+ * Replaces the seven elementwise torch ops of that expression. */
+MOM_API int mom_gumbel(const float *u, int64_t n, float noise_scale, float *out, void *stream);
+
 /* Reads (and clears) the device error word of a plan: MOM_OK, or
  * MOM_ERR_DEVICE_INDEX when mom_bucket saw an index outside [0, nb).
  * Synchronises `stream`. */

@@ -339,6 +339,16 @@ int mom_scale_bwd(const void *g, int g_dtype, const void *o, int o_dtype, int64_
     return e == cudaSuccess ? MOM_OK : cuda_fail(e, "scale_bwd");
 }
 
+int mom_gumbel(const float *u, int64_t n, float noise_scale, float *out, void *stream) {
+    MOM_REQUIRE(n >= 0, "n must be >= 0");
+    if (n == 0) return MOM_OK;
+    MOM_REQUIRE(u && out, "null pointer argument");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_gumbel(u, n, noise_scale, out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "gumbel");
+}
+
 int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *stream) {
     MOM_REQUIRE(plan, "null plan");
     const mom::PlanLayout L = mom::plan_layout(N, nb, top);

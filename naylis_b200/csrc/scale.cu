@@ -142,4 +142,43 @@ cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, con
     return cudaGetLastError();
 }
 
+// Gumbel noise of the router (model.py:209-213 of the reference:
+// noise_scale * -log(-log(u + 1e-9) + 1e-9) on torch.rand draws u), as one pass
+// instead of the add / log / neg / add / log / neg / mul kernels the expression
+// runs as torch ops. Each step is the same fp32 operation torch's kernel does
+// (an fp32 add of the float constant, logf, negation, one fp32 multiply), in
+// the same order, so the result is bit-identical. out may alias u.
+__device__ __forceinline__ float gumbel_of(float u, float scale) {
+    const float a = -logf(u + 1e-9f);
+    return scale * -logf(a + 1e-9f);
+}
+
+__global__ void __launch_bounds__(256)
+gumbel_kernel(const float *u, int64_t n, float scale, float *out, bool vec) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t i0 = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = n / 4;
+        for (int64_t i = i0; i < n4; i += stride) {
+            float4 v = reinterpret_cast<const float4 *>(u)[i];
+            v.x = gumbel_of(v.x, scale);
+            v.y = gumbel_of(v.y, scale);
+            v.z = gumbel_of(v.z, scale);
+            v.w = gumbel_of(v.w, scale);
+            reinterpret_cast<float4 *>(out)[i] = v;
+        }
+        done = n4 * 4;
+    }
+    for (int64_t i = done + i0; i < n; i += stride) out[i] = gumbel_of(u[i], scale);
+}
+
+cudaError_t launch_gumbel(const float *u, int64_t n, float scale, float *out, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    const bool v = vec_ok(u, MOM_F32) && vec_ok(out, MOM_F32);
+    gumbel_kernel<<<scale_grid(n), 256, 0, st>>>(u, n, scale, out, v);
+    count_launch();
+    return cudaGetLastError();
+}
+
 }  // namespace mom

@@ -192,7 +192,8 @@ class DecoderLayer(nn.Module):
     def grad_groups(self):
         """Weights whose gradients one GEMM produces, in that GEMM's row order."""
         a, m = self.self_attn, self.mlp
-        return [(a.q_proj.weight, a.k_proj.weight, a.v_proj.weight), (m.gate_proj.weight, m.up_proj.weight)]
+        return [(a.q_proj.weight, a.k_proj.weight, a.v_proj.weight), (m.gate_proj.weight, m.up_proj.weight),
+                *self.mom.grad_groups()]
 
     def forward_fused(self, x, pending, pending_scale, M_blocks, cos, sin):
         """bf16 path: each residual add runs inside the RMSNorm that follows it

@@ -106,6 +106,10 @@ class MoMLayer(nn.Module):
                 use_reentrant=False, preserve_rng_state=False)
         return self._read(xq, top_idx, log_gates, M_blocks, mode)
 
+    def grad_groups(self):
+        """The bank's k and v weights, whose gradients one GEMM produces (k rows first)."""
+        return [(self.k_proj.weight, self.v_proj.weight)]
+
     @staticmethod
     def _proj(lin, x):
         """lin(x); under CUDA bf16 autocast the bf16 GEMM with fp32 weight
@@ -117,9 +121,14 @@ class MoMLayer(nn.Module):
     def _read(self, x, top_idx, log_gates, M_blocks, mode):
         B, S, D = x.shape
         q_sh = self._proj(self.q_proj, x).view(B, S, self.n_heads, self.head_dim)
-        slots = M_blocks.view(self.mem_slots, D)
-        k_shared = self._proj(self.k_proj, slots)
-        v_shared = self._proj(self.v_proj, slots)
+        if M_blocks.is_cuda and torch.is_autocast_enabled("cuda") and \
+                torch.get_autocast_dtype("cuda") == torch.bfloat16 and M_blocks.dtype == torch.float32:
+            # both bank projections in one GEMM over the bank's bf16 copy
+            k_shared, v_shared = trunk.bank_kv(M_blocks, self.k_proj.weight, self.v_proj.weight, self.mem_slots)
+        else:
+            slots = M_blocks.view(self.mem_slots, D)
+            k_shared = self._proj(self.k_proj, slots)
+            v_shared = self._proj(self.v_proj, slots)
         out = mom_kernels.mom_read_log_gates(q_sh, k_shared, v_shared, top_idx, log_gates,
                                              num_blocks=self.num_blocks, block_size=self.block_size,
                                              mode=mode)

@@ -163,7 +163,18 @@ class _MomReadFunction(torch.autograd.Function):
                   dout.data_ptr(), lse.data_ptr(), _lib.BF16, B, S, H, hd, num_blocks, block_size,
                   top, plan.data_ptr(), q_rows.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                   dlg.data_ptr(), ws.data_ptr(), ws.numel(), st)
-        return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
+        return (dq, *_kv_grads(dk, dv, k.dtype), None, dlg, None, None)
+
+
+def _kv_grads(dk, dv, dtype):
+    """dK, dV cast to the bank's dtype, written side by side into one (L, 2n)
+    buffer and returned as its two halves, so the bank projection's backward
+    (trunk.bank_kv) reads [dK | dV] without another copy."""
+    L, n = dk.shape
+    both = torch.empty(L, 2 * n, dtype=dtype, device=dk.device)
+    both[:, :n].copy_(dk)
+    both[:, n:].copy_(dv)
+    return both[:, :n], both[:, n:]
 
 
 class _MomReadSplitFunction(torch.autograd.Function):
@@ -221,7 +232,7 @@ class _MomReadSplitFunction(torch.autograd.Function):
                   dout.data_ptr(), lse_rows.data_ptr(), weights.data_ptr(), _lib.BF16, B, S, H, hd, num_blocks,
                   block_size, top, idx.data_ptr(), idt, plan.data_ptr(), q_rows.data_ptr(), dq.data_ptr(),
                   dk.data_ptr(), dv.data_ptr(), dlg.data_ptr(), ws.data_ptr(), ws.numel(), st)
-        return dq, dk.to(k.dtype), dv.to(v.dtype), None, dlg, None, None
+        return (dq, *_kv_grads(dk, dv, k.dtype), None, dlg, None, None)
 
 
 class _MomReadF32Function(torch.autograd.Function):
@@ -526,9 +537,15 @@ def router_aux(probs, top_idx, num_blocks: int):
 
 def gumbel_noise(shape, device, noise_scale: float):
     """Scaled Gumbel noise drawn exactly as the reference draws it
-    (model.py:209-213: torch.rand_like on the fp32 logits)."""
+    (model.py:209-213: torch.rand_like on the fp32 logits, then
+    noise_scale * -log(-log(u + 1e-9) + 1e-9)); on CUDA the transform is one
+    kernel (csrc/scale.cu, gumbel) with the same fp32 results, in place.
+    CUDA devices only."""
+    if _device_type(device) != "cuda":
+        raise RuntimeError("sm100 gumbel_noise: device must be CUDA")
     u = torch.rand(shape, device=device, dtype=torch.float32)
-    return noise_scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
+    _lib.call("mom_gumbel", u.data_ptr(), u.numel(), float(noise_scale), u.data_ptr(), _stream(u.device))
+    return u
 
 
 __all__ = ["MODE", "preflight", "resolve_mode", "announce", "mom_read", "mom_route", "mom_scale", "router_aux",

@@ -297,6 +297,67 @@ def linear_f32grad(x, *weights):
     return _LinearF32Grad.apply(x, *weights)
 
 
+def _side_by_side(a, b):
+    """(R, n) a and b as one (R, 2n) tensor: a zero-copy view when b is the right
+    half of a buffer whose left half is a (how the read's backward returns its
+    dK / dV), else a copy."""
+    R, n = a.shape
+    if (b.dtype == a.dtype and b.device == a.device and a.stride() == (2 * n, 1) and b.stride() == (2 * n, 1)
+            and b.data_ptr() == a.data_ptr() + n * a.element_size()):
+        return a.as_strided((R, 2 * n), (2 * n, 1))
+    out = torch.empty(R, 2 * n, dtype=a.dtype, device=a.device)
+    out[:, :n].copy_(a)
+    out[:, n:].copy_(b)
+    return out
+
+
+class _BankKV(torch.autograd.Function):
+    """k = slots @ Wk^T, v = slots @ Wv^T for the bank's L slots (its rows viewed
+    as (L, d)) as one batched bf16 GEMM over the bank's bf16 copy; the backward
+    is one GEMM for the bank's gradient ([dk | dv] @ [Wk; Wv], fp32 out) and one
+    for both weights' gradients ([dk | dv]^T @ slots, fp32, into their slots
+    when they have them)."""
+
+    @staticmethod
+    def forward(ctx, bank, wk, wv, L):
+        d = wk.shape[1]
+        m16 = _bf16_weights([bank]).view(L, d)
+        w16 = _bf16_weights([wk, wv])
+        n = wk.shape[0]
+        kv = torch.bmm(m16.unsqueeze(0).expand(2, L, d), w16.view(2, n, d).transpose(1, 2))
+        ctx.save_for_backward(m16, w16)
+        ctx.weights = (wk, wv)
+        ctx.bank_shape = bank.shape
+        return kv[0], kv[1]
+
+    @staticmethod
+    def backward(ctx, dk, dv):
+        m16, w16 = ctx.saved_tensors
+        wk, wv = ctx.weights
+        n = wk.shape[0]
+        dkv = _side_by_side(dk.to(torch.bfloat16), dv.to(torch.bfloat16))
+        dbank = torch.mm(dkv, w16, out_dtype=torch.float32) if ctx.needs_input_grad[0] else None
+        slot = _claim_grad_rows(ctx.weights, m16.shape[1])
+        if slot is not None:
+            dw = torch.mm(dkv.t(), m16, out_dtype=torch.float32, out=slot)
+        else:
+            dw = torch.mm(dkv.t(), m16, out_dtype=torch.float32)
+        return (None if dbank is None else dbank.view(ctx.bank_shape), dw[:n], dw[n:], None)
+
+
+def bank_kv(bank, wk, wv, slots: int):
+    """The k and v projections of the memory bank under bf16 autocast: bank
+    (num_blocks, block_size * d) fp32 viewed as (slots, d); wk, wv (n, d) fp32.
+    Returns k, v (slots, n) bf16, contiguous. The bank and the weights are cast
+    to bf16 once per update (their bf16 copies, which the package's AdamW
+    rewrites); the weight gradients are fp32 from the GEMM."""
+    if not bank.is_cuda:
+        raise RuntimeError("bank_kv: CUDA tensors only")
+    if bank.numel() != slots * wk.shape[1] or wv.shape != wk.shape:
+        raise RuntimeError("bank_kv: bank must hold slots x d values and wk, wv be (n, d)")
+    return _BankKV.apply(bank, wk, wv, int(slots))
+
+
 class _CrossEntropySum(torch.autograd.Function):
     @staticmethod
     def forward(ctx, logits, labels, ignore_index):
@@ -333,5 +394,5 @@ def cross_entropy_sum(logits, labels, ignore_index: int = -100):
     return _CrossEntropySum.apply(logits, labels, int(ignore_index))
 
 
-__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum", "linear_f32grad", "register_grad_slot",
+__all__ = ["rope_qkv", "swiglu", "add_rmsnorm", "cross_entropy_sum", "linear_f32grad", "bank_kv", "register_grad_slot",
            "release_grad_slots", "unregister_grad_slots"]

@@ -216,7 +216,7 @@ def test_ctypes_signatures_match_the_header():
         decls[name] = (ret.replace(" ", ""), kinds)
     assert set(decls) == set(_lib.SIGNATURES)
     arg_type = {"ptr": ctypes.c_void_p, "int": ctypes.c_int, "int64_t": ctypes.c_int64, "size_t": ctypes.c_size_t,
-                "double": ctypes.c_double}
+                "double": ctypes.c_double, "float": ctypes.c_float}
     for name, (res, argtypes) in _lib.SIGNATURES.items():
         ret, kinds = decls[name]
         assert len(argtypes) == len(kinds), f"{name}: {len(argtypes)} ctypes args, header has {len(kinds)}"

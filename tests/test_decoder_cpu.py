@@ -131,3 +131,19 @@ def test_gradient_slot_claims():
         assert trunk._claim_grad_rows([a, b], 4) is not None
     finally:
         trunk.unregister_grad_slots([a, b, c])
+
+
+def test_side_by_side_views_and_copies():
+    """The bank projection's backward reads [dK | dV] as one (L, 2n) operand: a
+    view when the read's backward returned the two halves of one buffer, a copy
+    otherwise."""
+    import torch
+    from naylis_b200 import trunk
+    both = torch.randn(5, 8)
+    a, b = both[:, :4], both[:, 4:]
+    v = trunk._side_by_side(a, b)
+    assert v.data_ptr() == both.data_ptr() and torch.equal(v, both)
+    a2, b2 = torch.randn(5, 4), torch.randn(5, 4)
+    c = trunk._side_by_side(a2, b2)
+    assert torch.equal(c, torch.cat([a2, b2], 1))
+    assert torch.equal(trunk._side_by_side(b, a), torch.cat([b, a], 1))

@@ -399,3 +399,18 @@ def test_router_aux_matches_reference_formula(N, nb, top, idx_dtype):
     (out[0] * 0.3).backward()
     (aux * 0.3).backward()
     assert torch.allclose(probs.grad, pr.grad, rtol=1e-6, atol=1e-9)
+
+
+@pytest.mark.parametrize("shape,scale", [((8, 2048, 8), 1.0), ((3, 7, 5), 0.7), ((1, 1, 3), 2.5)])
+def test_gumbel_noise_is_the_torch_expression_bitwise(shape, scale):
+    """The router's Gumbel noise as one kernel equals the reference's torch
+    expression noise_scale * -log(-log(u + 1e-9) + 1e-9) on the same draws u,
+    bit for bit (105 values: the scalar tail; 131,072: the vector form)."""
+    from naylis_b200 import mom_kernels as mk
+    dev = torch.device("cuda")
+    torch.manual_seed(9)
+    got = mk.gumbel_noise(shape, dev, scale)
+    torch.manual_seed(9)
+    u = torch.rand(shape, device=dev, dtype=torch.float32)
+    want = scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
+    assert torch.equal(got, want)

@@ -148,3 +148,32 @@ def test_cross_entropy_matches_torch(R, V, scale):
     assert torch.all(got[labels == -100] == 0)
     # one bf16 step of the fp32 value, or an fp32 ulp-level absolute floor
     assert ((got - want).abs() <= want.abs() * 2.0 ** -7 + 1e-7).all()
+
+
+@pytest.mark.parametrize("nb,bs,d,n", [(8, 128, 1024, 1024), (4, 32, 256, 128)])
+def test_bank_kv_matches_two_linears(nb, bs, d, n):
+    """The bank's k / v projections as one batched GEMM (trunk.bank_kv) against
+    two bf16 linears on the bank cast to bf16: k and v within one bf16 rounding
+    step (cuBLAS may sum in another order), the bank and weight gradients
+    within 1e-2 of their largest magnitude (the reference rounds them through
+    bf16, bank_kv keeps fp32) — also when dK / dV do not arrive side by side."""
+    from naylis_b200 import trunk
+    torch.manual_seed(11)
+    dev = torch.device("cuda")
+    L = nb * bs
+    bank = torch.nn.Parameter(0.02 * torch.randn(nb, bs * d, device=dev))
+    wk = torch.nn.Parameter(0.02 * torch.randn(n, d, device=dev))
+    wv = torch.nn.Parameter(0.02 * torch.randn(n, d, device=dev))
+    gk = torch.randn(L, n, device=dev).bfloat16()
+    gv = torch.randn(L, n, device=dev).bfloat16()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        k, v = trunk.bank_kv(bank, wk, wv, L)
+        kr = torch.nn.functional.linear(bank.view(L, d), wk)
+        vr = torch.nn.functional.linear(bank.view(L, d), wv)
+    assert k.is_contiguous() and v.is_contiguous() and k.dtype == torch.bfloat16
+    for a, b in ((k, kr), (v, vr)):
+        assert ((a.float() - b.float()).abs() <= b.float().abs() * 2.0 ** -7 + 1e-6).all()
+    grads = torch.autograd.grad((k.float() * gk.float()).sum() + (v.float() * gv.float()).sum(), (bank, wk, wv))
+    refs = torch.autograd.grad((kr.float() * gk.float()).sum() + (vr.float() * gv.float()).sum(), (bank, wk, wv))
+    for a, b in zip(grads, refs):
+        assert float((a - b).abs().max()) <= 1e-2 * float(b.abs().max())
