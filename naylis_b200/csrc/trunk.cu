@@ -264,48 +264,108 @@ rope_qkv_bwd_v8_kernel(const uint16_t *__restrict__ dq, const uint16_t *__restri
 }
 
 // 8 columns per thread
+// The flat index i = t * fv + c of a grid-stride loop, advanced by the grid's
+// thread count without a 64-bit division per step (SwiGLU is issue-bound: the
+// division cost about as many instructions as the arithmetic of a vector).
+struct RowWalk {
+    int64_t t, dt;
+    int c, dc, fv;
+    __device__ RowWalk(int64_t i0, int64_t stride, int fv_) : fv(fv_) {
+        t = i0 / fv;
+        c = static_cast<int>(i0 - t * fv);
+        dt = stride / fv;
+        dc = static_cast<int>(stride - dt * fv);
+    }
+    __device__ __forceinline__ void next() {
+        t += dt;
+        c += dc;
+        if (c >= fv) { c -= fv; ++t; }
+    }
+};
+
+__device__ __forceinline__ uint4 swiglu8(uint4 gw, uint4 uw) {
+    float g[8], u[8], r[8];
+    unpack8(gw, g);
+    unpack8(uw, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r[j] = __fmul_rn(bf(tobf(silu_f(g[j]))), u[j]);
+    return pack8(r);
+}
+
+// Two vectors per round, both loaded before either is computed.
 __global__ void __launch_bounds__(256)
 swiglu_fwd_v8_kernel(const uint4 *__restrict__ gu, int64_t N, int f, uint4 *__restrict__ h) {
     const int fv = f / 8;
-    const int64_t total = N * fv;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t t = i / fv;
-        const int c = static_cast<int>(i - t * fv);
-        float g[8], u[8], r[8];
-        unpack8(gu[t * 2 * fv + c], g);
-        unpack8(gu[t * 2 * fv + fv + c], u);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) r[j] = __fmul_rn(bf(tobf(silu_f(g[j]))), u[j]);
-        h[t * fv + c] = pack8(r);
+    RowWalk w(static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+              static_cast<int64_t>(gridDim.x) * blockDim.x, fv);
+    while (w.t < N) {
+        const int64_t t0 = w.t;
+        const int c0 = w.c;
+        w.next();
+        const int64_t t1 = w.t;
+        const int c1 = w.c;
+        const bool two = t1 < N;
+        const uint4 g0 = gu[t0 * 2 * fv + c0], u0 = gu[t0 * 2 * fv + fv + c0];
+        uint4 g1 = make_uint4(0, 0, 0, 0), u1 = g1;
+        if (two) {
+            g1 = gu[t1 * 2 * fv + c1];
+            u1 = gu[t1 * 2 * fv + fv + c1];
+        }
+        h[t0 * fv + c0] = swiglu8(g0, u0);
+        if (two) h[t1 * fv + c1] = swiglu8(g1, u1);
+        w.next();
     }
+}
+
+__device__ __forceinline__ void swiglu_bwd8(uint4 gw, uint4 uw, uint4 dw, uint4 &dgw, uint4 &duw) {
+    float g[8], u[8], d[8], dg[8], du[8];
+    unpack8(gw, g);
+    unpack8(uw, u);
+    unpack8(dw, d);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        // one exp per element: silu(g) = g / (1 + e^-g), sigmoid = 1 / (1 + e^-g)
+        const float den = __fadd_rn(1.0f, expf(-g[j]));
+        const float a = bf(tobf(__fdiv_rn(g[j], den)));
+        const float da = bf(tobf(__fmul_rn(d[j], u[j])));
+        du[j] = __fmul_rn(d[j], a);
+        const float sg = __fdiv_rn(1.0f, den);
+        dg[j] = __fmul_rn(__fmul_rn(da, sg), __fadd_rn(1.0f, __fmul_rn(g[j], __fsub_rn(1.0f, sg))));
+    }
+    dgw = pack8(dg);
+    duw = pack8(du);
 }
 
 __global__ void __launch_bounds__(256)
 swiglu_bwd_v8_kernel(const uint4 *__restrict__ dh, const uint4 *__restrict__ gu, int64_t N, int f,
                      uint4 *__restrict__ dgu) {
     const int fv = f / 8;
-    const int64_t total = N * fv;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t t = i / fv;
-        const int c = static_cast<int>(i - t * fv);
-        float g[8], u[8], d[8], dg[8], du[8];
-        unpack8(gu[t * 2 * fv + c], g);
-        unpack8(gu[t * 2 * fv + fv + c], u);
-        unpack8(dh[t * fv + c], d);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            // one exp per element: silu(g) = g / (1 + e^-g), sigmoid = 1 / (1 + e^-g)
-            const float den = __fadd_rn(1.0f, expf(-g[j]));
-            const float a = bf(tobf(__fdiv_rn(g[j], den)));
-            const float da = bf(tobf(__fmul_rn(d[j], u[j])));
-            du[j] = __fmul_rn(d[j], a);
-            const float sg = __fdiv_rn(1.0f, den);
-            dg[j] = __fmul_rn(__fmul_rn(da, sg), __fadd_rn(1.0f, __fmul_rn(g[j], __fsub_rn(1.0f, sg))));
+    RowWalk w(static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x,
+              static_cast<int64_t>(gridDim.x) * blockDim.x, fv);
+    while (w.t < N) {
+        const int64_t t0 = w.t;
+        const int c0 = w.c;
+        w.next();
+        const int64_t t1 = w.t;
+        const int c1 = w.c;
+        const bool two = t1 < N;
+        const uint4 g0 = gu[t0 * 2 * fv + c0], u0 = gu[t0 * 2 * fv + fv + c0], d0 = dh[t0 * fv + c0];
+        uint4 g1 = make_uint4(0, 0, 0, 0), u1 = g1, d1 = g1;
+        if (two) {
+            g1 = gu[t1 * 2 * fv + c1];
+            u1 = gu[t1 * 2 * fv + fv + c1];
+            d1 = dh[t1 * fv + c1];
         }
-        dgu[t * 2 * fv + c] = pack8(dg);
-        dgu[t * 2 * fv + fv + c] = pack8(du);
+        uint4 dg, du;
+        swiglu_bwd8(g0, u0, d0, dg, du);
+        dgu[t0 * 2 * fv + c0] = dg;
+        dgu[t0 * 2 * fv + fv + c0] = du;
+        if (two) {
+            swiglu_bwd8(g1, u1, d1, dg, du);
+            dgu[t1 * 2 * fv + c1] = dg;
+            dgu[t1 * 2 * fv + fv + c1] = du;
+        }
+        w.next();
     }
 }
 

@@ -83,8 +83,8 @@ class MoMLayer(nn.Module):
         """o_proj(read) before the mom_scale factor, for a caller that folds the
         factor into the residual add that follows (the decoder's fused add +
         RMSNorm). x feeds the router (its prefix scan sees x's own values);
-        x_lowp, when given, is the same activations already in bf16 for the q
-        projection."""
+        x_lowp, when given, is the same activations already rounded to bf16
+        (to nearest even), for the q projection and the router's backward."""
         mode = self._resolve(x)
         B, S, _ = x.shape
         noise = None
@@ -94,7 +94,7 @@ class MoMLayer(nn.Module):
         # takes the log-gates, whose gradient goes straight back into the router kernel
         probs, top_idx, _, log_gates = mom_kernels.mom_route_log_gates(
             x, self.router_down.weight, self.router_up.weight, self.top_blocks, noise,
-            scan_mode=self.scan_mode)
+            scan_mode=self.scan_mode, x_lowp=x_lowp)
         if self.training:
             self.last_router_probs = probs.reshape(-1, self.num_blocks)
             self.last_top_idx = top_idx.reshape(-1, self.top_blocks)

@@ -366,7 +366,7 @@ class _MomRouteFunction(torch.autograd.Function):
     dW_up (the reverse prefix scan runs in rank-r space)."""
 
     @staticmethod
-    def forward(ctx, x, w_down, w_up, noise, top, compute_dtype, scan_mode):
+    def forward(ctx, x, w_down, w_up, noise, top, compute_dtype, scan_mode, x_lowp=None):
         B, S, d = x.shape
         r, nb = w_down.shape[0], w_up.shape[0]
         dev = x.device
@@ -388,15 +388,17 @@ class _MomRouteFunction(torch.autograd.Function):
                   wu.data_ptr(), cd, r, nb, top, _ptr(nz), _lib.SCAN_MODES[scan_mode],
                   probs.data_ptr(), top_idx.data_ptr(), _lib.I64, gates.data_ptr(), log_gates.data_ptr(),
                   act.data_ptr(), ws.data_ptr(), ws.numel(), st)
-        ctx.save_for_backward(x_c, wd, wu, probs, top_idx, gates, act)
-        ctx.meta = (top, cd, w_down.dtype, w_up.dtype)
+        # the backward reads x only as its bf16 rounding (dW_down = u^T bf16(x)): a caller
+        # that already holds bf16(x) (x_lowp) saves the fp32 read of x there
+        ctx.save_for_backward(x_c if x_lowp is None else x_lowp.contiguous(), wd, wu, probs, top_idx, gates, act)
+        ctx.meta = (top, cd, w_down.dtype, w_up.dtype, x.dtype)
         ctx.mark_non_differentiable(top_idx)
         return probs, top_idx, gates, log_gates
 
     @staticmethod
     def backward(ctx, dprobs, _didx, dgates, dlog_gates):
         x, wd, wu, probs, top_idx, gates, act = ctx.saved_tensors
-        top, cd, wd_dtype, wu_dtype = ctx.meta
+        top, cd, wd_dtype, wu_dtype, x_dtype = ctx.meta
         B, S, d = x.shape
         r, nb = wd.shape[0], wu.shape[0]
         dev = x.device
@@ -404,16 +406,16 @@ class _MomRouteFunction(torch.autograd.Function):
         dp = None if dprobs is None else dprobs.to(torch.float32).contiguous()
         dg = None if dgates is None else dgates.to(torch.float32).contiguous()
         dlg = None if dlog_gates is None else dlog_gates.to(torch.float32).contiguous()
-        dx = torch.empty_like(x)
+        dx = torch.empty(x.shape, dtype=x_dtype, device=dev)
         dw_down = torch.empty((r, d), dtype=torch.float32, device=dev)
         dw_up = torch.empty((nb, r), dtype=torch.float32, device=dev)
         ws = torch.empty(_lib.load().mom_route_bwd_workspace_size(B, S, d, r, nb), dtype=torch.uint8, device=dev)
         _lib.call("mom_route_bwd", x.data_ptr(), _dt_code(x.dtype), B, S, d, wd.data_ptr(),
                   wu.data_ptr(), cd, r, nb, top, probs.data_ptr(), top_idx.data_ptr(), _lib.I64,
                   gates.data_ptr(), act.data_ptr(), _ptr(dlg), _ptr(dg), _ptr(dp), dx.data_ptr(),
-                  _dt_code(x.dtype), 0, dw_down.data_ptr(), dw_up.data_ptr(), ws.data_ptr(),
+                  _dt_code(x_dtype), 0, dw_down.data_ptr(), dw_up.data_ptr(), ws.data_ptr(),
                   ws.numel(), st)
-        return dx, dw_down.to(wd_dtype), dw_up.to(wu_dtype), None, None, None, None
+        return dx, dw_down.to(wd_dtype), dw_up.to(wu_dtype), None, None, None, None, None
 
 
 def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
@@ -443,20 +445,26 @@ def mom_route(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=Non
 
 
 def mom_route_log_gates(x, w_down, w_up, top_blocks: int, noise=None, *, compute_dtype=None,
-                        scan_mode: str = "fp32"):
+                        scan_mode: str = "fp32", x_lowp=None):
     """``mom_route`` that also returns log(max(top_gates, 1e-9)) as a fourth,
     differentiable output, computed by the router kernel; its gradient goes
     into the router backward directly (the kernel applies the clamp / log
     derivative). For callers that feed the read with log-gates
     (``mom_read_log_gates``), as the MoM layer does: the same values as the
     reference's bias (mom_kernels/reference.py:14-29) without the torch
-    clamp / log ops and their backward."""
+    clamp / log ops and their backward.
+
+    x_lowp: optionally x rounded to bf16 (round to nearest even), when the
+    caller has it already; the backward then reads it instead of x, with the
+    same results (it uses x only in that rounding) and half the bytes."""
     if not x.is_cuda:
         raise RuntimeError("sm100 mom_route: x must be on a CUDA device")
     if scan_mode not in _lib.SCAN_MODES:
         raise RuntimeError(f"sm100 mom_route: scan_mode must be one of {sorted(_lib.SCAN_MODES)}")
+    if x_lowp is not None and (x_lowp.shape != x.shape or x_lowp.dtype != torch.bfloat16):
+        raise RuntimeError("sm100 mom_route: x_lowp must be x's shape in bf16")
     cd = compute_dtype or _compute_dtype(w_down)
-    return _MomRouteFunction.apply(x, w_down, w_up, noise, int(top_blocks), cd, scan_mode)
+    return _MomRouteFunction.apply(x, w_down, w_up, noise, int(top_blocks), cd, scan_mode, x_lowp)
 
 
 class _MomScaleFunction(torch.autograd.Function):

@@ -414,3 +414,31 @@ def test_gumbel_noise_is_the_torch_expression_bitwise(shape, scale):
     u = torch.rand(shape, device=dev, dtype=torch.float32)
     want = scale * (-torch.log(-torch.log(u + 1e-9) + 1e-9))
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("r", [32, 64])
+def test_router_backward_from_the_bf16_copy_of_x_is_identical(r):
+    """The router's backward uses x only rounded to bf16 (dW_down = u^T bf16(x));
+    handing it that rounding (x_lowp, as the decoder's add + RMSNorm writes it)
+    instead of the fp32 x gives the same dx bit for bit (an fp32 dx) and the
+    same dW_down, dW_up up to the order of their fp32 atomic sums."""
+    from naylis_b200 import mom_kernels as mk
+    torch.manual_seed(17)
+    dev = torch.device("cuda")
+    B, S, d, nb, top = 2, 700, 1024, 8, 2
+    x = torch.randn(B, S, d, device=dev)
+    w_down = 0.02 * torch.randn(r, d, device=dev)
+    w_up = 0.02 * torch.randn(nb, r, device=dev)
+    dlg = torch.randn(B, S, top, device=dev)
+    dpr = torch.randn(B, S, nb, device=dev)
+    out = []
+    for lowp in (None, x.bfloat16()):
+        xd, wd, wu = (t.clone().requires_grad_(True) for t in (x, w_down, w_up))
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            probs, _, _, lg = mk.mom_route_log_gates(xd, wd, wu, top, None, x_lowp=lowp)
+        torch.autograd.backward([lg, probs], [dlg, dpr])
+        out.append((xd.grad, wd.grad, wu.grad))
+    assert out[1][0].dtype == torch.float32
+    assert torch.equal(out[0][0], out[1][0])
+    for a, b in zip(out[0][1:], out[1][1:]):
+        assert float((a - b).abs().max()) <= 1e-5 * float(b.abs().max())
