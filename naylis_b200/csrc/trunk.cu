@@ -452,33 +452,50 @@ add_rmsnorm_fwd_kernel(const float *__restrict__ x, const void *__restrict__ del
     }
 }
 
+// Named barrier `id` (1..15) over `nthreads` threads of the CTA.
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Backward of add_rmsnorm. dy = dy16 (+ dy32), g = dy * w, xh = x_new * r:
 //   d(x_new) = dx_in + r * (g - xh * mean(g * xh))      (dx_in: the residual's own gradient)
 //   dx = d(x_new), d(delta) = scale * d(x_new), dw += dy * xh, dscale += sum d(x_new) * delta
+// SPLIT warps share a token, each holding d / SPLIT columns (NV vectors of 4 per
+// lane): with SPLIT = 2 the registers a lane needs halve and twice as many warps
+// are resident to cover the loads' latency; the two partial sums of g * xh meet
+// in shared memory behind a named barrier of the warp pair (double-buffered by
+// token parity, so a warp one token ahead never overwrites a value its partner
+// has yet to read) and both warps add them in the same order.
 // dw and dscale are kept per lane across the warp's tokens, reduced per CTA in
 // shared memory and added to global memory with one atomic each.
-template <int DDT, int NV>
+template <int DDT, int NV, int SPLIT>
 __global__ void __launch_bounds__(32 * kNormWarps)
 add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict__ rstd, const float *__restrict__ w,
                        const void *__restrict__ delta, const float *__restrict__ dscale_in,
                        const uint16_t *__restrict__ dy16, const float *__restrict__ dy32,
                        const float *__restrict__ dx_in, int64_t N, int d, float *__restrict__ dx,
                        void *__restrict__ ddelta, float *__restrict__ dw, float *__restrict__ dscale) {
-    extern __shared__ float sdw[];                  // [d] + [1]
+    static_assert(SPLIT == 1 || SPLIT == 2, "one or two warps per token");
+    constexpr int kGroups = kNormWarps / SPLIT;     // tokens in flight per CTA
+    extern __shared__ float sdw[];                  // [d] + [1] + partial dots [kGroups][2][SPLIT]
+    float *sdot = sdw + d + 1;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int grp = warp / SPLIT, part = warp % SPLIT;
+    const int col0 = part * (d / SPLIT) + 4 * lane;
     for (int c = threadIdx.x; c <= d; c += blockDim.x) sdw[c] = 0.0f;
     __syncthreads();
     const float sc = (DDT != 0 && dscale_in) ? *dscale_in : 1.0f;
     float4 wv[NV], aw[NV];
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-        wv[j] = ld4(w + 4 * lane + 128 * j);
+        wv[j] = ld4(w + col0 + 128 * j);
         aw[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float acc_s = 0.0f;
-    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kNormWarps + warp; t < N;
-         t += static_cast<int64_t>(gridDim.x) * kNormWarps) {
-        const int64_t base = t * d + 4 * lane;
+    int slot = 0;
+    for (int64_t t = static_cast<int64_t>(blockIdx.x) * kGroups + grp; t < N;
+         t += static_cast<int64_t>(gridDim.x) * kGroups) {
+        const int64_t base = t * d + col0;
         const float r = rstd[t];
         float4 xv[NV], gv[NV], rv[NV], dl[NV];
 #pragma unroll
@@ -502,6 +519,13 @@ add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict_
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (SPLIT == 2) {
+            float *pd = sdot + (grp * 2 + slot) * 2;
+            if (lane == 0) pd[part] = dot;
+            named_bar_sync(1 + grp, 64);
+            dot = pd[0] + pd[1];
+            slot ^= 1;
+        }
         const float mean = dot / static_cast<float>(d);
 #pragma unroll
         for (int j = 0; j < NV; ++j) {
@@ -524,7 +548,7 @@ add_rmsnorm_bwd_kernel(const float *__restrict__ x_new, const float *__restrict_
     }
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-        const int c = 4 * lane + 128 * j;
+        const int c = col0 + 128 * j;
         atomicAdd(&sdw[c], aw[j].x);
         atomicAdd(&sdw[c + 1], aw[j].y);
         atomicAdd(&sdw[c + 2], aw[j].z);
@@ -776,18 +800,28 @@ cudaError_t launch_add_rmsnorm_bwd(const float *x_new, const float *rstd, const 
     if (e == cudaSuccess && dscale) e = cudaMemsetAsync(dscale, 0, sizeof(float), st);
     if (e != cudaSuccess) return e;
     if (N == 0) return cudaSuccess;
-    const int blocks = static_cast<int>(std::min<int64_t>((N + kNormWarps - 1) / kNormWarps, 148 * 4));
-    const size_t smem = sizeof(float) * (d + 1);
     auto g16 = static_cast<const uint16_t *>(dy16);
     const int nv = d / 128;
-#define MOM_NORM_B(DDT, NVV)                                                                                     \
-    add_rmsnorm_bwd_kernel<DDT, NVV><<<blocks, 32 * kNormWarps, smem, st>>>(x_new, rstd, w, delta, dscale_in, g16, \
-                                                                            dy32, dx_in, N, d, dx, ddelta, dw,  \
-                                                                            dscale)
-#define MOM_NORM_BD(NVV) \
-    if (ddt == 0) MOM_NORM_B(0, NVV); else if (ddt == 1) MOM_NORM_B(1, NVV); else MOM_NORM_B(2, NVV);
-    if (nv == 8) { MOM_NORM_BD(8) } else if (nv == 16) { MOM_NORM_BD(16) } else if (nv == 4) { MOM_NORM_BD(4) }
-    else if (nv == 2) { MOM_NORM_BD(2) } else if (nv == 1) { MOM_NORM_BD(1) } else { return cudaErrorInvalidValue; }
+    // one resident wave: every CTA zeroes, reduces and flushes its dw partials once,
+    // so the fewer CTAs (the more tokens per warp) the less of that per token
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+#define MOM_NORM_B(DDT, NVV, SP)                                                                                 \
+    do {                                                                                                       \
+        const size_t smem = sizeof(float) * (d + 1 + 2 * kNormWarps);                                          \
+        int per_sm = 1;                                                                                        \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, add_rmsnorm_bwd_kernel<DDT, NVV, SP>,           \
+                                                      32 * kNormWarps, smem);                                  \
+        const int64_t groups = (N + kNormWarps / SP - 1) / (kNormWarps / SP);                                  \
+        const int blocks = static_cast<int>(std::min<int64_t>(groups, static_cast<int64_t>(sms) * std::max(per_sm, 1))); \
+        add_rmsnorm_bwd_kernel<DDT, NVV, SP><<<blocks, 32 * kNormWarps, smem, st>>>(                          \
+            x_new, rstd, w, delta, dscale_in, g16, dy32, dx_in, N, d, dx, ddelta, dw, dscale);                 \
+    } while (0)
+#define MOM_NORM_BD(NVV, SP) \
+    if (ddt == 0) MOM_NORM_B(0, NVV, SP); else if (ddt == 1) MOM_NORM_B(1, NVV, SP); else MOM_NORM_B(2, NVV, SP);
+    // d >= 1024: a warp pair per token (NV / 2 vectors per lane)
+    if (nv == 8) { MOM_NORM_BD(4, 2) } else if (nv == 16) { MOM_NORM_BD(8, 2) } else if (nv == 4) { MOM_NORM_BD(4, 1) }
+    else if (nv == 2) { MOM_NORM_BD(2, 1) } else if (nv == 1) { MOM_NORM_BD(1, 1) } else { return cudaErrorInvalidValue; }
 #undef MOM_NORM_BD
 #undef MOM_NORM_B
     count_launch();

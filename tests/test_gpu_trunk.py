@@ -73,19 +73,23 @@ def test_swiglu_matches_torch(N, f):
         assert worst <= 1.0 and frac < 1e-3, (name, frac, worst)
 
 
-@pytest.mark.parametrize("delta_dtype,scaled,want_f32", [(None, False, False), (torch.bfloat16, False, True),
-                                                         (torch.bfloat16, True, False), (torch.float32, False, False)])
-def test_add_rmsnorm_matches_torch(delta_dtype, scaled, want_f32):
+@pytest.mark.parametrize("delta_dtype,scaled,want_f32,d", [
+    (None, False, False, 1024), (torch.bfloat16, False, True, 1024), (torch.bfloat16, True, False, 1024),
+    (torch.float32, False, False, 1024), (torch.bfloat16, True, True, 2048), (torch.float32, True, False, 256),
+    (None, False, False, 128)])
+def test_add_rmsnorm_matches_torch(delta_dtype, scaled, want_f32, d):
     """x_new = x + s * delta then Llama's RMSNorm (transformers' LlamaRMSNorm:
     fp32 x * rsqrt(mean(x^2) + eps), times the weight) against torch ops on the
     same inputs. x_new is the same two roundings (exact match); y differs from
     torch's only by the order of the mean's sum (bf16 output: at most one ulp);
     gradients (the residual gradient passed through plus the norm's, dw, ds)
-    agree to 1e-5 of their largest magnitude."""
+    agree to 1e-5 of their largest magnitude. d = 1024 and 2048 take the
+    backward with a warp pair per token, 128 and 256 a warp per token; 777
+    tokens leave a ragged last group."""
     from naylis_b200 import trunk
     torch.manual_seed(2)
     dev = torch.device("cuda")
-    N, d, eps = 777, 1024, 1e-5
+    N, eps = 777, 1e-5
     x = torch.randn(N, d, device=dev).requires_grad_(True)
     delta = None if delta_dtype is None else torch.randn(N, d, device=dev).to(delta_dtype).requires_grad_(True)
     w = (1 + 0.1 * torch.randn(d, device=dev)).requires_grad_(True)
