@@ -88,35 +88,43 @@ class GradAllReduce:
             if id(g[0]) not in placed:
                 units.append(g)
                 placed.update(id(q) for q in g)
+        # every unit (a parameter, or a group) starts on a 16-byte boundary: a GEMM
+        # writing into a slot needs it (a 1-element mom_scale would otherwise shift
+        # every later slot), and the zero padding rides along in the all-reduce
+        pad = lambda n: (n + 3) // 4 * 4
         cap = int(bucket_mb * (1 << 20) // 4)
         self.buckets = []
         cur = []
         size = 0
         for g in units:
-            n = sum(p.numel() for p in g)
+            n = pad(sum(p.numel() for p in g))
             if cur and size + n > cap:
                 self.buckets.append(cur)
                 cur, size = [], 0
-            cur.extend(g)
+            cur.append(g)
             size += n
         if cur:
             self.buckets.append(cur)
-        self.params = [p for ps in self.buckets for p in ps]
+        self.params = [p for units_ in self.buckets for g in units_ for p in g]
         self.flat = []
         self._bucket_of = {}
         self._slot = {}
-        for i, ps in enumerate(self.buckets):
-            n = sum(p.numel() for p in ps)
-            buf = torch.zeros(n, dtype=torch.float32, device=ps[0].device)
+        for i, units_ in enumerate(self.buckets):
+            n = sum(pad(sum(p.numel() for p in g)) for g in units_)
+            buf = torch.zeros(n, dtype=torch.float32, device=units_[0][0].device)
             off = 0
-            for p in ps:
-                view = buf[off:off + p.numel()].view_as(p)
-                p.grad = view
-                self._slot[p] = view
-                trunk.register_grad_slot(p, buf, off)
-                off += p.numel()
-                self._bucket_of[p] = i
+            for g in units_:
+                start = off
+                for p in g:
+                    view = buf[off:off + p.numel()].view_as(p)
+                    p.grad = view
+                    self._slot[p] = view
+                    trunk.register_grad_slot(p, buf, off)
+                    off += p.numel()
+                    self._bucket_of[p] = i
+                off = start + pad(off - start)
             self.flat.append(buf)
+        self.buckets = [[p for g in units_ for p in g] for units_ in self.buckets]
         self.wire = [torch.empty(b.numel(), dtype=self.comm_dtype, device=b.device) for b in self.flat] \
             if self.comm_dtype is not None and self.world > 1 else None
         self._hooks = [p.register_post_accumulate_grad_hook(self._on_ready) for p in params]

@@ -315,12 +315,17 @@ class NaylisForCausalLM(nn.Module):
         h = self.model(input_ids)
         if labels is None:
             return self.lm_head(h)
-        shift_h = h[:, :-1].reshape(-1, h.shape[-1])
-        shift_labels = labels[:, 1:].reshape(-1)
-        if _bf16_path(shift_h):
-            logits = trunk.linear_f32grad(shift_h, self.lm_head.weight)
+        if _bf16_path(h):
+            # every position through the head, the last of each sequence with an ignored
+            # label: the same loss as the reference's h[:, :-1] / labels[:, 1:] shift, without
+            # the copy of the sliced activations and the scatter of its gradient
+            shift_labels = torch.full_like(labels, -100)
+            shift_labels[:, :-1] = labels[:, 1:]
+            shift_labels = shift_labels.reshape(-1)
+            logits = trunk.linear_f32grad(h.reshape(-1, h.shape[-1]), self.lm_head.weight)
         else:
-            logits = self.lm_head(shift_h)
+            shift_labels = labels[:, 1:].reshape(-1)
+            logits = self.lm_head(h[:, :-1].reshape(-1, h.shape[-1]))
         if logits.is_cuda and logits.dtype == torch.bfloat16:
             # fused (csrc/trunk.cu): the same fp32 math on the bf16 logits, no fp32 copy
             loss = trunk.cross_entropy_sum(logits, shift_labels)

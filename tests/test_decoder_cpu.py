@@ -78,7 +78,8 @@ def test_optimizer_table_layout():
 
 def test_gradient_buckets_keep_fused_projection_groups_contiguous():
     """GradAllReduce lays the decoder's q/k/v and gate/up weights next to each
-    other in one bucket in the fused GEMM's row order, registers every slot, and
+    other in one bucket in the fused GEMM's row order, starts every parameter on
+    a 16-byte boundary (the GEMMs writing there need it), registers every slot, and
     zero_grad clears the gradients to None; finish() gives a parameter that got
     no gradient its zero-filled slot."""
     import torch
@@ -96,7 +97,11 @@ def test_gradient_buckets_keep_fused_projection_groups_contiguous():
             assert all(e[0] is ents[0][0] for e in ents)
             offs = [e[1] for e in ents]
             assert offs == [offs[0] + sum(w.numel() for w in g[:i]) for i in range(len(g))]
-        assert sum(b.numel() for b in dp.flat) == sum(p.numel() for p in model.parameters())
+        # every unit starts on a 16-byte boundary (mom_scale holds one value)
+        assert all(trunk._GRAD_SLOTS[g[0]][1] % 4 == 0 for g in model.grad_groups())
+        assert all(trunk._GRAD_SLOTS[p][1] % 4 == 0 for p in model.parameters())
+        total = sum(p.numel() for p in model.parameters())
+        assert total <= sum(b.numel() for b in dp.flat) <= total + 3 * len(list(model.parameters()))
         dp.zero_grad()
         assert all(p.grad is None for p in model.parameters())
         dp.finish()
