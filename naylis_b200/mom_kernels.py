@@ -393,6 +393,9 @@ class _MomRouteFunction(torch.autograd.Function):
         ctx.save_for_backward(x_c if x_lowp is None else x_lowp.contiguous(), wd, wu, probs, top_idx, gates, act)
         ctx.meta = (top, cd, w_down.dtype, w_up.dtype, x.dtype)
         ctx.mark_non_differentiable(top_idx)
+        # outputs without a consumer (top_idx; gates when the read takes log_gates) reach the
+        # backward as None instead of zero-filled tensors
+        ctx.set_materialize_grads(False)
         return probs, top_idx, gates, log_gates
 
     @staticmethod

@@ -117,6 +117,9 @@ class _AddRMSNorm(torch.autograd.Function):
         ctx.save_for_backward(x_out, rstd, w, delta, sc)
         ctx.meta = (dcode, delta is not None, scale is not None, scale.dtype if scale is not None else None,
                     weight.dtype)
+        # an output nobody reads (the final norm's residual stream) reaches the backward as
+        # None, so the kernel skips it instead of reading a zero-filled gradient
+        ctx.set_materialize_grads(False)
         if want_f32:
             return x_out, y16, y32
         return x_out, y16
