@@ -345,7 +345,11 @@ def run_model_cfg3(args):
     torch.manual_seed(1234)                       # every replica starts from the same weights
     model = NaylisForCausalLM(cfg).to(dev).train()
     comm = torch.bfloat16 if args.bf16_grads else None
-    dp = GradAllReduce(model, bucket_mb=args.bucket_mb, comm_dtype=comm)
+    # one GPU: the step as one CUDA graph; more: eager, the buckets' all-reduces launched
+    # from the backward's hooks as the gradients become ready (measured at 2 GPUs);
+    # --graph replays the graph there too, with the exchange by finish() after each replay
+    use_graph = not args.no_graph and (world == 1 or args.graph)
+    dp = GradAllReduce(model, bucket_mb=args.bucket_mb, comm_dtype=comm, overlap=not use_graph)
     if args.optim == "torch":
         opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1, fused=True)
     else:
@@ -356,7 +360,17 @@ def run_model_cfg3(args):
     ids = torch.randint(0, cfg.vocab_size, (B, S), device=dev, generator=g)
     lib = _lib.load()
 
+    gstep = None
+    if use_graph:
+        # zero_grad + forward + loss + backward as one CUDA graph (the public helper)
+        from naylis_b200.graph_step import GraphedTrainStep
+        gstep = GraphedTrainStep(model, dp, ids)
+
     def step(batch):
+        if gstep is not None:
+            loss = gstep.step(None if batch is ids else batch)
+            opt.step()
+            return loss
         dp.zero_grad()
         with torch.autocast("cuda", dtype=torch.bfloat16):
             loss = model(batch, labels=batch)
@@ -390,6 +404,8 @@ def run_model_cfg3(args):
         dist.barrier()
     t_wall1 = time.time()
     launches = lib.mom_kernel_launches() - l0
+    if gstep is not None:
+        launches += gstep.kernels_per_replay * args.steps    # replayed, not counted by the host
     each_ms = sorted(a.elapsed_time(b) for a, b in zip(starts, ends))
     total_ms = sum(each_ms)
     if clocks:
@@ -413,8 +429,11 @@ def run_model_cfg3(args):
     b = torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(n_e2e):
-        dev_ids.copy_(ids_host, non_blocking=True)
-        loss = step(dev_ids)
+        if gstep is not None:
+            loss = step(ids_host)                 # copied from pinned host memory into the graph's input
+        else:
+            dev_ids.copy_(ids_host, non_blocking=True)
+            loss = step(dev_ids)
         loss_host[i:i + 1].copy_(loss.detach().float().reshape(1), non_blocking=True)
     b.record()
     torch.cuda.synchronize()
@@ -459,8 +478,13 @@ def run_model_cfg3(args):
                        "l2": "flushed between timed steps (256 MiB write, untimed); the step's working set "
                              "(weights, optimizer state, activations) is far above L2 as well",
                        "grad_exchange": (f"bucketed NCCL AVG all-reduce ({args.bucket_mb:g} MiB buckets, "
-                                         f"{'bf16' if comm is not None else 'fp32'} on the wire) launched from the "
-                                         "backward's hooks" if world > 1 else "none (one GPU)")},
+                                         f"{'bf16' if comm is not None else 'fp32'} on the wire) "
+                                         + ("after each graph replay" if use_graph else
+                                            "launched from the backward's hooks")
+                                         if world > 1 else "none (one GPU)"),
+                       "cuda_graph": ("zero_grad + forward + loss + backward replayed as one CUDA graph "
+                                      "(naylis_b200.graph_step.GraphedTrainStep); AdamW and the exchange outside"
+                                      if use_graph else "none (eager launches)")},
             "tokens_per_s_per_gpu": round(per_gpu, 1),
             "model_flops_per_token": fpt,
             "mfu": round(per_gpu * fpt / (pk["bf16_sust"] * 1e12), 4),
@@ -982,6 +1006,8 @@ def main():
     ap.add_argument("--cpu-samples", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step eagerly, no CUDA graph")
+    ap.add_argument("--graph", action="store_true",
+                    help="cfg3 on more than one GPU: replay the step as a CUDA graph as well (the default at N=1)")
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")

@@ -152,3 +152,19 @@ def test_side_by_side_views_and_copies():
     c = trunk._side_by_side(a2, b2)
     assert torch.equal(c, torch.cat([a2, b2], 1))
     assert torch.equal(trunk._side_by_side(b, a), torch.cat([b, a], 1))
+
+
+def test_graphed_step_refuses_what_it_cannot_capture():
+    """GraphedTrainStep takes CUDA token ids only, and on more than one process a
+    GradAllReduce whose hooks launch no collective (overlap=False): a capture
+    cannot hold the hooks' all-reduces."""
+    import types
+    import pytest
+    import torch
+    from naylis_b200.graph_step import GraphedTrainStep
+    with pytest.raises(RuntimeError, match="CUDA"):
+        GraphedTrainStep(None, types.SimpleNamespace(world=1, overlap=True), torch.zeros(1, 4, dtype=torch.long))
+    meta = torch.zeros(1, 4, dtype=torch.long, device="meta")
+    meta_cuda = types.SimpleNamespace(is_cuda=True, device=meta.device)
+    with pytest.raises(RuntimeError, match="overlap=False"):
+        GraphedTrainStep(None, types.SimpleNamespace(world=2, overlap=True), meta_cuda)
