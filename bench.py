@@ -345,10 +345,10 @@ def run_model_cfg3(args):
     torch.manual_seed(1234)                       # every replica starts from the same weights
     model = NaylisForCausalLM(cfg).to(dev).train()
     comm = torch.bfloat16 if args.bf16_grads else None
-    # one GPU: the step as one CUDA graph; more: eager, the buckets' all-reduces launched
-    # from the backward's hooks as the gradients become ready (measured at 2 GPUs);
-    # --graph replays the graph there too, with the exchange by finish() after each replay
-    use_graph = not args.no_graph and (world == 1 or args.graph)
+    # the step as one CUDA graph, the buckets exchanged by finish() after each replay
+    # (measured at 2 GPUs: faster than the eager step whose hooks overlap the all-reduces
+    # with the backward); --no-graph launches eagerly with that overlap
+    use_graph = not args.no_graph
     dp = GradAllReduce(model, bucket_mb=args.bucket_mb, comm_dtype=comm, overlap=not use_graph)
     if args.optim == "torch":
         opt = torch.optim.AdamW(model.parameters(), lr=3e-4, weight_decay=0.1, fused=True)
@@ -1006,8 +1006,6 @@ def main():
     ap.add_argument("--cpu-samples", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch the step eagerly, no CUDA graph")
-    ap.add_argument("--graph", action="store_true",
-                    help="cfg3 on more than one GPU: replay the step as a CUDA graph as well (the default at N=1)")
     ap.add_argument("--dp-in-graph", action="store_true",
                     help="N>1 with a graph: capture the bucket all-reduces with the backward")
     ap.add_argument("--bucket-mb", type=float, default=32.0, help="gradient bucket size for N>1 (MiB)")
