@@ -5,7 +5,9 @@ and the bucket all-reduces launched from the backward's hooks. After finish()
 both ranks hold the same gradients, equal to the mean of the two sequences'
 gradients computed one after the other in a single process (within 2e-2 of the
 largest magnitude: the read's dK / dV are fp32 atomic sums, so two runs differ
-in the last bf16 bits). Skipped with fewer than 2 GPUs.
+in the last bf16 bits). The same holds for the step replayed as one CUDA graph
+(graph_step.GraphedTrainStep) with the buckets exchanged after each replay.
+Skipped with fewer than 2 GPUs.
 """
 import datetime
 import os
@@ -71,9 +73,21 @@ def _worker(rank, world, port, q):
             loss.backward()
             dp.finish()
         torch.cuda.synchronize()
-        q.put((rank, {n: p.grad.float().cpu().numpy() for n, p in model.named_parameters()}))
-        dist.barrier()
+        eager = {n: p.grad.float().cpu().numpy() for n, p in model.named_parameters()}
         dp.remove()
+        # the same step replayed as one CUDA graph, the buckets exchanged after the replay
+        from naylis_b200.graph_step import GraphedTrainStep
+        model_g = _model().to(dev).train()
+        dp_g = GradAllReduce(model_g, bucket_mb=0.5, overlap=False)
+        gstep = GraphedTrainStep(model_g, dp_g, ids)
+        for _ in range(2):
+            gstep.step(ids)
+        torch.cuda.synchronize()
+        graphed = {n: p.grad.float().cpu().numpy() for n, p in model_g.named_parameters()}
+        q.put((rank, {"eager": eager, "graphed": graphed}))
+        dist.barrier()
+        del gstep
+        dp_g.remove()
         dist.destroy_process_group()
     except Exception:
         q.put((rank, traceback.format_exc()))
@@ -110,8 +124,10 @@ def test_decoder_data_parallel_on_two_gpus_equals_mean_gradient():
             loss = model(ids[r:r + 1], labels=ids[r:r + 1])
         loss.backward()
         per_seq.append({n: p.grad.float().cpu().numpy() for n, p in model.named_parameters()})
-    for n in per_seq[0]:
-        want = (per_seq[0][n] + per_seq[1][n]) / 2
-        assert np.array_equal(res[0][n], res[1][n]), n
-        err = float(np.abs(res[0][n] - want).max())
-        assert err <= 2e-2 * float(np.abs(want).max()) + 1e-12, (n, err)
+    for mode in ("eager", "graphed"):
+        for n in per_seq[0]:
+            want = (per_seq[0][n] + per_seq[1][n]) / 2
+            got = res[0][mode][n]
+            assert np.array_equal(got, res[1][mode][n]), (mode, n)
+            err = float(np.abs(got - want).max())
+            assert err <= 2e-2 * float(np.abs(want).max()) + 1e-12, (mode, n, err)
