@@ -350,6 +350,13 @@ MOM_API int mom_scale_bwd(const void *g, int g_dtype, const void *o, int o_dtype
  * Replaces the seven elementwise torch ops of that expression. */
 MOM_API int mom_gumbel(const float *u, int64_t n, float noise_scale, float *out, void *stream);
 
+/* The read backward's dK, dV (L, n) fp32, as mom_read_bwd leaves them, cast to bf16
+ * (round to nearest even) side by side into out (L, 2n) = [dK | dV]: the gradient of
+ * the bank's k and v projections (model.py:253-256, `k_proj(slots)`, `v_proj(slots)`
+ * under autocast, whose dK / dV the autograd casts to bf16) laid out for one GEMM over
+ * both. n % 4 == 0, dk / dv 16-byte and out 8-byte aligned. */
+MOM_API int mom_kv_pack_bf16(const float *dk, const float *dv, int64_t L, int64_t n, void *out, void *stream);
+
 /* Reads (and clears) the device error word of a plan: MOM_OK, or
  * MOM_ERR_DEVICE_INDEX when mom_bucket saw an index outside [0, nb).
  * Synchronises `stream`. */

@@ -49,6 +49,7 @@ SIGNATURES = {
     "mom_scale_fwd": (_int, [_vp, _int, _i64, _fp, _fp, _vp]),
     "mom_scale_bwd": (_int, [_vp, _int, _vp, _int, _i64, _fp, _vp, _fp, _vp]),
     "mom_gumbel": (_int, [_fp, _i64, _c.c_float, _fp, _vp]),
+    "mom_kv_pack_bf16": (_int, [_fp, _fp, _i64, _i64, _vp, _vp]),
     "mom_read_fwd": (_int, [_vp, _vp, _vp, _int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp,
                             _vp, _fp, _vp, _vp]),
     "mom_read_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),

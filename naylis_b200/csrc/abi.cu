@@ -349,6 +349,20 @@ int mom_gumbel(const float *u, int64_t n, float noise_scale, float *out, void *s
     return e == cudaSuccess ? MOM_OK : cuda_fail(e, "gumbel");
 }
 
+int mom_kv_pack_bf16(const float *dk, const float *dv, int64_t L, int64_t n, void *out, void *stream) {
+    MOM_REQUIRE(L >= 0 && n >= 0, "L and n must be >= 0");
+    if (L == 0 || n == 0) return MOM_OK;
+    MOM_REQUIRE(dk && dv && out, "null pointer argument");
+    MOM_REQUIRE(n % 4 == 0, "n must be a multiple of 4");
+    MOM_REQUIRE(((reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out) & 7) == 0,
+                "dk, dv must be 16-byte and out 8-byte aligned");
+    int rc = check_current_device();
+    if (rc) return rc;
+    cudaError_t e = mom::launch_kv_pack(dk, dv, L, n, out, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? MOM_OK : cuda_fail(e, "kv_pack");
+}
+
 int mom_plan_check(const void *plan, int64_t N, int64_t nb, int64_t top, void *stream) {
     MOM_REQUIRE(plan, "null plan");
     const mom::PlanLayout L = mom::plan_layout(N, nb, top);

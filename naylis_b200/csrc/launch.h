@@ -98,6 +98,8 @@ cudaError_t launch_scale_bwd(const void *g, int gdt, const void *o, int odt, con
                              void *d_o, float *d_scale, cudaStream_t st);
 // out = scale * -log(-log(u + 1e-9) + 1e-9), elementwise (out may alias u).
 cudaError_t launch_gumbel(const float *u, int64_t n, float scale, float *out, cudaStream_t st);
+// [dk | dv] (L, 2n) bf16 from dk, dv (L, n) fp32; n % 4 == 0, 16-B aligned inputs.
+cudaError_t launch_kv_pack(const float *dk, const float *dv, int64_t L, int64_t n, void *out, cudaStream_t st);
 cudaError_t launch_bucket(const void *top_idx, int idx64, const float *log_gates,
                           const PlanLayout &L, const PlanView &P, cudaStream_t st);
 // Row copy into routing-plan order: dst[r] = src[perm[r]] (rows of row_bytes, a multiple of 16).

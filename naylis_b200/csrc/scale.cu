@@ -181,4 +181,31 @@ cudaError_t launch_gumbel(const float *u, int64_t n, float scale, float *out, cu
     return cudaGetLastError();
 }
 
+// dK, dV (L, n) fp32 -> [dK | dV] (L, 2n) bf16 (round to nearest even) in one pass:
+// the read's backward accumulates dK / dV in fp32 and the bank projections' backward
+// reads them side by side as one bf16 operand. 16-byte loads, 8-byte stores.
+__global__ void __launch_bounds__(256)
+kv_pack_kernel(const float4 *__restrict__ dk, const float4 *__restrict__ dv, int64_t L, int n4,
+               uint2 *__restrict__ out) {
+    const int64_t total = L * 2 * n4;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t row = i / (2 * n4);
+        const int c = static_cast<int>(i - row * 2 * n4);
+        const float4 v = c < n4 ? dk[row * n4 + c] : dv[row * n4 + (c - n4)];
+        out[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    }
+}
+
+cudaError_t launch_kv_pack(const float *dk, const float *dv, int64_t L, int64_t n, void *out, cudaStream_t st) {
+    if (L == 0 || n == 0) return cudaSuccess;
+    if (n % 4 || !vec_ok(dk, MOM_F32) || !vec_ok(dv, MOM_F32) || (reinterpret_cast<uintptr_t>(out) & 7))
+        return cudaErrorInvalidValue;
+    kv_pack_kernel<<<scale_grid(L * 2 * n), 256, 0, st>>>(reinterpret_cast<const float4 *>(dk),
+                                                         reinterpret_cast<const float4 *>(dv), L,
+                                                         static_cast<int>(n / 4), static_cast<uint2 *>(out));
+    count_launch();
+    return cudaGetLastError();
+}
+
 }  // namespace mom

@@ -167,13 +167,15 @@ class _MomReadFunction(torch.autograd.Function):
 
 
 def _kv_grads(dk, dv, dtype):
-    """dK, dV cast to the bank's dtype, written side by side into one (L, 2n)
-    buffer and returned as its two halves, so the bank projection's backward
-    (trunk.bank_kv) reads [dK | dV] without another copy."""
+    """dK, dV (fp32) cast to the bank's dtype (bf16 here), written side by side into
+    one (L, 2n) buffer by one kernel (csrc/scale.cu, kv_pack) and returned as its
+    two halves, so the bank projection's backward (trunk.bank_kv) reads [dK | dV]
+    without another copy."""
     L, n = dk.shape
     both = torch.empty(L, 2 * n, dtype=dtype, device=dk.device)
-    both[:, :n].copy_(dk)
-    both[:, n:].copy_(dv)
+    if dtype != torch.bfloat16:
+        raise RuntimeError(f"sm100 mom_read backward: bf16 bank expected, got {dtype}")
+    _lib.call("mom_kv_pack_bf16", dk.data_ptr(), dv.data_ptr(), L, n, both.data_ptr(), _stream(dk.device))
     return both[:, :n], both[:, n:]
 
 

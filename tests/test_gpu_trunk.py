@@ -181,3 +181,19 @@ def test_bank_kv_matches_two_linears(nb, bs, d, n):
     refs = torch.autograd.grad((kr.float() * gk.float()).sum() + (vr.float() * gv.float()).sum(), (bank, wk, wv))
     for a, b in zip(grads, refs):
         assert float((a - b).abs().max()) <= 1e-2 * float(b.abs().max())
+
+
+@pytest.mark.parametrize("L,n", [(1024, 1024), (37, 12)])
+def test_kv_pack_is_the_torch_cast_bitwise(L, n):
+    """The read backward's fp32 dK / dV cast to bf16 side by side in one kernel
+    (mom_kv_pack_bf16, through the C ABI) equals torch's cast of their
+    concatenation bit for bit, large and small magnitudes included."""
+    from naylis_b200 import _lib
+    torch.manual_seed(13)
+    dev = torch.device("cuda")
+    dk = torch.randn(L, n, device=dev) * torch.logspace(-30, 30, L * n, device=dev).view(L, n)
+    dv = torch.randn(L, n, device=dev)
+    out = torch.empty(L, 2 * n, dtype=torch.bfloat16, device=dev)
+    _lib.call("mom_kv_pack_bf16", dk.data_ptr(), dv.data_ptr(), L, n, out.data_ptr(),
+              torch.cuda.current_stream().cuda_stream)
+    assert torch.equal(out.view(torch.int16), torch.cat([dk, dv], 1).bfloat16().view(torch.int16))
