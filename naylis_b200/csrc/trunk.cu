@@ -170,6 +170,27 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
                       pack_bf16x2(f[6], f[7]));
 }
 
+// (token, head, group of 8 pairs) of flat item i = (tok * H + h) * ng + p / 8, with 32-bit
+// unsigned divisions when the index fits (a 64-bit division costs several times as many
+// instructions, and these kernels do little else per item)
+__device__ __forceinline__ void rope_index(int64_t i, bool small, int ng, int H, int S, int &p, int &h,
+                                           int64_t &tok, int &s) {
+    if (small) {
+        const uint32_t u = static_cast<uint32_t>(i), th = u / static_cast<uint32_t>(ng);
+        const uint32_t t = th / static_cast<uint32_t>(H);
+        p = static_cast<int>(u - th * static_cast<uint32_t>(ng)) * 8;
+        h = static_cast<int>(th - t * static_cast<uint32_t>(H));
+        tok = t;
+        s = static_cast<int>(t % static_cast<uint32_t>(S));
+    } else {
+        const int64_t th = i / ng;
+        p = static_cast<int>(i - th * ng) * 8;
+        tok = th / H;
+        h = static_cast<int>(th - tok * H);
+        s = static_cast<int>(tok % S);
+    }
+}
+
 // one thread per (token, head, 8 pairs)
 __global__ void __launch_bounds__(256)
 rope_qkv_fwd_v8_kernel(const uint16_t *__restrict__ qkv, const float *__restrict__ cosv, const float *__restrict__ sinv,
@@ -177,14 +198,13 @@ rope_qkv_fwd_v8_kernel(const uint16_t *__restrict__ qkv, const float *__restrict
                        uint16_t *__restrict__ v) {
     const int half = hd / 2, ng = half / 8;
     const int64_t total = static_cast<int64_t>(B) * S * H * ng;
+    const bool small = total <= 0xFFFFFFFFLL;   // the index fits 32 bits: cheaper divisions
     const int64_t d3 = 3LL * H * hd;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(i % ng) * 8;
-        const int64_t th = i / ng;
-        const int h = static_cast<int>(th % H);
-        const int64_t tok = th / H;
-        const int s = static_cast<int>(tok % S);
+        int p, h, s;
+        int64_t tok;
+        rope_index(i, small, ng, H, S, p, h, tok, s);
         const uint16_t *row = qkv + tok * d3 + static_cast<int64_t>(h) * hd;
         const float *cs = cosv + static_cast<int64_t>(s) * hd, *sn = sinv + static_cast<int64_t>(s) * hd;
         float c1[8], c2[8], s1[8], s2[8];
@@ -223,14 +243,13 @@ rope_qkv_bwd_v8_kernel(const uint16_t *__restrict__ dq, const uint16_t *__restri
                        const float *__restrict__ sinv, int B, int S, int H, int hd, uint16_t *__restrict__ dqkv) {
     const int half = hd / 2, ng = half / 8;
     const int64_t total = static_cast<int64_t>(B) * S * H * ng;
+    const bool small = total <= 0xFFFFFFFFLL;   // the index fits 32 bits: cheaper divisions
     const int64_t d3 = 3LL * H * hd;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(i % ng) * 8;
-        const int64_t th = i / ng;
-        const int h = static_cast<int>(th % H);
-        const int64_t tok = th / H;
-        const int s = static_cast<int>(tok % S);
+        int p, h, s;
+        int64_t tok;
+        rope_index(i, small, ng, H, S, p, h, tok, s);
         uint16_t *row = dqkv + tok * d3 + static_cast<int64_t>(h) * hd;
         const float *cs = cosv + static_cast<int64_t>(s) * hd, *sn = sinv + static_cast<int64_t>(s) * hd;
         float c1[8], c2[8], s1[8], s2[8];
